@@ -1,0 +1,366 @@
+#!/usr/bin/env python
+"""Benchmark: Q4_0 decode throughput of the Llama-3-8B-shaped model
+("c4"): 32 sequences, each with a 2048-token random
+prompt prefilled, decoding greedily together with an fp16 KV cache.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one batched decode step of all 32 sequences (32 tokens).
+  value  : whole-job decode tok/s, inputs resident in HBM (hc_decode_step_dev),
+           device-timed with CUDA events on the model's stream, max over ranks.
+  e2e    : the same through the host-buffer C ABI call (hc_decode_step: ids
+           and sequence ids copied in from pinned host memory, greedy ids
+           copied back every step), wall-clocked, max over ranks.
+  prefill_tok_s : the 32 prompt prefills (hc_prefill), device-timed.
+  roofline      : the dominant kernel (the Q4_0 matmul of the fused gate/up
+           projection, N = 28672, K = 4096, M = 32) timed alone with CUDA events
+           over rotating weight copies larger than L2, against the measured
+           HBM copy bandwidth.
+  cpu_baseline  : the CPU oracle (restatement of hypno's CPU path) decoding
+           one sequence at context 2048 on the host cores (rank 0).
+With --gpus N > 1 (torchrun), every rank runs an independent replica of the
+workload (the model fits one GPU; tensor parallelism is not on this path yet):
+weak scaling, value = all ranks' tokens / the slowest rank's time.
+--impl reference times the CPU oracle on the same workload (rank 0 only).
+"""
+import argparse
+import ctypes
+import json
+import os
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "Q4_0 decode tok/s (Llama-3-8B shape, 32 sequences x 2048 context)"
+UNIT = "tok/s"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def _env_int(k, d):
+    try:
+        return int(os.environ.get(k, d))
+    except ValueError:
+        return d
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    def __init__(self, index, path):
+        self.path = path
+        self.proc = None
+        self.index = index
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        if self.proc is None or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[4:9]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = sorted(r[0] for r in rows)
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[2][i + 1].lower() == "active"})
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": max(r[1] for r in rows), "reasons": reasons,
+                "samples": len(rows)}
+
+
+def cuda_time_ms(stream_ptr, fn, reps):
+    """Average milliseconds of fn() over reps launches, CUDA events recorded on
+    the given raw stream (the stream the kernels run on)."""
+    import torch
+    s = torch.cuda.ExternalStream(stream_ptr) if stream_ptr else torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(s)
+    for i in range(reps):
+        fn(i)
+    e1.record(s)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+def roofline_gemv(dev, M=32, N=28672, K=4096, copies=4, reps=20):
+    """Times the Q4_0 matmul of the fused gate/up shape over `copies` rotating
+    weight matrices (together larger than L2) and returns the roofline dict."""
+    import torch
+    from hypno_b200 import synth
+    from hypno_b200._lib import call
+    mats = []
+    w32 = torch.empty(N * K, dtype=torch.float32, device=dev)
+    wq = torch.empty(N * K // 32 * 18, dtype=torch.uint8, device=dev)
+    for c in range(copies):
+        call("hc_synth_normal_dev", 100 + c, synth.fnv1a64("roofline.W"), 0, N * K, 0.02, w32.data_ptr(), None)
+        call("hc_q4_0_quantize_dev", w32.data_ptr(), N * K, wq.data_ptr(), None)
+        h = ctypes.c_void_p()
+        call("hc_q4_matrix_from_dev", wq.data_ptr(), wq.numel(), N, K, None, ctypes.byref(h))
+        mats.append(h)
+    torch.cuda.synchronize()
+    del w32, wq
+    X = torch.empty(M * K, dtype=torch.float32, device=dev)
+    call("hc_synth_normal_dev", 5, 5, 0, M * K, 1.0, X.data_ptr(), None)
+    Y = torch.empty(M * N, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def run(i):
+        call("hc_q4_matmul_dev", mats[i % copies], X.data_ptr(), M, Y.data_ptr(), stream)
+
+    for i in range(6):
+        run(i)
+    ms = cuda_time_ms(stream, run, reps)
+    for h in mats:
+        call("hc_q4_matrix_free", h)
+    algo = 0.5625 * N * K + 4.0 * M * K + 4.0 * M * N
+    peak, src = measured_peaks()
+    achieved = algo / (ms * 1e-3) / 1e9
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "gemv_gateup_traffic.json")
+    if os.path.exists(tp):
+        with open(tp) as f:
+            traffic = json.load(f).get("dram_bytes_per_launch")
+    return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+            "frac": round(achieved / peak, 4), "traffic": traffic,
+            "kernel": f"q4_0 matmul N={N} K={K} M={M}", "algorithmic_bytes": int(algo),
+            "avg_launch_us": round(ms * 1e3, 2), "peak_source": f"{src} (hbm_gbs)"}
+
+
+def cpu_baseline(img, cfg, budget_s=12.0, max_tokens=24):
+    """The oracle decoding one sequence at context 2048 on the host cores."""
+    from oracle import oracle as orc
+    om = orc.OracleModel(img)
+    kv = om.new_kv(cfg["max_pos"])
+    kv.set_pos(cfg["prompt"])
+    orc.model_forward(om, 1, kv)  # warm-up
+    n = 0
+    t0 = time.perf_counter()
+    while n < max_tokens and (time.perf_counter() - t0) < budget_s:
+        orc.model_forward(om, 1 + n, kv)
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": round(n / dt, 3), "unit": UNIT, "cores": orc.lib().orc_num_threads(), "kind": "port",
+            "sample": f"c4 model_forward, 1 sequence at context {cfg['prompt']} (KV positions set, zero-filled), "
+                      f"{n} tokens in {dt:.1f} s; the reference serialises sequences (serve.rs:175,193)"}
+
+
+def workload_config(world):
+    return {"workload": "c4 decode: Llama-3-8B shape (hidden 4096, 32 layers, 32/8 heads, im 14336, vocab 128256), "
+                        "32 sequences each prefilled with 2048 random tokens, greedy batched decode, fp16 KV",
+            "model": "llama-3-8b-shape-random-q4_0", "global_batch": 32 * world, "seq_len": 2048,
+            "parallelism": f"replicas{world}" if world > 1 else "single",
+            "l2": "inputs larger than L2 (4.22 GB of Q4_0 weights + ~8.6 GB KV read per step)"}
+
+
+def run_ours(args):
+    import torch
+    rank, world, local = _env_int("RANK", 0), _env_int("WORLD_SIZE", 1), _env_int("LOCAL_RANK", 0)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+    from hypno_b200 import build, engine, synth
+    from hypno_b200._lib import call, load
+    if rank == 0:
+        build.build()
+    if dist:
+        dist.barrier()
+    lib = load()
+    call("hc_set_device", local)
+    cfg = synth.CONFIGS["c4"]
+    S, P = cfg["seqs"], cfg["prompt"]
+    img = synth.build_image(cfg, seed=0, device=dev)
+    model = engine.HypnoModel(img)
+    if rank != 0:
+        del img
+        img = None
+    kv = engine.KVCache(model, n_seqs=S, max_pos=cfg["max_pos"], kv_dtype=engine.KV_FP16)
+    stream = model.stream
+
+    # ---- prefill (32 prompts), device-timed
+    prompts = [synth.prompt_ids(cfg["vocab"], P, seed=s) for s in range(S)]
+    first = np.empty(S, np.uint32)
+    import torch.cuda as tc
+    e0, e1 = tc.Event(enable_timing=True), tc.Event(enable_timing=True)
+    es = torch.cuda.ExternalStream(stream)
+    torch.cuda.synchronize()
+    e0.record(es)
+    for s in range(S):
+        logits = engine.batch_forward(model, prompts[s], kv, seq=s)
+        first[s] = int(np.nonzero(logits == logits.max())[0][-1])
+    e1.record(es)
+    torch.cuda.synchronize()
+    prefill_ms = e0.elapsed_time(e1)
+    prefill_tok_s = S * P / (prefill_ms * 1e-3)
+
+    # ---- decode, device-resident inputs
+    seqs_dev = torch.arange(S, dtype=torch.int32, device=dev)
+    ids_dev = torch.from_numpy(first.astype(np.int32)).to(dev)
+
+    def step(_i):
+        call("hc_decode_step_dev", model.handle, kv.handle, seqs_dev.data_ptr(), ids_dev.data_ptr(), S, None,
+             ids_dev.data_ptr())
+
+    def reset_pos():
+        for s in range(S):
+            kv.set_pos(P, s)
+
+    for i in range(args.warmup):
+        step(i)
+    reset_pos()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    l0 = lib.hc_kernel_launches()
+    with ClockSampler(local, os.path.join(ROOT, "gpurun_out", f"clocks_rank{rank}.csv")
+                      if os.path.isdir(os.path.join(ROOT, "gpurun_out")) else f"/tmp/hc_clocks_{rank}.csv") as clk:
+        ms = cuda_time_ms(stream, step, args.steps) * args.steps
+        torch.cuda.synchronize()
+    launches = lib.hc_kernel_launches() - l0
+    if dist:
+        dist.barrier()
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = world * S * args.steps / (ms * 1e-3)
+
+    # ---- end to end through the host-buffer C ABI call
+    reset_pos()
+    h_seqs = torch.arange(S, dtype=torch.int32).pin_memory()
+    h_ids = torch.from_numpy(first.astype(np.int32)).pin_memory()
+    h_out = torch.empty(S, dtype=torch.int32).pin_memory()
+    for _ in range(2):
+        call("hc_decode_step", model.handle, kv.handle, h_seqs.data_ptr(), h_ids.data_ptr(), S, None,
+             h_out.data_ptr())
+        h_ids.copy_(h_out)
+    reset_pos()
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        call("hc_decode_step", model.handle, kv.handle, h_seqs.data_ptr(), h_ids.data_ptr(), S, None,
+             h_out.data_ptr())
+        h_ids.copy_(h_out)
+    e2e_s = time.perf_counter() - t0
+    if dist:
+        t = torch.tensor([e2e_s], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e = {"value": round(world * S * args.steps / e2e_s, 2), "unit": UNIT,
+           "h2d_bytes_per_step": 2 * 4 * S, "d2h_bytes_per_step": 4 * S}
+
+    roof = roofline_gemv(dev) if rank == 0 else None
+    cpu = None
+    if rank == 0 and not args.no_cpu:
+        cpu = cpu_baseline(img, cfg)
+    if dist:
+        dist.barrier()
+    if rank == 0:
+        line = {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "q4_0 weights, f32 compute", "data": "synthetic",
+                "config": workload_config(world), "e2e": e2e, "gpu_launches": int(launches),
+                "prefill_tok_s": round(prefill_tok_s, 1), "clocks": clk.summary(), "roofline": roof,
+                "cpu_baseline": cpu}
+        print(json.dumps(line), flush=True)
+    kv.close()
+    model.close()
+    if dist:
+        dist.destroy_process_group()
+
+
+def run_reference(args):
+    rank, world = _env_int("RANK", 0), _env_int("WORLD_SIZE", 1)
+    if rank != 0:
+        return
+    from hypno_b200 import synth
+    from oracle import oracle as orc
+    cfg = synth.CONFIGS["c4"]
+    img = synth.build_image(cfg, seed=0, quantize=orc.quantize_f32_to_q4_0)
+    om = orc.OracleModel(img)
+    kv = om.new_kv(cfg["max_pos"])
+    kv.set_pos(cfg["prompt"])
+    for i in range(args.warmup):
+        orc.model_forward(om, 1 + i, kv)
+    kv.set_pos(cfg["prompt"])
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        orc.model_forward(om, 1 + i, kv)
+    dt = time.perf_counter() - t0
+    v = args.steps / dt
+    cpu = {"value": round(v, 3), "unit": UNIT, "cores": orc.lib().orc_num_threads(), "kind": "port",
+           "sample": f"each step = one model_forward of one sequence at context {cfg['prompt']} (the reference "
+                     f"decodes sequences one at a time, serve.rs:175,193); {args.steps} steps in {dt:.1f} s"}
+    line = {"impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 2),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "q4_0 weights, f32 compute",
+            "data": "synthetic", "config": workload_config(world), "cpu_baseline": cpu,
+            "e2e": {"value": round(v, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=40)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.steps + args.warmup > 250:
+        ap.error("steps + warmup must fit the 256 decode positions of the c4 workload")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

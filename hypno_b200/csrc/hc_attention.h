@@ -1,0 +1,36 @@
+// Attention / KV-cache launch interface (see hc_attention.cu).
+#pragma once
+#include "hc_internal.h"
+
+namespace hc {
+
+struct AttnParams {
+    const float* q;       // query rows; head h at q + row*ldq + h*hd
+    size_t ldq;
+    float* out;           // output rows; head h at out + row*ldo + h*hd
+    size_t ldo;
+    const float* vself;   // f32 V of the row's own token; kv head at + kvh*hd
+    size_t ldself;
+    int nh, nkv, hd;
+    float scale;          // 1/sqrt(hd)
+    int smem_n;           // capacity of the score buffer (>= max positions attended)
+    int mode_prefill;     // 1: K/V rows come from kp/vp (prompt-relative)
+    // decode source: cache[seq][layer][kvh][max_pos][hd], already offset to the layer
+    const void* kc;
+    const void* vc;
+    size_t seq_stride, head_stride;
+    const int* seqs;      // row -> sequence
+    const int* pos;       // sequence -> cached positions before this step
+    // prefill source: f32 K/V rows of the prompt with row stride ldkv
+    const float* kp;
+    const float* vp;
+    size_t ldkv;
+};
+
+int launch_attention(const AttnParams& P, int rows, int kv_fp16, cudaStream_t s);
+int launch_kv_store(const float* k, const float* v, size_t ld, int rows, int nkv, int hd, void* kc, void* vc,
+                    int kv_fp16, size_t seq_stride, size_t head_stride, int max_pos, const int* seqs,
+                    const int* pos, int fixed_seq, int pos0, cudaStream_t s);
+int launch_advance(const int* seqs, int* pos, int B, cudaStream_t s);
+
+}  // namespace hc

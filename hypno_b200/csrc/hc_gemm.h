@@ -1,0 +1,19 @@
+// Tensor-core (tcgen05) Q4_0 GEMM interface (see hc_gemm_tc.cu).
+#pragma once
+#include "hc_internal.h"
+
+namespace hc {
+
+struct GemmWorkspace;
+GemmWorkspace* gemm_workspace_new();
+void gemm_workspace_free(GemmWorkspace* ws);
+
+// True when Y = X . W^T for `tokens` rows should run on the tcgen05 path.
+bool gemm_tc_eligible(const hc_q4_matrix& w, size_t tokens);
+
+// Y[t][n] (+)= sum_k X[t][k] * deq(W)[n][k] for t < tokens, fp16 operands and
+// f32 accumulation in tensor memory; same epilogue contract as launch_matmul.
+int gemm_tc(GemmWorkspace* ws, const hc_q4_matrix& w, const float* x, size_t ldx, size_t tokens, float* y,
+            size_t ldy, int epi, const float* res, size_t ldres, cudaStream_t s);
+
+}  // namespace hc

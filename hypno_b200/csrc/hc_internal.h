@@ -1,0 +1,118 @@
+// Internal declarations shared by the translation units of libhypno_cuda.so.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+#include <stddef.h>
+#include <string>
+#include <vector>
+
+#include "../../include/hypno_cuda.h"
+
+#define HC_EXPORT extern "C" __attribute__((visibility("default")))
+
+// ---------------------------------------------------------------- errors
+void hc_set_error(const char* fmt, ...);
+int hc_cuda_fail(cudaError_t e, const char* what, const char* file, int line);
+
+#define HC_CUDA(call)                                                              \
+    do {                                                                           \
+        cudaError_t _e = (call);                                                   \
+        if (_e != cudaSuccess) return hc_cuda_fail(_e, #call, __FILE__, __LINE__); \
+    } while (0)
+
+#define HC_CHECK(cond, code, ...)         \
+    do {                                  \
+        if (!(cond)) {                    \
+            hc_set_error(__VA_ARGS__);    \
+            return (code);                \
+        }                                 \
+    } while (0)
+
+#define HC_TRY(expr)             \
+    do {                         \
+        int _r = (expr);         \
+        if (_r != HC_OK) return _r; \
+    } while (0)
+
+// Launch-error check after a kernel launch; also counts the launch (every
+// kernel launch of the library is followed by this macro).
+void hc_count_launch();
+#define HC_LAUNCH_CHECK()          \
+    do {                           \
+        hc_count_launch();         \
+        HC_CUDA(cudaGetLastError()); \
+    } while (0)
+
+// ---------------------------------------------------------------- Q4_0 matrix
+// Device layout of a Q4_0 tensor.  The .hypno payload is a sequence of
+// 18-byte blocks (f16 scale + 16 nibble bytes) over the flattened row-major
+// tensor (quant.rs:10-18, kernels.rs:273-283).  On the device the blocks are
+// split into two planes so every load is aligned and coalesced:
+//   qs[b]  : 16 nibble bytes of block b (uint4, 16-byte aligned)
+//   sc[b]  : fp16 scale of block b
+// Block order is unchanged (flattened row-major), so for k % 32 == 0 row r
+// owns blocks [r*k/32, (r+1)*k/32).  The split is exactly invertible.
+struct hc_q4_matrix {
+    size_t n = 0, k = 0, nblocks = 0;
+    uint4* qs = nullptr;
+    __half* sc = nullptr;
+    bool owns = true;
+};
+
+// Dense weight of any supported dtype resident in HBM.
+struct DevWeight {
+    uint32_t dtype = 0;  // HC_DTYPE_*
+    size_t n = 0, k = 0;
+    hc_q4_matrix q4;     // dtype == Q4_0
+    void* dense = nullptr;  // FP32 / FP16 payload
+    bool present = false;
+};
+
+// ---------------------------------------------------------------- kernels
+namespace hc {
+
+enum Epi : int { EPI_STORE = 0, EPI_ADD = 1 };
+
+// Q4_0 pack / unpack / repack (bit-exact with quant.rs).
+int launch_q4_quantize(const float* x, size_t nblocks, uint8_t* out, cudaStream_t s);
+int launch_q4_dequantize(const uint8_t* q, size_t nblocks, float* out, cudaStream_t s);
+int launch_q4_split(const uint8_t* aos, size_t nblocks, uint4* qs, __half* sc, cudaStream_t s);
+
+// Y[m][n] (+)= X[m][:] . W[n][:]  for m < mtok.  ldx/ldy in floats.
+// res (may alias y, may be null) is added when epi == EPI_ADD: y = acc + res.
+int launch_matmul(const DevWeight& w, const float* x, size_t ldx, size_t mtok, float* y, size_t ldy,
+                  int epi, const float* res, size_t ldres, cudaStream_t s);
+
+// Row-wise RMSNorm (kernels.rs:592-625): out[r] = x[r] * inv_rms(x[r]) * w.
+int launch_rmsnorm(const float* x, size_t ldx, const float* w, float* out, size_t ldo, size_t rows,
+                   size_t n, float eps, cudaStream_t s);
+int launch_softmax_rows(float* x, size_t rows, size_t n, cudaStream_t s);
+int launch_silu(float* x, size_t n, cudaStream_t s);
+// act[r][i] = silu(gu[r][i]) * gu[r][im + i]
+int launch_silu_mul(const float* gu, size_t ldgu, float* act, size_t ldact, size_t rows, size_t im,
+                    cudaStream_t s);
+// Rotation of `heads` adjacent-pair heads per row at position pos0 + row
+// using a (max_pos x hd/2) cos/sin table.
+int launch_rope_rows(float* x, size_t ldx, size_t rows, size_t heads, size_t hd, const float2* cs, size_t cs_rows,
+                     const int* pos_dev, int pos0, cudaStream_t s);
+
+// Embedding gather for B ids (FP32 / FP16 / Q4_0 rows of width hidden).
+int launch_embed(const DevWeight& emb, const uint32_t* ids, size_t B, float* out, size_t hidden,
+                 cudaStream_t s);
+int launch_argmax(const float* logits, size_t rows, size_t n, uint32_t* out, cudaStream_t s);
+
+// Synthetic normal stream (host and device versions agree bit for bit).
+int launch_synth_normal(uint64_t seed, uint64_t stream, uint64_t offset, uint64_t n, float std,
+                        float* out, cudaStream_t s);
+
+}  // namespace hc
+
+// RoPE angle table computed on the host with the C library's powf/cosf/sinf
+// (the functions Rust's f32 methods call on Linux), transformer.rs:317-343.
+std::vector<float2> hc_rope_table(size_t max_pos, size_t hd, float theta);
+
+// Host-side f16 helpers.
+uint16_t hc_f32_to_f16_host(float f);
+float hc_f16_to_f32_host(uint16_t h);

@@ -1,0 +1,525 @@
+// CUDA kernels of the hypno sm_100a backend (CUDA-core part): Q4_0 pack /
+// unpack / repack, the Q4_0 matvec for small token counts, RMSNorm, softmax,
+// SiLU, RoPE, embedding gather, argmax and the seeded synthetic generator.
+// The tensor-core GEMM lives in hc_gemm_tc.cu and attention in hc_attention.cu.
+#include "hc_internal.h"
+#include "hc_common.cuh"
+
+#include <algorithm>
+#include <math.h>
+
+namespace hc {
+
+// ============================================================ Q4_0 pack/unpack
+
+// Q4_0Block::quantize (quant.rs:49-71), one thread per 32-element block:
+// scale = max|x|/7 in f32 (1.0 for an all-zero block), stored as f16 (RNE);
+// q = clamp(round_half_away(x / scale_f32), -8, 7) + 8, low nibble = even
+// element.  IEEE division and roundf keep it bit-exact.
+__global__ void k_q4_quantize(const float* __restrict__ x, size_t nblocks, uint8_t* __restrict__ out) {
+    size_t b = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= nblocks) return;
+    const float* src = x + b * 32;
+    float v[32];
+#pragma unroll
+    for (int i = 0; i < 32; i++) v[i] = src[i];
+    float max_abs = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 32; i++) max_abs = fmaxf(max_abs, fabsf(v[i]));
+    float scale = (max_abs > 0.0f) ? __fdiv_rn(max_abs, 7.0f) : 1.0f;
+    __half h = __float2half_rn(scale);
+    uint16_t hb = __half_as_ushort(h);
+    uint8_t* o = out + b * 18;
+    o[0] = (uint8_t)(hb & 0xFF);
+    o[1] = (uint8_t)(hb >> 8);
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+        float r0 = roundf(__fdiv_rn(v[2 * i], scale));
+        float r1 = roundf(__fdiv_rn(v[2 * i + 1], scale));
+        int q0 = isnan(r0) ? 0 : (int)fminf(fmaxf(r0, -8.0f), 7.0f);
+        int q1 = isnan(r1) ? 0 : (int)fminf(fmaxf(r1, -8.0f), 7.0f);
+        o[2 + i] = (uint8_t)(((q0 + 8) & 0x0F) | (((q1 + 8) & 0x0F) << 4));
+    }
+}
+
+// Q4_0Block::dequantize (quant.rs:25-34): (nibble - 8) * scale, exact in f32.
+__global__ void k_q4_dequantize(const uint8_t* __restrict__ q, size_t nblocks, float* __restrict__ out) {
+    size_t b = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= nblocks) return;
+    const uint8_t* blk = q + b * 18;
+    float scale = __half2float(__ushort_as_half((uint16_t)(blk[0] | (blk[1] << 8))));
+    float* dst = out + b * 32;
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+        uint8_t byte = blk[2 + i];
+        dst[2 * i] = (float)((int)(byte & 0x0F) - 8) * scale;
+        dst[2 * i + 1] = (float)((int)(byte >> 4) - 8) * scale;
+    }
+}
+
+// AoS 18-byte blocks -> nibble plane (uint4 per block) + scale plane.
+__global__ void k_q4_split(const uint8_t* __restrict__ aos, size_t nblocks, uint4* __restrict__ qs,
+                           __half* __restrict__ sc) {
+    size_t b = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= nblocks) return;
+    const uint8_t* blk = aos + b * 18;
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+        w[i] = (uint32_t)blk[2 + 4 * i] | ((uint32_t)blk[3 + 4 * i] << 8) | ((uint32_t)blk[4 + 4 * i] << 16) |
+               ((uint32_t)blk[5 + 4 * i] << 24);
+    qs[b] = make_uint4(w[0], w[1], w[2], w[3]);
+    sc[b] = __ushort_as_half((uint16_t)(blk[0] | (blk[1] << 8)));
+}
+
+static inline unsigned grid_for(size_t n, unsigned threads) {
+    return (unsigned)((n + threads - 1) / threads);
+}
+
+int launch_q4_quantize(const float* x, size_t nblocks, uint8_t* out, cudaStream_t s) {
+    if (nblocks == 0) return HC_OK;
+    k_q4_quantize<<<grid_for(nblocks, 128), 128, 0, s>>>(x, nblocks, out);
+    HC_LAUNCH_CHECK();
+    return HC_OK;
+}
+int launch_q4_dequantize(const uint8_t* q, size_t nblocks, float* out, cudaStream_t s) {
+    if (nblocks == 0) return HC_OK;
+    k_q4_dequantize<<<grid_for(nblocks, 128), 128, 0, s>>>(q, nblocks, out);
+    HC_LAUNCH_CHECK();
+    return HC_OK;
+}
+int launch_q4_split(const uint8_t* aos, size_t nblocks, uint4* qs, __half* sc, cudaStream_t s) {
+    if (nblocks == 0) return HC_OK;
+    k_q4_split<<<grid_for(nblocks, 256), 256, 0, s>>>(aos, nblocks, qs, sc);
+    HC_LAUNCH_CHECK();
+    return HC_OK;
+}
+
+// ============================================================ Q4_0 matvec
+//
+// y[m][row] = sum_b scale[row,b] * sum_j (nib[row,b,j] - 8) * x[m][32b + j]
+// for k % 32 == 0 (blocks aligned with rows).  A row group of TPR threads
+// shares a row set of R rows: thread `li` walks blocks li, li+TPR, ... so a
+// warp's 16-byte nibble loads of one row are contiguous.  The x block (32
+// floats) is loaded once per block and reused for the R rows; up to MT
+// tokens are handled per pass.  The per-block dot is formed exactly on
+// integers-as-floats and folded in with one fma by the f32 scale.
+
+__device__ __forceinline__ float nib_f(uint32_t w, int j) {
+    // (nibble j of w) - 8 as an exact float: 2^23 + nib built by bit-or, then
+    // 2^23 + 8 subtracted.
+    return __int_as_float(0x4B000000 | ((w >> (4 * j)) & 0xF)) - 8388616.0f;
+}
+
+__device__ __forceinline__ float q4_block_dot(uint4 q, const float* xv) {
+    float d0 = 0.0f, d1 = 0.0f, d2 = 0.0f, d3 = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        d0 = fmaf(nib_f(q.x, j), xv[j], d0);
+        d1 = fmaf(nib_f(q.y, j), xv[8 + j], d1);
+        d2 = fmaf(nib_f(q.z, j), xv[16 + j], d2);
+        d3 = fmaf(nib_f(q.w, j), xv[24 + j], d3);
+    }
+    return (d0 + d1) + (d2 + d3);
+}
+
+template <int TPR, int R, int MT>
+__global__ void __launch_bounds__(128) k_q4_gemv(const uint4* __restrict__ qs, const __half* __restrict__ sc,
+                                                 const float* __restrict__ x, size_t ldx, int mtok,
+                                                 float* __restrict__ y, size_t ldy, int epi,
+                                                 const float* res, size_t ldres, int N, int KB) {
+    constexpr int GROUPS = 128 / TPR;
+    const int g = threadIdx.x / TPR, li = threadIdx.x % TPR;
+    const int row0 = (blockIdx.x * GROUPS + g) * R;
+    for (int m0 = 0; m0 < mtok; m0 += MT) {
+        float acc[R][MT];
+#pragma unroll
+        for (int r = 0; r < R; r++)
+#pragma unroll
+            for (int t = 0; t < MT; t++) acc[r][t] = 0.0f;
+        for (int b = li; b < KB; b += TPR) {
+            uint4 q[R];
+            float s[R];
+#pragma unroll
+            for (int r = 0; r < R; r++) {
+                int row = min(row0 + r, N - 1);
+                size_t bi = (size_t)row * KB + b;
+                q[r] = __ldg(qs + bi);
+                s[r] = __half2float(sc[bi]);
+            }
+#pragma unroll
+            for (int t = 0; t < MT; t++) {
+                if (m0 + t < mtok) {
+                    const float4* xp = reinterpret_cast<const float4*>(x + (size_t)(m0 + t) * ldx + (size_t)b * 32);
+                    float xv[32];
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        float4 f = __ldg(xp + i);
+                        xv[4 * i] = f.x; xv[4 * i + 1] = f.y; xv[4 * i + 2] = f.z; xv[4 * i + 3] = f.w;
+                    }
+#pragma unroll
+                    for (int r = 0; r < R; r++) acc[r][t] = fmaf(s[r], q4_block_dot(q[r], xv), acc[r][t]);
+                }
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < R; r++)
+#pragma unroll
+            for (int t = 0; t < MT; t++) {
+                float v = acc[r][t];
+#pragma unroll
+                for (int o = TPR / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                acc[r][t] = v;
+            }
+        if (li == 0) {
+#pragma unroll
+            for (int r = 0; r < R; r++) {
+                int row = row0 + r;
+                if (row >= N) continue;
+#pragma unroll
+                for (int t = 0; t < MT; t++) {
+                    int m = m0 + t;
+                    if (m >= mtok) continue;
+                    float v = acc[r][t];
+                    if (epi == EPI_ADD && res) v = v + res[(size_t)m * ldres + row];
+                    y[(size_t)m * ldy + row] = v;
+                }
+            }
+        }
+    }
+}
+
+// General Q4_0 matvec for k % 32 != 0: blocks straddle row boundaries
+// (kernels.rs:281-349).  One warp per (row, token); element e of the
+// flattened tensor uses block e/32, nibble e%32.
+__global__ void k_q4_gemv_general(const uint4* __restrict__ qs, const __half* __restrict__ sc, size_t nblocks,
+                                  const float* __restrict__ x, size_t ldx, int mtok, float* __restrict__ y,
+                                  size_t ldy, int epi, const float* res, size_t ldres, int N, int K) {
+    int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (warp >= N * mtok) return;
+    int row = warp % N, m = warp / N;
+    const uint8_t* qb = reinterpret_cast<const uint8_t*>(qs);
+    float acc = 0.0f;
+    for (int i = lane; i < K; i += 32) {
+        size_t e = (size_t)row * K + i;
+        size_t b = e >> 5;
+        if (b >= nblocks) break;
+        int j = (int)(e & 31);
+        uint8_t byte = qb[b * 16 + (j >> 1)];
+        int nib = (j & 1) ? (byte >> 4) : (byte & 0xF);
+        float deq = (float)(nib - 8) * __half2float(sc[b]);
+        acc = fmaf(deq, x[(size_t)m * ldx + i], acc);
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) {
+        if (epi == EPI_ADD && res) acc = acc + res[(size_t)m * ldres + row];
+        y[(size_t)m * ldy + row] = acc;
+    }
+}
+
+// FP32 / FP16 weight matvec (kernels.rs:69-241, 537-586): one warp per
+// (row, token).
+template <typename T>
+__device__ __forceinline__ float ld_as_f32(const T* p);
+template <>
+__device__ __forceinline__ float ld_as_f32<float>(const float* p) { return __ldg(p); }
+template <>
+__device__ __forceinline__ float ld_as_f32<__half>(const __half* p) { return __half2float(*p); }
+
+template <typename T>
+__global__ void k_dense_gemv(const T* __restrict__ w, const float* __restrict__ x, size_t ldx, int mtok,
+                             float* __restrict__ y, size_t ldy, int epi, const float* res, size_t ldres, int N,
+                             int K) {
+    int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (warp >= N * mtok) return;
+    int row = warp % N, m = warp / N;
+    const T* wr = w + (size_t)row * K;
+    const float* xr = x + (size_t)m * ldx;
+    float acc = 0.0f;
+    for (int i = lane; i < K; i += 32) acc = fmaf(ld_as_f32<T>(wr + i), xr[i], acc);
+    acc = warp_sum(acc);
+    if (lane == 0) {
+        if (epi == EPI_ADD && res) acc = acc + res[(size_t)m * ldres + row];
+        y[(size_t)m * ldy + row] = acc;
+    }
+}
+
+template <int TPR, int R, int MT>
+static void launch_gemv_t(const hc_q4_matrix& w, const float* x, size_t ldx, size_t mtok, float* y, size_t ldy,
+                          int epi, const float* res, size_t ldres, cudaStream_t s) {
+    constexpr int GROUPS = 128 / TPR;
+    int rows_per_cta = GROUPS * R;
+    unsigned grid = (unsigned)((w.n + rows_per_cta - 1) / rows_per_cta);
+    k_q4_gemv<TPR, R, MT><<<grid, 128, 0, s>>>(w.qs, w.sc, x, ldx, (int)mtok, y, ldy, epi, res, ldres, (int)w.n,
+                                               (int)(w.k / 32));
+}
+
+template <int TPR>
+static void launch_gemv_tpr(const hc_q4_matrix& w, const float* x, size_t ldx, size_t mtok, float* y, size_t ldy,
+                            int epi, const float* res, size_t ldres, cudaStream_t s) {
+    // Rows per thread: 4 when there are enough rows for ~2 waves, else 1.
+    size_t ctas4 = (w.n + (128 / TPR) * 4 - 1) / ((128 / TPR) * 4);
+    bool big = ctas4 >= 296;
+    if (mtok == 1) {
+        if (big) launch_gemv_t<TPR, 4, 1>(w, x, ldx, mtok, y, ldy, epi, res, ldres, s);
+        else launch_gemv_t<TPR, 1, 1>(w, x, ldx, mtok, y, ldy, epi, res, ldres, s);
+    } else if (mtok <= 4) {
+        if (big) launch_gemv_t<TPR, 2, 4>(w, x, ldx, mtok, y, ldy, epi, res, ldres, s);
+        else launch_gemv_t<TPR, 1, 4>(w, x, ldx, mtok, y, ldy, epi, res, ldres, s);
+    } else {
+        launch_gemv_t<TPR, 1, 8>(w, x, ldx, mtok, y, ldy, epi, res, ldres, s);
+    }
+}
+
+int launch_matmul(const DevWeight& w, const float* x, size_t ldx, size_t mtok, float* y, size_t ldy, int epi,
+                  const float* res, size_t ldres, cudaStream_t s) {
+    if (mtok == 0 || w.n == 0) return HC_OK;
+    if (w.dtype == HC_DTYPE_Q4_0) {
+        const hc_q4_matrix& q = w.q4;
+        bool aligned = (q.k % 32 == 0) && (((uintptr_t)x & 15) == 0) && (ldx % 4 == 0) &&
+                       (q.nblocks >= q.n * (q.k / 32));
+        if (aligned) {
+            size_t kb = q.k / 32;
+            if (kb >= 32) launch_gemv_tpr<32>(q, x, ldx, mtok, y, ldy, epi, res, ldres, s);
+            else if (kb >= 16) launch_gemv_tpr<16>(q, x, ldx, mtok, y, ldy, epi, res, ldres, s);
+            else launch_gemv_tpr<8>(q, x, ldx, mtok, y, ldy, epi, res, ldres, s);
+        } else {
+            size_t warps = q.n * mtok;
+            k_q4_gemv_general<<<grid_for(warps * 32, 256), 256, 0, s>>>(q.qs, q.sc, q.nblocks, x, ldx, (int)mtok, y,
+                                                                        ldy, epi, res, ldres, (int)q.n, (int)q.k);
+        }
+    } else if (w.dtype == HC_DTYPE_FP32) {
+        size_t warps = w.n * mtok;
+        k_dense_gemv<float><<<grid_for(warps * 32, 256), 256, 0, s>>>((const float*)w.dense, x, ldx, (int)mtok, y,
+                                                                      ldy, epi, res, ldres, (int)w.n, (int)w.k);
+    } else if (w.dtype == HC_DTYPE_FP16) {
+        size_t warps = w.n * mtok;
+        k_dense_gemv<__half><<<grid_for(warps * 32, 256), 256, 0, s>>>((const __half*)w.dense, x, ldx, (int)mtok,
+                                                                       y, ldy, epi, res, ldres, (int)w.n, (int)w.k);
+    } else {
+        hc_set_error("matmul: unsupported weight dtype %u", w.dtype);
+        return HC_ERR_UNSUPPORTED;
+    }
+    HC_LAUNCH_CHECK();
+    return HC_OK;
+}
+
+// ============================================================ RMSNorm
+// kernels.rs:592-625: ms = sum(x^2)/n, inv = 1/sqrt(ms + eps), y = (x*inv)*w.
+__global__ void k_rmsnorm(const float* __restrict__ x, size_t ldx, const float* __restrict__ w,
+                          float* __restrict__ out, size_t ldo, int n, float eps) {
+    __shared__ float red[32];
+    const float* xr = x + (size_t)blockIdx.x * ldx;
+    float* orow = out + (size_t)blockIdx.x * ldo;
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
+    ss = block_sum(ss, red);
+    float ms = __fdiv_rn(ss, (float)n);
+    float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
+    for (int i = threadIdx.x; i < n; i += blockDim.x) orow[i] = __fmul_rn(__fmul_rn(xr[i], inv), w[i]);
+}
+
+int launch_rmsnorm(const float* x, size_t ldx, const float* w, float* out, size_t ldo, size_t rows, size_t n,
+                   float eps, cudaStream_t s) {
+    if (rows == 0) return HC_OK;
+    k_rmsnorm<<<(unsigned)rows, 256, 0, s>>>(x, ldx, w, out, ldo, (int)n, eps);
+    HC_LAUNCH_CHECK();
+    return HC_OK;
+}
+
+// ============================================================ softmax rows
+// softmax_fast (kernels.rs:631-668), one CTA per row.
+__global__ void k_softmax_rows(float* __restrict__ x, int n) {
+    __shared__ float red[32];
+    float* xr = x + (size_t)blockIdx.x * n;
+    float mx = -INFINITY;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) mx = fmaxf(mx, xr[i]);
+    mx = block_max(mx, red);
+    int n8 = n - (n % 8);
+    float sum = 0.0f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        float e = softmax_weight(xr[i], mx, i, n8);
+        xr[i] = e;
+        sum += e;
+    }
+    float total = block_sum(sum, red);
+    float inv = __fdiv_rn(1.0f, total);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) xr[i] = (i < n8) ? __fmul_rn(xr[i], inv) : __fdiv_rn(xr[i], total);
+}
+
+int launch_softmax_rows(float* x, size_t rows, size_t n, cudaStream_t s) {
+    if (rows == 0 || n == 0) return HC_OK;
+    k_softmax_rows<<<(unsigned)rows, 256, 0, s>>>(x, (int)n);
+    HC_LAUNCH_CHECK();
+    return HC_OK;
+}
+
+// ============================================================ SiLU
+__device__ __forceinline__ float silu_f(float v) { return __fdiv_rn(v, __fadd_rn(1.0f, expf(-v))); }
+
+__global__ void k_silu(float* __restrict__ x, size_t n) {
+    size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) x[i] = silu_f(x[i]);
+}
+
+int launch_silu(float* x, size_t n, cudaStream_t s) {
+    if (n == 0) return HC_OK;
+    k_silu<<<grid_for(n, 256), 256, 0, s>>>(x, n);
+    HC_LAUNCH_CHECK();
+    return HC_OK;
+}
+
+// transformer.rs:446-449 / turbo.rs:235-237: silu(gate) * up.
+__global__ void k_silu_mul(const float* __restrict__ gu, size_t ldgu, float* __restrict__ act, size_t ldact,
+                           int im) {
+    const float* g = gu + (size_t)blockIdx.y * ldgu;
+    float* a = act + (size_t)blockIdx.y * ldact;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < im; i += gridDim.x * blockDim.x)
+        a[i] = __fmul_rn(silu_f(g[i]), g[im + i]);
+}
+
+int launch_silu_mul(const float* gu, size_t ldgu, float* act, size_t ldact, size_t rows, size_t im,
+                    cudaStream_t s) {
+    if (rows == 0) return HC_OK;
+    unsigned gx = (unsigned)std::min<size_t>((im + 255) / 256, 64);
+    k_silu_mul<<<dim3(gx, (unsigned)rows), 256, 0, s>>>(gu, ldgu, act, ldact, (int)im);
+    HC_LAUNCH_CHECK();
+    return HC_OK;
+}
+
+// ============================================================ RoPE
+// Adjacent-pair rotation (ops.rs:86-99, transformer.rs:317-343,
+// turbo.rs:113-142) with the (cos, sin) of (pos as f32) * freq_i taken from a
+// table built by the host C library; the rotation itself is done with
+// separately rounded products (no fma), as in the reference.
+__global__ void k_rope_rows(float* __restrict__ x, size_t ldx, int heads, int hd, const float2* __restrict__ cs,
+                            int cs_rows, const int* __restrict__ pos_dev, int pos0) {
+    int row = blockIdx.y;
+    int pos = pos_dev ? pos_dev[row] : pos0 + row;
+    if (pos < 0 || pos >= cs_rows) return;  // beyond the cache: the position is rejected elsewhere
+    int half = hd / 2;
+    float* xr = x + (size_t)row * ldx;
+    for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < heads * half; p += gridDim.x * blockDim.x) {
+        int h = p / half, i = p % half;
+        float2 c = cs[(size_t)pos * half + i];
+        float* e = xr + (size_t)h * hd + 2 * i;
+        float a = e[0], b = e[1];
+        e[0] = __fsub_rn(__fmul_rn(a, c.x), __fmul_rn(b, c.y));
+        e[1] = __fadd_rn(__fmul_rn(a, c.y), __fmul_rn(b, c.x));
+    }
+}
+
+int launch_rope_rows(float* x, size_t ldx, size_t rows, size_t heads, size_t hd, const float2* cs, size_t cs_rows,
+                     const int* pos_dev, int pos0, cudaStream_t s) {
+    if (rows == 0 || heads == 0) return HC_OK;
+    size_t pairs = heads * hd / 2;
+    unsigned gx = (unsigned)std::min<size_t>((pairs + 127) / 128, 64);
+    k_rope_rows<<<dim3(gx, (unsigned)rows), 128, 0, s>>>(x, ldx, (int)heads, (int)hd, cs, (int)cs_rows, pos_dev,
+                                                         pos0);
+    HC_LAUNCH_CHECK();
+    return HC_OK;
+}
+
+// ============================================================ embedding
+// transformer.rs:477-500 / turbo.rs:40-66 / quant.rs:139-153.
+__global__ void k_embed(uint32_t dtype, const void* __restrict__ dense, const uint4* __restrict__ qs,
+                        const __half* __restrict__ sc, const uint32_t* __restrict__ ids, float* __restrict__ out,
+                        int hidden) {
+    int b = blockIdx.y;
+    size_t id = ids[b];
+    float* o = out + (size_t)b * hidden;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < hidden; i += gridDim.x * blockDim.x) {
+        float v;
+        if (dtype == HC_DTYPE_FP32) {
+            v = reinterpret_cast<const float*>(dense)[id * hidden + i];
+        } else if (dtype == HC_DTYPE_FP16) {
+            v = __half2float(reinterpret_cast<const __half*>(dense)[id * hidden + i]);
+        } else {
+            size_t blk = id * (hidden / 32) + (i >> 5);
+            int j = i & 31;
+            const uint8_t* qb = reinterpret_cast<const uint8_t*>(qs + blk);
+            uint8_t byte = qb[j >> 1];
+            int nib = (j & 1) ? (byte >> 4) : (byte & 0xF);
+            v = (float)(nib - 8) * __half2float(sc[blk]);
+        }
+        o[i] = v;
+    }
+}
+
+int launch_embed(const DevWeight& emb, const uint32_t* ids, size_t B, float* out, size_t hidden, cudaStream_t s) {
+    if (B == 0) return HC_OK;
+    if (!emb.present) {
+        HC_CUDA(cudaMemsetAsync(out, 0, B * hidden * sizeof(float), s));
+        return HC_OK;
+    }
+    if (emb.dtype == HC_DTYPE_Q4_0 && hidden % 32 != 0) {
+        hc_set_error("Q4_0 embedding needs hidden %% 32 == 0 (quant.rs:139-153)");
+        return HC_ERR_UNSUPPORTED;
+    }
+    unsigned gx = (unsigned)std::min<size_t>((hidden + 255) / 256, 32);
+    k_embed<<<dim3(gx, (unsigned)B), 256, 0, s>>>(emb.dtype, emb.dense, emb.q4.qs, emb.q4.sc, ids, out, (int)hidden);
+    HC_LAUNCH_CHECK();
+    return HC_OK;
+}
+
+// ============================================================ argmax
+// Greedy pick: the LAST maximal index wins (Iterator::max_by, run.rs:234-238).
+__global__ void k_argmax(const float* __restrict__ logits, int n, uint32_t* __restrict__ out) {
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    const float* l = logits + (size_t)blockIdx.x * n;
+    float best = -INFINITY;
+    int bi = -1;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        float v = l[i];
+        if (bi < 0 || v >= best) { best = v; bi = i; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (oi >= 0 && (bi < 0 || ov > best || (ov == best && oi > bi))) { best = ov; bi = oi; }
+    }
+    int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    if (lane == 0) { sv[w] = best; si[w] = bi; }
+    __syncthreads();
+    if (w == 0) {
+        int nw = blockDim.x >> 5;
+        best = lane < nw ? sv[lane] : -INFINITY;
+        bi = lane < nw ? si[lane] : -1;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            float ov = __shfl_xor_sync(0xffffffffu, best, o);
+            int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (oi >= 0 && (bi < 0 || ov > best || (ov == best && oi > bi))) { best = ov; bi = oi; }
+        }
+        if (lane == 0) out[blockIdx.x] = (uint32_t)(bi < 0 ? 0 : bi);
+    }
+}
+
+int launch_argmax(const float* logits, size_t rows, size_t n, uint32_t* out, cudaStream_t s) {
+    if (rows == 0) return HC_OK;
+    k_argmax<<<(unsigned)rows, 1024, 0, s>>>(logits, (int)n, out);
+    HC_LAUNCH_CHECK();
+    return HC_OK;
+}
+
+// ============================================================ synthetic data
+__global__ void k_synth_normal(uint64_t key, uint64_t offset, uint64_t n, float scale, float* __restrict__ out) {
+    uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (; i < n; i += stride) out[i] = synth_normal(key, offset + i, scale);
+}
+
+int launch_synth_normal(uint64_t seed, uint64_t stream, uint64_t offset, uint64_t n, float std, float* out,
+                        cudaStream_t s) {
+    if (n == 0) return HC_OK;
+    uint64_t key = synth_key(seed, stream);
+    float scale = std / 65536.0f;
+    unsigned grid = (unsigned)std::min<uint64_t>((n + 255) / 256, 148ull * 16);
+    k_synth_normal<<<grid, 256, 0, s>>>(key, offset, n, scale, out);
+    HC_LAUNCH_CHECK();
+    return HC_OK;
+}
+
+}  // namespace hc

@@ -1,0 +1,807 @@
+// Host runtime of the hypno sm_100a backend: .hypno image parsing, one-time
+// weight upload (Q4_0 repacked into nibble/scale planes, projections that share
+// an input concatenated), the device KV cache, and the two forward passes:
+// hc_prefill (turbo::batch_forward) and hc_decode_step (model_forward,
+// batched over sequences).
+#include "hc_internal.h"
+#include "hc_attention.h"
+#include "hc_gemm.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+// ============================================================ .hypno parsing
+// format.rs:1-131 and loader.rs:39-133: 16-byte header ("HYPN", version 1,
+// metadata count, tensor count), length-prefixed metadata strings, then the
+// tensor table (name, ndim, u64 shape, dtype u32, offset u64, len u64).
+namespace {
+
+struct TensorEntry {
+    uint32_t dtype = 0;
+    std::vector<uint64_t> shape;
+    uint64_t offset = 0, len = 0;
+};
+
+struct HypnoImage {
+    const uint8_t* data = nullptr;
+    size_t size = 0;
+    std::unordered_map<std::string, std::string> meta;
+    std::unordered_map<std::string, TensorEntry> tensors;
+
+    const TensorEntry* find(const std::string& name) const {
+        auto it = tensors.find(name);
+        return it == tensors.end() ? nullptr : &it->second;
+    }
+    const uint8_t* payload(const TensorEntry& t) const { return data + t.offset; }
+};
+
+int parse_image(const uint8_t* data, size_t size, HypnoImage& img) {
+    img.data = data;
+    img.size = size;
+    HC_CHECK(data != nullptr && size >= 16, HC_ERR_FORMAT, "hypno: buffer too short: needed 16 bytes, got %zu", size);
+    HC_CHECK(std::memcmp(data, "HYPN", 4) == 0, HC_ERR_FORMAT, "hypno: invalid magic bytes");
+    uint32_t ver, nkv, nt;
+    std::memcpy(&ver, data + 4, 4);
+    std::memcpy(&nkv, data + 8, 4);
+    std::memcpy(&nt, data + 12, 4);
+    HC_CHECK(ver == 1, HC_ERR_FORMAT, "hypno: unsupported format version %u (expected 1)", ver);
+    size_t cur = 16;
+    auto rd32 = [&](uint32_t& v) -> bool {
+        if (cur + 4 > size) return false;
+        std::memcpy(&v, data + cur, 4);
+        cur += 4;
+        return true;
+    };
+    auto rd64 = [&](uint64_t& v) -> bool {
+        if (cur + 8 > size) return false;
+        std::memcpy(&v, data + cur, 8);
+        cur += 8;
+        return true;
+    };
+    auto rdstr = [&](uint32_t len, std::string& s) -> bool {
+        if (cur + len > size) return false;
+        s.assign(reinterpret_cast<const char*>(data + cur), len);
+        cur += len;
+        return true;
+    };
+    for (uint32_t i = 0; i < nkv; i++) {
+        uint32_t kl, vl;
+        std::string k, v;
+        HC_CHECK(rd32(kl) && rdstr(kl, k) && rd32(vl) && rdstr(vl, v), HC_ERR_FORMAT,
+                 "hypno: buffer too short in metadata entry %u", i);
+        img.meta[k] = v;
+    }
+    for (uint32_t i = 0; i < nt; i++) {
+        uint32_t nl, ndim, dt;
+        std::string name;
+        TensorEntry t;
+        HC_CHECK(rd32(nl) && rdstr(nl, name) && rd32(ndim), HC_ERR_FORMAT, "hypno: buffer too short in tensor %u", i);
+        HC_CHECK(ndim <= 16, HC_ERR_FORMAT, "hypno: tensor '%s' has ndim %u", name.c_str(), ndim);
+        t.shape.resize(ndim);
+        for (uint32_t d = 0; d < ndim; d++)
+            HC_CHECK(rd64(t.shape[d]), HC_ERR_FORMAT, "hypno: buffer too short in tensor '%s'", name.c_str());
+        HC_CHECK(rd32(dt) && rd64(t.offset) && rd64(t.len), HC_ERR_FORMAT, "hypno: buffer too short in tensor '%s'",
+                 name.c_str());
+        HC_CHECK(dt <= 3, HC_ERR_FORMAT, "hypno: unknown dtype code: %u", dt);
+        HC_CHECK(t.offset <= size && t.offset + t.len <= size, HC_ERR_FORMAT,
+                 "hypno: invalid tensor offset %llu: out of file bounds (%zu)", (unsigned long long)t.offset, size);
+        t.dtype = dt;
+        // Duplicate names: the reference's linear find returns the first.
+        if (!img.tensors.count(name)) img.tensors.emplace(name, std::move(t));
+    }
+    return HC_OK;
+}
+
+bool meta_u64(const HypnoImage& img, const char* key, uint64_t& out) {
+    auto it = img.meta.find(key);
+    if (it == img.meta.end()) return false;
+    const char* s = it->second.c_str();
+    char* end = nullptr;
+    unsigned long long v = std::strtoull(s, &end, 10);
+    if (end == s || *end != 0) return false;  // str::parse::<usize> rejects junk
+    out = v;
+    return true;
+}
+
+bool meta_f32(const HypnoImage& img, const char* key, float& out) {
+    auto it = img.meta.find(key);
+    if (it == img.meta.end()) return false;
+    const char* s = it->second.c_str();
+    char* end = nullptr;
+    float v = std::strtof(s, &end);
+    if (end == s || *end != 0) return false;
+    out = v;
+    return true;
+}
+
+}  // namespace
+
+// ============================================================ host f16 / RoPE table
+
+uint16_t hc_f32_to_f16_host(float f) {
+    uint32_t x;
+    std::memcpy(&x, &f, 4);
+    uint32_t sign = (x >> 16) & 0x8000u, exp = (x >> 23) & 0xFFu, man = x & 0x7FFFFFu;
+    if (exp == 0xFF) return (uint16_t)(sign | 0x7C00u | (man ? 0x200u | (man >> 13) : 0));
+    int e = (int)exp - 112;
+    if (e >= 31) return (uint16_t)(sign | 0x7C00u);
+    if (e <= 0) {
+        if (exp == 0) return (uint16_t)sign;
+        uint32_t full = man | 0x800000u;
+        int sh = 14 - e;
+        if (sh > 24) return (uint16_t)sign;
+        uint32_t m = full >> sh, rem = full & ((1u << sh) - 1u), half = 1u << (sh - 1);
+        if (rem > half || (rem == half && (m & 1u))) m++;
+        return (uint16_t)(sign | m);
+    }
+    uint32_t m = man >> 13, rem = man & 0x1FFFu;
+    if (rem > 0x1000u || (rem == 0x1000u && (m & 1u))) m++;
+    return (uint16_t)((sign | ((uint32_t)e << 10)) + m);
+}
+
+float hc_f16_to_f32_host(uint16_t h) {
+    uint32_t sign = ((uint32_t)h & 0x8000u) << 16, exp = ((uint32_t)h >> 10) & 0x1Fu, man = (uint32_t)h & 0x3FFu;
+    uint32_t out;
+    if (exp == 0) {
+        if (man == 0) out = sign;
+        else {
+            int e = -1;
+            do { e++; man <<= 1; } while (!(man & 0x400u));
+            out = sign | ((uint32_t)(112 - e) << 23) | ((man & 0x3FFu) << 13);
+        }
+    } else if (exp == 0x1F) out = sign | 0x7F800000u | (man << 13);
+    else out = sign | ((exp + 112) << 23) | (man << 13);
+    float f;
+    std::memcpy(&f, &out, 4);
+    return f;
+}
+
+std::vector<float2> hc_rope_table(size_t max_pos, size_t hd, float theta) {
+    size_t half = hd / 2;
+    std::vector<float2> t(max_pos * half);
+    std::vector<float> freq(half);
+    for (size_t j = 0; j < half; j++) freq[j] = 1.0f / powf(theta, (float)(2 * j) / (float)hd);
+    for (size_t p = 0; p < max_pos; p++)
+        for (size_t j = 0; j < half; j++) {
+            float a = (float)p * freq[j];
+            t[p * half + j] = make_float2(cosf(a), sinf(a));
+        }
+    return t;
+}
+
+// ============================================================ model structures
+
+struct LayerW {
+    DevWeight qkv;   // rows: q (nq), k (nk), v (nk)
+    DevWeight o;     // [hidden x nq]
+    DevWeight gu;    // rows: gate (im), up (im)
+    DevWeight down;  // [hidden x im]
+    float* in_norm = nullptr;
+    float* post_norm = nullptr;
+};
+
+struct Scratch {
+    size_t cap_tokens = 0, cap_logit_rows = 0;
+    float *hidden = nullptr, *xn = nullptr, *qkv = nullptr, *attn = nullptr, *gu = nullptr, *act = nullptr;
+    float* logits = nullptr;
+    uint32_t* ids = nullptr;
+    int* seqs = nullptr;
+    int* rowpos = nullptr;
+    uint32_t* argmax = nullptr;
+};
+
+struct hc_model {
+    hc_config cfg{};
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    std::vector<LayerW> layers;
+    DevWeight embed, lm_head;
+    float* final_norm = nullptr;
+    float2* rope = nullptr;
+    size_t rope_rows = 0;
+    size_t nq = 0, nk = 0;  // q rows, k (= v) rows per shard
+    Scratch sc;
+    std::vector<void*> allocs;
+    hc::GemmWorkspace* gemm_ws = nullptr;
+};
+
+struct hc_kv {
+    bool host_stale = false;
+    hc_model* model = nullptr;
+    int n_seqs = 0, max_pos = 0, kv_fp16 = 0;
+    void* k = nullptr;
+    void* v = nullptr;
+    int* pos_dev = nullptr;
+    std::vector<int> pos_host;
+    size_t seq_stride = 0, head_stride = 0, layer_stride = 0;
+};
+
+static int sync_pos(hc_kv* kv);
+
+namespace {
+
+int dev_alloc(hc_model* m, void** p, size_t bytes) {
+    if (bytes == 0) bytes = 16;
+    cudaError_t e = cudaMalloc(p, bytes);
+    if (e != cudaSuccess) {
+        hc_set_error("cudaMalloc(%zu) failed: %s", bytes, cudaGetErrorString(e));
+        cudaGetLastError();
+        return HC_ERR_OOM;
+    }
+    m->allocs.push_back(*p);
+    return HC_OK;
+}
+
+// One dense 1-D f32 vector (norm weights): FP32 / FP16 converted, anything
+// else (or absent) -> ones (load_1d_f32, transformer.rs:250-264).
+int upload_norm(hc_model* m, const HypnoImage& img, const std::string& name, size_t len, float** out) {
+    std::vector<float> h(len, 1.0f);
+    const TensorEntry* t = img.find(name);
+    if (t && t->dtype == HC_DTYPE_FP32 && t->len >= len * 4) {
+        std::memcpy(h.data(), img.payload(*t), len * 4);
+    } else if (t && t->dtype == HC_DTYPE_FP16 && t->len >= len * 2) {
+        const uint8_t* p = img.payload(*t);
+        for (size_t i = 0; i < len; i++) h[i] = hc_f16_to_f32_host((uint16_t)(p[2 * i] | (p[2 * i + 1] << 8)));
+    }
+    HC_TRY(dev_alloc(m, (void**)out, len * 4));
+    HC_CUDA(cudaMemcpyAsync(*out, h.data(), len * 4, cudaMemcpyHostToDevice, m->stream));
+    HC_CUDA(cudaStreamSynchronize(m->stream));
+    return HC_OK;
+}
+
+struct Part {
+    const TensorEntry* t;
+    size_t row0, rows;  // rows of this tensor to take (TP shard)
+    size_t col0, cols;  // columns to take (TP shard of the K dim)
+};
+
+// Uploads the row concatenation of `parts` (each an [rows x k_full] slice) as
+// one device weight of shape [sum rows x cols].  All parts share dtype.
+int upload_weight(hc_model* m, const HypnoImage& img, const std::vector<Part>& parts, size_t k_full, DevWeight& w,
+                  uint8_t** staging, size_t* staging_cap) {
+    uint32_t dt = parts[0].t->dtype;
+    size_t n = 0, cols = parts[0].cols;
+    for (auto& p : parts) {
+        HC_CHECK(p.t->dtype == dt, HC_ERR_UNSUPPORTED, "fused weight parts must share a dtype");
+        HC_CHECK(p.cols == cols, HC_ERR_INVALID, "fused weight parts must share a width");
+        n += p.rows;
+    }
+    w.dtype = dt;
+    w.n = n;
+    w.k = cols;
+    w.present = true;
+    if (dt == HC_DTYPE_Q4_0) {
+        bool full_cols = (parts[0].col0 == 0 && cols == k_full);
+        HC_CHECK(k_full % 32 == 0 || (parts.size() == 1 && full_cols && parts[0].row0 == 0), HC_ERR_UNSUPPORTED,
+                 "Q4_0 weights with width %% 32 != 0 cannot be fused or sharded");
+        HC_CHECK(cols % 32 == 0 || full_cols, HC_ERR_UNSUPPORTED, "Q4_0 shard width must be a multiple of 32");
+        size_t total_blocks;
+        if (k_full % 32 == 0) total_blocks = n * (cols / 32);
+        else total_blocks = parts[0].t->len / 18;
+        w.q4.n = n;
+        w.q4.k = cols;
+        w.q4.nblocks = total_blocks;
+        HC_TRY(dev_alloc(m, (void**)&w.q4.qs, total_blocks * 16));
+        HC_TRY(dev_alloc(m, (void**)&w.q4.sc, total_blocks * 2));
+        size_t blk_off = 0;
+        for (auto& p : parts) {
+            const uint8_t* src = img.payload(*p.t);
+            size_t kb_full = k_full / 32;
+            if (k_full % 32 != 0) {
+                size_t nb = p.t->len / 18;
+                size_t bytes = nb * 18;
+                if (bytes > *staging_cap) {
+                    if (*staging) cudaFree(*staging);
+                    HC_CUDA(cudaMalloc((void**)staging, bytes));
+                    *staging_cap = bytes;
+                }
+                HC_CUDA(cudaMemcpyAsync(*staging, src, bytes, cudaMemcpyHostToDevice, m->stream));
+                HC_TRY(hc::launch_q4_split(*staging, nb, w.q4.qs, w.q4.sc, m->stream));
+                HC_CUDA(cudaStreamSynchronize(m->stream));
+                continue;
+            }
+            HC_CHECK(p.t->len >= (p.row0 + p.rows) * kb_full * 18, HC_ERR_FORMAT,
+                     "Q4_0 tensor payload shorter than its shape");
+            size_t kb = cols / 32, kb0 = p.col0 / 32;
+            // Gather the shard's blocks row by row into a host-contiguous AoS run.
+            size_t bytes = p.rows * kb * 18;
+            if (bytes > *staging_cap) {
+                if (*staging) cudaFree(*staging);
+                HC_CUDA(cudaMalloc((void**)staging, bytes));
+                *staging_cap = bytes;
+            }
+            if (kb == kb_full) {
+                HC_CUDA(cudaMemcpyAsync(*staging, src + p.row0 * kb_full * 18, bytes, cudaMemcpyHostToDevice,
+                                        m->stream));
+            } else {
+                HC_CUDA(cudaMemcpy2DAsync(*staging, kb * 18, src + (p.row0 * kb_full + kb0) * 18, kb_full * 18,
+                                          kb * 18, p.rows, cudaMemcpyHostToDevice, m->stream));
+            }
+            HC_TRY(hc::launch_q4_split(*staging, p.rows * kb, w.q4.qs + blk_off, w.q4.sc + blk_off, m->stream));
+            HC_CUDA(cudaStreamSynchronize(m->stream));
+            blk_off += p.rows * kb;
+        }
+        return HC_OK;
+    }
+    size_t es = (dt == HC_DTYPE_FP32) ? 4 : (dt == HC_DTYPE_FP16 ? 2 : 0);
+    HC_CHECK(es != 0, HC_ERR_UNSUPPORTED, "weight dtype %u (Q8_0) is not supported by the GPU backend", dt);
+    HC_TRY(dev_alloc(m, &w.dense, n * cols * es));
+    size_t row_off = 0;
+    for (auto& p : parts) {
+        HC_CHECK(p.t->len >= (p.row0 + p.rows) * k_full * es, HC_ERR_FORMAT, "tensor payload shorter than its shape");
+        const uint8_t* src = img.payload(*p.t) + (p.row0 * k_full + p.col0) * es;
+        HC_CUDA(cudaMemcpy2DAsync((uint8_t*)w.dense + row_off * cols * es, cols * es, src, k_full * es, cols * es,
+                                  p.rows, cudaMemcpyHostToDevice, m->stream));
+        row_off += p.rows;
+    }
+    HC_CUDA(cudaStreamSynchronize(m->stream));
+    return HC_OK;
+}
+
+void free_model(hc_model* m) {
+    if (!m) return;
+    cudaSetDevice(m->device);
+    if (m->stream) cudaStreamSynchronize(m->stream);
+    for (void* p : m->allocs) cudaFree(p);
+    void* scr[] = {m->sc.hidden, m->sc.xn, m->sc.qkv, m->sc.attn, m->sc.gu, m->sc.act, m->sc.logits, m->sc.ids,
+                   m->sc.seqs, m->sc.rowpos, m->sc.argmax, m->rope};
+    for (void* p : scr)
+        if (p) cudaFree(p);
+    if (m->gemm_ws) hc::gemm_workspace_free(m->gemm_ws);
+    if (m->stream) cudaStreamDestroy(m->stream);
+    delete m;
+}
+
+int ensure_scratch(hc_model* m, size_t tokens, size_t logit_rows) {
+    Scratch& s = m->sc;
+    const hc_config& c = m->cfg;
+    if (tokens > s.cap_tokens) {
+        size_t t = std::max<size_t>(tokens, 8);
+        float** bufs[] = {&s.hidden, &s.xn, &s.qkv, &s.attn, &s.gu, &s.act};
+        size_t widths[] = {c.hidden_size, c.hidden_size, m->nq + 2 * m->nk, m->nq, 2 * (m->layers.empty() ? 0 : m->layers[0].gu.n / 2),
+                           m->layers.empty() ? 0 : m->layers[0].gu.n / 2};
+        for (int i = 0; i < 6; i++) {
+            if (*bufs[i]) cudaFree(*bufs[i]);
+            *bufs[i] = nullptr;
+            HC_CUDA(cudaMalloc((void**)bufs[i], std::max<size_t>(t * widths[i], 4) * sizeof(float)));
+        }
+        if (s.ids) cudaFree(s.ids);
+        if (s.seqs) cudaFree(s.seqs);
+        if (s.rowpos) cudaFree(s.rowpos);
+        HC_CUDA(cudaMalloc((void**)&s.ids, t * sizeof(uint32_t)));
+        HC_CUDA(cudaMalloc((void**)&s.seqs, t * sizeof(int)));
+        HC_CUDA(cudaMalloc((void**)&s.rowpos, t * sizeof(int)));
+        s.cap_tokens = t;
+    }
+    if (logit_rows > s.cap_logit_rows) {
+        size_t r = std::max<size_t>(logit_rows, 1);
+        if (s.logits) cudaFree(s.logits);
+        if (s.argmax) cudaFree(s.argmax);
+        HC_CUDA(cudaMalloc((void**)&s.logits, r * c.vocab_size * sizeof(float)));
+        HC_CUDA(cudaMalloc((void**)&s.argmax, r * sizeof(uint32_t)));
+        s.cap_logit_rows = r;
+    }
+    return HC_OK;
+}
+
+int ensure_rope(hc_model* m, size_t rows) {
+    if (rows <= m->rope_rows) return HC_OK;
+    std::vector<float2> t = hc_rope_table(rows, m->cfg.head_dim, m->cfg.rope_theta);
+    if (m->rope) cudaFree(m->rope);
+    m->rope = nullptr;
+    HC_CUDA(cudaMalloc((void**)&m->rope, t.size() * sizeof(float2)));
+    HC_CUDA(cudaMemcpy(m->rope, t.data(), t.size() * sizeof(float2), cudaMemcpyHostToDevice));
+    m->rope_rows = rows;
+    return HC_OK;
+}
+
+// y = W . x for `tokens` rows (the Q4_0 path picks the CUDA-core matvec for
+// few tokens and the tcgen05 GEMM otherwise).
+int matmul(hc_model* m, const DevWeight& w, const float* x, size_t ldx, size_t tokens, float* y, size_t ldy, int epi,
+           const float* res, size_t ldres) {
+    if (w.dtype == HC_DTYPE_Q4_0 && hc::gemm_tc_eligible(w.q4, tokens))
+        return hc::gemm_tc(m->gemm_ws, w.q4, x, ldx, tokens, y, ldy, epi, res, ldres, m->stream);
+    return hc::launch_matmul(w, x, ldx, tokens, y, ldy, epi, res, ldres, m->stream);
+}
+
+// The per-layer body shared by prefill (prefill = true, rows = prompt
+// tokens of one sequence) and decode (rows = sequences).
+int run_layers(hc_model* m, hc_kv* kv, size_t rows, bool prefill, int seq, int pos0) {
+    const hc_config& c = m->cfg;
+    Scratch& s = m->sc;
+    const size_t hd = c.head_dim, H = c.hidden_size;
+    const size_t nq = m->nq, nk = m->nk, ldqkv = nq + 2 * nk;
+    const size_t nh_l = nq / hd, nkv_l = nk / hd;
+    const float scale = 1.0f / sqrtf((float)hd);
+    for (size_t li = 0; li < m->layers.size(); li++) {
+        LayerW& L = m->layers[li];
+        HC_TRY(hc::launch_rmsnorm(s.hidden, H, L.in_norm, s.xn, H, rows, H, c.rms_norm_eps, m->stream));
+        HC_TRY(matmul(m, L.qkv, s.xn, H, rows, s.qkv, ldqkv, hc::EPI_STORE, nullptr, 0));
+        HC_TRY(hc::launch_rope_rows(s.qkv, ldqkv, rows, nh_l + nkv_l, hd, m->rope, m->rope_rows,
+                                    prefill ? nullptr : s.rowpos, pos0, m->stream));
+        size_t lofs = li * kv->layer_stride * (kv->kv_fp16 ? 2 : 4);
+        void* kc = (uint8_t*)kv->k + lofs;
+        void* vc = (uint8_t*)kv->v + lofs;
+        HC_TRY(hc::launch_kv_store(s.qkv + nq, s.qkv + nq + nk, ldqkv, (int)rows, (int)nkv_l, (int)hd, kc, vc,
+                                   kv->kv_fp16, kv->seq_stride, kv->head_stride, kv->max_pos,
+                                   prefill ? nullptr : s.seqs, kv->pos_dev, seq, pos0, m->stream));
+        hc::AttnParams P{};
+        P.q = s.qkv;
+        P.ldq = ldqkv;
+        P.out = s.attn;
+        P.ldo = nq;
+        P.vself = s.qkv + nq + nk;
+        P.ldself = ldqkv;
+        P.nh = (int)nh_l;
+        P.nkv = (int)nkv_l;
+        P.hd = (int)hd;
+        P.scale = scale;
+        if (prefill) {
+            P.mode_prefill = 1;
+            P.smem_n = (int)rows;
+            P.kp = s.qkv + nq;
+            P.vp = s.qkv + nq + nk;
+            P.ldkv = ldqkv;
+            HC_TRY(hc::launch_attention(P, (int)rows, 0, m->stream));
+        } else {
+            P.mode_prefill = 0;
+            P.smem_n = kv->max_pos;
+            P.kc = kc;
+            P.vc = vc;
+            P.seq_stride = kv->seq_stride;
+            P.head_stride = kv->head_stride;
+            P.seqs = s.seqs;
+            P.pos = kv->pos_dev;
+            HC_TRY(hc::launch_attention(P, (int)rows, kv->kv_fp16, m->stream));
+        }
+        HC_TRY(matmul(m, L.o, s.attn, nq, rows, s.hidden, H, hc::EPI_ADD, s.hidden, H));
+        HC_TRY(hc::launch_rmsnorm(s.hidden, H, L.post_norm, s.xn, H, rows, H, c.rms_norm_eps, m->stream));
+        size_t im = L.gu.n / 2;
+        HC_TRY(matmul(m, L.gu, s.xn, H, rows, s.gu, 2 * im, hc::EPI_STORE, nullptr, 0));
+        HC_TRY(hc::launch_silu_mul(s.gu, 2 * im, s.act, im, rows, im, m->stream));
+        HC_TRY(matmul(m, L.down, s.act, im, rows, s.hidden, H, hc::EPI_ADD, s.hidden, H));
+    }
+    return HC_OK;
+}
+
+__global__ void k_gather_pos(const int* __restrict__ seqs, const int* __restrict__ pos, int* __restrict__ rowpos,
+                             int B) {
+    int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b < B) rowpos[b] = pos[seqs[b]];
+}
+
+int decode_dev_impl(hc_model* m, hc_kv* kv, const int* seqs_dev, const uint32_t* ids_dev, int B, float* logits_dev,
+                    uint32_t* argmax_dev) {
+    const hc_config& c = m->cfg;
+    Scratch& s = m->sc;
+    HC_TRY(ensure_scratch(m, (size_t)B, (size_t)B));
+    if (seqs_dev != s.seqs) HC_CUDA(cudaMemcpyAsync(s.seqs, seqs_dev, B * sizeof(int), cudaMemcpyDeviceToDevice, m->stream));
+    if (ids_dev != s.ids) HC_CUDA(cudaMemcpyAsync(s.ids, ids_dev, B * sizeof(uint32_t), cudaMemcpyDeviceToDevice, m->stream));
+    k_gather_pos<<<(B + 127) / 128, 128, 0, m->stream>>>(s.seqs, kv->pos_dev, s.rowpos, B);
+    HC_LAUNCH_CHECK();
+    HC_TRY(hc::launch_embed(m->embed, s.ids, (size_t)B, s.hidden, c.hidden_size, m->stream));
+    HC_TRY(run_layers(m, kv, (size_t)B, false, 0, 0));
+    HC_TRY(hc::launch_advance(s.seqs, kv->pos_dev, B, m->stream));
+    HC_TRY(hc::launch_rmsnorm(s.hidden, c.hidden_size, m->final_norm, s.xn, c.hidden_size, (size_t)B, c.hidden_size,
+                              c.rms_norm_eps, m->stream));
+    float* logits = logits_dev ? logits_dev : s.logits;
+    if (m->lm_head.present) {
+        HC_TRY(matmul(m, m->lm_head, s.xn, c.hidden_size, (size_t)B, logits, c.vocab_size, hc::EPI_STORE, nullptr, 0));
+    } else {
+        HC_CUDA(cudaMemsetAsync(logits, 0, (size_t)B * c.vocab_size * sizeof(float), m->stream));
+    }
+    if (argmax_dev) HC_TRY(hc::launch_argmax(logits, (size_t)B, c.vocab_size, argmax_dev, m->stream));
+    return HC_OK;
+}
+
+}  // namespace
+
+// ============================================================ C ABI: model
+
+HC_EXPORT int hc_model_load(const uint8_t* image, size_t len, int tp_rank, int tp_size, hc_model** out) {
+    HC_CHECK(out != nullptr, HC_ERR_INVALID, "hc_model_load: out is NULL");
+    *out = nullptr;
+    HC_CHECK(tp_size >= 1 && tp_rank >= 0 && tp_rank < tp_size, HC_ERR_INVALID, "hc_model_load: bad tp rank/size %d/%d",
+             tp_rank, tp_size);
+    HypnoImage img;
+    HC_TRY(parse_image(image, len, img));
+    hc_config c{};
+    // HypnoConfig::from_model, transformer.rs:42-63
+    HC_CHECK(meta_u64(img, "hidden_size", c.hidden_size), HC_ERR_FORMAT, "hypno: metadata hidden_size missing");
+    HC_CHECK(meta_u64(img, "num_attention_heads", c.num_attention_heads), HC_ERR_FORMAT,
+             "hypno: metadata num_attention_heads missing");
+    if (!meta_u64(img, "num_key_value_heads", c.num_key_value_heads)) c.num_key_value_heads = c.num_attention_heads;
+    HC_CHECK(c.num_attention_heads > 0 && c.num_key_value_heads > 0, HC_ERR_FORMAT, "hypno: zero heads");
+    c.head_dim = c.hidden_size / c.num_attention_heads;
+    if (!meta_u64(img, "intermediate_size", c.intermediate_size)) c.intermediate_size = c.hidden_size * 8 / 3;
+    if (!meta_u64(img, "num_hidden_layers", c.num_hidden_layers)) c.num_hidden_layers = 0;
+    if (!meta_u64(img, "vocab_size", c.vocab_size)) c.vocab_size = 32000;
+    if (!meta_u64(img, "max_position_embeddings", c.max_position_embeddings)) c.max_position_embeddings = 2048;
+    if (!meta_f32(img, "rms_norm_eps", c.rms_norm_eps)) c.rms_norm_eps = 1e-5f;
+    if (!meta_f32(img, "rope_theta", c.rope_theta)) c.rope_theta = 10000.0f;
+    c.tp_rank = tp_rank;
+    c.tp_size = tp_size;
+    const size_t H = c.hidden_size, hd = c.head_dim, nh = c.num_attention_heads, nkv = c.num_key_value_heads;
+    const size_t im = c.intermediate_size;
+    HC_CHECK(hd % 2 == 0 && hd > 0, HC_ERR_UNSUPPORTED, "head_dim %zu must be even", hd);
+    HC_CHECK(nh % nkv == 0, HC_ERR_UNSUPPORTED, "num_attention_heads must be a multiple of num_key_value_heads");
+    HC_CHECK(nkv % (size_t)tp_size == 0 && nh % (size_t)tp_size == 0, HC_ERR_UNSUPPORTED,
+             "tensor parallel size %d must divide the query and KV heads", tp_size);
+    HC_CHECK(im % tp_size == 0 && (tp_size == 1 || (im / tp_size) % 32 == 0), HC_ERR_UNSUPPORTED,
+             "tensor parallel size %d must split intermediate_size into multiples of 32", tp_size);
+
+    hc_model* m = new hc_model();
+    m->cfg = c;
+    cudaGetDevice(&m->device);
+    if (cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess) {
+        hc_set_error("hc_model_load: no usable CUDA device (%s)", cudaGetErrorString(cudaGetLastError()));
+        delete m;
+        return HC_ERR_CUDA;
+    }
+    uint8_t* staging = nullptr;
+    size_t staging_cap = 0;
+    auto fail = [&](int r) {
+        if (staging) cudaFree(staging);
+        free_model(m);
+        return r;
+    };
+    const size_t nh_l = nh / tp_size, nkv_l = nkv / tp_size, im_l = im / tp_size;
+    m->nq = nh_l * hd;
+    m->nk = nkv_l * hd;
+    m->layers.resize(c.num_hidden_layers);
+    for (size_t li = 0; li < c.num_hidden_layers; li++) {
+        std::string p = "model.layers." + std::to_string(li) + ".";
+        const TensorEntry *tq = img.find(p + "self_attn.q_proj.weight"), *tk = img.find(p + "self_attn.k_proj.weight"),
+                          *tv = img.find(p + "self_attn.v_proj.weight"), *to = img.find(p + "self_attn.o_proj.weight"),
+                          *tg = img.find(p + "mlp.gate_proj.weight"), *tu = img.find(p + "mlp.up_proj.weight"),
+                          *td = img.find(p + "mlp.down_proj.weight");
+        if (!(tq && tk && tv && to && tg && tu && td)) {
+            hc_set_error("hypno: layer %zu is missing a projection tensor", li);
+            return fail(HC_ERR_UNSUPPORTED);
+        }
+        LayerW& L = m->layers[li];
+        int r;
+        if (tq->dtype == tk->dtype && tk->dtype == tv->dtype && (tq->dtype != HC_DTYPE_Q4_0 || H % 32 == 0)) {
+            r = upload_weight(m, img,
+                              {{tq, tp_rank * nh_l * hd, nh_l * hd, 0, H},
+                               {tk, tp_rank * nkv_l * hd, nkv_l * hd, 0, H},
+                               {tv, tp_rank * nkv_l * hd, nkv_l * hd, 0, H}},
+                              H, L.qkv, &staging, &staging_cap);
+        } else {
+            hc_set_error("hypno: q/k/v projections of layer %zu must share a dtype and (for Q4_0) a width that is a "
+                         "multiple of 32", li);
+            r = HC_ERR_UNSUPPORTED;
+        }
+        if (r) return fail(r);
+        if ((r = upload_weight(m, img, {{to, 0, H, tp_rank * nh_l * hd, nh_l * hd}}, nh * hd, L.o, &staging,
+                               &staging_cap)))
+            return fail(r);
+        if (tg->dtype != tu->dtype) {
+            hc_set_error("hypno: gate/up projections of layer %zu must share a dtype", li);
+            return fail(HC_ERR_UNSUPPORTED);
+        }
+        if ((r = upload_weight(m, img, {{tg, tp_rank * im_l, im_l, 0, H}, {tu, tp_rank * im_l, im_l, 0, H}}, H, L.gu,
+                               &staging, &staging_cap)))
+            return fail(r);
+        if ((r = upload_weight(m, img, {{td, 0, H, tp_rank * im_l, im_l}}, im, L.down, &staging, &staging_cap)))
+            return fail(r);
+        if ((r = upload_norm(m, img, p + "input_layernorm.weight", H, &L.in_norm))) return fail(r);
+        if ((r = upload_norm(m, img, p + "post_attention_layernorm.weight", H, &L.post_norm))) return fail(r);
+    }
+    int r;
+    if ((r = upload_norm(m, img, "model.norm.weight", H, &m->final_norm))) return fail(r);
+    const TensorEntry* te = img.find("model.embed_tokens.weight");
+    const TensorEntry* tl = img.find("lm_head.weight");
+    if (te) {
+        if ((r = upload_weight(m, img, {{te, 0, c.vocab_size, 0, H}}, H, m->embed, &staging, &staging_cap)))
+            return fail(r);
+        m->cfg.embed_dtype = te->dtype;
+    }
+    if (tl) {
+        if ((r = upload_weight(m, img, {{tl, 0, c.vocab_size, 0, H}}, H, m->lm_head, &staging, &staging_cap)))
+            return fail(r);
+        m->cfg.lm_head_dtype = tl->dtype;
+        m->cfg.lm_head_tied = 0;
+    } else if (te) {
+        m->lm_head = m->embed;  // tied: same device buffers (transformer.rs:521-524)
+        m->cfg.lm_head_dtype = te->dtype;
+        m->cfg.lm_head_tied = 1;
+    }
+    if (staging) cudaFree(staging);
+    staging = nullptr;
+    m->gemm_ws = hc::gemm_workspace_new();
+    if ((r = ensure_rope(m, c.max_position_embeddings))) return fail(r);
+    *out = m;
+    return HC_OK;
+}
+
+HC_EXPORT int hc_model_config(const hc_model* model, hc_config* out) {
+    HC_CHECK(model && out, HC_ERR_INVALID, "hc_model_config: NULL argument");
+    *out = model->cfg;
+    return HC_OK;
+}
+
+HC_EXPORT int hc_model_free(hc_model* model) {
+    free_model(model);
+    return HC_OK;
+}
+
+HC_EXPORT int hc_sync(hc_model* model) {
+    HC_CHECK(model, HC_ERR_INVALID, "hc_sync: NULL model");
+    HC_CUDA(cudaSetDevice(model->device));
+    HC_CUDA(cudaStreamSynchronize(model->stream));
+    return HC_OK;
+}
+
+HC_EXPORT void* hc_model_stream(hc_model* model) { return model ? (void*)model->stream : nullptr; }
+
+HC_EXPORT int hc_kv_alloc(hc_model* model, int n_seqs, int max_pos, int kv_dtype, hc_kv** out) {
+    HC_CHECK(model && out, HC_ERR_INVALID, "hc_kv_alloc: NULL argument");
+    HC_CHECK(n_seqs > 0, HC_ERR_INVALID, "hc_kv_alloc: n_seqs must be > 0");
+    HC_CHECK(kv_dtype == HC_KV_FP32 || kv_dtype == HC_KV_FP16, HC_ERR_INVALID, "hc_kv_alloc: bad kv dtype %d", kv_dtype);
+    HC_CUDA(cudaSetDevice(model->device));
+    if (max_pos <= 0) max_pos = (int)model->cfg.max_position_embeddings;
+    hc_kv* kv = new hc_kv();
+    kv->model = model;
+    kv->n_seqs = n_seqs;
+    kv->max_pos = max_pos;
+    kv->kv_fp16 = kv_dtype == HC_KV_FP16;
+    const size_t hd = model->cfg.head_dim, nkv_l = model->nk / hd, L = model->cfg.num_hidden_layers;
+    kv->head_stride = (size_t)max_pos * hd;
+    kv->layer_stride = nkv_l * kv->head_stride;
+    kv->seq_stride = L * kv->layer_stride;
+    size_t bytes = (size_t)n_seqs * kv->seq_stride * (kv->kv_fp16 ? 2 : 4);
+    cudaError_t e1 = cudaMalloc(&kv->k, std::max<size_t>(bytes, 16));
+    cudaError_t e2 = e1 == cudaSuccess ? cudaMalloc(&kv->v, std::max<size_t>(bytes, 16)) : e1;
+    cudaError_t e3 = e2 == cudaSuccess ? cudaMalloc((void**)&kv->pos_dev, n_seqs * sizeof(int)) : e2;
+    if (e3 != cudaSuccess) {
+        cudaGetLastError();
+        if (kv->k) cudaFree(kv->k);
+        if (kv->v) cudaFree(kv->v);
+        delete kv;
+        hc_set_error("hc_kv_alloc: cannot allocate %zu bytes of KV cache", 2 * bytes);
+        return HC_ERR_OOM;
+    }
+    kv->pos_host.assign(n_seqs, 0);
+    HC_CUDA(cudaMemsetAsync(kv->pos_dev, 0, n_seqs * sizeof(int), model->stream));
+    HC_CUDA(cudaMemsetAsync(kv->k, 0, bytes, model->stream));
+    HC_CUDA(cudaMemsetAsync(kv->v, 0, bytes, model->stream));
+    int r = ensure_rope(model, (size_t)max_pos);
+    if (r) {
+        hc_kv_free(kv);
+        return r;
+    }
+    HC_CUDA(cudaStreamSynchronize(model->stream));
+    *out = kv;
+    return HC_OK;
+}
+
+HC_EXPORT int hc_kv_free(hc_kv* kv) {
+    if (!kv) return HC_OK;
+    cudaSetDevice(kv->model->device);
+    cudaStreamSynchronize(kv->model->stream);
+    if (kv->k) cudaFree(kv->k);
+    if (kv->v) cudaFree(kv->v);
+    if (kv->pos_dev) cudaFree(kv->pos_dev);
+    delete kv;
+    return HC_OK;
+}
+
+HC_EXPORT int hc_kv_seq_len(const hc_kv* kv, int seq, int* out) {
+    HC_CHECK(kv && out, HC_ERR_INVALID, "hc_kv_seq_len: NULL argument");
+    HC_CHECK(seq >= 0 && seq < kv->n_seqs, HC_ERR_INVALID, "hc_kv_seq_len: seq %d out of range", seq);
+    HC_CUDA(cudaSetDevice(kv->model->device));
+    HC_TRY(sync_pos(const_cast<hc_kv*>(kv)));
+    *out = kv->pos_host[seq];
+    return HC_OK;
+}
+
+HC_EXPORT int hc_kv_set_pos(hc_kv* kv, int seq, int pos) {
+    HC_CHECK(kv, HC_ERR_INVALID, "hc_kv_set_pos: NULL kv");
+    HC_CHECK(seq >= 0 && seq < kv->n_seqs, HC_ERR_INVALID, "hc_kv_set_pos: seq %d out of range", seq);
+    HC_CHECK(pos >= 0 && pos <= kv->max_pos, HC_ERR_INVALID, "hc_kv_set_pos: pos %d out of range", pos);
+    HC_CUDA(cudaSetDevice(kv->model->device));
+    HC_TRY(sync_pos(kv));
+    kv->pos_host[seq] = pos;
+    HC_CUDA(cudaMemcpyAsync(kv->pos_dev + seq, &kv->pos_host[seq], sizeof(int), cudaMemcpyHostToDevice,
+                            kv->model->stream));
+    HC_CUDA(cudaStreamSynchronize(kv->model->stream));
+    return HC_OK;
+}
+
+HC_EXPORT int hc_prefill(hc_model* m, hc_kv* kv, int seq, const uint32_t* ids, int T, float* logits_out) {
+    HC_CHECK(m && kv && kv->model == m, HC_ERR_INVALID, "hc_prefill: bad model/kv");
+    HC_CHECK(seq >= 0 && seq < kv->n_seqs, HC_ERR_INVALID, "hc_prefill: seq %d out of range", seq);
+    HC_CHECK(T >= 0 && (T == 0 || ids), HC_ERR_INVALID, "hc_prefill: bad ids");
+    HC_CUDA(cudaSetDevice(m->device));
+    const hc_config& c = m->cfg;
+    HC_TRY(sync_pos(kv));
+    const int p0 = kv->pos_host[seq];
+    HC_CHECK((size_t)p0 + (size_t)T <= (size_t)kv->max_pos, HC_ERR_STATE, "hc_prefill: %d + %d positions exceed the cache (%d)",
+             p0, T, kv->max_pos);
+    for (int t = 0; t < T; t++)
+        HC_CHECK(ids[t] < c.vocab_size, HC_ERR_INVALID, "hc_prefill: token id %u >= vocab %llu", ids[t],
+                 (unsigned long long)c.vocab_size);
+    if (T == 0) {  // turbo.rs:255-258
+        if (logits_out) std::memset(logits_out, 0, c.vocab_size * sizeof(float));
+        return HC_OK;
+    }
+    Scratch& s = m->sc;
+    HC_TRY(ensure_scratch(m, (size_t)T, 1));
+    HC_CUDA(cudaMemcpyAsync(s.ids, ids, T * sizeof(uint32_t), cudaMemcpyHostToDevice, m->stream));
+    HC_TRY(hc::launch_embed(m->embed, s.ids, (size_t)T, s.hidden, c.hidden_size, m->stream));
+    HC_TRY(run_layers(m, kv, (size_t)T, true, seq, p0));
+    kv->pos_host[seq] = p0 + T;
+    HC_CUDA(cudaMemcpyAsync(kv->pos_dev + seq, &kv->pos_host[seq], sizeof(int), cudaMemcpyHostToDevice, m->stream));
+    const float* last = s.hidden + (size_t)(T - 1) * c.hidden_size;
+    HC_TRY(hc::launch_rmsnorm(last, c.hidden_size, m->final_norm, s.xn, c.hidden_size, 1, c.hidden_size,
+                              c.rms_norm_eps, m->stream));
+    if (m->lm_head.present)
+        HC_TRY(matmul(m, m->lm_head, s.xn, c.hidden_size, 1, s.logits, c.vocab_size, hc::EPI_STORE, nullptr, 0));
+    else
+        HC_CUDA(cudaMemsetAsync(s.logits, 0, c.vocab_size * sizeof(float), m->stream));
+    if (logits_out)
+        HC_CUDA(cudaMemcpyAsync(logits_out, s.logits, c.vocab_size * sizeof(float), cudaMemcpyDeviceToHost, m->stream));
+    HC_CUDA(cudaStreamSynchronize(m->stream));
+    return HC_OK;
+}
+
+static int sync_pos(hc_kv* kv) {
+    if (!kv->host_stale) return HC_OK;
+    HC_CUDA(cudaMemcpyAsync(kv->pos_host.data(), kv->pos_dev, kv->n_seqs * sizeof(int), cudaMemcpyDeviceToHost,
+                            kv->model->stream));
+    HC_CUDA(cudaStreamSynchronize(kv->model->stream));
+    kv->host_stale = false;
+    return HC_OK;
+}
+
+static int check_decode_args(hc_model* m, hc_kv* kv, const int* seqs, int B) {
+    HC_TRY(sync_pos(kv));
+    for (int b = 0; b < B; b++) {
+        HC_CHECK(seqs[b] >= 0 && seqs[b] < kv->n_seqs, HC_ERR_INVALID, "decode: seq %d out of range", seqs[b]);
+        HC_CHECK(kv->pos_host[seqs[b]] < kv->max_pos, HC_ERR_STATE, "decode: sequence %d is full (%d positions)",
+                 seqs[b], kv->max_pos);
+        for (int j = 0; j < b; j++)
+            HC_CHECK(seqs[j] != seqs[b], HC_ERR_INVALID, "decode: sequence %d appears twice in one step", seqs[b]);
+    }
+    return HC_OK;
+}
+
+HC_EXPORT int hc_decode_step(hc_model* m, hc_kv* kv, const int* seqs, const uint32_t* ids, int B, float* logits_out,
+                             uint32_t* argmax_out) {
+    HC_CHECK(m && kv && kv->model == m, HC_ERR_INVALID, "hc_decode_step: bad model/kv");
+    HC_CHECK(B > 0 && seqs && ids, HC_ERR_INVALID, "hc_decode_step: bad batch");
+    HC_CUDA(cudaSetDevice(m->device));
+    HC_TRY(check_decode_args(m, kv, seqs, B));
+    for (int b = 0; b < B; b++)
+        HC_CHECK(ids[b] < m->cfg.vocab_size, HC_ERR_INVALID, "decode: token id %u >= vocab", ids[b]);
+    Scratch& s = m->sc;
+    HC_TRY(ensure_scratch(m, (size_t)B, (size_t)B));
+    HC_CUDA(cudaMemcpyAsync(s.seqs, seqs, B * sizeof(int), cudaMemcpyHostToDevice, m->stream));
+    HC_CUDA(cudaMemcpyAsync(s.ids, ids, B * sizeof(uint32_t), cudaMemcpyHostToDevice, m->stream));
+    HC_TRY(decode_dev_impl(m, kv, s.seqs, s.ids, B, s.logits, argmax_out ? s.argmax : nullptr));
+    for (int b = 0; b < B; b++) kv->pos_host[seqs[b]] += 1;
+    const size_t V = m->cfg.vocab_size;
+    if (logits_out)
+        HC_CUDA(cudaMemcpyAsync(logits_out, s.logits, (size_t)B * V * sizeof(float), cudaMemcpyDeviceToHost, m->stream));
+    if (argmax_out)
+        HC_CUDA(cudaMemcpyAsync(argmax_out, s.argmax, B * sizeof(uint32_t), cudaMemcpyDeviceToHost, m->stream));
+    HC_CUDA(cudaStreamSynchronize(m->stream));
+    return HC_OK;
+}
+
+HC_EXPORT int hc_decode_step_dev(hc_model* m, hc_kv* kv, const int* seqs_dev, const uint32_t* ids_dev, int B,
+                                 float* logits_dev, uint32_t* argmax_dev) {
+    HC_CHECK(m && kv && kv->model == m, HC_ERR_INVALID, "hc_decode_step_dev: bad model/kv");
+    HC_CHECK(B > 0 && seqs_dev && ids_dev, HC_ERR_INVALID, "hc_decode_step_dev: bad batch");
+    HC_CUDA(cudaSetDevice(m->device));
+    // No host round trip: positions live on the device.  The kernels skip
+    // stores past the cache capacity; hc_kv_seq_len reports the positions.
+    HC_TRY(decode_dev_impl(m, kv, seqs_dev, ids_dev, B, logits_dev, argmax_dev));
+    kv->host_stale = true;
+    return HC_OK;
+}

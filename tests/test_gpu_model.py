@@ -1,0 +1,178 @@
+"""Model-level parity of the sm_100a backend (hc_prefill / hc_decode_step)
+against the CPU oracle's batch_forward / model_forward, through the C ABI.
+
+Bars (north_star): logits within max|gpu - ref| / max(1, max|ref|) <= 1e-3,
+greedy ids identical for the first 32 steps; the top-1/top-2 margin is
+reported so a flip on a sub-tolerance margin is visible."""
+import numpy as np
+import pytest
+
+from hypno_b200 import engine, hypno_file as hf, synth
+from hypno_b200._lib import HypnoCudaError
+from oracle import oracle as orc
+from tests import _models
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-3
+
+
+def rel_err(a, ref):
+    return float(np.max(np.abs(a.astype(np.float64) - ref)) / max(1.0, float(np.max(np.abs(ref)))))
+
+
+def margin(l):
+    s = np.sort(l)
+    return float(s[-1] - s[-2])
+
+
+def run_greedy_gpu(model, prompt, steps, kv_dtype=engine.KV_FP32, max_pos=0):
+    kv = engine.KVCache(model, 1, max_pos, kv_dtype)
+    logits = engine.batch_forward(model, prompt, kv)
+    out_logits = [logits]
+    ids = [orc.greedy(logits)]
+    for _ in range(steps - 1):
+        lg, am = engine.decode_step(model, kv, [0], [ids[-1]])
+        assert int(am[0]) == orc.greedy(lg[0])
+        out_logits.append(lg[0])
+        ids.append(int(am[0]))
+    return ids, out_logits
+
+
+def run_greedy_oracle(om, prompt, steps):
+    kv = om.new_kv()
+    logits = orc.batch_forward(om, prompt, kv)
+    out_logits = [logits]
+    ids = [orc.greedy(logits)]
+    for _ in range(steps - 1):
+        logits = orc.model_forward(om, ids[-1], kv)
+        out_logits.append(logits)
+        ids.append(orc.greedy(logits))
+    return ids, out_logits
+
+
+def compare(gpu, ref, label):
+    gids, glog = gpu
+    rids, rlog = ref
+    worst = 0.0
+    for step, (g, r) in enumerate(zip(glog, rlog)):
+        e = rel_err(g, r)
+        worst = max(worst, e)
+        assert e <= TOL, f"{label}: step {step} logits rel err {e:.3e}"
+    first_diff = next((i for i, (a, b) in enumerate(zip(gids, rids)) if a != b), None)
+    assert first_diff is None, (f"{label}: greedy ids diverge at step {first_diff} "
+                                f"(oracle margin there {margin(rlog[first_diff]):.3e})")
+    print(f"{label}: max logits rel err {worst:.3e}, min top-2 margin {min(margin(r) for r in rlog):.3e}")
+
+
+@pytest.fixture(scope="module")
+def tiny_images():
+    return {dt: _models.reference_model_image(_models.TINY, 0.01, dt) for dt in (hf.DT_FP32, hf.DT_Q4_0)}
+
+
+@pytest.mark.parametrize("dt", [hf.DT_FP32, hf.DT_Q4_0])
+def test_tiny_reference_model(cuda_device, tiny_images, dt):
+    """The reference's own test model (turbo.rs:381-472) in FP32 and Q4_0
+    (its Q4_0 form mixes FP32 q/k/v/o with Q4_0 matrices whose width 172 is
+    not a multiple of 32)."""
+    img = tiny_images[dt]
+    m = engine.HypnoModel(img)
+    om = orc.OracleModel(img)
+    prompt = np.array([1, 5, 10, 42, 100, 7, 3], np.uint32)
+    compare(run_greedy_gpu(m, prompt, 12), run_greedy_oracle(om, prompt, 12), f"tiny dt={dt}")
+
+
+def test_tiny_batch_equals_sequential_on_gpu(cuda_device, tiny_images):
+    """turbo.rs:474-568 on the GPU: prefill then decode == all-decode."""
+    m = engine.HypnoModel(tiny_images[hf.DT_FP32])
+    prompt, nxt = [1, 5, 10, 42], 100
+    kv_a = engine.KVCache(m)
+    engine.batch_forward(m, prompt, kv_a)
+    a = engine.model_forward(m, nxt, kv_a)
+    kv_b = engine.KVCache(m)
+    for t in prompt:
+        engine.model_forward(m, t, kv_b)
+    b = engine.model_forward(m, nxt, kv_b)
+    assert np.max(np.abs(a - b)) < 1e-5
+    assert kv_a.seq_len() == kv_b.seq_len() == 5
+
+
+def test_edge_cases(cuda_device, tiny_images):
+    m = engine.HypnoModel(tiny_images[hf.DT_FP32])
+    kv = engine.KVCache(m, n_seqs=2, max_pos=8)
+    out = engine.batch_forward(m, [], kv)  # turbo.rs:255-258
+    assert np.all(out == 0) and kv.seq_len() == 0
+    with pytest.raises(HypnoCudaError):
+        engine.batch_forward(m, list(range(9)), kv)  # past capacity
+    with pytest.raises(HypnoCudaError):
+        engine.decode_step(m, kv, [0, 0], [1, 2])  # same sequence twice
+    with pytest.raises(HypnoCudaError):
+        engine.decode_step(m, kv, [0], [1000])  # id >= vocab
+    engine.batch_forward(m, list(range(8)), kv)
+    with pytest.raises(HypnoCudaError) as e:
+        engine.decode_step(m, kv, [0], [1])  # cache full
+    assert e.value.code == -7
+    kv.clear(0)
+    assert kv.seq_len(0) == 0
+    with pytest.raises(HypnoCudaError):
+        engine.HypnoModel(np.frombuffer(b"HYPX" + b"\0" * 60, np.uint8))
+
+
+@pytest.fixture(scope="module")
+def c1_image():
+    return _models.synth_image("c1")
+
+
+def test_c1_greedy_32_steps(cuda_device, c1_image):
+    """128-token prompt + greedy decode, logits and ids vs oracle."""
+    cfg = synth.CONFIGS["c1"]
+    prompt = synth.prompt_ids(cfg["vocab"], cfg["prompt"], seed=0)
+    m = engine.HypnoModel(c1_image)
+    assert m.config.lm_head_tied == 0 and m.config.embed_dtype == hf.DT_FP32
+    om = orc.OracleModel(c1_image)
+    compare(run_greedy_gpu(m, prompt, 32), run_greedy_oracle(om, prompt, 32), "c1")
+
+
+def test_c1_batched_sequences_equal_single(cuda_device, c1_image):
+    """Several sequences decoded in one batched step give the same logits as
+    each decoded alone (and as the oracle), with different prompt lengths."""
+    cfg = synth.CONFIGS["c1"]
+    m = engine.HypnoModel(c1_image)
+    om = orc.OracleModel(c1_image)
+    prompts = [synth.prompt_ids(cfg["vocab"], T, seed=s) for s, T in ((1, 5), (2, 1), (3, 33), (4, 0))]
+    kv = engine.KVCache(m, n_seqs=4, max_pos=64)
+    okvs = []
+    for s, p in enumerate(prompts):
+        engine.batch_forward(m, p, kv, seq=s)
+        okv = om.new_kv(64)
+        orc.batch_forward(om, p, okv)
+        okvs.append(okv)
+    toks = [7, 8, 9, 10]
+    for step in range(3):
+        lg, am = engine.decode_step(m, kv, [0, 1, 2, 3], toks)
+        for s in range(4):
+            ref = orc.model_forward(om, toks[s], okvs[s])
+            assert rel_err(lg[s], ref) <= TOL, (step, s)
+        toks = [int(a) for a in am]
+    assert [kv.seq_len(s) for s in range(4)] == [len(p) + 3 for p in prompts]
+
+
+def test_c1_fp16_kv(cuda_device, c1_image):
+    """fp16 KV cache (new in this backend; the reference cache is FP32):
+    logits stay within tolerance of the FP32-KV oracle."""
+    cfg = synth.CONFIGS["c1"]
+    prompt = synth.prompt_ids(cfg["vocab"], cfg["prompt"], seed=0)
+    m = engine.HypnoModel(c1_image)
+    om = orc.OracleModel(c1_image)
+    compare(run_greedy_gpu(m, prompt, 16, kv_dtype=engine.KV_FP16), run_greedy_oracle(om, prompt, 16), "c1 fp16-kv")
+
+
+@pytest.mark.slow
+def test_c3_greedy_32_steps(cuda_device):
+    """512-token prefill + greedy decode vs the oracle."""
+    cfg = synth.CONFIGS["c3"]
+    img = _models.synth_image("c3")
+    prompt = synth.prompt_ids(cfg["vocab"], cfg["prompt"], seed=0)
+    m = engine.HypnoModel(img)
+    assert m.config.lm_head_tied == 1 and m.config.embed_dtype == hf.DT_Q4_0
+    om = orc.OracleModel(img)
+    compare(run_greedy_gpu(m, prompt, 32), run_greedy_oracle(om, prompt, 32), "c3")
