@@ -16,4 +16,12 @@ bool gemm_tc_eligible(const hc_q4_matrix& w, size_t tokens);
 int gemm_tc(GemmWorkspace* ws, const hc_q4_matrix& w, const float* x, size_t ldx, size_t tokens, float* y,
             size_t ldy, int epi, const float* res, size_t ldres, cudaStream_t s);
 
+// Reads and clears the device flag set by a timed-out pipeline wait
+// (synchronizes the device); HC_ERR_TIMEOUT when a kernel aborted.
+int gemm_check(GemmWorkspace* ws);
+
+// Changes whenever a workspace buffer captured by earlier launches moved
+// (captured CUDA graphs must then be rebuilt).
+uint64_t gemm_generation(GemmWorkspace* ws);
+
 }  // namespace hc

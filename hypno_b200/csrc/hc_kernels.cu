@@ -27,19 +27,23 @@ __global__ void k_q4_quantize(const float* __restrict__ x, size_t nblocks, uint8
 #pragma unroll
     for (int i = 0; i < 32; i++) max_abs = fmaxf(max_abs, fabsf(v[i]));
     float scale = (max_abs > 0.0f) ? __fdiv_rn(max_abs, 7.0f) : 1.0f;
-    __half h = __float2half_rn(scale);
-    uint16_t hb = __half_as_ushort(h);
-    uint8_t* o = out + b * 18;
-    o[0] = (uint8_t)(hb & 0xFF);
-    o[1] = (uint8_t)(hb >> 8);
+    uint32_t hb = (uint32_t)__half_as_ushort(__float2half_rn(scale));
+    uint32_t packed[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
     for (int i = 0; i < 16; i++) {
         float r0 = roundf(__fdiv_rn(v[2 * i], scale));
         float r1 = roundf(__fdiv_rn(v[2 * i + 1], scale));
         int q0 = isnan(r0) ? 0 : (int)fminf(fmaxf(r0, -8.0f), 7.0f);
         int q1 = isnan(r1) ? 0 : (int)fminf(fmaxf(r1, -8.0f), 7.0f);
-        o[2 + i] = (uint8_t)(((q0 + 8) & 0x0F) | (((q1 + 8) & 0x0F) << 4));
+        uint32_t byte = (uint32_t)((q0 + 8) & 0x0F) | ((uint32_t)((q1 + 8) & 0x0F) << 4);
+        packed[i >> 2] |= byte << (8 * (i & 3));
     }
+    // 18-byte block at an address that is only 2-byte aligned: scale first,
+    // then the 16 nibble bytes, written as 16-bit halves.
+    uint16_t* o16 = reinterpret_cast<uint16_t*>(out + b * 18);
+    o16[0] = (uint16_t)hb;
+#pragma unroll
+    for (int i = 0; i < 8; i++) o16[1 + i] = (uint16_t)(packed[i >> 1] >> (16 * (i & 1)));
 }
 
 // Q4_0Block::dequantize (quant.rs:25-34): (nibble - 8) * scale, exact in f32.

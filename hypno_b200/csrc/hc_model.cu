@@ -185,6 +185,7 @@ struct LayerW {
 };
 
 struct Scratch {
+    uint64_t generation = 0;  // bumped whenever a buffer moves
     size_t cap_tokens = 0, cap_logit_rows = 0;
     float *hidden = nullptr, *xn = nullptr, *qkv = nullptr, *attn = nullptr, *gu = nullptr, *act = nullptr;
     float* logits = nullptr;
@@ -195,6 +196,7 @@ struct Scratch {
 };
 
 struct hc_model {
+    int refs = 1;            // the caller's handle + one per live hc_kv
     hc_config cfg{};
     int device = 0;
     cudaStream_t stream = nullptr;
@@ -209,7 +211,18 @@ struct hc_model {
     hc::GemmWorkspace* gemm_ws = nullptr;
 };
 
+// A captured decode step: replayed while the key (batch, device pointers,
+// buffer generations) is unchanged.
+struct DecodeGraph {
+    int B = 0;
+    const void *seqs = nullptr, *ids = nullptr;
+    void *logits = nullptr, *argmax = nullptr;
+    uint64_t gen = 0;
+    cudaGraphExec_t exec = nullptr;
+};
+
 struct hc_kv {
+    std::vector<DecodeGraph> graphs;
     bool host_stale = false;
     hc_model* model = nullptr;
     int n_seqs = 0, max_pos = 0, kv_fp16 = 0;
@@ -376,6 +389,7 @@ int ensure_scratch(hc_model* m, size_t tokens, size_t logit_rows) {
         HC_CUDA(cudaMalloc((void**)&s.seqs, t * sizeof(int)));
         HC_CUDA(cudaMalloc((void**)&s.rowpos, t * sizeof(int)));
         s.cap_tokens = t;
+        s.generation++;
     }
     if (logit_rows > s.cap_logit_rows) {
         size_t r = std::max<size_t>(logit_rows, 1);
@@ -384,6 +398,7 @@ int ensure_scratch(hc_model* m, size_t tokens, size_t logit_rows) {
         HC_CUDA(cudaMalloc((void**)&s.logits, r * c.vocab_size * sizeof(float)));
         HC_CUDA(cudaMalloc((void**)&s.argmax, r * sizeof(uint32_t)));
         s.cap_logit_rows = r;
+        s.generation++;
     }
     return HC_OK;
 }
@@ -396,6 +411,7 @@ int ensure_rope(hc_model* m, size_t rows) {
     HC_CUDA(cudaMalloc((void**)&m->rope, t.size() * sizeof(float2)));
     HC_CUDA(cudaMemcpy(m->rope, t.data(), t.size() * sizeof(float2), cudaMemcpyHostToDevice));
     m->rope_rows = rows;
+    m->sc.generation++;
     return HC_OK;
 }
 
@@ -503,6 +519,7 @@ int decode_dev_impl(hc_model* m, hc_kv* kv, const int* seqs_dev, const uint32_t*
 // ============================================================ C ABI: model
 
 HC_EXPORT int hc_model_load(const uint8_t* image, size_t len, int tp_rank, int tp_size, hc_model** out) {
+    cudaGetLastError();  // a stale error of an earlier unrelated call is not ours
     HC_CHECK(out != nullptr, HC_ERR_INVALID, "hc_model_load: out is NULL");
     *out = nullptr;
     HC_CHECK(tp_size >= 1 && tp_rank >= 0 && tp_rank < tp_size, HC_ERR_INVALID, "hc_model_load: bad tp rank/size %d/%d",
@@ -625,8 +642,16 @@ HC_EXPORT int hc_model_config(const hc_model* model, hc_config* out) {
     return HC_OK;
 }
 
+static void model_release(hc_model* m) {
+    if (m && --m->refs == 0) free_model(m);
+}
+
+// Releases the caller's handle; the device state stays alive until the last
+// KV cache built on it is freed too.
 HC_EXPORT int hc_model_free(hc_model* model) {
-    free_model(model);
+    cudaGetLastError();
+    model_release(model);
+    cudaGetLastError();
     return HC_OK;
 }
 
@@ -634,12 +659,13 @@ HC_EXPORT int hc_sync(hc_model* model) {
     HC_CHECK(model, HC_ERR_INVALID, "hc_sync: NULL model");
     HC_CUDA(cudaSetDevice(model->device));
     HC_CUDA(cudaStreamSynchronize(model->stream));
-    return HC_OK;
+    return hc::gemm_check(model->gemm_ws);
 }
 
 HC_EXPORT void* hc_model_stream(hc_model* model) { return model ? (void*)model->stream : nullptr; }
 
 HC_EXPORT int hc_kv_alloc(hc_model* model, int n_seqs, int max_pos, int kv_dtype, hc_kv** out) {
+    cudaGetLastError();  // a stale error of an earlier unrelated call is not ours
     HC_CHECK(model && out, HC_ERR_INVALID, "hc_kv_alloc: NULL argument");
     HC_CHECK(n_seqs > 0, HC_ERR_INVALID, "hc_kv_alloc: n_seqs must be > 0");
     HC_CHECK(kv_dtype == HC_KV_FP32 || kv_dtype == HC_KV_FP16, HC_ERR_INVALID, "hc_kv_alloc: bad kv dtype %d", kv_dtype);
@@ -667,6 +693,7 @@ HC_EXPORT int hc_kv_alloc(hc_model* model, int n_seqs, int max_pos, int kv_dtype
         return HC_ERR_OOM;
     }
     kv->pos_host.assign(n_seqs, 0);
+    model->refs++;
     HC_CUDA(cudaMemsetAsync(kv->pos_dev, 0, n_seqs * sizeof(int), model->stream));
     HC_CUDA(cudaMemsetAsync(kv->k, 0, bytes, model->stream));
     HC_CUDA(cudaMemsetAsync(kv->v, 0, bytes, model->stream));
@@ -684,10 +711,15 @@ HC_EXPORT int hc_kv_free(hc_kv* kv) {
     if (!kv) return HC_OK;
     cudaSetDevice(kv->model->device);
     cudaStreamSynchronize(kv->model->stream);
+    for (auto& g : kv->graphs)
+        if (g.exec) cudaGraphExecDestroy(g.exec);
     if (kv->k) cudaFree(kv->k);
     if (kv->v) cudaFree(kv->v);
     if (kv->pos_dev) cudaFree(kv->pos_dev);
+    hc_model* m = kv->model;
     delete kv;
+    model_release(m);
+    cudaGetLastError();  // leave no stale error for the caller's next call
     return HC_OK;
 }
 
@@ -714,6 +746,7 @@ HC_EXPORT int hc_kv_set_pos(hc_kv* kv, int seq, int pos) {
 }
 
 HC_EXPORT int hc_prefill(hc_model* m, hc_kv* kv, int seq, const uint32_t* ids, int T, float* logits_out) {
+    cudaGetLastError();  // a stale error of an earlier unrelated call is not ours
     HC_CHECK(m && kv && kv->model == m, HC_ERR_INVALID, "hc_prefill: bad model/kv");
     HC_CHECK(seq >= 0 && seq < kv->n_seqs, HC_ERR_INVALID, "hc_prefill: seq %d out of range", seq);
     HC_CHECK(T >= 0 && (T == 0 || ids), HC_ERR_INVALID, "hc_prefill: bad ids");
@@ -747,8 +780,11 @@ HC_EXPORT int hc_prefill(hc_model* m, hc_kv* kv, int seq, const uint32_t* ids, i
     if (logits_out)
         HC_CUDA(cudaMemcpyAsync(logits_out, s.logits, c.vocab_size * sizeof(float), cudaMemcpyDeviceToHost, m->stream));
     HC_CUDA(cudaStreamSynchronize(m->stream));
-    return HC_OK;
+    return hc::gemm_check(m->gemm_ws);
 }
+
+static int decode_graphed(hc_model* m, hc_kv* kv, const int* seqs_dev, const uint32_t* ids_dev, int B,
+                          float* logits_dev, uint32_t* argmax_dev);
 
 static int sync_pos(hc_kv* kv) {
     if (!kv->host_stale) return HC_OK;
@@ -773,6 +809,7 @@ static int check_decode_args(hc_model* m, hc_kv* kv, const int* seqs, int B) {
 
 HC_EXPORT int hc_decode_step(hc_model* m, hc_kv* kv, const int* seqs, const uint32_t* ids, int B, float* logits_out,
                              uint32_t* argmax_out) {
+    cudaGetLastError();  // a stale error of an earlier unrelated call is not ours
     HC_CHECK(m && kv && kv->model == m, HC_ERR_INVALID, "hc_decode_step: bad model/kv");
     HC_CHECK(B > 0 && seqs && ids, HC_ERR_INVALID, "hc_decode_step: bad batch");
     HC_CUDA(cudaSetDevice(m->device));
@@ -783,7 +820,7 @@ HC_EXPORT int hc_decode_step(hc_model* m, hc_kv* kv, const int* seqs, const uint
     HC_TRY(ensure_scratch(m, (size_t)B, (size_t)B));
     HC_CUDA(cudaMemcpyAsync(s.seqs, seqs, B * sizeof(int), cudaMemcpyHostToDevice, m->stream));
     HC_CUDA(cudaMemcpyAsync(s.ids, ids, B * sizeof(uint32_t), cudaMemcpyHostToDevice, m->stream));
-    HC_TRY(decode_dev_impl(m, kv, s.seqs, s.ids, B, s.logits, argmax_out ? s.argmax : nullptr));
+    HC_TRY(decode_graphed(m, kv, s.seqs, s.ids, B, s.logits, argmax_out ? s.argmax : nullptr));
     for (int b = 0; b < B; b++) kv->pos_host[seqs[b]] += 1;
     const size_t V = m->cfg.vocab_size;
     if (logits_out)
@@ -791,6 +828,60 @@ HC_EXPORT int hc_decode_step(hc_model* m, hc_kv* kv, const int* seqs, const uint
     if (argmax_out)
         HC_CUDA(cudaMemcpyAsync(argmax_out, s.argmax, B * sizeof(uint32_t), cudaMemcpyDeviceToHost, m->stream));
     HC_CUDA(cudaStreamSynchronize(m->stream));
+    return hc::gemm_check(m->gemm_ws);
+}
+
+static uint64_t model_generation(hc_model* m) { return m->sc.generation * 1000003ull + hc::gemm_generation(m->gemm_ws); }
+
+// One decode step on the model's stream, replayed from a CUDA graph after the
+// first call with the same key.  The first call runs eagerly (sizing every
+// workspace), then captures the same launch sequence for later replays.
+static int decode_graphed(hc_model* m, hc_kv* kv, const int* seqs_dev, const uint32_t* ids_dev, int B,
+                          float* logits_dev, uint32_t* argmax_dev) {
+    uint64_t gen = model_generation(m);
+    for (auto& g : kv->graphs) {
+        if (g.B == B && g.seqs == seqs_dev && g.ids == ids_dev && g.logits == logits_dev && g.argmax == argmax_dev &&
+            g.gen == gen && g.exec) {
+            HC_CUDA(cudaGraphLaunch(g.exec, m->stream));
+            return HC_OK;
+        }
+    }
+    HC_TRY(decode_dev_impl(m, kv, seqs_dev, ids_dev, B, logits_dev, argmax_dev));
+    gen = model_generation(m);  // the eager run may have grown a workspace
+    cudaGraph_t graph = nullptr;
+    HC_CUDA(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+    int r = decode_dev_impl(m, kv, seqs_dev, ids_dev, B, logits_dev, argmax_dev);
+    cudaError_t e = cudaStreamEndCapture(m->stream, &graph);
+    if (r != HC_OK || e != cudaSuccess || model_generation(m) != gen) {
+        if (graph) cudaGraphDestroy(graph);
+        cudaGetLastError();
+        return r != HC_OK ? r : HC_OK;  // the eager step already ran; stay uncaptured
+    }
+    cudaGraphExec_t exec = nullptr;
+    e = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return HC_OK;
+    }
+    // Replace a stale entry with the same pointers, or add one.
+    for (auto& g : kv->graphs) {
+        if (g.B == B && g.seqs == seqs_dev && g.ids == ids_dev && g.logits == logits_dev && g.argmax == argmax_dev) {
+            if (g.exec) cudaGraphExecDestroy(g.exec);
+            g.exec = exec;
+            g.gen = gen;
+            return HC_OK;
+        }
+    }
+    DecodeGraph g;
+    g.B = B;
+    g.seqs = seqs_dev;
+    g.ids = ids_dev;
+    g.logits = logits_dev;
+    g.argmax = argmax_dev;
+    g.gen = gen;
+    g.exec = exec;
+    kv->graphs.push_back(g);
     return HC_OK;
 }
 
@@ -801,7 +892,7 @@ HC_EXPORT int hc_decode_step_dev(hc_model* m, hc_kv* kv, const int* seqs_dev, co
     HC_CUDA(cudaSetDevice(m->device));
     // No host round trip: positions live on the device.  The kernels skip
     // stores past the cache capacity; hc_kv_seq_len reports the positions.
-    HC_TRY(decode_dev_impl(m, kv, seqs_dev, ids_dev, B, logits_dev, argmax_dev));
+    HC_TRY(decode_graphed(m, kv, seqs_dev, ids_dev, B, logits_dev, argmax_dev));
     kv->host_stale = true;
     return HC_OK;
 }

@@ -53,6 +53,18 @@ def test_q4_pack_unpack_bit_exact(cuda_device, kind):
     assert np.array_equal(d_gpu.view(np.uint32), d_ref.view(np.uint32))
 
 
+def test_q4_pack_byte_diagnostic(cuda_device):
+    """Localises any pack mismatch: per block, which of the 18 bytes differ."""
+    x = (np.random.default_rng(2).standard_normal(32 * 64) * 0.02).astype(np.float32)
+    q_gpu = np.frombuffer(ops.quantize_f32_to_q4_0(x), np.uint8).reshape(64, 18)
+    q_ref = np.frombuffer(orc.quantize_f32_to_q4_0(x), np.uint8).reshape(64, 18)
+    bad = np.argwhere(q_gpu != q_ref)
+    if bad.size:
+        print("mismatching (block, byte):", bad[:40].tolist())
+        print("gpu block0", q_gpu[0].tobytes().hex(), "ref block0", q_ref[0].tobytes().hex())
+    assert bad.size == 0
+
+
 def test_q4_empty_and_short(cuda_device):
     assert ops.quantize_f32_to_q4_0(np.zeros(31, np.float32)) == b""
     assert ops.dequantize_q4_0(b"\x00" * 17).size == 0
