@@ -257,10 +257,12 @@ def run_ours(args):
         dist.barrier()
     torch.cuda.synchronize()
     l0 = lib.hc_kernel_launches()
+    torch.cuda.nvtx.range_push("timed_decode")
     with ClockSampler(local, os.path.join(ROOT, "gpurun_out", f"clocks_rank{rank}.csv")
                       if os.path.isdir(os.path.join(ROOT, "gpurun_out")) else f"/tmp/hc_clocks_{rank}.csv") as clk:
         ms = cuda_time_ms(stream, step, args.steps) * args.steps
         torch.cuda.synchronize()
+    torch.cuda.nvtx.range_pop()
     launches = lib.hc_kernel_launches() - l0
     if dist:
         dist.barrier()

@@ -178,4 +178,426 @@ int launch_advance(const int* seqs, int* pos, int B, cudaStream_t s) {
     return HC_OK;
 }
 
+
+
+// ============================================================ grouped decode attention
+//
+// Decode attention for long contexts, grouped by KV head: one CTA per
+// (sequence, kv head, position split) serves all G = nh/nkv query heads of
+// the group, so each K/V row is read once per group instead of once per
+// query head.  The reference's softmax weight depends on the row maximum
+// through a polynomial (not an exponential), so partial results cannot be
+// rescaled: pass 1 writes the scores and a per-split maximum, pass 2 takes
+// the global maximum, forms the weights and the partial P.V, pass 3 (only
+// with several splits) adds the partials and normalises.
+namespace {
+
+template <typename KT>
+__device__ __forceinline__ void load_row8(const KT* p, float* f);
+template <>
+__device__ __forceinline__ void load_row8<__half>(const __half* p, float* f) {
+    uint4 u = *reinterpret_cast<const uint4*>(p);
+    const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        float2 v = __half22float2(h[i]);
+        f[2 * i] = v.x;
+        f[2 * i + 1] = v.y;
+    }
+}
+template <>
+__device__ __forceinline__ void load_row8<float>(const float* p, float* f) {
+    float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+}
+
+constexpr int DA_THREADS = 256;
+constexpr int DA_MAXG = 16;
+
+// Pass 1: S[row][h][p] = (q_h . k_p) * scale for p in this split, plus the
+// split's maximum per head.  One thread per position; q in shared memory.
+template <typename KT, int G>
+__global__ void __launch_bounds__(DA_THREADS) k_dattn_scores(DecAttnParams P) {
+    extern __shared__ float sq[];  // G * hd
+    __shared__ float red[32];
+    const int row = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
+    const int hd = P.hd;
+    const int seq = P.seqs[row];
+    const int n = min(P.pos[seq], P.max_pos);
+    const int p0 = split * P.chunk, p1 = min(n, p0 + P.chunk);
+    if (n <= 1) return;
+    for (int i = threadIdx.x; i < G * hd; i += DA_THREADS)
+        sq[i] = P.q[(size_t)row * P.ldq + (size_t)(kvh * G) * hd + i];
+    __syncthreads();
+    const KT* kbase = reinterpret_cast<const KT*>(P.kc) + (size_t)seq * P.seq_stride + (size_t)kvh * P.head_stride;
+    float mx[G];
+#pragma unroll
+    for (int g = 0; g < G; g++) mx[g] = -INFINITY;
+    for (int p = p0 + threadIdx.x; p < p1; p += DA_THREADS) {
+        const KT* kp = kbase + (size_t)p * hd;
+        float acc[G];
+#pragma unroll
+        for (int g = 0; g < G; g++) acc[g] = 0.0f;
+        for (int d = 0; d < hd; d += 8) {
+            float k8[8];
+            load_row8<KT>(kp + d, k8);
+#pragma unroll
+            for (int g = 0; g < G; g++) {
+                const float* qg = sq + g * hd + d;
+#pragma unroll
+                for (int j = 0; j < 8; j++) acc[g] = fmaf(qg[j], k8[j], acc[g]);
+            }
+        }
+        float* srow = P.S + ((size_t)row * P.nh + kvh * G) * P.max_pos + p;
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+            float s = __fmul_rn(acc[g], P.scale);
+            srow[(size_t)g * P.max_pos] = s;
+            mx[g] = fmaxf(mx[g], s);
+        }
+    }
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+        float m = block_max(mx[g], red);
+        if (threadIdx.x == 0) P.smax[((size_t)row * P.nh + kvh * G + g) * P.nsplit + split] = m;
+    }
+}
+
+// Pass 2: weights with the global maximum and the split's partial P.V.
+// Warp w takes positions w, w+8, ...; lane l takes features [4l, 4l+4).
+template <typename KT, int G>
+__global__ void __launch_bounds__(DA_THREADS) k_dattn_pv(DecAttnParams P) {
+    extern __shared__ float sw[];  // G * chunk weights, then 8 * G * hd partials
+    __shared__ float red[32];
+    __shared__ float gmax[DA_MAXG];
+    const int row = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
+    const int hd = P.hd;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int seq = P.seqs[row];
+    const int n = min(P.pos[seq], P.max_pos);
+    if (n <= 1) {
+        // p <= 1: the output is the token's own V (weight 1.0), transformer.rs:514-548
+        if (split == 0)
+            for (int i = threadIdx.x; i < G * hd; i += DA_THREADS) {
+                int g = i / hd, d = i % hd;
+                P.out[(size_t)row * P.ldo + (size_t)(kvh * G + g) * hd + d] =
+                    P.vself[(size_t)row * P.ldself + (size_t)kvh * hd + d];
+            }
+        return;
+    }
+    const int nsplit_eff = (n + P.chunk - 1) / P.chunk;
+    if (split >= nsplit_eff) return;
+    const int p0 = split * P.chunk, p1 = min(n, p0 + P.chunk), len = p1 - p0;
+    if (threadIdx.x < G) {
+        float m = -INFINITY;
+        for (int s = 0; s < nsplit_eff; s++)
+            m = fmaxf(m, P.smax[((size_t)row * P.nh + kvh * G + threadIdx.x) * P.nsplit + s]);
+        gmax[threadIdx.x] = m;
+    }
+    __syncthreads();
+    const int n8 = n - (n % 8);
+    float lsum[G];
+#pragma unroll
+    for (int g = 0; g < G; g++) lsum[g] = 0.0f;
+    for (int i = threadIdx.x; i < len; i += DA_THREADS) {
+        int p = p0 + i;
+        const float* srow = P.S + ((size_t)row * P.nh + kvh * G) * P.max_pos + p;
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+            float e = softmax_weight(srow[(size_t)g * P.max_pos], gmax[g], p, n8);
+            sw[g * P.chunk + i] = e;
+            lsum[g] += e;
+        }
+    }
+    float* part = sw + G * P.chunk;  // [8 warps][G][hd]
+    float total[G];
+#pragma unroll
+    for (int g = 0; g < G; g++) total[g] = block_sum(lsum[g], red);  // also a barrier for sw
+    const KT* vbase = reinterpret_cast<const KT*>(P.vc) + (size_t)seq * P.seq_stride + (size_t)kvh * P.head_stride;
+    for (int d0 = lane * 4; d0 < hd; d0 += 128) {
+        float acc[G][4];
+#pragma unroll
+        for (int g = 0; g < G; g++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) acc[g][j] = 0.0f;
+        for (int i = warp; i < len; i += 8) {
+            const KT* vp = vbase + (size_t)(p0 + i) * hd + d0;
+            float v4[4];
+            if constexpr (sizeof(KT) == 2) {
+                uint2 u = *reinterpret_cast<const uint2*>(vp);
+                float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+                float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+                v4[0] = a.x; v4[1] = a.y; v4[2] = b.x; v4[3] = b.y;
+            } else {
+                float4 a = *reinterpret_cast<const float4*>(vp);
+                v4[0] = a.x; v4[1] = a.y; v4[2] = a.z; v4[3] = a.w;
+            }
+#pragma unroll
+            for (int g = 0; g < G; g++) {
+                float w = sw[g * P.chunk + i];
+#pragma unroll
+                for (int j = 0; j < 4; j++) acc[g][j] = fmaf(w, v4[j], acc[g][j]);
+            }
+        }
+#pragma unroll
+        for (int g = 0; g < G; g++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) part[((size_t)warp * G + g) * hd + d0 + j] = acc[g][j];
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < G * hd; i += DA_THREADS) {
+        int g = i / hd, d = i % hd;
+        float o = 0.0f;
+#pragma unroll
+        for (int w = 0; w < 8; w++) o += part[((size_t)w * G + g) * hd + d];
+        size_t hidx = (size_t)row * P.nh + kvh * G + g;
+        if (nsplit_eff == 1) {
+            P.out[(size_t)row * P.ldo + (size_t)(kvh * G + g) * hd + d] = __fdiv_rn(o, total[g]);
+        } else {
+            P.opart[(hidx * P.nsplit + split) * hd + d] = o;
+            if (d == 0) P.spart[hidx * P.nsplit + split] = total[g];
+        }
+    }
+}
+
+// Pass 3 (several splits): out = sum of partial P.V / sum of partial weights.
+__global__ void k_dattn_combine(DecAttnParams P) {
+    const int row = blockIdx.x, h = blockIdx.y;
+    const int seq = P.seqs[row];
+    const int n = min(P.pos[seq], P.max_pos);
+    if (n <= 1) return;
+    const int nsplit_eff = (n + P.chunk - 1) / P.chunk;
+    if (nsplit_eff == 1) return;
+    size_t hidx = (size_t)row * P.nh + h;
+    float total = 0.0f;
+    for (int s = 0; s < nsplit_eff; s++) total += P.spart[hidx * P.nsplit + s];
+    for (int d = threadIdx.x; d < P.hd; d += blockDim.x) {
+        float o = 0.0f;
+        for (int s = 0; s < nsplit_eff; s++) o += P.opart[(hidx * P.nsplit + s) * P.hd + d];
+        P.out[(size_t)row * P.ldo + (size_t)h * P.hd + d] = __fdiv_rn(o, total);
+    }
+}
+
+template <typename KT, int G>
+int launch_dattn_g(const DecAttnParams& P, int rows, cudaStream_t s) {
+    dim3 grid((unsigned)rows, (unsigned)P.nkv, (unsigned)P.nsplit);
+    size_t smem1 = (size_t)G * P.hd * sizeof(float);
+    k_dattn_scores<KT, G><<<grid, DA_THREADS, smem1, s>>>(P);
+    HC_LAUNCH_CHECK();
+    size_t smem2 = ((size_t)G * P.chunk + 8 * (size_t)G * P.hd) * sizeof(float);
+    if (smem2 > 48 * 1024)
+        HC_CUDA(cudaFuncSetAttribute(k_dattn_pv<KT, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2));
+    k_dattn_pv<KT, G><<<grid, DA_THREADS, smem2, s>>>(P);
+    HC_LAUNCH_CHECK();
+    if (P.nsplit > 1) {
+        k_dattn_combine<<<dim3((unsigned)rows, (unsigned)P.nh), 128, 0, s>>>(P);
+        HC_LAUNCH_CHECK();
+    }
+    return HC_OK;
+}
+
+template <typename KT>
+int launch_dattn_kt(const DecAttnParams& P, int rows, cudaStream_t s) {
+    switch (P.nh / P.nkv) {
+        case 1: return launch_dattn_g<KT, 1>(P, rows, s);
+        case 2: return launch_dattn_g<KT, 2>(P, rows, s);
+        case 3: return launch_dattn_g<KT, 3>(P, rows, s);
+        case 4: return launch_dattn_g<KT, 4>(P, rows, s);
+        case 8: return launch_dattn_g<KT, 8>(P, rows, s);
+        default:
+            hc_set_error("grouped decode attention: unsupported group size %d", P.nh / P.nkv);
+            return HC_ERR_UNSUPPORTED;
+    }
+}
+
+}  // namespace
+
+bool dattn_supported(int nh, int nkv, int hd) {
+    int g = nh / nkv;
+    return hd % 8 == 0 && hd <= 512 && (g == 1 || g == 2 || g == 3 || g == 4 || g == 8);
+}
+
+int launch_decode_attention(const DecAttnParams& P, int rows, int kv_fp16, cudaStream_t s) {
+    if (rows == 0) return HC_OK;
+    return kv_fp16 ? launch_dattn_kt<__half>(P, rows, s) : launch_dattn_kt<float>(P, rows, s);
+}
+
+
+// ============================================================ tiled prefill attention
+//
+// turbo.rs:144-185 for a whole prompt: query t (t >= 2) attends prompt
+// positions [0, t); t < 2 takes its own V.  One CTA per (64-query block,
+// query head).  S = Q K^T tiles are formed in shared memory with a 4x4
+// micro-tile per thread (f32 FMA); pass 1 takes each row's maximum over all
+// its keys, pass 2 recomputes the tiles, forms the polynomial / exp weights
+// with that maximum and accumulates W V.
+namespace {
+
+constexpr int PA_BQ = 64, PA_BK = 64, PA_THREADS = 256, PA_KT_STRIDE = PA_BK + 4;
+
+template <int HD>
+__global__ void __launch_bounds__(PA_THREADS) k_pattn(AttnParams P, int T) {
+    extern __shared__ float sm[];
+    float* Qt = sm;                          // [HD][BQ]
+    float* Kt = Qt + HD * PA_BQ;             // [HD][BK + 4]   (also V tile [BK][HD])
+    float* W = Kt + HD * PA_KT_STRIDE;       // [BQ][BK]
+    const int t0 = blockIdx.x * PA_BQ, h = blockIdx.y;
+    const int kvh = h / (P.nh / P.nkv);
+    const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+    const int qend = min(t0 + PA_BQ, T);
+
+    // Q tile, transposed
+    for (int i = tid; i < PA_BQ * HD; i += PA_THREADS) {
+        int r = i / HD, d = i % HD;
+        int t = t0 + r;
+        Qt[d * PA_BQ + r] = (t < T) ? P.q[(size_t)t * P.ldq + (size_t)h * HD + d] : 0.0f;
+    }
+    const float* kb = P.kp + (size_t)kvh * HD;
+    const float* vb = P.vp + (size_t)kvh * HD;
+    const int nkt = (qend - 1 + PA_BK - 1) / PA_BK;  // key tiles covering keys < qend - 1
+
+    auto load_kt = [&](int s0) {
+        for (int i = tid; i < PA_BK * HD; i += PA_THREADS) {
+            int c = i / HD, d = i % HD;
+            int sidx = s0 + c;
+            Kt[d * PA_KT_STRIDE + c] = (sidx < T) ? kb[(size_t)sidx * P.ldkv + d] : 0.0f;
+        }
+    };
+    auto tile_s = [&](float (&acc)[4][4]) {
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) acc[i][j] = 0.0f;
+#pragma unroll 8
+        for (int d = 0; d < HD; d++) {
+            float4 q4 = *reinterpret_cast<const float4*>(Qt + d * PA_BQ + ty * 4);
+            float4 k4 = *reinterpret_cast<const float4*>(Kt + d * PA_KT_STRIDE + tx * 4);
+            float qv[4] = {q4.x, q4.y, q4.z, q4.w}, kv[4] = {k4.x, k4.y, k4.z, k4.w};
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) acc[i][j] = fmaf(qv[i], kv[j], acc[i][j]);
+        }
+    };
+
+    // ---- pass 1: row maxima over keys s < t
+    float rmax[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+    for (int kt = 0; kt < nkt; kt++) {
+        __syncthreads();
+        load_kt(kt * PA_BK);
+        __syncthreads();
+        float acc[4][4];
+        tile_s(acc);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            int t = t0 + ty * 4 + i;
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                int sidx = kt * PA_BK + tx * 4 + j;
+                if (sidx < t) rmax[i] = fmaxf(rmax[i], __fmul_rn(acc[i][j], P.scale));
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) rmax[i] = fmaxf(rmax[i], __shfl_xor_sync(0xffffffffu, rmax[i], o));
+
+    // ---- pass 2: weights and W V
+    constexpr int DC = HD / 16;  // output columns per thread
+    float o[4][DC];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < DC; j++) o[i][j] = 0.0f;
+    float rsum[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (int kt = 0; kt < nkt; kt++) {
+        __syncthreads();
+        load_kt(kt * PA_BK);
+        __syncthreads();
+        float acc[4][4];
+        tile_s(acc);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            int t = t0 + ty * 4 + i;
+            int n8 = t - (t % 8);
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                int sidx = kt * PA_BK + tx * 4 + j;
+                float w = 0.0f;
+                if (sidx < t) w = softmax_weight(__fmul_rn(acc[i][j], P.scale), rmax[i], sidx, n8);
+                rsum[i] += w;
+                W[(ty * 4 + i) * PA_BK + tx * 4 + j] = w;
+            }
+        }
+        __syncthreads();
+        // V tile [BK][HD] into the K buffer
+        float* Vs = Kt;
+        for (int i = tid; i < PA_BK * HD; i += PA_THREADS) {
+            int c = i / HD, d = i % HD;
+            int sidx = kt * PA_BK + c;
+            Vs[c * HD + d] = (sidx < T) ? vb[(size_t)sidx * P.ldkv + d] : 0.0f;
+        }
+        __syncthreads();
+#pragma unroll 4
+        for (int k = 0; k < PA_BK; k++) {
+            float wv[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) wv[i] = W[(ty * 4 + i) * PA_BK + k];
+            const float* vr = Vs + k * HD + tx * DC;
+#pragma unroll
+            for (int j = 0; j < DC; j++) {
+                float v = vr[j];
+#pragma unroll
+                for (int i = 0; i < 4; i++) o[i][j] = fmaf(wv[i], v, o[i][j]);
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int off = 8; off > 0; off >>= 1) rsum[i] += __shfl_xor_sync(0xffffffffu, rsum[i], off);
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        int t = t0 + ty * 4 + i;
+        if (t >= T) continue;
+        float* out = P.out + (size_t)t * P.ldo + (size_t)h * HD + tx * DC;
+        if (t < 2) {
+            const float* vs = P.vself + (size_t)t * P.ldself + (size_t)kvh * HD + tx * DC;
+#pragma unroll
+            for (int j = 0; j < DC; j++) out[j] = vs[j];
+        } else {
+#pragma unroll
+            for (int j = 0; j < DC; j++) out[j] = __fdiv_rn(o[i][j], rsum[i]);
+        }
+    }
+}
+
+template <int HD>
+int launch_pattn_hd(const AttnParams& P, int T, cudaStream_t s) {
+    size_t smem = ((size_t)HD * PA_BQ + (size_t)HD * PA_KT_STRIDE + (size_t)PA_BQ * PA_BK) * sizeof(float);
+    if (smem > 48 * 1024) HC_CUDA(cudaFuncSetAttribute(k_pattn<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    dim3 grid((unsigned)((T + PA_BQ - 1) / PA_BQ), (unsigned)P.nh);
+    k_pattn<HD><<<grid, PA_THREADS, smem, s>>>(P, T);
+    HC_LAUNCH_CHECK();
+    return HC_OK;
+}
+
+}  // namespace
+
+bool pattn_supported(int hd) { return hd == 16 || hd == 32 || hd == 64 || hd == 128; }
+
+int launch_prefill_attention(const AttnParams& P, int T, cudaStream_t s) {
+    if (T == 0) return HC_OK;
+    switch (P.hd) {
+        case 16: return launch_pattn_hd<16>(P, T, s);
+        case 32: return launch_pattn_hd<32>(P, T, s);
+        case 64: return launch_pattn_hd<64>(P, T, s);
+        case 128: return launch_pattn_hd<128>(P, T, s);
+        default:
+            hc_set_error("tiled prefill attention: unsupported head_dim %d", P.hd);
+            return HC_ERR_UNSUPPORTED;
+    }
+}
+
 }  // namespace hc

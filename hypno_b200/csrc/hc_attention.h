@@ -33,4 +33,33 @@ int launch_kv_store(const float* k, const float* v, size_t ld, int rows, int nkv
                     const int* pos, int fixed_seq, int pos0, cudaStream_t s);
 int launch_advance(const int* seqs, int* pos, int B, cudaStream_t s);
 
+// Grouped (GQA) split-position decode attention, see hc_attention.cu.
+struct DecAttnParams {
+    const float* q;       // query rows, head h at q + row*ldq + h*hd
+    size_t ldq;
+    float* out;
+    size_t ldo;
+    const float* vself;   // own f32 V of each row, kv head at + kvh*hd
+    size_t ldself;
+    int nh, nkv, hd;
+    float scale;
+    const void* kc;       // cache for this layer: [seq][.][kvh][max_pos][hd]
+    const void* vc;
+    size_t seq_stride, head_stride;
+    const int* seqs;
+    const int* pos;
+    int max_pos;
+    int chunk;            // positions per split
+    int nsplit;           // splits launched (>= ceil(max n / chunk))
+    float* S;             // scores [rows][nh][max_pos]
+    float* smax;          // [rows][nh][nsplit]
+    float* opart;         // [rows][nh][nsplit][hd]
+    float* spart;         // [rows][nh][nsplit]
+};
+bool dattn_supported(int nh, int nkv, int hd);
+// Tiled f32 prefill attention over the prompt's own K/V rows (mode_prefill).
+bool pattn_supported(int hd);
+int launch_prefill_attention(const AttnParams& P, int T, cudaStream_t s);
+int launch_decode_attention(const DecAttnParams& P, int rows, int kv_fp16, cudaStream_t s);
+
 }  // namespace hc

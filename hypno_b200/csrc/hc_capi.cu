@@ -36,6 +36,7 @@ HC_EXPORT const char* hc_last_error(void) { return g_err.c_str(); }
 
 static std::atomic<unsigned long long> g_launches{0};
 void hc_count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+void hc_count_launches(size_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 HC_EXPORT uint64_t hc_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }
 
 HC_EXPORT int hc_version(void) { return 100; }

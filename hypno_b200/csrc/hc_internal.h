@@ -39,6 +39,7 @@ int hc_cuda_fail(cudaError_t e, const char* what, const char* file, int line);
 // Launch-error check after a kernel launch; also counts the launch (every
 // kernel launch of the library is followed by this macro).
 void hc_count_launch();
+void hc_count_launches(size_t n);
 #define HC_LAUNCH_CHECK()          \
     do {                           \
         hc_count_launch();         \

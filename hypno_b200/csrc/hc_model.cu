@@ -193,6 +193,9 @@ struct Scratch {
     int* seqs = nullptr;
     int* rowpos = nullptr;
     uint32_t* argmax = nullptr;
+    // grouped decode attention workspace
+    size_t attn_cap = 0;
+    float* attn_ws = nullptr;
 };
 
 struct hc_model {
@@ -218,6 +221,7 @@ struct DecodeGraph {
     const void *seqs = nullptr, *ids = nullptr;
     void *logits = nullptr, *argmax = nullptr;
     uint64_t gen = 0;
+    size_t kernels = 0;  // kernel nodes in the graph (counted per replay)
     cudaGraphExec_t exec = nullptr;
 };
 
@@ -361,7 +365,7 @@ void free_model(hc_model* m) {
     if (m->stream) cudaStreamSynchronize(m->stream);
     for (void* p : m->allocs) cudaFree(p);
     void* scr[] = {m->sc.hidden, m->sc.xn, m->sc.qkv, m->sc.attn, m->sc.gu, m->sc.act, m->sc.logits, m->sc.ids,
-                   m->sc.seqs, m->sc.rowpos, m->sc.argmax, m->rope};
+                   m->sc.seqs, m->sc.rowpos, m->sc.argmax, m->rope, m->sc.attn_ws};
     for (void* p : scr)
         if (p) cudaFree(p);
     if (m->gemm_ws) hc::gemm_workspace_free(m->gemm_ws);
@@ -415,6 +419,20 @@ int ensure_rope(hc_model* m, size_t rows) {
     return HC_OK;
 }
 
+int ensure_attn_ws(hc_model* m, size_t rows, size_t nh, size_t max_pos, size_t nsplit, size_t hd) {
+    Scratch& s = m->sc;
+    size_t need = rows * nh * (max_pos + 2 * nsplit + nsplit * hd);
+    if (need > s.attn_cap) {
+        if (s.attn_ws) cudaFree(s.attn_ws);
+        s.attn_ws = nullptr;
+        s.attn_cap = 0;
+        HC_CUDA(cudaMalloc((void**)&s.attn_ws, need * sizeof(float)));
+        s.attn_cap = need;
+        s.generation++;
+    }
+    return HC_OK;
+}
+
 // y = W . x for `tokens` rows (the Q4_0 path picks the CUDA-core matvec for
 // few tokens and the tcgen05 GEMM otherwise).
 int matmul(hc_model* m, const DevWeight& w, const float* x, size_t ldx, size_t tokens, float* y, size_t ldy, int epi,
@@ -462,7 +480,43 @@ int run_layers(hc_model* m, hc_kv* kv, size_t rows, bool prefill, int seq, int p
             P.kp = s.qkv + nq;
             P.vp = s.qkv + nq + nk;
             P.ldkv = ldqkv;
-            HC_TRY(hc::launch_attention(P, (int)rows, 0, m->stream));
+            if (hc::pattn_supported((int)hd))
+                HC_TRY(hc::launch_prefill_attention(P, (int)rows, m->stream));
+            else
+                HC_TRY(hc::launch_attention(P, (int)rows, 0, m->stream));
+        } else if (hc::dattn_supported((int)nh_l, (int)nkv_l, (int)hd)) {
+            hc::DecAttnParams D{};
+            D.q = s.qkv;
+            D.ldq = ldqkv;
+            D.out = s.attn;
+            D.ldo = nq;
+            D.vself = s.qkv + nq + nk;
+            D.ldself = ldqkv;
+            D.nh = (int)nh_l;
+            D.nkv = (int)nkv_l;
+            D.hd = (int)hd;
+            D.scale = scale;
+            D.kc = kc;
+            D.vc = vc;
+            D.seq_stride = kv->seq_stride;
+            D.head_stride = kv->head_stride;
+            D.seqs = s.seqs;
+            D.pos = kv->pos_dev;
+            D.max_pos = kv->max_pos;
+            const int G = (int)(nh_l / nkv_l);
+            int max_chunk = (40960 - 8 * G * (int)hd) / G;
+            int want_splits = (int)std::max<size_t>(1, (296 + rows * nkv_l - 1) / (rows * nkv_l));
+            int chunk = std::max(256, (kv->max_pos + want_splits - 1) / want_splits);
+            chunk = std::min(chunk, max_chunk);
+            chunk = std::min(chunk, kv->max_pos);
+            D.chunk = chunk;
+            D.nsplit = (kv->max_pos + chunk - 1) / chunk;
+            HC_TRY(ensure_attn_ws(m, rows, nh_l, (size_t)kv->max_pos, (size_t)D.nsplit, hd));
+            D.S = s.attn_ws;
+            D.smax = D.S + rows * nh_l * (size_t)kv->max_pos;
+            D.spart = D.smax + rows * nh_l * (size_t)D.nsplit;
+            D.opart = D.spart + rows * nh_l * (size_t)D.nsplit;
+            HC_TRY(hc::launch_decode_attention(D, (int)rows, kv->kv_fp16, m->stream));
         } else {
             P.mode_prefill = 0;
             P.smem_n = kv->max_pos;
@@ -843,6 +897,7 @@ static int decode_graphed(hc_model* m, hc_kv* kv, const int* seqs_dev, const uin
         if (g.B == B && g.seqs == seqs_dev && g.ids == ids_dev && g.logits == logits_dev && g.argmax == argmax_dev &&
             g.gen == gen && g.exec) {
             HC_CUDA(cudaGraphLaunch(g.exec, m->stream));
+            hc_count_launches(g.kernels);
             return HC_OK;
         }
     }
@@ -857,6 +912,18 @@ static int decode_graphed(hc_model* m, hc_kv* kv, const int* seqs_dev, const uin
         cudaGetLastError();
         return r != HC_OK ? r : HC_OK;  // the eager step already ran; stay uncaptured
     }
+    size_t kernels = 0;
+    {
+        size_t nn = 0;
+        if (cudaGraphGetNodes(graph, nullptr, &nn) == cudaSuccess && nn) {
+            std::vector<cudaGraphNode_t> nodes(nn);
+            if (cudaGraphGetNodes(graph, nodes.data(), &nn) == cudaSuccess)
+                for (auto nd : nodes) {
+                    cudaGraphNodeType t;
+                    if (cudaGraphNodeGetType(nd, &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) kernels++;
+                }
+        }
+    }
     cudaGraphExec_t exec = nullptr;
     e = cudaGraphInstantiate(&exec, graph, 0);
     cudaGraphDestroy(graph);
@@ -870,6 +937,7 @@ static int decode_graphed(hc_model* m, hc_kv* kv, const int* seqs_dev, const uin
             if (g.exec) cudaGraphExecDestroy(g.exec);
             g.exec = exec;
             g.gen = gen;
+            g.kernels = kernels;
             return HC_OK;
         }
     }
@@ -880,6 +948,7 @@ static int decode_graphed(hc_model* m, hc_kv* kv, const int* seqs_dev, const uin
     g.logits = logits_dev;
     g.argmax = argmax_dev;
     g.gen = gen;
+    g.kernels = kernels;
     g.exec = exec;
     kv->graphs.push_back(g);
     return HC_OK;

@@ -176,3 +176,40 @@ def test_c3_greedy_32_steps(cuda_device):
     assert m.config.lm_head_tied == 1 and m.config.embed_dtype == hf.DT_Q4_0
     om = orc.OracleModel(img)
     compare(run_greedy_gpu(m, prompt, 32), run_greedy_oracle(om, prompt, 32), "c3")
+
+
+C4_GEOMETRY = dict(hidden=1024, layers=2, heads=8, kv_heads=2, inter=2816, vocab=8192, theta=500000.0,
+                   max_pos=1024, embed="q4", lm_head="tied")
+
+
+@pytest.mark.parametrize("kv_dtype", [engine.KV_FP32, engine.KV_FP16])
+def test_c4_geometry_batched_decode(cuda_device, kv_dtype):
+    """head_dim 128, 4 query heads per KV head, theta 5e5 (configs[3]'s
+    attention geometry) on a 2-layer model: ragged prompts (600, 300, 17, 1
+    and 0 tokens) prefilled, then batched greedy decode vs the oracle; fp16 KV
+    within the same tolerance."""
+    from hypno_b200 import synth as sy
+    img = sy.build_image(C4_GEOMETRY, seed=3, quantize=orc.quantize_f32_to_q4_0)
+    m = engine.HypnoModel(img)
+    om = orc.OracleModel(img)
+    lens = [600, 300, 17, 1, 0]
+    kv = engine.KVCache(m, n_seqs=len(lens), max_pos=1024, kv_dtype=kv_dtype)
+    okvs, toks = [], []
+    for s, T in enumerate(lens):
+        p = sy.prompt_ids(C4_GEOMETRY["vocab"], T, seed=10 + s)
+        g = engine.batch_forward(m, p, kv, seq=s)
+        okv = om.new_kv(1024)
+        r = orc.batch_forward(om, p, okv)
+        assert rel_err(g, r) <= TOL, (s, rel_err(g, r))
+        okvs.append(okv)
+        toks.append(orc.greedy(r) if T else 5)
+    seqs = list(range(len(lens)))
+    for step in range(6):
+        lg, am = engine.decode_step(m, kv, seqs, toks)
+        nxt = []
+        for s in seqs:
+            ref = orc.model_forward(om, toks[s], okvs[s])
+            assert rel_err(lg[s], ref) <= TOL, (step, s, rel_err(lg[s], ref))
+            assert int(am[s]) == orc.greedy(ref), (step, s, margin(ref))
+            nxt.append(int(am[s]))
+        toks = nxt

@@ -50,7 +50,11 @@ def test_q4_pack_unpack_bit_exact(cuda_device, kind):
     assert q_gpu == q_ref
     d_gpu = ops.dequantize_q4_0(q_gpu)
     d_ref = orc.dequantize_q4_0(q_ref)
-    assert np.array_equal(d_gpu.view(np.uint32), d_ref.view(np.uint32))
+    # 0 * inf scales give NaN on both sides; NaN payloads differ between the
+    # GPU's canonical NaN and x86's default NaN, every other value is bit-equal
+    nan = np.isnan(d_ref)
+    assert np.array_equal(nan, np.isnan(d_gpu))
+    assert np.array_equal(d_gpu[~nan].view(np.uint32), d_ref[~nan].view(np.uint32))
 
 
 def test_q4_pack_byte_diagnostic(cuda_device):
