@@ -167,6 +167,63 @@ def roofline_gemv(dev, M=32, N=28672, K=4096, copies=4, reps=20):
             "avg_launch_us": round(ms * 1e3, 2), "peak_source": f"{src} (hbm_gbs)"}
 
 
+def q4_sweep(dev, reps=10):
+    """Y = X W^T for (N, K) in the sweep and M in {1, 8, 64, 512},
+    each timed with CUDA events over rotating weight copies (> L2 in total).
+    M <= 64 is graded against HBM bandwidth, M = 512 against dense tensor peak."""
+    import torch
+    from hypno_b200 import synth
+    from hypno_b200._lib import call
+    peak_gbs, src = measured_peaks()
+    peak_tf = None
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            peak_tf = float(json.load(f).get("bf16_tflops", 0)) or None
+    peak_tf = peak_tf or 1590.0
+    out = []
+    stream = torch.cuda.current_stream().cuda_stream
+    for (N, K) in synth.SWEEP_NK:
+        wbytes = N * K // 32 * 18
+        copies = max(2, min(6, -(-400 * 2 ** 20 // wbytes)))
+        w32 = torch.empty(N * K, dtype=torch.float32, device=dev)
+        wq = torch.empty(wbytes, dtype=torch.uint8, device=dev)
+        mats = []
+        for c in range(copies):
+            call("hc_synth_normal_dev", 200 + c, synth.fnv1a64(f"sweep.W.{N}x{K}"), 0, N * K, 0.02, w32.data_ptr(), None)
+            call("hc_q4_0_quantize_dev", w32.data_ptr(), N * K, wq.data_ptr(), None)
+            h = ctypes.c_void_p()
+            call("hc_q4_matrix_from_dev", wq.data_ptr(), wbytes, N, K, None, ctypes.byref(h))
+            mats.append(h)
+        torch.cuda.synchronize()
+        del w32, wq
+        for M in synth.SWEEP_M:
+            X = torch.empty(M * K, dtype=torch.float32, device=dev)
+            call("hc_synth_normal_dev", 1, synth.fnv1a64(f"sweep.X.{M}x{K}"), 0, M * K, 1.0, X.data_ptr(), None)
+            Y = torch.empty(M * N, dtype=torch.float32, device=dev)
+
+            def run(i):
+                call("hc_q4_matmul_dev", mats[i % copies], X.data_ptr(), M, Y.data_ptr(), stream)
+
+            for i in range(3):
+                run(i)
+            ms = cuda_time_ms(stream, run, reps)
+            algo = 0.5625 * N * K + 4.0 * M * K + 4.0 * M * N
+            flops = 2.0 * M * N * K
+            row = {"N": N, "K": K, "M": M, "us": round(ms * 1e3, 2), "gbs": round(algo / (ms * 1e-3) / 1e9, 1),
+                   "tflops": round(flops / (ms * 1e-3) / 1e12, 2)}
+            if M <= 64:
+                row["bound"], row["frac"] = "hbm", round(row["gbs"] / peak_gbs, 4)
+            else:
+                row["bound"], row["frac"] = "tensor", round(row["tflops"] / peak_tf, 4)
+            out.append(row)
+            del X, Y
+        for h in mats:
+            call("hc_q4_matrix_free", h)
+        torch.cuda.empty_cache()
+    return {"rows": out, "peaks": {"hbm_gbs": peak_gbs, "bf16_tflops": peak_tf, "source": src}}
+
+
 def cpu_baseline(img, cfg, budget_s=12.0, max_tokens=24):
     """The oracle decoding one sequence at context 2048 on the host cores."""
     from oracle import oracle as orc
@@ -297,6 +354,7 @@ def run_ours(args):
            "h2d_bytes_per_step": 2 * 4 * S, "d2h_bytes_per_step": 4 * S}
 
     roof = roofline_gemv(dev) if rank == 0 else None
+    sweep = q4_sweep(dev) if rank == 0 and not args.no_sweep else None
     cpu = None
     if rank == 0 and not args.no_cpu:
         cpu = cpu_baseline(img, cfg)
@@ -308,7 +366,7 @@ def run_ours(args):
                 "scaling": "weak", "vs_baseline": None, "dtype": "q4_0 weights, f32 compute", "data": "synthetic",
                 "config": workload_config(world), "e2e": e2e, "gpu_launches": int(launches),
                 "prefill_tok_s": round(prefill_tok_s, 1), "clocks": clk.summary(), "roofline": roof,
-                "cpu_baseline": cpu}
+                "cpu_baseline": cpu, "q4_sweep": sweep}
         print(json.dumps(line), flush=True)
     kv.close()
     model.close()
@@ -353,6 +411,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the configs[1] operator sweep report")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

@@ -215,45 +215,66 @@ constexpr int DA_THREADS = 256;
 constexpr int DA_MAXG = 16;
 
 // Pass 1: S[row][h][p] = (q_h . k_p) * scale for p in this split, plus the
-// split's maximum per head.  One thread per position; q in shared memory.
-template <typename KT, int G>
+// split's maximum per head.  One thread per position: the whole K row is
+// requested before any arithmetic (HD/8 16-byte loads in flight per thread),
+// q sits transposed in shared memory so one broadcast read serves all G heads.
+template <typename KT, int G, int HD>
 __global__ void __launch_bounds__(DA_THREADS) k_dattn_scores(DecAttnParams P) {
-    extern __shared__ float sq[];  // G * hd
+    __shared__ float sq[HD * G];  // [d][g]
     __shared__ float red[32];
     const int row = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
-    const int hd = P.hd;
     const int seq = P.seqs[row];
     const int n = min(P.pos[seq], P.max_pos);
     const int p0 = split * P.chunk, p1 = min(n, p0 + P.chunk);
     if (n <= 1) return;
-    for (int i = threadIdx.x; i < G * hd; i += DA_THREADS)
-        sq[i] = P.q[(size_t)row * P.ldq + (size_t)(kvh * G) * hd + i];
+    for (int i = threadIdx.x; i < G * HD; i += DA_THREADS) {
+        int g = i / HD, d = i % HD;
+        sq[d * G + g] = P.q[(size_t)row * P.ldq + (size_t)(kvh * G) * HD + i];
+    }
     __syncthreads();
     const KT* kbase = reinterpret_cast<const KT*>(P.kc) + (size_t)seq * P.seq_stride + (size_t)kvh * P.head_stride;
     float mx[G];
 #pragma unroll
     for (int g = 0; g < G; g++) mx[g] = -INFINITY;
     for (int p = p0 + threadIdx.x; p < p1; p += DA_THREADS) {
-        const KT* kp = kbase + (size_t)p * hd;
+        const KT* kp = kbase + (size_t)p * HD;
+        constexpr int NV = HD * (int)sizeof(KT) / 16;  // 16-byte vectors per row
+        uint4 raw[NV];
+#pragma unroll
+        for (int v = 0; v < NV; v++) raw[v] = __ldg(reinterpret_cast<const uint4*>(kp) + v);
         float acc[G];
 #pragma unroll
         for (int g = 0; g < G; g++) acc[g] = 0.0f;
-        for (int d = 0; d < hd; d += 8) {
-            float k8[8];
-            load_row8<KT>(kp + d, k8);
 #pragma unroll
-            for (int g = 0; g < G; g++) {
-                const float* qg = sq + g * hd + d;
+        for (int v = 0; v < NV; v++) {
+            constexpr int EPV = 16 / (int)sizeof(KT);
+            float k8[EPV];
+            if constexpr (sizeof(KT) == 2) {
+                const __half2* h2 = reinterpret_cast<const __half2*>(&raw[v]);
 #pragma unroll
-                for (int j = 0; j < 8; j++) acc[g] = fmaf(qg[j], k8[j], acc[g]);
+                for (int i = 0; i < 4; i++) {
+                    float2 f = __half22float2(h2[i]);
+                    k8[2 * i] = f.x;
+                    k8[2 * i + 1] = f.y;
+                }
+            } else {
+                const float* f = reinterpret_cast<const float*>(&raw[v]);
+#pragma unroll
+                for (int i = 0; i < 4; i++) k8[i] = f[i];
+            }
+#pragma unroll
+            for (int e = 0; e < EPV; e++) {
+                const float* qd = sq + (v * EPV + e) * G;
+#pragma unroll
+                for (int g = 0; g < G; g++) acc[g] = fmaf(qd[g], k8[e], acc[g]);
             }
         }
         float* srow = P.S + ((size_t)row * P.nh + kvh * G) * P.max_pos + p;
 #pragma unroll
         for (int g = 0; g < G; g++) {
-            float s = __fmul_rn(acc[g], P.scale);
-            srow[(size_t)g * P.max_pos] = s;
-            mx[g] = fmaxf(mx[g], s);
+            float sc = __fmul_rn(acc[g], P.scale);
+            srow[(size_t)g * P.max_pos] = sc;
+            mx[g] = fmaxf(mx[g], sc);
         }
     }
 #pragma unroll
@@ -320,23 +341,38 @@ __global__ void __launch_bounds__(DA_THREADS) k_dattn_pv(DecAttnParams P) {
         for (int g = 0; g < G; g++)
 #pragma unroll
             for (int j = 0; j < 4; j++) acc[g][j] = 0.0f;
-        for (int i = warp; i < len; i += 8) {
-            const KT* vp = vbase + (size_t)(p0 + i) * hd + d0;
-            float v4[4];
-            if constexpr (sizeof(KT) == 2) {
-                uint2 u = *reinterpret_cast<const uint2*>(vp);
-                float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
-                float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
-                v4[0] = a.x; v4[1] = a.y; v4[2] = b.x; v4[3] = b.y;
-            } else {
-                float4 a = *reinterpret_cast<const float4*>(vp);
-                v4[0] = a.x; v4[1] = a.y; v4[2] = a.z; v4[3] = a.w;
+        // 4 positions per iteration: four independent row loads in flight per lane
+        constexpr int U = 4;
+        for (int i0 = warp; i0 < len; i0 += 8 * U) {
+            float v4[U][4];
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                int i = i0 + 8 * u;
+                if (i < len) {
+                    const KT* vp = vbase + (size_t)(p0 + i) * hd + d0;
+                    if constexpr (sizeof(KT) == 2) {
+                        uint2 uu = __ldg(reinterpret_cast<const uint2*>(vp));
+                        float2 a = __half22float2(*reinterpret_cast<const __half2*>(&uu.x));
+                        float2 b = __half22float2(*reinterpret_cast<const __half2*>(&uu.y));
+                        v4[u][0] = a.x; v4[u][1] = a.y; v4[u][2] = b.x; v4[u][3] = b.y;
+                    } else {
+                        float4 a = __ldg(reinterpret_cast<const float4*>(vp));
+                        v4[u][0] = a.x; v4[u][1] = a.y; v4[u][2] = a.z; v4[u][3] = a.w;
+                    }
+                } else {
+                    v4[u][0] = v4[u][1] = v4[u][2] = v4[u][3] = 0.0f;
+                }
             }
 #pragma unroll
-            for (int g = 0; g < G; g++) {
-                float w = sw[g * P.chunk + i];
+            for (int u = 0; u < U; u++) {
+                int i = i0 + 8 * u;
+                if (i >= len) break;
 #pragma unroll
-                for (int j = 0; j < 4; j++) acc[g][j] = fmaf(w, v4[j], acc[g][j]);
+                for (int g = 0; g < G; g++) {
+                    float w = sw[g * P.chunk + i];
+#pragma unroll
+                    for (int j = 0; j < 4; j++) acc[g][j] = fmaf(w, v4[u][j], acc[g][j]);
+                }
             }
         }
 #pragma unroll
@@ -381,8 +417,15 @@ __global__ void k_dattn_combine(DecAttnParams P) {
 template <typename KT, int G>
 int launch_dattn_g(const DecAttnParams& P, int rows, cudaStream_t s) {
     dim3 grid((unsigned)rows, (unsigned)P.nkv, (unsigned)P.nsplit);
-    size_t smem1 = (size_t)G * P.hd * sizeof(float);
-    k_dattn_scores<KT, G><<<grid, DA_THREADS, smem1, s>>>(P);
+    switch (P.hd) {
+        case 16: k_dattn_scores<KT, G, 16><<<grid, DA_THREADS, 0, s>>>(P); break;
+        case 32: k_dattn_scores<KT, G, 32><<<grid, DA_THREADS, 0, s>>>(P); break;
+        case 64: k_dattn_scores<KT, G, 64><<<grid, DA_THREADS, 0, s>>>(P); break;
+        case 128: k_dattn_scores<KT, G, 128><<<grid, DA_THREADS, 0, s>>>(P); break;
+        default:
+            hc_set_error("grouped decode attention: unsupported head_dim %d", P.hd);
+            return HC_ERR_UNSUPPORTED;
+    }
     HC_LAUNCH_CHECK();
     size_t smem2 = ((size_t)G * P.chunk + 8 * (size_t)G * P.hd) * sizeof(float);
     if (smem2 > 48 * 1024)
@@ -414,7 +457,7 @@ int launch_dattn_kt(const DecAttnParams& P, int rows, cudaStream_t s) {
 
 bool dattn_supported(int nh, int nkv, int hd) {
     int g = nh / nkv;
-    return hd % 8 == 0 && hd <= 512 && (g == 1 || g == 2 || g == 3 || g == 4 || g == 8);
+    return (hd == 16 || hd == 32 || hd == 64 || hd == 128) && (g == 1 || g == 2 || g == 3 || g == 4 || g == 8);
 }
 
 int launch_decode_attention(const DecAttnParams& P, int rows, int kv_fp16, cudaStream_t s) {

@@ -40,9 +40,7 @@ namespace {
 
 constexpr int BM = 128;      // weight rows per tile (MMA M)
 constexpr int BK = 128;      // K per pipeline stage
-constexpr int NTHREADS = 384;
 constexpr int TMEM_COLS = 512;
-constexpr int D_COL = 256;   // accumulator column base; A stages use [0, 64 * STAGES)
 constexpr long long WAIT_CYCLES = 4000000000LL;  // ~2 s at 1.9 GHz
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -160,39 +158,69 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
                  : "memory");
 }
 
-// Two nibbles (low = element 2j, high = element 2j+1 of byte j) -> fp16x2 of
-// (nib - 8) * scale, the low half holding the lower K index.  1024 + nib is
-// exact in fp16 (0x6400 | nib); subtracting 1032 is exact; the product by the
-// fp16 scale rounds once, like converting the exact f32 product to fp16.
-__device__ __forceinline__ uint32_t deq_pair(uint32_t lo_nibs, uint32_t hi_nibs, int j, __half2 s2) {
-    uint32_t sel = (uint32_t)j | ((uint32_t)(j + 4) << 8);  // byte0 <- lo byte j, byte2 <- hi byte j
-    uint32_t v = __byte_perm(lo_nibs, hi_nibs, sel) & 0x000F000Fu;
-    v |= 0x64006400u;
+// K order inside a 32-element Q4_0 block.  Word i (4 bytes = elements
+// 8i..8i+7, low nibble first) yields four fp16 pairs with one shift and one
+// and/or each: pair k = (element 8i+k, element 8i+k+4).  The A operand (the
+// weights) is therefore laid out along K in the order
+//   position 8i+2k <- element 8i+k,   position 8i+2k+1 <- element 8i+k+4,
+// and the B operand (the activations) is written in the same order by
+// k_rows_to_f16_perm, so every dot product sees matching pairs.
+// (nib + 1024) is exact in fp16 (0x6400 | nib); subtracting 1032 is exact;
+// multiplying by the fp16 scale rounds once: fp16((nib - 8) * scale).
+__device__ __forceinline__ uint32_t deq_pair(uint32_t w, int k, __half2 s2) {
+    uint32_t v = ((w >> (4 * k)) & 0x000F000Fu) | 0x64006400u;
     __half2 h = *reinterpret_cast<__half2*>(&v);
     h = __hsub2(h, __float2half2_rn(1032.0f));
     h = __hmul2(h, s2);
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
-struct SmemLayout {
-    int stages, tn;
-    __host__ __device__ constexpr int x_stage_bytes() const { return 2 * tn * 128; }
-    __host__ __device__ constexpr int w_stage_bytes() const { return BM * (BK / 2); }
-    __host__ __device__ constexpr int x_off(int s) const { return s * x_stage_bytes(); }
-    __host__ __device__ constexpr int w_off(int s) const { return stages * x_stage_bytes() + s * w_stage_bytes(); }
-    __host__ __device__ constexpr int bar_off() const { return stages * (x_stage_bytes() + w_stage_bytes()); }
-    __host__ __device__ constexpr int total() const { return bar_off() + (3 * stages + 1) * 8 + 16 + 1024; }
+__device__ __forceinline__ void tmem_st_x16(uint32_t taddr, const uint32_t* v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
+}
+
+// Warp-uniform bounded wait: lane 0 polls, the verdict is broadcast, then
+// every lane observes the completed phase once itself (acquire ordering for
+// its own reads of the data the barrier guards).
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+    bool ok = true;
+    if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort_flag);
+    ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+    if (ok) (void)mbar_try_wait(bar, parity);
+    return ok;
+}
+
+template <int TN>
+struct Cfg {
+    static constexpr int STAGES = TN <= 64 ? 7 : (TN == 128 ? 5 : 3);
+    static constexpr int A_COL = TN <= 64 ? 64 : TN;  // A stages start here; D occupies [0, TN)
+    static constexpr int X_STAGE = 2 * TN * 128;      // two 64-element K halves, 128 B per token row
+    static constexpr int W_STAGE = BM * (BK / 2);     // 128 rows x 64 nibble bytes
+    __host__ __device__ static constexpr int x_off(int s) { return s * X_STAGE; }
+    __host__ __device__ static constexpr int w_off(int s) { return STAGES * X_STAGE + s * W_STAGE; }
+    __host__ __device__ static constexpr int bar_off() { return STAGES * (X_STAGE + W_STAGE); }
+    __host__ __device__ static constexpr int smem() { return bar_off() + (3 * STAGES + 1) * 8 + 16 + 1024; }
+    static_assert(A_COL + 64 * STAGES <= TMEM_COLS, "tensor memory budget");
 };
 
-template <int TN, int STAGES>
-__global__ void __launch_bounds__(NTHREADS, 1)
+constexpr int NDEQ_WARPS = 16;                  // 4 warpgroups, one Q4_0 block of the stage each
+constexpr int GEMM_THREADS = 128 + 32 * NDEQ_WARPS;
+
+template <int TN>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
     k_q4_gemm_tc(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
                  const __half* __restrict__ scales, float* __restrict__ y, size_t ldy, const float* res, size_t ldres,
-                 int epi, int N, int K, int T, int* __restrict__ err) {
+                 int epi, int N, int K, int T, int splits, float* __restrict__ partial, int* __restrict__ err) {
+    using C = Cfg<TN>;
+    constexpr int STAGES = C::STAGES;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    constexpr SmemLayout L{STAGES, TN};
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off());
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::bar_off());
     uint64_t* aready = full + STAGES;
     uint64_t* empty = aready + STAGES;
     uint64_t* dfull = empty + STAGES;
@@ -200,16 +228,18 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     __shared__ int abort_flag;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * BM, t0 = blockIdx.y * TN;
+    const int n0 = blockIdx.x * BM, t0 = blockIdx.y * TN, split = blockIdx.z;
     const int KB = K / 32;
-    const int nk = K / BK;
+    const int nk_all = K / BK;
+    const int it0 = (int)((long long)nk_all * split / splits), it1 = (int)((long long)nk_all * (split + 1) / splits);
+    const int nk = it1 - it0;
 
     if (threadIdx.x == 0) {
         abort_flag = 0;
-        for (int s = 0; s < STAGES; s++) {
-            mbar_init(&full[s], 1);
-            mbar_init(&aready[s], 8);
-            mbar_init(&empty[s], 1);
+        for (int st = 0; st < STAGES; st++) {
+            mbar_init(&full[st], 1);
+            mbar_init(&aready[st], NDEQ_WARPS);
+            mbar_init(&empty[st], 1);
         }
         mbar_init(dfull, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -228,104 +258,98 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     if (warp == 0) {
         // ---------------- TMA producer
         if (lane == 0) {
-            for (int it = 0; it < nk; it++) {
-                int s = it % STAGES;
-                uint32_t ph = (uint32_t)(it / STAGES) & 1u;
-                if (!mbar_wait(&empty[s], ph ^ 1u, &abort_flag)) break;
-                mbar_expect_tx(&full[s], (uint32_t)(L.x_stage_bytes() + L.w_stage_bytes()));
-                uint8_t* xs = smem + L.x_off(s);
-                tma_load_2d(xs, &xmap, &full[s], it * BK, t0);
-                tma_load_2d(xs + TN * 128, &xmap, &full[s], it * BK + 64, t0);
-                tma_load_2d(smem + L.w_off(s), &wmap, &full[s], it * (BK / 2), n0);
+            for (int j = 0; j < nk; j++) {
+                int st = j % STAGES;
+                uint32_t ph = (uint32_t)(j / STAGES) & 1u;
+                if (!mbar_wait(&empty[st], ph ^ 1u, &abort_flag)) break;
+                mbar_expect_tx(&full[st], (uint32_t)(C::X_STAGE + C::W_STAGE));
+                uint8_t* xs = smem + C::x_off(st);
+                int kk = (it0 + j) * BK;
+                tma_load_2d(xs, &xmap, &full[st], kk, t0);
+                tma_load_2d(xs + TN * 128, &xmap, &full[st], kk + 64, t0);
+                tma_load_2d(smem + C::w_off(st), &wmap, &full[st], kk / 2, n0);
             }
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer
         if (lane == 0) {
             constexpr uint32_t idesc = make_idesc(TN);
-            const uint32_t d_tmem = tmem + D_COL;
             bool ok = true;
-            for (int it = 0; it < nk && ok; it++) {
-                int s = it % STAGES;
-                uint32_t ph = (uint32_t)(it / STAGES) & 1u;
-                if (!mbar_wait(&aready[s], ph, &abort_flag)) {
+            for (int j = 0; j < nk; j++) {
+                int st = j % STAGES;
+                uint32_t ph = (uint32_t)(j / STAGES) & 1u;
+                if (!mbar_wait(&aready[st], ph, &abort_flag)) {
                     ok = false;
                     break;
                 }
                 tmem_fence_after();
-                const uint32_t xs = smem_u32(smem + L.x_off(s));
+                const uint32_t xs = smem_u32(smem + C::x_off(st));
 #pragma unroll
                 for (int kk = 0; kk < BK / 16; kk++) {
-                    uint32_t a_tmem = tmem + (uint32_t)(s * 64 + kk * 8);
+                    uint32_t a_tmem = tmem + (uint32_t)(C::A_COL + st * 64 + kk * 8);
                     uint32_t b_addr = xs + (uint32_t)((kk >> 2) * TN * 128 + (kk & 3) * 32);
-                    mma_f16_ts(d_tmem, a_tmem, sw128_desc(b_addr), idesc, (it > 0 || kk > 0) ? 1u : 0u);
+                    mma_f16_ts(tmem, a_tmem, sw128_desc(b_addr), idesc, (j > 0 || kk > 0) ? 1u : 0u);
                 }
-                mma_commit(&empty[s]);
+                mma_commit(&empty[st]);
             }
             if (ok) mma_commit(dfull);
         }
     } else if (warp >= 4) {
-        // ---------------- dequant: thread <-> weight row (TMEM lane)
-        const int g = (warp - 4) >> 2;   // warpgroup: K half of the stage
-        const int q = warp & 3;          // TMEM lane quarter accessible to this warp
-        const int r = q * 32 + lane;     // row within the tile
+        // ---------------- dequant: thread <-> weight row (TMEM lane), warpgroup <-> Q4_0 block of the stage
+        const int g = (warp - 4) >> 2;   // block 0..3 of the 128-element stage
+        const int q = warp & 3;          // TMEM lane quarter of this warp
+        const int r = q * 32 + lane;
         const int n = n0 + r;
         const bool row_ok = n < N;
         const __half* srow = scales + (size_t)(row_ok ? n : 0) * KB;
-        uint32_t sc_next = row_ok ? __ldg(reinterpret_cast<const unsigned int*>(srow + 2 * g)) : 0u;
+        unsigned short sc_next = row_ok ? __ldg(reinterpret_cast<const unsigned short*>(srow) + it0 * 4 + g) : 0;
         bool ok = true;
-        for (int it = 0; it < nk; it++) {
-            int s = it % STAGES;
-            uint32_t ph = (uint32_t)(it / STAGES) & 1u;
-            uint32_t sc = sc_next;
-            if (it + 1 < nk && row_ok)
-                sc_next = __ldg(reinterpret_cast<const unsigned int*>(srow + (it + 1) * (BK / 32) + 2 * g));
-            bool w1 = mbar_wait(&empty[s], ph ^ 1u, &abort_flag);
-            bool w2 = w1 && mbar_wait(&full[s], ph, &abort_flag);
-            if (!__all_sync(0xffffffffu, w2)) {
+        for (int j = 0; j < nk; j++) {
+            int st = j % STAGES;
+            uint32_t ph = (uint32_t)(j / STAGES) & 1u;
+            unsigned short sc = sc_next;
+            if (j + 1 < nk && row_ok)
+                sc_next = __ldg(reinterpret_cast<const unsigned short*>(srow) + (it0 + j + 1) * 4 + g);
+            if (!warp_wait(&empty[st], ph ^ 1u, &abort_flag) || !warp_wait(&full[st], ph, &abort_flag)) {
                 ok = false;
                 break;
             }
-            const uint4* nib = reinterpret_cast<const uint4*>(smem + L.w_off(s) + r * (BK / 2) + g * 32);
-            uint32_t v[32];
+            uint4 q4 = *reinterpret_cast<const uint4*>(smem + C::w_off(st) + r * (BK / 2) + g * 16);
+            __half2 s2 = __half2half2(__ushort_as_half(sc));
+            uint32_t v[16];
+            const uint32_t w4[4] = {q4.x, q4.y, q4.z, q4.w};
 #pragma unroll
-            for (int b = 0; b < 2; b++) {  // two Q4_0 blocks of 32 elements
-                uint4 q4 = nib[b];
-                __half2 s2 = __half2half2(__ushort_as_half((uint16_t)(b == 0 ? (sc & 0xFFFF) : (sc >> 16))));
-                uint32_t w4[4] = {q4.x, q4.y, q4.z, q4.w};
+            for (int wd = 0; wd < 4; wd++)
 #pragma unroll
-                for (int wd = 0; wd < 4; wd++) {
-                    uint32_t lo = w4[wd] & 0x0F0F0F0Fu, hi = (w4[wd] >> 4) & 0x0F0F0F0Fu;
-#pragma unroll
-                    for (int j = 0; j < 4; j++) v[b * 16 + wd * 4 + j] = deq_pair(lo, hi, j, s2);
-                }
-            }
-            uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(s * 64 + g * 32);
-            tmem_st_x32(taddr, v);
+                for (int k = 0; k < 4; k++) v[wd * 4 + k] = deq_pair(w4[wd], k, s2);
+            tmem_st_x16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(C::A_COL + st * 64 + g * 16), v);
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             tmem_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&aready[s]);
+            if (lane == 0) mbar_arrive(&aready[st]);
         }
-        // ---------------- epilogue (first dequant warpgroup)
+        // ---------------- epilogue (first warpgroup)
         if (g == 0) {
-            bool okd = ok && mbar_wait(dfull, 0, &abort_flag);
-            okd = __all_sync(0xffffffffu, okd);
+            bool okd = ok && warp_wait(dfull, 0, &abort_flag);
             if (okd) {
                 tmem_fence_after();
 #pragma unroll 1
                 for (int c0 = 0; c0 < TN; c0 += 32) {
                     uint32_t v[32];
-                    tmem_ld_x32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(D_COL + c0), v);
+                    tmem_ld_x32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
                     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
                     if (row_ok) {
 #pragma unroll
-                        for (int j = 0; j < 32; j++) {
-                            int t = t0 + c0 + j;
+                        for (int jj = 0; jj < 32; jj++) {
+                            int t = t0 + c0 + jj;
                             if (t < T) {
-                                float o = __uint_as_float(v[j]);
-                                if (epi == EPI_ADD && res) o = o + res[(size_t)t * ldres + n];
-                                y[(size_t)t * ldy + n] = o;
+                                float o = __uint_as_float(v[jj]);
+                                if (splits > 1) {
+                                    partial[((size_t)split * T + t) * N + n] = o;
+                                } else {
+                                    if (epi == EPI_ADD && res) o = o + res[(size_t)t * ldres + n];
+                                    y[(size_t)t * ldy + n] = o;
+                                }
                             }
                         }
                     }
@@ -342,13 +366,29 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     if (threadIdx.x == 0 && abort_flag) atomicExch(err, 1);
 }
 
-// fp32 rows -> fp16 rows (the B operand of the MMA).
-__global__ void k_rows_to_f16(const float* __restrict__ x, size_t ldx, __half* __restrict__ out, int K, int T) {
+// y[t][n] = (res[t][n] +) sum_s partial[s][t][n], in split order.
+__global__ void k_splitk_reduce(const float* __restrict__ partial, int splits, int T, int N, float* y, size_t ldy,
+                                int epi, const float* res, size_t ldres) {
+    size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (size_t)T * N) return;
+    int t = (int)(i / N), n = (int)(i % N);
+    float o = partial[i];
+    for (int sp = 1; sp < splits; sp++) o += partial[(size_t)sp * T * N + i];
+    if (epi == EPI_ADD && res) o = o + res[(size_t)t * ldres + n];
+    y[(size_t)t * ldy + n] = o;
+}
+
+// fp32 rows -> fp16 rows in the K order of the weight tiles (see deq_pair):
+// within every 8 elements, [e0 e4 e1 e5 e2 e6 e3 e7].
+__global__ void k_rows_to_f16_perm(const float* __restrict__ x, size_t ldx, __half* __restrict__ out, int K, int T) {
     int t = blockIdx.y;
     const float* xr = x + (size_t)t * ldx;
     __half2* o = reinterpret_cast<__half2*>(out + (size_t)t * K);
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < K / 2; i += gridDim.x * blockDim.x)
-        o[i] = __floats2half2_rn(xr[2 * i], xr[2 * i + 1]);
+    for (int gi = blockIdx.x * blockDim.x + threadIdx.x; gi < K / 8; gi += gridDim.x * blockDim.x) {
+        const float* e = xr + 8 * gi;
+#pragma unroll
+        for (int k = 0; k < 4; k++) o[4 * gi + k] = __floats2half2_rn(e[k], e[k + 4]);
+    }
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
@@ -378,10 +418,6 @@ int encode_2d(CUtensorMap* map, CUtensorMapDataType dt, void* base, uint64_t inn
     return HC_OK;
 }
 
-template <int TN, int STAGES>
-int launch_tc(GemmWorkspace* ws, const hc_q4_matrix& w, const CUtensorMap& xmap, const CUtensorMap& wmap, size_t T,
-              float* y, size_t ldy, int epi, const float* res, size_t ldres, int* err, cudaStream_t s);
-
 }  // namespace
 
 struct GemmWorkspace {
@@ -389,6 +425,8 @@ struct GemmWorkspace {
     uint64_t generation = 0;  // bumped whenever a buffer a launch refers to moves
     __half* xh = nullptr;
     size_t xh_cap = 0;
+    float* part = nullptr;    // split-K partial sums
+    size_t part_cap = 0;
     int* err = nullptr;
     int device = -1;
     std::map<std::tuple<const void*, size_t, size_t>, CUtensorMap> wmaps;  // (nibble plane, n, k)
@@ -399,6 +437,7 @@ GemmWorkspace* gemm_workspace_new() { return new GemmWorkspace(); }
 void gemm_workspace_free(GemmWorkspace* ws) {
     if (!ws) return;
     if (ws->xh) cudaFree(ws->xh);
+    if (ws->part) cudaFree(ws->part);
     if (ws->err) cudaFree(ws->err);
     delete ws;
 }
@@ -408,20 +447,47 @@ bool gemm_tc_eligible(const hc_q4_matrix& w, size_t tokens) {
 }
 
 namespace {
-template <int TN, int STAGES>
-int launch_tc(GemmWorkspace* ws, const hc_q4_matrix& w, const CUtensorMap& xmap, const CUtensorMap& wmap, size_t T,
-              float* y, size_t ldy, int epi, const float* res, size_t ldres, int* err, cudaStream_t s) {
-    constexpr SmemLayout L{STAGES, TN};
-    static_assert(L.total() <= 232448, "shared memory budget");
-    auto kfn = k_q4_gemm_tc<TN, STAGES>;
+template <int TN>
+int launch_tc(const hc_q4_matrix& w, const CUtensorMap& xmap, const CUtensorMap& wmap, size_t T, float* y,
+              size_t ldy, int epi, const float* res, size_t ldres, int splits, float* partial, int* err,
+              cudaStream_t s) {
+    using C = Cfg<TN>;
+    static_assert(C::smem() <= 232448, "shared memory budget");
+    auto kfn = k_q4_gemm_tc<TN>;
     // At least 116 KB of shared memory keeps one CTA per SM, so two CTAs never
     // contend for the 512 tensor-memory columns each allocates.
-    const int smem = L.total() < 118784 ? 118784 : L.total();
+    const int smem = C::smem() < 118784 ? 118784 : C::smem();
     HC_CUDA(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    dim3 grid((unsigned)((w.n + BM - 1) / BM), (unsigned)((T + TN - 1) / TN));
-    kfn<<<grid, NTHREADS, smem, s>>>(xmap, wmap, w.sc, y, ldy, res, ldres, epi, (int)w.n, (int)w.k, (int)T, err);
+    dim3 grid((unsigned)((w.n + BM - 1) / BM), (unsigned)((T + TN - 1) / TN), (unsigned)splits);
+    kfn<<<grid, GEMM_THREADS, smem, s>>>(xmap, wmap, w.sc, y, ldy, res, ldres, epi, (int)w.n, (int)w.k, (int)T, splits,
+                                         partial, err);
     HC_LAUNCH_CHECK();
+    if (splits > 1) {
+        size_t tot = T * w.n;
+        k_splitk_reduce<<<(unsigned)((tot + 255) / 256), 256, 0, s>>>(partial, splits, (int)T, (int)w.n, y, ldy, epi,
+                                                                        res, ldres);
+        HC_LAUNCH_CHECK();
+    }
     return HC_OK;
+}
+
+// Split K so that row tiles x token tiles x splits fills the 148 SMs
+// (one CTA per SM) without splits shorter than 4 pipeline stages.
+int choose_splits(size_t tiles, size_t nk) {
+    const size_t sms = 148;
+    if (tiles >= sms) return 1;
+    size_t best = 1;
+    double best_eff = (double)tiles / (double)sms;
+    for (size_t sp = 2; sp <= 16 && nk / sp >= 4; sp++) {
+        size_t ctas = tiles * sp;
+        size_t waves = (ctas + sms - 1) / sms;
+        double eff = (double)ctas / (double)(waves * sms);
+        if (eff > best_eff + 1e-9) {
+            best_eff = eff;
+            best = sp;
+        }
+    }
+    return (int)best;
 }
 }  // namespace
 
@@ -450,8 +516,8 @@ int gemm_tc(GemmWorkspace* ws, const hc_q4_matrix& w, const float* x, size_t ldx
         ws->xh_cap = T * K;
     }
     {
-        unsigned gx = (unsigned)std::min<size_t>((K / 2 + 255) / 256, 16);
-        k_rows_to_f16<<<dim3(gx, (unsigned)T), 256, 0, s>>>(x, ldx, ws->xh, (int)K, (int)T);
+        unsigned gx = (unsigned)std::min<size_t>((K / 8 + 255) / 256, 16);
+        k_rows_to_f16_perm<<<dim3(gx, (unsigned)T), 256, 0, s>>>(x, ldx, ws->xh, (int)K, (int)T);
         HC_LAUNCH_CHECK();
     }
     // Token tile: the smallest of 32/64/128/256 covering T (one tile for decode).
@@ -469,11 +535,21 @@ int gemm_tc(GemmWorkspace* ws, const hc_q4_matrix& w, const float* x, size_t ldx
                          CU_TENSOR_MAP_SWIZZLE_NONE));
         if (w.owns) ws->wmaps[key] = wmap;
     }
+    size_t tiles = ((w.n + BM - 1) / BM) * ((T + tn - 1) / tn);
+    int splits = choose_splits(tiles, K / BK);
+    if (splits > 1 && (size_t)splits * T * w.n > ws->part_cap) {
+        if (ws->part) cudaFree(ws->part);
+        ws->part = nullptr;
+        ws->part_cap = 0;
+        ws->generation++;
+        HC_CUDA(cudaMalloc((void**)&ws->part, (size_t)splits * T * w.n * sizeof(float)));
+        ws->part_cap = (size_t)splits * T * w.n;
+    }
     switch (tn) {
-        case 32: return launch_tc<32, 4>(ws, w, xmap, wmap, T, y, ldy, epi, res, ldres, ws->err, s);
-        case 64: return launch_tc<64, 4>(ws, w, xmap, wmap, T, y, ldy, epi, res, ldres, ws->err, s);
-        case 128: return launch_tc<128, 4>(ws, w, xmap, wmap, T, y, ldy, epi, res, ldres, ws->err, s);
-        default: return launch_tc<256, 3>(ws, w, xmap, wmap, T, y, ldy, epi, res, ldres, ws->err, s);
+        case 32: return launch_tc<32>(w, xmap, wmap, T, y, ldy, epi, res, ldres, splits, ws->part, ws->err, s);
+        case 64: return launch_tc<64>(w, xmap, wmap, T, y, ldy, epi, res, ldres, splits, ws->part, ws->err, s);
+        case 128: return launch_tc<128>(w, xmap, wmap, T, y, ldy, epi, res, ldres, splits, ws->part, ws->err, s);
+        default: return launch_tc<256>(w, xmap, wmap, T, y, ldy, epi, res, ldres, splits, ws->part, ws->err, s);
     }
 }
 
