@@ -18,9 +18,11 @@ One step = one batched decode step of all 32 sequences (32 tokens).
            HBM copy bandwidth.
   cpu_baseline  : the CPU oracle (restatement of hypno's CPU path) decoding
            one sequence at context 2048 on the host cores (rank 0).
-With --gpus N > 1 (torchrun), every rank runs an independent replica of the
-workload (the model fits one GPU; tensor parallelism is not on this path yet):
-weak scaling, value = all ranks' tokens / the slowest rank's time.
+With --gpus N > 1 (torchrun) the model is tensor-parallel over the N ranks
+(attention heads and FFN columns sharded, NCCL
+all-reduce after o_proj / down_proj, vocabulary-sharded LM head): the same
+32 sequences, strong scaling, value = 32 x steps / the slowest rank's time.
+--parallel dp instead runs N independent replicas (weak scaling).
 --impl reference times the CPU oracle on the same workload (rank 0 only).
 """
 import argparse
@@ -242,11 +244,12 @@ def cpu_baseline(img, cfg, budget_s=12.0, max_tokens=24):
                       f"{n} tokens in {dt:.1f} s; the reference serialises sequences (serve.rs:175,193)"}
 
 
-def workload_config(world):
+def workload_config(world, mode="tp"):
+    par = "single" if world == 1 else (f"tp{world}" if mode == "tp" else f"replicas{world}")
     return {"workload": "c4 decode: Llama-3-8B shape (hidden 4096, 32 layers, 32/8 heads, im 14336, vocab 128256), "
                         "32 sequences each prefilled with 2048 random tokens, greedy batched decode, fp16 KV",
             "model": "llama-3-8b-shape-random-q4_0", "global_batch": 32 * world, "seq_len": 2048,
-            "parallelism": f"replicas{world}" if world > 1 else "single",
+            "parallelism": par,
             "l2": "inputs larger than L2 (4.22 GB of Q4_0 weights + ~8.6 GB KV read per step)"}
 
 
@@ -270,8 +273,12 @@ def run_ours(args):
     call("hc_set_device", local)
     cfg = synth.CONFIGS["c4"]
     S, P = cfg["seqs"], cfg["prompt"]
+    tp = world > 1 and args.parallel == "tp"
     img = synth.build_image(cfg, seed=0, device=dev)
-    model = engine.HypnoModel(img)
+    model = engine.HypnoModel(img, rank if tp else 0, world if tp else 1)
+    if tp:
+        from hypno_b200 import tp as tpmod
+        tpmod.join(model, rank, world)
     if rank != 0:
         del img
         img = None
@@ -326,7 +333,8 @@ def run_ours(args):
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    value = world * S * args.steps / (ms * 1e-3)
+    jobs = 1 if tp else world  # tensor parallel: one model instance across all ranks
+    value = jobs * S * args.steps / (ms * 1e-3)
 
     # ---- end to end through the host-buffer C ABI call
     reset_pos()
@@ -350,7 +358,7 @@ def run_ours(args):
         t = torch.tensor([e2e_s], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
-    e2e = {"value": round(world * S * args.steps / e2e_s, 2), "unit": UNIT,
+    e2e = {"value": round(jobs * S * args.steps / e2e_s, 2), "unit": UNIT,
            "h2d_bytes_per_step": 2 * 4 * S, "d2h_bytes_per_step": 4 * S}
 
     roof = roofline_gemv(dev) if rank == 0 else None
@@ -363,8 +371,8 @@ def run_ours(args):
     if rank == 0:
         line = {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "q4_0 weights, f32 compute", "data": "synthetic",
-                "config": workload_config(world), "e2e": e2e, "gpu_launches": int(launches),
+                "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": "q4_0 weights, f32 compute", "data": "synthetic",
+                "config": workload_config(world, "tp" if tp else "dp"), "e2e": e2e, "gpu_launches": int(launches),
                 "prefill_tok_s": round(prefill_tok_s, 1), "clocks": clk.summary(), "roofline": roof,
                 "cpu_baseline": cpu, "q4_sweep": sweep}
         print(json.dumps(line), flush=True)
@@ -412,6 +420,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-sweep", action="store_true", help="skip the configs[1] operator sweep report")
+    ap.add_argument("--parallel", default="tp", choices=["tp", "dp"],
+                    help="N > 1: tensor parallel over the ranks (default) or independent replicas")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

@@ -96,6 +96,8 @@ SIGNATURES = {
     "hc_prefill": (_I, [_P, _P, _I, _P, _I, _P]),
     "hc_decode_step": (_I, [_P, _P, _P, _P, _I, _P, _P]),
     "hc_decode_step_dev": (_I, [_P, _P, _P, _P, _I, _P, _P]),
+    "hc_comm_unique_id": (_I, [_P]),
+    "hc_comm_init": (_I, [_P, _P, _I, _I, ctypes.c_double]),
     "hc_synth_normal_host": (_I, [_U64, _U64, _U64, _U64, _F, _P]),
     "hc_synth_normal_dev": (_I, [_U64, _U64, _U64, _U64, _F, _P, _P]),
 }

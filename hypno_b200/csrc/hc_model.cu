@@ -6,6 +6,7 @@
 #include "hc_internal.h"
 #include "hc_attention.h"
 #include "hc_gemm.h"
+#include "hc_comm.h"
 
 #include <algorithm>
 #include <cmath>
@@ -193,6 +194,8 @@ struct Scratch {
     int* seqs = nullptr;
     int* rowpos = nullptr;
     uint32_t* argmax = nullptr;
+    float* tp_tmp = nullptr;      // [tokens][hidden] partial sums to all-reduce
+    float* tp_gather = nullptr;   // [tp][rows][vocab_shard] gathered logits
     // grouped decode attention workspace
     size_t attn_cap = 0;
     float* attn_ws = nullptr;
@@ -212,6 +215,11 @@ struct hc_model {
     Scratch sc;
     std::vector<void*> allocs;
     hc::GemmWorkspace* gemm_ws = nullptr;
+    // tensor parallelism: this rank's vocabulary slice of the LM head, the
+    // communicator, and the host watchdog limit for one step
+    size_t vocab0 = 0, vocab_shard = 0;
+    hc::Comm* comm = nullptr;
+    double comm_timeout_s = 60.0;
 };
 
 // A captured decode step: replayed while the key (batch, device pointers,
@@ -369,6 +377,9 @@ void free_model(hc_model* m) {
     for (void* p : scr)
         if (p) cudaFree(p);
     if (m->gemm_ws) hc::gemm_workspace_free(m->gemm_ws);
+    if (m->sc.tp_tmp) cudaFree(m->sc.tp_tmp);
+    if (m->sc.tp_gather) cudaFree(m->sc.tp_gather);
+    if (m->comm) hc::comm_free(m->comm);
     if (m->stream) cudaStreamDestroy(m->stream);
     delete m;
 }
@@ -389,6 +400,9 @@ int ensure_scratch(hc_model* m, size_t tokens, size_t logit_rows) {
         if (s.ids) cudaFree(s.ids);
         if (s.seqs) cudaFree(s.seqs);
         if (s.rowpos) cudaFree(s.rowpos);
+        if (s.tp_tmp) cudaFree(s.tp_tmp);
+        s.tp_tmp = nullptr;
+        if (m->cfg.tp_size > 1) HC_CUDA(cudaMalloc((void**)&s.tp_tmp, t * c.hidden_size * sizeof(float)));
         HC_CUDA(cudaMalloc((void**)&s.ids, t * sizeof(uint32_t)));
         HC_CUDA(cudaMalloc((void**)&s.seqs, t * sizeof(int)));
         HC_CUDA(cudaMalloc((void**)&s.rowpos, t * sizeof(int)));
@@ -400,6 +414,10 @@ int ensure_scratch(hc_model* m, size_t tokens, size_t logit_rows) {
         if (s.logits) cudaFree(s.logits);
         if (s.argmax) cudaFree(s.argmax);
         HC_CUDA(cudaMalloc((void**)&s.logits, r * c.vocab_size * sizeof(float)));
+        if (s.tp_gather) cudaFree(s.tp_gather);
+        s.tp_gather = nullptr;
+        if (m->cfg.tp_size > 1)
+            HC_CUDA(cudaMalloc((void**)&s.tp_gather, r * m->vocab_shard * m->cfg.tp_size * sizeof(float)));
         HC_CUDA(cudaMalloc((void**)&s.argmax, r * sizeof(uint32_t)));
         s.cap_logit_rows = r;
         s.generation++;
@@ -440,6 +458,67 @@ int matmul(hc_model* m, const DevWeight& w, const float* x, size_t ldx, size_t t
     if (w.dtype == HC_DTYPE_Q4_0 && hc::gemm_tc_eligible(w.q4, tokens))
         return hc::gemm_tc(m->gemm_ws, w.q4, x, ldx, tokens, y, ldy, epi, res, ldres, m->stream);
     return hc::launch_matmul(w, x, ldx, tokens, y, ldy, epi, res, ldres, m->stream);
+}
+
+__global__ void k_add_rows(float* __restrict__ y, const float* __restrict__ a, size_t n) {
+    size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) y[i] = a[i] + y[i];
+}
+
+// hidden (+)= W x for a projection whose K dimension is split across the
+// tensor-parallel ranks (o_proj, down_proj): each rank's partial product is
+// summed by an all-reduce, then added to the residual stream (the reference's
+// `hidden[i] = residual[i] + proj[i]`, transformer.rs:561-563, 595-598).
+int row_parallel(hc_model* m, const DevWeight& w, const float* x, size_t ldx, size_t rows) {
+    const size_t H = m->cfg.hidden_size;
+    Scratch& s = m->sc;
+    if (m->cfg.tp_size <= 1) return matmul(m, w, x, ldx, rows, s.hidden, H, hc::EPI_ADD, s.hidden, H);
+    HC_CHECK(m->comm, HC_ERR_STATE, "tensor-parallel model used before hc_comm_init");
+    HC_TRY(matmul(m, w, x, ldx, rows, s.tp_tmp, H, hc::EPI_STORE, nullptr, 0));
+    HC_TRY(hc::comm_allreduce_sum(m->comm, s.tp_tmp, rows * H, m->stream));
+    size_t n = rows * H;
+    k_add_rows<<<(unsigned)((n + 255) / 256), 256, 0, m->stream>>>(s.hidden, s.tp_tmp, n);
+    HC_LAUNCH_CHECK();
+    return HC_OK;
+}
+
+__global__ void k_unshard_logits(const float* __restrict__ g, float* __restrict__ out, int rows, int vs, int tp) {
+    size_t n = (size_t)rows * vs * tp;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        size_t r = i / ((size_t)vs * tp), rem = i % ((size_t)vs * tp);
+        size_t rank = rem / vs, v = rem % vs;
+        out[i] = g[(rank * rows + r) * vs + v];
+    }
+}
+
+// logits[rows][vocab] = W_lm x; with tensor parallelism each rank computes
+// its vocabulary slice and the slices are all-gathered.
+int lm_head_logits(hc_model* m, const float* x, size_t rows, float* logits) {
+    const hc_config& c = m->cfg;
+    if (!m->lm_head.present) {
+        HC_CUDA(cudaMemsetAsync(logits, 0, rows * c.vocab_size * sizeof(float), m->stream));
+        return HC_OK;
+    }
+    if (c.tp_size <= 1)
+        return matmul(m, m->lm_head, x, c.hidden_size, rows, logits, c.vocab_size, hc::EPI_STORE, nullptr, 0);
+    HC_CHECK(m->comm, HC_ERR_STATE, "tensor-parallel model used before hc_comm_init");
+    const size_t vs = m->vocab_shard;
+    float* mine = m->sc.tp_gather + (size_t)c.tp_rank * rows * vs;
+    HC_TRY(matmul(m, m->lm_head, x, c.hidden_size, rows, mine, vs, hc::EPI_STORE, nullptr, 0));
+    HC_TRY(hc::comm_allgather(m->comm, mine, m->sc.tp_gather, rows * vs, m->stream));
+    size_t n = rows * c.vocab_size;
+    unsigned grid = (unsigned)std::min<size_t>((n + 255) / 256, 4096);
+    k_unshard_logits<<<grid, 256, 0, m->stream>>>(m->sc.tp_gather, logits, (int)rows, (int)vs, c.tp_size);
+    HC_LAUNCH_CHECK();
+    return HC_OK;
+}
+
+// Waits for the model's stream; with a communicator the wait is watched
+// (a peer that stopped participating aborts the communicator).
+int model_wait(hc_model* m) {
+    if (m->comm) return hc::comm_wait(m->comm, m->stream, m->comm_timeout_s);
+    HC_CUDA(cudaStreamSynchronize(m->stream));
+    return HC_OK;
 }
 
 // The per-layer body shared by prefill (prefill = true, rows = prompt
@@ -528,12 +607,12 @@ int run_layers(hc_model* m, hc_kv* kv, size_t rows, bool prefill, int seq, int p
             P.pos = kv->pos_dev;
             HC_TRY(hc::launch_attention(P, (int)rows, kv->kv_fp16, m->stream));
         }
-        HC_TRY(matmul(m, L.o, s.attn, nq, rows, s.hidden, H, hc::EPI_ADD, s.hidden, H));
+        HC_TRY(row_parallel(m, L.o, s.attn, nq, rows));
         HC_TRY(hc::launch_rmsnorm(s.hidden, H, L.post_norm, s.xn, H, rows, H, c.rms_norm_eps, m->stream));
         size_t im = L.gu.n / 2;
         HC_TRY(matmul(m, L.gu, s.xn, H, rows, s.gu, 2 * im, hc::EPI_STORE, nullptr, 0));
         HC_TRY(hc::launch_silu_mul(s.gu, 2 * im, s.act, im, rows, im, m->stream));
-        HC_TRY(matmul(m, L.down, s.act, im, rows, s.hidden, H, hc::EPI_ADD, s.hidden, H));
+        HC_TRY(row_parallel(m, L.down, s.act, im, rows));
     }
     return HC_OK;
 }
@@ -559,11 +638,7 @@ int decode_dev_impl(hc_model* m, hc_kv* kv, const int* seqs_dev, const uint32_t*
     HC_TRY(hc::launch_rmsnorm(s.hidden, c.hidden_size, m->final_norm, s.xn, c.hidden_size, (size_t)B, c.hidden_size,
                               c.rms_norm_eps, m->stream));
     float* logits = logits_dev ? logits_dev : s.logits;
-    if (m->lm_head.present) {
-        HC_TRY(matmul(m, m->lm_head, s.xn, c.hidden_size, (size_t)B, logits, c.vocab_size, hc::EPI_STORE, nullptr, 0));
-    } else {
-        HC_CUDA(cudaMemsetAsync(logits, 0, (size_t)B * c.vocab_size * sizeof(float), m->stream));
-    }
+    HC_TRY(lm_head_logits(m, s.xn, (size_t)B, logits));
     if (argmax_dev) HC_TRY(hc::launch_argmax(logits, (size_t)B, c.vocab_size, argmax_dev, m->stream));
     return HC_OK;
 }
@@ -672,13 +747,35 @@ HC_EXPORT int hc_model_load(const uint8_t* image, size_t len, int tp_rank, int t
             return fail(r);
         m->cfg.embed_dtype = te->dtype;
     }
+    // LM head: with tensor parallelism each rank keeps a vocabulary slice.
+    const size_t V = c.vocab_size;
+    const bool shard_vocab = tp_size > 1 && V % (size_t)tp_size == 0;
+    m->vocab_shard = shard_vocab ? V / tp_size : V;
+    m->vocab0 = shard_vocab ? (size_t)tp_rank * m->vocab_shard : 0;
+    if (tp_size > 1 && !shard_vocab) {
+        hc_set_error("tensor parallel size %d must divide the vocabulary (%zu)", tp_size, V);
+        return fail(HC_ERR_UNSUPPORTED);
+    }
     if (tl) {
-        if ((r = upload_weight(m, img, {{tl, 0, c.vocab_size, 0, H}}, H, m->lm_head, &staging, &staging_cap)))
+        if ((r = upload_weight(m, img, {{tl, m->vocab0, m->vocab_shard, 0, H}}, H, m->lm_head, &staging,
+                               &staging_cap)))
             return fail(r);
         m->cfg.lm_head_dtype = tl->dtype;
         m->cfg.lm_head_tied = 0;
     } else if (te) {
-        m->lm_head = m->embed;  // tied: same device buffers (transformer.rs:521-524)
+        // tied: a view of the embedding rows of this rank (transformer.rs:521-524)
+        m->lm_head = m->embed;
+        m->lm_head.n = m->vocab_shard;
+        if (m->embed.dtype == HC_DTYPE_Q4_0) {
+            size_t kb = H / 32;
+            m->lm_head.q4.n = m->vocab_shard;
+            m->lm_head.q4.qs = m->embed.q4.qs + m->vocab0 * kb;
+            m->lm_head.q4.sc = m->embed.q4.sc + m->vocab0 * kb;
+            m->lm_head.q4.nblocks = m->vocab_shard * kb;
+        } else if (m->embed.dense) {
+            size_t es = m->embed.dtype == HC_DTYPE_FP32 ? 4 : 2;
+            m->lm_head.dense = (uint8_t*)m->embed.dense + m->vocab0 * H * es;
+        }
         m->cfg.lm_head_dtype = te->dtype;
         m->cfg.lm_head_tied = 1;
     }
@@ -712,7 +809,7 @@ HC_EXPORT int hc_model_free(hc_model* model) {
 HC_EXPORT int hc_sync(hc_model* model) {
     HC_CHECK(model, HC_ERR_INVALID, "hc_sync: NULL model");
     HC_CUDA(cudaSetDevice(model->device));
-    HC_CUDA(cudaStreamSynchronize(model->stream));
+    HC_TRY(model_wait(model));
     return hc::gemm_check(model->gemm_ws);
 }
 
@@ -827,13 +924,10 @@ HC_EXPORT int hc_prefill(hc_model* m, hc_kv* kv, int seq, const uint32_t* ids, i
     const float* last = s.hidden + (size_t)(T - 1) * c.hidden_size;
     HC_TRY(hc::launch_rmsnorm(last, c.hidden_size, m->final_norm, s.xn, c.hidden_size, 1, c.hidden_size,
                               c.rms_norm_eps, m->stream));
-    if (m->lm_head.present)
-        HC_TRY(matmul(m, m->lm_head, s.xn, c.hidden_size, 1, s.logits, c.vocab_size, hc::EPI_STORE, nullptr, 0));
-    else
-        HC_CUDA(cudaMemsetAsync(s.logits, 0, c.vocab_size * sizeof(float), m->stream));
+    HC_TRY(lm_head_logits(m, s.xn, 1, s.logits));
     if (logits_out)
         HC_CUDA(cudaMemcpyAsync(logits_out, s.logits, c.vocab_size * sizeof(float), cudaMemcpyDeviceToHost, m->stream));
-    HC_CUDA(cudaStreamSynchronize(m->stream));
+    HC_TRY(model_wait(m));
     return hc::gemm_check(m->gemm_ws);
 }
 
@@ -881,7 +975,7 @@ HC_EXPORT int hc_decode_step(hc_model* m, hc_kv* kv, const int* seqs, const uint
         HC_CUDA(cudaMemcpyAsync(logits_out, s.logits, (size_t)B * V * sizeof(float), cudaMemcpyDeviceToHost, m->stream));
     if (argmax_out)
         HC_CUDA(cudaMemcpyAsync(argmax_out, s.argmax, B * sizeof(uint32_t), cudaMemcpyDeviceToHost, m->stream));
-    HC_CUDA(cudaStreamSynchronize(m->stream));
+    HC_TRY(model_wait(m));
     return hc::gemm_check(m->gemm_ws);
 }
 
@@ -964,4 +1058,25 @@ HC_EXPORT int hc_decode_step_dev(hc_model* m, hc_kv* kv, const int* seqs_dev, co
     HC_TRY(decode_graphed(m, kv, seqs_dev, ids_dev, B, logits_dev, argmax_dev));
     kv->host_stale = true;
     return HC_OK;
+}
+
+// ============================================================ C ABI: tensor parallel
+
+HC_EXPORT int hc_comm_unique_id(uint8_t* out128) {
+    HC_CHECK(out128, HC_ERR_INVALID, "hc_comm_unique_id: NULL out");
+    return hc::comm_unique_id(out128);
+}
+
+HC_EXPORT int hc_comm_init(hc_model* m, const uint8_t* id128, int rank, int size, double timeout_s) {
+    HC_CHECK(m && id128, HC_ERR_INVALID, "hc_comm_init: NULL argument");
+    HC_CHECK(size == m->cfg.tp_size && rank == m->cfg.tp_rank, HC_ERR_INVALID,
+             "hc_comm_init: rank/size %d/%d differ from the model's shard %d/%d", rank, size, m->cfg.tp_rank,
+             m->cfg.tp_size);
+    HC_CUDA(cudaSetDevice(m->device));
+    if (m->comm) {
+        hc::comm_free(m->comm);
+        m->comm = nullptr;
+    }
+    if (timeout_s > 0) m->comm_timeout_s = timeout_s;
+    return hc::comm_init(&m->comm, id128, rank, size, m->comm_timeout_s);
 }

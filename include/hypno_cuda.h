@@ -175,6 +175,20 @@ int hc_decode_step(hc_model* model, hc_kv* kv, const int* seqs, const uint32_t* 
 int hc_decode_step_dev(hc_model* model, hc_kv* kv, const int* seqs_dev, const uint32_t* ids_dev,
                        int B, float* logits_dev, uint32_t* argmax_dev);
 
+/* ---- tensor parallelism (new in this backend; the reference is single-CPU) */
+
+/* Writes a fresh 128-byte NCCL unique id (rank 0 creates it and shares it
+ * with the other ranks by any host channel). */
+int hc_comm_unique_id(uint8_t* out128);
+/* Joins the tensor-parallel group of a model loaded with
+ * hc_model_load(..., rank, size, ...).  The all-reduce after o_proj and
+ * down_proj and the all-gather of the vocabulary-sharded logits then run on
+ * the model's stream.  Host waits of the model (hc_sync, hc_prefill,
+ * hc_decode_step) are watched: a collective that does not finish within
+ * timeout_s seconds (<= 0: 60) aborts the communicator and returns
+ * HC_ERR_TIMEOUT. */
+int hc_comm_init(hc_model* model, const uint8_t* id128, int rank, int size, double timeout_s);
+
 /* ---- synthetic inputs (seeded; identical bytes on host and device) ----- */
 
 /* Fills out[i] (i < n) with element offset+i of the seeded stream

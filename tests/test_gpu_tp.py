@@ -1,0 +1,86 @@
+"""Tensor parallelism on 2 GPUs: the c4-geometry model sharded over two ranks
+(NCCL all-reduce after o_proj / down_proj, vocabulary-sharded LM head) must
+match the single-device oracle.  Skipped on a 1-GPU machine."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+GEOM = dict(hidden=1024, layers=2, heads=8, kv_heads=2, inter=2816, vocab=8192, theta=500000.0,
+            max_pos=1024, embed="q4", lm_head="tied")
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank(rank, size, port, q):
+    try:
+        import datetime
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(rank)
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+        dist.init_process_group("gloo", rank=rank, world_size=size, timeout=datetime.timedelta(seconds=120))
+        from hypno_b200 import engine, synth, tp
+        from hypno_b200._lib import call
+        from oracle import oracle as orc
+        call("hc_set_device", rank)
+        img = synth.build_image(GEOM, seed=3, quantize=orc.quantize_f32_to_q4_0)
+        m = engine.HypnoModel(img, rank, size)
+        tp.join(m, rank, size, timeout_s=60)
+        kv = engine.KVCache(m, n_seqs=2, max_pos=1024, kv_dtype=engine.KV_FP16)
+        prompts = [synth.prompt_ids(GEOM["vocab"], T, seed=20 + s) for s, T in enumerate((300, 9))]
+        first = [engine.batch_forward(m, p, kv, seq=s) for s, p in enumerate(prompts)]
+        toks = [int(np.nonzero(f == f.max())[0][-1]) for f in first]
+        steps = []
+        for _ in range(4):
+            lg, am = engine.decode_step(m, kv, [0, 1], toks)
+            steps.append(lg)
+            toks = [int(a) for a in am]
+        ok, msg = True, ""
+        if rank == 0:
+            om = orc.OracleModel(img)
+            for s, p in enumerate(prompts):
+                okv = om.new_kv(1024)
+                r = orc.batch_forward(om, p, okv)
+                err = np.max(np.abs(first[s] - r)) / max(1.0, np.max(np.abs(r)))
+                tok = orc.greedy(r)
+                for st in range(4):
+                    rl = orc.model_forward(om, tok, okv)
+                    e = np.max(np.abs(steps[st][s] - rl)) / max(1.0, np.max(np.abs(rl)))
+                    err = max(err, e)
+                    tok = orc.greedy(rl)
+                    if tok != orc.greedy(steps[st][s]):
+                        ok, msg = False, f"greedy mismatch seq {s} step {st}"
+                if err > 1e-3:
+                    ok, msg = False, f"seq {s} rel err {err:.3e}"
+        kv.close()
+        m.close()
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, ok, msg))
+    except Exception as e:
+        q.put((rank, False, repr(e)))
+
+
+def test_tp2_matches_oracle():
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=600) for _ in procs]
+    for p in procs:
+        p.join(timeout=120)
+    assert all(ok for _, ok, _ in res), res
