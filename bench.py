@@ -271,7 +271,9 @@ def run_ours(args):
         dist.barrier()
     lib = load()
     call("hc_set_device", local)
-    cfg = synth.CONFIGS["c4"]
+    cfg = dict(synth.CONFIGS["c4"])
+    if args.layers:
+        cfg["layers"] = args.layers  # smaller model with the same per-layer kernels (profiling captures)
     S, P = cfg["seqs"], cfg["prompt"]
     tp = world > 1 and args.parallel == "tp"
     img = synth.build_image(cfg, seed=0, device=dev)
@@ -372,7 +374,7 @@ def run_ours(args):
         line = {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
                 "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": "q4_0 weights, f32 compute", "data": "synthetic",
-                "config": workload_config(world, "tp" if tp else "dp"), "e2e": e2e, "gpu_launches": int(launches),
+                "config": dict(workload_config(world, "tp" if tp else "dp"), layers=cfg["layers"]), "e2e": e2e, "gpu_launches": int(launches),
                 "prefill_tok_s": round(prefill_tok_s, 1), "clocks": clk.summary(), "roofline": roof,
                 "cpu_baseline": cpu, "q4_sweep": sweep}
         print(json.dumps(line), flush=True)
@@ -420,6 +422,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-sweep", action="store_true", help="skip the configs[1] operator sweep report")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="override the layer count (a small case for ncu captures; reported in config)")
     ap.add_argument("--parallel", default="tp", choices=["tp", "dp"],
                     help="N > 1: tensor parallel over the ranks (default) or independent replicas")
     args = ap.parse_args()
