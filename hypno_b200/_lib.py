@@ -84,6 +84,7 @@ SIGNATURES = {
     "hc_q4_matrix_from_dev": (_I, [_P, _SZ, _SZ, _SZ, _P, ctypes.POINTER(_P)]),
     "hc_q4_matrix_free": (_I, [_P]),
     "hc_q4_matmul_dev": (_I, [_P, _P, _SZ, _P, _P]),
+    "hc_q4_matmul_noalloc": (_I, [_P, _P, _SZ, _P, _P]),
     "hc_model_load": (_I, [_P, _SZ, _I, _I, ctypes.POINTER(_P)]),
     "hc_model_config": (_I, [_P, ctypes.POINTER(HcConfig)]),
     "hc_model_free": (_I, [_P]),

@@ -192,25 +192,6 @@ int launch_advance(const int* seqs, int* pos, int B, cudaStream_t s) {
 // with several splits) adds the partials and normalises.
 namespace {
 
-template <typename KT>
-__device__ __forceinline__ void load_row8(const KT* p, float* f);
-template <>
-__device__ __forceinline__ void load_row8<__half>(const __half* p, float* f) {
-    uint4 u = *reinterpret_cast<const uint4*>(p);
-    const __half2* h = reinterpret_cast<const __half2*>(&u);
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        float2 v = __half22float2(h[i]);
-        f[2 * i] = v.x;
-        f[2 * i + 1] = v.y;
-    }
-}
-template <>
-__device__ __forceinline__ void load_row8<float>(const float* p, float* f) {
-    float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
-    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
-}
-
 constexpr int DA_THREADS = 256;
 constexpr int DA_MAXG = 16;
 

@@ -99,17 +99,6 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
 __device__ __forceinline__ void tmem_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tmem_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-__device__ __forceinline__ void tmem_st_x32(uint32_t taddr, const uint32_t* v) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
-        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
-        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
-        "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
-        "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
-        : "memory");
-}
-
 __device__ __forceinline__ void tmem_ld_x32(uint32_t taddr, uint32_t* v) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
@@ -568,3 +557,92 @@ int gemm_check(GemmWorkspace* ws) {
 }
 
 }  // namespace hc
+
+// ============================================================ allocation-free entry point
+//
+// Some callers cannot allocate device memory once they are running: a serving
+// process that hands all device memory to its own pool at start-up and must
+// not grow it, or a caller that may not call cudaMalloc (which can
+// synchronize the device) while other work is in flight.  For them the
+// tensor-core matmul below keeps its scratch (the fp16 copy of the
+// activations and the pipeline abort flag) in a fixed array that lives in the
+// library's device image, so a call allocates nothing.
+namespace {
+
+// Stated maximum: 8 MiB per device, held by every GPU that loads the library
+// until the process exits.  tokens * k * 2 bytes must fit after the flag.
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;
+constexpr size_t kNoAllocFlagBytes = 256;
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+uint8_t* g_noalloc_ptr[kMaxDevices] = {nullptr};
+std::mutex g_noalloc_mu;
+
+// Device address of the array for the current device.  In host code the
+// symbol is only a host-side stand-in, never a device address, so the address
+// is looked up with cudaGetSymbolAddress once per device (with that device
+// current) and cached.
+int noalloc_scratch(uint8_t** out) {
+    int dev = 0;
+    HC_CUDA(cudaGetDevice(&dev));
+    HC_CHECK(dev >= 0 && dev < kMaxDevices, HC_ERR_UNSUPPORTED, "device index %d out of range", dev);
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        void* p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return hc_cuda_fail(e, "cudaGetSymbolAddress(g_noalloc_scratch)", __FILE__, __LINE__);
+        g_noalloc_ptr[dev] = static_cast<uint8_t*>(p);
+    }
+    *out = g_noalloc_ptr[dev];
+    return HC_OK;
+}
+
+}  // namespace
+
+// Y[mtok x n] = X[mtok x k] . W^T like hc_q4_matmul_dev, without allocating
+// device or host memory: shapes the tensor cores take (mtok >= 2, k % 128 ==
+// 0, n >= 128) run the tcgen05 kernel with its scratch in the fixed array and
+// no split-K; other shapes run the CUDA-core matvec, which needs no scratch.
+HC_EXPORT int hc_q4_matmul_noalloc(const hc_q4_matrix* w, const float* x, size_t mtok, float* y, void* stream) {
+    HC_CHECK(w && x && y, HC_ERR_INVALID, "hc_q4_matmul_noalloc: NULL argument");
+    cudaStream_t s = (cudaStream_t)stream;
+    if (!hc::gemm_tc_eligible(*w, mtok)) {
+        DevWeight dw;
+        dw.dtype = HC_DTYPE_Q4_0;
+        dw.n = w->n;
+        dw.k = w->k;
+        dw.q4 = *w;
+        dw.present = true;
+        return hc::launch_matmul(dw, x, w->k, mtok, y, w->n, hc::EPI_STORE, nullptr, 0, s);
+    }
+    const size_t K = w->k, T = mtok;
+    HC_CHECK(T <= (kNoAllocScratchBytes - kNoAllocFlagBytes) / (K * sizeof(__half)), HC_ERR_INVALID,
+             "hc_q4_matmul_noalloc: %zu tokens x %zu columns exceed the fixed %zu-byte scratch (at most %zu tokens "
+             "at this width)",
+             T, K, kNoAllocScratchBytes, (kNoAllocScratchBytes - kNoAllocFlagBytes) / (K * sizeof(__half)));
+    uint8_t* base = nullptr;
+    HC_TRY(noalloc_scratch(&base));
+    int* err = reinterpret_cast<int*>(base);
+    __half* xh = reinterpret_cast<__half*>(base + kNoAllocFlagBytes);
+    // The array keeps the previous call's contents: the abort flag must start at zero.
+    HC_CUDA(cudaMemsetAsync(err, 0, sizeof(int), s));
+    {
+        unsigned gx = (unsigned)std::min<size_t>((K / 8 + 255) / 256, 16);
+        hc::k_rows_to_f16_perm<<<dim3(gx, (unsigned)T), 256, 0, s>>>(x, K, xh, (int)K, (int)T);
+        HC_LAUNCH_CHECK();
+    }
+    int tn = T <= 32 ? 32 : T <= 64 ? 64 : T <= 128 ? 128 : 256;
+    CUtensorMap xmap, wmap;
+    HC_TRY(hc::encode_2d(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xh, K, T, K * 2, 64, (uint32_t)tn,
+                         CU_TENSOR_MAP_SWIZZLE_128B));
+    HC_TRY(hc::encode_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->qs, K / 2, w->n, K / 2, hc::BK / 2, hc::BM,
+                         CU_TENSOR_MAP_SWIZZLE_NONE));
+    switch (tn) {
+        case 32: return hc::launch_tc<32>(*w, xmap, wmap, T, y, w->n, hc::EPI_STORE, nullptr, 0, 1, nullptr, err, s);
+        case 64: return hc::launch_tc<64>(*w, xmap, wmap, T, y, w->n, hc::EPI_STORE, nullptr, 0, 1, nullptr, err, s);
+        case 128: return hc::launch_tc<128>(*w, xmap, wmap, T, y, w->n, hc::EPI_STORE, nullptr, 0, 1, nullptr, err, s);
+        default: return hc::launch_tc<256>(*w, xmap, wmap, T, y, w->n, hc::EPI_STORE, nullptr, 0, 1, nullptr, err, s);
+    }
+}
+

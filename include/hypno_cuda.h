@@ -108,6 +108,22 @@ int hc_q4_matrix_free(hc_q4_matrix* mat);
  * kernels::matmul_q4_0 (turbo::batch_matmul for mtok > 1). */
 int hc_q4_matmul_dev(const hc_q4_matrix* w, const float* x, size_t mtok, float* y, void* stream);
 
+/* The same product as hc_q4_matmul_dev for callers that cannot allocate
+ * device memory while running (a serving process whose device memory is all
+ * handed to its own pool at start-up, or code that may not call cudaMalloc,
+ * which can synchronize the device, while other work is in flight).  This
+ * entry point has no counterpart in the reference engine.  It allocates
+ * nothing: tensor-core shapes (mtok >= 2, k % 128 == 0, n >= 128) keep their
+ * scratch in a fixed 8 MiB array inside the library's device image (held by
+ * every GPU that loads the library until the process exits) and require
+ * mtok * k * 2 <= 8 MiB - 256 bytes, else HC_ERR_INVALID; other shapes use the
+ * CUDA-core matvec, which needs no scratch.  The first call on a device looks
+ * up the array's device address (cudaGetSymbolAddress) and should come before
+ * any stream capture.  Every call shares the array: calls that overlap on the
+ * GPU (different streams, or different host threads on one device) race, so
+ * order them on one stream.  Stream-ordered, no synchronization. */
+int hc_q4_matmul_noalloc(const hc_q4_matrix* w, const float* x, size_t mtok, float* y, void* stream);
+
 /* ---- model level: the forward passes ---------------------------------- */
 
 typedef struct hc_model hc_model;
