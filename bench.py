@@ -125,6 +125,31 @@ def cuda_time_ms(stream_ptr, fn, reps):
     return e0.elapsed_time(e1) / reps
 
 
+def graph_time_ms(fn, n, replays=3):
+    """Average milliseconds per call of fn(i, stream) for i in range(n), the n
+    calls captured once in a CUDA graph and replayed, CUDA events recorded on
+    the replay stream; host launch overhead is not part of the number."""
+    import torch
+    s = torch.cuda.Stream()
+    g = torch.cuda.CUDAGraph()
+    torch.cuda.synchronize()
+    with torch.cuda.graph(g, stream=s, capture_error_mode="relaxed"):
+        for i in range(n):
+            fn(i, s.cuda_stream)
+    cur = torch.cuda.current_stream()
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(cur)
+    for _ in range(replays):
+        g.replay()
+    e1.record(cur)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / (replays * n)
+    del g
+    return ms
+
+
 def roofline_gemv(dev, M=32, N=28672, K=4096, copies=4, reps=20):
     """Times the Q4_0 matmul of the fused gate/up shape over `copies` rotating
     weight matrices (together larger than L2) and returns the roofline dict."""
@@ -147,12 +172,12 @@ def roofline_gemv(dev, M=32, N=28672, K=4096, copies=4, reps=20):
     Y = torch.empty(M * N, dtype=torch.float32, device=dev)
     stream = torch.cuda.current_stream().cuda_stream
 
-    def run(i):
-        call("hc_q4_matmul_dev", mats[i % copies], X.data_ptr(), M, Y.data_ptr(), stream)
+    def run(i, st=stream):
+        call("hc_q4_matmul_dev", mats[i % copies], X.data_ptr(), M, Y.data_ptr(), st)
 
     for i in range(6):
         run(i)
-    ms = cuda_time_ms(stream, run, reps)
+    ms = graph_time_ms(run, reps)
     for h in mats:
         call("hc_q4_matrix_free", h)
     algo = 0.5625 * N * K + 4.0 * M * K + 4.0 * M * N
@@ -171,7 +196,8 @@ def roofline_gemv(dev, M=32, N=28672, K=4096, copies=4, reps=20):
 
 def q4_sweep(dev, reps=10):
     """Y = X W^T for (N, K) in the sweep and M in {1, 8, 64, 512},
-    each timed with CUDA events over rotating weight copies (> L2 in total).
+    each timed as a CUDA graph of launches over rotating weight copies (> L2
+    in total).
     M <= 64 is graded against HBM bandwidth, M = 512 against dense tensor peak."""
     import torch
     from hypno_b200 import synth
@@ -204,12 +230,12 @@ def q4_sweep(dev, reps=10):
             call("hc_synth_normal_dev", 1, synth.fnv1a64(f"sweep.X.{M}x{K}"), 0, M * K, 1.0, X.data_ptr(), None)
             Y = torch.empty(M * N, dtype=torch.float32, device=dev)
 
-            def run(i):
-                call("hc_q4_matmul_dev", mats[i % copies], X.data_ptr(), M, Y.data_ptr(), stream)
+            def run(i, st=stream):
+                call("hc_q4_matmul_dev", mats[i % copies], X.data_ptr(), M, Y.data_ptr(), st)
 
             for i in range(3):
                 run(i)
-            ms = cuda_time_ms(stream, run, reps)
+            ms = graph_time_ms(run, reps * copies)
             algo = 0.5625 * N * K + 4.0 * M * K + 4.0 * M * N
             flops = 2.0 * M * N * K
             row = {"N": N, "K": K, "M": M, "us": round(ms * 1e3, 2), "gbs": round(algo / (ms * 1e-3) / 1e9, 1),

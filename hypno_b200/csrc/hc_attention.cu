@@ -14,6 +14,7 @@
 #include "hc_internal.h"
 #include "hc_common.cuh"
 #include "hc_attention.h"
+#include "hc_gemm.h"
 
 namespace hc {
 
@@ -57,7 +58,10 @@ __global__ void __launch_bounds__(128) k_attention(AttnParams P) {
     }
 
     if (n <= 1) {
-        for (int d = threadIdx.x; d < hd; d += blockDim.x) out[d] = vself[d];
+        for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+            out[d] = vself[d];
+            if (P.out16) P.out16[(size_t)row * P.nh * hd + perm_k(h * hd + d)] = __float2half_rn(vself[d]);
+        }
         return;
     }
 
@@ -96,8 +100,11 @@ __global__ void __launch_bounds__(128) k_attention(AttnParams P) {
         part[warp * hd + d] = acc;
     }
     __syncthreads();
-    for (int d = threadIdx.x; d < hd; d += blockDim.x)
-        out[d] = (part[d] + part[hd + d]) + (part[2 * hd + d] + part[3 * hd + d]);
+    for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+        float o = (part[d] + part[hd + d]) + (part[2 * hd + d] + part[3 * hd + d]);
+        out[d] = o;
+        if (P.out16) P.out16[(size_t)row * P.nh * hd + perm_k(h * hd + d)] = __float2half_rn(o);
+    }
 }
 
 int launch_attention(const AttnParams& P, int rows, int kv_fp16, cudaStream_t s) {
@@ -192,99 +199,273 @@ int launch_advance(const int* seqs, int* pos, int B, cudaStream_t s) {
 // with several splits) adds the partials and normalises.
 namespace {
 
-constexpr int DA_THREADS = 256;
-constexpr int DA_MAXG = 16;
+constexpr int DA_WARPS = DA_REDUCE_WARPS;
+constexpr int DA_THREADS = DA_WARPS * 32;
+constexpr int DA_MAXG = 8;
 
-// Pass 1: S[row][h][p] = (q_h . k_p) * scale for p in this split, plus the
-// split's maximum per head.  One thread per position: the whole K row is
-// requested before any arithmetic (HD/8 16-byte loads in flight per thread),
-// q sits transposed in shared memory so one broadcast read serves all G heads.
+// Lane-group mapping for one (sequence, KV head): LPP lanes share a K or V
+// row, each lane owning EPL consecutive elements of it (32 bytes, 16 bytes for
+// groups of 4 or more heads), so a warp reads whole rows with coalesced 16-byte loads
+// and keeps its slice of the G query vectors in registers.  U row groups are
+// loaded before any arithmetic to keep enough bytes in flight.
 template <typename KT, int G, int HD>
-__global__ void __launch_bounds__(DA_THREADS) k_dattn_scores(DecAttnParams P) {
-    __shared__ float sq[HD * G];  // [d][g]
-    __shared__ float red[32];
+struct DA {
+    static constexpr int BPL = (G <= 2) ? 32 : 16;                  // bytes per lane per row
+    static constexpr int EPL = BPL / (int)sizeof(KT);               // elements per lane
+    static constexpr int LPP = HD * (int)sizeof(KT) / BPL;          // lanes per row
+    static constexpr int PPW = 32 / LPP;                            // rows per warp per step
+    static constexpr int NV = BPL / 16;                             // 16-byte loads per lane per row
+    static constexpr int U = (BPL == 16 && G < 8) ? 8 : 4;          // row groups in flight
+    static_assert(LPP >= 1 && LPP <= 32 && (LPP & (LPP - 1)) == 0, "head_dim / lane mapping");
+};
+
+template <typename KT, int EPL>
+__device__ __forceinline__ void cvt_elems(const uint4* raw, float* out) {
+    if constexpr (sizeof(KT) == 2) {
+#pragma unroll
+        for (int v = 0; v < EPL / 8; v++) {
+            const __half2* h2 = reinterpret_cast<const __half2*>(&raw[v]);
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                float2 f = __half22float2(h2[i]);
+                out[v * 8 + 2 * i] = f.x;
+                out[v * 8 + 2 * i + 1] = f.y;
+            }
+        }
+    } else {
+#pragma unroll
+        for (int v = 0; v < EPL / 4; v++) {
+            const float* f = reinterpret_cast<const float*>(&raw[v]);
+#pragma unroll
+            for (int i = 0; i < 4; i++) out[v * 4 + i] = f[i];
+        }
+    }
+}
+
+// Scores of positions [p0, p1) written to S[g * ldS + (p - sbase)]; mx gets
+// each head's maximum over the positions this lane wrote.
+template <typename KT, int G, int HD>
+__device__ __forceinline__ void da_scores(const KT* __restrict__ kbase, const float (&qr)[G][DA<KT, G, HD>::EPL],
+                                          int p0, int p1, float scale, float* S, size_t ldS, int sbase,
+                                          float (&mx)[G]) {
+    using C = DA<KT, G, HD>;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int slot = lane / C::LPP, sub = lane % C::LPP;
+    constexpr int STEP = C::U * C::PPW;
+    for (int c0 = p0 + warp * STEP; c0 < p1; c0 += DA_WARPS * STEP) {
+        uint4 raw[C::U][C::NV];
+#pragma unroll
+        for (int u = 0; u < C::U; u++) {
+            int p = c0 + u * C::PPW + slot;
+            const uint4* src = reinterpret_cast<const uint4*>(kbase + (size_t)p * HD + sub * C::EPL);
+#pragma unroll
+            for (int v = 0; v < C::NV; v++) raw[u][v] = (p < p1) ? __ldg(src + v) : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int u = 0; u < C::U; u++) {
+            float k[C::EPL];
+            cvt_elems<KT, C::EPL>(raw[u], k);
+            float acc[G];
+#pragma unroll
+            for (int g = 0; g < G; g++) {
+                acc[g] = 0.0f;
+#pragma unroll
+                for (int e = 0; e < C::EPL; e++) acc[g] = fmaf(qr[g][e], k[e], acc[g]);
+#pragma unroll
+                for (int off = C::LPP / 2; off > 0; off >>= 1) acc[g] += __shfl_xor_sync(0xffffffffu, acc[g], off);
+            }
+            int p = c0 + u * C::PPW + slot;
+            if (sub == 0 && p < p1) {
+#pragma unroll
+                for (int g = 0; g < G; g++) {
+                    float sc = __fmul_rn(acc[g], scale);
+                    S[(size_t)g * ldS + (p - sbase)] = sc;
+                    mx[g] = fmaxf(mx[g], sc);
+                }
+            }
+        }
+    }
+}
+
+// o[g][e] += sum over positions [p0, p1) of W[g * ldW + (p - wbase)] * V[p][d0 + e]
+// for this lane's slot and slice (not yet reduced across slots or warps).
+template <typename KT, int G, int HD>
+__device__ __forceinline__ void da_pv(const KT* __restrict__ vbase, const float* W, size_t ldW, int wbase, int p0,
+                                      int p1, float (&o)[G][DA<KT, G, HD>::EPL]) {
+    using C = DA<KT, G, HD>;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int slot = lane / C::LPP, sub = lane % C::LPP;
+    constexpr int STEP = C::U * C::PPW;
+    for (int c0 = p0 + warp * STEP; c0 < p1; c0 += DA_WARPS * STEP) {
+        uint4 raw[C::U][C::NV];
+#pragma unroll
+        for (int u = 0; u < C::U; u++) {
+            int p = c0 + u * C::PPW + slot;
+            const uint4* src = reinterpret_cast<const uint4*>(vbase + (size_t)p * HD + sub * C::EPL);
+#pragma unroll
+            for (int v = 0; v < C::NV; v++) raw[u][v] = (p < p1) ? __ldg(src + v) : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int u = 0; u < C::U; u++) {
+            int p = c0 + u * C::PPW + slot;
+            if (p >= p1) continue;
+            float v[C::EPL];
+            cvt_elems<KT, C::EPL>(raw[u], v);
+#pragma unroll
+            for (int g = 0; g < G; g++) {
+                float w = W[(size_t)g * ldW + (p - wbase)];
+#pragma unroll
+                for (int e = 0; e < C::EPL; e++) o[g][e] = fmaf(w, v[e], o[g][e]);
+            }
+        }
+    }
+}
+
+// Sum o over the slots of a warp and over the warps; the result for head g,
+// feature d lands in red[g * HD + d] (red holds DA_WARPS * G * HD floats).
+template <typename KT, int G, int HD>
+__device__ __forceinline__ void da_reduce_o(float (&o)[G][DA<KT, G, HD>::EPL], float* red) {
+    using C = DA<KT, G, HD>;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int sub = lane % C::LPP;
+#pragma unroll
+    for (int g = 0; g < G; g++)
+#pragma unroll
+        for (int e = 0; e < C::EPL; e++)
+#pragma unroll
+            for (int off = C::LPP; off < 32; off <<= 1) o[g][e] += __shfl_xor_sync(0xffffffffu, o[g][e], off);
+    __syncthreads();
+    if (lane < C::LPP) {
+#pragma unroll
+        for (int g = 0; g < G; g++)
+#pragma unroll
+            for (int e = 0; e < C::EPL; e++) red[((size_t)warp * G + g) * HD + sub * C::EPL + e] = o[g][e];
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < G * HD; i += DA_THREADS) {
+        float t = 0.0f;
+#pragma unroll
+        for (int w = 0; w < DA_WARPS; w++) t += red[(size_t)w * G * HD + i];
+        red[(size_t)DA_WARPS * G * HD + i] = t;
+    }
+    __syncthreads();
+}
+
+template <typename KT, int G, int HD>
+__device__ __forceinline__ void da_load_q(const DecAttnParams& P, int row, int kvh,
+                                          float (&qr)[G][DA<KT, G, HD>::EPL]) {
+    using C = DA<KT, G, HD>;
+    const int sub = (threadIdx.x & 31) % C::LPP;
+#pragma unroll
+    for (int g = 0; g < G; g++)
+#pragma unroll
+        for (int e = 0; e < C::EPL; e++)
+            qr[g][e] = P.q[(size_t)row * P.ldq + (size_t)(kvh * G + g) * HD + sub * C::EPL + e];
+}
+
+__device__ __forceinline__ void da_write_out(const DecAttnParams& P, int row, int h, int d, float v) {
+    P.out[(size_t)row * P.ldo + (size_t)h * P.hd + d] = v;
+    if (P.out16) P.out16[(size_t)row * P.nh * P.hd + perm_k(h * P.hd + d)] = __float2half_rn(v);
+}
+
+// Whole context in one CTA per (sequence, KV head): scores kept in shared
+// memory, then weights, then P.V; K and V are each read once.
+template <typename KT, int G, int HD>
+__global__ void __launch_bounds__(DA_THREADS, 2) k_dattn_fused(DecAttnParams P) {
+    using C = DA<KT, G, HD>;
+    extern __shared__ float smem[];
+    __shared__ float redv[32];
+    const int row = blockIdx.x, kvh = blockIdx.y;
+    const int seq = P.seqs[row];
+    const int n = min(P.pos[seq], P.max_pos);
+    if (n <= 1) {
+        for (int i = threadIdx.x; i < G * HD; i += DA_THREADS)
+            da_write_out(P, row, kvh * G + i / HD, i % HD, P.vself[(size_t)row * P.ldself + (size_t)kvh * HD + i % HD]);
+        return;
+    }
+    float* S = smem;                        // [G][max_pos]
+    float* red = smem + (size_t)G * P.max_pos;  // [(DA_WARPS + 1) * G * HD]
+    const size_t off = (size_t)seq * P.seq_stride + (size_t)kvh * P.head_stride;
+    const KT* kbase = reinterpret_cast<const KT*>(P.kc) + off;
+    const KT* vbase = reinterpret_cast<const KT*>(P.vc) + off;
+    float qr[G][C::EPL];
+    da_load_q<KT, G, HD>(P, row, kvh, qr);
+    float mx[G];
+#pragma unroll
+    for (int g = 0; g < G; g++) mx[g] = -INFINITY;
+    da_scores<KT, G, HD>(kbase, qr, 0, n, P.scale, S, (size_t)P.max_pos, 0, mx);
+    float gmax[G];
+#pragma unroll
+    for (int g = 0; g < G; g++) gmax[g] = block_max(mx[g], redv);  // also orders the S writes
+    const int n8 = n - (n % 8);
+    float lsum[G];
+#pragma unroll
+    for (int g = 0; g < G; g++) lsum[g] = 0.0f;
+    for (int p = threadIdx.x; p < n; p += DA_THREADS) {
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+            float e = softmax_weight(S[(size_t)g * P.max_pos + p], gmax[g], p, n8);
+            S[(size_t)g * P.max_pos + p] = e;
+            lsum[g] += e;
+        }
+    }
+    float total[G];
+#pragma unroll
+    for (int g = 0; g < G; g++) total[g] = block_sum(lsum[g], redv);  // also orders the weight writes
+    float o[G][C::EPL];
+#pragma unroll
+    for (int g = 0; g < G; g++)
+#pragma unroll
+        for (int e = 0; e < C::EPL; e++) o[g][e] = 0.0f;
+    da_pv<KT, G, HD>(vbase, S, (size_t)P.max_pos, 0, 0, n, o);
+    da_reduce_o<KT, G, HD>(o, red);
+    const float* fin = red + (size_t)DA_WARPS * G * HD;
+    for (int i = threadIdx.x; i < G * HD; i += DA_THREADS) {
+        int g = i / HD;
+        da_write_out(P, row, kvh * G + g, i % HD, __fdiv_rn(fin[i], total[g]));
+    }
+}
+
+// Split path, pass 1: scores of one split to global S, split maximum.
+template <typename KT, int G, int HD>
+__global__ void __launch_bounds__(DA_THREADS, 2) k_dattn_scores(DecAttnParams P) {
+    using C = DA<KT, G, HD>;
+    __shared__ float redv[32];
     const int row = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
     const int seq = P.seqs[row];
     const int n = min(P.pos[seq], P.max_pos);
     const int p0 = split * P.chunk, p1 = min(n, p0 + P.chunk);
     if (n <= 1) return;
-    for (int i = threadIdx.x; i < G * HD; i += DA_THREADS) {
-        int g = i / HD, d = i % HD;
-        sq[d * G + g] = P.q[(size_t)row * P.ldq + (size_t)(kvh * G) * HD + i];
-    }
-    __syncthreads();
     const KT* kbase = reinterpret_cast<const KT*>(P.kc) + (size_t)seq * P.seq_stride + (size_t)kvh * P.head_stride;
+    float qr[G][C::EPL];
+    da_load_q<KT, G, HD>(P, row, kvh, qr);
     float mx[G];
 #pragma unroll
     for (int g = 0; g < G; g++) mx[g] = -INFINITY;
-    for (int p = p0 + threadIdx.x; p < p1; p += DA_THREADS) {
-        const KT* kp = kbase + (size_t)p * HD;
-        constexpr int NV = HD * (int)sizeof(KT) / 16;  // 16-byte vectors per row
-        uint4 raw[NV];
-#pragma unroll
-        for (int v = 0; v < NV; v++) raw[v] = __ldg(reinterpret_cast<const uint4*>(kp) + v);
-        float acc[G];
-#pragma unroll
-        for (int g = 0; g < G; g++) acc[g] = 0.0f;
-#pragma unroll
-        for (int v = 0; v < NV; v++) {
-            constexpr int EPV = 16 / (int)sizeof(KT);
-            float k8[EPV];
-            if constexpr (sizeof(KT) == 2) {
-                const __half2* h2 = reinterpret_cast<const __half2*>(&raw[v]);
-#pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    float2 f = __half22float2(h2[i]);
-                    k8[2 * i] = f.x;
-                    k8[2 * i + 1] = f.y;
-                }
-            } else {
-                const float* f = reinterpret_cast<const float*>(&raw[v]);
-#pragma unroll
-                for (int i = 0; i < 4; i++) k8[i] = f[i];
-            }
-#pragma unroll
-            for (int e = 0; e < EPV; e++) {
-                const float* qd = sq + (v * EPV + e) * G;
-#pragma unroll
-                for (int g = 0; g < G; g++) acc[g] = fmaf(qd[g], k8[e], acc[g]);
-            }
-        }
-        float* srow = P.S + ((size_t)row * P.nh + kvh * G) * P.max_pos + p;
-#pragma unroll
-        for (int g = 0; g < G; g++) {
-            float sc = __fmul_rn(acc[g], P.scale);
-            srow[(size_t)g * P.max_pos] = sc;
-            mx[g] = fmaxf(mx[g], sc);
-        }
-    }
+    float* S = P.S + ((size_t)row * P.nh + kvh * G) * P.max_pos;
+    da_scores<KT, G, HD>(kbase, qr, p0, p1, P.scale, S, (size_t)P.max_pos, 0, mx);
 #pragma unroll
     for (int g = 0; g < G; g++) {
-        float m = block_max(mx[g], red);
+        float m = block_max(mx[g], redv);
         if (threadIdx.x == 0) P.smax[((size_t)row * P.nh + kvh * G + g) * P.nsplit + split] = m;
     }
 }
 
-// Pass 2: weights with the global maximum and the split's partial P.V.
-// Warp w takes positions w, w+8, ...; lane l takes features [4l, 4l+4).
-template <typename KT, int G>
-__global__ void __launch_bounds__(DA_THREADS) k_dattn_pv(DecAttnParams P) {
-    extern __shared__ float sw[];  // G * chunk weights, then 8 * G * hd partials
-    __shared__ float red[32];
+// Split path, pass 2: weights with the global maximum, partial P.V of the split.
+template <typename KT, int G, int HD>
+__global__ void __launch_bounds__(DA_THREADS, 2) k_dattn_pv(DecAttnParams P) {
+    using C = DA<KT, G, HD>;
+    extern __shared__ float smem[];  // [G][chunk] weights, then the reduction buffer
+    __shared__ float redv[32];
     __shared__ float gmax[DA_MAXG];
     const int row = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
-    const int hd = P.hd;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int seq = P.seqs[row];
     const int n = min(P.pos[seq], P.max_pos);
     if (n <= 1) {
-        // p <= 1: the output is the token's own V (weight 1.0), transformer.rs:514-548
         if (split == 0)
-            for (int i = threadIdx.x; i < G * hd; i += DA_THREADS) {
-                int g = i / hd, d = i % hd;
-                P.out[(size_t)row * P.ldo + (size_t)(kvh * G + g) * hd + d] =
-                    P.vself[(size_t)row * P.ldself + (size_t)kvh * hd + d];
-            }
+            for (int i = threadIdx.x; i < G * HD; i += DA_THREADS)
+                da_write_out(P, row, kvh * G + i / HD, i % HD,
+                             P.vself[(size_t)row * P.ldself + (size_t)kvh * HD + i % HD]);
         return;
     }
     const int nsplit_eff = (n + P.chunk - 1) / P.chunk;
@@ -292,92 +473,51 @@ __global__ void __launch_bounds__(DA_THREADS) k_dattn_pv(DecAttnParams P) {
     const int p0 = split * P.chunk, p1 = min(n, p0 + P.chunk), len = p1 - p0;
     if (threadIdx.x < G) {
         float m = -INFINITY;
-        for (int s = 0; s < nsplit_eff; s++)
-            m = fmaxf(m, P.smax[((size_t)row * P.nh + kvh * G + threadIdx.x) * P.nsplit + s]);
+        for (int s2 = 0; s2 < nsplit_eff; s2++)
+            m = fmaxf(m, P.smax[((size_t)row * P.nh + kvh * G + threadIdx.x) * P.nsplit + s2]);
         gmax[threadIdx.x] = m;
     }
     __syncthreads();
+    float* W = smem;
+    float* red = smem + (size_t)G * P.chunk;
     const int n8 = n - (n % 8);
+    const float* Sg = P.S + ((size_t)row * P.nh + kvh * G) * P.max_pos;
     float lsum[G];
 #pragma unroll
     for (int g = 0; g < G; g++) lsum[g] = 0.0f;
     for (int i = threadIdx.x; i < len; i += DA_THREADS) {
-        int p = p0 + i;
-        const float* srow = P.S + ((size_t)row * P.nh + kvh * G) * P.max_pos + p;
 #pragma unroll
         for (int g = 0; g < G; g++) {
-            float e = softmax_weight(srow[(size_t)g * P.max_pos], gmax[g], p, n8);
-            sw[g * P.chunk + i] = e;
+            float e = softmax_weight(Sg[(size_t)g * P.max_pos + p0 + i], gmax[g], p0 + i, n8);
+            W[(size_t)g * P.chunk + i] = e;
             lsum[g] += e;
         }
     }
-    float* part = sw + G * P.chunk;  // [8 warps][G][hd]
     float total[G];
 #pragma unroll
-    for (int g = 0; g < G; g++) total[g] = block_sum(lsum[g], red);  // also a barrier for sw
+    for (int g = 0; g < G; g++) total[g] = block_sum(lsum[g], redv);
     const KT* vbase = reinterpret_cast<const KT*>(P.vc) + (size_t)seq * P.seq_stride + (size_t)kvh * P.head_stride;
-    for (int d0 = lane * 4; d0 < hd; d0 += 128) {
-        float acc[G][4];
+    float o[G][C::EPL];
 #pragma unroll
-        for (int g = 0; g < G; g++)
+    for (int g = 0; g < G; g++)
 #pragma unroll
-            for (int j = 0; j < 4; j++) acc[g][j] = 0.0f;
-        // 4 positions per iteration: four independent row loads in flight per lane
-        constexpr int U = 4;
-        for (int i0 = warp; i0 < len; i0 += 8 * U) {
-            float v4[U][4];
-#pragma unroll
-            for (int u = 0; u < U; u++) {
-                int i = i0 + 8 * u;
-                if (i < len) {
-                    const KT* vp = vbase + (size_t)(p0 + i) * hd + d0;
-                    if constexpr (sizeof(KT) == 2) {
-                        uint2 uu = __ldg(reinterpret_cast<const uint2*>(vp));
-                        float2 a = __half22float2(*reinterpret_cast<const __half2*>(&uu.x));
-                        float2 b = __half22float2(*reinterpret_cast<const __half2*>(&uu.y));
-                        v4[u][0] = a.x; v4[u][1] = a.y; v4[u][2] = b.x; v4[u][3] = b.y;
-                    } else {
-                        float4 a = __ldg(reinterpret_cast<const float4*>(vp));
-                        v4[u][0] = a.x; v4[u][1] = a.y; v4[u][2] = a.z; v4[u][3] = a.w;
-                    }
-                } else {
-                    v4[u][0] = v4[u][1] = v4[u][2] = v4[u][3] = 0.0f;
-                }
-            }
-#pragma unroll
-            for (int u = 0; u < U; u++) {
-                int i = i0 + 8 * u;
-                if (i >= len) break;
-#pragma unroll
-                for (int g = 0; g < G; g++) {
-                    float w = sw[g * P.chunk + i];
-#pragma unroll
-                    for (int j = 0; j < 4; j++) acc[g][j] = fmaf(w, v4[u][j], acc[g][j]);
-                }
-            }
-        }
-#pragma unroll
-        for (int g = 0; g < G; g++)
-#pragma unroll
-            for (int j = 0; j < 4; j++) part[((size_t)warp * G + g) * hd + d0 + j] = acc[g][j];
-    }
-    __syncthreads();
-    for (int i = threadIdx.x; i < G * hd; i += DA_THREADS) {
-        int g = i / hd, d = i % hd;
-        float o = 0.0f;
-#pragma unroll
-        for (int w = 0; w < 8; w++) o += part[((size_t)w * G + g) * hd + d];
+        for (int e = 0; e < C::EPL; e++) o[g][e] = 0.0f;
+    da_pv<KT, G, HD>(vbase, W, (size_t)P.chunk, p0, p0, p1, o);
+    da_reduce_o<KT, G, HD>(o, red);
+    const float* fin = red + (size_t)DA_WARPS * G * HD;
+    for (int i = threadIdx.x; i < G * HD; i += DA_THREADS) {
+        int g = i / HD, d = i % HD;
         size_t hidx = (size_t)row * P.nh + kvh * G + g;
         if (nsplit_eff == 1) {
-            P.out[(size_t)row * P.ldo + (size_t)(kvh * G + g) * hd + d] = __fdiv_rn(o, total[g]);
+            da_write_out(P, row, kvh * G + g, d, __fdiv_rn(fin[i], total[g]));
         } else {
-            P.opart[(hidx * P.nsplit + split) * hd + d] = o;
+            P.opart[(hidx * P.nsplit + split) * HD + d] = fin[i];
             if (d == 0) P.spart[hidx * P.nsplit + split] = total[g];
         }
     }
 }
 
-// Pass 3 (several splits): out = sum of partial P.V / sum of partial weights.
+// Split path, pass 3: out = sum of partial P.V / sum of partial weights.
 __global__ void k_dattn_combine(DecAttnParams P) {
     const int row = blockIdx.x, h = blockIdx.y;
     const int seq = P.seqs[row];
@@ -387,37 +527,52 @@ __global__ void k_dattn_combine(DecAttnParams P) {
     if (nsplit_eff == 1) return;
     size_t hidx = (size_t)row * P.nh + h;
     float total = 0.0f;
-    for (int s = 0; s < nsplit_eff; s++) total += P.spart[hidx * P.nsplit + s];
+    for (int s2 = 0; s2 < nsplit_eff; s2++) total += P.spart[hidx * P.nsplit + s2];
     for (int d = threadIdx.x; d < P.hd; d += blockDim.x) {
         float o = 0.0f;
-        for (int s = 0; s < nsplit_eff; s++) o += P.opart[(hidx * P.nsplit + s) * P.hd + d];
-        P.out[(size_t)row * P.ldo + (size_t)h * P.hd + d] = __fdiv_rn(o, total);
+        for (int s2 = 0; s2 < nsplit_eff; s2++) o += P.opart[(hidx * P.nsplit + s2) * P.hd + d];
+        da_write_out(P, row, h, d, __fdiv_rn(o, total));
     }
+}
+
+template <typename KT, int G, int HD>
+int launch_dattn_ghd(const DecAttnParams& P, int rows, cudaStream_t s) {
+    const size_t red_floats = (size_t)(DA_WARPS + 1) * G * HD;
+    if (P.nsplit == 1) {
+        size_t smem = ((size_t)G * P.max_pos + red_floats) * sizeof(float);
+        HC_CHECK(smem <= 220 * 1024, HC_ERR_UNSUPPORTED, "decode attention: context %d too long for one split",
+                 P.max_pos);
+        if (smem > 48 * 1024)
+            HC_CUDA(cudaFuncSetAttribute(k_dattn_fused<KT, G, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem));
+        k_dattn_fused<KT, G, HD><<<dim3((unsigned)rows, (unsigned)P.nkv), DA_THREADS, smem, s>>>(P);
+        HC_LAUNCH_CHECK();
+        return HC_OK;
+    }
+    dim3 grid((unsigned)rows, (unsigned)P.nkv, (unsigned)P.nsplit);
+    k_dattn_scores<KT, G, HD><<<grid, DA_THREADS, 0, s>>>(P);
+    HC_LAUNCH_CHECK();
+    size_t smem2 = ((size_t)G * P.chunk + red_floats) * sizeof(float);
+    if (smem2 > 48 * 1024)
+        HC_CUDA(cudaFuncSetAttribute(k_dattn_pv<KT, G, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2));
+    k_dattn_pv<KT, G, HD><<<grid, DA_THREADS, smem2, s>>>(P);
+    HC_LAUNCH_CHECK();
+    k_dattn_combine<<<dim3((unsigned)rows, (unsigned)P.nh), 128, 0, s>>>(P);
+    HC_LAUNCH_CHECK();
+    return HC_OK;
 }
 
 template <typename KT, int G>
 int launch_dattn_g(const DecAttnParams& P, int rows, cudaStream_t s) {
-    dim3 grid((unsigned)rows, (unsigned)P.nkv, (unsigned)P.nsplit);
     switch (P.hd) {
-        case 16: k_dattn_scores<KT, G, 16><<<grid, DA_THREADS, 0, s>>>(P); break;
-        case 32: k_dattn_scores<KT, G, 32><<<grid, DA_THREADS, 0, s>>>(P); break;
-        case 64: k_dattn_scores<KT, G, 64><<<grid, DA_THREADS, 0, s>>>(P); break;
-        case 128: k_dattn_scores<KT, G, 128><<<grid, DA_THREADS, 0, s>>>(P); break;
+        case 16: return launch_dattn_ghd<KT, G, 16>(P, rows, s);
+        case 32: return launch_dattn_ghd<KT, G, 32>(P, rows, s);
+        case 64: return launch_dattn_ghd<KT, G, 64>(P, rows, s);
+        case 128: return launch_dattn_ghd<KT, G, 128>(P, rows, s);
         default:
             hc_set_error("grouped decode attention: unsupported head_dim %d", P.hd);
             return HC_ERR_UNSUPPORTED;
     }
-    HC_LAUNCH_CHECK();
-    size_t smem2 = ((size_t)G * P.chunk + 8 * (size_t)G * P.hd) * sizeof(float);
-    if (smem2 > 48 * 1024)
-        HC_CUDA(cudaFuncSetAttribute(k_dattn_pv<KT, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2));
-    k_dattn_pv<KT, G><<<grid, DA_THREADS, smem2, s>>>(P);
-    HC_LAUNCH_CHECK();
-    if (P.nsplit > 1) {
-        k_dattn_combine<<<dim3((unsigned)rows, (unsigned)P.nh), 128, 0, s>>>(P);
-        HC_LAUNCH_CHECK();
-    }
-    return HC_OK;
 }
 
 template <typename KT>
@@ -425,7 +580,6 @@ int launch_dattn_kt(const DecAttnParams& P, int rows, cudaStream_t s) {
     switch (P.nh / P.nkv) {
         case 1: return launch_dattn_g<KT, 1>(P, rows, s);
         case 2: return launch_dattn_g<KT, 2>(P, rows, s);
-        case 3: return launch_dattn_g<KT, 3>(P, rows, s);
         case 4: return launch_dattn_g<KT, 4>(P, rows, s);
         case 8: return launch_dattn_g<KT, 8>(P, rows, s);
         default:
@@ -438,7 +592,7 @@ int launch_dattn_kt(const DecAttnParams& P, int rows, cudaStream_t s) {
 
 bool dattn_supported(int nh, int nkv, int hd) {
     int g = nh / nkv;
-    return (hd == 16 || hd == 32 || hd == 64 || hd == 128) && (g == 1 || g == 2 || g == 3 || g == 4 || g == 8);
+    return (hd == 16 || hd == 32 || hd == 64 || hd == 128) && (g == 1 || g == 2 || g == 4 || g == 8);
 }
 
 int launch_decode_attention(const DecAttnParams& P, int rows, int kv_fp16, cudaStream_t s) {
@@ -586,13 +740,13 @@ __global__ void __launch_bounds__(PA_THREADS) k_pattn(AttnParams P, int T) {
         int t = t0 + ty * 4 + i;
         if (t >= T) continue;
         float* out = P.out + (size_t)t * P.ldo + (size_t)h * HD + tx * DC;
-        if (t < 2) {
-            const float* vs = P.vself + (size_t)t * P.ldself + (size_t)kvh * HD + tx * DC;
+        __half* o16 = P.out16 ? P.out16 + (size_t)t * P.nh * HD : nullptr;
+        const float* vs = P.vself + (size_t)t * P.ldself + (size_t)kvh * HD + tx * DC;
 #pragma unroll
-            for (int j = 0; j < DC; j++) out[j] = vs[j];
-        } else {
-#pragma unroll
-            for (int j = 0; j < DC; j++) out[j] = __fdiv_rn(o[i][j], rsum[i]);
+        for (int j = 0; j < DC; j++) {
+            float r = (t < 2) ? vs[j] : __fdiv_rn(o[i][j], rsum[i]);
+            out[j] = r;
+            if (o16) o16[perm_k(h * HD + tx * DC + j)] = __float2half_rn(r);
         }
     }
 }

@@ -344,8 +344,11 @@ HC_EXPORT int hc_q4_matmul_dev(const hc_q4_matrix* w, const float* x, size_t mto
         static std::atomic<unsigned> calls{0};
         HC_TRY(hc::gemm_tc(ws, *w, x, w->k, mtok, y, w->n, hc::EPI_STORE, nullptr, 0, s));
         // The abort flag is read (with a device sync) only every 64th call so
-        // timing loops stay asynchronous; hc_q4_matmul_check reads it now.
-        if ((++calls & 63u) == 0) return hc::gemm_check(ws);
+        // timing loops stay asynchronous, and never while the stream is being
+        // captured into a graph (a capturing stream cannot be synchronized).
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        HC_CUDA(cudaStreamIsCapturing(s, &cs));
+        if (cs == cudaStreamCaptureStatusNone && (++calls & 63u) == 0) return hc::gemm_check(ws);
         return HC_OK;
     }
     DevWeight dw;

@@ -13,8 +13,14 @@ bool gemm_tc_eligible(const hc_q4_matrix& w, size_t tokens);
 
 // Y[t][n] (+)= sum_k X[t][k] * deq(W)[n][k] for t < tokens, fp16 operands and
 // f32 accumulation in tensor memory; same epilogue contract as launch_matmul.
+// xh_ready: the same activations already in fp16, rows of k elements in the
+// GEMM's K order (within every 8 elements: e0 e4 e1 e5 e2 e6 e3 e7); when
+// null, x is converted first.
 int gemm_tc(GemmWorkspace* ws, const hc_q4_matrix& w, const float* x, size_t ldx, size_t tokens, float* y,
-            size_t ldy, int epi, const float* res, size_t ldres, cudaStream_t s);
+            size_t ldy, int epi, const float* res, size_t ldres, cudaStream_t s, const __half* xh_ready = nullptr);
+
+// Index of element e of a row in the GEMM's fp16 K order.
+__host__ __device__ inline int perm_k(int e) { return (e & ~7) | ((e & 3) << 1) | ((e >> 2) & 1); }
 
 // Reads and clears the device flag set by a timed-out pipeline wait
 // (synchronizes the device); HC_ERR_TIMEOUT when a kernel aborted.

@@ -10,15 +10,17 @@
 //
 //   TMA (warp 0)      X tile (fp16, K-major, 128B swizzle) + the Q4_0 nibble
 //                     tile of 128 rows x 128 K  -> shared memory stage s
-//   dequant (warps 4-11, two warpgroups, one weight row per thread)
-//                     nibbles -> (nib - 8) * scale in fp16 -> tcgen05.st into
-//                     tensor memory (the A operand never touches shared
-//                     memory, so shared-memory bandwidth is left to the TMA
-//                     traffic and the B operand)
+//   dequant (warps 4-19 for prefill tiles, 4-11 for decode tiles; one
+//                     weight row per thread) nibbles -> (nib - 8) * scale in
+//                     fp16 -> tcgen05.st into tensor memory (the A operand
+//                     never touches shared memory, so shared-memory bandwidth
+//                     is left to the TMA traffic and the B operand)
 //   MMA (warp 1)      tcgen05.mma.kind::f16, A from TMEM, B from the smem
 //                     descriptor, f32 accumulator in TMEM; tcgen05.commit
 //                     frees the stage
-//   epilogue (warps 4-7)  tcgen05.ld of the accumulator -> Y (+ residual)
+//   epilogue (warps 4-7)  tcgen05.ld of the accumulator -> Y (+ residual);
+//                     with split K, the last CTA of a tile to finish adds the
+//                     partial sums in split order
 //
 // No cluster multicast is used anywhere (the same code runs under tensor
 // parallelism on several GPUs).  Every mbarrier wait is bounded by a clock
@@ -40,7 +42,6 @@ namespace {
 
 constexpr int BM = 128;      // weight rows per tile (MMA M)
 constexpr int BK = 128;      // K per pipeline stage
-constexpr int TMEM_COLS = 512;
 constexpr long long WAIT_CYCLES = 4000000000LL;  // ~2 s at 1.9 GHz
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -99,6 +100,36 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
 __device__ __forceinline__ void tmem_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tmem_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
+__device__ __forceinline__ void tmem_st_x32(uint32_t taddr, const uint32_t* v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
+        "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
+        "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_st_x16(uint32_t taddr, const uint32_t* v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld_x16(uint32_t taddr, uint32_t* v) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+          "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr)
+        : "memory");
+}
+
 __device__ __forceinline__ void tmem_ld_x32(uint32_t taddr, uint32_t* v) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
@@ -147,6 +178,47 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
                  : "memory");
 }
 
+constexpr int EPI_CH = 16;     // tokens per epilogue chunk (one tcgen05.ld x16)
+constexpr int MAX_SPLITS = 8;  // split-K cluster size limit (portable cluster size)
+
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// f32 at shared-memory offset `local` (this CTA's address of it) in the CTA
+// of the cluster with the given rank.
+__device__ __forceinline__ float ld_dsmem_f32(uint32_t local, int rank) {
+    uint32_t remote;
+    float v;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local), "r"(rank));
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+    return v;
+}
+
+// y[jj * ldy] = v[jj] (+ res[jj * ldres]) for jj < tl, one column of an
+// EPI_CH-token chunk.  The residuals are all loaded before the first store
+// (res may alias y element for element, so plain coherent loads are used).
+__device__ __forceinline__ void store_chunk(float* y, size_t ldy, const uint32_t* v, int tl, const float* res,
+                                            size_t ldres) {
+    float r[EPI_CH];
+#pragma unroll
+    for (int jj = 0; jj < EPI_CH; jj++) r[jj] = (res && jj < tl) ? res[(size_t)jj * ldres] : 0.0f;
+#pragma unroll
+    for (int jj = 0; jj < EPI_CH; jj++) {
+        if (jj < tl) {
+            float o = __uint_as_float(v[jj]);
+            if (res) o = o + r[jj];
+            y[(size_t)jj * ldy] = o;
+        }
+    }
+}
+
 // K order inside a 32-element Q4_0 block.  Word i (4 bytes = elements
 // 8i..8i+7, low nibble first) yields four fp16 pairs with one shift and one
 // and/or each: pair k = (element 8i+k, element 8i+k+4).  The A operand (the
@@ -164,15 +236,6 @@ __device__ __forceinline__ uint32_t deq_pair(uint32_t w, int k, __half2 s2) {
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
-__device__ __forceinline__ void tmem_st_x16(uint32_t taddr, const uint32_t* v) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-        "%15, %16};" ::"r"(taddr),
-        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
-        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
-        : "memory");
-}
-
 // Warp-uniform bounded wait: lane 0 polls, the verdict is broadcast, then
 // every lane observes the completed phase once itself (acquire ordering for
 // its own reads of the data the barrier guards).
@@ -184,35 +247,55 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
     return ok;
 }
 
+// Pipeline shapes.  A decode tile (TN <= 64 tokens) is bound by the rate at
+// which ONE thread can issue MMAs (each tcgen05.mma of 128 x TN x 16 plus its
+// commit and the fence after a barrier wait holds the issuing thread far
+// longer than the tensor pipe needs), so two CTAs share an SM, each with 256
+// tensor-memory columns and its own issuer; each keeps a deep shared-memory
+// ring of TMA stages (hiding DRAM latency) but only three tensor-memory A
+// slots.  A prefill tile (TN >= 128) keeps one CTA per SM with all 512
+// columns, where the larger N makes every MMA worth its issue cost.
 template <int TN>
 struct Cfg {
-    static constexpr int STAGES = TN <= 64 ? 7 : (TN == 128 ? 5 : 3);
-    static constexpr int A_COL = TN <= 64 ? 64 : TN;  // A stages start here; D occupies [0, TN)
-    static constexpr int X_STAGE = 2 * TN * 128;      // two 64-element K halves, 128 B per token row
-    static constexpr int W_STAGE = BM * (BK / 2);     // 128 rows x 64 nibble bytes
+    static constexpr bool DUAL = TN <= 64;                   // two CTAs per SM
+    static constexpr int COLS = DUAL ? 256 : 512;            // tensor-memory columns per CTA
+    static constexpr int DEQ_WARPS = DUAL ? 8 : 16;
+    static constexpr int THREADS = 128 + 32 * DEQ_WARPS;
+    static constexpr int MIN_BLOCKS = DUAL ? 2 : 1;
+    static constexpr int X_STAGE = 2 * TN * 128;             // two 64-element K halves, 128 B per token row
+    static constexpr int W_STAGE = BM * (BK / 2);            // 128 rows x 64 nibble bytes
+    static constexpr int S_SM = DUAL ? (TN <= 32 ? 6 : 4) : (TN == 128 ? 5 : 3);  // TMA ring stages
+    static constexpr int A_COL = TN <= 64 ? 64 : TN;         // A slots start here; D occupies [0, TN)
+    static constexpr int S_TM = (COLS - A_COL) / 64 < S_SM ? (COLS - A_COL) / 64 : S_SM;  // A slots
+    static constexpr int MMA_BATCH = S_TM < 4 ? S_TM : 4;   // stages issued under one wait + fence
+    static constexpr int RR = DUAL ? 1 : (S_TM >= 4 ? 4 : 2);  // dequant groups working on different stages
+    static constexpr int WG_PER = (DEQ_WARPS / 4) / RR;       // warpgroups per group, each 4 / WG_PER blocks
     __host__ __device__ static constexpr int x_off(int s) { return s * X_STAGE; }
-    __host__ __device__ static constexpr int w_off(int s) { return STAGES * X_STAGE + s * W_STAGE; }
-    __host__ __device__ static constexpr int bar_off() { return STAGES * (X_STAGE + W_STAGE); }
-    __host__ __device__ static constexpr int smem() { return bar_off() + (3 * STAGES + 1) * 8 + 16 + 1024; }
-    static_assert(A_COL + 64 * STAGES <= TMEM_COLS, "tensor memory budget");
+    __host__ __device__ static constexpr int w_off(int s) { return S_SM * X_STAGE + s * W_STAGE; }
+    __host__ __device__ static constexpr int bar_off() { return S_SM * (X_STAGE + W_STAGE); }
+    __host__ __device__ static constexpr int smem() { return bar_off() + (2 * S_SM + 2 * S_TM + 1) * 8 + 16 + 1024; }
+    static_assert(A_COL + 64 * S_TM <= COLS, "tensor memory budget");
+    static_assert(RR <= S_TM && RR <= S_SM, "dequant groups must not run more than one barrier phase apart");
+    static_assert(WG_PER >= 1 && 4 % WG_PER == 0, "dequant split");
+    static_assert(!DUAL || 2 * (smem() + 1024) <= 233472, "two CTAs must fit in one SM's shared memory");
+    static constexpr int RED_PITCH = TN + 1;                  // floats per row of the split-K partial tile
+    static_assert(BM * RED_PITCH * 4 <= S_SM * (X_STAGE + W_STAGE), "partial tile fits in the TMA stages");
 };
 
-constexpr int NDEQ_WARPS = 16;                  // 4 warpgroups, one Q4_0 block of the stage each
-constexpr int GEMM_THREADS = 128 + 32 * NDEQ_WARPS;
-
 template <int TN>
-__global__ void __launch_bounds__(GEMM_THREADS, 1)
+__global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
     k_q4_gemm_tc(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
                  const __half* __restrict__ scales, float* __restrict__ y, size_t ldy, const float* res, size_t ldres,
-                 int epi, int N, int K, int T, int splits, float* __restrict__ partial, int* __restrict__ err) {
+                 int epi, int N, int K, int T, int splits, int* __restrict__ err) {
     using C = Cfg<TN>;
-    constexpr int STAGES = C::STAGES;
+    constexpr int S_SM = C::S_SM, S_TM = C::S_TM;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::bar_off());
-    uint64_t* aready = full + STAGES;
-    uint64_t* empty = aready + STAGES;
-    uint64_t* dfull = empty + STAGES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::bar_off());  // [S_SM] TMA landed
+    uint64_t* sempty = full + S_SM;                                     // [S_SM] MMAs reading it done
+    uint64_t* aready = sempty + S_SM;                                   // [S_TM] A slot written
+    uint64_t* tempty = aready + S_TM;                                   // [S_TM] MMAs reading it done
+    uint64_t* dfull = tempty + S_TM;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dfull + 1);
     __shared__ int abort_flag;
 
@@ -225,17 +308,20 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 
     if (threadIdx.x == 0) {
         abort_flag = 0;
-        for (int st = 0; st < STAGES; st++) {
+        for (int st = 0; st < S_SM; st++) {
             mbar_init(&full[st], 1);
-            mbar_init(&aready[st], NDEQ_WARPS);
-            mbar_init(&empty[st], 1);
+            mbar_init(&sempty[st], 1);
+        }
+        for (int a = 0; a < S_TM; a++) {
+            mbar_init(&aready[a], 4 * C::WG_PER);  // the warps of the group that owns the stage
+            mbar_init(&tempty[a], 1);
         }
         mbar_init(dfull, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 2) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(TMEM_COLS)
+                     "r"(C::COLS)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -244,13 +330,17 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     tmem_fence_after();
     const uint32_t tmem = *tmem_slot;
 
+    // Stage j (k range it0 + j) lives in TMA ring stage j % S_SM and tensor-
+    // memory A slot j % S_TM.  Phase parities below are those of the j-th use
+    // of each barrier; every wait is at most one phase away from the phase it
+    // observes (see the dequant note), which is what parity waits require.
     if (warp == 0) {
         // ---------------- TMA producer
         if (lane == 0) {
             for (int j = 0; j < nk; j++) {
-                int st = j % STAGES;
-                uint32_t ph = (uint32_t)(j / STAGES) & 1u;
-                if (!mbar_wait(&empty[st], ph ^ 1u, &abort_flag)) break;
+                const int st = j % S_SM;
+                const uint32_t ph = (uint32_t)(j / S_SM) & 1u;
+                if (!mbar_wait(&sempty[st], ph ^ 1u, &abort_flag)) break;
                 mbar_expect_tx(&full[st], (uint32_t)(C::X_STAGE + C::W_STAGE));
                 uint8_t* xs = smem + C::x_off(st);
                 int kk = (it0 + j) * BK;
@@ -261,86 +351,131 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer
+        // The tcgen05 fence that must follow each barrier wait stalls the
+        // issuing thread, so every stage that is already dequantized when the
+        // oldest one is (up to MMA_BATCH) is taken under a single wait + fence.
+        // A slot observed here cannot be a phase ahead (its next fill needs
+        // this thread's MMA of it).
         if (lane == 0) {
             constexpr uint32_t idesc = make_idesc(TN);
             bool ok = true;
-            for (int j = 0; j < nk; j++) {
-                int st = j % STAGES;
-                uint32_t ph = (uint32_t)(j / STAGES) & 1u;
-                if (!mbar_wait(&aready[st], ph, &abort_flag)) {
+            for (int j = 0; j < nk;) {
+                if (!mbar_wait(&aready[j % S_TM], (uint32_t)(j / S_TM) & 1u, &abort_flag)) {
                     ok = false;
                     break;
                 }
+                int cnt = 1;
+                while (cnt < C::MMA_BATCH && j + cnt < nk &&
+                       mbar_try_wait(&aready[(j + cnt) % S_TM], (uint32_t)((j + cnt) / S_TM) & 1u))
+                    cnt++;
                 tmem_fence_after();
-                const uint32_t xs = smem_u32(smem + C::x_off(st));
+                for (int b = 0; b < cnt; b++, j++) {
+                    const int st = j % S_SM, a = j % S_TM;
+                    const uint32_t xs = smem_u32(smem + C::x_off(st));
 #pragma unroll
-                for (int kk = 0; kk < BK / 16; kk++) {
-                    uint32_t a_tmem = tmem + (uint32_t)(C::A_COL + st * 64 + kk * 8);
-                    uint32_t b_addr = xs + (uint32_t)((kk >> 2) * TN * 128 + (kk & 3) * 32);
-                    mma_f16_ts(tmem, a_tmem, sw128_desc(b_addr), idesc, (j > 0 || kk > 0) ? 1u : 0u);
+                    for (int kk = 0; kk < BK / 16; kk++) {
+                        uint32_t a_tmem = tmem + (uint32_t)(C::A_COL + a * 64 + kk * 8);
+                        uint32_t b_addr = xs + (uint32_t)((kk >> 2) * TN * 128 + (kk & 3) * 32);
+                        mma_f16_ts(tmem, a_tmem, sw128_desc(b_addr), idesc, (j > 0 || kk > 0) ? 1u : 0u);
+                    }
+                    mma_commit(&sempty[st]);
+                    mma_commit(&tempty[a]);
                 }
-                mma_commit(&empty[st]);
             }
             if (ok) mma_commit(dfull);
         }
     } else if (warp >= 4) {
-        // ---------------- dequant: thread <-> weight row (TMEM lane), warpgroup <-> Q4_0 block of the stage
-        const int g = (warp - 4) >> 2;   // block 0..3 of the 128-element stage
+        // ---------------- dequant: thread <-> weight row (TMEM lane).  The
+        // dequant warpgroups form RR groups; group g converts the stages j
+        // with j % RR == g (each of its WG_PER warpgroups 4 / WG_PER of the
+        // stage's Q4_0 blocks), so RR stages are in flight at once.  RR <= S_TM
+        // and RR <= S_SM keep every group within one barrier phase of the
+        // others: a group reaching stage j has finished j - RR, which needed
+        // the MMA of j - RR - S_TM and the TMA of j - RR (itself issued after
+        // the MMA of j - RR - S_SM), so the phases a wait can observe are the
+        // awaited one and the one before it (parity waits cannot tell phases
+        // two apart).
+        const int wg = (warp - 4) >> 2;
+        const int g = wg / C::WG_PER;
+        const int part = wg % C::WG_PER;
         const int q = warp & 3;          // TMEM lane quarter of this warp
         const int r = q * 32 + lane;
         const int n = n0 + r;
         const bool row_ok = n < N;
-        const __half* srow = scales + (size_t)(row_ok ? n : 0) * KB;
-        unsigned short sc_next = row_ok ? __ldg(reinterpret_cast<const unsigned short*>(srow) + it0 * 4 + g) : 0;
+        const uint2* srow = reinterpret_cast<const uint2*>(scales + (size_t)(row_ok ? n : 0) * KB);
+        uint2 sc_next = make_uint2(0u, 0u);
+        if (row_ok && g < nk) sc_next = __ldg(srow + it0 + g);
         bool ok = true;
-        for (int j = 0; j < nk; j++) {
-            int st = j % STAGES;
-            uint32_t ph = (uint32_t)(j / STAGES) & 1u;
-            unsigned short sc = sc_next;
-            if (j + 1 < nk && row_ok)
-                sc_next = __ldg(reinterpret_cast<const unsigned short*>(srow) + (it0 + j + 1) * 4 + g);
-            if (!warp_wait(&empty[st], ph ^ 1u, &abort_flag) || !warp_wait(&full[st], ph, &abort_flag)) {
+        for (int j = g; j < nk; j += C::RR) {
+            const int st = j % S_SM, a = j % S_TM;
+            uint2 sc = sc_next;
+            if (j + C::RR < nk && row_ok) sc_next = __ldg(srow + it0 + j + C::RR);
+            if (!warp_wait(&tempty[a], ((uint32_t)(j / S_TM) & 1u) ^ 1u, &abort_flag) ||
+                !warp_wait(&full[st], (uint32_t)(j / S_SM) & 1u, &abort_flag)) {
                 ok = false;
                 break;
             }
-            uint4 q4 = *reinterpret_cast<const uint4*>(smem + C::w_off(st) + r * (BK / 2) + g * 16);
-            __half2 s2 = __half2half2(__ushort_as_half(sc));
-            uint32_t v[16];
-            const uint32_t w4[4] = {q4.x, q4.y, q4.z, q4.w};
+            // 64-byte rows of nibbles, 16-byte chunk c of row r stored at chunk c ^ ((r >> 1) & 3)
+            const uint8_t* wrow = smem + C::w_off(st) + r * (BK / 2);
+            const int sw = (r >> 1) & 3;
+            const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(C::A_COL + a * 64);
+            // Q4_0 blocks [blk0, blk0 + BLK_PER) of the stage, two per TMEM
+            // store (one when a warpgroup converts a single block)
+            constexpr int BLK_PER = 4 / C::WG_PER;
+            constexpr int PER_ST = BLK_PER >= 2 ? 2 : 1;
+            const int blk0 = part * BLK_PER;
 #pragma unroll
-            for (int wd = 0; wd < 4; wd++)
+            for (int hh = 0; hh < BLK_PER / PER_ST; hh++) {
+                uint32_t v[16 * PER_ST];
 #pragma unroll
-                for (int k = 0; k < 4; k++) v[wd * 4 + k] = deq_pair(w4[wd], k, s2);
-            tmem_st_x16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(C::A_COL + st * 64 + g * 16), v);
+                for (int bb = 0; bb < PER_ST; bb++) {
+                    const int blk = blk0 + hh * PER_ST + bb;
+                    uint4 q4 = *reinterpret_cast<const uint4*>(wrow + ((blk ^ sw) << 4));
+                    uint32_t s32 = (blk < 2) ? sc.x : sc.y;
+                    uint32_t s16 = (blk & 1) ? (s32 >> 16) : (s32 & 0xFFFFu);
+                    __half2 s2 = __half2half2(__ushort_as_half((unsigned short)s16));
+                    const uint32_t w4[4] = {q4.x, q4.y, q4.z, q4.w};
+#pragma unroll
+                    for (int wd = 0; wd < 4; wd++)
+#pragma unroll
+                        for (int k = 0; k < 4; k++) v[bb * 16 + wd * 4 + k] = deq_pair(w4[wd], k, s2);
+                }
+                const uint32_t tcol = tbase + (uint32_t)((blk0 + hh * PER_ST) * 16);
+                if constexpr (PER_ST == 2) tmem_st_x32(tcol, v);
+                else tmem_st_x16(tcol, v);
+            }
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             tmem_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&aready[st]);
+            if (lane == 0) mbar_arrive(&aready[a]);
         }
         // ---------------- epilogue (first warpgroup)
-        if (g == 0) {
-            bool okd = ok && warp_wait(dfull, 0, &abort_flag);
+        if (wg == 0) {
+            bool okd = __all_sync(0xffffffffu, ok) && warp_wait(dfull, 0, &abort_flag);
+            // Every load of a 16-token chunk (residuals) is issued before the
+            // first dependent add: one memory round trip per chunk.
             if (okd) {
                 tmem_fence_after();
+                // split K: this CTA's partial tile goes to its own shared memory
+                // (the TMA stages are idle now: every load was consumed and
+                // every MMA reading them has completed), row-major with an odd
+                // row pitch so both the row-per-thread writes here and the
+                // token-fastest reads of the reduction are conflict-free
+                float* red = reinterpret_cast<float*>(smem);
 #pragma unroll 1
-                for (int c0 = 0; c0 < TN; c0 += 32) {
-                    uint32_t v[32];
-                    tmem_ld_x32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
+                for (int c0 = 0; c0 < TN; c0 += EPI_CH) {
+                    uint32_t v[EPI_CH];
+                    tmem_ld_x16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
                     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                    if (row_ok) {
+                    if (splits > 1) {
 #pragma unroll
-                        for (int jj = 0; jj < 32; jj++) {
-                            int t = t0 + c0 + jj;
-                            if (t < T) {
-                                float o = __uint_as_float(v[jj]);
-                                if (splits > 1) {
-                                    partial[((size_t)split * T + t) * N + n] = o;
-                                } else {
-                                    if (epi == EPI_ADD && res) o = o + res[(size_t)t * ldres + n];
-                                    y[(size_t)t * ldy + n] = o;
-                                }
-                            }
-                        }
+                        for (int jj = 0; jj < EPI_CH; jj++) red[r * C::RED_PITCH + c0 + jj] = __uint_as_float(v[jj]);
+                    } else {
+                        const int tl = min(EPI_CH, T - (t0 + c0));  // tokens of this chunk
+                        if (row_ok && tl > 0)
+                            store_chunk(y + (size_t)(t0 + c0) * ldy + n, ldy, v, tl,
+                                        (epi == EPI_ADD && res) ? res + (size_t)(t0 + c0) * ldres + n : nullptr,
+                                        ldres);
                     }
                 }
             }
@@ -350,21 +485,37 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     __syncthreads();
     if (warp == 2) {
         tmem_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::COLS) : "memory");
+    }
+    if (splits > 1) {
+        // The splits of a tile form one thread-block cluster.  After the
+        // cluster barrier every CTA reduces a slab of the tile's rows, adding
+        // the ranks' partial tiles in rank (= split) order through
+        // distributed shared memory, so the result is deterministic and no
+        // partial sum leaves the chip.  Every CTA reaches both barriers, also
+        // after an abort (the error flag then reports the garbage).
+        cluster_sync();
+        const uint32_t red_local = smem_u32(smem);
+        const int rows = min(BM, N - n0), toks = min(TN, T - t0);
+        const int rank = (int)cluster_ctarank();
+        const int r0 = rows * rank / splits, r1 = rows * (rank + 1) / splits, nr = r1 - r0;
+        for (int o = threadIdx.x; o < nr * toks; o += C::THREADS) {
+            const int rr = r0 + o % nr, t = o / nr;
+            const uint32_t off = (uint32_t)((rr * C::RED_PITCH + t) * 4);
+            float pv[MAX_SPLITS];
+#pragma unroll
+            for (int sp = 0; sp < MAX_SPLITS; sp++) pv[sp] = sp < splits ? ld_dsmem_f32(red_local + off, sp) : 0.0f;
+            float acc = 0.0f;
+#pragma unroll
+            for (int sp = 0; sp < MAX_SPLITS; sp++)
+                if (sp < splits) acc += pv[sp];
+            const size_t yi = (size_t)(t0 + t) * ldy + n0 + rr;
+            if (epi == EPI_ADD && res) acc = acc + res[(size_t)(t0 + t) * ldres + n0 + rr];
+            y[yi] = acc;
+        }
+        cluster_sync();  // peers finished reading this CTA's partial tile
     }
     if (threadIdx.x == 0 && abort_flag) atomicExch(err, 1);
-}
-
-// y[t][n] = (res[t][n] +) sum_s partial[s][t][n], in split order.
-__global__ void k_splitk_reduce(const float* __restrict__ partial, int splits, int T, int N, float* y, size_t ldy,
-                                int epi, const float* res, size_t ldres) {
-    size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= (size_t)T * N) return;
-    int t = (int)(i / N), n = (int)(i % N);
-    float o = partial[i];
-    for (int sp = 1; sp < splits; sp++) o += partial[(size_t)sp * T * N + i];
-    if (epi == EPI_ADD && res) o = o + res[(size_t)t * ldres + n];
-    y[(size_t)t * ldy + n] = o;
 }
 
 // fp32 rows -> fp16 rows in the K order of the weight tiles (see deq_pair):
@@ -414,8 +565,6 @@ struct GemmWorkspace {
     uint64_t generation = 0;  // bumped whenever a buffer a launch refers to moves
     __half* xh = nullptr;
     size_t xh_cap = 0;
-    float* part = nullptr;    // split-K partial sums
-    size_t part_cap = 0;
     int* err = nullptr;
     int device = -1;
     std::map<std::tuple<const void*, size_t, size_t>, CUtensorMap> wmaps;  // (nibble plane, n, k)
@@ -426,7 +575,6 @@ GemmWorkspace* gemm_workspace_new() { return new GemmWorkspace(); }
 void gemm_workspace_free(GemmWorkspace* ws) {
     if (!ws) return;
     if (ws->xh) cudaFree(ws->xh);
-    if (ws->part) cudaFree(ws->part);
     if (ws->err) cudaFree(ws->err);
     delete ws;
 }
@@ -438,50 +586,58 @@ bool gemm_tc_eligible(const hc_q4_matrix& w, size_t tokens) {
 namespace {
 template <int TN>
 int launch_tc(const hc_q4_matrix& w, const CUtensorMap& xmap, const CUtensorMap& wmap, size_t T, float* y,
-              size_t ldy, int epi, const float* res, size_t ldres, int splits, float* partial, int* err,
-              cudaStream_t s) {
+              size_t ldy, int epi, const float* res, size_t ldres, int splits, int* err, cudaStream_t s) {
     using C = Cfg<TN>;
     static_assert(C::smem() <= 232448, "shared memory budget");
     auto kfn = k_q4_gemm_tc<TN>;
-    // At least 116 KB of shared memory keeps one CTA per SM, so two CTAs never
-    // contend for the 512 tensor-memory columns each allocates.
-    const int smem = C::smem() < 118784 ? 118784 : C::smem();
+    // A 512-column CTA asks for at least 116 KB of shared memory, so it is
+    // alone on its SM; the 256-column (decode) CTAs fit two per SM and never
+    // three (their shared memory), so tensor-memory allocation never waits.
+    const int smem = (!C::DUAL && C::smem() < 118784) ? 118784 : C::smem();
     HC_CUDA(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    dim3 grid((unsigned)((w.n + BM - 1) / BM), (unsigned)((T + TN - 1) / TN), (unsigned)splits);
-    kfn<<<grid, GEMM_THREADS, smem, s>>>(xmap, wmap, w.sc, y, ldy, res, ldres, epi, (int)w.n, (int)w.k, (int)T, splits,
-                                         partial, err);
-    HC_LAUNCH_CHECK();
-    if (splits > 1) {
-        size_t tot = T * w.n;
-        k_splitk_reduce<<<(unsigned)((tot + 255) / 256), 256, 0, s>>>(partial, splits, (int)T, (int)w.n, y, ldy, epi,
-                                                                        res, ldres);
-        HC_LAUNCH_CHECK();
+    HC_CHECK(splits >= 1 && splits <= MAX_SPLITS, HC_ERR_INVALID, "tcgen05 GEMM: %d K splits", splits);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((w.n + BM - 1) / BM), (unsigned)((T + TN - 1) / TN), (unsigned)splits);
+    cfg.blockDim = dim3(C::THREADS);
+    cfg.dynamicSmemBytes = (size_t)smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    if (splits > 1) {  // the splits of one tile form a cluster (reduction over distributed shared memory)
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 1;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = (unsigned)splits;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
     }
+    HC_CUDA(cudaLaunchKernelEx(&cfg, kfn, xmap, wmap, (const __half*)w.sc, y, ldy, res, ldres, epi, (int)w.n,
+                               (int)w.k, (int)T, splits, err));
+    hc_count_launch();
     return HC_OK;
 }
 
-// Split K so that row tiles x token tiles x splits fills the 148 SMs
-// (one CTA per SM) without splits shorter than 4 pipeline stages.
-int choose_splits(size_t tiles, size_t nk) {
-    const size_t sms = 148;
-    if (tiles >= sms) return 1;
-    size_t best = 1;
-    double best_eff = (double)tiles / (double)sms;
-    for (size_t sp = 2; sp <= 16 && nk / sp >= 4; sp++) {
-        size_t ctas = tiles * sp;
-        size_t waves = (ctas + sms - 1) / sms;
-        double eff = (double)ctas / (double)(waves * sms);
-        if (eff > best_eff + 1e-9) {
-            best_eff = eff;
-            best = sp;
+// K splits per tile (1..MAX_SPLITS) minimizing a simple time model in units
+// of one pipeline stage: waves x (fixed cost of a CTA + its stages), plus
+// the cluster reduction when split.  The fixed cost (pipeline fill, tensor-
+// memory setup, epilogue) is worth about 11 stages.
+int choose_splits(size_t tiles, size_t nk, size_t slots) {
+    const double fixed = 11.0, reduce = 3.0;
+    int best = 1;
+    double best_cost = 1e300;
+    for (size_t sp = 1; sp <= (size_t)MAX_SPLITS && (sp == 1 || nk / sp >= 2); sp++) {
+        size_t waves = (tiles * sp + slots - 1) / slots;
+        double cost = (double)waves * (fixed + (double)((nk + sp - 1) / sp)) + (sp > 1 ? reduce : 0.0);
+        if (cost < best_cost - 1e-9) {
+            best_cost = cost;
+            best = (int)sp;
         }
     }
-    return (int)best;
+    return best;
 }
 }  // namespace
 
 int gemm_tc(GemmWorkspace* ws, const hc_q4_matrix& w, const float* x, size_t ldx, size_t tokens, float* y,
-            size_t ldy, int epi, const float* res, size_t ldres, cudaStream_t s) {
+            size_t ldy, int epi, const float* res, size_t ldres, cudaStream_t s, const __half* xh_ready) {
     std::lock_guard<std::mutex> lock(ws->mu);
     const size_t K = w.k, T = tokens;
     int dev = 0;
@@ -497,22 +653,24 @@ int gemm_tc(GemmWorkspace* ws, const hc_q4_matrix& w, const float* x, size_t ldx
         HC_CUDA(cudaMalloc((void**)&ws->err, sizeof(int)));
         HC_CUDA(cudaMemset(ws->err, 0, sizeof(int)));
     }
-    if (T * K > ws->xh_cap) {
+    if (!xh_ready && T * K > ws->xh_cap) {
         if (ws->xh) cudaFree(ws->xh);
         ws->xh = nullptr;
         ws->generation++;
         HC_CUDA(cudaMalloc((void**)&ws->xh, T * K * sizeof(__half)));
         ws->xh_cap = T * K;
     }
-    {
+    const __half* xh = xh_ready;
+    if (!xh) {
         unsigned gx = (unsigned)std::min<size_t>((K / 8 + 255) / 256, 16);
         k_rows_to_f16_perm<<<dim3(gx, (unsigned)T), 256, 0, s>>>(x, ldx, ws->xh, (int)K, (int)T);
         HC_LAUNCH_CHECK();
+        xh = ws->xh;
     }
     // Token tile: the smallest of 32/64/128/256 covering T (one tile for decode).
     int tn = T <= 32 ? 32 : T <= 64 ? 64 : T <= 128 ? 128 : 256;
     CUtensorMap xmap;
-    HC_TRY(encode_2d(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, ws->xh, K, T, K * 2, 64, (uint32_t)tn,
+    HC_TRY(encode_2d(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, const_cast<__half*>(xh), K, T, K * 2, 64, (uint32_t)tn,
                      CU_TENSOR_MAP_SWIZZLE_128B));
     auto key = std::make_tuple((const void*)w.qs, w.n, w.k);
     auto itw = ws->wmaps.find(key);
@@ -521,24 +679,16 @@ int gemm_tc(GemmWorkspace* ws, const hc_q4_matrix& w, const float* x, size_t ldx
         wmap = itw->second;
     } else {
         HC_TRY(encode_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.qs, K / 2, w.n, K / 2, BK / 2, BM,
-                         CU_TENSOR_MAP_SWIZZLE_NONE));
+                         CU_TENSOR_MAP_SWIZZLE_64B));
         if (w.owns) ws->wmaps[key] = wmap;
     }
     size_t tiles = ((w.n + BM - 1) / BM) * ((T + tn - 1) / tn);
-    int splits = choose_splits(tiles, K / BK);
-    if (splits > 1 && (size_t)splits * T * w.n > ws->part_cap) {
-        if (ws->part) cudaFree(ws->part);
-        ws->part = nullptr;
-        ws->part_cap = 0;
-        ws->generation++;
-        HC_CUDA(cudaMalloc((void**)&ws->part, (size_t)splits * T * w.n * sizeof(float)));
-        ws->part_cap = (size_t)splits * T * w.n;
-    }
+    int splits = choose_splits(tiles, K / BK, tn <= 64 ? 148 * Cfg<32>::MIN_BLOCKS : 148);
     switch (tn) {
-        case 32: return launch_tc<32>(w, xmap, wmap, T, y, ldy, epi, res, ldres, splits, ws->part, ws->err, s);
-        case 64: return launch_tc<64>(w, xmap, wmap, T, y, ldy, epi, res, ldres, splits, ws->part, ws->err, s);
-        case 128: return launch_tc<128>(w, xmap, wmap, T, y, ldy, epi, res, ldres, splits, ws->part, ws->err, s);
-        default: return launch_tc<256>(w, xmap, wmap, T, y, ldy, epi, res, ldres, splits, ws->part, ws->err, s);
+        case 32: return launch_tc<32>(w, xmap, wmap, T, y, ldy, epi, res, ldres, splits, ws->err, s);
+        case 64: return launch_tc<64>(w, xmap, wmap, T, y, ldy, epi, res, ldres, splits, ws->err, s);
+        case 128: return launch_tc<128>(w, xmap, wmap, T, y, ldy, epi, res, ldres, splits, ws->err, s);
+        default: return launch_tc<256>(w, xmap, wmap, T, y, ldy, epi, res, ldres, splits, ws->err, s);
     }
 }
 
@@ -637,12 +787,12 @@ HC_EXPORT int hc_q4_matmul_noalloc(const hc_q4_matrix* w, const float* x, size_t
     HC_TRY(hc::encode_2d(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xh, K, T, K * 2, 64, (uint32_t)tn,
                          CU_TENSOR_MAP_SWIZZLE_128B));
     HC_TRY(hc::encode_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->qs, K / 2, w->n, K / 2, hc::BK / 2, hc::BM,
-                         CU_TENSOR_MAP_SWIZZLE_NONE));
+                         CU_TENSOR_MAP_SWIZZLE_64B));
     switch (tn) {
-        case 32: return hc::launch_tc<32>(*w, xmap, wmap, T, y, w->n, hc::EPI_STORE, nullptr, 0, 1, nullptr, err, s);
-        case 64: return hc::launch_tc<64>(*w, xmap, wmap, T, y, w->n, hc::EPI_STORE, nullptr, 0, 1, nullptr, err, s);
-        case 128: return hc::launch_tc<128>(*w, xmap, wmap, T, y, w->n, hc::EPI_STORE, nullptr, 0, 1, nullptr, err, s);
-        default: return hc::launch_tc<256>(*w, xmap, wmap, T, y, w->n, hc::EPI_STORE, nullptr, 0, 1, nullptr, err, s);
+        case 32: return hc::launch_tc<32>(*w, xmap, wmap, T, y, w->n, hc::EPI_STORE, nullptr, 0, 1, err, s);
+        case 64: return hc::launch_tc<64>(*w, xmap, wmap, T, y, w->n, hc::EPI_STORE, nullptr, 0, 1, err, s);
+        case 128: return hc::launch_tc<128>(*w, xmap, wmap, T, y, w->n, hc::EPI_STORE, nullptr, 0, 1, err, s);
+        default: return hc::launch_tc<256>(*w, xmap, wmap, T, y, w->n, hc::EPI_STORE, nullptr, 0, 1, err, s);
     }
 }
 

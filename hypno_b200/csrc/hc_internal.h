@@ -87,13 +87,14 @@ int launch_matmul(const DevWeight& w, const float* x, size_t ldx, size_t mtok, f
                   int epi, const float* res, size_t ldres, cudaStream_t s);
 
 // Row-wise RMSNorm (kernels.rs:592-625): out[r] = x[r] * inv_rms(x[r]) * w.
+// out16 (may be null): the same rows in fp16, in the tensor-core GEMM's K order.
 int launch_rmsnorm(const float* x, size_t ldx, const float* w, float* out, size_t ldo, size_t rows,
-                   size_t n, float eps, cudaStream_t s);
+                   size_t n, float eps, cudaStream_t s, __half* out16 = nullptr);
 int launch_softmax_rows(float* x, size_t rows, size_t n, cudaStream_t s);
 int launch_silu(float* x, size_t n, cudaStream_t s);
 // act[r][i] = silu(gu[r][i]) * gu[r][im + i]
 int launch_silu_mul(const float* gu, size_t ldgu, float* act, size_t ldact, size_t rows, size_t im,
-                    cudaStream_t s);
+                    cudaStream_t s, __half* act16 = nullptr);
 // Rotation of `heads` adjacent-pair heads per row at position pos0 + row
 // using a (max_pos x hd/2) cos/sin table.
 int launch_rope_rows(float* x, size_t ldx, size_t rows, size_t heads, size_t hd, const float2* cs, size_t cs_rows,

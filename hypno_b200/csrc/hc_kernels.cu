@@ -4,6 +4,7 @@
 // The tensor-core GEMM lives in hc_gemm_tc.cu and attention in hc_attention.cu.
 #include "hc_internal.h"
 #include "hc_common.cuh"
+#include "hc_gemm.h"
 
 #include <algorithm>
 #include <math.h>
@@ -311,7 +312,7 @@ int launch_matmul(const DevWeight& w, const float* x, size_t ldx, size_t mtok, f
 // ============================================================ RMSNorm
 // kernels.rs:592-625: ms = sum(x^2)/n, inv = 1/sqrt(ms + eps), y = (x*inv)*w.
 __global__ void k_rmsnorm(const float* __restrict__ x, size_t ldx, const float* __restrict__ w,
-                          float* __restrict__ out, size_t ldo, int n, float eps) {
+                          float* __restrict__ out, size_t ldo, int n, float eps, __half* __restrict__ out16) {
     __shared__ float red[32];
     const float* xr = x + (size_t)blockIdx.x * ldx;
     float* orow = out + (size_t)blockIdx.x * ldo;
@@ -320,14 +321,18 @@ __global__ void k_rmsnorm(const float* __restrict__ x, size_t ldx, const float* 
     ss = block_sum(ss, red);
     float ms = __fdiv_rn(ss, (float)n);
     float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
-    for (int i = threadIdx.x; i < n; i += blockDim.x) orow[i] = __fmul_rn(__fmul_rn(xr[i], inv), w[i]);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        float o = __fmul_rn(__fmul_rn(xr[i], inv), w[i]);
+        orow[i] = o;
+        if (out16) out16[(size_t)blockIdx.x * n + perm_k(i)] = __float2half_rn(o);
+    }
 }
 
 // Same arithmetic with 16-byte accesses (n % 4 == 0, 16-byte aligned rows):
 // one float4 per thread per pass, the row held in registers between passes.
 template <int VPT>
 __global__ void k_rmsnorm_v4(const float* __restrict__ x, size_t ldx, const float* __restrict__ w,
-                             float* __restrict__ out, size_t ldo, int n, float eps) {
+                             float* __restrict__ out, size_t ldo, int n, float eps, __half* __restrict__ out16) {
     __shared__ float red[32];
     const float4* xr = reinterpret_cast<const float4*>(x + (size_t)blockIdx.x * ldx);
     const float4* wr = reinterpret_cast<const float4*>(w);
@@ -357,12 +362,19 @@ __global__ void k_rmsnorm_v4(const float* __restrict__ x, size_t ldx, const floa
             o.z = __fmul_rn(__fmul_rn(v[j].z, inv), ww.z);
             o.w = __fmul_rn(__fmul_rn(v[j].w, inv), ww.w);
             orow[i] = o;
+            if (out16) {
+                __half* r16 = out16 + (size_t)blockIdx.x * n;
+                r16[perm_k(4 * i)] = __float2half_rn(o.x);
+                r16[perm_k(4 * i + 1)] = __float2half_rn(o.y);
+                r16[perm_k(4 * i + 2)] = __float2half_rn(o.z);
+                r16[perm_k(4 * i + 3)] = __float2half_rn(o.w);
+            }
         }
     }
 }
 
 int launch_rmsnorm(const float* x, size_t ldx, const float* w, float* out, size_t ldo, size_t rows, size_t n,
-                   float eps, cudaStream_t s) {
+                   float eps, cudaStream_t s, __half* out16) {
     if (rows == 0) return HC_OK;
     bool vec = n % 4 == 0 && ldx % 4 == 0 && ldo % 4 == 0 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)w & 15) == 0 &&
                ((uintptr_t)out & 15) == 0 && n <= 4 * 1024 * 4;
@@ -370,11 +382,11 @@ int launch_rmsnorm(const float* x, size_t ldx, const float* w, float* out, size_
         size_t n4 = n / 4;
         unsigned threads = (unsigned)std::min<size_t>(1024, ((n4 + 31) / 32) * 32);
         size_t vpt = (n4 + threads - 1) / threads;
-        if (vpt <= 1) k_rmsnorm_v4<1><<<(unsigned)rows, threads, 0, s>>>(x, ldx, w, out, ldo, (int)n, eps);
-        else if (vpt <= 2) k_rmsnorm_v4<2><<<(unsigned)rows, threads, 0, s>>>(x, ldx, w, out, ldo, (int)n, eps);
-        else k_rmsnorm_v4<4><<<(unsigned)rows, threads, 0, s>>>(x, ldx, w, out, ldo, (int)n, eps);
+        if (vpt <= 1) k_rmsnorm_v4<1><<<(unsigned)rows, threads, 0, s>>>(x, ldx, w, out, ldo, (int)n, eps, out16);
+        else if (vpt <= 2) k_rmsnorm_v4<2><<<(unsigned)rows, threads, 0, s>>>(x, ldx, w, out, ldo, (int)n, eps, out16);
+        else k_rmsnorm_v4<4><<<(unsigned)rows, threads, 0, s>>>(x, ldx, w, out, ldo, (int)n, eps, out16);
     } else {
-        k_rmsnorm<<<(unsigned)rows, 256, 0, s>>>(x, ldx, w, out, ldo, (int)n, eps);
+        k_rmsnorm<<<(unsigned)rows, 256, 0, s>>>(x, ldx, w, out, ldo, (int)n, eps, out16);
     }
     HC_LAUNCH_CHECK();
     return HC_OK;
@@ -424,18 +436,21 @@ int launch_silu(float* x, size_t n, cudaStream_t s) {
 
 // transformer.rs:446-449 / turbo.rs:235-237: silu(gate) * up.
 __global__ void k_silu_mul(const float* __restrict__ gu, size_t ldgu, float* __restrict__ act, size_t ldact,
-                           int im) {
+                           int im, __half* __restrict__ act16) {
     const float* g = gu + (size_t)blockIdx.y * ldgu;
     float* a = act + (size_t)blockIdx.y * ldact;
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < im; i += gridDim.x * blockDim.x)
-        a[i] = __fmul_rn(silu_f(g[i]), g[im + i]);
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < im; i += gridDim.x * blockDim.x) {
+        float o = __fmul_rn(silu_f(g[i]), g[im + i]);
+        a[i] = o;
+        if (act16) act16[(size_t)blockIdx.y * im + perm_k(i)] = __float2half_rn(o);
+    }
 }
 
 int launch_silu_mul(const float* gu, size_t ldgu, float* act, size_t ldact, size_t rows, size_t im,
-                    cudaStream_t s) {
+                    cudaStream_t s, __half* act16) {
     if (rows == 0) return HC_OK;
     unsigned gx = (unsigned)std::min<size_t>((im + 255) / 256, 64);
-    k_silu_mul<<<dim3(gx, (unsigned)rows), 256, 0, s>>>(gu, ldgu, act, ldact, (int)im);
+    k_silu_mul<<<dim3(gx, (unsigned)rows), 256, 0, s>>>(gu, ldgu, act, ldact, (int)im, act16);
     HC_LAUNCH_CHECK();
     return HC_OK;
 }
@@ -523,9 +538,35 @@ __global__ void k_argmax(const float* __restrict__ logits, int n, uint32_t* __re
     const float* l = logits + (size_t)blockIdx.x * n;
     float best = -INFINITY;
     int bi = -1;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        float v = l[i];
-        if (bi < 0 || v >= best) { best = v; bi = i; }
+    // Each thread visits its indices in increasing order, so ">=" keeps its
+    // last maximum; the reductions below break ties toward the larger index.
+    if ((n & 3) == 0 && ((uintptr_t)l & 15) == 0) {
+        constexpr int U = 4;  // float4 loads in flight per thread
+        const float4* l4 = reinterpret_cast<const float4*>(l);
+        const int n4 = n >> 2;
+        for (int i0 = threadIdx.x; i0 < n4; i0 += U * blockDim.x) {
+            float4 v[U];
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                int i = i0 + u * blockDim.x;
+                if (i < n4) v[u] = __ldg(l4 + i);
+            }
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                int i = i0 + u * blockDim.x;
+                if (i < n4) {
+                    const float e[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+                    for (int c = 0; c < 4; c++)
+                        if (bi < 0 || e[c] >= best) { best = e[c]; bi = 4 * i + c; }
+                }
+            }
+        }
+    } else {
+        for (int i = threadIdx.x; i < n; i += blockDim.x) {
+            float v = l[i];
+            if (bi < 0 || v >= best) { best = v; bi = i; }
+        }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {

@@ -189,6 +189,8 @@ struct Scratch {
     uint64_t generation = 0;  // bumped whenever a buffer moves
     size_t cap_tokens = 0, cap_logit_rows = 0;
     float *hidden = nullptr, *xn = nullptr, *qkv = nullptr, *attn = nullptr, *gu = nullptr, *act = nullptr;
+    // fp16 copies in the tensor-core GEMM's K order, written by the producers
+    __half *xn16 = nullptr, *attn16 = nullptr, *act16 = nullptr;
     float* logits = nullptr;
     uint32_t* ids = nullptr;
     int* seqs = nullptr;
@@ -373,7 +375,8 @@ void free_model(hc_model* m) {
     if (m->stream) cudaStreamSynchronize(m->stream);
     for (void* p : m->allocs) cudaFree(p);
     void* scr[] = {m->sc.hidden, m->sc.xn, m->sc.qkv, m->sc.attn, m->sc.gu, m->sc.act, m->sc.logits, m->sc.ids,
-                   m->sc.seqs, m->sc.rowpos, m->sc.argmax, m->rope, m->sc.attn_ws};
+                   m->sc.seqs, m->sc.rowpos, m->sc.argmax, m->rope, m->sc.attn_ws, m->sc.xn16, m->sc.attn16,
+                   m->sc.act16};
     for (void* p : scr)
         if (p) cudaFree(p);
     if (m->gemm_ws) hc::gemm_workspace_free(m->gemm_ws);
@@ -400,6 +403,15 @@ int ensure_scratch(hc_model* m, size_t tokens, size_t logit_rows) {
         if (s.ids) cudaFree(s.ids);
         if (s.seqs) cudaFree(s.seqs);
         if (s.rowpos) cudaFree(s.rowpos);
+        {
+            __half** h16[] = {&s.xn16, &s.attn16, &s.act16};
+            size_t w16[] = {c.hidden_size, m->nq, m->layers.empty() ? 0 : m->layers[0].gu.n / 2};
+            for (int i = 0; i < 3; i++) {
+                if (*h16[i]) cudaFree(*h16[i]);
+                *h16[i] = nullptr;
+                HC_CUDA(cudaMalloc((void**)h16[i], std::max<size_t>(t * w16[i], 8) * sizeof(__half)));
+            }
+        }
         if (s.tp_tmp) cudaFree(s.tp_tmp);
         s.tp_tmp = nullptr;
         if (m->cfg.tp_size > 1) HC_CUDA(cudaMalloc((void**)&s.tp_tmp, t * c.hidden_size * sizeof(float)));
@@ -454,9 +466,9 @@ int ensure_attn_ws(hc_model* m, size_t rows, size_t nh, size_t max_pos, size_t n
 // y = W . x for `tokens` rows (the Q4_0 path picks the CUDA-core matvec for
 // few tokens and the tcgen05 GEMM otherwise).
 int matmul(hc_model* m, const DevWeight& w, const float* x, size_t ldx, size_t tokens, float* y, size_t ldy, int epi,
-           const float* res, size_t ldres) {
+           const float* res, size_t ldres, const __half* x16 = nullptr) {
     if (w.dtype == HC_DTYPE_Q4_0 && hc::gemm_tc_eligible(w.q4, tokens))
-        return hc::gemm_tc(m->gemm_ws, w.q4, x, ldx, tokens, y, ldy, epi, res, ldres, m->stream);
+        return hc::gemm_tc(m->gemm_ws, w.q4, x, ldx, tokens, y, ldy, epi, res, ldres, m->stream, x16);
     return hc::launch_matmul(w, x, ldx, tokens, y, ldy, epi, res, ldres, m->stream);
 }
 
@@ -469,12 +481,12 @@ __global__ void k_add_rows(float* __restrict__ y, const float* __restrict__ a, s
 // tensor-parallel ranks (o_proj, down_proj): each rank's partial product is
 // summed by an all-reduce, then added to the residual stream (the reference's
 // `hidden[i] = residual[i] + proj[i]`, transformer.rs:561-563, 595-598).
-int row_parallel(hc_model* m, const DevWeight& w, const float* x, size_t ldx, size_t rows) {
+int row_parallel(hc_model* m, const DevWeight& w, const float* x, size_t ldx, size_t rows, const __half* x16) {
     const size_t H = m->cfg.hidden_size;
     Scratch& s = m->sc;
-    if (m->cfg.tp_size <= 1) return matmul(m, w, x, ldx, rows, s.hidden, H, hc::EPI_ADD, s.hidden, H);
+    if (m->cfg.tp_size <= 1) return matmul(m, w, x, ldx, rows, s.hidden, H, hc::EPI_ADD, s.hidden, H, x16);
     HC_CHECK(m->comm, HC_ERR_STATE, "tensor-parallel model used before hc_comm_init");
-    HC_TRY(matmul(m, w, x, ldx, rows, s.tp_tmp, H, hc::EPI_STORE, nullptr, 0));
+    HC_TRY(matmul(m, w, x, ldx, rows, s.tp_tmp, H, hc::EPI_STORE, nullptr, 0, x16));
     HC_TRY(hc::comm_allreduce_sum(m->comm, s.tp_tmp, rows * H, m->stream));
     size_t n = rows * H;
     k_add_rows<<<(unsigned)((n + 255) / 256), 256, 0, m->stream>>>(s.hidden, s.tp_tmp, n);
@@ -493,18 +505,18 @@ __global__ void k_unshard_logits(const float* __restrict__ g, float* __restrict_
 
 // logits[rows][vocab] = W_lm x; with tensor parallelism each rank computes
 // its vocabulary slice and the slices are all-gathered.
-int lm_head_logits(hc_model* m, const float* x, size_t rows, float* logits) {
+int lm_head_logits(hc_model* m, const float* x, size_t rows, float* logits, const __half* x16 = nullptr) {
     const hc_config& c = m->cfg;
     if (!m->lm_head.present) {
         HC_CUDA(cudaMemsetAsync(logits, 0, rows * c.vocab_size * sizeof(float), m->stream));
         return HC_OK;
     }
     if (c.tp_size <= 1)
-        return matmul(m, m->lm_head, x, c.hidden_size, rows, logits, c.vocab_size, hc::EPI_STORE, nullptr, 0);
+        return matmul(m, m->lm_head, x, c.hidden_size, rows, logits, c.vocab_size, hc::EPI_STORE, nullptr, 0, x16);
     HC_CHECK(m->comm, HC_ERR_STATE, "tensor-parallel model used before hc_comm_init");
     const size_t vs = m->vocab_shard;
     float* mine = m->sc.tp_gather + (size_t)c.tp_rank * rows * vs;
-    HC_TRY(matmul(m, m->lm_head, x, c.hidden_size, rows, mine, vs, hc::EPI_STORE, nullptr, 0));
+    HC_TRY(matmul(m, m->lm_head, x, c.hidden_size, rows, mine, vs, hc::EPI_STORE, nullptr, 0, x16));
     HC_TRY(hc::comm_allgather(m->comm, mine, m->sc.tp_gather, rows * vs, m->stream));
     size_t n = rows * c.vocab_size;
     unsigned grid = (unsigned)std::min<size_t>((n + 255) / 256, 4096);
@@ -532,8 +544,8 @@ int run_layers(hc_model* m, hc_kv* kv, size_t rows, bool prefill, int seq, int p
     const float scale = 1.0f / sqrtf((float)hd);
     for (size_t li = 0; li < m->layers.size(); li++) {
         LayerW& L = m->layers[li];
-        HC_TRY(hc::launch_rmsnorm(s.hidden, H, L.in_norm, s.xn, H, rows, H, c.rms_norm_eps, m->stream));
-        HC_TRY(matmul(m, L.qkv, s.xn, H, rows, s.qkv, ldqkv, hc::EPI_STORE, nullptr, 0));
+        HC_TRY(hc::launch_rmsnorm(s.hidden, H, L.in_norm, s.xn, H, rows, H, c.rms_norm_eps, m->stream, s.xn16));
+        HC_TRY(matmul(m, L.qkv, s.xn, H, rows, s.qkv, ldqkv, hc::EPI_STORE, nullptr, 0, s.xn16));
         HC_TRY(hc::launch_rope_rows(s.qkv, ldqkv, rows, nh_l + nkv_l, hd, m->rope, m->rope_rows,
                                     prefill ? nullptr : s.rowpos, pos0, m->stream));
         size_t lofs = li * kv->layer_stride * (kv->kv_fp16 ? 2 : 4);
@@ -543,6 +555,7 @@ int run_layers(hc_model* m, hc_kv* kv, size_t rows, bool prefill, int seq, int p
                                    kv->kv_fp16, kv->seq_stride, kv->head_stride, kv->max_pos,
                                    prefill ? nullptr : s.seqs, kv->pos_dev, seq, pos0, m->stream));
         hc::AttnParams P{};
+        P.out16 = s.attn16;
         P.q = s.qkv;
         P.ldq = ldqkv;
         P.out = s.attn;
@@ -565,6 +578,7 @@ int run_layers(hc_model* m, hc_kv* kv, size_t rows, bool prefill, int seq, int p
                 HC_TRY(hc::launch_attention(P, (int)rows, 0, m->stream));
         } else if (hc::dattn_supported((int)nh_l, (int)nkv_l, (int)hd)) {
             hc::DecAttnParams D{};
+            D.out16 = s.attn16;
             D.q = s.qkv;
             D.ldq = ldqkv;
             D.out = s.attn;
@@ -582,14 +596,28 @@ int run_layers(hc_model* m, hc_kv* kv, size_t rows, bool prefill, int seq, int p
             D.seqs = s.seqs;
             D.pos = kv->pos_dev;
             D.max_pos = kv->max_pos;
+            // One CTA per (sequence, KV head) streams the whole context when
+            // that already fills most of the 2 x 148 CTA slots and its scores
+            // fit in shared memory; otherwise the context is split so that
+            // about one wave of CTAs runs.
             const int G = (int)(nh_l / nkv_l);
-            int max_chunk = (40960 - 8 * G * (int)hd) / G;
-            int want_splits = (int)std::max<size_t>(1, (296 + rows * nkv_l - 1) / (rows * nkv_l));
-            int chunk = std::max(256, (kv->max_pos + want_splits - 1) / want_splits);
-            chunk = std::min(chunk, max_chunk);
-            chunk = std::min(chunk, kv->max_pos);
-            D.chunk = chunk;
-            D.nsplit = (kv->max_pos + chunk - 1) / chunk;
+            const size_t ctas = rows * nkv_l, slots = 2 * 148;
+            const int red_floats = (hc::DA_REDUCE_WARPS + 1) * G * (int)hd;
+            const int smem_floats = 110 * 1024 / 4;
+            const bool whole = ctas * 4 >= slots * 3 || kv->max_pos <= 256;
+            if (whole && G * kv->max_pos + red_floats <= smem_floats) {
+                D.chunk = kv->max_pos;
+                D.nsplit = 1;
+            } else {
+                int max_chunk = std::max(64, (smem_floats - red_floats) / G);
+                int want_splits = (int)std::max<size_t>(1, (slots + ctas - 1) / ctas);
+                int chunk = std::max(256, (kv->max_pos + want_splits - 1) / want_splits);
+                chunk = std::min(chunk, max_chunk);
+                chunk = std::min(chunk, kv->max_pos);
+                D.chunk = chunk;
+                D.nsplit = (kv->max_pos + chunk - 1) / chunk;
+                if (D.nsplit == 1) D.chunk = kv->max_pos;
+            }
             HC_TRY(ensure_attn_ws(m, rows, nh_l, (size_t)kv->max_pos, (size_t)D.nsplit, hd));
             D.S = s.attn_ws;
             D.smax = D.S + rows * nh_l * (size_t)kv->max_pos;
@@ -607,12 +635,12 @@ int run_layers(hc_model* m, hc_kv* kv, size_t rows, bool prefill, int seq, int p
             P.pos = kv->pos_dev;
             HC_TRY(hc::launch_attention(P, (int)rows, kv->kv_fp16, m->stream));
         }
-        HC_TRY(row_parallel(m, L.o, s.attn, nq, rows));
-        HC_TRY(hc::launch_rmsnorm(s.hidden, H, L.post_norm, s.xn, H, rows, H, c.rms_norm_eps, m->stream));
+        HC_TRY(row_parallel(m, L.o, s.attn, nq, rows, s.attn16));
+        HC_TRY(hc::launch_rmsnorm(s.hidden, H, L.post_norm, s.xn, H, rows, H, c.rms_norm_eps, m->stream, s.xn16));
         size_t im = L.gu.n / 2;
-        HC_TRY(matmul(m, L.gu, s.xn, H, rows, s.gu, 2 * im, hc::EPI_STORE, nullptr, 0));
-        HC_TRY(hc::launch_silu_mul(s.gu, 2 * im, s.act, im, rows, im, m->stream));
-        HC_TRY(row_parallel(m, L.down, s.act, im, rows));
+        HC_TRY(matmul(m, L.gu, s.xn, H, rows, s.gu, 2 * im, hc::EPI_STORE, nullptr, 0, s.xn16));
+        HC_TRY(hc::launch_silu_mul(s.gu, 2 * im, s.act, im, rows, im, m->stream, s.act16));
+        HC_TRY(row_parallel(m, L.down, s.act, im, rows, s.act16));
     }
     return HC_OK;
 }
@@ -636,9 +664,9 @@ int decode_dev_impl(hc_model* m, hc_kv* kv, const int* seqs_dev, const uint32_t*
     HC_TRY(run_layers(m, kv, (size_t)B, false, 0, 0));
     HC_TRY(hc::launch_advance(s.seqs, kv->pos_dev, B, m->stream));
     HC_TRY(hc::launch_rmsnorm(s.hidden, c.hidden_size, m->final_norm, s.xn, c.hidden_size, (size_t)B, c.hidden_size,
-                              c.rms_norm_eps, m->stream));
+                              c.rms_norm_eps, m->stream, s.xn16));
     float* logits = logits_dev ? logits_dev : s.logits;
-    HC_TRY(lm_head_logits(m, s.xn, (size_t)B, logits));
+    HC_TRY(lm_head_logits(m, s.xn, (size_t)B, logits, s.xn16));
     if (argmax_dev) HC_TRY(hc::launch_argmax(logits, (size_t)B, c.vocab_size, argmax_dev, m->stream));
     return HC_OK;
 }
