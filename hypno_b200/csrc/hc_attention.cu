@@ -28,6 +28,7 @@ __device__ __forceinline__ float ldkv<__half>(const __half* p) { return __half2f
 // One CTA (4 warps) per (query row, query head).
 template <typename KT>
 __global__ void __launch_bounds__(128) k_attention(AttnParams P) {
+    pdl_trigger();
     extern __shared__ float smem[];
     const int row = blockIdx.x, h = blockIdx.y;
     const int hd = P.hd;
@@ -205,9 +206,11 @@ constexpr int DA_MAXG = 8;
 
 // Lane-group mapping for one (sequence, KV head): LPP lanes share a K or V
 // row, each lane owning EPL consecutive elements of it (32 bytes, 16 bytes for
-// groups of 4 or more heads), so a warp reads whole rows with coalesced 16-byte loads
-// and keeps its slice of the G query vectors in registers.  U row groups are
-// loaded before any arithmetic to keep enough bytes in flight.
+// groups of 4 or more heads), so a warp reads whole rows with coalesced
+// 16-byte loads and keeps its slice of the G query vectors in registers.  U
+// row groups are loaded before any arithmetic to keep enough bytes in flight.
+// Scores and weights are stored position-major, [p][G], so the weighted-V
+// pass reads a row's G weights with one vector load.
 template <typename KT, int G, int HD>
 struct DA {
     static constexpr int BPL = (G <= 2) ? 32 : 16;                  // bytes per lane per row
@@ -216,41 +219,70 @@ struct DA {
     static constexpr int PPW = 32 / LPP;                            // rows per warp per step
     static constexpr int NV = BPL / 16;                             // 16-byte loads per lane per row
     static constexpr int U = (BPL == 16 && G < 8) ? 8 : 4;          // row groups in flight
+    // G <= LPP: the G partial dots of a row are reduce-scattered over the
+    // lane group (lane sub ends with head sub / (LPP / G)); otherwise every
+    // head is all-reduced.
+    static constexpr bool SCATTER = G > 1 && G <= LPP;
+    static constexpr int GSPAN = SCATTER ? LPP / G : LPP;           // lanes sharing one head's sum
     static_assert(LPP >= 1 && LPP <= 32 && (LPP & (LPP - 1)) == 0, "head_dim / lane mapping");
+    static_assert(EPL % 2 == 0, "pairs of elements");
 };
 
+// 16-byte chunks of fp16 or f32 elements -> pairs of f32
 template <typename KT, int EPL>
-__device__ __forceinline__ void cvt_elems(const uint4* raw, float* out) {
+__device__ __forceinline__ void cvt_pairs(const uint4* raw, float2* out) {
     if constexpr (sizeof(KT) == 2) {
 #pragma unroll
         for (int v = 0; v < EPL / 8; v++) {
             const __half2* h2 = reinterpret_cast<const __half2*>(&raw[v]);
 #pragma unroll
-            for (int i = 0; i < 4; i++) {
-                float2 f = __half22float2(h2[i]);
-                out[v * 8 + 2 * i] = f.x;
-                out[v * 8 + 2 * i + 1] = f.y;
-            }
+            for (int i = 0; i < 4; i++) out[v * 4 + i] = __half22float2(h2[i]);
         }
     } else {
 #pragma unroll
         for (int v = 0; v < EPL / 4; v++) {
-            const float* f = reinterpret_cast<const float*>(&raw[v]);
-#pragma unroll
-            for (int i = 0; i < 4; i++) out[v * 4 + i] = f[i];
+            const float2* f = reinterpret_cast<const float2*>(&raw[v]);
+            out[v * 2] = f[0];
+            out[v * 2 + 1] = f[1];
         }
     }
 }
 
-// Scores of positions [p0, p1) written to S[g * ldS + (p - sbase)]; mx gets
-// each head's maximum over the positions this lane wrote.
+// Reduce-scatter of v[0..C) over the lanes of a group (offsets OFF, OFF/2,
+// ..): at each level a lane keeps the half of its values selected by its
+// lane bit and adds the partner's copy of that half; once one value is left
+// the remaining levels all-reduce it.
+template <int C, int OFF>
+struct Scatter {
+    static __device__ __forceinline__ void run(float* v, int sub) {
+        if constexpr (C > 1) {
+            constexpr int H = C / 2;
+            const bool up = (sub & OFF) != 0;
+#pragma unroll
+            for (int i = 0; i < H; i++) {
+                const float send = up ? v[i] : v[H + i];
+                const float keep = up ? v[H + i] : v[i];
+                v[i] = keep + __shfl_xor_sync(0xffffffffu, send, OFF);
+            }
+            Scatter<H, OFF / 2>::run(v, sub);
+        } else if constexpr (OFF > 0) {
+            v[0] += __shfl_xor_sync(0xffffffffu, v[0], OFF);
+            Scatter<1, OFF / 2>::run(v, sub);
+        }
+    }
+};
+
+// Scores of positions [p0, p1) written to S[(p - sbase) * G + g]; mx gets
+// the maximum of the scores this lane wrote (head g_own of the lane when
+// scattering, every head otherwise).
 template <typename KT, int G, int HD>
-__device__ __forceinline__ void da_scores(const KT* __restrict__ kbase, const float (&qr)[G][DA<KT, G, HD>::EPL],
-                                          int p0, int p1, float scale, float* S, size_t ldS, int sbase,
-                                          float (&mx)[G]) {
+__device__ __forceinline__ void da_scores(const KT* __restrict__ kbase, const float2 (&qr)[G][DA<KT, G, HD>::EPL / 2],
+                                          int p0, int p1, float scale, float* S, int sbase, float (&mx)[G]) {
     using C = DA<KT, G, HD>;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int slot = lane / C::LPP, sub = lane % C::LPP;
+    const int g_own = sub / C::GSPAN;
+    const bool writer = (sub % C::GSPAN) == 0;
     constexpr int STEP = C::U * C::PPW;
     for (int c0 = p0 + warp * STEP; c0 < p1; c0 += DA_WARPS * STEP) {
         uint4 raw[C::U][C::NV];
@@ -263,35 +295,62 @@ __device__ __forceinline__ void da_scores(const KT* __restrict__ kbase, const fl
         }
 #pragma unroll
         for (int u = 0; u < C::U; u++) {
-            float k[C::EPL];
-            cvt_elems<KT, C::EPL>(raw[u], k);
+            float2 k[C::EPL / 2];
+            cvt_pairs<KT, C::EPL>(raw[u], k);
             float acc[G];
 #pragma unroll
             for (int g = 0; g < G; g++) {
-                acc[g] = 0.0f;
+                float2 a2 = make_float2(0.0f, 0.0f);
 #pragma unroll
-                for (int e = 0; e < C::EPL; e++) acc[g] = fmaf(qr[g][e], k[e], acc[g]);
-#pragma unroll
-                for (int off = C::LPP / 2; off > 0; off >>= 1) acc[g] += __shfl_xor_sync(0xffffffffu, acc[g], off);
+                for (int e = 0; e < C::EPL / 2; e++) a2 = __ffma2_rn(qr[g][e], k[e], a2);
+                acc[g] = a2.x + a2.y;
             }
-            int p = c0 + u * C::PPW + slot;
-            if (sub == 0 && p < p1) {
+            const int p = c0 + u * C::PPW + slot;
+            if constexpr (C::SCATTER) {
+                Scatter<G, C::LPP / 2>::run(acc, sub);
+                if (writer && p < p1) {
+                    float sc = __fmul_rn(acc[0], scale);
+                    S[(size_t)(p - sbase) * G + g_own] = sc;
+                    mx[0] = fmaxf(mx[0], sc);
+                }
+            } else {
 #pragma unroll
-                for (int g = 0; g < G; g++) {
-                    float sc = __fmul_rn(acc[g], scale);
-                    S[(size_t)g * ldS + (p - sbase)] = sc;
-                    mx[g] = fmaxf(mx[g], sc);
+                for (int g = 0; g < G; g++) Scatter<1, C::LPP / 2>::run(&acc[g], sub);
+                if (sub == 0 && p < p1) {
+#pragma unroll
+                    for (int g = 0; g < G; g++) {
+                        float sc = __fmul_rn(acc[g], scale);
+                        S[(size_t)(p - sbase) * G + g] = sc;
+                        mx[g] = fmaxf(mx[g], sc);
+                    }
                 }
             }
         }
     }
 }
 
-// o[g][e] += sum over positions [p0, p1) of W[g * ldW + (p - wbase)] * V[p][d0 + e]
+// The G weights of row p: W[(p - wbase) * G .. + G)
+template <int G>
+__device__ __forceinline__ void load_w(const float* W, int idx, float (&w)[G]) {
+    if constexpr (G % 4 == 0) {
+#pragma unroll
+        for (int i = 0; i < G / 4; i++) {
+            float4 f = reinterpret_cast<const float4*>(W + (size_t)idx * G)[i];
+            w[4 * i] = f.x; w[4 * i + 1] = f.y; w[4 * i + 2] = f.z; w[4 * i + 3] = f.w;
+        }
+    } else if constexpr (G == 2) {
+        float2 f = reinterpret_cast<const float2*>(W)[idx];
+        w[0] = f.x; w[1] = f.y;
+    } else {
+        w[0] = W[idx];
+    }
+}
+
+// o[g][e] += sum over positions [p0, p1) of W[(p - wbase) * G + g] * V[p][d0 + e]
 // for this lane's slot and slice (not yet reduced across slots or warps).
 template <typename KT, int G, int HD>
-__device__ __forceinline__ void da_pv(const KT* __restrict__ vbase, const float* W, size_t ldW, int wbase, int p0,
-                                      int p1, float (&o)[G][DA<KT, G, HD>::EPL]) {
+__device__ __forceinline__ void da_pv(const KT* __restrict__ vbase, const float* W, int wbase, int p0, int p1,
+                                      float2 (&o)[G][DA<KT, G, HD>::EPL / 2]) {
     using C = DA<KT, G, HD>;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int slot = lane / C::LPP, sub = lane % C::LPP;
@@ -309,37 +368,44 @@ __device__ __forceinline__ void da_pv(const KT* __restrict__ vbase, const float*
         for (int u = 0; u < C::U; u++) {
             int p = c0 + u * C::PPW + slot;
             if (p >= p1) continue;
-            float v[C::EPL];
-            cvt_elems<KT, C::EPL>(raw[u], v);
+            float2 v2[C::EPL / 2];
+            cvt_pairs<KT, C::EPL>(raw[u], v2);
+            float w[G];
+            load_w<G>(W, p - wbase, w);
 #pragma unroll
             for (int g = 0; g < G; g++) {
-                float w = W[(size_t)g * ldW + (p - wbase)];
+                const float2 w2 = make_float2(w[g], w[g]);
 #pragma unroll
-                for (int e = 0; e < C::EPL; e++) o[g][e] = fmaf(w, v[e], o[g][e]);
+                for (int e = 0; e < C::EPL / 2; e++) o[g][e] = __ffma2_rn(w2, v2[e], o[g][e]);
             }
         }
     }
 }
 
 // Sum o over the slots of a warp and over the warps; the result for head g,
-// feature d lands in red[g * HD + d] (red holds DA_WARPS * G * HD floats).
+// feature d lands in red[DA_WARPS * G * HD + g * HD + d] (red holds
+// (DA_WARPS + 1) * G * HD floats).
 template <typename KT, int G, int HD>
-__device__ __forceinline__ void da_reduce_o(float (&o)[G][DA<KT, G, HD>::EPL], float* red) {
+__device__ __forceinline__ void da_reduce_o(float2 (&o)[G][DA<KT, G, HD>::EPL / 2], float* red) {
     using C = DA<KT, G, HD>;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int sub = lane % C::LPP;
 #pragma unroll
     for (int g = 0; g < G; g++)
 #pragma unroll
-        for (int e = 0; e < C::EPL; e++)
+        for (int e = 0; e < C::EPL / 2; e++)
 #pragma unroll
-            for (int off = C::LPP; off < 32; off <<= 1) o[g][e] += __shfl_xor_sync(0xffffffffu, o[g][e], off);
+            for (int off = C::LPP; off < 32; off <<= 1) {
+                o[g][e].x += __shfl_xor_sync(0xffffffffu, o[g][e].x, off);
+                o[g][e].y += __shfl_xor_sync(0xffffffffu, o[g][e].y, off);
+            }
     __syncthreads();
     if (lane < C::LPP) {
 #pragma unroll
         for (int g = 0; g < G; g++)
 #pragma unroll
-            for (int e = 0; e < C::EPL; e++) red[((size_t)warp * G + g) * HD + sub * C::EPL + e] = o[g][e];
+            for (int e = 0; e < C::EPL / 2; e++)
+                reinterpret_cast<float2*>(red + ((size_t)warp * G + g) * HD + sub * C::EPL)[e] = o[g][e];
     }
     __syncthreads();
     for (int i = threadIdx.x; i < G * HD; i += DA_THREADS) {
@@ -353,14 +419,16 @@ __device__ __forceinline__ void da_reduce_o(float (&o)[G][DA<KT, G, HD>::EPL], f
 
 template <typename KT, int G, int HD>
 __device__ __forceinline__ void da_load_q(const DecAttnParams& P, int row, int kvh,
-                                          float (&qr)[G][DA<KT, G, HD>::EPL]) {
+                                          float2 (&qr)[G][DA<KT, G, HD>::EPL / 2]) {
     using C = DA<KT, G, HD>;
     const int sub = (threadIdx.x & 31) % C::LPP;
 #pragma unroll
-    for (int g = 0; g < G; g++)
+    for (int g = 0; g < G; g++) {
+        const float2* q2 =
+            reinterpret_cast<const float2*>(P.q + (size_t)row * P.ldq + (size_t)(kvh * G + g) * HD + sub * C::EPL);
 #pragma unroll
-        for (int e = 0; e < C::EPL; e++)
-            qr[g][e] = P.q[(size_t)row * P.ldq + (size_t)(kvh * G + g) * HD + sub * C::EPL + e];
+        for (int e = 0; e < C::EPL / 2; e++) qr[g][e] = q2[e];
+    }
 }
 
 __device__ __forceinline__ void da_write_out(const DecAttnParams& P, int row, int h, int d, float v) {
@@ -368,10 +436,30 @@ __device__ __forceinline__ void da_write_out(const DecAttnParams& P, int row, in
     if (P.out16) P.out16[(size_t)row * P.nh * P.hd + perm_k(h * P.hd + d)] = __float2half_rn(v);
 }
 
+// Block maxima per head of the lanes' maxima (one head per lane when the
+// scores were scattered).
+template <typename KT, int G, int HD>
+__device__ __forceinline__ void da_head_max(const float (&mx)[G], float (&gmax)[G], float* redv) {
+    using C = DA<KT, G, HD>;
+    if constexpr (C::SCATTER) {
+        const int g_own = ((threadIdx.x & 31) % C::LPP) / C::GSPAN;
+#pragma unroll
+        for (int g = 0; g < G; g++) gmax[g] = block_max(g_own == g ? mx[0] : -INFINITY, redv);
+    } else {
+#pragma unroll
+        for (int g = 0; g < G; g++) gmax[g] = block_max(mx[g], redv);
+    }
+}
+
+// Floats before the reduction buffer that follows n score floats (kept a
+// multiple of 4 so the buffer's vector accesses stay aligned).
+__host__ __device__ __forceinline__ size_t red_offset(int n) { return ((size_t)n + 3) & ~(size_t)3; }
+
 // Whole context in one CTA per (sequence, KV head): scores kept in shared
 // memory, then weights, then P.V; K and V are each read once.
 template <typename KT, int G, int HD>
 __global__ void __launch_bounds__(DA_THREADS, 2) k_dattn_fused(DecAttnParams P) {
+    pdl_trigger();
     using C = DA<KT, G, HD>;
     extern __shared__ float smem[];
     __shared__ float redv[32];
@@ -383,20 +471,19 @@ __global__ void __launch_bounds__(DA_THREADS, 2) k_dattn_fused(DecAttnParams P) 
             da_write_out(P, row, kvh * G + i / HD, i % HD, P.vself[(size_t)row * P.ldself + (size_t)kvh * HD + i % HD]);
         return;
     }
-    float* S = smem;                        // [G][max_pos]
-    float* red = smem + (size_t)G * P.max_pos;  // [(DA_WARPS + 1) * G * HD]
+    float* S = smem;                                // [max_pos][G]
+    float* red = smem + red_offset(G * P.max_pos);  // [(DA_WARPS + 1) * G * HD], 16-byte aligned
     const size_t off = (size_t)seq * P.seq_stride + (size_t)kvh * P.head_stride;
     const KT* kbase = reinterpret_cast<const KT*>(P.kc) + off;
     const KT* vbase = reinterpret_cast<const KT*>(P.vc) + off;
-    float qr[G][C::EPL];
+    float2 qr[G][C::EPL / 2];
     da_load_q<KT, G, HD>(P, row, kvh, qr);
     float mx[G];
 #pragma unroll
     for (int g = 0; g < G; g++) mx[g] = -INFINITY;
-    da_scores<KT, G, HD>(kbase, qr, 0, n, P.scale, S, (size_t)P.max_pos, 0, mx);
+    da_scores<KT, G, HD>(kbase, qr, 0, n, P.scale, S, 0, mx);
     float gmax[G];
-#pragma unroll
-    for (int g = 0; g < G; g++) gmax[g] = block_max(mx[g], redv);  // also orders the S writes
+    da_head_max<KT, G, HD>(mx, gmax, redv);  // also orders the S writes
     const int n8 = n - (n % 8);
     float lsum[G];
 #pragma unroll
@@ -404,20 +491,20 @@ __global__ void __launch_bounds__(DA_THREADS, 2) k_dattn_fused(DecAttnParams P) 
     for (int p = threadIdx.x; p < n; p += DA_THREADS) {
 #pragma unroll
         for (int g = 0; g < G; g++) {
-            float e = softmax_weight(S[(size_t)g * P.max_pos + p], gmax[g], p, n8);
-            S[(size_t)g * P.max_pos + p] = e;
+            float e = softmax_weight(S[(size_t)p * G + g], gmax[g], p, n8);
+            S[(size_t)p * G + g] = e;
             lsum[g] += e;
         }
     }
     float total[G];
 #pragma unroll
     for (int g = 0; g < G; g++) total[g] = block_sum(lsum[g], redv);  // also orders the weight writes
-    float o[G][C::EPL];
+    float2 o[G][C::EPL / 2];
 #pragma unroll
     for (int g = 0; g < G; g++)
 #pragma unroll
-        for (int e = 0; e < C::EPL; e++) o[g][e] = 0.0f;
-    da_pv<KT, G, HD>(vbase, S, (size_t)P.max_pos, 0, 0, n, o);
+        for (int e = 0; e < C::EPL / 2; e++) o[g][e] = make_float2(0.0f, 0.0f);
+    da_pv<KT, G, HD>(vbase, S, 0, 0, n, o);
     da_reduce_o<KT, G, HD>(o, red);
     const float* fin = red + (size_t)DA_WARPS * G * HD;
     for (int i = threadIdx.x; i < G * HD; i += DA_THREADS) {
@@ -437,17 +524,19 @@ __global__ void __launch_bounds__(DA_THREADS, 2) k_dattn_scores(DecAttnParams P)
     const int p0 = split * P.chunk, p1 = min(n, p0 + P.chunk);
     if (n <= 1) return;
     const KT* kbase = reinterpret_cast<const KT*>(P.kc) + (size_t)seq * P.seq_stride + (size_t)kvh * P.head_stride;
-    float qr[G][C::EPL];
+    float2 qr[G][C::EPL / 2];
     da_load_q<KT, G, HD>(P, row, kvh, qr);
     float mx[G];
 #pragma unroll
     for (int g = 0; g < G; g++) mx[g] = -INFINITY;
-    float* S = P.S + ((size_t)row * P.nh + kvh * G) * P.max_pos;
-    da_scores<KT, G, HD>(kbase, qr, p0, p1, P.scale, S, (size_t)P.max_pos, 0, mx);
+    float* S = P.S + ((size_t)row * P.nh + kvh * G) * P.max_pos;  // [max_pos][G] of this (row, kv head)
+    da_scores<KT, G, HD>(kbase, qr, p0, p1, P.scale, S, 0, mx);
+    float gmax[G];
+    da_head_max<KT, G, HD>(mx, gmax, redv);
+    if (threadIdx.x < G) {
 #pragma unroll
-    for (int g = 0; g < G; g++) {
-        float m = block_max(mx[g], redv);
-        if (threadIdx.x == 0) P.smax[((size_t)row * P.nh + kvh * G + g) * P.nsplit + split] = m;
+        for (int g = 0; g < G; g++)
+            if (threadIdx.x == g) P.smax[((size_t)row * P.nh + kvh * G + g) * P.nsplit + split] = gmax[g];
     }
 }
 
@@ -455,7 +544,7 @@ __global__ void __launch_bounds__(DA_THREADS, 2) k_dattn_scores(DecAttnParams P)
 template <typename KT, int G, int HD>
 __global__ void __launch_bounds__(DA_THREADS, 2) k_dattn_pv(DecAttnParams P) {
     using C = DA<KT, G, HD>;
-    extern __shared__ float smem[];  // [G][chunk] weights, then the reduction buffer
+    extern __shared__ float smem[];  // [chunk][G] weights, then the reduction buffer
     __shared__ float redv[32];
     __shared__ float gmax[DA_MAXG];
     const int row = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
@@ -479,7 +568,7 @@ __global__ void __launch_bounds__(DA_THREADS, 2) k_dattn_pv(DecAttnParams P) {
     }
     __syncthreads();
     float* W = smem;
-    float* red = smem + (size_t)G * P.chunk;
+    float* red = smem + red_offset(G * P.chunk);
     const int n8 = n - (n % 8);
     const float* Sg = P.S + ((size_t)row * P.nh + kvh * G) * P.max_pos;
     float lsum[G];
@@ -488,8 +577,8 @@ __global__ void __launch_bounds__(DA_THREADS, 2) k_dattn_pv(DecAttnParams P) {
     for (int i = threadIdx.x; i < len; i += DA_THREADS) {
 #pragma unroll
         for (int g = 0; g < G; g++) {
-            float e = softmax_weight(Sg[(size_t)g * P.max_pos + p0 + i], gmax[g], p0 + i, n8);
-            W[(size_t)g * P.chunk + i] = e;
+            float e = softmax_weight(Sg[(size_t)(p0 + i) * G + g], gmax[g], p0 + i, n8);
+            W[(size_t)i * G + g] = e;
             lsum[g] += e;
         }
     }
@@ -497,12 +586,12 @@ __global__ void __launch_bounds__(DA_THREADS, 2) k_dattn_pv(DecAttnParams P) {
 #pragma unroll
     for (int g = 0; g < G; g++) total[g] = block_sum(lsum[g], redv);
     const KT* vbase = reinterpret_cast<const KT*>(P.vc) + (size_t)seq * P.seq_stride + (size_t)kvh * P.head_stride;
-    float o[G][C::EPL];
+    float2 o[G][C::EPL / 2];
 #pragma unroll
     for (int g = 0; g < G; g++)
 #pragma unroll
-        for (int e = 0; e < C::EPL; e++) o[g][e] = 0.0f;
-    da_pv<KT, G, HD>(vbase, W, (size_t)P.chunk, p0, p0, p1, o);
+        for (int e = 0; e < C::EPL / 2; e++) o[g][e] = make_float2(0.0f, 0.0f);
+    da_pv<KT, G, HD>(vbase, W, p0, p0, p1, o);
     da_reduce_o<KT, G, HD>(o, red);
     const float* fin = red + (size_t)DA_WARPS * G * HD;
     for (int i = threadIdx.x; i < G * HD; i += DA_THREADS) {
@@ -519,6 +608,7 @@ __global__ void __launch_bounds__(DA_THREADS, 2) k_dattn_pv(DecAttnParams P) {
 
 // Split path, pass 3: out = sum of partial P.V / sum of partial weights.
 __global__ void k_dattn_combine(DecAttnParams P) {
+    pdl_trigger();
     const int row = blockIdx.x, h = blockIdx.y;
     const int seq = P.seqs[row];
     const int n = min(P.pos[seq], P.max_pos);
@@ -539,7 +629,7 @@ template <typename KT, int G, int HD>
 int launch_dattn_ghd(const DecAttnParams& P, int rows, cudaStream_t s) {
     const size_t red_floats = (size_t)(DA_WARPS + 1) * G * HD;
     if (P.nsplit == 1) {
-        size_t smem = ((size_t)G * P.max_pos + red_floats) * sizeof(float);
+        size_t smem = (red_offset(G * P.max_pos) + red_floats) * sizeof(float);
         HC_CHECK(smem <= 220 * 1024, HC_ERR_UNSUPPORTED, "decode attention: context %d too long for one split",
                  P.max_pos);
         if (smem > 48 * 1024)
@@ -552,7 +642,7 @@ int launch_dattn_ghd(const DecAttnParams& P, int rows, cudaStream_t s) {
     dim3 grid((unsigned)rows, (unsigned)P.nkv, (unsigned)P.nsplit);
     k_dattn_scores<KT, G, HD><<<grid, DA_THREADS, 0, s>>>(P);
     HC_LAUNCH_CHECK();
-    size_t smem2 = ((size_t)G * P.chunk + red_floats) * sizeof(float);
+    size_t smem2 = (red_offset(G * P.chunk) + red_floats) * sizeof(float);
     if (smem2 > 48 * 1024)
         HC_CUDA(cudaFuncSetAttribute(k_dattn_pv<KT, G, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2));
     k_dattn_pv<KT, G, HD><<<grid, DA_THREADS, smem2, s>>>(P);
@@ -615,6 +705,7 @@ constexpr int PA_BQ = 64, PA_BK = 64, PA_THREADS = 256, PA_KT_STRIDE = PA_BK + 4
 
 template <int HD>
 __global__ void __launch_bounds__(PA_THREADS) k_pattn(AttnParams P, int T) {
+    pdl_trigger();
     extern __shared__ float sm[];
     float* Qt = sm;                          // [HD][BQ]
     float* Kt = Qt + HD * PA_BQ;             // [HD][BK + 4]   (also V tile [BK][HD])

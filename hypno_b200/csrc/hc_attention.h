@@ -55,7 +55,7 @@ struct DecAttnParams {
     int max_pos;
     int chunk;            // positions per split
     int nsplit;           // splits launched (>= ceil(max n / chunk))
-    float* S;             // scores [rows][nh][max_pos]
+    float* S;             // scores [rows][nkv][max_pos][G] (G = nh / nkv)
     float* smax;          // [rows][nh][nsplit]
     float* opart;         // [rows][nh][nsplit][hd]
     float* spart;         // [rows][nh][nsplit]

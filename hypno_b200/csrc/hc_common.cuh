@@ -21,6 +21,61 @@ __device__ __forceinline__ float warp_max(float v) {
 
 // Block-wide sum for blockDim.x a multiple of 32 and <= 1024.  `red` holds
 // 32 floats of shared memory.  Every thread receives the total.
+// ---- mbarrier helpers (shared memory, CTA scope) for the TMA pipelines
+
+constexpr long long WAIT_CYCLES = 4000000000LL;  // bound of every pipeline wait, ~2 s at 1.9 GHz
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait on the phase with the given parity.  Returns false when the
+// deadline passes or another role already reported a failure.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+    long long start = clock64();
+    for (uint32_t i = 0;; i++) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 255) == 255) {
+            if (*abort_flag) return false;
+            if (clock64() - start > WAIT_CYCLES) {
+                *abort_flag = 1;
+                return false;
+            }
+        }
+    }
+}
+
+// Programmatic dependent launch: lets the next kernel in the stream, when it
+// is launched as a programmatic dependent (the tensor-core GEMM), start its
+// prologue and weight prefetch now; it waits for this grid's completion
+// before it touches anything this grid writes.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ float block_sum(float v, float* red) {
     int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     v = warp_sum(v);

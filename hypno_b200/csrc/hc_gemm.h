@@ -26,6 +26,11 @@ __host__ __device__ inline int perm_k(int e) { return (e & ~7) | ((e & 3) << 1) 
 // (synchronizes the device); HC_ERR_TIMEOUT when a kernel aborted.
 int gemm_check(GemmWorkspace* ws);
 
+// The workspace's device error flag (allocated on first use; null when that
+// fails): other pipelined kernels report expired waits through it too, so
+// gemm_check covers them.
+int* gemm_error_flag(GemmWorkspace* ws);
+
 // Changes whenever a workspace buffer captured by earlier launches moved
 // (captured CUDA graphs must then be rebuilt).
 uint64_t gemm_generation(GemmWorkspace* ws);

@@ -42,53 +42,6 @@ namespace {
 
 constexpr int BM = 128;      // weight rows per tile (MMA M)
 constexpr int BK = 128;      // K per pipeline stage
-constexpr long long WAIT_CYCLES = 4000000000LL;  // ~2 s at 1.9 GHz
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-    return (uint32_t)__cvta_generic_to_shared(p);
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-                 : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-
-// Bounded wait on the phase with the given parity.  Returns false when the
-// deadline passes or another role already reported a failure.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
-    long long start = clock64();
-    for (uint32_t i = 0;; i++) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 255) == 255) {
-            if (*abort_flag) return false;
-            if (clock64() - start > WAIT_CYCLES) {
-                *abort_flag = 1;
-                return false;
-            }
-        }
-    }
-}
-
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
@@ -111,33 +64,12 @@ __device__ __forceinline__ void tmem_st_x32(uint32_t taddr, const uint32_t* v) {
         : "memory");
 }
 
-__device__ __forceinline__ void tmem_st_x16(uint32_t taddr, const uint32_t* v) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-        "%15, %16};" ::"r"(taddr),
-        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
-        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
-        : "memory");
-}
-
 __device__ __forceinline__ void tmem_ld_x16(uint32_t taddr, uint32_t* v) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
         "%15}, [%16];"
         : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
           "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
-        : "r"(taddr)
-        : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld_x32(uint32_t taddr, uint32_t* v) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
-          "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
-          "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
-          "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
         : "r"(taddr)
         : "memory");
 }
@@ -180,6 +112,11 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
 
 constexpr int EPI_CH = 16;     // tokens per epilogue chunk (one tcgen05.ld x16)
 constexpr int MAX_SPLITS = 8;  // split-K cluster size limit (portable cluster size)
+
+// Programmatic dependent launch: wait until the grids this one depends on
+// have completed and their writes are visible (returns at once when the
+// kernel was launched without the attribute).
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 __device__ __forceinline__ void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
@@ -276,7 +213,7 @@ struct Cfg {
     __host__ __device__ static constexpr int smem() { return bar_off() + (2 * S_SM + 2 * S_TM + 1) * 8 + 16 + 1024; }
     static_assert(A_COL + 64 * S_TM <= COLS, "tensor memory budget");
     static_assert(RR <= S_TM && RR <= S_SM, "dequant groups must not run more than one barrier phase apart");
-    static_assert(WG_PER >= 1 && 4 % WG_PER == 0, "dequant split");
+    static_assert(WG_PER == 1 || WG_PER == 2, "dequant split: 4 or 2 blocks per warpgroup");
     static_assert(!DUAL || 2 * (smem() + 1024) <= 233472, "two CTAs must fit in one SM's shared memory");
     static constexpr int RED_PITCH = TN + 1;                  // floats per row of the split-K partial tile
     static_assert(BM * RED_PITCH * 4 <= S_SM * (X_STAGE + W_STAGE), "partial tile fits in the TMA stages");
@@ -336,8 +273,24 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
     // observes (see the dequant note), which is what parity waits require.
     if (warp == 0) {
         // ---------------- TMA producer
+        // The weight tiles of the first ring round do not depend on the
+        // previous kernel, so they are requested before the grid-dependency
+        // wait (launched as a programmatic dependent, this CTA may start while
+        // the kernel producing X is still running); X follows the wait.
         if (lane == 0) {
-            for (int j = 0; j < nk; j++) {
+            const int pre = nk < S_SM ? nk : S_SM;
+            for (int j = 0; j < pre; j++) {  // fresh ring: no sempty wait needed
+                mbar_expect_tx(&full[j], (uint32_t)(C::X_STAGE + C::W_STAGE));
+                tma_load_2d(smem + C::w_off(j), &wmap, &full[j], (it0 + j) * BK / 2, n0);
+            }
+            grid_dependency_wait();
+            for (int j = 0; j < pre; j++) {
+                uint8_t* xs = smem + C::x_off(j);
+                int kk = (it0 + j) * BK;
+                tma_load_2d(xs, &xmap, &full[j], kk, t0);
+                tma_load_2d(xs + TN * 128, &xmap, &full[j], kk + 64, t0);
+            }
+            for (int j = pre; j < nk; j++) {
                 const int st = j % S_SM;
                 const uint32_t ph = (uint32_t)(j / S_SM) & 1u;
                 if (!mbar_wait(&sempty[st], ph ^ 1u, &abort_flag)) break;
@@ -419,10 +372,10 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
             const uint8_t* wrow = smem + C::w_off(st) + r * (BK / 2);
             const int sw = (r >> 1) & 3;
             const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(C::A_COL + a * 64);
-            // Q4_0 blocks [blk0, blk0 + BLK_PER) of the stage, two per TMEM
-            // store (one when a warpgroup converts a single block)
+            // Q4_0 blocks [blk0, blk0 + BLK_PER) of the stage, two per TMEM store
             constexpr int BLK_PER = 4 / C::WG_PER;
-            constexpr int PER_ST = BLK_PER >= 2 ? 2 : 1;
+            constexpr int PER_ST = 2;
+            static_assert(BLK_PER % PER_ST == 0, "whole TMEM stores per warpgroup");
             const int blk0 = part * BLK_PER;
 #pragma unroll
             for (int hh = 0; hh < BLK_PER / PER_ST; hh++) {
@@ -441,8 +394,7 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
                         for (int k = 0; k < 4; k++) v[bb * 16 + wd * 4 + k] = deq_pair(w4[wd], k, s2);
                 }
                 const uint32_t tcol = tbase + (uint32_t)((blk0 + hh * PER_ST) * 16);
-                if constexpr (PER_ST == 2) tmem_st_x32(tcol, v);
-                else tmem_st_x16(tcol, v);
+                tmem_st_x32(tcol, v);
             }
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             tmem_fence_before();
@@ -452,6 +404,7 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
         // ---------------- epilogue (first warpgroup)
         if (wg == 0) {
             bool okd = __all_sync(0xffffffffu, ok) && warp_wait(dfull, 0, &abort_flag);
+            grid_dependency_wait();  // y and the residual may be touched by the previous kernel
             // Every load of a 16-token chunk (residuals) is issued before the
             // first dependent add: one memory round trip per chunk.
             if (okd) {
@@ -495,6 +448,7 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
         // partial sum leaves the chip.  Every CTA reaches both barriers, also
         // after an abort (the error flag then reports the garbage).
         cluster_sync();
+        grid_dependency_wait();
         const uint32_t red_local = smem_u32(smem);
         const int rows = min(BM, N - n0), toks = min(TN, T - t0);
         const int rank = (int)cluster_ctarank();
@@ -521,6 +475,7 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
 // fp32 rows -> fp16 rows in the K order of the weight tiles (see deq_pair):
 // within every 8 elements, [e0 e4 e1 e5 e2 e6 e3 e7].
 __global__ void k_rows_to_f16_perm(const float* __restrict__ x, size_t ldx, __half* __restrict__ out, int K, int T) {
+    pdl_trigger();
     int t = blockIdx.y;
     const float* xr = x + (size_t)t * ldx;
     __half2* o = reinterpret_cast<__half2*>(out + (size_t)t * K);
@@ -601,15 +556,22 @@ int launch_tc(const hc_q4_matrix& w, const CUtensorMap& xmap, const CUtensorMap&
     cfg.blockDim = dim3(C::THREADS);
     cfg.dynamicSmemBytes = (size_t)smem;
     cfg.stream = s;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    // programmatic dependent launch: the weight prefetch overlaps the tail of
+    // the kernel that produces X (the kernel waits on the dependency itself)
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    na++;
     if (splits > 1) {  // the splits of one tile form a cluster (reduction over distributed shared memory)
-        attr[0].id = cudaLaunchAttributeClusterDimension;
-        attr[0].val.clusterDim.x = 1;
-        attr[0].val.clusterDim.y = 1;
-        attr[0].val.clusterDim.z = (unsigned)splits;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = 1;
+        attr[na].val.clusterDim.y = 1;
+        attr[na].val.clusterDim.z = (unsigned)splits;
+        na++;
     }
+    cfg.attrs = attr;
+    cfg.numAttrs = (unsigned)na;
     HC_CUDA(cudaLaunchKernelEx(&cfg, kfn, xmap, wmap, (const __half*)w.sc, y, ldy, res, ldres, epi, (int)w.n,
                                (int)w.k, (int)T, splits, err));
     hc_count_launch();
@@ -694,13 +656,32 @@ int gemm_tc(GemmWorkspace* ws, const hc_q4_matrix& w, const float* x, size_t ldx
 
 uint64_t gemm_generation(GemmWorkspace* ws) { return ws ? ws->generation : 0; }
 
+int* gemm_error_flag(GemmWorkspace* ws) {
+    std::lock_guard<std::mutex> lock(ws->mu);
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+    if (ws->device != dev) {
+        ws->xh = nullptr;
+        ws->xh_cap = 0;
+        ws->err = nullptr;
+        ws->wmaps.clear();
+        ws->device = dev;
+    }
+    if (!ws->err) {
+        if (cudaMalloc((void**)&ws->err, sizeof(int)) != cudaSuccess) return nullptr;
+        if (cudaMemset(ws->err, 0, sizeof(int)) != cudaSuccess) return nullptr;
+    }
+    return ws->err;
+}
+
 int gemm_check(GemmWorkspace* ws) {
     if (!ws || !ws->err) return HC_OK;
     int h = 0;
     HC_CUDA(cudaMemcpy(&h, ws->err, sizeof(int), cudaMemcpyDeviceToHost));
     if (h) {
         HC_CUDA(cudaMemset(ws->err, 0, sizeof(int)));
-        hc_set_error("tcgen05 GEMM: a pipeline wait timed out (the kernel aborted and skipped its stores)");
+        hc_set_error("a bounded pipeline wait timed out in a tcgen05 GEMM or a TMA attention kernel (the kernel "
+                     "aborted and skipped its stores)");
         return HC_ERR_TIMEOUT;
     }
     return HC_OK;

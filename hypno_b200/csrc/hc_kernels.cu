@@ -313,6 +313,7 @@ int launch_matmul(const DevWeight& w, const float* x, size_t ldx, size_t mtok, f
 // kernels.rs:592-625: ms = sum(x^2)/n, inv = 1/sqrt(ms + eps), y = (x*inv)*w.
 __global__ void k_rmsnorm(const float* __restrict__ x, size_t ldx, const float* __restrict__ w,
                           float* __restrict__ out, size_t ldo, int n, float eps, __half* __restrict__ out16) {
+    pdl_trigger();
     __shared__ float red[32];
     const float* xr = x + (size_t)blockIdx.x * ldx;
     float* orow = out + (size_t)blockIdx.x * ldo;
@@ -333,6 +334,7 @@ __global__ void k_rmsnorm(const float* __restrict__ x, size_t ldx, const float* 
 template <int VPT>
 __global__ void k_rmsnorm_v4(const float* __restrict__ x, size_t ldx, const float* __restrict__ w,
                              float* __restrict__ out, size_t ldo, int n, float eps, __half* __restrict__ out16) {
+    pdl_trigger();
     __shared__ float red[32];
     const float4* xr = reinterpret_cast<const float4*>(x + (size_t)blockIdx.x * ldx);
     const float4* wr = reinterpret_cast<const float4*>(w);
@@ -437,6 +439,7 @@ int launch_silu(float* x, size_t n, cudaStream_t s) {
 // transformer.rs:446-449 / turbo.rs:235-237: silu(gate) * up.
 __global__ void k_silu_mul(const float* __restrict__ gu, size_t ldgu, float* __restrict__ act, size_t ldact,
                            int im, __half* __restrict__ act16) {
+    pdl_trigger();
     const float* g = gu + (size_t)blockIdx.y * ldgu;
     float* a = act + (size_t)blockIdx.y * ldact;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < im; i += gridDim.x * blockDim.x) {

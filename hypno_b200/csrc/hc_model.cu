@@ -605,11 +605,11 @@ int run_layers(hc_model* m, hc_kv* kv, size_t rows, bool prefill, int seq, int p
             const int red_floats = (hc::DA_REDUCE_WARPS + 1) * G * (int)hd;
             const int smem_floats = 110 * 1024 / 4;
             const bool whole = ctas * 4 >= slots * 3 || kv->max_pos <= 256;
-            if (whole && G * kv->max_pos + red_floats <= smem_floats) {
+            if (whole && G * kv->max_pos + 4 + red_floats <= smem_floats) {
                 D.chunk = kv->max_pos;
                 D.nsplit = 1;
             } else {
-                int max_chunk = std::max(64, (smem_floats - red_floats) / G);
+                int max_chunk = std::max(64, (smem_floats - 4 - red_floats) / G);
                 int want_splits = (int)std::max<size_t>(1, (slots + ctas - 1) / ctas);
                 int chunk = std::max(256, (kv->max_pos + want_splits - 1) / want_splits);
                 chunk = std::min(chunk, max_chunk);
@@ -810,6 +810,10 @@ HC_EXPORT int hc_model_load(const uint8_t* image, size_t len, int tp_rank, int t
     if (staging) cudaFree(staging);
     staging = nullptr;
     m->gemm_ws = hc::gemm_workspace_new();
+    if (!hc::gemm_error_flag(m->gemm_ws)) {  // allocated now: kernels captured later refer to it
+        hc_set_error("cannot allocate the pipeline error flag");
+        return fail(HC_ERR_OOM);
+    }
     if ((r = ensure_rope(m, c.max_position_embeddings))) return fail(r);
     *out = m;
     return HC_OK;
