@@ -28,6 +28,7 @@ all-reduce after o_proj / down_proj, vocabulary-sharded LM head): the same
 import argparse
 import ctypes
 import json
+import re
 import os
 import subprocess
 import sys
@@ -183,11 +184,15 @@ def roofline_gemv(dev, M=32, N=28672, K=4096, copies=4, reps=20):
     algo = 0.5625 * N * K + 4.0 * M * K + 4.0 * M * N
     peak, src = measured_peaks()
     achieved = algo / (ms * 1e-3) / 1e9
+    # DRAM bytes per launch of this kernel from the committed ncu summary
     traffic = None
-    tp = os.path.join(ROOT, "profiles", "gemv_gateup_traffic.json")
+    tp = os.path.join(ROOT, "profiles", "gemm_tc_gateup_c4_decode.md")
     if os.path.exists(tp):
         with open(tp) as f:
-            traffic = json.load(f).get("dram_bytes_per_launch")
+            for line in f:
+                mt = re.match(r"\|\s*dram_bytes_per_launch\s*\|\s*(\d+)", line)
+                if mt:
+                    traffic = int(mt.group(1))
     return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
             "frac": round(achieved / peak, 4), "traffic": traffic,
             "kernel": f"q4_0 matmul N={N} K={K} M={M}", "algorithmic_bytes": int(algo),
