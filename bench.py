@@ -293,7 +293,7 @@ def run_ours(args):
     if world > 1:
         import datetime
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
     from hypno_b200 import build, engine, synth
     from hypno_b200._lib import call, load
     if rank == 0:

@@ -68,6 +68,7 @@ int nccl_fail(ncclResult_t r, const char* what) {
 struct Comm {
     ncclComm_t comm = nullptr;
     int rank = 0, size = 1;
+    double timeout_s = 60.0;
     bool aborted = false;
 };
 
@@ -93,6 +94,7 @@ int comm_init(Comm** out, const uint8_t* id128, int rank, int size, double timeo
     Comm* c = new Comm();
     c->rank = rank;
     c->size = size;
+    c->timeout_s = timeout_s;
     ncclResult_t r = a.commInitRankConfig(&c->comm, size, id, rank, &cfg);
     if (r != ncclSuccess && r != ncclInProgress) {
         delete c;
@@ -129,18 +131,26 @@ void comm_free(Comm* c) {
     delete c;
 }
 
-// Waits for an in-progress non-blocking enqueue.
+// Waits for an in-progress non-blocking enqueue.  The first collective of a
+// communicator also sets up its peer connections, which can take far longer
+// than later enqueues, so the bound is the communicator's own timeout; on
+// expiry the communicator is aborted.
 static int comm_enqueue_ok(Comm* c, ncclResult_t r, const char* what) {
     if (r == ncclSuccess) return HC_OK;
     if (r != ncclInProgress) return nccl_fail(r, what);
-    for (int i = 0; i < 100000; i++) {
+    auto t0 = std::chrono::steady_clock::now();
+    for (int i = 0;; i++) {
         ncclResult_t st = ncclInProgress;
         api().commGetAsyncError(c->comm, &st);
         if (st == ncclSuccess) return HC_OK;
         if (st != ncclInProgress) return nccl_fail(st, what);
-        std::this_thread::yield();
+        if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > c->timeout_s) break;
+        if (i < 1000) std::this_thread::yield();
+        else std::this_thread::sleep_for(std::chrono::microseconds(20));
     }
-    hc_set_error("NCCL %s: enqueue did not complete", what);
+    api().commAbort(c->comm);
+    c->aborted = true;
+    hc_set_error("NCCL %s: enqueue did not complete within %.0f s; communicator aborted", what, c->timeout_s);
     return HC_ERR_TIMEOUT;
 }
 
@@ -152,6 +162,28 @@ int comm_allreduce_sum(Comm* c, float* buf, size_t count, cudaStream_t s) {
 int comm_allgather(Comm* c, const float* send, float* recv, size_t count, cudaStream_t s) {
     HC_CHECK(c && !c->aborted, HC_ERR_STATE, "communicator unavailable");
     return comm_enqueue_ok(c, api().allGather(send, recv, count, ncclFloat32, c->comm, s), "AllGather");
+}
+
+int comm_allgather_host(Comm* c, const void* send, void* recv, size_t bytes) {
+    HC_CHECK(c && !c->aborted, HC_ERR_STATE, "communicator unavailable");
+    uint8_t* d = nullptr;
+    HC_CUDA(cudaMalloc((void**)&d, bytes * (size_t)(c->size + 1)));
+    cudaStream_t s = nullptr;
+    int rc = HC_OK;
+    if (cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) != cudaSuccess) {
+        cudaFree(d);
+        return hc_cuda_fail(cudaGetLastError(), "cudaStreamCreate", __FILE__, __LINE__);
+    }
+    uint8_t* dsend = d + bytes * (size_t)c->size;
+    if (cudaMemcpyAsync(dsend, send, bytes, cudaMemcpyHostToDevice, s) != cudaSuccess)
+        rc = hc_cuda_fail(cudaGetLastError(), "cudaMemcpyAsync", __FILE__, __LINE__);
+    if (rc == HC_OK) rc = comm_enqueue_ok(c, api().allGather(dsend, d, bytes, ncclUint8, c->comm, s), "AllGather");
+    if (rc == HC_OK) rc = comm_wait(c, s, c->timeout_s);
+    if (rc == HC_OK && cudaMemcpy(recv, d, bytes * (size_t)c->size, cudaMemcpyDeviceToHost) != cudaSuccess)
+        rc = hc_cuda_fail(cudaGetLastError(), "cudaMemcpy", __FILE__, __LINE__);
+    cudaStreamDestroy(s);
+    cudaFree(d);
+    return rc;
 }
 
 // Host watchdog: waits for the stream while polling the communicator; a peer

@@ -12,5 +12,19 @@ void comm_free(Comm* c);
 int comm_allreduce_sum(Comm* c, float* buf, size_t count, cudaStream_t s);
 int comm_allgather(Comm* c, const float* send, float* recv, size_t count, cudaStream_t s);
 int comm_wait(Comm* c, cudaStream_t s, double timeout_s);
+// Every rank's `bytes` host bytes gathered in rank order into recv (blocking).
+int comm_allgather_host(Comm* c, const void* send, void* recv, size_t bytes);
+
+// One-shot peer all-reduce fused with the residual add and the next RMSNorm
+// (hc_peer_ar.cu), for decode-sized row-parallel outputs.
+struct PeerAr;
+int peer_ar_init(Comm* c, int rank, int size, size_t rows_cap, size_t H, PeerAr** out);
+void peer_ar_free(PeerAr* a, int rank, int size);
+float* peer_ar_partial(PeerAr* a);  // this rank's [rows_cap][H] partial buffer
+bool peer_ar_fits(const PeerAr* a, size_t rows, size_t H);
+// hidden[r] += sum over ranks of partial[r] (rank order); then, when w is not
+// null, xn[r] = RMSNorm(hidden[r]) * w and its fp16 copy in GEMM K order.
+int peer_ar_residual_norm(PeerAr* a, int rank, int size, size_t rows, float* hidden, size_t ldh, const float* w,
+                          float eps, float* xn, size_t ldxn, __half* xn16, int* err, cudaStream_t s);
 
 }  // namespace hc

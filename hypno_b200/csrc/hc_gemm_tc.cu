@@ -22,8 +22,10 @@
 //                     with split K, the last CTA of a tile to finish adds the
 //                     partial sums in split order
 //
-// No cluster multicast is used anywhere (the same code runs under tensor
-// parallelism on several GPUs).  Every mbarrier wait is bounded by a clock
+// Every TMA load writes only the issuing CTA's own shared memory (the same
+// code runs under tensor parallelism on several GPUs; split-K clusters share
+// partial tiles through distributed shared memory loads, never through TMA).
+// Every mbarrier wait is bounded by a clock
 // deadline; on expiry the kernel records an error flag, skips its stores, and
 // still frees its tensor memory before returning.
 #include "hc_gemm.h"
@@ -202,7 +204,11 @@ struct Cfg {
     static constexpr int X_STAGE = 2 * TN * 128;             // two 64-element K halves, 128 B per token row
     static constexpr int W_STAGE = BM * (BK / 2);            // 128 rows x 64 nibble bytes
     static constexpr int S_SM = DUAL ? (TN <= 32 ? 6 : 4) : (TN == 128 ? 5 : 3);  // TMA ring stages
-    static constexpr int A_COL = TN <= 64 ? 64 : TN;         // A slots start here; D occupies [0, TN)
+    // Decode CTAs issue their MMAs from two warps (one per 64-wide K half of
+    // each stage, each into its own accumulator, summed by the epilogue):
+    // the issue path of one thread, not the tensor pipe, bounds these tiles.
+    static constexpr int ISS = DUAL ? 2 : 1;
+    static constexpr int A_COL = DUAL ? (ISS * TN < 64 ? 64 : ISS * TN) : TN;  // A slots start here; D_i at [i TN, (i+1) TN)
     static constexpr int S_TM = (COLS - A_COL) / 64 < S_SM ? (COLS - A_COL) / 64 : S_SM;  // A slots
     static constexpr int MMA_BATCH = S_TM < 4 ? S_TM : 4;   // stages issued under one wait + fence
     static constexpr int RR = DUAL ? 1 : (S_TM >= 4 ? 4 : 2);  // dequant groups working on different stages
@@ -210,8 +216,10 @@ struct Cfg {
     __host__ __device__ static constexpr int x_off(int s) { return s * X_STAGE; }
     __host__ __device__ static constexpr int w_off(int s) { return S_SM * X_STAGE + s * W_STAGE; }
     __host__ __device__ static constexpr int bar_off() { return S_SM * (X_STAGE + W_STAGE); }
-    __host__ __device__ static constexpr int smem() { return bar_off() + (2 * S_SM + 2 * S_TM + 1) * 8 + 16 + 1024; }
-    static_assert(A_COL + 64 * S_TM <= COLS, "tensor memory budget");
+    __host__ __device__ static constexpr int smem() { return bar_off() + (2 * S_SM + S_TM + 1) * 8 + 16 + 1024; }
+    static_assert(A_COL + 64 * S_TM <= COLS && ISS * TN <= A_COL, "tensor memory budget");
+    static_assert(ISS == 1 || ISS == 2, "one or two issuing warps");
+    static_assert(S_SM % S_TM == 0, "an A slot is freed with the TMA stage of the same MMA commit");
     static_assert(RR <= S_TM && RR <= S_SM, "dequant groups must not run more than one barrier phase apart");
     static_assert(WG_PER == 1 || WG_PER == 2, "dequant split: 4 or 2 blocks per warpgroup");
     static_assert(!DUAL || 2 * (smem() + 1024) <= 233472, "two CTAs must fit in one SM's shared memory");
@@ -231,8 +239,7 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::bar_off());  // [S_SM] TMA landed
     uint64_t* sempty = full + S_SM;                                     // [S_SM] MMAs reading it done
     uint64_t* aready = sempty + S_SM;                                   // [S_TM] A slot written
-    uint64_t* tempty = aready + S_TM;                                   // [S_TM] MMAs reading it done
-    uint64_t* dfull = tempty + S_TM;
+    uint64_t* dfull = aready + S_TM;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dfull + 1);
     __shared__ int abort_flag;
 
@@ -247,13 +254,10 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
         abort_flag = 0;
         for (int st = 0; st < S_SM; st++) {
             mbar_init(&full[st], 1);
-            mbar_init(&sempty[st], 1);
+            mbar_init(&sempty[st], C::ISS);  // a commit of every issuer
         }
-        for (int a = 0; a < S_TM; a++) {
-            mbar_init(&aready[a], 4 * C::WG_PER);  // the warps of the group that owns the stage
-            mbar_init(&tempty[a], 1);
-        }
-        mbar_init(dfull, 1);
+        for (int a = 0; a < S_TM; a++) mbar_init(&aready[a], 4 * C::WG_PER);  // the warps of the owning group
+        mbar_init(dfull, C::ISS);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 2) {
@@ -302,8 +306,10 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
                 tma_load_2d(smem + C::w_off(st), &wmap, &full[st], kk / 2, n0);
             }
         }
-    } else if (warp == 1) {
-        // ---------------- MMA issuer
+    } else if (warp == 1 || (C::ISS == 2 && warp == 3)) {
+        // ---------------- MMA issuer(s): issuer i takes the K steps
+        // [i * 8 / ISS, (i + 1) * 8 / ISS) of every stage into accumulator
+        // D_i (columns [i TN, (i + 1) TN)).
         // The tcgen05 fence that must follow each barrier wait stalls the
         // issuing thread, so every stage that is already dequantized when the
         // oldest one is (up to MMA_BATCH) is taken under a single wait + fence.
@@ -311,6 +317,9 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
         // this thread's MMA of it).
         if (lane == 0) {
             constexpr uint32_t idesc = make_idesc(TN);
+            constexpr int KSTEPS = BK / 16 / C::ISS;
+            const int iss = warp == 1 ? 0 : 1;
+            const uint32_t d_tmem = tmem + (uint32_t)(iss * TN);
             bool ok = true;
             for (int j = 0; j < nk;) {
                 if (!mbar_wait(&aready[j % S_TM], (uint32_t)(j / S_TM) & 1u, &abort_flag)) {
@@ -326,13 +335,13 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
                     const int st = j % S_SM, a = j % S_TM;
                     const uint32_t xs = smem_u32(smem + C::x_off(st));
 #pragma unroll
-                    for (int kk = 0; kk < BK / 16; kk++) {
+                    for (int k2 = 0; k2 < KSTEPS; k2++) {
+                        const int kk = iss * KSTEPS + k2;
                         uint32_t a_tmem = tmem + (uint32_t)(C::A_COL + a * 64 + kk * 8);
                         uint32_t b_addr = xs + (uint32_t)((kk >> 2) * TN * 128 + (kk & 3) * 32);
-                        mma_f16_ts(tmem, a_tmem, sw128_desc(b_addr), idesc, (j > 0 || kk > 0) ? 1u : 0u);
+                        mma_f16_ts(d_tmem, a_tmem, sw128_desc(b_addr), idesc, (j > 0 || k2 > 0) ? 1u : 0u);
                     }
-                    mma_commit(&sempty[st]);
-                    mma_commit(&tempty[a]);
+                    mma_commit(&sempty[st]);  // frees the TMA stage and (S_TM | S_SM) the A slot
                 }
             }
             if (ok) mma_commit(dfull);
@@ -363,7 +372,12 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
             const int st = j % S_SM, a = j % S_TM;
             uint2 sc = sc_next;
             if (j + C::RR < nk && row_ok) sc_next = __ldg(srow + it0 + j + C::RR);
-            if (!warp_wait(&tempty[a], ((uint32_t)(j / S_TM) & 1u) ^ 1u, &abort_flag) ||
+            // A slot a was last read by the MMAs of stage j - S_TM, whose
+            // completion is phase (j - S_TM) / S_SM of that stage's sempty
+            // barrier (S_TM divides S_SM, so the slot and the stage are freed
+            // by the same commit)
+            if ((j >= S_TM &&
+                 !warp_wait(&sempty[(j - S_TM) % S_SM], (uint32_t)((j - S_TM) / S_SM) & 1u, &abort_flag)) ||
                 !warp_wait(&full[st], (uint32_t)(j / S_SM) & 1u, &abort_flag)) {
                 ok = false;
                 break;
@@ -419,6 +433,14 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
                 for (int c0 = 0; c0 < TN; c0 += EPI_CH) {
                     uint32_t v[EPI_CH];
                     tmem_ld_x16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
+                    if constexpr (C::ISS == 2) {
+                        uint32_t v1[EPI_CH];
+                        tmem_ld_x16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(TN + c0), v1);
+                        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+                        for (int jj = 0; jj < EPI_CH; jj++)
+                            v[jj] = __float_as_uint(__uint_as_float(v[jj]) + __uint_as_float(v1[jj]));
+                    }
                     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
                     if (splits > 1) {
 #pragma unroll

@@ -221,6 +221,7 @@ struct hc_model {
     // communicator, and the host watchdog limit for one step
     size_t vocab0 = 0, vocab_shard = 0;
     hc::Comm* comm = nullptr;
+    hc::PeerAr* par = nullptr;  // one-shot peer all-reduce (decode sizes), when peers are mapped
     double comm_timeout_s = 60.0;
 };
 
@@ -382,6 +383,7 @@ void free_model(hc_model* m) {
     if (m->gemm_ws) hc::gemm_workspace_free(m->gemm_ws);
     if (m->sc.tp_tmp) cudaFree(m->sc.tp_tmp);
     if (m->sc.tp_gather) cudaFree(m->sc.tp_gather);
+    if (m->par) hc::peer_ar_free(m->par, m->cfg.tp_rank, m->cfg.tp_size);
     if (m->comm) hc::comm_free(m->comm);
     if (m->stream) cudaStreamDestroy(m->stream);
     delete m;
@@ -481,11 +483,25 @@ __global__ void k_add_rows(float* __restrict__ y, const float* __restrict__ a, s
 // tensor-parallel ranks (o_proj, down_proj): each rank's partial product is
 // summed by an all-reduce, then added to the residual stream (the reference's
 // `hidden[i] = residual[i] + proj[i]`, transformer.rs:561-563, 595-598).
-int row_parallel(hc_model* m, const DevWeight& w, const float* x, size_t ldx, size_t rows, const __half* x16) {
+// Decode-sized outputs use the one-shot peer all-reduce, which also applies
+// the next RMSNorm (weight next_norm, when given) and then sets *normed; other
+// sizes (prefill) use NCCL and leave the norm to the caller.
+int row_parallel(hc_model* m, const DevWeight& w, const float* x, size_t ldx, size_t rows, const __half* x16,
+                 const float* next_norm = nullptr, bool* normed = nullptr) {
     const size_t H = m->cfg.hidden_size;
     Scratch& s = m->sc;
+    if (normed) *normed = false;
     if (m->cfg.tp_size <= 1) return matmul(m, w, x, ldx, rows, s.hidden, H, hc::EPI_ADD, s.hidden, H, x16);
     HC_CHECK(m->comm, HC_ERR_STATE, "tensor-parallel model used before hc_comm_init");
+    if (m->par && hc::peer_ar_fits(m->par, rows, H)) {
+        float* part = hc::peer_ar_partial(m->par);
+        HC_TRY(matmul(m, w, x, ldx, rows, part, H, hc::EPI_STORE, nullptr, 0, x16));
+        HC_TRY(hc::peer_ar_residual_norm(m->par, m->cfg.tp_rank, m->cfg.tp_size, rows, s.hidden, H, next_norm,
+                                         m->cfg.rms_norm_eps, s.xn, H, s.xn16, hc::gemm_error_flag(m->gemm_ws),
+                                         m->stream));
+        if (normed) *normed = next_norm != nullptr;
+        return HC_OK;
+    }
     HC_TRY(matmul(m, w, x, ldx, rows, s.tp_tmp, H, hc::EPI_STORE, nullptr, 0, x16));
     HC_TRY(hc::comm_allreduce_sum(m->comm, s.tp_tmp, rows * H, m->stream));
     size_t n = rows * H;
@@ -535,16 +551,24 @@ int model_wait(hc_model* m) {
 
 // The per-layer body shared by prefill (prefill = true, rows = prompt
 // tokens of one sequence) and decode (rows = sequences).
-int run_layers(hc_model* m, hc_kv* kv, size_t rows, bool prefill, int seq, int pos0) {
+// tail_norm: the norm that follows the last layer (the final norm in decode);
+// *tail_normed reports whether the last projection's all-reduce already
+// applied it to s.xn.
+int run_layers(hc_model* m, hc_kv* kv, size_t rows, bool prefill, int seq, int pos0,
+               const float* tail_norm = nullptr, bool* tail_normed = nullptr) {
     const hc_config& c = m->cfg;
     Scratch& s = m->sc;
     const size_t hd = c.head_dim, H = c.hidden_size;
     const size_t nq = m->nq, nk = m->nk, ldqkv = nq + 2 * nk;
     const size_t nh_l = nq / hd, nkv_l = nk / hd;
     const float scale = 1.0f / sqrtf((float)hd);
+    bool xn_ready = false;  // s.xn already holds this layer's input norm
+    if (tail_normed) *tail_normed = false;
     for (size_t li = 0; li < m->layers.size(); li++) {
         LayerW& L = m->layers[li];
-        HC_TRY(hc::launch_rmsnorm(s.hidden, H, L.in_norm, s.xn, H, rows, H, c.rms_norm_eps, m->stream, s.xn16));
+        if (!xn_ready)
+            HC_TRY(hc::launch_rmsnorm(s.hidden, H, L.in_norm, s.xn, H, rows, H, c.rms_norm_eps, m->stream, s.xn16));
+        xn_ready = false;
         HC_TRY(matmul(m, L.qkv, s.xn, H, rows, s.qkv, ldqkv, hc::EPI_STORE, nullptr, 0, s.xn16));
         HC_TRY(hc::launch_rope_rows(s.qkv, ldqkv, rows, nh_l + nkv_l, hd, m->rope, m->rope_rows,
                                     prefill ? nullptr : s.rowpos, pos0, m->stream));
@@ -635,12 +659,21 @@ int run_layers(hc_model* m, hc_kv* kv, size_t rows, bool prefill, int seq, int p
             P.pos = kv->pos_dev;
             HC_TRY(hc::launch_attention(P, (int)rows, kv->kv_fp16, m->stream));
         }
-        HC_TRY(row_parallel(m, L.o, s.attn, nq, rows, s.attn16));
-        HC_TRY(hc::launch_rmsnorm(s.hidden, H, L.post_norm, s.xn, H, rows, H, c.rms_norm_eps, m->stream, s.xn16));
+        bool normed = false;
+        HC_TRY(row_parallel(m, L.o, s.attn, nq, rows, s.attn16, L.post_norm, &normed));
+        if (!normed)
+            HC_TRY(hc::launch_rmsnorm(s.hidden, H, L.post_norm, s.xn, H, rows, H, c.rms_norm_eps, m->stream, s.xn16));
         size_t im = L.gu.n / 2;
         HC_TRY(matmul(m, L.gu, s.xn, H, rows, s.gu, 2 * im, hc::EPI_STORE, nullptr, 0, s.xn16));
         HC_TRY(hc::launch_silu_mul(s.gu, 2 * im, s.act, im, rows, im, m->stream, s.act16));
-        HC_TRY(row_parallel(m, L.down, s.act, im, rows, s.act16));
+        const bool last = li + 1 == m->layers.size();
+        const float* next = last ? tail_norm : m->layers[li + 1].in_norm;
+        HC_TRY(row_parallel(m, L.down, s.act, im, rows, s.act16, next, &normed));
+        if (last) {
+            if (tail_normed) *tail_normed = normed;
+        } else {
+            xn_ready = normed;
+        }
     }
     return HC_OK;
 }
@@ -661,10 +694,12 @@ int decode_dev_impl(hc_model* m, hc_kv* kv, const int* seqs_dev, const uint32_t*
     k_gather_pos<<<(B + 127) / 128, 128, 0, m->stream>>>(s.seqs, kv->pos_dev, s.rowpos, B);
     HC_LAUNCH_CHECK();
     HC_TRY(hc::launch_embed(m->embed, s.ids, (size_t)B, s.hidden, c.hidden_size, m->stream));
-    HC_TRY(run_layers(m, kv, (size_t)B, false, 0, 0));
+    bool final_normed = false;
+    HC_TRY(run_layers(m, kv, (size_t)B, false, 0, 0, m->final_norm, &final_normed));
     HC_TRY(hc::launch_advance(s.seqs, kv->pos_dev, B, m->stream));
-    HC_TRY(hc::launch_rmsnorm(s.hidden, c.hidden_size, m->final_norm, s.xn, c.hidden_size, (size_t)B, c.hidden_size,
-                              c.rms_norm_eps, m->stream, s.xn16));
+    if (!final_normed)
+        HC_TRY(hc::launch_rmsnorm(s.hidden, c.hidden_size, m->final_norm, s.xn, c.hidden_size, (size_t)B,
+                                  c.hidden_size, c.rms_norm_eps, m->stream, s.xn16));
     float* logits = logits_dev ? logits_dev : s.logits;
     HC_TRY(lm_head_logits(m, s.xn, (size_t)B, logits, s.xn16));
     if (argmax_dev) HC_TRY(hc::launch_argmax(logits, (size_t)B, c.vocab_size, argmax_dev, m->stream));
@@ -1105,10 +1140,20 @@ HC_EXPORT int hc_comm_init(hc_model* m, const uint8_t* id128, int rank, int size
              "hc_comm_init: rank/size %d/%d differ from the model's shard %d/%d", rank, size, m->cfg.tp_rank,
              m->cfg.tp_size);
     HC_CUDA(cudaSetDevice(m->device));
+    if (m->par) {
+        hc::peer_ar_free(m->par, rank, size);
+        m->par = nullptr;
+    }
     if (m->comm) {
         hc::comm_free(m->comm);
         m->comm = nullptr;
     }
     if (timeout_s > 0) m->comm_timeout_s = timeout_s;
-    return hc::comm_init(&m->comm, id128, rank, size, m->comm_timeout_s);
+    HC_TRY(hc::comm_init(&m->comm, id128, rank, size, m->comm_timeout_s));
+    // decode-sized all-reduces over mapped peer memory (up to 256 rows); NCCL
+    // stays for larger ones and whenever peer mappings are unavailable
+    const char* env = getenv("HC_PEER_ALLREDUCE");
+    if (!(env && env[0] == '0'))
+        HC_TRY(hc::peer_ar_init(m->comm, rank, size, 256, m->cfg.hidden_size, &m->par));
+    return HC_OK;
 }
