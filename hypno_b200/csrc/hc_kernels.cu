@@ -103,12 +103,9 @@ int launch_q4_split(const uint8_t* aos, size_t nblocks, uint4* qs, __half* sc, c
 // ============================================================ Q4_0 matvec
 //
 // y[m][row] = sum_b scale[row,b] * sum_j (nib[row,b,j] - 8) * x[m][32b + j]
-// for k % 32 == 0 (blocks aligned with rows).  A row group of TPR threads
-// shares a row set of R rows: thread `li` walks blocks li, li+TPR, ... so a
-// warp's 16-byte nibble loads of one row are contiguous.  The x block (32
-// floats) is loaded once per block and reused for the R rows; up to MT
-// tokens are handled per pass.  The per-block dot is formed exactly on
-// integers-as-floats and folded in with one fma by the f32 scale.
+// for k % 32 == 0 (blocks aligned with rows).  Up to MT tokens are handled
+// per pass.  The per-block dot is formed exactly on integers-as-floats and
+// folded in with one fma by the f32 scale.
 
 __device__ __forceinline__ float nib_f(uint32_t w, int j) {
     // (nibble j of w) - 8 as an exact float: 2^23 + nib built by bit-or, then
@@ -128,42 +125,69 @@ __device__ __forceinline__ float q4_block_dot(uint4 q, const float* xv) {
     return (d0 + d1) + (d2 + d3);
 }
 
-template <int TPR, int R, int MT>
-__global__ void __launch_bounds__(128) k_q4_gemv(const uint4* __restrict__ qs, const __half* __restrict__ sc,
-                                                 const float* __restrict__ x, size_t ldx, int mtok,
-                                                 float* __restrict__ y, size_t ldy, int epi,
-                                                 const float* res, size_t ldres, int N, int KB) {
-    constexpr int GROUPS = 128 / TPR;
-    const int g = threadIdx.x / TPR, li = threadIdx.x % TPR;
-    const int row0 = (blockIdx.x * GROUPS + g) * R;
+// One CTA (GV_THREADS threads) per R rows.  Thread t takes blocks t,
+// t + GV_THREADS, ... of every row (16-byte nibble loads, coalesced across the
+// CTA), loads U such blocks of all R rows before any arithmetic (U x R x 16
+// bytes in flight per thread), and loads each f32 x block once for the R rows
+// (x traffic 128 B per R x 18 B of weights, so L1 stays below the DRAM rate).
+// Each block's dot product is exact-order within the block and scaled once
+// (fmaf by the f32 scale), as in kernels.rs:286-344; a thread sums its blocks
+// in order, then the CTA reduces (warp tree, then warps in order), so the
+// result does not depend on scheduling.
+constexpr int GV_THREADS = 128;
+
+template <int R, int U, int MT>
+__global__ void __launch_bounds__(GV_THREADS) k_q4_gemv(const uint4* __restrict__ qs, const __half* __restrict__ sc,
+                                                        const float* __restrict__ x, size_t ldx, int mtok,
+                                                        float* __restrict__ y, size_t ldy, int epi,
+                                                        const float* res, size_t ldres, int N, int KB) {
+    __shared__ float red[GV_THREADS / 32][R * MT];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int row0 = blockIdx.x * R;
+    int rows[R];
+#pragma unroll
+    for (int r = 0; r < R; r++) rows[r] = min(row0 + r, N - 1);
     for (int m0 = 0; m0 < mtok; m0 += MT) {
         float acc[R][MT];
 #pragma unroll
         for (int r = 0; r < R; r++)
 #pragma unroll
             for (int t = 0; t < MT; t++) acc[r][t] = 0.0f;
-        for (int b = li; b < KB; b += TPR) {
-            uint4 q[R];
-            float s[R];
+        for (int b0 = threadIdx.x; b0 < KB; b0 += GV_THREADS * U) {
+            uint4 q[U][R];
+            float s[U][R];
 #pragma unroll
-            for (int r = 0; r < R; r++) {
-                int row = min(row0 + r, N - 1);
-                size_t bi = (size_t)row * KB + b;
-                q[r] = __ldg(qs + bi);
-                s[r] = __half2float(sc[bi]);
+            for (int u = 0; u < U; u++) {
+                const int b = b0 + u * GV_THREADS;
+#pragma unroll
+                for (int r = 0; r < R; r++) {
+                    if (b < KB) {
+                        size_t bi = (size_t)rows[r] * KB + b;
+                        q[u][r] = __ldg(qs + bi);
+                        s[u][r] = __half2float(sc[bi]);
+                    } else {
+                        q[u][r] = make_uint4(0x88888888u, 0x88888888u, 0x88888888u, 0x88888888u);
+                        s[u][r] = 0.0f;
+                    }
+                }
             }
 #pragma unroll
-            for (int t = 0; t < MT; t++) {
-                if (m0 + t < mtok) {
-                    const float4* xp = reinterpret_cast<const float4*>(x + (size_t)(m0 + t) * ldx + (size_t)b * 32);
-                    float xv[32];
+            for (int u = 0; u < U; u++) {
+                const int b = b0 + u * GV_THREADS;
 #pragma unroll
-                    for (int i = 0; i < 8; i++) {
-                        float4 f = __ldg(xp + i);
-                        xv[4 * i] = f.x; xv[4 * i + 1] = f.y; xv[4 * i + 2] = f.z; xv[4 * i + 3] = f.w;
+                for (int t = 0; t < MT; t++) {
+                    if (b < KB && m0 + t < mtok) {
+                        const float4* xp =
+                            reinterpret_cast<const float4*>(x + (size_t)(m0 + t) * ldx + (size_t)b * 32);
+                        float xv[32];
+#pragma unroll
+                        for (int i = 0; i < 8; i++) {
+                            float4 f = __ldg(xp + i);
+                            xv[4 * i] = f.x; xv[4 * i + 1] = f.y; xv[4 * i + 2] = f.z; xv[4 * i + 3] = f.w;
+                        }
+#pragma unroll
+                        for (int r = 0; r < R; r++) acc[r][t] = fmaf(s[u][r], q4_block_dot(q[u][r], xv), acc[r][t]);
                     }
-#pragma unroll
-                    for (int r = 0; r < R; r++) acc[r][t] = fmaf(s[r], q4_block_dot(q[r], xv), acc[r][t]);
                 }
             }
         }
@@ -171,26 +195,22 @@ __global__ void __launch_bounds__(128) k_q4_gemv(const uint4* __restrict__ qs, c
         for (int r = 0; r < R; r++)
 #pragma unroll
             for (int t = 0; t < MT; t++) {
-                float v = acc[r][t];
-#pragma unroll
-                for (int o = TPR / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-                acc[r][t] = v;
+                float v = warp_sum(acc[r][t]);
+                if (lane == 0) red[warp][r * MT + t] = v;
             }
-        if (li == 0) {
+        __syncthreads();
+        if (threadIdx.x < R * MT) {
+            const int r = threadIdx.x / MT, t = threadIdx.x % MT;
+            const int row = row0 + r, m = m0 + t;
+            float v = 0.0f;
 #pragma unroll
-            for (int r = 0; r < R; r++) {
-                int row = row0 + r;
-                if (row >= N) continue;
-#pragma unroll
-                for (int t = 0; t < MT; t++) {
-                    int m = m0 + t;
-                    if (m >= mtok) continue;
-                    float v = acc[r][t];
-                    if (epi == EPI_ADD && res) v = v + res[(size_t)m * ldres + row];
-                    y[(size_t)m * ldy + row] = v;
-                }
+            for (int w = 0; w < GV_THREADS / 32; w++) v += red[w][threadIdx.x];
+            if (row < N && m < mtok) {
+                if (epi == EPI_ADD && res) v = v + res[(size_t)m * ldres + row];
+                y[(size_t)m * ldy + row] = v;
             }
         }
+        __syncthreads();
     }
 }
 
@@ -249,31 +269,44 @@ __global__ void k_dense_gemv(const T* __restrict__ w, const float* __restrict__ 
     }
 }
 
-template <int TPR, int R, int MT>
+template <int R, int U, int MT>
 static void launch_gemv_t(const hc_q4_matrix& w, const float* x, size_t ldx, size_t mtok, float* y, size_t ldy,
                           int epi, const float* res, size_t ldres, cudaStream_t s) {
-    constexpr int GROUPS = 128 / TPR;
-    int rows_per_cta = GROUPS * R;
-    unsigned grid = (unsigned)((w.n + rows_per_cta - 1) / rows_per_cta);
-    k_q4_gemv<TPR, R, MT><<<grid, 128, 0, s>>>(w.qs, w.sc, x, ldx, (int)mtok, y, ldy, epi, res, ldres, (int)w.n,
-                                               (int)(w.k / 32));
+    unsigned grid = (unsigned)((w.n + R - 1) / R);
+    k_q4_gemv<R, U, MT><<<grid, GV_THREADS, 0, s>>>(w.qs, w.sc, x, ldx, (int)mtok, y, ldy, epi, res, ldres,
+                                                    (int)w.n, (int)(w.k / 32));
 }
 
-template <int TPR>
-static void launch_gemv_tpr(const hc_q4_matrix& w, const float* x, size_t ldx, size_t mtok, float* y, size_t ldy,
-                            int epi, const float* res, size_t ldres, cudaStream_t s) {
-    // Rows per thread: 4 when there are enough rows for ~2 waves, else 1.
-    size_t ctas4 = (w.n + (128 / TPR) * 4 - 1) / ((128 / TPR) * 4);
-    bool big = ctas4 >= 296;
-    if (mtok == 1) {
-        if (big) launch_gemv_t<TPR, 4, 1>(w, x, ldx, mtok, y, ldy, epi, res, ldres, s);
-        else launch_gemv_t<TPR, 1, 1>(w, x, ldx, mtok, y, ldy, epi, res, ldres, s);
-    } else if (mtok <= 4) {
-        if (big) launch_gemv_t<TPR, 2, 4>(w, x, ldx, mtok, y, ldy, epi, res, ldres, s);
-        else launch_gemv_t<TPR, 1, 4>(w, x, ldx, mtok, y, ldy, epi, res, ldres, s);
+// 8 rows per CTA (x reused 8 times) when that still gives ~2 CTAs per SM,
+// fewer for short matrices; U = 2 unrolled blocks per thread when the rows
+// are longer than one block per thread.
+template <int MT>
+static void launch_gemv_mt(const hc_q4_matrix& w, const float* x, size_t ldx, size_t mtok, float* y, size_t ldy,
+                           int epi, const float* res, size_t ldres, cudaStream_t s) {
+    const size_t kb = w.k / 32;
+    const bool u2 = kb > (size_t)GV_THREADS;
+    if constexpr (MT > 1) {  // several tokens: their accumulators take the registers of extra rows
+        if (u2) launch_gemv_t<2, 2, MT>(w, x, ldx, mtok, y, ldy, epi, res, ldres, s);
+        else launch_gemv_t<2, 1, MT>(w, x, ldx, mtok, y, ldy, epi, res, ldres, s);
     } else {
-        launch_gemv_t<TPR, 1, 8>(w, x, ldx, mtok, y, ldy, epi, res, ldres, s);
+        if (w.n >= 8 * 296) {
+            if (u2) launch_gemv_t<8, 2, 1>(w, x, ldx, mtok, y, ldy, epi, res, ldres, s);
+            else launch_gemv_t<8, 1, 1>(w, x, ldx, mtok, y, ldy, epi, res, ldres, s);
+        } else if (w.n >= 4 * 296) {
+            if (u2) launch_gemv_t<4, 2, 1>(w, x, ldx, mtok, y, ldy, epi, res, ldres, s);
+            else launch_gemv_t<4, 1, 1>(w, x, ldx, mtok, y, ldy, epi, res, ldres, s);
+        } else {
+            if (u2) launch_gemv_t<2, 2, 1>(w, x, ldx, mtok, y, ldy, epi, res, ldres, s);
+            else launch_gemv_t<2, 1, 1>(w, x, ldx, mtok, y, ldy, epi, res, ldres, s);
+        }
     }
+}
+
+static void launch_gemv(const hc_q4_matrix& w, const float* x, size_t ldx, size_t mtok, float* y, size_t ldy,
+                        int epi, const float* res, size_t ldres, cudaStream_t s) {
+    if (mtok == 1) launch_gemv_mt<1>(w, x, ldx, mtok, y, ldy, epi, res, ldres, s);
+    else if (mtok <= 4) launch_gemv_mt<4>(w, x, ldx, mtok, y, ldy, epi, res, ldres, s);
+    else launch_gemv_mt<8>(w, x, ldx, mtok, y, ldy, epi, res, ldres, s);
 }
 
 int launch_matmul(const DevWeight& w, const float* x, size_t ldx, size_t mtok, float* y, size_t ldy, int epi,
@@ -284,10 +317,7 @@ int launch_matmul(const DevWeight& w, const float* x, size_t ldx, size_t mtok, f
         bool aligned = (q.k % 32 == 0) && (((uintptr_t)x & 15) == 0) && (ldx % 4 == 0) &&
                        (q.nblocks >= q.n * (q.k / 32));
         if (aligned) {
-            size_t kb = q.k / 32;
-            if (kb >= 32) launch_gemv_tpr<32>(q, x, ldx, mtok, y, ldy, epi, res, ldres, s);
-            else if (kb >= 16) launch_gemv_tpr<16>(q, x, ldx, mtok, y, ldy, epi, res, ldres, s);
-            else launch_gemv_tpr<8>(q, x, ldx, mtok, y, ldy, epi, res, ldres, s);
+            launch_gemv(q, x, ldx, mtok, y, ldy, epi, res, ldres, s);
         } else {
             size_t warps = q.n * mtok;
             k_q4_gemv_general<<<grid_for(warps * 32, 256), 256, 0, s>>>(q.qs, q.sc, q.nblocks, x, ldx, (int)mtok, y,
