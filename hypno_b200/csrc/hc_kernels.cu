@@ -214,6 +214,135 @@ __global__ void __launch_bounds__(GV_THREADS) k_q4_gemv(const uint4* __restrict_
     }
 }
 
+// ---- Single-token matvec with a packed dot (k % 32 == 0, k <= 24576).
+//
+// Nibble p of a 32-bit word w (p = 0..4: bits 4p..4p+3, inside the f32
+// mantissa) is isolated with one AND; the bits read as an f32 are the
+// denormal nib * 2^(4p) * 2^-149.  One packed f32x2 fma with x 2^126 and
+// + (-8 * 2^(4p-23)) gives (nib - 8) * 2^(4p-23) exactly (a power-of-two
+// product, then an exact sum of small integers times one power of two;
+// denormals are kept, the build does not flush them).  Nibbles 5..7 come from
+// w >> 20 at positions 0..2.  x is staged once per CTA in shared memory
+// scaled by 2^(23-4p) (exact), so a second packed fma accumulates
+// (nib - 8) * x with an exact product and one rounding per add, as the scalar
+// path does.  Position of element j (0..7) of a word: 0 1 2 3 4 | 0 1 2.
+constexpr int G1_THREADS = 256;
+
+__device__ __forceinline__ float2 nib_pair(uint32_t a, uint32_t ma, uint32_t b, uint32_t mb, float2 bias) {
+    const float2 f = make_float2(__uint_as_float(a & ma), __uint_as_float(b & mb));
+    const float2 up = make_float2(__uint_as_float(0x7E800000u), __uint_as_float(0x7E800000u));  // 2^126
+    return __ffma2_rn(f, up, bias);
+}
+
+// Adds word w's 8 products (nib_j - 8) * x_j to the two pair accumulators;
+// xa / xb are the word's scaled x elements 0..3 / 4..7.
+__device__ __forceinline__ void word_dot_packed(uint32_t w, float4 xa, float4 xb, float2& a0, float2& a1) {
+    const float b0 = -9.5367431640625e-07f, b1 = -1.52587890625e-05f, b2 = -0.000244140625f;  // -8 * 2^(4p-23)
+    const float b3 = -0.00390625f, b4 = -0.0625f;
+    const uint32_t hi = w >> 20;
+    a0 = __ffma2_rn(nib_pair(w, 0xFu, w, 0xF0u, make_float2(b0, b1)), make_float2(xa.x, xa.y), a0);
+    a1 = __ffma2_rn(nib_pair(w, 0xF00u, w, 0xF000u, make_float2(b2, b3)), make_float2(xa.z, xa.w), a1);
+    a0 = __ffma2_rn(nib_pair(w, 0xF0000u, hi, 0xFu, make_float2(b4, b0)), make_float2(xb.x, xb.y), a0);
+    a1 = __ffma2_rn(nib_pair(hi, 0xF0u, hi, 0xF00u, make_float2(b1, b2)), make_float2(xb.z, xb.w), a1);
+}
+
+// Scaled x of block b starts at float4 G1_XS * b: 8 float4 of data plus one of
+// padding, so lanes reading consecutive blocks hit distinct shared-memory banks.
+constexpr int G1_XS = 9;
+
+// One warp per group of R rows at a time (grid-stride over the groups); lane
+// l takes blocks l, l + 32, ... of the R rows, U blocks of loads before any
+// arithmetic; each x chunk (one word's 8 elements) is read once for the R
+// rows; the warp then sums its lanes in a fixed tree.
+template <int R, int U>
+__global__ void __launch_bounds__(G1_THREADS, 3) k_q4_gemv1(const uint4* __restrict__ qs, const __half* __restrict__ sc,
+                                                         const float* __restrict__ x, float* __restrict__ y, int epi,
+                                                         const float* res, int N, int KB) {
+    extern __shared__ float4 xs4[];  // x' = x scaled per nibble position, KB x G1_XS float4
+    for (int i = threadIdx.x; i < KB * 8; i += G1_THREADS) {
+        float4 v = __ldg(reinterpret_cast<const float4*>(x) + i);
+        // elements 4i..4i+3: positions (4i & 7) + 0..3 of a word
+        // x 2^(23-4p): 2^23, 2^19, 2^15, 2^11, 2^7 for positions 0..4
+        if ((i & 1) == 0) {  // word elements 0..3: positions 0 1 2 3
+            v.x = __fmul_rn(v.x, 8388608.0f);
+            v.y = __fmul_rn(v.y, 524288.0f);
+            v.z = __fmul_rn(v.z, 32768.0f);
+            v.w = __fmul_rn(v.w, 2048.0f);
+        } else {             // word elements 4..7: positions 4 0 1 2
+            v.x = __fmul_rn(v.x, 128.0f);
+            v.y = __fmul_rn(v.y, 8388608.0f);
+            v.z = __fmul_rn(v.z, 524288.0f);
+            v.w = __fmul_rn(v.w, 32768.0f);
+        }
+        xs4[(i >> 3) * G1_XS + (i & 7)] = v;
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int groups = (N + R - 1) / R;
+    for (int g = blockIdx.x * (G1_THREADS / 32) + warp; g < groups; g += gridDim.x * (G1_THREADS / 32)) {
+        int rows[R];
+#pragma unroll
+        for (int r = 0; r < R; r++) rows[r] = min(g * R + r, N - 1);
+        float acc[R];
+#pragma unroll
+        for (int r = 0; r < R; r++) acc[r] = 0.0f;
+        for (int b0 = lane; b0 < KB; b0 += 32 * U) {
+            uint4 q[U][R];
+            float s[U][R];
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                const int b = b0 + u * 32;
+#pragma unroll
+                for (int r = 0; r < R; r++) {
+                    if (b < KB) {
+                        size_t bi = (size_t)rows[r] * KB + b;
+                        q[u][r] = __ldg(qs + bi);
+                        s[u][r] = __half2float(sc[bi]);
+                    } else {
+                        q[u][r] = make_uint4(0x88888888u, 0x88888888u, 0x88888888u, 0x88888888u);
+                        s[u][r] = 0.0f;
+                    }
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                const int b = b0 + u * 32;
+                if (b < KB) {
+                    const float4* xb4 = xs4 + (size_t)b * G1_XS;
+                    float2 a[R][2];
+#pragma unroll
+                    for (int r = 0; r < R; r++) a[r][0] = a[r][1] = make_float2(0.0f, 0.0f);
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        const float4 xa = xb4[2 * i], xb = xb4[2 * i + 1];
+#pragma unroll
+                        for (int r = 0; r < R; r++) {
+                            const uint32_t wd = i == 0 ? q[u][r].x : i == 1 ? q[u][r].y : i == 2 ? q[u][r].z : q[u][r].w;
+                            word_dot_packed(wd, xa, xb, a[r][0], a[r][1]);
+                        }
+                    }
+#pragma unroll
+                    for (int r = 0; r < R; r++)
+                        acc[r] = fmaf(s[u][r], (a[r][0].x + a[r][0].y) + (a[r][1].x + a[r][1].y), acc[r]);
+                }
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < R; r++) acc[r] = warp_sum(acc[r]);
+        if (lane == 0) {
+#pragma unroll
+            for (int r = 0; r < R; r++) {
+                const int row = g * R + r;
+                if (row < N) {
+                    float v = acc[r];
+                    if (epi == EPI_ADD && res) v = v + res[row];
+                    y[row] = v;
+                }
+            }
+        }
+    }
+}
+
 // General Q4_0 matvec for k % 32 != 0: blocks straddle row boundaries
 // (kernels.rs:281-349).  One warp per (row, token); element e of the
 // flattened tensor uses block e/32, nibble e%32.
@@ -304,6 +433,18 @@ static void launch_gemv_mt(const hc_q4_matrix& w, const float* x, size_t ldx, si
 
 static void launch_gemv(const hc_q4_matrix& w, const float* x, size_t ldx, size_t mtok, float* y, size_t ldy,
                         int epi, const float* res, size_t ldres, cudaStream_t s) {
+    const size_t kb = w.k / 32;
+    if (mtok == 1 && kb <= 768) {
+        // a few CTAs per SM, each staging x once and striding over row groups
+        const size_t smem = kb * G1_XS * sizeof(float4);
+        const size_t groups = (w.n + 1) / 2;  // 2 rows per warp
+        const size_t per_cta = G1_THREADS / 32;
+        unsigned grid = (unsigned)std::min<size_t>((groups + per_cta - 1) / per_cta, 148 * 3);
+        if (smem > 48 * 1024)
+            cudaFuncSetAttribute(k_q4_gemv1<2, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        k_q4_gemv1<2, 4><<<grid, G1_THREADS, smem, s>>>(w.qs, w.sc, x, y, epi, res, (int)w.n, (int)kb);
+        return;
+    }
     if (mtok == 1) launch_gemv_mt<1>(w, x, ldx, mtok, y, ldy, epi, res, ldres, s);
     else if (mtok <= 4) launch_gemv_mt<4>(w, x, ldx, mtok, y, ldy, epi, res, ldres, s);
     else launch_gemv_mt<8>(w, x, ldx, mtok, y, ldy, epi, res, ldres, s);
