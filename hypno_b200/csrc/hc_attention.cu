@@ -513,6 +513,120 @@ __global__ void __launch_bounds__(DA_THREADS, 2) k_dattn_fused(DecAttnParams P) 
     }
 }
 
+// ---- Cluster split.  When the batch has too few (sequence, KV head) pairs
+// to fill the GPU (tensor-parallel shards), the NCL CTAs of a thread-block
+// cluster share one pair: CTA c scores positions [c len, (c+1) len), the CTAs
+// exchange their per-head maxima through distributed shared memory (every CTA
+// then holds the same global maxima), form their weights and partial P.V, and
+// after a second exchange CTA c finishes the output features
+// [c G HD / NCL, (c+1) G HD / NCL) by adding the partials in rank order.
+__device__ __forceinline__ void cl_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t cl_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+__device__ __forceinline__ float cl_ld(const float* local, int rank) {
+    uint32_t a = (uint32_t)__cvta_generic_to_shared(local), remote;
+    float v;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(a), "r"(rank));
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+    return v;
+}
+
+template <typename KT, int G, int HD>
+__global__ void __launch_bounds__(DA_THREADS, 2) k_dattn_cluster(DecAttnParams P) {
+    pdl_trigger();
+    using C = DA<KT, G, HD>;
+    extern __shared__ float smem[];
+    __shared__ float redv[32];
+    __shared__ float xch[2 * DA_MAXG];  // this CTA's per-head maxima, then its weight sums
+    const int row = blockIdx.x, kvh = blockIdx.y;
+    const int ncl = (int)gridDim.z;
+    const int rank = (int)cl_rank();
+    const int seq = P.seqs[row];
+    const int n = min(P.pos[seq], P.max_pos);
+    if (n <= 1) {  // uniform over the cluster: no exchange
+        if (rank == 0)
+            for (int i = threadIdx.x; i < G * HD; i += DA_THREADS)
+                da_write_out(P, row, kvh * G + i / HD, i % HD,
+                             P.vself[(size_t)row * P.ldself + (size_t)kvh * HD + i % HD]);
+        return;
+    }
+    const int len = (n + ncl - 1) / ncl;
+    const int p0 = min(n, rank * len), p1 = min(n, p0 + len);
+    float* S = smem;                              // [chunk][G] (chunk >= len)
+    float* red = smem + red_offset(G * P.chunk);  // [(DA_WARPS + 1) * G * HD]
+    const size_t off = (size_t)seq * P.seq_stride + (size_t)kvh * P.head_stride;
+    const KT* kbase = reinterpret_cast<const KT*>(P.kc) + off;
+    const KT* vbase = reinterpret_cast<const KT*>(P.vc) + off;
+    float2 qr[G][C::EPL / 2];
+    da_load_q<KT, G, HD>(P, row, kvh, qr);
+    float mx[G];
+#pragma unroll
+    for (int g = 0; g < G; g++) mx[g] = -INFINITY;
+    da_scores<KT, G, HD>(kbase, qr, p0, p1, P.scale, S, p0, mx);
+    float lmax[G];
+    da_head_max<KT, G, HD>(mx, lmax, redv);  // also orders the S writes
+    if (threadIdx.x < G) {
+#pragma unroll
+        for (int g = 0; g < G; g++)
+            if (threadIdx.x == g) xch[g] = lmax[g];
+    }
+    cl_sync();
+    float gmax[G];
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+        float m = -INFINITY;
+        for (int c = 0; c < ncl; c++) m = fmaxf(m, cl_ld(&xch[g], c));
+        gmax[g] = m;
+    }
+    const int n8 = n - (n % 8);
+    float lsum[G];
+#pragma unroll
+    for (int g = 0; g < G; g++) lsum[g] = 0.0f;
+    for (int p = p0 + threadIdx.x; p < p1; p += DA_THREADS) {
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+            float e = softmax_weight(S[(size_t)(p - p0) * G + g], gmax[g], p, n8);
+            S[(size_t)(p - p0) * G + g] = e;
+            lsum[g] += e;
+        }
+    }
+    float tsum[G];
+#pragma unroll
+    for (int g = 0; g < G; g++) tsum[g] = block_sum(lsum[g], redv);  // also orders the weight writes
+    float2 o[G][C::EPL / 2];
+#pragma unroll
+    for (int g = 0; g < G; g++)
+#pragma unroll
+        for (int e = 0; e < C::EPL / 2; e++) o[g][e] = make_float2(0.0f, 0.0f);
+    da_pv<KT, G, HD>(vbase, S, p0, p0, p1, o);
+    da_reduce_o<KT, G, HD>(o, red);  // this CTA's partial P.V in red[DA_WARPS * G * HD ..]
+    if (threadIdx.x < G) {
+#pragma unroll
+        for (int g = 0; g < G; g++)
+            if (threadIdx.x == g) xch[DA_MAXG + g] = tsum[g];
+    }
+    cl_sync();  // partials and sums of every CTA are visible
+    const float* fin = red + (size_t)DA_WARPS * G * HD;
+    const int f0 = (G * HD) * rank / ncl, f1 = (G * HD) * (rank + 1) / ncl;
+    for (int i = f0 + (int)threadIdx.x; i < f1; i += DA_THREADS) {
+        const int g = i / HD;
+        float num = 0.0f, den = 0.0f;
+        for (int c = 0; c < ncl; c++) {
+            num += cl_ld(&fin[i], c);
+            den += cl_ld(&xch[DA_MAXG + g], c);
+        }
+        da_write_out(P, row, kvh * G + g, i % HD, __fdiv_rn(num, den));
+    }
+    cl_sync();  // peers finished reading this CTA's shared memory
+}
+
 // Split path, pass 1: scores of one split to global S, split maximum.
 template <typename KT, int G, int HD>
 __global__ void __launch_bounds__(DA_THREADS, 2) k_dattn_scores(DecAttnParams P) {
@@ -628,6 +742,31 @@ __global__ void k_dattn_combine(DecAttnParams P) {
 template <typename KT, int G, int HD>
 int launch_dattn_ghd(const DecAttnParams& P, int rows, cudaStream_t s) {
     const size_t red_floats = (size_t)(DA_WARPS + 1) * G * HD;
+    if (P.cluster > 1) {  // chunk = positions per CTA of the cluster
+        HC_CHECK(P.cluster <= 8 && (size_t)P.chunk * P.cluster >= (size_t)P.max_pos, HC_ERR_INVALID,
+                 "decode attention: cluster %d x chunk %d does not cover %d positions", P.cluster, P.chunk,
+                 P.max_pos);
+        size_t smem = (red_offset(G * P.chunk) + red_floats) * sizeof(float);
+        HC_CHECK(smem <= 220 * 1024, HC_ERR_UNSUPPORTED, "decode attention: chunk %d too long", P.chunk);
+        if (smem > 48 * 1024)
+            HC_CUDA(cudaFuncSetAttribute(k_dattn_cluster<KT, G, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem));
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)rows, (unsigned)P.nkv, (unsigned)P.cluster);
+        cfg.blockDim = dim3(DA_THREADS);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = s;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 1;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = (unsigned)P.cluster;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        HC_CUDA(cudaLaunchKernelEx(&cfg, k_dattn_cluster<KT, G, HD>, P));
+        hc_count_launch();
+        return HC_OK;
+    }
     if (P.nsplit == 1) {
         size_t smem = (red_offset(G * P.max_pos) + red_floats) * sizeof(float);
         HC_CHECK(smem <= 220 * 1024, HC_ERR_UNSUPPORTED, "decode attention: context %d too long for one split",

@@ -26,6 +26,7 @@ struct AttnParams {
     const float* vp;
     size_t ldkv;
     __half* out16 = nullptr;  // optional fp16 copy of out (rows of nh*hd, GEMM K order)
+    int cluster = 1;          // > 1: that many CTAs of a cluster share a (sequence, KV head), chunk positions each
 };
 
 int launch_attention(const AttnParams& P, int rows, int kv_fp16, cudaStream_t s);
@@ -34,9 +35,10 @@ int launch_kv_store(const float* k, const float* v, size_t ld, int rows, int nkv
                     const int* pos, int fixed_seq, int pos0, cudaStream_t s);
 int launch_advance(const int* seqs, int* pos, int B, cudaStream_t s);
 
-// Grouped (GQA) decode attention, see hc_attention.cu.  nsplit == 1 runs one
-// fused pass per (sequence, KV head) (chunk must equal max_pos); nsplit > 1
-// runs scores / weighted-V / combine over splits of chunk positions.
+// Grouped (GQA) decode attention, see hc_attention.cu.  cluster > 1 runs one
+// pass per (sequence, KV head) split over a thread-block cluster; otherwise
+// nsplit == 1 runs one fused pass per pair (chunk must equal max_pos) and
+// nsplit > 1 runs scores / weighted-V / combine over splits of chunk positions.
 constexpr int DA_REDUCE_WARPS = 8;  // warps per attention CTA
 struct DecAttnParams {
     const float* q;       // query rows, head h at q + row*ldq + h*hd
@@ -60,6 +62,7 @@ struct DecAttnParams {
     float* opart;         // [rows][nh][nsplit][hd]
     float* spart;         // [rows][nh][nsplit]
     __half* out16 = nullptr;  // optional fp16 copy of out (rows of nh*hd, GEMM K order)
+    int cluster = 1;          // > 1: that many CTAs of a cluster share a (sequence, KV head), chunk positions each
 };
 bool dattn_supported(int nh, int nkv, int hd);
 // Tiled f32 prefill attention over the prompt's own K/V rows (mode_prefill).

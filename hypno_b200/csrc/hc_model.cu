@@ -622,15 +622,24 @@ int run_layers(hc_model* m, hc_kv* kv, size_t rows, bool prefill, int seq, int p
             D.max_pos = kv->max_pos;
             // One CTA per (sequence, KV head) streams the whole context when
             // that already fills most of the 2 x 148 CTA slots and its scores
-            // fit in shared memory; otherwise the context is split so that
-            // about one wave of CTAs runs.
+            // fit in shared memory; with fewer pairs (tensor-parallel shards)
+            // a cluster of 2-8 CTAs shares each pair; with fewer still (a
+            // single sequence) the context is split over CTAs that exchange
+            // through global scratch, so that about one wave of CTAs runs.
             const int G = (int)(nh_l / nkv_l);
             const size_t ctas = rows * nkv_l, slots = 2 * 148;
             const int red_floats = (hc::DA_REDUCE_WARPS + 1) * G * (int)hd;
             const int smem_floats = 110 * 1024 / 4;
             const bool whole = ctas * 4 >= slots * 3 || kv->max_pos <= 256;
+            int ncl = 1;  // CTAs of a cluster sharing one (sequence, KV head) when the pairs are too few
+            while (!whole && ncl < 8 && ctas * ncl * 4 < slots * 3) ncl *= 2;
+            const int cl_chunk = (kv->max_pos + ncl - 1) / ncl;
             if (whole && G * kv->max_pos + 4 + red_floats <= smem_floats) {
                 D.chunk = kv->max_pos;
+                D.nsplit = 1;
+            } else if (!whole && ctas * ncl * 4 >= slots * 3 && G * cl_chunk + 4 + red_floats <= smem_floats) {
+                D.cluster = ncl;
+                D.chunk = cl_chunk;
                 D.nsplit = 1;
             } else {
                 int max_chunk = std::max(64, (smem_floats - 4 - red_floats) / G);

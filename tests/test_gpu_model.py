@@ -213,3 +213,36 @@ def test_c4_geometry_batched_decode(cuda_device, kv_dtype):
             assert int(am[s]) == orc.greedy(ref), (step, s, margin(ref))
             nxt.append(int(am[s]))
         toks = nxt
+
+
+@pytest.mark.parametrize("n_seqs", [16, 40, 120])
+def test_decode_attention_paths(cuda_device, n_seqs):
+    """Batched decode over 16, 40 and 120 sequences of a 2-KV-head model: 32
+    and 80 (sequence, KV head) pairs run the cluster-split attention (clusters
+    of 8 and 4 CTAs, contexts split at 128- and 256-position boundaries), 240
+    pairs the single fused pass.  Ragged contexts (0..299 cached positions, so
+    some cluster CTAs own no positions) against the oracle for 2 steps."""
+    from hypno_b200 import synth as sy
+    img = sy.build_image(C4_GEOMETRY, seed=3, quantize=orc.quantize_f32_to_q4_0)
+    m = engine.HypnoModel(img)
+    om = orc.OracleModel(img)
+    rng = np.random.default_rng(n_seqs)
+    lens = [int(v) for v in rng.integers(0, 300, n_seqs)]
+    kv = engine.KVCache(m, n_seqs=n_seqs, max_pos=1024, kv_dtype=engine.KV_FP16)
+    okvs, toks = [], []
+    for s, T in enumerate(lens):
+        p = sy.prompt_ids(C4_GEOMETRY["vocab"], T, seed=100 + s)
+        engine.batch_forward(m, p, kv, seq=s)
+        okv = om.new_kv(1024)
+        r = orc.batch_forward(om, p, okv)
+        okvs.append(okv)
+        toks.append(orc.greedy(r) if T else 5)
+    seqs = list(range(n_seqs))
+    for step in range(2):
+        lg, am = engine.decode_step(m, kv, seqs, toks)
+        nxt = []
+        for s in seqs:
+            ref = orc.model_forward(om, toks[s], okvs[s])
+            assert rel_err(lg[s], ref) <= TOL, (step, s, lens[s], rel_err(lg[s], ref))
+            nxt.append(orc.greedy(ref))
+        toks = nxt
