@@ -213,9 +213,13 @@ struct Cfg {
     static constexpr int MMA_BATCH = S_TM < 4 ? S_TM : 4;   // stages issued under one wait + fence
     static constexpr int RR = DUAL ? 1 : (S_TM >= 4 ? 4 : 2);  // dequant groups working on different stages
     static constexpr int WG_PER = (DEQ_WARPS / 4) / RR;       // warpgroups per group, each 4 / WG_PER blocks
+    // fp16 block scales of the stage's 128 rows: the aligned 16-byte box of
+    // 8 scales (this stage's 4 and its pair's) per row
+    static constexpr int S_STAGE = BM * 16;
     __host__ __device__ static constexpr int x_off(int s) { return s * X_STAGE; }
     __host__ __device__ static constexpr int w_off(int s) { return S_SM * X_STAGE + s * W_STAGE; }
-    __host__ __device__ static constexpr int bar_off() { return S_SM * (X_STAGE + W_STAGE); }
+    __host__ __device__ static constexpr int s_off(int s) { return S_SM * (X_STAGE + W_STAGE) + s * S_STAGE; }
+    __host__ __device__ static constexpr int bar_off() { return S_SM * (X_STAGE + W_STAGE + S_STAGE); }
     __host__ __device__ static constexpr int smem() { return bar_off() + (2 * S_SM + S_TM + 1) * 8 + 16 + 1024; }
     static_assert(A_COL + 64 * S_TM <= COLS && ISS * TN <= A_COL, "tensor memory budget");
     static_assert(ISS == 1 || ISS == 2, "one or two issuing warps");
@@ -230,7 +234,7 @@ struct Cfg {
 template <int TN>
 __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
     k_q4_gemm_tc(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
-                 const __half* __restrict__ scales, float* __restrict__ y, size_t ldy, const float* res, size_t ldres,
+                 const __grid_constant__ CUtensorMap smap, float* __restrict__ y, size_t ldy, const float* res, size_t ldres,
                  int epi, int N, int K, int T, int splits, int* __restrict__ err) {
     using C = Cfg<TN>;
     constexpr int S_SM = C::S_SM, S_TM = C::S_TM;
@@ -245,7 +249,6 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n0 = blockIdx.x * BM, t0 = blockIdx.y * TN, split = blockIdx.z;
-    const int KB = K / 32;
     const int nk_all = K / BK;
     const int it0 = (int)((long long)nk_all * split / splits), it1 = (int)((long long)nk_all * (split + 1) / splits);
     const int nk = it1 - it0;
@@ -284,8 +287,9 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
         if (lane == 0) {
             const int pre = nk < S_SM ? nk : S_SM;
             for (int j = 0; j < pre; j++) {  // fresh ring: no sempty wait needed
-                mbar_expect_tx(&full[j], (uint32_t)(C::X_STAGE + C::W_STAGE));
+                mbar_expect_tx(&full[j], (uint32_t)(C::X_STAGE + C::W_STAGE + C::S_STAGE));
                 tma_load_2d(smem + C::w_off(j), &wmap, &full[j], (it0 + j) * BK / 2, n0);
+                tma_load_2d(smem + C::s_off(j), &smap, &full[j], 8 * ((it0 + j) >> 1), n0);
             }
             grid_dependency_wait();
             for (int j = 0; j < pre; j++) {
@@ -298,12 +302,13 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
                 const int st = j % S_SM;
                 const uint32_t ph = (uint32_t)(j / S_SM) & 1u;
                 if (!mbar_wait(&sempty[st], ph ^ 1u, &abort_flag)) break;
-                mbar_expect_tx(&full[st], (uint32_t)(C::X_STAGE + C::W_STAGE));
+                mbar_expect_tx(&full[st], (uint32_t)(C::X_STAGE + C::W_STAGE + C::S_STAGE));
                 uint8_t* xs = smem + C::x_off(st);
                 int kk = (it0 + j) * BK;
                 tma_load_2d(xs, &xmap, &full[st], kk, t0);
                 tma_load_2d(xs + TN * 128, &xmap, &full[st], kk + 64, t0);
                 tma_load_2d(smem + C::w_off(st), &wmap, &full[st], kk / 2, n0);
+                tma_load_2d(smem + C::s_off(st), &smap, &full[st], 8 * ((it0 + j) >> 1), n0);
             }
         }
     } else if (warp == 1 || (C::ISS == 2 && warp == 3)) {
@@ -364,14 +369,9 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
         const int r = q * 32 + lane;
         const int n = n0 + r;
         const bool row_ok = n < N;
-        const uint2* srow = reinterpret_cast<const uint2*>(scales + (size_t)(row_ok ? n : 0) * KB);
-        uint2 sc_next = make_uint2(0u, 0u);
-        if (row_ok && g < nk) sc_next = __ldg(srow + it0 + g);
         bool ok = true;
         for (int j = g; j < nk; j += C::RR) {
             const int st = j % S_SM, a = j % S_TM;
-            uint2 sc = sc_next;
-            if (j + C::RR < nk && row_ok) sc_next = __ldg(srow + it0 + j + C::RR);
             // A slot a was last read by the MMAs of stage j - S_TM, whose
             // completion is phase (j - S_TM) / S_SM of that stage's sempty
             // barrier (S_TM divides S_SM, so the slot and the stage are freed
@@ -382,6 +382,8 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
                 ok = false;
                 break;
             }
+            // the stage's 4 scales of row r (the scale box holds the stage pair's 8)
+            const uint2 sc = *reinterpret_cast<const uint2*>(smem + C::s_off(st) + r * 16 + ((it0 + j) & 1) * 8);
             // 64-byte rows of nibbles, 16-byte chunk c of row r stored at chunk c ^ ((r >> 1) & 3)
             const uint8_t* wrow = smem + C::w_off(st) + r * (BK / 2);
             const int sw = (r >> 1) & 3;
@@ -535,6 +537,17 @@ int encode_2d(CUtensorMap* map, CUtensorMapDataType dt, void* base, uint64_t inn
     return HC_OK;
 }
 
+// Nibble plane as [n][k/2] bytes in 128-row x 64-byte boxes (64-byte swizzle);
+// scale plane as [n][k/32] fp16 in 128-row x 8-scale boxes (16 bytes: the
+// scales of a pair of 128-wide K stages, so every box starts 16-byte aligned).
+int encode_weight_maps(const hc_q4_matrix& w, CUtensorMap* wmap, CUtensorMap* smap) {
+    const size_t K = w.k, KB = K / 32;
+    HC_TRY(encode_2d(wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.qs, K / 2, w.n, K / 2, BK / 2, BM,
+                     CU_TENSOR_MAP_SWIZZLE_64B));
+    HC_TRY(encode_2d(smap, CU_TENSOR_MAP_DATA_TYPE_UINT16, w.sc, KB, w.n, KB * 2, 8, BM, CU_TENSOR_MAP_SWIZZLE_NONE));
+    return HC_OK;
+}
+
 }  // namespace
 
 struct GemmWorkspace {
@@ -544,7 +557,8 @@ struct GemmWorkspace {
     size_t xh_cap = 0;
     int* err = nullptr;
     int device = -1;
-    std::map<std::tuple<const void*, size_t, size_t>, CUtensorMap> wmaps;  // (nibble plane, n, k)
+    // (nibble plane, scale plane, n, k) -> nibble and scale tensor maps
+    std::map<std::tuple<const void*, const void*, size_t, size_t>, std::pair<CUtensorMap, CUtensorMap>> wmaps;
 };
 
 GemmWorkspace* gemm_workspace_new() { return new GemmWorkspace(); }
@@ -557,12 +571,16 @@ void gemm_workspace_free(GemmWorkspace* ws) {
 }
 
 bool gemm_tc_eligible(const hc_q4_matrix& w, size_t tokens) {
-    return tokens >= 2 && w.k % BK == 0 && w.n >= BM && w.nblocks >= w.n * (w.k / 32) && w.k <= (1u << 20);
+    // k % 256: the scale plane's row pitch (k / 32 fp16) is then a multiple of
+    // 16 bytes, as a tensor map needs
+    return tokens >= 2 && w.k % (2 * BK) == 0 && w.n >= BM && w.nblocks >= w.n * (w.k / 32) && w.k <= (1u << 20) &&
+           ((uintptr_t)w.sc & 15) == 0;
 }
 
 namespace {
 template <int TN>
-int launch_tc(const hc_q4_matrix& w, const CUtensorMap& xmap, const CUtensorMap& wmap, size_t T, float* y,
+int launch_tc(const hc_q4_matrix& w, const CUtensorMap& xmap, const CUtensorMap& wmap, const CUtensorMap& smap,
+              size_t T, float* y,
               size_t ldy, int epi, const float* res, size_t ldres, int splits, int* err, cudaStream_t s) {
     using C = Cfg<TN>;
     static_assert(C::smem() <= 232448, "shared memory budget");
@@ -594,7 +612,7 @@ int launch_tc(const hc_q4_matrix& w, const CUtensorMap& xmap, const CUtensorMap&
     }
     cfg.attrs = attr;
     cfg.numAttrs = (unsigned)na;
-    HC_CUDA(cudaLaunchKernelEx(&cfg, kfn, xmap, wmap, (const __half*)w.sc, y, ldy, res, ldres, epi, (int)w.n,
+    HC_CUDA(cudaLaunchKernelEx(&cfg, kfn, xmap, wmap, smap, y, ldy, res, ldres, epi, (int)w.n,
                                (int)w.k, (int)T, splits, err));
     hc_count_launch();
     return HC_OK;
@@ -656,23 +674,23 @@ int gemm_tc(GemmWorkspace* ws, const hc_q4_matrix& w, const float* x, size_t ldx
     CUtensorMap xmap;
     HC_TRY(encode_2d(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, const_cast<__half*>(xh), K, T, K * 2, 64, (uint32_t)tn,
                      CU_TENSOR_MAP_SWIZZLE_128B));
-    auto key = std::make_tuple((const void*)w.qs, w.n, w.k);
+    auto key = std::make_tuple((const void*)w.qs, (const void*)w.sc, w.n, w.k);
     auto itw = ws->wmaps.find(key);
-    CUtensorMap wmap;
+    CUtensorMap wmap, smap;
     if (itw != ws->wmaps.end()) {
-        wmap = itw->second;
+        wmap = itw->second.first;
+        smap = itw->second.second;
     } else {
-        HC_TRY(encode_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.qs, K / 2, w.n, K / 2, BK / 2, BM,
-                         CU_TENSOR_MAP_SWIZZLE_64B));
-        if (w.owns) ws->wmaps[key] = wmap;
+        HC_TRY(encode_weight_maps(w, &wmap, &smap));
+        if (w.owns) ws->wmaps[key] = std::make_pair(wmap, smap);
     }
     size_t tiles = ((w.n + BM - 1) / BM) * ((T + tn - 1) / tn);
     int splits = choose_splits(tiles, K / BK, tn <= 64 ? 148 * Cfg<32>::MIN_BLOCKS : 148);
     switch (tn) {
-        case 32: return launch_tc<32>(w, xmap, wmap, T, y, ldy, epi, res, ldres, splits, ws->err, s);
-        case 64: return launch_tc<64>(w, xmap, wmap, T, y, ldy, epi, res, ldres, splits, ws->err, s);
-        case 128: return launch_tc<128>(w, xmap, wmap, T, y, ldy, epi, res, ldres, splits, ws->err, s);
-        default: return launch_tc<256>(w, xmap, wmap, T, y, ldy, epi, res, ldres, splits, ws->err, s);
+        case 32: return launch_tc<32>(w, xmap, wmap, smap, T, y, ldy, epi, res, ldres, splits, ws->err, s);
+        case 64: return launch_tc<64>(w, xmap, wmap, smap, T, y, ldy, epi, res, ldres, splits, ws->err, s);
+        case 128: return launch_tc<128>(w, xmap, wmap, smap, T, y, ldy, epi, res, ldres, splits, ws->err, s);
+        default: return launch_tc<256>(w, xmap, wmap, smap, T, y, ldy, epi, res, ldres, splits, ws->err, s);
     }
 }
 
@@ -754,7 +772,7 @@ int noalloc_scratch(uint8_t** out) {
 }  // namespace
 
 // Y[mtok x n] = X[mtok x k] . W^T like hc_q4_matmul_dev, without allocating
-// device or host memory: shapes the tensor cores take (mtok >= 2, k % 128 ==
+// device or host memory: shapes the tensor cores take (mtok >= 2, k % 256 ==
 // 0, n >= 128) run the tcgen05 kernel with its scratch in the fixed array and
 // no split-K; other shapes run the CUDA-core matvec, which needs no scratch.
 HC_EXPORT int hc_q4_matmul_noalloc(const hc_q4_matrix* w, const float* x, size_t mtok, float* y, void* stream) {
@@ -786,16 +804,15 @@ HC_EXPORT int hc_q4_matmul_noalloc(const hc_q4_matrix* w, const float* x, size_t
         HC_LAUNCH_CHECK();
     }
     int tn = T <= 32 ? 32 : T <= 64 ? 64 : T <= 128 ? 128 : 256;
-    CUtensorMap xmap, wmap;
+    CUtensorMap xmap, wmap, smap;
     HC_TRY(hc::encode_2d(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xh, K, T, K * 2, 64, (uint32_t)tn,
                          CU_TENSOR_MAP_SWIZZLE_128B));
-    HC_TRY(hc::encode_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->qs, K / 2, w->n, K / 2, hc::BK / 2, hc::BM,
-                         CU_TENSOR_MAP_SWIZZLE_64B));
+    HC_TRY(hc::encode_weight_maps(*w, &wmap, &smap));
     switch (tn) {
-        case 32: return hc::launch_tc<32>(*w, xmap, wmap, T, y, w->n, hc::EPI_STORE, nullptr, 0, 1, err, s);
-        case 64: return hc::launch_tc<64>(*w, xmap, wmap, T, y, w->n, hc::EPI_STORE, nullptr, 0, 1, err, s);
-        case 128: return hc::launch_tc<128>(*w, xmap, wmap, T, y, w->n, hc::EPI_STORE, nullptr, 0, 1, err, s);
-        default: return hc::launch_tc<256>(*w, xmap, wmap, T, y, w->n, hc::EPI_STORE, nullptr, 0, 1, err, s);
+        case 32: return hc::launch_tc<32>(*w, xmap, wmap, smap, T, y, w->n, hc::EPI_STORE, nullptr, 0, 1, err, s);
+        case 64: return hc::launch_tc<64>(*w, xmap, wmap, smap, T, y, w->n, hc::EPI_STORE, nullptr, 0, 1, err, s);
+        case 128: return hc::launch_tc<128>(*w, xmap, wmap, smap, T, y, w->n, hc::EPI_STORE, nullptr, 0, 1, err, s);
+        default: return hc::launch_tc<256>(*w, xmap, wmap, smap, T, y, w->n, hc::EPI_STORE, nullptr, 0, 1, err, s);
     }
 }
 
