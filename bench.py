@@ -279,7 +279,8 @@ def workload_config(world, mode="tp"):
     par = "single" if world == 1 else (f"tp{world}" if mode == "tp" else f"replicas{world}")
     return {"workload": "c4 decode: Llama-3-8B shape (hidden 4096, 32 layers, 32/8 heads, im 14336, vocab 128256), "
                         "32 sequences each prefilled with 2048 random tokens, greedy batched decode, fp16 KV",
-            "model": "llama-3-8b-shape-random-q4_0", "global_batch": 32 * world, "seq_len": 2048,
+            "model": "llama-3-8b-shape-random-q4_0", "global_batch": 32 if mode == "tp" else 32 * world,
+            "seq_len": 2048,
             "parallelism": par,
             "l2": "inputs larger than L2 (4.22 GB of Q4_0 weights + ~8.6 GB KV read per step)"}
 
@@ -439,8 +440,9 @@ def run_reference(args):
                      f"decodes sequences one at a time, serve.rs:175,193); {args.steps} steps in {dt:.1f} s"}
     line = {"impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 2),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "q4_0 weights, f32 compute",
-            "data": "synthetic", "config": workload_config(world), "cpu_baseline": cpu,
+            "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+            "dtype": "q4_0 weights, f32 compute", "data": "synthetic", "config": workload_config(world),
+            "cpu_baseline": cpu,
             "e2e": {"value": round(v, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 

@@ -199,7 +199,11 @@ int hc_comm_unique_id(uint8_t* out128);
 /* Joins the tensor-parallel group of a model loaded with
  * hc_model_load(..., rank, size, ...).  The all-reduce after o_proj and
  * down_proj and the all-gather of the vocabulary-sharded logits then run on
- * the model's stream.  Host waits of the model (hc_sync, hc_prefill,
+ * the model's stream.  Decode-sized all-reduces (up to 256 rows) read the
+ * peers' partial sums over CUDA-IPC-mapped device memory, fused with the
+ * residual add and the next RMSNorm; NCCL carries larger ones, and all of
+ * them when the environment sets HC_PEER_ALLREDUCE=0 or a peer cannot be
+ * mapped.  Host waits of the model (hc_sync, hc_prefill,
  * hc_decode_step) are watched: a collective that does not finish within
  * timeout_s seconds (<= 0: 60) aborts the communicator and returns
  * HC_ERR_TIMEOUT. */

@@ -1,6 +1,7 @@
-"""Tensor parallelism on 2 GPUs: the c4-geometry model sharded over two ranks
-(NCCL all-reduce after o_proj / down_proj, vocabulary-sharded LM head) must
-match the single-device oracle.  Skipped on a 1-GPU machine."""
+"""Tensor parallelism on 2, 4 and 8 GPUs: a small Llama-geometry model sharded
+over the ranks (all-reduce after o_proj / down_proj, vocabulary-sharded LM
+head) must match the single-device oracle.  Each size is skipped on a machine
+with fewer GPUs.  The 4- and 8-rank geometries leave one KV head per rank."""
 import os
 import socket
 
@@ -11,6 +12,7 @@ pytestmark = pytest.mark.gpu
 
 GEOM = dict(hidden=1024, layers=2, heads=8, kv_heads=2, inter=2816, vocab=8192, theta=500000.0,
             max_pos=1024, embed="q4", lm_head="tied")
+GEOMS = {2: GEOM, 4: dict(GEOM, heads=16, kv_heads=4), 8: dict(GEOM, heads=32, kv_heads=8)}
 
 
 def _free_port():
@@ -20,6 +22,7 @@ def _free_port():
 
 
 def _rank(rank, size, port, q):
+    geom = GEOMS[size]
     try:
         import datetime
         import torch
@@ -31,11 +34,11 @@ def _rank(rank, size, port, q):
         from hypno_b200._lib import call
         from oracle import oracle as orc
         call("hc_set_device", rank)
-        img = synth.build_image(GEOM, seed=3, quantize=orc.quantize_f32_to_q4_0)
+        img = synth.build_image(geom, seed=3, quantize=orc.quantize_f32_to_q4_0)
         m = engine.HypnoModel(img, rank, size)
         tp.join(m, rank, size, timeout_s=60)
         kv = engine.KVCache(m, n_seqs=2, max_pos=1024, kv_dtype=engine.KV_FP16)
-        prompts = [synth.prompt_ids(GEOM["vocab"], T, seed=20 + s) for s, T in enumerate((300, 9))]
+        prompts = [synth.prompt_ids(geom["vocab"], T, seed=20 + s) for s, T in enumerate((300, 9))]
         first = [engine.batch_forward(m, p, kv, seq=s) for s, p in enumerate(prompts)]
         toks = [int(np.nonzero(f == f.max())[0][-1]) for f in first]
         steps = []
@@ -69,15 +72,16 @@ def _rank(rank, size, port, q):
         q.put((rank, False, repr(e)))
 
 
-def test_tp2_matches_oracle():
+@pytest.mark.parametrize("size", [2, 4, 8])
+def test_tp_matches_oracle(size):
     import torch
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+    if torch.cuda.device_count() < size:
+        pytest.skip(f"needs {size} GPUs")
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, size, port, q)) for r in range(size)]
     for p in procs:
         p.start()
     res = [q.get(timeout=600) for _ in procs]
