@@ -8,19 +8,20 @@
 // tile is the M = 128 side and the tokens are the N side, so one CTA tile is
 // 128 weight rows x TN tokens.
 //
-//   TMA (warp 0)      X tile (fp16, K-major, 128B swizzle) + the Q4_0 nibble
-//                     tile of 128 rows x 128 K  -> shared memory stage s
+//   TMA (warps 0, 2)  the Q4_0 nibble tile of 128 rows x 128 K and its scales
+//                     -> weight ring; X tile (fp16, K-major, 128B swizzle)
+//                     -> X ring
 //   dequant (warps 4-19 for prefill tiles, 4-11 for decode tiles; one
 //                     weight row per thread) nibbles -> (nib - 8) * scale in
 //                     fp16 -> tcgen05.st into tensor memory (the A operand
 //                     never touches shared memory, so shared-memory bandwidth
 //                     is left to the TMA traffic and the B operand)
-//   MMA (warp 1)      tcgen05.mma.kind::f16, A from TMEM, B from the smem
-//                     descriptor, f32 accumulator in TMEM; tcgen05.commit
-//                     frees the stage
+//   MMA (warp 1, and warp 3 for decode tiles)  tcgen05.mma.kind::f16, A from
+//                     TMEM, B from the smem descriptor, f32 accumulator in
+//                     TMEM; tcgen05.commit frees the X stage and the A slot
 //   epilogue (warps 4-7)  tcgen05.ld of the accumulator -> Y (+ residual);
-//                     with split K, the last CTA of a tile to finish adds the
-//                     partial sums in split order
+//                     with split K, the CTAs of a tile (one cluster) add their
+//                     partial tiles in split order over distributed shared memory
 //
 // Every TMA load writes only the issuing CTA's own shared memory (the same
 // code runs under tensor parallelism on several GPUs; split-K clusters share
@@ -190,10 +191,16 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
 // which ONE thread can issue MMAs (each tcgen05.mma of 128 x TN x 16 plus its
 // commit and the fence after a barrier wait holds the issuing thread far
 // longer than the tensor pipe needs), so two CTAs share an SM, each with 256
-// tensor-memory columns and its own issuer; each keeps a deep shared-memory
-// ring of TMA stages (hiding DRAM latency) but only three tensor-memory A
-// slots.  A prefill tile (TN >= 128) keeps one CTA per SM with all 512
-// columns, where the larger N makes every MMA worth its issue cost.
+// tensor-memory columns and two issuers; a prefill tile (TN >= 128) keeps one
+// CTA per SM with all 512 columns, where the larger N makes every MMA worth
+// its issue cost.
+//
+// Shared memory holds two rings.  The weight ring (nibble tile + scale box,
+// S_W stages) is released by the dequant warps as soon as they have read a
+// stage, so its depth is spent on DRAM latency alone; the X ring (S_X
+// stages) is released by the MMA commit.  Tensor memory holds S_TM A slots;
+// S_TM divides S_X, so the commit that frees X stage j % S_X also frees A
+// slot j % S_TM.
 template <int TN>
 struct Cfg {
     static constexpr bool DUAL = TN <= 64;                   // two CTAs per SM
@@ -203,32 +210,35 @@ struct Cfg {
     static constexpr int MIN_BLOCKS = DUAL ? 2 : 1;
     static constexpr int X_STAGE = 2 * TN * 128;             // two 64-element K halves, 128 B per token row
     static constexpr int W_STAGE = BM * (BK / 2);            // 128 rows x 64 nibble bytes
-    static constexpr int S_SM = DUAL ? (TN <= 32 ? 6 : 4) : (TN == 128 ? 5 : 3);  // TMA ring stages
-    // Decode CTAs issue their MMAs from two warps (one per 64-wide K half of
-    // each stage, each into its own accumulator, summed by the epilogue):
-    // the issue path of one thread, not the tensor pipe, bounds these tiles.
-    static constexpr int ISS = DUAL ? 2 : 1;
-    static constexpr int A_COL = DUAL ? (ISS * TN < 64 ? 64 : ISS * TN) : TN;  // A slots start here; D_i at [i TN, (i+1) TN)
-    static constexpr int S_TM = (COLS - A_COL) / 64 < S_SM ? (COLS - A_COL) / 64 : S_SM;  // A slots
-    static constexpr int MMA_BATCH = S_TM < 4 ? S_TM : 4;   // stages issued under one wait + fence
-    static constexpr int RR = DUAL ? 1 : (S_TM >= 4 ? 4 : 2);  // dequant groups working on different stages
-    static constexpr int WG_PER = (DEQ_WARPS / 4) / RR;       // warpgroups per group, each 4 / WG_PER blocks
     // fp16 block scales of the stage's 128 rows: the aligned 16-byte box of
     // 8 scales (this stage's 4 and its pair's) per row
     static constexpr int S_STAGE = BM * 16;
+    static constexpr int S_X = DUAL ? (TN <= 32 ? 6 : 4) : (TN == 128 ? 5 : 3);  // X ring stages
+    static constexpr int S_W = DUAL ? (TN <= 32 ? 6 : 4) : (TN == 128 ? 5 : 3);  // weight ring stages
+    // Decode CTAs issue their MMAs from two warps (one per 64-wide K half of
+    // each stage, each into its own accumulator, summed by the epilogue).
+    static constexpr int ISS = DUAL ? 2 : 1;
+    static constexpr int A_COL = DUAL ? (ISS * TN < 64 ? 64 : ISS * TN) : TN;  // A slots start here; D_i at [i TN, (i+1) TN)
+    static constexpr int S_TM = (COLS - A_COL) / 64 < S_X ? (COLS - A_COL) / 64 : S_X;  // A slots
+    static constexpr int MMA_BATCH = S_TM < 4 ? S_TM : 4;   // stages issued under one wait + fence
+    static constexpr int RR = DUAL ? 1 : (S_TM >= 4 ? 4 : 2);  // dequant groups working on different stages
+    static constexpr int WG_PER = (DEQ_WARPS / 4) / RR;       // warpgroups per group, each 4 / WG_PER blocks
     __host__ __device__ static constexpr int x_off(int s) { return s * X_STAGE; }
-    __host__ __device__ static constexpr int w_off(int s) { return S_SM * X_STAGE + s * W_STAGE; }
-    __host__ __device__ static constexpr int s_off(int s) { return S_SM * (X_STAGE + W_STAGE) + s * S_STAGE; }
-    __host__ __device__ static constexpr int bar_off() { return S_SM * (X_STAGE + W_STAGE + S_STAGE); }
-    __host__ __device__ static constexpr int smem() { return bar_off() + (2 * S_SM + S_TM + 1) * 8 + 16 + 1024; }
+    __host__ __device__ static constexpr int w_off(int s) { return S_X * X_STAGE + s * W_STAGE; }
+    __host__ __device__ static constexpr int s_off(int s) { return S_X * X_STAGE + S_W * W_STAGE + s * S_STAGE; }
+    __host__ __device__ static constexpr int ring_bytes() { return S_X * X_STAGE + S_W * (W_STAGE + S_STAGE); }
+    __host__ __device__ static constexpr int bar_off() { return ring_bytes(); }
+    static constexpr int NBARS = 2 * S_W + 2 * S_X + S_TM + 1;
+    __host__ __device__ static constexpr int smem() { return bar_off() + NBARS * 8 + 16 + 1024; }
     static_assert(A_COL + 64 * S_TM <= COLS && ISS * TN <= A_COL, "tensor memory budget");
     static_assert(ISS == 1 || ISS == 2, "one or two issuing warps");
-    static_assert(S_SM % S_TM == 0, "an A slot is freed with the TMA stage of the same MMA commit");
-    static_assert(RR <= S_TM && RR <= S_SM, "dequant groups must not run more than one barrier phase apart");
+    static_assert(S_X % S_TM == 0, "an A slot is freed by the MMA commit that frees an X stage");
+    static_assert(RR <= S_TM && RR <= S_W, "dequant groups must not run more than one barrier phase apart");
+    static_assert(S_W >= S_TM && (RR == 1 || S_X == S_TM), "barrier phase ordering (see the dequant warps)");
     static_assert(WG_PER == 1 || WG_PER == 2, "dequant split: 4 or 2 blocks per warpgroup");
     static_assert(!DUAL || 2 * (smem() + 1024) <= 233472, "two CTAs must fit in one SM's shared memory");
     static constexpr int RED_PITCH = TN + 1;                  // floats per row of the split-K partial tile
-    static_assert(BM * RED_PITCH * 4 <= S_SM * (X_STAGE + W_STAGE), "partial tile fits in the TMA stages");
+    static_assert(BM * RED_PITCH * 4 <= ring_bytes(), "partial tile fits in the rings");
 };
 
 template <int TN>
@@ -237,12 +247,14 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
                  const __grid_constant__ CUtensorMap smap, float* __restrict__ y, size_t ldy, const float* res, size_t ldres,
                  int epi, int N, int K, int T, int splits, int* __restrict__ err) {
     using C = Cfg<TN>;
-    constexpr int S_SM = C::S_SM, S_TM = C::S_TM;
+    constexpr int S_X = C::S_X, S_W = C::S_W, S_TM = C::S_TM;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::bar_off());  // [S_SM] TMA landed
-    uint64_t* sempty = full + S_SM;                                     // [S_SM] MMAs reading it done
-    uint64_t* aready = sempty + S_SM;                                   // [S_TM] A slot written
+    uint64_t* wfull = reinterpret_cast<uint64_t*>(smem + C::bar_off());  // [S_W] weight stage landed
+    uint64_t* wempty = wfull + S_W;                                      // [S_W] weight stage read by dequant
+    uint64_t* xfull = wempty + S_W;                                      // [S_X] X stage landed
+    uint64_t* mdone = xfull + S_X;                                       // [S_X] MMAs of the stage done
+    uint64_t* aready = mdone + S_X;                                      // [S_TM] A slot written
     uint64_t* dfull = aready + S_TM;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dfull + 1);
     __shared__ int abort_flag;
@@ -255,11 +267,15 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
 
     if (threadIdx.x == 0) {
         abort_flag = 0;
-        for (int st = 0; st < S_SM; st++) {
-            mbar_init(&full[st], 1);
-            mbar_init(&sempty[st], C::ISS);  // a commit of every issuer
+        for (int st = 0; st < S_W; st++) {
+            mbar_init(&wfull[st], 1);
+            mbar_init(&wempty[st], 4 * C::WG_PER);  // the warps of the converting group
         }
-        for (int a = 0; a < S_TM; a++) mbar_init(&aready[a], 4 * C::WG_PER);  // the warps of the owning group
+        for (int st = 0; st < S_X; st++) {
+            mbar_init(&xfull[st], 1);
+            mbar_init(&mdone[st], C::ISS);  // a commit of every issuer
+        }
+        for (int a = 0; a < S_TM; a++) mbar_init(&aready[a], 4 * C::WG_PER);
         mbar_init(dfull, C::ISS);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -274,41 +290,36 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
     tmem_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    // Stage j (k range it0 + j) lives in TMA ring stage j % S_SM and tensor-
-    // memory A slot j % S_TM.  Phase parities below are those of the j-th use
-    // of each barrier; every wait is at most one phase away from the phase it
-    // observes (see the dequant note), which is what parity waits require.
+    // Stage j (k range it0 + j) lives in weight stage j % S_W, X stage
+    // j % S_X and tensor-memory A slot j % S_TM.  Phase parities below are
+    // those of the j-th use of each barrier; every wait is at most one phase
+    // away from the phase it observes (see the dequant note), which is what
+    // parity waits require.
     if (warp == 0) {
-        // ---------------- TMA producer
-        // The weight tiles of the first ring round do not depend on the
-        // previous kernel, so they are requested before the grid-dependency
-        // wait (launched as a programmatic dependent, this CTA may start while
-        // the kernel producing X is still running); X follows the wait.
+        // ---------------- weight producer.  The weights do not depend on the
+        // previous kernel, so (launched as a programmatic dependent) this CTA
+        // streams them while the kernel producing X may still be running.
         if (lane == 0) {
-            const int pre = nk < S_SM ? nk : S_SM;
-            for (int j = 0; j < pre; j++) {  // fresh ring: no sempty wait needed
-                mbar_expect_tx(&full[j], (uint32_t)(C::X_STAGE + C::W_STAGE + C::S_STAGE));
-                tma_load_2d(smem + C::w_off(j), &wmap, &full[j], (it0 + j) * BK / 2, n0);
-                tma_load_2d(smem + C::s_off(j), &smap, &full[j], 8 * ((it0 + j) >> 1), n0);
+            for (int j = 0; j < nk; j++) {
+                const int st = j % S_W;
+                if (j >= S_W && !mbar_wait(&wempty[st], ((uint32_t)(j / S_W) & 1u) ^ 1u, &abort_flag)) break;
+                mbar_expect_tx(&wfull[st], (uint32_t)(C::W_STAGE + C::S_STAGE));
+                tma_load_2d(smem + C::w_off(st), &wmap, &wfull[st], (it0 + j) * BK / 2, n0);
+                tma_load_2d(smem + C::s_off(st), &smap, &wfull[st], 8 * ((it0 + j) >> 1), n0);
             }
+        }
+    } else if (warp == 2) {
+        // ---------------- X producer (after the grid dependency)
+        if (lane == 0) {
             grid_dependency_wait();
-            for (int j = 0; j < pre; j++) {
-                uint8_t* xs = smem + C::x_off(j);
-                int kk = (it0 + j) * BK;
-                tma_load_2d(xs, &xmap, &full[j], kk, t0);
-                tma_load_2d(xs + TN * 128, &xmap, &full[j], kk + 64, t0);
-            }
-            for (int j = pre; j < nk; j++) {
-                const int st = j % S_SM;
-                const uint32_t ph = (uint32_t)(j / S_SM) & 1u;
-                if (!mbar_wait(&sempty[st], ph ^ 1u, &abort_flag)) break;
-                mbar_expect_tx(&full[st], (uint32_t)(C::X_STAGE + C::W_STAGE + C::S_STAGE));
+            for (int j = 0; j < nk; j++) {
+                const int st = j % S_X;
+                if (j >= S_X && !mbar_wait(&mdone[st], ((uint32_t)(j / S_X) & 1u) ^ 1u, &abort_flag)) break;
+                mbar_expect_tx(&xfull[st], (uint32_t)C::X_STAGE);
                 uint8_t* xs = smem + C::x_off(st);
-                int kk = (it0 + j) * BK;
-                tma_load_2d(xs, &xmap, &full[st], kk, t0);
-                tma_load_2d(xs + TN * 128, &xmap, &full[st], kk + 64, t0);
-                tma_load_2d(smem + C::w_off(st), &wmap, &full[st], kk / 2, n0);
-                tma_load_2d(smem + C::s_off(st), &smap, &full[st], 8 * ((it0 + j) >> 1), n0);
+                const int kk = (it0 + j) * BK;
+                tma_load_2d(xs, &xmap, &xfull[st], kk, t0);
+                tma_load_2d(xs + TN * 128, &xmap, &xfull[st], kk + 64, t0);
             }
         }
     } else if (warp == 1 || (C::ISS == 2 && warp == 3)) {
@@ -316,10 +327,10 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
         // [i * 8 / ISS, (i + 1) * 8 / ISS) of every stage into accumulator
         // D_i (columns [i TN, (i + 1) TN)).
         // The tcgen05 fence that must follow each barrier wait stalls the
-        // issuing thread, so every stage that is already dequantized when the
-        // oldest one is (up to MMA_BATCH) is taken under a single wait + fence.
-        // A slot observed here cannot be a phase ahead (its next fill needs
-        // this thread's MMA of it).
+        // issuing thread, so every stage that is already dequantized (and
+        // whose X has landed) when the oldest one is, up to MMA_BATCH, is
+        // taken under a single wait + fence.  A slot or X stage observed here
+        // cannot be a phase ahead (its next fill needs this thread's MMA of it).
         if (lane == 0) {
             constexpr uint32_t idesc = make_idesc(TN);
             constexpr int KSTEPS = BK / 16 / C::ISS;
@@ -327,17 +338,19 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
             const uint32_t d_tmem = tmem + (uint32_t)(iss * TN);
             bool ok = true;
             for (int j = 0; j < nk;) {
-                if (!mbar_wait(&aready[j % S_TM], (uint32_t)(j / S_TM) & 1u, &abort_flag)) {
+                if (!mbar_wait(&xfull[j % S_X], (uint32_t)(j / S_X) & 1u, &abort_flag) ||
+                    !mbar_wait(&aready[j % S_TM], (uint32_t)(j / S_TM) & 1u, &abort_flag)) {
                     ok = false;
                     break;
                 }
                 int cnt = 1;
                 while (cnt < C::MMA_BATCH && j + cnt < nk &&
-                       mbar_try_wait(&aready[(j + cnt) % S_TM], (uint32_t)((j + cnt) / S_TM) & 1u))
+                       mbar_try_wait(&aready[(j + cnt) % S_TM], (uint32_t)((j + cnt) / S_TM) & 1u) &&
+                       mbar_try_wait(&xfull[(j + cnt) % S_X], (uint32_t)((j + cnt) / S_X) & 1u))
                     cnt++;
                 tmem_fence_after();
                 for (int b = 0; b < cnt; b++, j++) {
-                    const int st = j % S_SM, a = j % S_TM;
+                    const int st = j % S_X, a = j % S_TM;
                     const uint32_t xs = smem_u32(smem + C::x_off(st));
 #pragma unroll
                     for (int k2 = 0; k2 < KSTEPS; k2++) {
@@ -346,7 +359,7 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
                         uint32_t b_addr = xs + (uint32_t)((kk >> 2) * TN * 128 + (kk & 3) * 32);
                         mma_f16_ts(d_tmem, a_tmem, sw128_desc(b_addr), idesc, (j > 0 || k2 > 0) ? 1u : 0u);
                     }
-                    mma_commit(&sempty[st]);  // frees the TMA stage and (S_TM | S_SM) the A slot
+                    mma_commit(&mdone[st]);  // frees the X stage and (S_TM | S_X) the A slot
                 }
             }
             if (ok) mma_commit(dfull);
@@ -355,13 +368,17 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
         // ---------------- dequant: thread <-> weight row (TMEM lane).  The
         // dequant warpgroups form RR groups; group g converts the stages j
         // with j % RR == g (each of its WG_PER warpgroups 4 / WG_PER of the
-        // stage's Q4_0 blocks), so RR stages are in flight at once.  RR <= S_TM
-        // and RR <= S_SM keep every group within one barrier phase of the
-        // others: a group reaching stage j has finished j - RR, which needed
-        // the MMA of j - RR - S_TM and the TMA of j - RR (itself issued after
-        // the MMA of j - RR - S_SM), so the phases a wait can observe are the
-        // awaited one and the one before it (parity waits cannot tell phases
-        // two apart).
+        // stage's Q4_0 blocks), so RR stages are in flight at once.  Parity
+        // waits cannot tell phases two apart, so each wait below must find its
+        // barrier in the awaited phase or the one after it:
+        //  * mdone of stage j - S_TM: its previous phase (stage j - S_TM - S_X)
+        //    completed before this group finished stage j - RR (RR <= S_X);
+        //    its next phase (stage j - S_TM + S_X >= j) needs the dequant of
+        //    stage j first (one group in order, or S_X == S_TM).
+        //  * wfull of stage j: the mdone wait before it (S_W >= S_TM) means
+        //    the MMAs up to stage j - S_TM, hence the dequant and the weight
+        //    load of stage j - S_W, are done; its next phase needs this
+        //    group's release of stage j.
         const int wg = (warp - 4) >> 2;
         const int g = wg / C::WG_PER;
         const int part = wg % C::WG_PER;
@@ -371,14 +388,12 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
         const bool row_ok = n < N;
         bool ok = true;
         for (int j = g; j < nk; j += C::RR) {
-            const int st = j % S_SM, a = j % S_TM;
+            const int st = j % S_W, a = j % S_TM;
             // A slot a was last read by the MMAs of stage j - S_TM, whose
-            // completion is phase (j - S_TM) / S_SM of that stage's sempty
-            // barrier (S_TM divides S_SM, so the slot and the stage are freed
-            // by the same commit)
+            // completion is phase (j - S_TM) / S_X of mdone[(j - S_TM) % S_X]
             if ((j >= S_TM &&
-                 !warp_wait(&sempty[(j - S_TM) % S_SM], (uint32_t)((j - S_TM) / S_SM) & 1u, &abort_flag)) ||
-                !warp_wait(&full[st], (uint32_t)(j / S_SM) & 1u, &abort_flag)) {
+                 !warp_wait(&mdone[(j - S_TM) % S_X], (uint32_t)((j - S_TM) / S_X) & 1u, &abort_flag)) ||
+                !warp_wait(&wfull[st], (uint32_t)(j / S_W) & 1u, &abort_flag)) {
                 ok = false;
                 break;
             }
@@ -396,14 +411,22 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
 #pragma unroll
             for (int hh = 0; hh < BLK_PER / PER_ST; hh++) {
                 uint32_t v[16 * PER_ST];
+                uint4 q4[PER_ST];
+#pragma unroll
+                for (int bb = 0; bb < PER_ST; bb++)
+                    q4[bb] = *reinterpret_cast<const uint4*>(wrow + (((blk0 + hh * PER_ST + bb) ^ sw) << 4));
+                if (hh == BLK_PER / PER_ST - 1) {
+                    // the warp's last read of the weight stage: release it
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&wempty[st]);
+                }
 #pragma unroll
                 for (int bb = 0; bb < PER_ST; bb++) {
                     const int blk = blk0 + hh * PER_ST + bb;
-                    uint4 q4 = *reinterpret_cast<const uint4*>(wrow + ((blk ^ sw) << 4));
                     uint32_t s32 = (blk < 2) ? sc.x : sc.y;
                     uint32_t s16 = (blk & 1) ? (s32 >> 16) : (s32 & 0xFFFFu);
                     __half2 s2 = __half2half2(__ushort_as_half((unsigned short)s16));
-                    const uint32_t w4[4] = {q4.x, q4.y, q4.z, q4.w};
+                    const uint32_t w4[4] = {q4[bb].x, q4[bb].y, q4[bb].z, q4[bb].w};
 #pragma unroll
                     for (int wd = 0; wd < 4; wd++)
 #pragma unroll
@@ -461,6 +484,7 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
     tmem_fence_before();
     __syncthreads();
     if (warp == 2) {
+        __syncwarp();  // lane 0 ran the X producer
         tmem_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::COLS) : "memory");
     }
@@ -559,6 +583,8 @@ struct GemmWorkspace {
     int device = -1;
     // (nibble plane, scale plane, n, k) -> nibble and scale tensor maps
     std::map<std::tuple<const void*, const void*, size_t, size_t>, std::pair<CUtensorMap, CUtensorMap>> wmaps;
+    // [token tile 32/64/128/256][splits] -> CTAs resident at once (0: not yet queried)
+    int slots[4][MAX_SPLITS + 1] = {};
 };
 
 GemmWorkspace* gemm_workspace_new() { return new GemmWorkspace(); }
@@ -578,17 +604,60 @@ bool gemm_tc_eligible(const hc_q4_matrix& w, size_t tokens) {
 }
 
 namespace {
+// Dynamic shared memory of a launch.  A 512-column CTA asks for at least
+// 116 KB, so it is alone on its SM; the 256-column (decode) CTAs fit two per
+// SM and never three (their shared memory), so tensor-memory allocation never
+// waits.
+template <int TN>
+int launch_smem() {
+    using C = Cfg<TN>;
+    static_assert(C::smem() <= 232448, "shared memory budget");
+    return (!C::DUAL && C::smem() < 118784) ? 118784 : C::smem();
+}
+
+// CTAs of the kernel resident at once when the splits of a tile form a
+// cluster of `sp` CTAs.  A cluster must fit within one GPC, so with large
+// clusters fewer CTAs than (blocks per SM x SMs) run together, and a grid of
+// clusters beyond that number runs a second wave.
+template <int TN>
+int resident_ctas(int sp) {
+    using C = Cfg<TN>;
+    auto kfn = k_q4_gemm_tc<TN>;
+    const int smem = launch_smem<TN>();
+    int dev = 0, nsm = 0, nb = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kfn, C::THREADS, (size_t)smem) != cudaSuccess || nb < 1) {
+        (void)cudaGetLastError();
+        return 148 * C::MIN_BLOCKS;
+    }
+    if (sp == 1) return nb * nsm;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1, 1, (unsigned)sp);
+    cfg.blockDim = dim3(C::THREADS);
+    cfg.dynamicSmemBytes = (size_t)smem;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 1;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = (unsigned)sp;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int nc = 0;
+    if (cudaOccupancyMaxActiveClusters(&nc, kfn, &cfg) != cudaSuccess || nc < 1) {
+        (void)cudaGetLastError();
+        return nb * nsm;
+    }
+    return nc * sp;
+}
+
 template <int TN>
 int launch_tc(const hc_q4_matrix& w, const CUtensorMap& xmap, const CUtensorMap& wmap, const CUtensorMap& smap,
               size_t T, float* y,
               size_t ldy, int epi, const float* res, size_t ldres, int splits, int* err, cudaStream_t s) {
     using C = Cfg<TN>;
-    static_assert(C::smem() <= 232448, "shared memory budget");
     auto kfn = k_q4_gemm_tc<TN>;
-    // A 512-column CTA asks for at least 116 KB of shared memory, so it is
-    // alone on its SM; the 256-column (decode) CTAs fit two per SM and never
-    // three (their shared memory), so tensor-memory allocation never waits.
-    const int smem = (!C::DUAL && C::smem() < 118784) ? 118784 : C::smem();
+    const int smem = launch_smem<TN>();
     HC_CUDA(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     HC_CHECK(splits >= 1 && splits <= MAX_SPLITS, HC_ERR_INVALID, "tcgen05 GEMM: %d K splits", splits);
     cudaLaunchConfig_t cfg = {};
@@ -620,14 +689,16 @@ int launch_tc(const hc_q4_matrix& w, const CUtensorMap& xmap, const CUtensorMap&
 
 // K splits per tile (1..MAX_SPLITS) minimizing a simple time model in units
 // of one pipeline stage: waves x (fixed cost of a CTA + its stages), plus
-// the cluster reduction when split.  The fixed cost (pipeline fill, tensor-
-// memory setup, epilogue) is worth about 11 stages.
-int choose_splits(size_t tiles, size_t nk, size_t slots) {
+// the cluster reduction when split; slots[sp] = CTAs resident at once with
+// clusters of sp.  The fixed cost (pipeline fill, tensor-memory setup,
+// epilogue) is worth about 11 stages.
+int choose_splits(size_t tiles, size_t nk, const int* slots) {
     const double fixed = 11.0, reduce = 3.0;
     int best = 1;
     double best_cost = 1e300;
     for (size_t sp = 1; sp <= (size_t)MAX_SPLITS && (sp == 1 || nk / sp >= 2); sp++) {
-        size_t waves = (tiles * sp + slots - 1) / slots;
+        const size_t sl = (size_t)(slots[sp] > 0 ? slots[sp] : 1);
+        size_t waves = (tiles * sp + sl - 1) / sl;
         double cost = (double)waves * (fixed + (double)((nk + sp - 1) / sp)) + (sp > 1 ? reduce : 0.0);
         if (cost < best_cost - 1e-9) {
             best_cost = cost;
@@ -635,6 +706,14 @@ int choose_splits(size_t tiles, size_t nk, size_t slots) {
         }
     }
     return best;
+}
+
+template <int TN>
+const int* tile_slots(GemmWorkspace* ws, int ti) {
+    int* sl = ws->slots[ti];
+    if (!sl[1])
+        for (int sp = 1; sp <= MAX_SPLITS; sp++) sl[sp] = resident_ctas<TN>(sp);
+    return sl;
 }
 }  // namespace
 
@@ -649,6 +728,8 @@ int gemm_tc(GemmWorkspace* ws, const hc_q4_matrix& w, const float* x, size_t ldx
         ws->xh_cap = 0;
         ws->err = nullptr;
         ws->wmaps.clear();
+        for (auto& row : ws->slots)
+            for (int& v : row) v = 0;
         ws->device = dev;
     }
     if (!ws->err) {
@@ -685,12 +766,24 @@ int gemm_tc(GemmWorkspace* ws, const hc_q4_matrix& w, const float* x, size_t ldx
         if (w.owns) ws->wmaps[key] = std::make_pair(wmap, smap);
     }
     size_t tiles = ((w.n + BM - 1) / BM) * ((T + tn - 1) / tn);
-    int splits = choose_splits(tiles, K / BK, tn <= 64 ? 148 * Cfg<32>::MIN_BLOCKS : 148);
+    const size_t nk = K / BK;
     switch (tn) {
-        case 32: return launch_tc<32>(w, xmap, wmap, smap, T, y, ldy, epi, res, ldres, splits, ws->err, s);
-        case 64: return launch_tc<64>(w, xmap, wmap, smap, T, y, ldy, epi, res, ldres, splits, ws->err, s);
-        case 128: return launch_tc<128>(w, xmap, wmap, smap, T, y, ldy, epi, res, ldres, splits, ws->err, s);
-        default: return launch_tc<256>(w, xmap, wmap, smap, T, y, ldy, epi, res, ldres, splits, ws->err, s);
+        case 32: {
+            int splits = choose_splits(tiles, nk, tile_slots<32>(ws, 0));
+            return launch_tc<32>(w, xmap, wmap, smap, T, y, ldy, epi, res, ldres, splits, ws->err, s);
+        }
+        case 64: {
+            int splits = choose_splits(tiles, nk, tile_slots<64>(ws, 1));
+            return launch_tc<64>(w, xmap, wmap, smap, T, y, ldy, epi, res, ldres, splits, ws->err, s);
+        }
+        case 128: {
+            int splits = choose_splits(tiles, nk, tile_slots<128>(ws, 2));
+            return launch_tc<128>(w, xmap, wmap, smap, T, y, ldy, epi, res, ldres, splits, ws->err, s);
+        }
+        default: {
+            int splits = choose_splits(tiles, nk, tile_slots<256>(ws, 3));
+            return launch_tc<256>(w, xmap, wmap, smap, T, y, ldy, epi, res, ldres, splits, ws->err, s);
+        }
     }
 }
 
@@ -705,6 +798,8 @@ int* gemm_error_flag(GemmWorkspace* ws) {
         ws->xh_cap = 0;
         ws->err = nullptr;
         ws->wmaps.clear();
+        for (auto& row : ws->slots)
+            for (int& v : row) v = 0;
         ws->device = dev;
     }
     if (!ws->err) {
