@@ -221,7 +221,7 @@ struct Cfg {
     static constexpr int A_COL = DUAL ? (ISS * TN < 64 ? 64 : ISS * TN) : TN;  // A slots start here; D_i at [i TN, (i+1) TN)
     static constexpr int S_TM = (COLS - A_COL) / 64 < S_X ? (COLS - A_COL) / 64 : S_X;  // A slots
     static constexpr int MMA_BATCH = S_TM < 4 ? S_TM : 4;   // stages issued under one wait + fence
-    static constexpr int RR = DUAL ? 1 : (S_TM >= 4 ? 4 : 2);  // dequant groups working on different stages
+    static constexpr int RR = DUAL ? 2 : (S_TM >= 4 ? 4 : 2);  // dequant groups working on different stages
     static constexpr int WG_PER = (DEQ_WARPS / 4) / RR;       // warpgroups per group, each 4 / WG_PER blocks
     __host__ __device__ static constexpr int x_off(int s) { return s * X_STAGE; }
     __host__ __device__ static constexpr int w_off(int s) { return S_X * X_STAGE + s * W_STAGE; }
@@ -234,7 +234,7 @@ struct Cfg {
     static_assert(ISS == 1 || ISS == 2, "one or two issuing warps");
     static_assert(S_X % S_TM == 0, "an A slot is freed by the MMA commit that frees an X stage");
     static_assert(RR <= S_TM && RR <= S_W, "dequant groups must not run more than one barrier phase apart");
-    static_assert(S_W >= S_TM && (RR == 1 || S_X == S_TM), "barrier phase ordering (see the dequant warps)");
+    static_assert(S_W >= S_TM && RR <= S_X, "barrier phase ordering (see the dequant warps)");
     static_assert(WG_PER == 1 || WG_PER == 2, "dequant split: 4 or 2 blocks per warpgroup");
     static_assert(!DUAL || 2 * (smem() + 1024) <= 233472, "two CTAs must fit in one SM's shared memory");
     static constexpr int RED_PITCH = TN + 1;                  // floats per row of the split-K partial tile
@@ -373,8 +373,8 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
         // barrier in the awaited phase or the one after it:
         //  * mdone of stage j - S_TM: its previous phase (stage j - S_TM - S_X)
         //    completed before this group finished stage j - RR (RR <= S_X);
-        //    its next phase (stage j - S_TM + S_X >= j) needs the dequant of
-        //    stage j first (one group in order, or S_X == S_TM).
+        //    its next phase is the MMA of stage j - S_TM + S_X >= j, which the
+        //    issuer (in stage order) cannot reach before this dequant of j.
         //  * wfull of stage j: the mdone wait before it (S_W >= S_TM) means
         //    the MMAs up to stage j - S_TM, hence the dequant and the weight
         //    load of stage j - S_W, are done; its next phase needs this
