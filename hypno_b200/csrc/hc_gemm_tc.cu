@@ -131,14 +131,13 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
     return r;
 }
 
-// f32 at shared-memory offset `local` (this CTA's address of it) in the CTA
-// of the cluster with the given rank.
-__device__ __forceinline__ float ld_dsmem_f32(uint32_t local, int rank) {
+
+// Store v at shared-memory offset `local` (this CTA's address of it) in the
+// CTA of the cluster with the given rank.
+__device__ __forceinline__ void st_dsmem_f32(uint32_t local, int rank, float v) {
     uint32_t remote;
-    float v;
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local), "r"(rank));
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
-    return v;
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote), "f"(v) : "memory");
 }
 
 // y[jj * ldy] = v[jj] (+ res[jj * ldres]) for jj < tl, one column of an
@@ -203,6 +202,7 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
 // slot j % S_TM.
 template <int TN>
 struct Cfg {
+    static constexpr int TN_ = TN;
     static constexpr bool DUAL = TN <= 64;                   // two CTAs per SM
     static constexpr int COLS = DUAL ? 256 : 512;            // tensor-memory columns per CTA
     static constexpr int DEQ_WARPS = DUAL ? 8 : 16;
@@ -215,14 +215,19 @@ struct Cfg {
     static constexpr int S_STAGE = BM * 16;
     static constexpr int S_X = DUAL ? (TN <= 32 ? 6 : 4) : (TN == 128 ? 5 : 3);  // X ring stages
     static constexpr int S_W = DUAL ? (TN <= 32 ? 6 : 4) : (TN == 128 ? 5 : 3);  // weight ring stages
-    // Decode CTAs issue their MMAs from two warps (one per 64-wide K half of
-    // each stage, each into its own accumulator, summed by the epilogue).
+    // Decode CTAs issue their MMAs from two warps taking alternate stages,
+    // each into its own accumulator (summed by the epilogue): every barrier
+    // wait, tcgen05 fence and commit holds the issuing thread for hundreds of
+    // cycles, so one issuer per stage halves that cost per weight.
     static constexpr int ISS = DUAL ? 2 : 1;
     static constexpr int A_COL = DUAL ? (ISS * TN < 64 ? 64 : ISS * TN) : TN;  // A slots start here; D_i at [i TN, (i+1) TN)
     static constexpr int S_TM = (COLS - A_COL) / 64 < S_X ? (COLS - A_COL) / 64 : S_X;  // A slots
     static constexpr int MMA_BATCH = S_TM < 4 ? S_TM : 4;   // stages issued under one wait + fence
     static constexpr int RR = DUAL ? 2 : (S_TM >= 4 ? 4 : 2);  // dequant groups working on different stages
     static constexpr int WG_PER = (DEQ_WARPS / 4) / RR;       // warpgroups per group, each 4 / WG_PER blocks
+    // decode tiles: the dequant warps wait for the weight stage before the A
+    // slot (the stage S_W back was this group's own, S_W % RR == 0)
+    static constexpr bool PRELOAD = DUAL;
     __host__ __device__ static constexpr int x_off(int s) { return s * X_STAGE; }
     __host__ __device__ static constexpr int w_off(int s) { return S_X * X_STAGE + s * W_STAGE; }
     __host__ __device__ static constexpr int s_off(int s) { return S_X * X_STAGE + S_W * W_STAGE + s * S_STAGE; }
@@ -232,14 +237,34 @@ struct Cfg {
     __host__ __device__ static constexpr int smem() { return bar_off() + NBARS * 8 + 16 + 1024; }
     static_assert(A_COL + 64 * S_TM <= COLS && ISS * TN <= A_COL, "tensor memory budget");
     static_assert(ISS == 1 || ISS == 2, "one or two issuing warps");
+    // two issuers: issuer i takes the stages j % 2 == i, fed by dequant group
+    // i (RR == 2); the phase arguments below need the ring sizes to respect
+    // the stage parity
+    static_assert(ISS == 1 || (RR == 2 && S_X % 2 == 0 && S_W % S_TM == 0), "alternating issuers");
     static_assert(S_X % S_TM == 0, "an A slot is freed by the MMA commit that frees an X stage");
     static_assert(RR <= S_TM && RR <= S_W, "dequant groups must not run more than one barrier phase apart");
-    static_assert(S_W >= S_TM && RR <= S_X, "barrier phase ordering (see the dequant warps)");
+    static_assert(S_W >= S_TM && RR <= S_X && (ISS == 1 || S_W % S_TM == 0), "barrier phase ordering (see the dequant warps)");
     static_assert(WG_PER == 1 || WG_PER == 2, "dequant split: 4 or 2 blocks per warpgroup");
+    static_assert(!PRELOAD || S_W % RR == 0, "weight-first waits (see the dequant warps)");
     static_assert(!DUAL || 2 * (smem() + 1024) <= 233472, "two CTAs must fit in one SM's shared memory");
-    static constexpr int RED_PITCH = TN + 1;                  // floats per row of the split-K partial tile
-    static_assert(BM * RED_PITCH * 4 <= ring_bytes(), "partial tile fits in the rings");
+    static constexpr int RED_PITCH = TN + 1;                  // floats per row of the split-K partial tiles
+    static_assert((BM + MAX_SPLITS) * RED_PITCH * 4 <= ring_bytes(), "split-K partials fit in the rings");
 };
+
+// Tokens [c0, c0 + EPI_CH) of TMEM lane quarter q of the accumulator (the sum
+// D_0 + D_1 when a second issuer wrote D_1).  Warp-collective.
+template <typename C>
+__device__ __forceinline__ void load_accumulators(uint32_t tmem, int q, int c0, int nk, uint32_t* v) {
+    tmem_ld_x16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
+    if (C::ISS == 2 && nk > 1) {  // issuer 1 wrote D_1
+        uint32_t v1[EPI_CH];
+        tmem_ld_x16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(C::TN_ + c0), v1);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+        for (int jj = 0; jj < EPI_CH; jj++) v[jj] = __float_as_uint(__uint_as_float(v[jj]) + __uint_as_float(v1[jj]));
+    }
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
 
 template <int TN>
 __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
@@ -258,6 +283,7 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
     uint64_t* dfull = aready + S_TM;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dfull + 1);
     __shared__ int abort_flag;
+    bool epi_ok = false;  // epilogue warpgroup: the accumulators are complete
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n0 = blockIdx.x * BM, t0 = blockIdx.y * TN, split = blockIdx.z;
@@ -273,7 +299,7 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
         }
         for (int st = 0; st < S_X; st++) {
             mbar_init(&xfull[st], 1);
-            mbar_init(&mdone[st], C::ISS);  // a commit of every issuer
+            mbar_init(&mdone[st], 1);  // the commit of the stage's issuer
         }
         for (int a = 0; a < S_TM; a++) mbar_init(&aready[a], 4 * C::WG_PER);
         mbar_init(dfull, C::ISS);
@@ -323,46 +349,54 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
             }
         }
     } else if (warp == 1 || (C::ISS == 2 && warp == 3)) {
-        // ---------------- MMA issuer(s): issuer i takes the K steps
-        // [i * 8 / ISS, (i + 1) * 8 / ISS) of every stage into accumulator
-        // D_i (columns [i TN, (i + 1) TN)).
+        // ---------------- MMA issuer(s): issuer i takes the stages
+        // j = i, i + ISS, ... (all eight K steps) into accumulator D_i
+        // (columns [i TN, (i + 1) TN)).
         // The tcgen05 fence that must follow each barrier wait stalls the
-        // issuing thread, so every stage that is already dequantized (and
-        // whose X has landed) when the oldest one is, up to MMA_BATCH, is
-        // taken under a single wait + fence.  A slot or X stage observed here
-        // cannot be a phase ahead (its next fill needs this thread's MMA of it).
+        // issuing thread; a single issuer therefore takes every stage that is
+        // already dequantized (and whose X has landed) when the oldest one is,
+        // up to MMA_BATCH, under a single wait + fence.
+        // Phases: an issuer's aready / xfull wait for stage j must find the
+        // barrier's previous phase (stage j - S_TM, resp. j - S_X) complete.
+        // With one issuer that stage was its own.  With two, stage j - S_X
+        // (S_X even) is its own; stage j - S_TM may be the other issuer's, so
+        // the issuer first waits for that stage's MMAs (mdone), which follow
+        // its aready.  The next phases need this issuer's MMA of stage j.
         if (lane == 0) {
             constexpr uint32_t idesc = make_idesc(TN);
-            constexpr int KSTEPS = BK / 16 / C::ISS;
+            constexpr int KSTEPS = BK / 16;
             const int iss = warp == 1 ? 0 : 1;
             const uint32_t d_tmem = tmem + (uint32_t)(iss * TN);
             bool ok = true;
-            for (int j = 0; j < nk;) {
-                if (!mbar_wait(&xfull[j % S_X], (uint32_t)(j / S_X) & 1u, &abort_flag) ||
+            for (int j = iss; j < nk;) {
+                if ((C::ISS == 2 && (S_TM & 1) && j >= S_TM &&
+                     !mbar_wait(&mdone[(j - S_TM) % S_X], (uint32_t)((j - S_TM) / S_X) & 1u, &abort_flag)) ||
+                    !mbar_wait(&xfull[j % S_X], (uint32_t)(j / S_X) & 1u, &abort_flag) ||
                     !mbar_wait(&aready[j % S_TM], (uint32_t)(j / S_TM) & 1u, &abort_flag)) {
                     ok = false;
                     break;
                 }
                 int cnt = 1;
-                while (cnt < C::MMA_BATCH && j + cnt < nk &&
-                       mbar_try_wait(&aready[(j + cnt) % S_TM], (uint32_t)((j + cnt) / S_TM) & 1u) &&
-                       mbar_try_wait(&xfull[(j + cnt) % S_X], (uint32_t)((j + cnt) / S_X) & 1u))
-                    cnt++;
+                if constexpr (C::ISS == 1) {
+                    while (cnt < C::MMA_BATCH && j + cnt < nk &&
+                           mbar_try_wait(&aready[(j + cnt) % S_TM], (uint32_t)((j + cnt) / S_TM) & 1u) &&
+                           mbar_try_wait(&xfull[(j + cnt) % S_X], (uint32_t)((j + cnt) / S_X) & 1u))
+                        cnt++;
+                }
                 tmem_fence_after();
-                for (int b = 0; b < cnt; b++, j++) {
+                for (int b = 0; b < cnt; b++, j += C::ISS) {
                     const int st = j % S_X, a = j % S_TM;
                     const uint32_t xs = smem_u32(smem + C::x_off(st));
 #pragma unroll
-                    for (int k2 = 0; k2 < KSTEPS; k2++) {
-                        const int kk = iss * KSTEPS + k2;
+                    for (int kk = 0; kk < KSTEPS; kk++) {
                         uint32_t a_tmem = tmem + (uint32_t)(C::A_COL + a * 64 + kk * 8);
                         uint32_t b_addr = xs + (uint32_t)((kk >> 2) * TN * 128 + (kk & 3) * 32);
-                        mma_f16_ts(d_tmem, a_tmem, sw128_desc(b_addr), idesc, (j > 0 || k2 > 0) ? 1u : 0u);
+                        mma_f16_ts(d_tmem, a_tmem, sw128_desc(b_addr), idesc, (j > iss || kk > 0) ? 1u : 0u);
                     }
                     mma_commit(&mdone[st]);  // frees the X stage and (S_TM | S_X) the A slot
                 }
             }
-            if (ok) mma_commit(dfull);
+            if (ok) mma_commit(dfull);  // also when this issuer had no stage
         }
     } else if (warp >= 4) {
         // ---------------- dequant: thread <-> weight row (TMEM lane).  The
@@ -371,13 +405,20 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
         // stage's Q4_0 blocks), so RR stages are in flight at once.  Parity
         // waits cannot tell phases two apart, so each wait below must find its
         // barrier in the awaited phase or the one after it:
+        // The dequant of stage j needs the MMA of j - S_TM, which needs the
+        // dequant of j - S_TM: the dequant of j follows that of every stage
+        // j - m S_TM.
         //  * mdone of stage j - S_TM: its previous phase (stage j - S_TM - S_X)
-        //    completed before this group finished stage j - RR (RR <= S_X);
-        //    its next phase is the MMA of stage j - S_TM + S_X >= j, which the
-        //    issuer (in stage order) cannot reach before this dequant of j.
-        //  * wfull of stage j: the mdone wait before it (S_W >= S_TM) means
-        //    the MMAs up to stage j - S_TM, hence the dequant and the weight
-        //    load of stage j - S_W, are done; its next phase needs this
+        //    completed before this group finished stage j - RR: that stage
+        //    waited for the MMA of j - RR - S_TM, which the same issuer (one
+        //    issuer, or S_X - RR even) issued after the earlier one;
+        //    its next phase is the MMA of stage j - S_TM + S_X, which (S_TM
+        //    divides S_X) follows the dequant of j.
+        //  * wfull of stage j: with PRELOAD, stage j - S_W was this group's
+        //    own (S_W % RR == 0) and its load was waited for; otherwise the
+        //    mdone wait before it means the dequant of stage j - S_TM, hence
+        //    (S_TM divides S_W, or one in-order issuer) that of j - S_W, is
+        //    done, so the load of j - S_W landed.  Its next phase needs this
         //    group's release of stage j.
         const int wg = (warp - 4) >> 2;
         const int g = wg / C::WG_PER;
@@ -387,11 +428,20 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
         const int n = n0 + r;
         const bool row_ok = n < N;
         bool ok = true;
+        constexpr int BLK_PER = 4 / C::WG_PER;  // Q4_0 blocks of the stage per thread
+        constexpr int PER_ST = 2;               // blocks per TMEM store
+        constexpr int NH = BLK_PER / PER_ST;
+        static_assert(BLK_PER % PER_ST == 0, "whole TMEM stores per warpgroup");
+        const int blk0 = part * BLK_PER;
+        const int sw = (r >> 1) & 3;  // 16-byte chunk c of row r is stored at chunk c ^ sw
         for (int j = g; j < nk; j += C::RR) {
             const int st = j % S_W, a = j % S_TM;
             // A slot a was last read by the MMAs of stage j - S_TM, whose
-            // completion is phase (j - S_TM) / S_X of mdone[(j - S_TM) % S_X]
-            if ((j >= S_TM &&
+            // completion is phase (j - S_TM) / S_X of mdone[(j - S_TM) % S_X].
+            // Decode tiles (PRELOAD) read and release the weight stage and
+            // convert its first blocks before they wait for the slot.
+            const bool slot_wait = j >= S_TM;
+            if ((!C::PRELOAD && slot_wait &&
                  !warp_wait(&mdone[(j - S_TM) % S_X], (uint32_t)((j - S_TM) / S_X) & 1u, &abort_flag)) ||
                 !warp_wait(&wfull[st], (uint32_t)(j / S_W) & 1u, &abort_flag)) {
                 ok = false;
@@ -399,26 +449,31 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
             }
             // the stage's 4 scales of row r (the scale box holds the stage pair's 8)
             const uint2 sc = *reinterpret_cast<const uint2*>(smem + C::s_off(st) + r * 16 + ((it0 + j) & 1) * 8);
-            // 64-byte rows of nibbles, 16-byte chunk c of row r stored at chunk c ^ ((r >> 1) & 3)
-            const uint8_t* wrow = smem + C::w_off(st) + r * (BK / 2);
-            const int sw = (r >> 1) & 3;
+            const uint8_t* wrow = smem + C::w_off(st) + r * (BK / 2);  // 64-byte rows of nibbles
             const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(C::A_COL + a * 64);
-            // Q4_0 blocks [blk0, blk0 + BLK_PER) of the stage, two per TMEM store
-            constexpr int BLK_PER = 4 / C::WG_PER;
-            constexpr int PER_ST = 2;
-            static_assert(BLK_PER % PER_ST == 0, "whole TMEM stores per warpgroup");
-            const int blk0 = part * BLK_PER;
+            uint4 q4[C::PRELOAD ? BLK_PER : PER_ST];
+            if constexpr (C::PRELOAD) {
 #pragma unroll
-            for (int hh = 0; hh < BLK_PER / PER_ST; hh++) {
+                for (int bb = 0; bb < BLK_PER; bb++)
+                    q4[bb] = *reinterpret_cast<const uint4*>(wrow + (((blk0 + bb) ^ sw) << 4));
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&wempty[st]);  // the warp's last read of the weight stage
+            }
+            bool okw = true;
+#pragma unroll
+            for (int hh = 0; hh < NH; hh++) {
                 uint32_t v[16 * PER_ST];
-                uint4 q4[PER_ST];
+                uint4 qv[PER_ST];
 #pragma unroll
-                for (int bb = 0; bb < PER_ST; bb++)
-                    q4[bb] = *reinterpret_cast<const uint4*>(wrow + (((blk0 + hh * PER_ST + bb) ^ sw) << 4));
-                if (hh == BLK_PER / PER_ST - 1) {
-                    // the warp's last read of the weight stage: release it
+                for (int bb = 0; bb < PER_ST; bb++) {
+                    if constexpr (C::PRELOAD)
+                        qv[bb] = q4[hh * PER_ST + bb];
+                    else
+                        qv[bb] = *reinterpret_cast<const uint4*>(wrow + (((blk0 + hh * PER_ST + bb) ^ sw) << 4));
+                }
+                if (!C::PRELOAD && hh == NH - 1) {
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&wempty[st]);
+                    if (lane == 0) mbar_arrive(&wempty[st]);  // the warp's last read of the weight stage
                 }
 #pragma unroll
                 for (int bb = 0; bb < PER_ST; bb++) {
@@ -426,14 +481,19 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
                     uint32_t s32 = (blk < 2) ? sc.x : sc.y;
                     uint32_t s16 = (blk & 1) ? (s32 >> 16) : (s32 & 0xFFFFu);
                     __half2 s2 = __half2half2(__ushort_as_half((unsigned short)s16));
-                    const uint32_t w4[4] = {q4[bb].x, q4[bb].y, q4[bb].z, q4[bb].w};
+                    const uint32_t w4[4] = {qv[bb].x, qv[bb].y, qv[bb].z, qv[bb].w};
 #pragma unroll
                     for (int wd = 0; wd < 4; wd++)
 #pragma unroll
                         for (int k = 0; k < 4; k++) v[bb * 16 + wd * 4 + k] = deq_pair(w4[wd], k, s2);
                 }
-                const uint32_t tcol = tbase + (uint32_t)((blk0 + hh * PER_ST) * 16);
-                tmem_st_x32(tcol, v);
+                if (C::PRELOAD && hh == 0 && slot_wait)
+                    okw = warp_wait(&mdone[(j - S_TM) % S_X], (uint32_t)((j - S_TM) / S_X) & 1u, &abort_flag);
+                if (okw) tmem_st_x32(tbase + (uint32_t)((blk0 + hh * PER_ST) * 16), v);
+            }
+            if (!okw) {
+                ok = false;
+                break;
             }
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             tmem_fence_before();
@@ -442,80 +502,82 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
         }
         // ---------------- epilogue (first warpgroup)
         if (wg == 0) {
-            bool okd = __all_sync(0xffffffffu, ok) && warp_wait(dfull, 0, &abort_flag);
+            epi_ok = __all_sync(0xffffffffu, ok) && warp_wait(dfull, 0, &abort_flag);
             grid_dependency_wait();  // y and the residual may be touched by the previous kernel
             // Every load of a 16-token chunk (residuals) is issued before the
             // first dependent add: one memory round trip per chunk.
-            if (okd) {
+            if (epi_ok && splits == 1) {
                 tmem_fence_after();
-                // split K: this CTA's partial tile goes to its own shared memory
-                // (the TMA stages are idle now: every load was consumed and
-                // every MMA reading them has completed), row-major with an odd
-                // row pitch so both the row-per-thread writes here and the
-                // token-fastest reads of the reduction are conflict-free
-                float* red = reinterpret_cast<float*>(smem);
 #pragma unroll 1
                 for (int c0 = 0; c0 < TN; c0 += EPI_CH) {
                     uint32_t v[EPI_CH];
-                    tmem_ld_x16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
-                    if constexpr (C::ISS == 2) {
-                        uint32_t v1[EPI_CH];
-                        tmem_ld_x16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(TN + c0), v1);
-                        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-                        for (int jj = 0; jj < EPI_CH; jj++)
-                            v[jj] = __float_as_uint(__uint_as_float(v[jj]) + __uint_as_float(v1[jj]));
-                    }
-                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                    if (splits > 1) {
-#pragma unroll
-                        for (int jj = 0; jj < EPI_CH; jj++) red[r * C::RED_PITCH + c0 + jj] = __uint_as_float(v[jj]);
-                    } else {
-                        const int tl = min(EPI_CH, T - (t0 + c0));  // tokens of this chunk
-                        if (row_ok && tl > 0)
-                            store_chunk(y + (size_t)(t0 + c0) * ldy + n, ldy, v, tl,
-                                        (epi == EPI_ADD && res) ? res + (size_t)(t0 + c0) * ldres + n : nullptr,
-                                        ldres);
-                    }
+                    load_accumulators<C>(tmem, q, c0, nk, v);
+                    const int tl = min(EPI_CH, T - (t0 + c0));  // tokens of this chunk
+                    if (row_ok && tl > 0)
+                        store_chunk(y + (size_t)(t0 + c0) * ldy + n, ldy, v, tl,
+                                    (epi == EPI_ADD && res) ? res + (size_t)(t0 + c0) * ldres + n : nullptr,
+                                    ldres);
                 }
             }
         }
     }
     tmem_fence_before();
     __syncthreads();
+    // Split K: the splits of a tile form one thread-block cluster.  Rows of
+    // the tile are divided among the cluster's CTAs (rank R owns rows
+    // [rows R / splits, rows (R + 1) / splits)); after a cluster barrier (every
+    // CTA is past its main loop, so its rings are free) each CTA stores its
+    // partial sums of every row into the owner's shared memory over the
+    // cluster (posted stores, no round trips), and after a second barrier each
+    // owner adds the splits' partials of its rows in split order, so the
+    // result is deterministic and no partial sum leaves the chip.  Every CTA
+    // reaches both barriers, also after an abort (the error flag then reports
+    // the garbage).
+    const int rows = min(BM, N - n0), toks = min(TN, T - t0);
+    const int slab = (BM + splits - 1) / splits;  // >= rows owned by any rank
+    const uint32_t recv = smem_u32(smem);         // [split][slab][RED_PITCH] floats
+    if (splits > 1) {
+        cluster_sync();
+        if (warp >= 4 && warp < 8 && epi_ok) {
+            tmem_fence_after();
+            const int q = warp & 3, r = q * 32 + lane;
+            const bool has_row = r < rows;
+            int owner = 0;
+            while (has_row && owner + 1 < splits && rows * (owner + 1) / splits <= r) owner++;
+            const uint32_t row_addr =
+                recv + (uint32_t)(((split * slab + (has_row ? r - rows * owner / splits : 0)) * C::RED_PITCH) * 4);
+#pragma unroll 1
+            for (int c0 = 0; c0 < TN; c0 += EPI_CH) {
+                uint32_t v[EPI_CH];
+                load_accumulators<C>(tmem, q, c0, nk, v);  // warp-collective
+                if (has_row) {
+#pragma unroll
+                    for (int jj = 0; jj < EPI_CH; jj++)
+                        st_dsmem_f32(row_addr + (uint32_t)((c0 + jj) * 4), owner, __uint_as_float(v[jj]));
+                }
+            }
+        }
+        tmem_fence_before();
+        __syncthreads();
+    }
     if (warp == 2) {
         __syncwarp();  // lane 0 ran the X producer
         tmem_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::COLS) : "memory");
     }
     if (splits > 1) {
-        // The splits of a tile form one thread-block cluster.  After the
-        // cluster barrier every CTA reduces a slab of the tile's rows, adding
-        // the ranks' partial tiles in rank (= split) order through
-        // distributed shared memory, so the result is deterministic and no
-        // partial sum leaves the chip.  Every CTA reaches both barriers, also
-        // after an abort (the error flag then reports the garbage).
-        cluster_sync();
+        cluster_sync();  // every partial has landed
         grid_dependency_wait();
-        const uint32_t red_local = smem_u32(smem);
-        const int rows = min(BM, N - n0), toks = min(TN, T - t0);
         const int rank = (int)cluster_ctarank();
         const int r0 = rows * rank / splits, r1 = rows * (rank + 1) / splits, nr = r1 - r0;
+        const float* rv = reinterpret_cast<const float*>(smem);
         for (int o = threadIdx.x; o < nr * toks; o += C::THREADS) {
-            const int rr = r0 + o % nr, t = o / nr;
-            const uint32_t off = (uint32_t)((rr * C::RED_PITCH + t) * 4);
-            float pv[MAX_SPLITS];
-#pragma unroll
-            for (int sp = 0; sp < MAX_SPLITS; sp++) pv[sp] = sp < splits ? ld_dsmem_f32(red_local + off, sp) : 0.0f;
+            const int rr = o % nr, t = o / nr;
             float acc = 0.0f;
-#pragma unroll
-            for (int sp = 0; sp < MAX_SPLITS; sp++)
-                if (sp < splits) acc += pv[sp];
-            const size_t yi = (size_t)(t0 + t) * ldy + n0 + rr;
-            if (epi == EPI_ADD && res) acc = acc + res[(size_t)(t0 + t) * ldres + n0 + rr];
-            y[yi] = acc;
+            for (int sp = 0; sp < splits; sp++) acc += rv[(sp * slab + rr) * C::RED_PITCH + t];
+            if (epi == EPI_ADD && res) acc = acc + res[(size_t)(t0 + t) * ldres + n0 + r0 + rr];
+            y[(size_t)(t0 + t) * ldy + n0 + r0 + rr] = acc;
         }
-        cluster_sync();  // peers finished reading this CTA's partial tile
     }
     if (threadIdx.x == 0 && abort_flag) atomicExch(err, 1);
 }
