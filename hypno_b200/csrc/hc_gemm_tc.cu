@@ -237,6 +237,7 @@ struct Cfg {
     __host__ __device__ static constexpr int smem() { return bar_off() + NBARS * 8 + 16 + 1024; }
     static_assert(A_COL + 64 * S_TM <= COLS && ISS * TN <= A_COL, "tensor memory budget");
     static_assert(ISS == 1 || ISS == 2, "one or two issuing warps");
+    static_assert(MMA_BATCH >= 1 && MMA_BATCH <= S_TM, "batched stages each need their own A slot");
     // two issuers: issuer i takes the stages j % 2 == i, fed by dequant group
     // i (RR == 2); the phase arguments below need the ring sizes to respect
     // the stage parity
@@ -749,19 +750,24 @@ int launch_tc(const hc_q4_matrix& w, const CUtensorMap& xmap, const CUtensorMap&
     return HC_OK;
 }
 
-// K splits per tile (1..MAX_SPLITS) minimizing a simple time model in units
-// of one pipeline stage: waves x (fixed cost of a CTA + its stages), plus
-// the cluster reduction when split; slots[sp] = CTAs resident at once with
-// clusters of sp.  The fixed cost (pipeline fill, tensor-memory setup,
-// epilogue) is worth about 11 stages.
-int choose_splits(size_t tiles, size_t nk, const int* slots) {
-    const double fixed = 11.0, reduce = 3.0;
+// K splits per tile (1..MAX_SPLITS) minimizing a time model in units of one
+// pipeline stage (measured on decode shapes): a CTA costs a fixed ~10 stages
+// (launch, pipeline fill, epilogue) plus its stages, which run ~1.67x slower
+// when two CTAs share an SM (`dual` kernels with more CTAs than SMs); a split
+// tile adds the cluster barriers and the reduction (~7 stages for two
+// splits, ~10 up to four, ~15 up to eight); slots[sp] = CTAs resident at once
+// with clusters of sp, so CTAs beyond it run in further waves.
+int choose_splits(size_t tiles, size_t nk, const int* slots, int nsm, bool dual) {
+    const double fixed = 10.0, shared = 1.67;
     int best = 1;
     double best_cost = 1e300;
     for (size_t sp = 1; sp <= (size_t)MAX_SPLITS && (sp == 1 || nk / sp >= 2); sp++) {
         const size_t sl = (size_t)(slots[sp] > 0 ? slots[sp] : 1);
-        size_t waves = (tiles * sp + sl - 1) / sl;
-        double cost = (double)waves * (fixed + (double)((nk + sp - 1) / sp)) + (sp > 1 ? reduce : 0.0);
+        const size_t ctas = tiles * sp;
+        const size_t waves = (ctas + sl - 1) / sl;
+        const double pace = (dual && ctas > (size_t)nsm) ? shared : 1.0;
+        const double reduce = sp == 1 ? 0.0 : sp == 2 ? 7.0 : sp <= 4 ? 10.0 : 15.0;
+        const double cost = (double)waves * (fixed + pace * (double)((nk + sp - 1) / sp)) + reduce;
         if (cost < best_cost - 1e-9) {
             best_cost = cost;
             best = (int)sp;
@@ -829,21 +835,23 @@ int gemm_tc(GemmWorkspace* ws, const hc_q4_matrix& w, const float* x, size_t ldx
     }
     size_t tiles = ((w.n + BM - 1) / BM) * ((T + tn - 1) / tn);
     const size_t nk = K / BK;
+    int nsm = 148;
+    HC_CUDA(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
     switch (tn) {
         case 32: {
-            int splits = choose_splits(tiles, nk, tile_slots<32>(ws, 0));
+            int splits = choose_splits(tiles, nk, tile_slots<32>(ws, 0), nsm, Cfg<32>::DUAL);
             return launch_tc<32>(w, xmap, wmap, smap, T, y, ldy, epi, res, ldres, splits, ws->err, s);
         }
         case 64: {
-            int splits = choose_splits(tiles, nk, tile_slots<64>(ws, 1));
+            int splits = choose_splits(tiles, nk, tile_slots<64>(ws, 1), nsm, Cfg<64>::DUAL);
             return launch_tc<64>(w, xmap, wmap, smap, T, y, ldy, epi, res, ldres, splits, ws->err, s);
         }
         case 128: {
-            int splits = choose_splits(tiles, nk, tile_slots<128>(ws, 2));
+            int splits = choose_splits(tiles, nk, tile_slots<128>(ws, 2), nsm, Cfg<128>::DUAL);
             return launch_tc<128>(w, xmap, wmap, smap, T, y, ldy, epi, res, ldres, splits, ws->err, s);
         }
         default: {
-            int splits = choose_splits(tiles, nk, tile_slots<256>(ws, 3));
+            int splits = choose_splits(tiles, nk, tile_slots<256>(ws, 3), nsm, Cfg<256>::DUAL);
             return launch_tc<256>(w, xmap, wmap, smap, T, y, ldy, epi, res, ldres, splits, ws->err, s);
         }
     }
