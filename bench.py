@@ -61,14 +61,56 @@ def measured_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle sampling during the timed region."""
+    """SM clock / clock-event-reason sampling during the timed region: an NVML
+    polling thread (every 5 ms, read-only queries) writing one CSV line per
+    sample, so that even a timed region of a few tens of milliseconds has
+    samples; nvidia-smi when NVML is unavailable."""
 
-    def __init__(self, index, path):
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+               ("sw_power_cap", 0x4))
+
+    def __init__(self, index, path, period_s=0.005):
         self.path = path
-        self.proc = None
         self.index = index
+        self.period = period_s
+        self.proc = None
+        self.thread = None
+        self.rows = []
+
+    def _handle(self, nv):
+        try:
+            import torch
+            p = torch.cuda.get_device_properties(self.index)
+            bus = f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0"
+            return nv.nvmlDeviceGetHandleByPciBusId(bus.encode())
+        except Exception:
+            return nv.nvmlDeviceGetHandleByIndex(self.index)
 
     def __enter__(self):
+        try:
+            import threading
+            import pynvml as nv
+            nv.nvmlInit()
+            h = self._handle(nv)
+            smax = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            self.stop = threading.Event()
+
+            def poll():
+                while not self.stop.is_set():
+                    try:
+                        sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                        rs = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                        pw = nv.nvmlDeviceGetPowerUsage(h) / 1000.0
+                        self.rows.append((float(sm), float(smax), int(rs), pw))
+                    except Exception:
+                        pass
+                    self.stop.wait(self.period)
+
+            self.thread = threading.Thread(target=poll, daemon=True)
+            self.thread.start()
+            return self
+        except Exception:
+            self.thread = None
         q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -82,6 +124,16 @@ class ClockSampler:
         return self
 
     def __exit__(self, *a):
+        if self.thread is not None:
+            self.stop.set()
+            self.thread.join(timeout=5)
+            try:
+                with open(self.path, "w") as f:
+                    f.write("sm_mhz,sm_max_mhz,reasons_mask,power_w\n")
+                    for r in self.rows:
+                        f.write(f"{r[0]:.0f},{r[1]:.0f},{r[2]:#x},{r[3]:.1f}\n")
+            except OSError:
+                pass
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -91,6 +143,13 @@ class ClockSampler:
             self.f.close()
 
     def summary(self):
+        if self.thread is not None:
+            if not self.rows:
+                return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "source": "nvml"}
+            sm = sorted(r[0] for r in self.rows)
+            reasons = sorted({n for r in self.rows for n, bit in self.REASONS if r[2] & bit})
+            return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": max(r[1] for r in self.rows), "reasons": reasons,
+                    "samples": len(self.rows), "source": "nvml"}
         if self.proc is None or not os.path.exists(self.path):
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         rows = []

@@ -19,6 +19,13 @@ bool gemm_tc_eligible(const hc_q4_matrix& w, size_t tokens);
 int gemm_tc(GemmWorkspace* ws, const hc_q4_matrix& w, const float* x, size_t ldx, size_t tokens, float* y,
             size_t ldy, int epi, const float* res, size_t ldres, cudaStream_t s, const __half* xh_ready = nullptr);
 
+// The same product with K split over up to max_splits CTAs per tile whose
+// partial products are NOT added here: split i writes its [tokens][n] slab
+// at part + i * tokens * n; *splits reports how many slabs were written (the
+// caller adds them in slab order, e.g. launch_residual_splits_norm).
+int gemm_tc_partials(GemmWorkspace* ws, const hc_q4_matrix& w, const float* x, size_t ldx, size_t tokens,
+                     float* part, int max_splits, int* splits, cudaStream_t s, const __half* xh_ready = nullptr);
+
 // Index of element e of a row in the GEMM's fp16 K order.
 __host__ __device__ inline int perm_k(int e) { return (e & ~7) | ((e & 3) << 1) | ((e >> 2) & 1); }
 

@@ -159,20 +159,29 @@ __device__ __forceinline__ void store_chunk(float* y, size_t ldy, const uint32_t
 }
 
 // K order inside a 32-element Q4_0 block.  Word i (4 bytes = elements
-// 8i..8i+7, low nibble first) yields four fp16 pairs with one shift and one
-// and/or each: pair k = (element 8i+k, element 8i+k+4).  The A operand (the
-// weights) is therefore laid out along K in the order
+// 8i..8i+7, low nibble first) yields four fp16 pairs: pair k = (element
+// 8i+k, element 8i+k+4), i.e. bits [4k, 4k+4) and [16+4k, 16+4k+4).  The A
+// operand (the weights) is therefore laid out along K in the order
 //   position 8i+2k <- element 8i+k,   position 8i+2k+1 <- element 8i+k+4,
 // and the B operand (the activations) is written in the same order by
 // k_rows_to_f16_perm, so every dot product sees matching pairs.
-// (nib + 1024) is exact in fp16 (0x6400 | nib); subtracting 1032 is exact;
-// multiplying by the fp16 scale rounds once: fp16((nib - 8) * scale).
-__device__ __forceinline__ uint32_t deq_pair(uint32_t w, int k, __half2 s2) {
-    uint32_t v = ((w >> (4 * k)) & 0x000F000Fu) | 0x64006400u;
-    __half2 h = *reinterpret_cast<__half2*>(&v);
-    h = __hsub2(h, __float2half2_rn(1032.0f));
-    h = __hmul2(h, s2);
-    return *reinterpret_cast<uint32_t*>(&h);
+// Pairs 0 and 2 (the low nibble of a byte pair) become (nib + 1024) with one
+// and/or, exact in fp16 (0x6400 | nib), minus 1032; pairs 1 and 3 are taken
+// in place as (16 nib + 1024) and turned into nib - 8 by one fma with 1/16
+// and -72, both exact; multiplying by the fp16 scale then rounds once:
+// fp16((nib - 8) * scale).  One shift serves the word's upper bytes.
+__device__ __forceinline__ void deq_word(uint32_t w, __half2 s2, uint32_t* out) {
+    const uint32_t hi = w >> 8;
+    uint32_t v[4] = {(w & 0x000F000Fu) | 0x64006400u, (w & 0x00F000F0u) | 0x64006400u,
+                     (hi & 0x000F000Fu) | 0x64006400u, (hi & 0x00F000F0u) | 0x64006400u};
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        __half2 h = *reinterpret_cast<__half2*>(&v[k]);
+        h = (k & 1) ? __hfma2(h, __float2half2_rn(0.0625f), __float2half2_rn(-72.0f))
+                    : __hsub2(h, __float2half2_rn(1032.0f));
+        h = __hmul2(h, s2);
+        out[k] = *reinterpret_cast<uint32_t*>(&h);
+    }
 }
 
 // Warp-uniform bounded wait: lane 0 polls, the verdict is broadcast, then
@@ -271,7 +280,7 @@ template <int TN>
 __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
     k_q4_gemm_tc(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
                  const __grid_constant__ CUtensorMap smap, float* __restrict__ y, size_t ldy, const float* res, size_t ldres,
-                 int epi, int N, int K, int T, int splits, int* __restrict__ err) {
+                 int epi, int N, int K, int T, int splits, size_t split_stride, int* __restrict__ err) {
     using C = Cfg<TN>;
     constexpr int S_X = C::S_X, S_W = C::S_W, S_TM = C::S_TM;
     extern __shared__ uint8_t smem_raw[];
@@ -484,9 +493,7 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
                     __half2 s2 = __half2half2(__ushort_as_half((unsigned short)s16));
                     const uint32_t w4[4] = {qv[bb].x, qv[bb].y, qv[bb].z, qv[bb].w};
 #pragma unroll
-                    for (int wd = 0; wd < 4; wd++)
-#pragma unroll
-                        for (int k = 0; k < 4; k++) v[bb * 16 + wd * 4 + k] = deq_pair(w4[wd], k, s2);
+                    for (int wd = 0; wd < 4; wd++) deq_word(w4[wd], s2, &v[bb * 16 + wd * 4]);
                 }
                 if (C::PRELOAD && hh == 0 && slot_wait)
                     okw = warp_wait(&mdone[(j - S_TM) % S_X], (uint32_t)((j - S_TM) / S_X) & 1u, &abort_flag);
@@ -507,17 +514,20 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
             grid_dependency_wait();  // y and the residual may be touched by the previous kernel
             // Every load of a 16-token chunk (residuals) is issued before the
             // first dependent add: one memory round trip per chunk.
-            if (epi_ok && splits == 1) {
+            // split_stride > 0: split `split` stores its partial product to
+            // its own slab y + split * split_stride (the caller adds the slabs)
+            if (epi_ok && (splits == 1 || split_stride)) {
                 tmem_fence_after();
+                float* ys = y + (size_t)split * split_stride;
+                const bool add = epi == EPI_ADD && res && !split_stride;
 #pragma unroll 1
                 for (int c0 = 0; c0 < TN; c0 += EPI_CH) {
                     uint32_t v[EPI_CH];
                     load_accumulators<C>(tmem, q, c0, nk, v);
                     const int tl = min(EPI_CH, T - (t0 + c0));  // tokens of this chunk
                     if (row_ok && tl > 0)
-                        store_chunk(y + (size_t)(t0 + c0) * ldy + n, ldy, v, tl,
-                                    (epi == EPI_ADD && res) ? res + (size_t)(t0 + c0) * ldres + n : nullptr,
-                                    ldres);
+                        store_chunk(ys + (size_t)(t0 + c0) * ldy + n, ldy, v, tl,
+                                    add ? res + (size_t)(t0 + c0) * ldres + n : nullptr, ldres);
                 }
             }
         }
@@ -537,7 +547,8 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
     const int rows = min(BM, N - n0), toks = min(TN, T - t0);
     const int slab = (BM + splits - 1) / splits;  // >= rows owned by any rank
     const uint32_t recv = smem_u32(smem);         // [split][slab][RED_PITCH] floats
-    if (splits > 1) {
+    const bool cluster_reduce = splits > 1 && split_stride == 0;
+    if (cluster_reduce) {
         cluster_sync();
         if (warp >= 4 && warp < 8 && epi_ok) {
             tmem_fence_after();
@@ -566,7 +577,7 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
         tmem_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::COLS) : "memory");
     }
-    if (splits > 1) {
+    if (cluster_reduce) {
         cluster_sync();  // every partial has landed
         grid_dependency_wait();
         const int rank = (int)cluster_ctarank();
@@ -583,7 +594,7 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
     if (threadIdx.x == 0 && abort_flag) atomicExch(err, 1);
 }
 
-// fp32 rows -> fp16 rows in the K order of the weight tiles (see deq_pair):
+// fp32 rows -> fp16 rows in the K order of the weight tiles (see deq_word):
 // within every 8 elements, [e0 e4 e1 e5 e2 e6 e3 e7].
 __global__ void k_rows_to_f16_perm(const float* __restrict__ x, size_t ldx, __half* __restrict__ out, int K, int T) {
     pdl_trigger();
@@ -717,7 +728,8 @@ int resident_ctas(int sp) {
 template <int TN>
 int launch_tc(const hc_q4_matrix& w, const CUtensorMap& xmap, const CUtensorMap& wmap, const CUtensorMap& smap,
               size_t T, float* y,
-              size_t ldy, int epi, const float* res, size_t ldres, int splits, int* err, cudaStream_t s) {
+              size_t ldy, int epi, const float* res, size_t ldres, int splits, int* err, cudaStream_t s,
+              size_t split_stride = 0) {
     using C = Cfg<TN>;
     auto kfn = k_q4_gemm_tc<TN>;
     const int smem = launch_smem<TN>();
@@ -735,7 +747,7 @@ int launch_tc(const hc_q4_matrix& w, const CUtensorMap& xmap, const CUtensorMap&
     attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[na].val.programmaticStreamSerializationAllowed = 1;
     na++;
-    if (splits > 1) {  // the splits of one tile form a cluster (reduction over distributed shared memory)
+    if (splits > 1 && split_stride == 0) {  // the splits of one tile form a cluster (reduction in shared memory)
         attr[na].id = cudaLaunchAttributeClusterDimension;
         attr[na].val.clusterDim.x = 1;
         attr[na].val.clusterDim.y = 1;
@@ -745,7 +757,7 @@ int launch_tc(const hc_q4_matrix& w, const CUtensorMap& xmap, const CUtensorMap&
     cfg.attrs = attr;
     cfg.numAttrs = (unsigned)na;
     HC_CUDA(cudaLaunchKernelEx(&cfg, kfn, xmap, wmap, smap, y, ldy, res, ldres, epi, (int)w.n,
-                               (int)w.k, (int)T, splits, err));
+                               (int)w.k, (int)T, splits, split_stride, err));
     hc_count_launch();
     return HC_OK;
 }
@@ -757,16 +769,25 @@ int launch_tc(const hc_q4_matrix& w, const CUtensorMap& xmap, const CUtensorMap&
 // tile adds the cluster barriers and the reduction (~7 stages for two
 // splits, ~10 up to four, ~15 up to eight); slots[sp] = CTAs resident at once
 // with clusters of sp, so CTAs beyond it run in further waves.
-int choose_splits(size_t tiles, size_t nk, const int* slots, int nsm, bool dual) {
+// With max_part > 0 the splits are not reduced in a cluster but written as
+// slabs the caller adds (up to max_part of them): no cluster residency limit,
+// and each extra slab costs the consumer about half a stage of reading.
+int choose_splits(size_t tiles, size_t nk, const int* slots, int nsm, bool dual, int max_part = 0) {
     const double fixed = 10.0, shared = 1.67;
+    const int max_sp = max_part > 0 ? std::min(max_part, MAX_SPLITS) : MAX_SPLITS;
     int best = 1;
     double best_cost = 1e300;
-    for (size_t sp = 1; sp <= (size_t)MAX_SPLITS && (sp == 1 || nk / sp >= 2); sp++) {
-        const size_t sl = (size_t)(slots[sp] > 0 ? slots[sp] : 1);
+    for (size_t sp = 1; sp <= (size_t)max_sp && (sp == 1 || nk / sp >= 2); sp++) {
+        const int sl_raw = max_part > 0 ? slots[1] : slots[sp];
+        const size_t sl = (size_t)(sl_raw > 0 ? sl_raw : 1);
         const size_t ctas = tiles * sp;
         const size_t waves = (ctas + sl - 1) / sl;
         const double pace = (dual && ctas > (size_t)nsm) ? shared : 1.0;
-        const double reduce = sp == 1 ? 0.0 : sp == 2 ? 7.0 : sp <= 4 ? 10.0 : 15.0;
+        const double reduce = max_part > 0 ? 0.5 * (double)(sp - 1)
+                              : sp == 1    ? 0.0
+                              : sp == 2    ? 7.0
+                              : sp <= 4    ? 10.0
+                                           : 15.0;
         const double cost = (double)waves * (fixed + pace * (double)((nk + sp - 1) / sp)) + reduce;
         if (cost < best_cost - 1e-9) {
             best_cost = cost;
@@ -785,8 +806,10 @@ const int* tile_slots(GemmWorkspace* ws, int ti) {
 }
 }  // namespace
 
-int gemm_tc(GemmWorkspace* ws, const hc_q4_matrix& w, const float* x, size_t ldx, size_t tokens, float* y,
-            size_t ldy, int epi, const float* res, size_t ldres, cudaStream_t s, const __half* xh_ready) {
+namespace {
+int gemm_tc_impl(GemmWorkspace* ws, const hc_q4_matrix& w, const float* x, size_t ldx, size_t tokens, float* y,
+                 size_t ldy, int epi, const float* res, size_t ldres, cudaStream_t s, const __half* xh_ready,
+                 int max_part, int* splits_out) {
     std::lock_guard<std::mutex> lock(ws->mu);
     const size_t K = w.k, T = tokens;
     int dev = 0;
@@ -837,24 +860,40 @@ int gemm_tc(GemmWorkspace* ws, const hc_q4_matrix& w, const float* x, size_t ldx
     const size_t nk = K / BK;
     int nsm = 148;
     HC_CUDA(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
+    const size_t stride = max_part > 0 ? T * ldy : 0;  // slab stride in partial mode
+    int splits = 1;
     switch (tn) {
-        case 32: {
-            int splits = choose_splits(tiles, nk, tile_slots<32>(ws, 0), nsm, Cfg<32>::DUAL);
-            return launch_tc<32>(w, xmap, wmap, smap, T, y, ldy, epi, res, ldres, splits, ws->err, s);
-        }
-        case 64: {
-            int splits = choose_splits(tiles, nk, tile_slots<64>(ws, 1), nsm, Cfg<64>::DUAL);
-            return launch_tc<64>(w, xmap, wmap, smap, T, y, ldy, epi, res, ldres, splits, ws->err, s);
-        }
-        case 128: {
-            int splits = choose_splits(tiles, nk, tile_slots<128>(ws, 2), nsm, Cfg<128>::DUAL);
-            return launch_tc<128>(w, xmap, wmap, smap, T, y, ldy, epi, res, ldres, splits, ws->err, s);
-        }
-        default: {
-            int splits = choose_splits(tiles, nk, tile_slots<256>(ws, 3), nsm, Cfg<256>::DUAL);
-            return launch_tc<256>(w, xmap, wmap, smap, T, y, ldy, epi, res, ldres, splits, ws->err, s);
-        }
+        case 32:
+            splits = choose_splits(tiles, nk, tile_slots<32>(ws, 0), nsm, Cfg<32>::DUAL, max_part);
+            HC_TRY(launch_tc<32>(w, xmap, wmap, smap, T, y, ldy, epi, res, ldres, splits, ws->err, s, stride));
+            break;
+        case 64:
+            splits = choose_splits(tiles, nk, tile_slots<64>(ws, 1), nsm, Cfg<64>::DUAL, max_part);
+            HC_TRY(launch_tc<64>(w, xmap, wmap, smap, T, y, ldy, epi, res, ldres, splits, ws->err, s, stride));
+            break;
+        case 128:
+            splits = choose_splits(tiles, nk, tile_slots<128>(ws, 2), nsm, Cfg<128>::DUAL, max_part);
+            HC_TRY(launch_tc<128>(w, xmap, wmap, smap, T, y, ldy, epi, res, ldres, splits, ws->err, s, stride));
+            break;
+        default:
+            splits = choose_splits(tiles, nk, tile_slots<256>(ws, 3), nsm, Cfg<256>::DUAL, max_part);
+            HC_TRY(launch_tc<256>(w, xmap, wmap, smap, T, y, ldy, epi, res, ldres, splits, ws->err, s, stride));
+            break;
     }
+    if (splits_out) *splits_out = splits;
+    return HC_OK;
+}
+}  // namespace
+
+int gemm_tc(GemmWorkspace* ws, const hc_q4_matrix& w, const float* x, size_t ldx, size_t tokens, float* y,
+            size_t ldy, int epi, const float* res, size_t ldres, cudaStream_t s, const __half* xh_ready) {
+    return gemm_tc_impl(ws, w, x, ldx, tokens, y, ldy, epi, res, ldres, s, xh_ready, 0, nullptr);
+}
+
+int gemm_tc_partials(GemmWorkspace* ws, const hc_q4_matrix& w, const float* x, size_t ldx, size_t tokens,
+                     float* part, int max_splits, int* splits, cudaStream_t s, const __half* xh_ready) {
+    HC_CHECK(max_splits >= 1 && splits, HC_ERR_INVALID, "gemm_tc_partials: max_splits %d", max_splits);
+    return gemm_tc_impl(ws, w, x, ldx, tokens, part, w.n, EPI_STORE, nullptr, 0, s, xh_ready, max_splits, splits);
 }
 
 uint64_t gemm_generation(GemmWorkspace* ws) { return ws ? ws->generation : 0; }

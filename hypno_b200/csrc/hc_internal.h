@@ -88,6 +88,12 @@ int launch_matmul(const DevWeight& w, const float* x, size_t ldx, size_t mtok, f
 
 // Row-wise RMSNorm (kernels.rs:592-625): out[r] = x[r] * inv_rms(x[r]) * w.
 // out16 (may be null): the same rows in fp16, in the tensor-core GEMM's K order.
+// hidden[r] += sum of the split slabs part[i][r] (slab order; slab i at
+// part + i * rows * n), then, when w is given, xn[r] = RMSNorm(hidden[r]) * w
+// and its fp16 copy in GEMM K order (xn16 may be null).
+bool residual_splits_norm_ok(size_t n, size_t ldh, size_t ldxn);
+int launch_residual_splits_norm(const float* part, int splits, size_t rows, size_t n, float* hidden, size_t ldh,
+                                const float* w, float eps, float* xn, size_t ldxn, __half* xn16, cudaStream_t s);
 int launch_rmsnorm(const float* x, size_t ldx, const float* w, float* out, size_t ldo, size_t rows,
                    size_t n, float eps, cudaStream_t s, __half* out16 = nullptr);
 int launch_softmax_rows(float* x, size_t rows, size_t n, cudaStream_t s);

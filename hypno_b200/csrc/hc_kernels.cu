@@ -565,6 +565,102 @@ int launch_rmsnorm(const float* x, size_t ldx, const float* w, float* out, size_
     return HC_OK;
 }
 
+// ============================================================ split-K slabs + residual + RMSNorm
+// hidden[row] += (part[0][row] + part[1][row] + ... + part[S-1][row]) (slab
+// order, then the residual: the reference's `hidden[i] = residual[i] +
+// proj[i]`, transformer.rs:561-563, 595-598), then, when w is given,
+// xn[row] = RMSNorm(hidden[row]) * w and its fp16 copy in GEMM K order
+// (rms_norm_fused, kernels.rs:592-625).  One CTA per row.
+template <int VPT>
+__global__ void k_residual_splits_norm(const float* __restrict__ part, int splits, size_t slab, float* hidden,
+                                       size_t ldh, const float* __restrict__ w, float* __restrict__ xn, size_t ldxn,
+                                       __half* __restrict__ xn16, int n, float eps) {
+    pdl_trigger();
+    __shared__ float red[32];
+    const size_t row = blockIdx.x;
+    const int n4 = n / 4;
+    float4* hrow = reinterpret_cast<float4*>(hidden + row * ldh);
+    const float4* prow = reinterpret_cast<const float4*>(part + row * (size_t)n);
+    float4 v[VPT];
+    float ss = 0.0f;
+#pragma unroll
+    for (int j = 0; j < VPT; j++) {
+        const int i = threadIdx.x + j * blockDim.x;
+        if (i < n4) {
+            float4 acc = prow[i];
+            for (int sp = 1; sp < splits; sp++) {
+                const float4 q = prow[(size_t)sp * (slab / 4) + i];
+                acc.x = acc.x + q.x;
+                acc.y = acc.y + q.y;
+                acc.z = acc.z + q.z;
+                acc.w = acc.w + q.w;
+            }
+            float4 r = hrow[i];
+            r.x = acc.x + r.x;
+            r.y = acc.y + r.y;
+            r.z = acc.z + r.z;
+            r.w = acc.w + r.w;
+            hrow[i] = r;
+            v[j] = r;
+        } else {
+            v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        ss = fmaf(v[j].x, v[j].x, ss);
+        ss = fmaf(v[j].y, v[j].y, ss);
+        ss = fmaf(v[j].z, v[j].z, ss);
+        ss = fmaf(v[j].w, v[j].w, ss);
+    }
+    if (!w) return;  // uniform over the grid
+    ss = block_sum(ss, red);
+    const float ms = __fdiv_rn(ss, (float)n);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
+    const float4* wr = reinterpret_cast<const float4*>(w);
+    float4* orow = reinterpret_cast<float4*>(xn + row * ldxn);
+#pragma unroll
+    for (int j = 0; j < VPT; j++) {
+        const int i = threadIdx.x + j * blockDim.x;
+        if (i < n4) {
+            float4 ww = wr[i], o;
+            o.x = __fmul_rn(__fmul_rn(v[j].x, inv), ww.x);
+            o.y = __fmul_rn(__fmul_rn(v[j].y, inv), ww.y);
+            o.z = __fmul_rn(__fmul_rn(v[j].z, inv), ww.z);
+            o.w = __fmul_rn(__fmul_rn(v[j].w, inv), ww.w);
+            orow[i] = o;
+            if (xn16) {
+                __half* r16 = xn16 + row * (size_t)n;
+                r16[perm_k(4 * i)] = __float2half_rn(o.x);
+                r16[perm_k(4 * i + 1)] = __float2half_rn(o.y);
+                r16[perm_k(4 * i + 2)] = __float2half_rn(o.z);
+                r16[perm_k(4 * i + 3)] = __float2half_rn(o.w);
+            }
+        }
+    }
+}
+
+bool residual_splits_norm_ok(size_t n, size_t ldh, size_t ldxn) {
+    return n % 4 == 0 && ldh % 4 == 0 && ldxn % 4 == 0 && n <= 2 * 1024 * 4;
+}
+
+int launch_residual_splits_norm(const float* part, int splits, size_t rows, size_t n, float* hidden, size_t ldh,
+                                const float* w, float eps, float* xn, size_t ldxn, __half* xn16, cudaStream_t s) {
+    if (rows == 0) return HC_OK;
+    HC_CHECK(splits >= 1 && residual_splits_norm_ok(n, ldh, ldxn) && ((uintptr_t)part & 15) == 0 &&
+                 ((uintptr_t)hidden & 15) == 0 && (!w || ((uintptr_t)w & 15) == 0) && (!w || ((uintptr_t)xn & 15) == 0),
+             HC_ERR_INVALID, "residual_splits_norm: unsupported layout (n %zu)", n);
+    const size_t n4 = n / 4;
+    const unsigned threads = (unsigned)std::min<size_t>(1024, ((n4 + 31) / 32) * 32);
+    const size_t vpt = (n4 + threads - 1) / threads;
+    const size_t slab = rows * n;
+    if (vpt <= 1)
+        k_residual_splits_norm<1><<<(unsigned)rows, threads, 0, s>>>(part, splits, slab, hidden, ldh, w, xn, ldxn, xn16,
+                                                                     (int)n, eps);
+    else
+        k_residual_splits_norm<2><<<(unsigned)rows, threads, 0, s>>>(part, splits, slab, hidden, ldh, w, xn, ldxn, xn16,
+                                                                     (int)n, eps);
+    HC_LAUNCH_CHECK();
+    return HC_OK;
+}
+
 // ============================================================ softmax rows
 // softmax_fast (kernels.rs:631-668), one CTA per row.
 __global__ void k_softmax_rows(float* __restrict__ x, int n) {

@@ -185,6 +185,9 @@ struct LayerW {
     float* post_norm = nullptr;
 };
 
+constexpr size_t kPartRows = 256;  // largest row count (decode batch) using split-K slabs
+constexpr int kPartSplits = 8;      // most slabs one projection writes
+
 struct Scratch {
     uint64_t generation = 0;  // bumped whenever a buffer moves
     size_t cap_tokens = 0, cap_logit_rows = 0;
@@ -197,6 +200,7 @@ struct Scratch {
     int* rowpos = nullptr;
     uint32_t* argmax = nullptr;
     float* tp_tmp = nullptr;      // [tokens][hidden] partial sums to all-reduce
+    float* split_part = nullptr;  // [kPartSplits][min(tokens, kPartRows)][hidden] split-K slabs
     float* tp_gather = nullptr;   // [tp][rows][vocab_shard] gathered logits
     // grouped decode attention workspace
     size_t attn_cap = 0;
@@ -382,6 +386,7 @@ void free_model(hc_model* m) {
         if (p) cudaFree(p);
     if (m->gemm_ws) hc::gemm_workspace_free(m->gemm_ws);
     if (m->sc.tp_tmp) cudaFree(m->sc.tp_tmp);
+    if (m->sc.split_part) cudaFree(m->sc.split_part);
     if (m->sc.tp_gather) cudaFree(m->sc.tp_gather);
     if (m->par) hc::peer_ar_free(m->par, m->cfg.tp_rank, m->cfg.tp_size);
     if (m->comm) hc::comm_free(m->comm);
@@ -417,6 +422,11 @@ int ensure_scratch(hc_model* m, size_t tokens, size_t logit_rows) {
         if (s.tp_tmp) cudaFree(s.tp_tmp);
         s.tp_tmp = nullptr;
         if (m->cfg.tp_size > 1) HC_CUDA(cudaMalloc((void**)&s.tp_tmp, t * c.hidden_size * sizeof(float)));
+        if (s.split_part) cudaFree(s.split_part);
+        s.split_part = nullptr;
+        if (m->cfg.tp_size <= 1)
+            HC_CUDA(cudaMalloc((void**)&s.split_part,
+                               (size_t)kPartSplits * std::min(t, kPartRows) * c.hidden_size * sizeof(float)));
         HC_CUDA(cudaMalloc((void**)&s.ids, t * sizeof(uint32_t)));
         HC_CUDA(cudaMalloc((void**)&s.seqs, t * sizeof(int)));
         HC_CUDA(cudaMalloc((void**)&s.rowpos, t * sizeof(int)));
@@ -491,7 +501,21 @@ int row_parallel(hc_model* m, const DevWeight& w, const float* x, size_t ldx, si
     const size_t H = m->cfg.hidden_size;
     Scratch& s = m->sc;
     if (normed) *normed = false;
-    if (m->cfg.tp_size <= 1) return matmul(m, w, x, ldx, rows, s.hidden, H, hc::EPI_ADD, s.hidden, H, x16);
+    if (m->cfg.tp_size <= 1) {
+        // decode sizes: K split over CTAs whose partial slabs are added by the
+        // residual + next-RMSNorm kernel (no cluster reduction in the GEMM)
+        if (s.split_part && rows <= kPartRows && w.dtype == HC_DTYPE_Q4_0 && hc::gemm_tc_eligible(w.q4, rows) &&
+            hc::residual_splits_norm_ok(H, H, H)) {
+            int splits = 1;
+            HC_TRY(hc::gemm_tc_partials(m->gemm_ws, w.q4, x, ldx, rows, s.split_part, kPartSplits, &splits, m->stream,
+                                        x16));
+            HC_TRY(hc::launch_residual_splits_norm(s.split_part, splits, rows, H, s.hidden, H, next_norm,
+                                                   m->cfg.rms_norm_eps, s.xn, H, s.xn16, m->stream));
+            if (normed) *normed = next_norm != nullptr;
+            return HC_OK;
+        }
+        return matmul(m, w, x, ldx, rows, s.hidden, H, hc::EPI_ADD, s.hidden, H, x16);
+    }
     HC_CHECK(m->comm, HC_ERR_STATE, "tensor-parallel model used before hc_comm_init");
     if (m->par && hc::peer_ar_fits(m->par, rows, H)) {
         float* part = hc::peer_ar_partial(m->par);
