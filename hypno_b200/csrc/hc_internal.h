@@ -101,6 +101,12 @@ int launch_silu(float* x, size_t n, cudaStream_t s);
 // act[r][i] = silu(gu[r][i]) * gu[r][im + i]
 int launch_silu_mul(const float* gu, size_t ldgu, float* act, size_t ldact, size_t rows, size_t im,
                     cudaStream_t s, __half* act16 = nullptr);
+// x[row] = sum of the split slabs part[i][row] (slab order; slab i at part +
+// i * rows * width, `width` elements per row), the first `heads` heads then
+// rotated as launch_rope_rows does.
+int launch_rope_rows_slabs(const float* part, int splits, float* x, size_t ldx, size_t rows, size_t width,
+                           size_t heads, size_t hd, const float2* cs, size_t cs_rows, const int* pos_dev, int pos0,
+                           cudaStream_t s);
 // Rotation of `heads` adjacent-pair heads per row at position pos0 + row
 // using a (max_pos x hd/2) cos/sin table.
 int launch_rope_rows(float* x, size_t ldx, size_t rows, size_t heads, size_t hd, const float2* cs, size_t cs_rows,

@@ -758,6 +758,52 @@ int launch_rope_rows(float* x, size_t ldx, size_t rows, size_t heads, size_t hd,
     return HC_OK;
 }
 
+// The same rotation applied while adding the split-K slabs of the qkv
+// projection: x[row][e] = sum over slabs (slab order) of part[i][row][e] for
+// the row's `width` elements, rotated for the first `heads` heads (q and k;
+// v is only summed).  Slab i starts at part + i * rows * width.
+__global__ void k_rope_rows_slabs(const float* __restrict__ part, int splits, size_t slab, float* __restrict__ x,
+                                  size_t ldx, int width, int heads, int hd, const float2* __restrict__ cs, int cs_rows,
+                                  const int* __restrict__ pos_dev, int pos0) {
+    const int row = blockIdx.y;
+    const int pos = pos_dev ? pos_dev[row] : pos0 + row;
+    const bool rot_ok = pos >= 0 && pos < cs_rows;  // else the position is rejected elsewhere
+    const int half = hd / 2;
+    const float2* pr = reinterpret_cast<const float2*>(part + (size_t)row * width);
+    float2* xr = reinterpret_cast<float2*>(x + (size_t)row * ldx);
+    for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < width / 2; p += gridDim.x * blockDim.x) {
+        float2 v = pr[p];
+        for (int sp = 1; sp < splits; sp++) {
+            const float2 q = pr[(size_t)sp * (slab / 2) + p];
+            v.x = v.x + q.x;
+            v.y = v.y + q.y;
+        }
+        const int h = p / half, i = p % half;
+        if (h < heads && rot_ok) {
+            const float2 c = cs[(size_t)pos * half + i];
+            const float a = v.x, b = v.y;
+            v.x = __fsub_rn(__fmul_rn(a, c.x), __fmul_rn(b, c.y));
+            v.y = __fadd_rn(__fmul_rn(a, c.y), __fmul_rn(b, c.x));
+        }
+        xr[p] = v;
+    }
+}
+
+int launch_rope_rows_slabs(const float* part, int splits, float* x, size_t ldx, size_t rows, size_t width,
+                           size_t heads, size_t hd, const float2* cs, size_t cs_rows, const int* pos_dev, int pos0,
+                           cudaStream_t s) {
+    if (rows == 0) return HC_OK;
+    HC_CHECK(splits >= 1 && width % 2 == 0 && hd % 2 == 0 && ldx % 2 == 0 && heads * hd <= width &&
+                 ((uintptr_t)part & 7) == 0 && ((uintptr_t)x & 7) == 0,
+             HC_ERR_INVALID, "rope_rows_slabs: unsupported layout");
+    const size_t pairs = width / 2;
+    const unsigned gx = (unsigned)std::min<size_t>((pairs + 127) / 128, 64);
+    k_rope_rows_slabs<<<dim3(gx, (unsigned)rows), 128, 0, s>>>(part, splits, rows * width, x, ldx, (int)width,
+                                                               (int)heads, (int)hd, cs, (int)cs_rows, pos_dev, pos0);
+    HC_LAUNCH_CHECK();
+    return HC_OK;
+}
+
 // ============================================================ embedding
 // transformer.rs:477-500 / turbo.rs:40-66 / quant.rs:139-153.
 __global__ void k_embed(uint32_t dtype, const void* __restrict__ dense, const uint4* __restrict__ qs,

@@ -200,7 +200,7 @@ struct Scratch {
     int* rowpos = nullptr;
     uint32_t* argmax = nullptr;
     float* tp_tmp = nullptr;      // [tokens][hidden] partial sums to all-reduce
-    float* split_part = nullptr;  // [kPartSplits][min(tokens, kPartRows)][hidden] split-K slabs
+    float* split_part = nullptr;  // [kPartSplits][min(tokens, kPartRows)][max(hidden, qkv)] split-K slabs
     float* tp_gather = nullptr;   // [tp][rows][vocab_shard] gathered logits
     // grouped decode attention workspace
     size_t attn_cap = 0;
@@ -424,9 +424,9 @@ int ensure_scratch(hc_model* m, size_t tokens, size_t logit_rows) {
         if (m->cfg.tp_size > 1) HC_CUDA(cudaMalloc((void**)&s.tp_tmp, t * c.hidden_size * sizeof(float)));
         if (s.split_part) cudaFree(s.split_part);
         s.split_part = nullptr;
-        if (m->cfg.tp_size <= 1)
-            HC_CUDA(cudaMalloc((void**)&s.split_part,
-                               (size_t)kPartSplits * std::min(t, kPartRows) * c.hidden_size * sizeof(float)));
+        HC_CUDA(cudaMalloc((void**)&s.split_part, (size_t)kPartSplits * std::min(t, kPartRows) *
+                                                      std::max<size_t>(c.hidden_size, m->nq + 2 * m->nk) *
+                                                      sizeof(float)));
         HC_CUDA(cudaMalloc((void**)&s.ids, t * sizeof(uint32_t)));
         HC_CUDA(cudaMalloc((void**)&s.seqs, t * sizeof(int)));
         HC_CUDA(cudaMalloc((void**)&s.rowpos, t * sizeof(int)));
@@ -593,9 +593,19 @@ int run_layers(hc_model* m, hc_kv* kv, size_t rows, bool prefill, int seq, int p
         if (!xn_ready)
             HC_TRY(hc::launch_rmsnorm(s.hidden, H, L.in_norm, s.xn, H, rows, H, c.rms_norm_eps, m->stream, s.xn16));
         xn_ready = false;
-        HC_TRY(matmul(m, L.qkv, s.xn, H, rows, s.qkv, ldqkv, hc::EPI_STORE, nullptr, 0, s.xn16));
-        HC_TRY(hc::launch_rope_rows(s.qkv, ldqkv, rows, nh_l + nkv_l, hd, m->rope, m->rope_rows,
-                                    prefill ? nullptr : s.rowpos, pos0, m->stream));
+        if (s.split_part && rows <= kPartRows && L.qkv.dtype == HC_DTYPE_Q4_0 &&
+            hc::gemm_tc_eligible(L.qkv.q4, rows)) {
+            // decode sizes: K split over CTAs into slabs that the RoPE kernel adds
+            int splits = 1;
+            HC_TRY(hc::gemm_tc_partials(m->gemm_ws, L.qkv.q4, s.xn, H, rows, s.split_part, kPartSplits, &splits,
+                                        m->stream, s.xn16));
+            HC_TRY(hc::launch_rope_rows_slabs(s.split_part, splits, s.qkv, ldqkv, rows, ldqkv, nh_l + nkv_l, hd,
+                                              m->rope, m->rope_rows, prefill ? nullptr : s.rowpos, pos0, m->stream));
+        } else {
+            HC_TRY(matmul(m, L.qkv, s.xn, H, rows, s.qkv, ldqkv, hc::EPI_STORE, nullptr, 0, s.xn16));
+            HC_TRY(hc::launch_rope_rows(s.qkv, ldqkv, rows, nh_l + nkv_l, hd, m->rope, m->rope_rows,
+                                        prefill ? nullptr : s.rowpos, pos0, m->stream));
+        }
         size_t lofs = li * kv->layer_stride * (kv->kv_fp16 ? 2 : 4);
         void* kc = (uint8_t*)kv->k + lofs;
         void* vc = (uint8_t*)kv->v + lofs;
