@@ -382,6 +382,151 @@ __device__ __forceinline__ void da_pv(const KT* __restrict__ vbase, const float*
     }
 }
 
+// ---- Staged variants (the whole-context kernel): each lane copies its own
+// 16-byte chunks of the next row groups into a per-warp shared-memory ring
+// with cp.async (no registers held while the copies are in flight), so two
+// stages of U row groups are in flight per warp instead of one.  A lane only
+// reads back what it copied itself, so its own cp.async.wait_group is the
+// only synchronisation.
+constexpr int DA_NS = 2;  // stages of the per-warp ring
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, int bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+                 "l"(src), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// uint4 slots of one warp's ring
+template <typename KT, int G, int HD>
+__host__ __device__ constexpr int da_ring_u4() { return DA_NS * DA<KT, G, HD>::U * DA<KT, G, HD>::NV * 32; }
+
+// Copies (zero-filled past p1) the row groups of the stage starting at c0
+// into ring slot `slot`, as one commit group.
+template <typename KT, int G, int HD>
+__device__ __forceinline__ void da_stage(const KT* __restrict__ base, int c0, int p1, uint4* ring, int slot) {
+    using C = DA<KT, G, HD>;
+    const int lane = threadIdx.x & 31;
+    const int sl = lane / C::LPP, sub = lane % C::LPP;
+#pragma unroll
+    for (int u = 0; u < C::U; u++) {
+        const int p = c0 + u * C::PPW + sl;
+        const bool in = p < p1;
+        const uint4* src = reinterpret_cast<const uint4*>(base + (size_t)(in ? p : 0) * HD + sub * C::EPL);
+#pragma unroll
+        for (int v = 0; v < C::NV; v++) cp_async16(ring + ((slot * C::U + u) * C::NV + v) * 32 + lane, src + v, in ? 16 : 0);
+    }
+    cp_async_commit();
+}
+
+template <typename KT, int G, int HD>
+__device__ __forceinline__ void da_unstage(const uint4* ring, int slot, uint4 (&raw)[DA<KT, G, HD>::U][DA<KT, G, HD>::NV]) {
+    using C = DA<KT, G, HD>;
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int u = 0; u < C::U; u++)
+#pragma unroll
+        for (int v = 0; v < C::NV; v++) raw[u][v] = ring[((slot * C::U + u) * C::NV + v) * 32 + lane];
+}
+
+// da_scores through the ring (ring: this CTA's DA_WARPS rings)
+template <typename KT, int G, int HD>
+__device__ __forceinline__ void da_scores_staged(const KT* __restrict__ kbase, const float2 (&qr)[G][DA<KT, G, HD>::EPL / 2],
+                                                 int p0, int p1, float scale, float* S, int sbase, float (&mx)[G],
+                                                 uint4* ring_all) {
+    using C = DA<KT, G, HD>;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int slot = lane / C::LPP, sub = lane % C::LPP;
+    const int g_own = sub / C::GSPAN;
+    const bool writer = (sub % C::GSPAN) == 0;
+    constexpr int STEP = C::U * C::PPW;
+    constexpr int WSTEP = DA_WARPS * STEP;
+    uint4* ring = ring_all + warp * da_ring_u4<KT, G, HD>();
+    int c0 = p0 + warp * STEP;
+    da_stage<KT, G, HD>(kbase, c0, p1, ring, 0);
+    da_stage<KT, G, HD>(kbase, c0 + WSTEP, p1, ring, 1);
+    for (int it = 0; c0 < p1; it++, c0 += WSTEP) {
+        uint4 raw[C::U][C::NV];
+        cp_async_wait<1>();  // this stage landed (the next may still be in flight)
+        da_unstage<KT, G, HD>(ring, it & 1, raw);
+#pragma unroll
+        for (int u = 0; u < C::U; u++) {
+            float2 k[C::EPL / 2];
+            cvt_pairs<KT, C::EPL>(raw[u], k);
+            float acc[G];
+#pragma unroll
+            for (int g = 0; g < G; g++) {
+                float2 a2 = make_float2(0.0f, 0.0f);
+#pragma unroll
+                for (int e = 0; e < C::EPL / 2; e++) a2 = __ffma2_rn(qr[g][e], k[e], a2);
+                acc[g] = a2.x + a2.y;
+            }
+            const int p = c0 + u * C::PPW + slot;
+            if constexpr (C::SCATTER) {
+                Scatter<G, C::LPP / 2>::run(acc, sub);
+                if (writer && p < p1) {
+                    float sc = __fmul_rn(acc[0], scale);
+                    S[(size_t)(p - sbase) * G + g_own] = sc;
+                    mx[0] = fmaxf(mx[0], sc);
+                }
+            } else {
+#pragma unroll
+                for (int g = 0; g < G; g++) Scatter<1, C::LPP / 2>::run(&acc[g], sub);
+                if (sub == 0 && p < p1) {
+#pragma unroll
+                    for (int g = 0; g < G; g++) {
+                        float sc = __fmul_rn(acc[g], scale);
+                        S[(size_t)(p - sbase) * G + g] = sc;
+                        mx[g] = fmaxf(mx[g], sc);
+                    }
+                }
+            }
+        }
+        // the slot's data is in registers and used: refill it two stages ahead
+        da_stage<KT, G, HD>(kbase, c0 + 2 * WSTEP, p1, ring, it & 1);
+    }
+    cp_async_wait<0>();
+}
+
+// da_pv through the ring
+template <typename KT, int G, int HD>
+__device__ __forceinline__ void da_pv_staged(const KT* __restrict__ vbase, const float* W, int wbase, int p0, int p1,
+                                             float2 (&o)[G][DA<KT, G, HD>::EPL / 2], uint4* ring_all) {
+    using C = DA<KT, G, HD>;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int slot = lane / C::LPP;
+    constexpr int STEP = C::U * C::PPW;
+    constexpr int WSTEP = DA_WARPS * STEP;
+    uint4* ring = ring_all + warp * da_ring_u4<KT, G, HD>();
+    int c0 = p0 + warp * STEP;
+    da_stage<KT, G, HD>(vbase, c0, p1, ring, 0);
+    da_stage<KT, G, HD>(vbase, c0 + WSTEP, p1, ring, 1);
+    for (int it = 0; c0 < p1; it++, c0 += WSTEP) {
+        uint4 raw[C::U][C::NV];
+        cp_async_wait<1>();
+        da_unstage<KT, G, HD>(ring, it & 1, raw);
+#pragma unroll
+        for (int u = 0; u < C::U; u++) {
+            int p = c0 + u * C::PPW + slot;
+            if (p >= p1) continue;
+            float2 v2[C::EPL / 2];
+            cvt_pairs<KT, C::EPL>(raw[u], v2);
+            float w[G];
+            load_w<G>(W, p - wbase, w);
+#pragma unroll
+            for (int g = 0; g < G; g++) {
+                const float2 w2 = make_float2(w[g], w[g]);
+#pragma unroll
+                for (int e = 0; e < C::EPL / 2; e++) o[g][e] = __ffma2_rn(w2, v2[e], o[g][e]);
+            }
+        }
+        da_stage<KT, G, HD>(vbase, c0 + 2 * WSTEP, p1, ring, it & 1);
+    }
+    cp_async_wait<0>();
+}
+
 // Sum o over the slots of a warp and over the warps; the result for head g,
 // feature d lands in red[DA_WARPS * G * HD + g * HD + d] (red holds
 // (DA_WARPS + 1) * G * HD floats).
@@ -457,7 +602,9 @@ __host__ __device__ __forceinline__ size_t red_offset(int n) { return ((size_t)n
 
 // Whole context in one CTA per (sequence, KV head): scores kept in shared
 // memory, then weights, then P.V; K and V are each read once.
-template <typename KT, int G, int HD>
+// ST: K and V stream through per-warp cp.async rings that share the
+// reduction buffer's shared memory.
+template <typename KT, int G, int HD, bool ST>
 __global__ void __launch_bounds__(DA_THREADS, 2) k_dattn_fused(DecAttnParams P) {
     pdl_trigger();
     using C = DA<KT, G, HD>;
@@ -481,7 +628,10 @@ __global__ void __launch_bounds__(DA_THREADS, 2) k_dattn_fused(DecAttnParams P) 
     float mx[G];
 #pragma unroll
     for (int g = 0; g < G; g++) mx[g] = -INFINITY;
-    da_scores<KT, G, HD>(kbase, qr, 0, n, P.scale, S, 0, mx);
+    if constexpr (ST)
+        da_scores_staged<KT, G, HD>(kbase, qr, 0, n, P.scale, S, 0, mx, reinterpret_cast<uint4*>(red));
+    else
+        da_scores<KT, G, HD>(kbase, qr, 0, n, P.scale, S, 0, mx);
     float gmax[G];
     da_head_max<KT, G, HD>(mx, gmax, redv);  // also orders the S writes
     const int n8 = n - (n % 8);
@@ -504,8 +654,11 @@ __global__ void __launch_bounds__(DA_THREADS, 2) k_dattn_fused(DecAttnParams P) 
     for (int g = 0; g < G; g++)
 #pragma unroll
         for (int e = 0; e < C::EPL / 2; e++) o[g][e] = make_float2(0.0f, 0.0f);
-    da_pv<KT, G, HD>(vbase, S, 0, 0, n, o);
-    da_reduce_o<KT, G, HD>(o, red);
+    if constexpr (ST)
+        da_pv_staged<KT, G, HD>(vbase, S, 0, 0, n, o, reinterpret_cast<uint4*>(red));
+    else
+        da_pv<KT, G, HD>(vbase, S, 0, 0, n, o);
+    da_reduce_o<KT, G, HD>(o, red);  // its first barrier follows every warp's last ring read
     const float* fin = red + (size_t)DA_WARPS * G * HD;
     for (int i = threadIdx.x; i < G * HD; i += DA_THREADS) {
         int g = i / HD;
@@ -771,10 +924,20 @@ int launch_dattn_ghd(const DecAttnParams& P, int rows, cudaStream_t s) {
         size_t smem = (red_offset(G * P.max_pos) + red_floats) * sizeof(float);
         HC_CHECK(smem <= 220 * 1024, HC_ERR_UNSUPPORTED, "decode attention: context %d too long for one split",
                  P.max_pos);
-        if (smem > 48 * 1024)
-            HC_CUDA(cudaFuncSetAttribute(k_dattn_fused<KT, G, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem));
-        k_dattn_fused<KT, G, HD><<<dim3((unsigned)rows, (unsigned)P.nkv), DA_THREADS, smem, s>>>(P);
+        // the cp.async rings when they still leave two CTAs per SM
+        const size_t ring_floats = (size_t)DA_WARPS * da_ring_u4<KT, G, HD>() * 4;
+        const size_t smem_st = (red_offset(G * P.max_pos) + std::max<size_t>(red_floats, ring_floats)) * sizeof(float);
+        if (smem_st <= 112 * 1024) {
+            if (smem_st > 48 * 1024)
+                HC_CUDA(cudaFuncSetAttribute(k_dattn_fused<KT, G, HD, true>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_st));
+            k_dattn_fused<KT, G, HD, true><<<dim3((unsigned)rows, (unsigned)P.nkv), DA_THREADS, smem_st, s>>>(P);
+        } else {
+            if (smem > 48 * 1024)
+                HC_CUDA(cudaFuncSetAttribute(k_dattn_fused<KT, G, HD, false>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+            k_dattn_fused<KT, G, HD, false><<<dim3((unsigned)rows, (unsigned)P.nkv), DA_THREADS, smem, s>>>(P);
+        }
         HC_LAUNCH_CHECK();
         return HC_OK;
     }
