@@ -666,6 +666,222 @@ __global__ void __launch_bounds__(DA_THREADS, 2) k_dattn_fused(DecAttnParams P) 
     }
 }
 
+// ---- Tensor-core variant of the whole-context kernel for fp16 caches with
+// G <= 4 query heads per KV head (mma.sync m16n8k16, f16 in, f32 accumulate).
+// Scores: A = 16 cached K rows x 16 features (exact fp16), B = 16 features x 8
+// columns holding each query head rounded to fp16 (columns g) and its rounding
+// remainder (columns 4 + g); hi and lo are accumulated separately in f32 and
+// then added, which recovers the f32 query to ~2^-22 relative.  Weighted V:
+// A = the weights split the same way (rows g: fp16 parts, rows 4 + g: the
+// remainders, rows 8-15 zero) x 16 positions, B = 16 positions x 8 features of
+// V (exact fp16).  K and V tiles of 16 rows stream through per-warp cp.async
+// rings (rows of HD/8 16-byte chunks, chunk c of row r stored at c ^ (r & 7)
+// so the ldmatrix reads are conflict-free); each warp takes every eighth tile.
+namespace {
+constexpr int DM_TILE = 16;  // positions per tile
+constexpr int DM_NS = 2;     // ring stages per warp
+
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"((uint32_t)__cvta_generic_to_shared(p)));
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"((uint32_t)__cvta_generic_to_shared(p)));
+}
+
+// fp16 pair (lo half = a) of the hi part (lo == false) or the rounding
+// remainder (lo == true) of two f32 values
+__device__ __forceinline__ uint32_t split_pair(float a, float b, bool lo) {
+    const __half ah = __float2half_rn(a), bh = __float2half_rn(b);
+    __half2 h = lo ? __halves2half2(__float2half_rn(a - __half2float(ah)), __float2half_rn(b - __half2float(bh)))
+                   : __halves2half2(ah, bh);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Copies tile `tile` (rows [16 tile, 16 tile + 16), zero past n) into ring slot
+// `slot` (16 B units), one commit group.
+template <int HD>
+__device__ __forceinline__ void dm_stage(const __half* __restrict__ base, int tile, int n, uint4* slot_base) {
+    constexpr int CPR = HD / 8;  // 16-byte chunks per row
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int j = 0; j < DM_TILE * CPR / 32; j++) {
+        const int i = lane + 32 * j, r = i / CPR, c = i % CPR;
+        const int p = tile * DM_TILE + r;
+        const bool in = p < n;
+        cp_async16(slot_base + r * CPR + (c ^ (r & 7)), base + (size_t)(in ? p : 0) * HD + c * 8, in ? 16 : 0);
+    }
+    cp_async_commit();
+}
+}  // namespace
+
+template <int G, int HD>
+__global__ void __launch_bounds__(DA_THREADS, 2) k_dattn_mma(DecAttnParams P) {
+    static_assert(G == 1 || G == 2 || G == 4, "hi and lo columns of G heads in 8");
+    static_assert(HD == 64 || HD == 128, "feature tiles");
+    constexpr int CPR = HD / 8;
+    constexpr int SLOT = DM_TILE * CPR;  // uint4 per ring slot
+    pdl_trigger();
+    extern __shared__ float smem[];
+    __shared__ float redv[32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int t = lane & 3, q4 = lane >> 2;
+    const int row = blockIdx.x, kvh = blockIdx.y;
+    const int seq = P.seqs[row];
+    const int n = min(P.pos[seq], P.max_pos);
+    if (n <= 1) {
+        for (int i = threadIdx.x; i < G * HD; i += DA_THREADS)
+            da_write_out(P, row, kvh * G + i / HD, i % HD, P.vself[(size_t)row * P.ldself + (size_t)kvh * HD + i % HD]);
+        return;
+    }
+    float* S = smem;                                // [max_pos][G]
+    float* red = smem + red_offset(G * P.max_pos);  // rings, then the reduction buffer
+    uint4* ring = reinterpret_cast<uint4*>(red) + (size_t)warp * DM_NS * SLOT;
+    const size_t off = (size_t)seq * P.seq_stride + (size_t)kvh * P.head_stride;
+    const __half* kbase = reinterpret_cast<const __half*>(P.kc) + off;
+    const __half* vbase = reinterpret_cast<const __half*>(P.vc) + off;
+    const int ntiles = (n + DM_TILE - 1) / DM_TILE;
+
+    // ---- query fragments: column q4 of B = head q4 % 4, hi (q4 < 4) or lo
+    uint32_t qf[HD / 16][2];
+    {
+        const int g = q4 & 3;
+        const bool lo = q4 >= 4, valid = g < G;
+        const float* qrow = P.q + (size_t)row * P.ldq + (size_t)(kvh * G + (valid ? g : 0)) * HD;
+#pragma unroll
+        for (int ks = 0; ks < HD / 16; ks++)
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const int k = ks * 16 + 2 * t + 8 * h;
+                const float a = valid ? qrow[k] : 0.0f, b = valid ? qrow[k + 1] : 0.0f;
+                qf[ks][h] = split_pair(a, b, lo);
+            }
+    }
+
+    // ---- scores
+    float mx0 = -INFINITY, mx1 = -INFINITY;  // heads 2t, 2t + 1 (lanes t < 2)
+    dm_stage<HD>(kbase, warp, n, ring);
+    dm_stage<HD>(kbase, warp + DA_WARPS, n, ring + SLOT);
+    for (int tile = warp, it = 0; tile < ntiles; tile += DA_WARPS, it++) {
+        cp_async_wait<1>();
+        __syncwarp();  // every lane's copies of this tile landed
+        const uint4* sl = ring + (it & 1) * SLOT;
+        float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+        for (int ks = 0; ks < HD / 16; ks++) {
+            const int mi = lane >> 3, r = (lane & 7) + 8 * (mi & 1);
+            uint32_t a[4];
+            ldsm_x4(a, sl + r * CPR + ((2 * ks + (mi >> 1)) ^ (r & 7)));
+            mma16816(d, a, qf[ks][0], qf[ks][1]);
+        }
+        // columns 2t, 2t + 1: hi parts (t < 2) and lo parts (t >= 2) of heads 2(t & 1), 2(t & 1) + 1
+        float e[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) e[i] = __shfl_xor_sync(0xffffffffu, d[i], 2);
+        if (t < 2) {
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int g = 2 * t + (i & 1);
+                const int p = tile * DM_TILE + q4 + 8 * (i >> 1);
+                if (g < G && p < n) {
+                    const float sc = __fmul_rn(d[i] + e[i], P.scale);
+                    S[(size_t)p * G + g] = sc;
+                    if (i & 1) mx1 = fmaxf(mx1, sc);
+                    else mx0 = fmaxf(mx0, sc);
+                }
+            }
+        }
+        __syncwarp();  // the slot is read: refill it two tiles ahead
+        dm_stage<HD>(kbase, tile + 2 * DA_WARPS, n, ring + (it & 1) * SLOT);
+    }
+    cp_async_wait<0>();
+    float gmax[G];
+#pragma unroll
+    for (int g = 0; g < G; g++) gmax[g] = block_max(t == (g >> 1) ? ((g & 1) ? mx1 : mx0) : -INFINITY, redv);
+
+    // ---- weights (the reference's polynomial softmax over the global maximum)
+    const int n8 = n - (n % 8);
+    float lsum[G];
+#pragma unroll
+    for (int g = 0; g < G; g++) lsum[g] = 0.0f;
+    for (int p = threadIdx.x; p < n; p += DA_THREADS) {
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+            float w = softmax_weight(S[(size_t)p * G + g], gmax[g], p, n8);
+            S[(size_t)p * G + g] = w;
+            lsum[g] += w;
+        }
+    }
+    float total[G];
+#pragma unroll
+    for (int g = 0; g < G; g++) total[g] = block_sum(lsum[g], redv);  // also orders the weight writes
+
+    // ---- weighted V: rows q4 of A = head q4 % 4, hi (q4 < 4) or lo
+    float acc[HD / 8][4];
+#pragma unroll
+    for (int j = 0; j < HD / 8; j++) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
+    const int ga = q4 & 3;
+    const bool alo = q4 >= 4, avalid = ga < G;
+    dm_stage<HD>(vbase, warp, n, ring);
+    dm_stage<HD>(vbase, warp + DA_WARPS, n, ring + SLOT);
+    for (int tile = warp, it = 0; tile < ntiles; tile += DA_WARPS, it++) {
+        const int p0 = tile * DM_TILE + 2 * t;
+        float w[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int p = p0 + (i & 1) + 8 * (i >> 1);
+            w[i] = (avalid && p < n) ? S[(size_t)p * G + ga] : 0.0f;
+        }
+        const uint32_t a[4] = {split_pair(w[0], w[1], alo), 0u, split_pair(w[2], w[3], alo), 0u};
+        cp_async_wait<1>();
+        __syncwarp();
+        const uint4* sl = ring + (it & 1) * SLOT;
+#pragma unroll
+        for (int j = 0; j < HD / 16; j++) {
+            const int mi = lane >> 3, r = (lane & 7) + 8 * (mi & 1);
+            uint32_t b[4];
+            ldsm_x4_t(b, sl + r * CPR + ((2 * j + (mi >> 1)) ^ (r & 7)));
+            mma16816(acc[2 * j], a, b[0], b[1]);
+            mma16816(acc[2 * j + 1], a, b[2], b[3]);
+        }
+        __syncwarp();
+        dm_stage<HD>(vbase, tile + 2 * DA_WARPS, n, ring + (it & 1) * SLOT);
+    }
+    cp_async_wait<0>();
+    // rows q4 and q4 + 4 (lanes l and l + 16) are the hi and lo sums of head q4
+#pragma unroll
+    for (int j = 0; j < HD / 8; j++) {
+        acc[j][0] += __shfl_down_sync(0xffffffffu, acc[j][0], 16);
+        acc[j][1] += __shfl_down_sync(0xffffffffu, acc[j][1], 16);
+    }
+    __syncthreads();  // every warp is done with its ring: the buffer becomes the reduction area
+    if (lane < 16 && q4 < G) {
+#pragma unroll
+        for (int j = 0; j < HD / 8; j++)
+            *reinterpret_cast<float2*>(red + ((size_t)warp * G + q4) * HD + 8 * j + 2 * t) =
+                make_float2(acc[j][0], acc[j][1]);
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < G * HD; i += DA_THREADS) {
+        float o = 0.0f;
+#pragma unroll
+        for (int w = 0; w < DA_WARPS; w++) o += red[(size_t)w * G * HD + i];
+        da_write_out(P, row, kvh * G + i / HD, i % HD, __fdiv_rn(o, total[i / HD]));
+    }
+}
+
 // ---- Cluster split.  When the batch has too few (sequence, KV head) pairs
 // to fill the GPU (tensor-parallel shards), the NCL CTAs of a thread-block
 // cluster share one pair: CTA c scores positions [c len, (c+1) len), the CTAs
@@ -924,6 +1140,20 @@ int launch_dattn_ghd(const DecAttnParams& P, int rows, cudaStream_t s) {
         size_t smem = (red_offset(G * P.max_pos) + red_floats) * sizeof(float);
         HC_CHECK(smem <= 220 * 1024, HC_ERR_UNSUPPORTED, "decode attention: context %d too long for one split",
                  P.max_pos);
+        if constexpr (sizeof(KT) == 2 && (G == 1 || G == 2 || G == 4) && (HD == 64 || HD == 128)) {
+            // tensor-core variant: rings of 16-row tiles, two CTAs per SM
+            const size_t mring_floats = (size_t)DA_WARPS * DM_NS * DM_TILE * HD / 2;
+            const size_t smem_m =
+                (red_offset(G * P.max_pos) + std::max<size_t>((size_t)DA_WARPS * G * HD, mring_floats)) * sizeof(float);
+            if (smem_m <= 112 * 1024) {
+                if (smem_m > 48 * 1024)
+                    HC_CUDA(cudaFuncSetAttribute(k_dattn_mma<G, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)smem_m));
+                k_dattn_mma<G, HD><<<dim3((unsigned)rows, (unsigned)P.nkv), DA_THREADS, smem_m, s>>>(P);
+                HC_LAUNCH_CHECK();
+                return HC_OK;
+            }
+        }
         // the cp.async rings when they still leave two CTAs per SM
         const size_t ring_floats = (size_t)DA_WARPS * da_ring_u4<KT, G, HD>() * 4;
         const size_t smem_st = (red_offset(G * P.max_pos) + std::max<size_t>(red_floats, ring_floats)) * sizeof(float);
