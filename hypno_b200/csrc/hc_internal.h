@@ -104,9 +104,22 @@ int launch_silu_mul(const float* gu, size_t ldgu, float* act, size_t ldact, size
 // x[row] = sum of the split slabs part[i][row] (slab order; slab i at part +
 // i * rows * width, `width` elements per row), the first `heads` heads then
 // rotated as launch_rope_rows does.
+// kv (optional): also store the row's k and v elements (the nk elements at
+// nq, then the nk at nq + nk) into the cache as launch_kv_store does.
+struct KvStoreArgs {
+    void* kc = nullptr;  // null: no store
+    void* vc = nullptr;
+    int kv_fp16 = 0;
+    size_t seq_stride = 0, head_stride = 0;
+    int max_pos = 0;
+    const int* seqs = nullptr;  // row -> sequence (decode); null: fixed_seq, position pos0 + row
+    const int* pos = nullptr;   // sequence -> cached positions
+    int fixed_seq = 0, pos0 = 0;
+    int nq = 0, nk = 0;         // k block at element nq, v block at nq + nk (nk = kv heads x head_dim)
+};
 int launch_rope_rows_slabs(const float* part, int splits, float* x, size_t ldx, size_t rows, size_t width,
                            size_t heads, size_t hd, const float2* cs, size_t cs_rows, const int* pos_dev, int pos0,
-                           cudaStream_t s);
+                           cudaStream_t s, const KvStoreArgs* kv = nullptr);
 // Rotation of `heads` adjacent-pair heads per row at position pos0 + row
 // using a (max_pos x hd/2) cos/sin table.
 int launch_rope_rows(float* x, size_t ldx, size_t rows, size_t heads, size_t hd, const float2* cs, size_t cs_rows,

@@ -761,14 +761,23 @@ int launch_rope_rows(float* x, size_t ldx, size_t rows, size_t heads, size_t hd,
 // The same rotation applied while adding the split-K slabs of the qkv
 // projection: x[row][e] = sum over slabs (slab order) of part[i][row][e] for
 // the row's `width` elements, rotated for the first `heads` heads (q and k;
-// v is only summed).  Slab i starts at part + i * rows * width.
+// v is only summed).  Slab i starts at part + i * rows * width.  With kv.kc
+// set, the row's (rotated) k and v elements are also stored into the cache
+// exactly as launch_kv_store does.
+template <typename KT>
 __global__ void k_rope_rows_slabs(const float* __restrict__ part, int splits, size_t slab, float* __restrict__ x,
                                   size_t ldx, int width, int heads, int hd, const float2* __restrict__ cs, int cs_rows,
-                                  const int* __restrict__ pos_dev, int pos0) {
+                                  const int* __restrict__ pos_dev, int pos0, KvStoreArgs kv) {
     const int row = blockIdx.y;
     const int pos = pos_dev ? pos_dev[row] : pos0 + row;
     const bool rot_ok = pos >= 0 && pos < cs_rows;  // else the position is rejected elsewhere
     const int half = hd / 2;
+    int kseq = 0, kpos = -1;
+    if (kv.kc) {
+        kseq = kv.seqs ? kv.seqs[row] : kv.fixed_seq;
+        kpos = kv.seqs ? kv.pos[kseq] : kv.pos0 + row;
+    }
+    const bool store = kv.kc && kpos >= 0 && kpos < kv.max_pos;  // capacity guard of launch_kv_store
     const float2* pr = reinterpret_cast<const float2*>(part + (size_t)row * width);
     float2* xr = reinterpret_cast<float2*>(x + (size_t)row * ldx);
     for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < width / 2; p += gridDim.x * blockDim.x) {
@@ -786,20 +795,45 @@ __global__ void k_rope_rows_slabs(const float* __restrict__ part, int splits, si
             v.y = __fadd_rn(__fmul_rn(a, c.y), __fmul_rn(b, c.x));
         }
         xr[p] = v;
+        const int e = 2 * p - kv.nq;  // element within the k (then v) block
+        if (store && e >= 0) {
+            const bool is_v = e >= kv.nk;
+            const int ev = is_v ? e - kv.nk : e;
+            const size_t off = (size_t)kseq * kv.seq_stride + (size_t)(ev / hd) * kv.head_stride + (size_t)kpos * hd +
+                               (size_t)(ev % hd);
+            KT* dst = reinterpret_cast<KT*>(is_v ? kv.vc : kv.kc) + off;
+            if constexpr (sizeof(KT) == 2) {
+                dst[0] = __float2half_rn(v.x);
+                dst[1] = __float2half_rn(v.y);
+            } else {
+                dst[0] = v.x;
+                dst[1] = v.y;
+            }
+        }
     }
 }
 
 int launch_rope_rows_slabs(const float* part, int splits, float* x, size_t ldx, size_t rows, size_t width,
                            size_t heads, size_t hd, const float2* cs, size_t cs_rows, const int* pos_dev, int pos0,
-                           cudaStream_t s) {
+                           cudaStream_t s, const KvStoreArgs* kv) {
     if (rows == 0) return HC_OK;
     HC_CHECK(splits >= 1 && width % 2 == 0 && hd % 2 == 0 && ldx % 2 == 0 && heads * hd <= width &&
                  ((uintptr_t)part & 7) == 0 && ((uintptr_t)x & 7) == 0,
              HC_ERR_INVALID, "rope_rows_slabs: unsupported layout");
+    KvStoreArgs k{};
+    if (kv) {
+        k = *kv;
+        HC_CHECK(k.nq >= 0 && (size_t)(k.nq + 2 * k.nk) <= width && k.nq % 2 == 0 && k.nk % (int)hd == 0,
+                 HC_ERR_INVALID, "rope_rows_slabs: k/v block outside the row");
+    }
     const size_t pairs = width / 2;
     const unsigned gx = (unsigned)std::min<size_t>((pairs + 127) / 128, 64);
-    k_rope_rows_slabs<<<dim3(gx, (unsigned)rows), 128, 0, s>>>(part, splits, rows * width, x, ldx, (int)width,
-                                                               (int)heads, (int)hd, cs, (int)cs_rows, pos_dev, pos0);
+    if (kv && k.kv_fp16)
+        k_rope_rows_slabs<__half><<<dim3(gx, (unsigned)rows), 128, 0, s>>>(
+            part, splits, rows * width, x, ldx, (int)width, (int)heads, (int)hd, cs, (int)cs_rows, pos_dev, pos0, k);
+    else
+        k_rope_rows_slabs<float><<<dim3(gx, (unsigned)rows), 128, 0, s>>>(
+            part, splits, rows * width, x, ldx, (int)width, (int)heads, (int)hd, cs, (int)cs_rows, pos_dev, pos0, k);
     HC_LAUNCH_CHECK();
     return HC_OK;
 }

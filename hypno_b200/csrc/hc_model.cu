@@ -593,25 +593,40 @@ int run_layers(hc_model* m, hc_kv* kv, size_t rows, bool prefill, int seq, int p
         if (!xn_ready)
             HC_TRY(hc::launch_rmsnorm(s.hidden, H, L.in_norm, s.xn, H, rows, H, c.rms_norm_eps, m->stream, s.xn16));
         xn_ready = false;
+        size_t lofs = li * kv->layer_stride * (kv->kv_fp16 ? 2 : 4);
+        void* kc = (uint8_t*)kv->k + lofs;
+        void* vc = (uint8_t*)kv->v + lofs;
         if (s.split_part && rows <= kPartRows && L.qkv.dtype == HC_DTYPE_Q4_0 &&
             hc::gemm_tc_eligible(L.qkv.q4, rows)) {
-            // decode sizes: K split over CTAs into slabs that the RoPE kernel adds
+            // decode sizes: K split over CTAs into slabs that the RoPE kernel
+            // adds, also storing k and v into the cache
             int splits = 1;
             HC_TRY(hc::gemm_tc_partials(m->gemm_ws, L.qkv.q4, s.xn, H, rows, s.split_part, kPartSplits, &splits,
                                         m->stream, s.xn16));
+            hc::KvStoreArgs ka;
+            ka.kc = kc;
+            ka.vc = vc;
+            ka.kv_fp16 = kv->kv_fp16;
+            ka.seq_stride = kv->seq_stride;
+            ka.head_stride = kv->head_stride;
+            ka.max_pos = kv->max_pos;
+            ka.seqs = prefill ? nullptr : s.seqs;
+            ka.pos = kv->pos_dev;
+            ka.fixed_seq = seq;
+            ka.pos0 = pos0;
+            ka.nq = (int)nq;
+            ka.nk = (int)nk;
             HC_TRY(hc::launch_rope_rows_slabs(s.split_part, splits, s.qkv, ldqkv, rows, ldqkv, nh_l + nkv_l, hd,
-                                              m->rope, m->rope_rows, prefill ? nullptr : s.rowpos, pos0, m->stream));
+                                              m->rope, m->rope_rows, prefill ? nullptr : s.rowpos, pos0, m->stream,
+                                              &ka));
         } else {
             HC_TRY(matmul(m, L.qkv, s.xn, H, rows, s.qkv, ldqkv, hc::EPI_STORE, nullptr, 0, s.xn16));
             HC_TRY(hc::launch_rope_rows(s.qkv, ldqkv, rows, nh_l + nkv_l, hd, m->rope, m->rope_rows,
                                         prefill ? nullptr : s.rowpos, pos0, m->stream));
+            HC_TRY(hc::launch_kv_store(s.qkv + nq, s.qkv + nq + nk, ldqkv, (int)rows, (int)nkv_l, (int)hd, kc, vc,
+                                       kv->kv_fp16, kv->seq_stride, kv->head_stride, kv->max_pos,
+                                       prefill ? nullptr : s.seqs, kv->pos_dev, seq, pos0, m->stream));
         }
-        size_t lofs = li * kv->layer_stride * (kv->kv_fp16 ? 2 : 4);
-        void* kc = (uint8_t*)kv->k + lofs;
-        void* vc = (uint8_t*)kv->v + lofs;
-        HC_TRY(hc::launch_kv_store(s.qkv + nq, s.qkv + nq + nk, ldqkv, (int)rows, (int)nkv_l, (int)hd, kc, vc,
-                                   kv->kv_fp16, kv->seq_stride, kv->head_stride, kv->max_pos,
-                                   prefill ? nullptr : s.seqs, kv->pos_dev, seq, pos0, m->stream));
         hc::AttnParams P{};
         P.out16 = s.attn16;
         P.q = s.qkv;
