@@ -119,6 +119,9 @@ __device__ __forceinline__ float poly_exp8(float v) {
 
 // Weight of entry i of an n-long softmax row before normalisation
 // (kernels.rs:642-652): polynomial on the 8-lane body, libm exp on the tail.
+// x / (1 + exp(-x)) as the reference computes it (transformer.rs:446-449)
+__device__ __forceinline__ float silu_f(float v) { return __fdiv_rn(v, __fadd_rn(1.0f, expf(-v))); }
+
 __device__ __forceinline__ float softmax_weight(float s, float mx, int i, int n8) {
     float d = __fsub_rn(s, mx);
     return (i < n8) ? poly_exp8(d) : expf(d);

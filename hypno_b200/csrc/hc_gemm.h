@@ -19,6 +19,13 @@ bool gemm_tc_eligible(const hc_q4_matrix& w, size_t tokens);
 int gemm_tc(GemmWorkspace* ws, const hc_q4_matrix& w, const float* x, size_t ldx, size_t tokens, float* y,
             size_t ldy, int epi, const float* res, size_t ldres, cudaStream_t s, const __half* xh_ready = nullptr);
 
+// act[t][i] = silu(gate_i . x_t) * (up_i . x_t) for a fused gate/up weight
+// whose rows alternate in blocks of GU_BLOCK (gate rows, then the matching up
+// rows), computed in the GEMM epilogue; act16 (may be null) gets the fp16
+// copy in the GEMM K order.  act has w.n / 2 columns (row stride ldact).
+int gemm_tc_silu(GemmWorkspace* ws, const hc_q4_matrix& w, const float* x, size_t ldx, size_t tokens, float* act,
+                 size_t ldact, __half* act16, cudaStream_t s, const __half* xh_ready = nullptr);
+
 // The same product with K split over up to max_splits CTAs per tile whose
 // partial products are NOT added here: split i writes its [tokens][n] slab
 // at part + i * tokens * n; *splits reports how many slabs were written (the

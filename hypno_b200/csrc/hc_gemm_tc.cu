@@ -280,7 +280,8 @@ template <int TN>
 __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
     k_q4_gemm_tc(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
                  const __grid_constant__ CUtensorMap smap, float* __restrict__ y, size_t ldy, const float* res, size_t ldres,
-                 int epi, int N, int K, int T, int splits, size_t split_stride, int* __restrict__ err) {
+                 int epi, int N, int K, int T, int splits, size_t split_stride, __half* __restrict__ y16,
+                 int* __restrict__ err) {
     using C = Cfg<TN>;
     constexpr int S_X = C::S_X, S_W = C::S_W, S_TM = C::S_TM;
     extern __shared__ uint8_t smem_raw[];
@@ -514,9 +515,44 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
             grid_dependency_wait();  // y and the residual may be touched by the previous kernel
             // Every load of a 16-token chunk (residuals) is issued before the
             // first dependent add: one memory round trip per chunk.
+            if (epi_ok && epi == EPI_SILU) {
+                // rows [0, 64) of the tile are gate rows, [64, 128) the matching
+                // up rows (the fused weight's blocked row order): each chunk of
+                // the accumulator goes through shared memory (the rings are
+                // idle), then the warpgroup writes y[t][c] = silu(gate) * up
+                // for c = blockIdx.x * 64 + row and its fp16 copy in the next
+                // GEMM's K order
+                tmem_fence_after();
+                float* xb = reinterpret_cast<float*>(smem);  // [BM][EPI_CH + 1]
+                const int e = threadIdx.x - 128;             // 0..127 over the epilogue warpgroup
+                const int orow = e & (GU_BLOCK - 1), half = e >> 6;
+                const int col = blockIdx.x * GU_BLOCK + orow;
+                const size_t ncols = (size_t)N / 2;
+#pragma unroll 1
+                for (int c0 = 0; c0 < TN; c0 += EPI_CH) {
+                    uint32_t v[EPI_CH];
+                    load_accumulators<C>(tmem, q, c0, nk, v);
+#pragma unroll
+                    for (int jj = 0; jj < EPI_CH; jj++) xb[r * (EPI_CH + 1) + jj] = __uint_as_float(v[jj]);
+                    asm volatile("bar.sync 1, 128;" ::: "memory");  // the epilogue warpgroup
+                    const int tl = min(EPI_CH, T - (t0 + c0));
+#pragma unroll 1
+                    for (int k = 0; k < EPI_CH / 2; k++) {
+                        const int jj = half * (EPI_CH / 2) + k;
+                        if (jj < tl) {
+                            const float o = __fmul_rn(silu_f(xb[orow * (EPI_CH + 1) + jj]),
+                                                      xb[(orow + GU_BLOCK) * (EPI_CH + 1) + jj]);
+                            const size_t t = (size_t)(t0 + c0 + jj);
+                            y[t * ldy + col] = o;
+                            if (y16) y16[t * ncols + perm_k(col)] = __float2half_rn(o);
+                        }
+                    }
+                    asm volatile("bar.sync 1, 128;" ::: "memory");  // before the next chunk reuses xb
+                }
+            }
             // split_stride > 0: split `split` stores its partial product to
             // its own slab y + split * split_stride (the caller adds the slabs)
-            if (epi_ok && (splits == 1 || split_stride)) {
+            else if (epi_ok && (splits == 1 || split_stride)) {
                 tmem_fence_after();
                 float* ys = y + (size_t)split * split_stride;
                 const bool add = epi == EPI_ADD && res && !split_stride;
@@ -729,7 +765,7 @@ template <int TN>
 int launch_tc(const hc_q4_matrix& w, const CUtensorMap& xmap, const CUtensorMap& wmap, const CUtensorMap& smap,
               size_t T, float* y,
               size_t ldy, int epi, const float* res, size_t ldres, int splits, int* err, cudaStream_t s,
-              size_t split_stride = 0) {
+              size_t split_stride = 0, __half* y16 = nullptr) {
     using C = Cfg<TN>;
     auto kfn = k_q4_gemm_tc<TN>;
     const int smem = launch_smem<TN>();
@@ -757,7 +793,7 @@ int launch_tc(const hc_q4_matrix& w, const CUtensorMap& xmap, const CUtensorMap&
     cfg.attrs = attr;
     cfg.numAttrs = (unsigned)na;
     HC_CUDA(cudaLaunchKernelEx(&cfg, kfn, xmap, wmap, smap, y, ldy, res, ldres, epi, (int)w.n,
-                               (int)w.k, (int)T, splits, split_stride, err));
+                               (int)w.k, (int)T, splits, split_stride, y16, err));
     hc_count_launch();
     return HC_OK;
 }
@@ -809,7 +845,7 @@ const int* tile_slots(GemmWorkspace* ws, int ti) {
 namespace {
 int gemm_tc_impl(GemmWorkspace* ws, const hc_q4_matrix& w, const float* x, size_t ldx, size_t tokens, float* y,
                  size_t ldy, int epi, const float* res, size_t ldres, cudaStream_t s, const __half* xh_ready,
-                 int max_part, int* splits_out) {
+                 int max_part, int* splits_out, __half* y16 = nullptr) {
     std::lock_guard<std::mutex> lock(ws->mu);
     const size_t K = w.k, T = tokens;
     int dev = 0;
@@ -861,23 +897,24 @@ int gemm_tc_impl(GemmWorkspace* ws, const hc_q4_matrix& w, const float* x, size_
     int nsm = 148;
     HC_CUDA(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
     const size_t stride = max_part > 0 ? T * ldy : 0;  // slab stride in partial mode
+    const bool one = epi == EPI_SILU;                  // the SiLU epilogue needs whole sums
     int splits = 1;
     switch (tn) {
         case 32:
-            splits = choose_splits(tiles, nk, tile_slots<32>(ws, 0), nsm, Cfg<32>::DUAL, max_part);
-            HC_TRY(launch_tc<32>(w, xmap, wmap, smap, T, y, ldy, epi, res, ldres, splits, ws->err, s, stride));
+            if (!one) splits = choose_splits(tiles, nk, tile_slots<32>(ws, 0), nsm, Cfg<32>::DUAL, max_part);
+            HC_TRY(launch_tc<32>(w, xmap, wmap, smap, T, y, ldy, epi, res, ldres, splits, ws->err, s, stride, y16));
             break;
         case 64:
-            splits = choose_splits(tiles, nk, tile_slots<64>(ws, 1), nsm, Cfg<64>::DUAL, max_part);
-            HC_TRY(launch_tc<64>(w, xmap, wmap, smap, T, y, ldy, epi, res, ldres, splits, ws->err, s, stride));
+            if (!one) splits = choose_splits(tiles, nk, tile_slots<64>(ws, 1), nsm, Cfg<64>::DUAL, max_part);
+            HC_TRY(launch_tc<64>(w, xmap, wmap, smap, T, y, ldy, epi, res, ldres, splits, ws->err, s, stride, y16));
             break;
         case 128:
-            splits = choose_splits(tiles, nk, tile_slots<128>(ws, 2), nsm, Cfg<128>::DUAL, max_part);
-            HC_TRY(launch_tc<128>(w, xmap, wmap, smap, T, y, ldy, epi, res, ldres, splits, ws->err, s, stride));
+            if (!one) splits = choose_splits(tiles, nk, tile_slots<128>(ws, 2), nsm, Cfg<128>::DUAL, max_part);
+            HC_TRY(launch_tc<128>(w, xmap, wmap, smap, T, y, ldy, epi, res, ldres, splits, ws->err, s, stride, y16));
             break;
         default:
-            splits = choose_splits(tiles, nk, tile_slots<256>(ws, 3), nsm, Cfg<256>::DUAL, max_part);
-            HC_TRY(launch_tc<256>(w, xmap, wmap, smap, T, y, ldy, epi, res, ldres, splits, ws->err, s, stride));
+            if (!one) splits = choose_splits(tiles, nk, tile_slots<256>(ws, 3), nsm, Cfg<256>::DUAL, max_part);
+            HC_TRY(launch_tc<256>(w, xmap, wmap, smap, T, y, ldy, epi, res, ldres, splits, ws->err, s, stride, y16));
             break;
     }
     if (splits_out) *splits_out = splits;
@@ -888,6 +925,12 @@ int gemm_tc_impl(GemmWorkspace* ws, const hc_q4_matrix& w, const float* x, size_
 int gemm_tc(GemmWorkspace* ws, const hc_q4_matrix& w, const float* x, size_t ldx, size_t tokens, float* y,
             size_t ldy, int epi, const float* res, size_t ldres, cudaStream_t s, const __half* xh_ready) {
     return gemm_tc_impl(ws, w, x, ldx, tokens, y, ldy, epi, res, ldres, s, xh_ready, 0, nullptr);
+}
+
+int gemm_tc_silu(GemmWorkspace* ws, const hc_q4_matrix& w, const float* x, size_t ldx, size_t tokens, float* act,
+                 size_t ldact, __half* act16, cudaStream_t s, const __half* xh_ready) {
+    HC_CHECK(w.n % (2 * GU_BLOCK) == 0, HC_ERR_INVALID, "gemm_tc_silu: %zu rows are not whole gate/up blocks", w.n);
+    return gemm_tc_impl(ws, w, x, ldx, tokens, act, ldact, EPI_SILU, nullptr, 0, s, xh_ready, 0, nullptr, act16);
 }
 
 int gemm_tc_partials(GemmWorkspace* ws, const hc_q4_matrix& w, const float* x, size_t ldx, size_t tokens,

@@ -74,7 +74,11 @@ struct DevWeight {
 // ---------------------------------------------------------------- kernels
 namespace hc {
 
-enum Epi : int { EPI_STORE = 0, EPI_ADD = 1 };
+enum Epi : int { EPI_STORE = 0, EPI_ADD = 1, EPI_SILU = 2 };  // EPI_SILU: tensor-core GEMM only
+// Rows of the fused gate/up weight alternate in blocks of GU_BLOCK gate rows
+// then the matching GU_BLOCK up rows (when the intermediate size allows), so
+// one 128-row GEMM tile holds both halves of 64 SiLU-gate outputs.
+constexpr int GU_BLOCK = 64;
 
 // Q4_0 pack / unpack / repack (bit-exact with quant.rs).
 int launch_q4_quantize(const float* x, size_t nblocks, uint8_t* out, cudaStream_t s);
@@ -98,9 +102,10 @@ int launch_rmsnorm(const float* x, size_t ldx, const float* w, float* out, size_
                    size_t n, float eps, cudaStream_t s, __half* out16 = nullptr);
 int launch_softmax_rows(float* x, size_t rows, size_t n, cudaStream_t s);
 int launch_silu(float* x, size_t n, cudaStream_t s);
-// act[r][i] = silu(gu[r][i]) * gu[r][im + i]
+// act[r][i] = silu(gu[r][i]) * gu[r][im + i] (blocked: gate/up alternate in
+// blocks of GU_BLOCK columns)
 int launch_silu_mul(const float* gu, size_t ldgu, float* act, size_t ldact, size_t rows, size_t im,
-                    cudaStream_t s, __half* act16 = nullptr);
+                    cudaStream_t s, __half* act16 = nullptr, bool blocked = false);
 // x[row] = sum of the split slabs part[i][row] (slab order; slab i at part +
 // i * rows * width, `width` elements per row), the first `heads` heads then
 // rotated as launch_rope_rows does.

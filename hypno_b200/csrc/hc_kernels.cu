@@ -689,7 +689,6 @@ int launch_softmax_rows(float* x, size_t rows, size_t n, cudaStream_t s) {
 }
 
 // ============================================================ SiLU
-__device__ __forceinline__ float silu_f(float v) { return __fdiv_rn(v, __fadd_rn(1.0f, expf(-v))); }
 
 __global__ void k_silu(float* __restrict__ x, size_t n) {
     size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -703,24 +702,30 @@ int launch_silu(float* x, size_t n, cudaStream_t s) {
     return HC_OK;
 }
 
-// transformer.rs:446-449 / turbo.rs:235-237: silu(gate) * up.
+// transformer.rs:446-449 / turbo.rs:235-237: silu(gate) * up.  With
+// `blocked`, gate and up rows alternate in blocks of GU_BLOCK (the fused
+// weight's row order): gate i sits at column (i / B) * 2B + i % B, its up at
+// + B; otherwise gate i at i and up at im + i.
 __global__ void k_silu_mul(const float* __restrict__ gu, size_t ldgu, float* __restrict__ act, size_t ldact,
-                           int im, __half* __restrict__ act16) {
+                           int im, __half* __restrict__ act16, int blocked) {
     pdl_trigger();
     const float* g = gu + (size_t)blockIdx.y * ldgu;
     float* a = act + (size_t)blockIdx.y * ldact;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < im; i += gridDim.x * blockDim.x) {
-        float o = __fmul_rn(silu_f(g[i]), g[im + i]);
+        const int gi = blocked ? (i / GU_BLOCK) * (2 * GU_BLOCK) + i % GU_BLOCK : i;
+        const int ui = blocked ? gi + GU_BLOCK : im + i;
+        float o = __fmul_rn(silu_f(g[gi]), g[ui]);
         a[i] = o;
         if (act16) act16[(size_t)blockIdx.y * im + perm_k(i)] = __float2half_rn(o);
     }
 }
 
 int launch_silu_mul(const float* gu, size_t ldgu, float* act, size_t ldact, size_t rows, size_t im,
-                    cudaStream_t s, __half* act16) {
+                    cudaStream_t s, __half* act16, bool blocked) {
     if (rows == 0) return HC_OK;
+    HC_CHECK(!blocked || im % GU_BLOCK == 0, HC_ERR_INVALID, "silu_mul: blocked layout needs im %% %d == 0", GU_BLOCK);
     unsigned gx = (unsigned)std::min<size_t>((im + 255) / 256, 64);
-    k_silu_mul<<<dim3(gx, (unsigned)rows), 256, 0, s>>>(gu, ldgu, act, ldact, (int)im, act16);
+    k_silu_mul<<<dim3(gx, (unsigned)rows), 256, 0, s>>>(gu, ldgu, act, ldact, (int)im, act16, blocked ? 1 : 0);
     HC_LAUNCH_CHECK();
     return HC_OK;
 }

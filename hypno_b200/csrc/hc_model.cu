@@ -179,7 +179,8 @@ std::vector<float2> hc_rope_table(size_t max_pos, size_t hd, float theta) {
 struct LayerW {
     DevWeight qkv;   // rows: q (nq), k (nk), v (nk)
     DevWeight o;     // [hidden x nq]
-    DevWeight gu;    // rows: gate (im), up (im)
+    DevWeight gu;    // rows: gate (im), up (im); gu_blocked: alternating blocks of GU_BLOCK gate / up rows
+    bool gu_blocked = false;
     DevWeight down;  // [hidden x im]
     float* in_norm = nullptr;
     float* post_norm = nullptr;
@@ -722,8 +723,12 @@ int run_layers(hc_model* m, hc_kv* kv, size_t rows, bool prefill, int seq, int p
         if (!normed)
             HC_TRY(hc::launch_rmsnorm(s.hidden, H, L.post_norm, s.xn, H, rows, H, c.rms_norm_eps, m->stream, s.xn16));
         size_t im = L.gu.n / 2;
-        HC_TRY(matmul(m, L.gu, s.xn, H, rows, s.gu, 2 * im, hc::EPI_STORE, nullptr, 0, s.xn16));
-        HC_TRY(hc::launch_silu_mul(s.gu, 2 * im, s.act, im, rows, im, m->stream, s.act16));
+        if (L.gu_blocked && hc::gemm_tc_eligible(L.gu.q4, rows)) {
+            HC_TRY(hc::gemm_tc_silu(m->gemm_ws, L.gu.q4, s.xn, H, rows, s.act, im, s.act16, m->stream, s.xn16));
+        } else {
+            HC_TRY(matmul(m, L.gu, s.xn, H, rows, s.gu, 2 * im, hc::EPI_STORE, nullptr, 0, s.xn16));
+            HC_TRY(hc::launch_silu_mul(s.gu, 2 * im, s.act, im, rows, im, m->stream, s.act16, L.gu_blocked));
+        }
         const bool last = li + 1 == m->layers.size();
         const float* next = last ? tail_norm : m->layers[li + 1].in_norm;
         HC_TRY(row_parallel(m, L.down, s.act, im, rows, s.act16, next, &normed));
@@ -851,9 +856,22 @@ HC_EXPORT int hc_model_load(const uint8_t* image, size_t len, int tp_rank, int t
             hc_set_error("hypno: gate/up projections of layer %zu must share a dtype", li);
             return fail(HC_ERR_UNSUPPORTED);
         }
-        if ((r = upload_weight(m, img, {{tg, tp_rank * im_l, im_l, 0, H}, {tu, tp_rank * im_l, im_l, 0, H}}, H, L.gu,
-                               &staging, &staging_cap)))
-            return fail(r);
+        // Q4_0 gate/up rows are interleaved in blocks of GU_BLOCK so that the
+        // tensor-core GEMM can apply the SiLU gate in its epilogue
+        L.gu_blocked = tg->dtype == HC_DTYPE_Q4_0 && im_l % hc::GU_BLOCK == 0 && H % 32 == 0;
+        if (L.gu_blocked) {
+            std::vector<Part> parts;
+            parts.reserve(2 * im_l / hc::GU_BLOCK);
+            for (size_t b = 0; b < im_l; b += hc::GU_BLOCK) {
+                parts.push_back({tg, tp_rank * im_l + b, (size_t)hc::GU_BLOCK, 0, H});
+                parts.push_back({tu, tp_rank * im_l + b, (size_t)hc::GU_BLOCK, 0, H});
+            }
+            r = upload_weight(m, img, parts, H, L.gu, &staging, &staging_cap);
+        } else {
+            r = upload_weight(m, img, {{tg, tp_rank * im_l, im_l, 0, H}, {tu, tp_rank * im_l, im_l, 0, H}}, H, L.gu,
+                              &staging, &staging_cap);
+        }
+        if (r) return fail(r);
         if ((r = upload_weight(m, img, {{td, 0, H, tp_rank * im_l, im_l}}, im, L.down, &staging, &staging_cap)))
             return fail(r);
         if ((r = upload_norm(m, img, p + "input_layernorm.weight", H, &L.in_norm))) return fail(r);
