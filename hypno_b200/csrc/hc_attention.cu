@@ -679,7 +679,6 @@ __global__ void __launch_bounds__(DA_THREADS, 2) k_dattn_fused(DecAttnParams P) 
 // so the ldmatrix reads are conflict-free); each warp takes every eighth tile.
 namespace {
 constexpr int DM_TILE = 16;  // positions per tile
-constexpr int DM_NS = 2;     // ring stages per warp
 
 __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
     asm volatile(
@@ -729,6 +728,7 @@ __device__ __forceinline__ void dm_stage(const __half* __restrict__ base, int ti
 
 template <int G, int HD>
 __global__ void __launch_bounds__(DA_THREADS, 2) k_dattn_mma(DecAttnParams P) {
+    constexpr int NS = 2;  // ring stages per warp
     static_assert(G == 1 || G == 2 || G == 4, "hi and lo columns of G heads in 8");
     static_assert(HD == 64 || HD == 128, "feature tiles");
     constexpr int CPR = HD / 8;
@@ -748,7 +748,7 @@ __global__ void __launch_bounds__(DA_THREADS, 2) k_dattn_mma(DecAttnParams P) {
     }
     float* S = smem;                                // [max_pos][G]
     float* red = smem + red_offset(G * P.max_pos);  // rings, then the reduction buffer
-    uint4* ring = reinterpret_cast<uint4*>(red) + (size_t)warp * DM_NS * SLOT;
+    uint4* ring = reinterpret_cast<uint4*>(red) + (size_t)warp * NS * SLOT;
     const size_t off = (size_t)seq * P.seq_stride + (size_t)kvh * P.head_stride;
     const __half* kbase = reinterpret_cast<const __half*>(P.kc) + off;
     const __half* vbase = reinterpret_cast<const __half*>(P.vc) + off;
@@ -772,12 +772,12 @@ __global__ void __launch_bounds__(DA_THREADS, 2) k_dattn_mma(DecAttnParams P) {
 
     // ---- scores
     float mx0 = -INFINITY, mx1 = -INFINITY;  // heads 2t, 2t + 1 (lanes t < 2)
-    dm_stage<HD>(kbase, warp, n, ring);
-    dm_stage<HD>(kbase, warp + DA_WARPS, n, ring + SLOT);
+#pragma unroll
+    for (int i = 0; i < NS; i++) dm_stage<HD>(kbase, warp + i * DA_WARPS, n, ring + i * SLOT);
     for (int tile = warp, it = 0; tile < ntiles; tile += DA_WARPS, it++) {
-        cp_async_wait<1>();
+        cp_async_wait<NS - 1>();
         __syncwarp();  // every lane's copies of this tile landed
-        const uint4* sl = ring + (it & 1) * SLOT;
+        const uint4* sl = ring + (it % NS) * SLOT;
         float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
         for (int ks = 0; ks < HD / 16; ks++) {
@@ -803,30 +803,18 @@ __global__ void __launch_bounds__(DA_THREADS, 2) k_dattn_mma(DecAttnParams P) {
                 }
             }
         }
-        __syncwarp();  // the slot is read: refill it two tiles ahead
-        dm_stage<HD>(kbase, tile + 2 * DA_WARPS, n, ring + (it & 1) * SLOT);
+        __syncwarp();  // the slot is read: refill it NS tiles ahead
+        dm_stage<HD>(kbase, tile + NS * DA_WARPS, n, ring + (it % NS) * SLOT);
     }
     cp_async_wait<0>();
     float gmax[G];
 #pragma unroll
     for (int g = 0; g < G; g++) gmax[g] = block_max(t == (g >> 1) ? ((g & 1) ? mx1 : mx0) : -INFINITY, redv);
 
-    // ---- weights (the reference's polynomial softmax over the global maximum)
+    // The weights (the reference's polynomial softmax over the global
+    // maximum) are formed from the scores tile by tile in the weighted-V
+    // pass, which also sums them.
     const int n8 = n - (n % 8);
-    float lsum[G];
-#pragma unroll
-    for (int g = 0; g < G; g++) lsum[g] = 0.0f;
-    for (int p = threadIdx.x; p < n; p += DA_THREADS) {
-#pragma unroll
-        for (int g = 0; g < G; g++) {
-            float w = softmax_weight(S[(size_t)p * G + g], gmax[g], p, n8);
-            S[(size_t)p * G + g] = w;
-            lsum[g] += w;
-        }
-    }
-    float total[G];
-#pragma unroll
-    for (int g = 0; g < G; g++) total[g] = block_sum(lsum[g], redv);  // also orders the weight writes
 
     // ---- weighted V: rows q4 of A = head q4 % 4, hi (q4 < 4) or lo
     float acc[HD / 8][4];
@@ -834,20 +822,26 @@ __global__ void __launch_bounds__(DA_THREADS, 2) k_dattn_mma(DecAttnParams P) {
     for (int j = 0; j < HD / 8; j++) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
     const int ga = q4 & 3;
     const bool alo = q4 >= 4, avalid = ga < G;
-    dm_stage<HD>(vbase, warp, n, ring);
-    dm_stage<HD>(vbase, warp + DA_WARPS, n, ring + SLOT);
+    float gm = gmax[0];  // global maximum of head ga
+#pragma unroll
+    for (int g = 1; g < G; g++)
+        if (ga == g) gm = gmax[g];
+    float lsum = 0.0f;  // lanes 0-15 (the hi rows): this lane's share of head ga's weight sum
+#pragma unroll
+    for (int i = 0; i < NS; i++) dm_stage<HD>(vbase, warp + i * DA_WARPS, n, ring + i * SLOT);
     for (int tile = warp, it = 0; tile < ntiles; tile += DA_WARPS, it++) {
         const int p0 = tile * DM_TILE + 2 * t;
+        cp_async_wait<NS - 1>();
+        __syncwarp();
+        const uint4* sl = ring + (it % NS) * SLOT;
         float w[4];
 #pragma unroll
         for (int i = 0; i < 4; i++) {
             const int p = p0 + (i & 1) + 8 * (i >> 1);
-            w[i] = (avalid && p < n) ? S[(size_t)p * G + ga] : 0.0f;
+            w[i] = (avalid && p < n) ? softmax_weight(S[(size_t)p * G + ga], gm, p, n8) : 0.0f;
+            if (!alo) lsum += w[i];
         }
         const uint32_t a[4] = {split_pair(w[0], w[1], alo), 0u, split_pair(w[2], w[3], alo), 0u};
-        cp_async_wait<1>();
-        __syncwarp();
-        const uint4* sl = ring + (it & 1) * SLOT;
 #pragma unroll
         for (int j = 0; j < HD / 16; j++) {
             const int mi = lane >> 3, r = (lane & 7) + 8 * (mi & 1);
@@ -857,7 +851,7 @@ __global__ void __launch_bounds__(DA_THREADS, 2) k_dattn_mma(DecAttnParams P) {
             mma16816(acc[2 * j + 1], a, b[2], b[3]);
         }
         __syncwarp();
-        dm_stage<HD>(vbase, tile + 2 * DA_WARPS, n, ring + (it & 1) * SLOT);
+        dm_stage<HD>(vbase, tile + NS * DA_WARPS, n, ring + (it % NS) * SLOT);
     }
     cp_async_wait<0>();
     // rows q4 and q4 + 4 (lanes l and l + 16) are the hi and lo sums of head q4
@@ -866,6 +860,9 @@ __global__ void __launch_bounds__(DA_THREADS, 2) k_dattn_mma(DecAttnParams P) {
         acc[j][0] += __shfl_down_sync(0xffffffffu, acc[j][0], 16);
         acc[j][1] += __shfl_down_sync(0xffffffffu, acc[j][1], 16);
     }
+    float total[G];
+#pragma unroll
+    for (int g = 0; g < G; g++) total[g] = block_sum(lane < 16 && q4 == g ? lsum : 0.0f, redv);
     __syncthreads();  // every warp is done with its ring: the buffer becomes the reduction area
     if (lane < 16 && q4 < G) {
 #pragma unroll
@@ -1141,10 +1138,10 @@ int launch_dattn_ghd(const DecAttnParams& P, int rows, cudaStream_t s) {
         HC_CHECK(smem <= 220 * 1024, HC_ERR_UNSUPPORTED, "decode attention: context %d too long for one split",
                  P.max_pos);
         if constexpr (sizeof(KT) == 2 && (G == 1 || G == 2 || G == 4) && (HD == 64 || HD == 128)) {
-            // tensor-core variant: rings of 16-row tiles, two CTAs per SM
-            const size_t mring_floats = (size_t)DA_WARPS * DM_NS * DM_TILE * HD / 2;
-            const size_t smem_m =
-                (red_offset(G * P.max_pos) + std::max<size_t>((size_t)DA_WARPS * G * HD, mring_floats)) * sizeof(float);
+            // tensor-core variant: two ring stages per warp, two CTAs per SM
+            const size_t smem_m = (red_offset(G * P.max_pos) +
+                                   std::max<size_t>((size_t)DA_WARPS * G * HD, (size_t)DA_WARPS * DM_TILE * HD)) *
+                                  sizeof(float);
             if (smem_m <= 112 * 1024) {
                 if (smem_m > 48 * 1024)
                     HC_CUDA(cudaFuncSetAttribute(k_dattn_mma<G, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
