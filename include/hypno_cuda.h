@@ -113,7 +113,7 @@ int hc_q4_matmul_dev(const hc_q4_matrix* w, const float* x, size_t mtok, float* 
  * handed to its own pool at start-up, or code that may not call cudaMalloc,
  * which can synchronize the device, while other work is in flight).  This
  * entry point has no counterpart in the reference engine.  It allocates
- * nothing: tensor-core shapes (mtok >= 2, k % 128 == 0, n >= 128) keep their
+ * nothing: tensor-core shapes (mtok >= 2, k % 256 == 0, n >= 128) keep their
  * scratch in a fixed 8 MiB array inside the library's device image (held by
  * every GPU that loads the library until the process exits) and require
  * mtok * k * 2 <= 8 MiB - 256 bytes, else HC_ERR_INVALID; other shapes use the
