@@ -814,7 +814,8 @@ int choose_splits(size_t tiles, size_t nk, const int* slots, int nsm, bool dual,
     int best = 1;
     double best_cost = 1e300;
     for (size_t sp = 1; sp <= (size_t)max_sp && (sp == 1 || nk / sp >= 2); sp++) {
-        const int sl_raw = max_part > 0 ? slots[1] : slots[sp];
+        // slabs: plain CTAs, two per SM for the dual (decode) kernels by design
+        const int sl_raw = max_part > 0 ? nsm * (dual ? 2 : 1) : slots[sp];
         const size_t sl = (size_t)(sl_raw > 0 ? sl_raw : 1);
         const size_t ctas = tiles * sp;
         const size_t waves = (ctas + sl - 1) / sl;
