@@ -726,8 +726,11 @@ __device__ __forceinline__ void dm_stage(const __half* __restrict__ base, int ti
 }
 }  // namespace
 
-template <int G, int HD>
-__global__ void __launch_bounds__(DA_THREADS, 2) k_dattn_mma(DecAttnParams P) {
+// NW warps per CTA: 8 (two CTAs per SM) when the pairs fill the GPU, 16 (one
+// CTA per SM, twice the copies in flight) when there are only about as many
+// pairs as SMs.
+template <int G, int HD, int NW>
+__global__ void __launch_bounds__(NW * 32, 16 / NW) k_dattn_mma(DecAttnParams P) {
     constexpr int NS = 2;  // ring stages per warp
     static_assert(G == 1 || G == 2 || G == 4, "hi and lo columns of G heads in 8");
     static_assert(HD == 64 || HD == 128, "feature tiles");
@@ -742,7 +745,7 @@ __global__ void __launch_bounds__(DA_THREADS, 2) k_dattn_mma(DecAttnParams P) {
     const int seq = P.seqs[row];
     const int n = min(P.pos[seq], P.max_pos);
     if (n <= 1) {
-        for (int i = threadIdx.x; i < G * HD; i += DA_THREADS)
+        for (int i = threadIdx.x; i < G * HD; i += NW * 32)
             da_write_out(P, row, kvh * G + i / HD, i % HD, P.vself[(size_t)row * P.ldself + (size_t)kvh * HD + i % HD]);
         return;
     }
@@ -773,8 +776,8 @@ __global__ void __launch_bounds__(DA_THREADS, 2) k_dattn_mma(DecAttnParams P) {
     // ---- scores
     float mx0 = -INFINITY, mx1 = -INFINITY;  // heads 2t, 2t + 1 (lanes t < 2)
 #pragma unroll
-    for (int i = 0; i < NS; i++) dm_stage<HD>(kbase, warp + i * DA_WARPS, n, ring + i * SLOT);
-    for (int tile = warp, it = 0; tile < ntiles; tile += DA_WARPS, it++) {
+    for (int i = 0; i < NS; i++) dm_stage<HD>(kbase, warp + i * NW, n, ring + i * SLOT);
+    for (int tile = warp, it = 0; tile < ntiles; tile += NW, it++) {
         cp_async_wait<NS - 1>();
         __syncwarp();  // every lane's copies of this tile landed
         const uint4* sl = ring + (it % NS) * SLOT;
@@ -804,7 +807,7 @@ __global__ void __launch_bounds__(DA_THREADS, 2) k_dattn_mma(DecAttnParams P) {
             }
         }
         __syncwarp();  // the slot is read: refill it NS tiles ahead
-        dm_stage<HD>(kbase, tile + NS * DA_WARPS, n, ring + (it % NS) * SLOT);
+        dm_stage<HD>(kbase, tile + NS * NW, n, ring + (it % NS) * SLOT);
     }
     cp_async_wait<0>();
     float gmax[G];
@@ -828,8 +831,8 @@ __global__ void __launch_bounds__(DA_THREADS, 2) k_dattn_mma(DecAttnParams P) {
         if (ga == g) gm = gmax[g];
     float lsum = 0.0f;  // lanes 0-15 (the hi rows): this lane's share of head ga's weight sum
 #pragma unroll
-    for (int i = 0; i < NS; i++) dm_stage<HD>(vbase, warp + i * DA_WARPS, n, ring + i * SLOT);
-    for (int tile = warp, it = 0; tile < ntiles; tile += DA_WARPS, it++) {
+    for (int i = 0; i < NS; i++) dm_stage<HD>(vbase, warp + i * NW, n, ring + i * SLOT);
+    for (int tile = warp, it = 0; tile < ntiles; tile += NW, it++) {
         const int p0 = tile * DM_TILE + 2 * t;
         cp_async_wait<NS - 1>();
         __syncwarp();
@@ -851,7 +854,7 @@ __global__ void __launch_bounds__(DA_THREADS, 2) k_dattn_mma(DecAttnParams P) {
             mma16816(acc[2 * j + 1], a, b[2], b[3]);
         }
         __syncwarp();
-        dm_stage<HD>(vbase, tile + NS * DA_WARPS, n, ring + (it % NS) * SLOT);
+        dm_stage<HD>(vbase, tile + NS * NW, n, ring + (it % NS) * SLOT);
     }
     cp_async_wait<0>();
     // rows q4 and q4 + 4 (lanes l and l + 16) are the hi and lo sums of head q4
@@ -871,10 +874,10 @@ __global__ void __launch_bounds__(DA_THREADS, 2) k_dattn_mma(DecAttnParams P) {
                 make_float2(acc[j][0], acc[j][1]);
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < G * HD; i += DA_THREADS) {
+    for (int i = threadIdx.x; i < G * HD; i += NW * 32) {
         float o = 0.0f;
 #pragma unroll
-        for (int w = 0; w < DA_WARPS; w++) o += red[(size_t)w * G * HD + i];
+        for (int w = 0; w < NW; w++) o += red[(size_t)w * G * HD + i];
         da_write_out(P, row, kvh * G + i / HD, i % HD, __fdiv_rn(o, total[i / HD]));
     }
 }
@@ -1138,15 +1141,24 @@ int launch_dattn_ghd(const DecAttnParams& P, int rows, cudaStream_t s) {
         HC_CHECK(smem <= 220 * 1024, HC_ERR_UNSUPPORTED, "decode attention: context %d too long for one split",
                  P.max_pos);
         if constexpr (sizeof(KT) == 2 && (G == 1 || G == 2 || G == 4) && (HD == 64 || HD == 128)) {
-            // tensor-core variant: two ring stages per warp, two CTAs per SM
-            const size_t smem_m = (red_offset(G * P.max_pos) +
-                                   std::max<size_t>((size_t)DA_WARPS * G * HD, (size_t)DA_WARPS * DM_TILE * HD)) *
-                                  sizeof(float);
-            if (smem_m <= 112 * 1024) {
+            // tensor-core variant: two ring stages per warp; P.wide: 16 warps,
+            // one CTA per SM, else 8 warps, two CTAs per SM
+            const int nw = P.wide ? 16 : DA_WARPS;
+            const size_t smem_m =
+                (red_offset(G * P.max_pos) + std::max<size_t>((size_t)nw * G * HD, (size_t)nw * DM_TILE * HD)) *
+                sizeof(float);
+            if (P.wide && smem_m <= 220 * 1024) {
+                HC_CUDA(cudaFuncSetAttribute(k_dattn_mma<G, HD, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem_m));
+                k_dattn_mma<G, HD, 16><<<dim3((unsigned)rows, (unsigned)P.nkv), 16 * 32, smem_m, s>>>(P);
+                HC_LAUNCH_CHECK();
+                return HC_OK;
+            }
+            if (!P.wide && smem_m <= 112 * 1024) {
                 if (smem_m > 48 * 1024)
-                    HC_CUDA(cudaFuncSetAttribute(k_dattn_mma<G, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                    HC_CUDA(cudaFuncSetAttribute(k_dattn_mma<G, HD, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  (int)smem_m));
-                k_dattn_mma<G, HD><<<dim3((unsigned)rows, (unsigned)P.nkv), DA_THREADS, smem_m, s>>>(P);
+                k_dattn_mma<G, HD, 8><<<dim3((unsigned)rows, (unsigned)P.nkv), DA_THREADS, smem_m, s>>>(P);
                 HC_LAUNCH_CHECK();
                 return HC_OK;
             }
@@ -1208,6 +1220,14 @@ int launch_dattn_kt(const DecAttnParams& P, int rows, cudaStream_t s) {
 }
 
 }  // namespace
+
+bool dattn_wide_ok(int nh, int nkv, int hd, int max_pos, int kv_fp16) {
+    const int g = nh / nkv;
+    if (!kv_fp16 || !(g == 1 || g == 2 || g == 4) || !(hd == 64 || hd == 128)) return false;
+    const size_t smem = (red_offset(g * max_pos) + std::max<size_t>((size_t)16 * g * hd, (size_t)16 * DM_TILE * hd)) *
+                        sizeof(float);
+    return smem <= 220 * 1024;
+}
 
 bool dattn_supported(int nh, int nkv, int hd) {
     int g = nh / nkv;

@@ -63,8 +63,13 @@ struct DecAttnParams {
     float* spart;         // [rows][nh][nsplit]
     __half* out16 = nullptr;  // optional fp16 copy of out (rows of nh*hd, GEMM K order)
     int cluster = 1;          // > 1: that many CTAs of a cluster share a (sequence, KV head), chunk positions each
+    int wide = 0;             // whole context (nsplit 1): one 16-warp CTA per SM (see dattn_wide_ok)
 };
 bool dattn_supported(int nh, int nkv, int hd);
+// The whole-context pass with one 16-warp CTA per (sequence, KV head) is
+// available (fp16 cache, 1, 2 or 4 heads per KV head, head_dim 64 or 128,
+// scores of max_pos positions in shared memory).
+bool dattn_wide_ok(int nh, int nkv, int hd, int max_pos, int kv_fp16);
 // Tiled f32 prefill attention over the prompt's own K/V rows (mode_prefill).
 bool pattn_supported(int hd);
 int launch_prefill_attention(const AttnParams& P, int T, cudaStream_t s);

@@ -684,7 +684,14 @@ int run_layers(hc_model* m, hc_kv* kv, size_t rows, bool prefill, int seq, int p
             int ncl = 1;  // CTAs of a cluster sharing one (sequence, KV head) when the pairs are too few
             while (!whole && ncl < 8 && ctas * ncl * 4 < slots * 3) ncl *= 2;
             const int cl_chunk = (kv->max_pos + ncl - 1) / ncl;
-            if (whole && G * kv->max_pos + 4 + red_floats <= smem_floats) {
+            // about one pair per SM: one 16-warp tensor-core CTA each
+            const bool wide = !whole && ctas * 3 >= 148 * 2 && ctas <= 148 &&
+                              hc::dattn_wide_ok((int)nh_l, (int)nkv_l, (int)hd, kv->max_pos, kv->kv_fp16);
+            if (wide) {
+                D.chunk = kv->max_pos;
+                D.nsplit = 1;
+                D.wide = 1;
+            } else if (whole && G * kv->max_pos + 4 + red_floats <= smem_floats) {
                 D.chunk = kv->max_pos;
                 D.nsplit = 1;
             } else if (!whole && ctas * ncl * 4 >= slots * 3 && G * cl_chunk + 4 + red_floats <= smem_floats) {

@@ -215,12 +215,13 @@ def test_c4_geometry_batched_decode(cuda_device, kv_dtype):
         toks = nxt
 
 
-@pytest.mark.parametrize("n_seqs", [16, 40, 120])
+@pytest.mark.parametrize("n_seqs", [16, 40, 60, 120])
 def test_decode_attention_paths(cuda_device, n_seqs):
-    """Batched decode over 16, 40 and 120 sequences of a 2-KV-head model: 32
-    and 80 (sequence, KV head) pairs run the cluster-split attention (clusters
-    of 8 and 4 CTAs, contexts split at 128- and 256-position boundaries), 240
-    pairs the single fused pass (its tensor-core form for the fp16 cache).  Ragged contexts (0..299 cached positions, so
+    """Batched decode over 16, 40, 60 and 120 sequences of a 2-KV-head model:
+    32 and 80 (sequence, KV head) pairs run the cluster-split attention
+    (clusters of 8 and 4 CTAs, contexts split at 128- and 256-position
+    boundaries), 120 pairs one 16-warp tensor-core CTA each, 240 pairs the
+    single fused pass (its tensor-core form for the fp16 cache).  Ragged contexts (0..299 cached positions, so
     some cluster CTAs own no positions) against the oracle for 2 steps."""
     from hypno_b200 import synth as sy
     img = sy.build_image(C4_GEOMETRY, seed=3, quantize=orc.quantize_f32_to_q4_0)
