@@ -76,6 +76,17 @@ class ClockSampler:
         self.proc = None
         self.thread = None
         self.rows = []
+        self.start = 0
+
+    def wait_first(self, limit_s=2.0):
+        """Wait (bounded) until the sampling thread has taken its first sample."""
+        t_end = time.perf_counter() + limit_s
+        while self.thread is not None and not self.rows and time.perf_counter() < t_end:
+            time.sleep(0.001)
+
+    def mark(self):
+        """Start of the timed region: the summary keeps the samples from here on."""
+        self.start = len(self.rows)
 
     def _handle(self, nv):
         try:
@@ -144,12 +155,13 @@ class ClockSampler:
 
     def summary(self):
         if self.thread is not None:
-            if not self.rows:
+            rows = self.rows[self.start:] or self.rows[-1:]
+            if not rows:
                 return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "source": "nvml"}
-            sm = sorted(r[0] for r in self.rows)
-            reasons = sorted({n for r in self.rows for n, bit in self.REASONS if r[2] & bit})
-            return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": max(r[1] for r in self.rows), "reasons": reasons,
-                    "samples": len(self.rows), "source": "nvml"}
+            sm = sorted(r[0] for r in rows)
+            reasons = sorted({n for r in rows for n, bit in self.REASONS if r[2] & bit})
+            return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": max(r[1] for r in rows), "reasons": reasons,
+                    "samples": len(rows), "source": "nvml"}
         if self.proc is None or not os.path.exists(self.path):
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         rows = []
@@ -385,6 +397,9 @@ def run_ours(args):
     e0, e1 = tc.Event(enable_timing=True), tc.Event(enable_timing=True)
     es = torch.cuda.ExternalStream(stream)
     torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+        torch.cuda.synchronize()
     e0.record(es)
     for s in range(S):
         logits = engine.batch_forward(model, prompts[s], kv, seq=s)
@@ -410,17 +425,23 @@ def run_ours(args):
         step(i)
     reset_pos()
     torch.cuda.synchronize()
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize()
-    l0 = lib.hc_kernel_launches()
-    torch.cuda.nvtx.range_push("timed_decode")
+    # The sampler starts (NVML init takes a different time in each process)
+    # before the ranks line up: a rank that starts its timed region early
+    # would otherwise spend the difference waiting in the first step's
+    # cross-rank exchange, inside its own events.
     with ClockSampler(local, os.path.join(ROOT, "gpurun_out", f"clocks_rank{rank}.csv")
                       if os.path.isdir(os.path.join(ROOT, "gpurun_out")) else f"/tmp/hc_clocks_{rank}.csv") as clk:
+        clk.wait_first()
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        clk.mark()
+        l0 = lib.hc_kernel_launches()
+        torch.cuda.nvtx.range_push("timed_decode")
         ms = cuda_time_ms(stream, step, args.steps) * args.steps
         torch.cuda.synchronize()
-    torch.cuda.nvtx.range_pop()
-    launches = lib.hc_kernel_launches() - l0
+        torch.cuda.nvtx.range_pop()
+        launches = lib.hc_kernel_launches() - l0
     if dist:
         dist.barrier()
         t = torch.tensor([ms], device=dev)
