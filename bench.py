@@ -542,6 +542,8 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
+    if args.steps < 1:
+        ap.error("--steps must be >= 1")
     if args.steps + args.warmup > 250:
         ap.error("steps + warmup must fit the 256 decode positions of the c4 workload")
     if args.impl == "reference":

@@ -1,0 +1,56 @@
+"""Host-side pieces of bench.py that need no GPU: the workload description per
+parallel layout, the clock-sample summary (samples taken before the timed
+region do not count), and the argument rules of the timing contract."""
+import os
+import subprocess
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+import bench  # noqa: E402
+
+
+def test_workload_config_layouts():
+    one = bench.workload_config(1)
+    assert one["parallelism"] == "single" and one["global_batch"] == 32 and one["seq_len"] == 2048
+    tp = bench.workload_config(4, "tp")
+    assert tp["parallelism"] == "tp4" and tp["global_batch"] == 32  # strong scaling: same 32 sequences
+    dp = bench.workload_config(4, "dp")
+    assert dp["parallelism"] == "replicas4" and dp["global_batch"] == 128  # one c4 job per rank
+
+
+def test_clock_summary_keeps_timed_samples_only():
+    c = bench.ClockSampler(0, os.devnull)
+    c.thread = object()  # as if the NVML thread ran
+    c.rows = [(900.0, 1965.0, 0x0, 100.0), (1200.0, 1965.0, 0x8, 200.0)]  # before the timed region
+    c.mark()
+    c.rows += [(1965.0, 1965.0, 0x4, 900.0), (1950.0, 1965.0, 0x0, 950.0), (1965.0, 1965.0, 0x0, 940.0)]
+    s = c.summary()
+    assert s["samples"] == 3 and s["sm_mhz"] == 1965.0 and s["sm_max_mhz"] == 1965.0
+    assert s["reasons"] == ["sw_power_cap"]  # the hw_slowdown sample came before the mark
+
+
+def test_clock_summary_without_timed_samples_uses_last():
+    c = bench.ClockSampler(0, os.devnull)
+    c.thread = object()
+    c.rows = [(1965.0, 1965.0, 0x0, 120.0)]
+    c.mark()
+    s = c.summary()
+    assert s["samples"] == 1 and s["sm_mhz"] == 1965.0
+
+
+def test_clock_wait_first_is_bounded():
+    c = bench.ClockSampler(0, os.devnull)
+    c.thread = object()  # a thread that never samples
+    c.wait_first(limit_s=0.05)
+    assert c.rows == []
+
+
+@pytest.mark.parametrize("argv", [["--warmup", "2"], ["--steps", "0"], ["--steps", "248", "--warmup", "3"]])
+def test_timing_contract_arguments(argv):
+    r = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py")] + argv, capture_output=True, text=True,
+                       timeout=120)
+    assert r.returncode != 0 and ("warmup" in r.stderr or "steps" in r.stderr)
