@@ -79,6 +79,7 @@ class KVCache:
         self._h = h
         self.model = model
         self.n_seqs = n_seqs
+        self.max_pos = max_pos if max_pos > 0 else int(model.config.max_position_embeddings)
 
     @property
     def handle(self):
