@@ -6,7 +6,10 @@ import numpy as np
 from hypno_b200 import synth
 from oracle import oracle as orc
 
-SMALL = dict(hidden=128, inter=256, heads=4, kv_heads=2, layers=2, vocab=512, theta=10000.0, max_pos=48,
+# head_dim 64, GQA group 2; with std 0.5 every greedy pick of request_mix has a
+# top-2 margin of at least 2.4x the logits tolerance (1e-3 of max(1, max|logit|)),
+# apart from the empty prompt's all-zero logits (an exact tie everywhere)
+SMALL = dict(hidden=256, inter=512, heads=4, kv_heads=2, layers=2, vocab=512, theta=10000.0, max_pos=48,
              embed="fp32", lm_head="separate")
 
 
@@ -14,14 +17,17 @@ def small_image(seed=3):
     return synth.build_image(SMALL, seed=seed, std=0.5, quantize=orc.quantize_f32_to_q4_0)
 
 
-def serial_generation(om, prompt, max_tokens, eos_id, max_pos):
+def serial_generation(om, prompt, max_tokens, eos_id, max_pos, seen=None):
     """serve.rs:239-255 with the greedy pick (run.rs:234-238), one request
     alone on a fresh cache; stops with "length" where the next forward would
-    need a position the cache does not have."""
+    need a position the cache does not have.  `seen` collects the logits each
+    pick was made from."""
     kv = om.new_kv(max_pos)
     logits = orc.batch_forward(om, prompt, kv)
     toks, reason = [], "stop"
     for _ in range(max_tokens):
+        if seen is not None:
+            seen.append(logits)
         nxt = orc.greedy(logits)
         if eos_id is not None and nxt == eos_id:
             reason = "stop"
