@@ -429,8 +429,8 @@ def run_ours(args):
     # before the ranks line up: a rank that starts its timed region early
     # would otherwise spend the difference waiting in the first step's
     # cross-rank exchange, inside its own events.
-    with ClockSampler(local, os.path.join(ROOT, "gpurun_out", f"clocks_rank{rank}.csv")
-                      if os.path.isdir(os.path.join(ROOT, "gpurun_out")) else f"/tmp/hc_clocks_{rank}.csv") as clk:
+    clk_dir = os.environ.get("HC_CLOCKS_DIR", "/tmp")  # where the per-rank clock samples are kept
+    with ClockSampler(local, os.path.join(clk_dir, f"clocks_rank{rank}.csv")) as clk:
         clk.wait_first()
         if dist:
             dist.barrier()

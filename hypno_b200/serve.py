@@ -156,7 +156,7 @@ class BatchScheduler:
     def step(self):
         """Admits waiting requests into free slots (prefill each), then runs one
         batched decode over every running request.  Returns the (request id,
-        token) pairs emitted in this round: the admitted requests' first
+        token) pairs emitted by this call: the admitted requests' first
         tokens in admission order, then the decode's in slot order."""
         emitted = []
         while self.waiting and self.free:

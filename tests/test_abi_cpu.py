@@ -99,8 +99,8 @@ def test_compute_without_gpu_fails_loudly(lib):
     assert e.value.code == -2
 
 
-def test_model_bytes_match_survey_figures():
-    # per-step Q4_0 weight bytes quoted for the configs
+def test_model_bytes_match_quoted_figures():
+    # per-step Q4_0 weight bytes of the benchmark configs (0.5625 B per weight)
     assert synth.model_bytes(synth.CONFIGS["c1"]) == 75_644_928
     assert synth.model_bytes(synth.CONFIGS["c3"]) == 581_861_376
     assert synth.model_bytes(synth.CONFIGS["c4"]) == 4_221_370_368
