@@ -475,6 +475,28 @@ def run_ours(args):
     e2e = {"value": round(jobs * S * args.steps / e2e_s, 2), "unit": UNIT,
            "h2d_bytes_per_step": 2 * 4 * S, "d2h_bytes_per_step": 4 * S}
 
+    # ---- optional: the same 32 requests through the continuous-batching
+    # scheduler (prefill of each prompt + `steps` greedy tokens each), wall-clocked
+    serve = None
+    if args.serve:
+        from hypno_b200.serve import BatchScheduler
+        sch = BatchScheduler(model, kv)
+        for s in range(S):
+            sch.submit(prompts[s], args.steps)
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        done = sch.run()
+        serve_s = time.perf_counter() - t0
+        if dist:
+            t = torch.tensor([serve_s], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            serve_s = float(t.item())
+        ntok = sum(r.completion_tokens for r in done.values())
+        serve = {"requests": S, "prompt_tokens": S * P, "completion_tokens": ntok, "seconds": round(serve_s, 3),
+                 "completion_tok_s": round(ntok / serve_s, 1), "decode_rounds": sch.decode_steps}
+
     roof = roofline_gemv(dev) if rank == 0 else None
     sweep = q4_sweep(dev) if rank == 0 and not args.no_sweep else None
     cpu = None
@@ -489,6 +511,8 @@ def run_ours(args):
                 "config": dict(workload_config(world, "tp" if tp else "dp"), layers=cfg["layers"]), "e2e": e2e, "gpu_launches": int(launches),
                 "prefill_tok_s": round(prefill_tok_s, 1), "clocks": clk.summary(), "roofline": roof,
                 "cpu_baseline": cpu, "q4_sweep": sweep}
+        if serve is not None:
+            line["serve"] = serve
         print(json.dumps(line), flush=True)
     kv.close()
     model.close()
@@ -537,6 +561,8 @@ def main():
     ap.add_argument("--no-sweep", action="store_true", help="skip the configs[1] operator sweep report")
     ap.add_argument("--layers", type=int, default=0,
                     help="override the layer count (a small case for ncu captures; reported in config)")
+    ap.add_argument("--serve", action="store_true",
+                    help="also time the requests end to end through hypno_b200.serve.BatchScheduler")
     ap.add_argument("--parallel", default="tp", choices=["tp", "dp"],
                     help="N > 1: tensor parallel over the ranks (default) or independent replicas")
     args = ap.parse_args()
