@@ -110,3 +110,28 @@ def test_submit_rejects():
         BatchScheduler()
     with pytest.raises(ValueError):
         BatchScheduler(prefill=lambda s, i: None, decode=lambda s, i, w: None, n_slots=0, max_pos=8)
+
+
+def test_planted_decode_error_is_seen(om):
+    """The comparison has teeth: one wrong token planted in one batched decode
+    (host model, one slot, one round) shows up in exactly the request that
+    owned that slot."""
+    reqs = request_mix(SMALL["vocab"])
+    want = _expected(om, reqs, None)
+    hb = HostBackend(om, 3, SMALL["max_pos"])
+    calls = {"n": 0}
+
+    def bad_decode(slots, ids, want_logits):
+        logits, greedy = hb.decode(slots, ids, want_logits)
+        calls["n"] += 1
+        if calls["n"] == 3:
+            greedy = greedy.copy()
+            greedy[-1] = (int(greedy[-1]) + 1) % SMALL["vocab"]
+            bad_decode.slot = slots[-1]
+        return logits, greedy
+
+    sch = BatchScheduler(prefill=hb.prefill, decode=bad_decode, n_slots=3, max_pos=SMALL["max_pos"])
+    ids = [sch.submit(p, m) for p, m in reqs]
+    out = sch.run()
+    wrong = [rid for rid in ids if out[rid].tokens != want[rid][0]]
+    assert len(wrong) == 1 and out[wrong[0]].slot == bad_decode.slot
