@@ -39,10 +39,20 @@ __all__ = ["Request", "BatchScheduler", "greedy_last_max"]
 
 
 def greedy_last_max(logits):
-    """Last index of the maximum (Iterator::max_by keeps the last of equals,
-    run.rs:234-238)."""
-    v = np.asarray(logits)
-    return int(np.flatnonzero(v == v.max())[-1])
+    """Index picked by `max_by(|a, b| a.partial_cmp(b).unwrap_or(Equal))`
+    (run.rs:234-238, serve.rs:300): the last index of the maximum; 0 for no
+    logits.  A NaN compares Equal with everything, so the fold moves onto it
+    and past it; that slow path runs only when a NaN is present."""
+    v = np.asarray(logits).reshape(-1)
+    if v.size == 0:
+        return 0
+    if not np.isnan(v).any():
+        return int(np.flatnonzero(v == v.max())[-1])
+    best = 0
+    for i in range(1, v.size):      # fold: keep `best` only while it is strictly greater
+        if not (v[best] > v[i]):
+            best = i
+    return best
 
 
 class Request:

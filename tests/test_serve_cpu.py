@@ -135,3 +135,12 @@ def test_planted_decode_error_is_seen(om):
     out = sch.run()
     wrong = [rid for rid in ids if out[rid].tokens != want[rid][0]]
     assert len(wrong) == 1 and out[wrong[0]].slot == bad_decode.slot
+
+
+def test_greedy_pick_follows_max_by():
+    nan = float("nan")
+    assert greedy_last_max(np.array([1.0, 3.0, 3.0, 2.0], np.float32)) == 2   # last of equal maxima
+    assert greedy_last_max(np.array([], np.float32)) == 0
+    assert greedy_last_max(np.array([1.0, nan, 0.5], np.float32)) == 2        # the fold moves past a NaN
+    assert greedy_last_max(np.array([nan, 1.0, 0.5], np.float32)) == 1
+    assert greedy_last_max(np.array([2.0, 1.0, nan], np.float32)) == 2
