@@ -61,7 +61,7 @@ __global__ void __launch_bounds__(128) k_attention(AttnParams P) {
     if (n <= 1) {
         for (int d = threadIdx.x; d < hd; d += blockDim.x) {
             out[d] = vself[d];
-            if (P.out16) P.out16[(size_t)row * P.nh * hd + perm_k(h * hd + d)] = __float2half_rn(vself[d]);
+            if (P.out16) store_x16(P.out16 + (size_t)row * 2 * P.nh * hd, P.nh * hd, h * hd + d, vself[d]);
         }
         return;
     }
@@ -104,7 +104,7 @@ __global__ void __launch_bounds__(128) k_attention(AttnParams P) {
     for (int d = threadIdx.x; d < hd; d += blockDim.x) {
         float o = (part[d] + part[hd + d]) + (part[2 * hd + d] + part[3 * hd + d]);
         out[d] = o;
-        if (P.out16) P.out16[(size_t)row * P.nh * hd + perm_k(h * hd + d)] = __float2half_rn(o);
+        if (P.out16) store_x16(P.out16 + (size_t)row * 2 * P.nh * hd, P.nh * hd, h * hd + d, o);
     }
 }
 
@@ -578,7 +578,7 @@ __device__ __forceinline__ void da_load_q(const DecAttnParams& P, int row, int k
 
 __device__ __forceinline__ void da_write_out(const DecAttnParams& P, int row, int h, int d, float v) {
     P.out[(size_t)row * P.ldo + (size_t)h * P.hd + d] = v;
-    if (P.out16) P.out16[(size_t)row * P.nh * P.hd + perm_k(h * P.hd + d)] = __float2half_rn(v);
+    if (P.out16) store_x16(P.out16 + (size_t)row * 2 * P.nh * P.hd, P.nh * P.hd, h * P.hd + d, v);
 }
 
 // Block maxima per head of the lanes' maxima (one head per lane when the
@@ -1380,13 +1380,13 @@ __global__ void __launch_bounds__(PA_THREADS) k_pattn(AttnParams P, int T) {
         int t = t0 + ty * 4 + i;
         if (t >= T) continue;
         float* out = P.out + (size_t)t * P.ldo + (size_t)h * HD + tx * DC;
-        __half* o16 = P.out16 ? P.out16 + (size_t)t * P.nh * HD : nullptr;
+        __half* o16 = P.out16 ? P.out16 + (size_t)t * 2 * P.nh * HD : nullptr;
         const float* vs = P.vself + (size_t)t * P.ldself + (size_t)kvh * HD + tx * DC;
 #pragma unroll
         for (int j = 0; j < DC; j++) {
             float r = (t < 2) ? vs[j] : __fdiv_rn(o[i][j], rsum[i]);
             out[j] = r;
-            if (o16) o16[perm_k(h * HD + tx * DC + j)] = __float2half_rn(r);
+            if (o16) store_x16(o16, P.nh * HD, h * HD + tx * DC + j, r);
         }
     }
 }

@@ -36,6 +36,21 @@ int gemm_tc_partials(GemmWorkspace* ws, const hc_q4_matrix& w, const float* x, s
 // Index of element e of a row in the GEMM's fp16 K order.
 __host__ __device__ inline int perm_k(int e) { return (e & ~7) | ((e & 3) << 1) | ((e >> 2) & 1); }
 
+#ifdef __CUDACC__
+// The tensor-core GEMM reads its activations as one row of 2k fp16 values per
+// token: hi = fp16(v) in the first k, lo = fp16(v - hi) in the second k (both
+// in perm_k order).  v - hi is exact in f32, so hi + lo carries v to ~22
+// significant bits: the products of the exact two-term weights with hi and
+// lo keep the GEMM within ~1e-6 of an f32 dot product, where one fp16 operand
+// would leave errors of ~3e-4 per product.
+__device__ __forceinline__ void store_x16(__half* row, int k, int e, float v) {
+    const __half h = __float2half_rn(v);
+    const int p = perm_k(e);
+    row[p] = h;
+    row[k + p] = __float2half_rn(__fsub_rn(v, __half2float(h)));
+}
+#endif
+
 // Reads and clears the device flag set by a timed-out pipeline wait
 // (synchronizes the device); HC_ERR_TIMEOUT when a kernel aborted.
 int gemm_check(GemmWorkspace* ws);

@@ -56,17 +56,6 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
 __device__ __forceinline__ void tmem_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tmem_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-__device__ __forceinline__ void tmem_st_x32(uint32_t taddr, const uint32_t* v) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
-        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
-        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
-        "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
-        "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
-        : "memory");
-}
-
 __device__ __forceinline__ void tmem_ld_x16(uint32_t taddr, uint32_t* v) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
@@ -168,20 +157,49 @@ __device__ __forceinline__ void store_chunk(float* y, size_t ldy, const uint32_t
 // Pairs 0 and 2 (the low nibble of a byte pair) become (nib + 1024) with one
 // and/or, exact in fp16 (0x6400 | nib), minus 1032; pairs 1 and 3 are taken
 // in place as (16 nib + 1024) and turned into nib - 8 by one fma with 1/16
-// and -72, both exact; multiplying by the fp16 scale then rounds once:
-// fp16((nib - 8) * scale).  One shift serves the word's upper bytes.
-__device__ __forceinline__ void deq_word(uint32_t w, __half2 s2, uint32_t* out) {
-    const uint32_t hi = w >> 8;
+// and -72, both exact.  One shift serves the word's upper bytes.
+//
+// The weight (nib - 8) * scale (the reference dequantizes in f32,
+// quant.rs:25-34) needs up to 14 significant bits, more than fp16 holds, so
+// it enters the MMAs as two exact fp16 terms: scale = s_hi + s_lo, s_hi the
+// scale with the 3 low mantissa bits cleared (8 significant bits) and s_lo
+// the rest (3 bits); |nib - 8| <= 8 has at most 3 significant bits, so
+// (nib - 8) * s_hi (<= 11 bits) and (nib - 8) * s_lo (<= 6 bits) are both
+// exact fp16 products, and their sum is the f32 weight.
+__device__ __forceinline__ void split_scale(uint32_t s16, __half2& shi2, __half2& slo2) {
+    const bool special = (s16 & 0x7C00u) == 0x7C00u;  // inf / NaN scale: kept whole, lo = 0
+    const __half s = __ushort_as_half((unsigned short)s16);
+    const __half sh = __ushort_as_half((unsigned short)(special ? s16 : (s16 & 0xFFF8u)));
+    const __half sl = special ? __ushort_as_half((unsigned short)0) : __hsub(s, sh);  // exact
+    shi2 = __half2half2(sh);
+    slo2 = __half2half2(sl);
+}
+
+// The (hi, lo) weight pairs of one Q4_0 word: hi[k] = (nib - 8) * s_hi,
+// lo[k] = (nib - 8) * s_lo for the four pairs of the word (see above).
+__device__ __forceinline__ void deq_word_split(uint32_t w, __half2 shi2, __half2 slo2, uint32_t* hi_out,
+                                               uint32_t* lo_out) {
+    const uint32_t up = w >> 8;
     uint32_t v[4] = {(w & 0x000F000Fu) | 0x64006400u, (w & 0x00F000F0u) | 0x64006400u,
-                     (hi & 0x000F000Fu) | 0x64006400u, (hi & 0x00F000F0u) | 0x64006400u};
+                     (up & 0x000F000Fu) | 0x64006400u, (up & 0x00F000F0u) | 0x64006400u};
 #pragma unroll
     for (int k = 0; k < 4; k++) {
         __half2 h = *reinterpret_cast<__half2*>(&v[k]);
         h = (k & 1) ? __hfma2(h, __float2half2_rn(0.0625f), __float2half2_rn(-72.0f))
                     : __hsub2(h, __float2half2_rn(1032.0f));
-        h = __hmul2(h, s2);
-        out[k] = *reinterpret_cast<uint32_t*>(&h);
+        __half2 a = __hmul2(h, shi2), b = __hmul2(h, slo2);
+        hi_out[k] = *reinterpret_cast<uint32_t*>(&a);
+        lo_out[k] = *reinterpret_cast<uint32_t*>(&b);
     }
+}
+
+__device__ __forceinline__ void tmem_st_x16(uint32_t taddr, const uint32_t* v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
 }
 
 // Warp-uniform bounded wait: lane 0 polls, the verdict is broadcast, then
@@ -195,48 +213,51 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
     return ok;
 }
 
-// Pipeline shapes.  A decode tile (TN <= 64 tokens) is bound by the rate at
-// which ONE thread can issue MMAs (each tcgen05.mma of 128 x TN x 16 plus its
-// commit and the fence after a barrier wait holds the issuing thread far
-// longer than the tensor pipe needs), so two CTAs share an SM, each with 256
-// tensor-memory columns and two issuers; a prefill tile (TN >= 128) keeps one
-// CTA per SM with all 512 columns, where the larger N makes every MMA worth
-// its issue cost.
+// Pipeline shapes.  Every tile is 128 weight rows x TN tokens (TN = 32, 64
+// or 128) on one CTA per SM that owns all 512 tensor-memory columns.  The
+// MMA's B operand is 2 TN rows, the fp16 hi rows of the tile's tokens and
+// then their lo rows, so one instruction w_hi x [x_hi; x_lo] (N = 2 TN) and
+// one w_lo x x_hi (N = TN) per 16-wide K step give every product the f32
+// path needs (w_lo x x_lo is below 2^-20 of the result); the epilogue adds
+// the accumulator's two column halves.  Decode tiles (TN = 32) are bound by
+// the rate at which one thread can issue MMAs (every barrier wait, tcgen05
+// fence and commit holds the issuing thread for hundreds of cycles), so two
+// warps issue alternate stages, each into its own accumulator.
 //
 // Shared memory holds two rings.  The weight ring (nibble tile + scale box,
 // S_W stages) is released by the dequant warps as soon as they have read a
 // stage, so its depth is spent on DRAM latency alone; the X ring (S_X
-// stages) is released by the MMA commit.  Tensor memory holds S_TM A slots;
-// S_TM divides S_X, so the commit that frees X stage j % S_X also frees A
-// slot j % S_TM.
+// stages) is released by the MMA commit.  Tensor memory holds S_TM A slots of
+// 128 columns (the hi weights of a 128-K stage, then its lo weights); S_TM
+// divides S_X, so the commit that frees X stage j % S_X also frees A slot
+// j % S_TM.
 template <int TN>
 struct Cfg {
     static constexpr int TN_ = TN;
-    static constexpr bool DUAL = TN <= 64;                   // two CTAs per SM
-    static constexpr int COLS = DUAL ? 256 : 512;            // tensor-memory columns per CTA
-    static constexpr int DEQ_WARPS = DUAL ? 8 : 16;
+    static constexpr int NB = 2 * TN;                        // B rows of an MMA: hi tokens, then lo tokens
+    static constexpr int COLS = 512;                         // tensor-memory columns (one CTA per SM)
+    static constexpr int DEQ_WARPS = 16;
     static constexpr int THREADS = 128 + 32 * DEQ_WARPS;
-    static constexpr int MIN_BLOCKS = DUAL ? 2 : 1;
-    static constexpr int X_STAGE = 2 * TN * 128;             // two 64-element K halves, 128 B per token row
+    static constexpr int MIN_BLOCKS = 1;
+    static constexpr int X_STAGE = 2 * NB * 128;             // two 64-element K halves, 128 B per B row
     static constexpr int W_STAGE = BM * (BK / 2);            // 128 rows x 64 nibble bytes
     // fp16 block scales of the stage's 128 rows: the aligned 16-byte box of
     // 8 scales (this stage's 4 and its pair's) per row
     static constexpr int S_STAGE = BM * 16;
-    static constexpr int S_X = DUAL ? (TN <= 32 ? 6 : 4) : (TN == 128 ? 5 : 3);  // X ring stages
-    static constexpr int S_W = DUAL ? (TN <= 32 ? 6 : 4) : (TN == 128 ? 5 : 3);  // weight ring stages
+    static constexpr int S_X = TN <= 32 ? 6 : (TN <= 64 ? 3 : 2);  // X ring stages
+    static constexpr int S_W = TN <= 64 ? 6 : 4;                    // weight ring stages
     // Decode CTAs issue their MMAs from two warps taking alternate stages,
-    // each into its own accumulator (summed by the epilogue): every barrier
-    // wait, tcgen05 fence and commit holds the issuing thread for hundreds of
-    // cycles, so one issuer per stage halves that cost per weight.
-    static constexpr int ISS = DUAL ? 2 : 1;
-    static constexpr int A_COL = DUAL ? (ISS * TN < 64 ? 64 : ISS * TN) : TN;  // A slots start here; D_i at [i TN, (i+1) TN)
-    static constexpr int S_TM = (COLS - A_COL) / 64 < S_X ? (COLS - A_COL) / 64 : S_X;  // A slots
-    static constexpr int MMA_BATCH = S_TM < 4 ? S_TM : 4;   // stages issued under one wait + fence
-    static constexpr int RR = DUAL ? 2 : (S_TM >= 4 ? 4 : 2);  // dequant groups working on different stages
-    static constexpr int WG_PER = (DEQ_WARPS / 4) / RR;       // warpgroups per group, each 4 / WG_PER blocks
-    // decode tiles: the dequant warps wait for the weight stage before the A
-    // slot (the stage S_W back was this group's own, S_W % RR == 0)
-    static constexpr bool PRELOAD = DUAL;
+    // each into its own accumulator (summed by the epilogue).
+    static constexpr int ISS = TN <= 32 ? 2 : 1;
+    static constexpr int A_COL = ISS * NB;                   // D_i at [i NB, (i + 1) NB); A slots from here
+    static constexpr int A_SLOT = 128;                       // hi weights (64 columns), then lo weights
+    static constexpr int S_TM = (COLS - A_COL) / A_SLOT;     // A slots
+    static constexpr int MMA_BATCH = S_TM < 4 ? S_TM : 4;    // stages issued under one wait + fence
+    static constexpr int RR = 2;                             // dequant groups working on different stages
+    static constexpr int WG_PER = (DEQ_WARPS / 4) / RR;      // warpgroups per group, each 4 / WG_PER blocks
+    // the dequant warps wait for the weight stage before the A slot (the
+    // stage S_W back was this group's own, S_W % RR == 0)
+    static constexpr bool PRELOAD = true;
     __host__ __device__ static constexpr int x_off(int s) { return s * X_STAGE; }
     __host__ __device__ static constexpr int w_off(int s) { return S_X * X_STAGE + s * W_STAGE; }
     __host__ __device__ static constexpr int s_off(int s) { return S_X * X_STAGE + S_W * W_STAGE + s * S_STAGE; }
@@ -244,7 +265,8 @@ struct Cfg {
     __host__ __device__ static constexpr int bar_off() { return ring_bytes(); }
     static constexpr int NBARS = 2 * S_W + 2 * S_X + S_TM + 1;
     __host__ __device__ static constexpr int smem() { return bar_off() + NBARS * 8 + 16 + 1024; }
-    static_assert(A_COL + 64 * S_TM <= COLS && ISS * TN <= A_COL, "tensor memory budget");
+    static_assert(NB <= 256 && NB % 16 == 0, "MMA N of a 128-row tile");
+    static_assert(S_TM >= 2 && A_COL + A_SLOT * S_TM <= COLS, "tensor memory budget");
     static_assert(ISS == 1 || ISS == 2, "one or two issuing warps");
     static_assert(MMA_BATCH >= 1 && MMA_BATCH <= S_TM, "batched stages each need their own A slot");
     // two issuers: issuer i takes the stages j % 2 == i, fed by dequant group
@@ -256,24 +278,33 @@ struct Cfg {
     static_assert(S_W >= S_TM && RR <= S_X && (ISS == 1 || S_W % S_TM == 0), "barrier phase ordering (see the dequant warps)");
     static_assert(WG_PER == 1 || WG_PER == 2, "dequant split: 4 or 2 blocks per warpgroup");
     static_assert(!PRELOAD || S_W % RR == 0, "weight-first waits (see the dequant warps)");
-    static_assert(!DUAL || 2 * (smem() + 1024) <= 233472, "two CTAs must fit in one SM's shared memory");
+    static_assert(smem() <= 232448, "shared memory budget");
+    static_assert((TN * 128) % 1024 == 0, "each X box starts on a 1024-byte swizzle atom");
     static constexpr int RED_PITCH = TN + 1;                  // floats per row of the split-K partial tiles
     static_assert((BM + MAX_SPLITS) * RED_PITCH * 4 <= ring_bytes(), "split-K partials fit in the rings");
 };
 
-// Tokens [c0, c0 + EPI_CH) of TMEM lane quarter q of the accumulator (the sum
-// D_0 + D_1 when a second issuer wrote D_1).  Warp-collective.
+// Tokens [c0, c0 + EPI_CH) of TMEM lane quarter q of the accumulator: the
+// sum of its hi-token and lo-token column halves (and of D_1 when a second
+// issuer wrote it).  Warp-collective.
 template <typename C>
 __device__ __forceinline__ void load_accumulators(uint32_t tmem, int q, int c0, int nk, uint32_t* v) {
-    tmem_ld_x16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
+    const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0;
+    uint32_t a[EPI_CH];
+    tmem_ld_x16(base, v);
+    tmem_ld_x16(base + (uint32_t)C::TN_, a);
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int jj = 0; jj < EPI_CH; jj++) v[jj] = __float_as_uint(__uint_as_float(v[jj]) + __uint_as_float(a[jj]));
     if (C::ISS == 2 && nk > 1) {  // issuer 1 wrote D_1
-        uint32_t v1[EPI_CH];
-        tmem_ld_x16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(C::TN_ + c0), v1);
+        uint32_t b[EPI_CH];
+        tmem_ld_x16(base + (uint32_t)C::NB, a);
+        tmem_ld_x16(base + (uint32_t)(C::NB + C::TN_), b);
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-        for (int jj = 0; jj < EPI_CH; jj++) v[jj] = __float_as_uint(__uint_as_float(v[jj]) + __uint_as_float(v1[jj]));
+        for (int jj = 0; jj < EPI_CH; jj++)
+            v[jj] = __float_as_uint(__uint_as_float(v[jj]) + (__uint_as_float(a[jj]) + __uint_as_float(b[jj])));
     }
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
 template <int TN>
@@ -355,8 +386,14 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
                 mbar_expect_tx(&xfull[st], (uint32_t)C::X_STAGE);
                 uint8_t* xs = smem + C::x_off(st);
                 const int kk = (it0 + j) * BK;
-                tma_load_2d(xs, &xmap, &xfull[st], kk, t0);
-                tma_load_2d(xs + TN * 128, &xmap, &xfull[st], kk + 64, t0);
+                // K half h of the stage holds NB rows: the tile's hi rows
+                // (columns [0, K) of the activation rows), then its lo rows
+                // (columns [K, 2K)); rows past the last token read as zeros
+#pragma unroll
+                for (int h = 0; h < 2; h++)
+#pragma unroll
+                    for (int p = 0; p < 2; p++)
+                        tma_load_2d(xs + (h * C::NB + p * TN) * 128, &xmap, &xfull[st], p * K + kk + 64 * h, t0);
             }
         }
     } else if (warp == 1 || (C::ISS == 2 && warp == 3)) {
@@ -374,10 +411,11 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
         // the issuer first waits for that stage's MMAs (mdone), which follow
         // its aready.  The next phases need this issuer's MMA of stage j.
         if (lane == 0) {
-            constexpr uint32_t idesc = make_idesc(TN);
+            constexpr uint32_t idesc_hi = make_idesc(C::NB);  // hi weights x (hi, lo) tokens
+            constexpr uint32_t idesc_lo = make_idesc(TN);     // lo weights x hi tokens
             constexpr int KSTEPS = BK / 16;
             const int iss = warp == 1 ? 0 : 1;
-            const uint32_t d_tmem = tmem + (uint32_t)(iss * TN);
+            const uint32_t d_tmem = tmem + (uint32_t)(iss * C::NB);
             bool ok = true;
             for (int j = iss; j < nk;) {
                 if ((C::ISS == 2 && (S_TM & 1) && j >= S_TM &&
@@ -400,9 +438,10 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
                     const uint32_t xs = smem_u32(smem + C::x_off(st));
 #pragma unroll
                     for (int kk = 0; kk < KSTEPS; kk++) {
-                        uint32_t a_tmem = tmem + (uint32_t)(C::A_COL + a * 64 + kk * 8);
-                        uint32_t b_addr = xs + (uint32_t)((kk >> 2) * TN * 128 + (kk & 3) * 32);
-                        mma_f16_ts(d_tmem, a_tmem, sw128_desc(b_addr), idesc, (j > iss || kk > 0) ? 1u : 0u);
+                        const uint32_t a_tmem = tmem + (uint32_t)(C::A_COL + a * C::A_SLOT + kk * 8);
+                        const uint64_t bd = sw128_desc(xs + (uint32_t)((kk >> 2) * C::NB * 128 + (kk & 3) * 32));
+                        mma_f16_ts(d_tmem, a_tmem, bd, idesc_hi, (j > iss || kk > 0) ? 1u : 0u);
+                        mma_f16_ts(d_tmem, a_tmem + 64u, bd, idesc_lo, 1u);
                     }
                     mma_commit(&mdone[st]);  // frees the X stage and (S_TM | S_X) the A slot
                 }
@@ -440,65 +479,46 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
         const bool row_ok = n < N;
         bool ok = true;
         constexpr int BLK_PER = 4 / C::WG_PER;  // Q4_0 blocks of the stage per thread
-        constexpr int PER_ST = 2;               // blocks per TMEM store
-        constexpr int NH = BLK_PER / PER_ST;
-        static_assert(BLK_PER % PER_ST == 0, "whole TMEM stores per warpgroup");
         const int blk0 = part * BLK_PER;
         const int sw = (r >> 1) & 3;  // 16-byte chunk c of row r is stored at chunk c ^ sw
         for (int j = g; j < nk; j += C::RR) {
             const int st = j % S_W, a = j % S_TM;
             // A slot a was last read by the MMAs of stage j - S_TM, whose
             // completion is phase (j - S_TM) / S_X of mdone[(j - S_TM) % S_X].
-            // Decode tiles (PRELOAD) read and release the weight stage and
-            // convert its first blocks before they wait for the slot.
+            // The warps read and release the weight stage and convert its
+            // first block before they wait for the slot.
             const bool slot_wait = j >= S_TM;
-            if ((!C::PRELOAD && slot_wait &&
-                 !warp_wait(&mdone[(j - S_TM) % S_X], (uint32_t)((j - S_TM) / S_X) & 1u, &abort_flag)) ||
-                !warp_wait(&wfull[st], (uint32_t)(j / S_W) & 1u, &abort_flag)) {
+            if (!warp_wait(&wfull[st], (uint32_t)(j / S_W) & 1u, &abort_flag)) {
                 ok = false;
                 break;
             }
             // the stage's 4 scales of row r (the scale box holds the stage pair's 8)
             const uint2 sc = *reinterpret_cast<const uint2*>(smem + C::s_off(st) + r * 16 + ((it0 + j) & 1) * 8);
             const uint8_t* wrow = smem + C::w_off(st) + r * (BK / 2);  // 64-byte rows of nibbles
-            const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(C::A_COL + a * 64);
-            uint4 q4[C::PRELOAD ? BLK_PER : PER_ST];
-            if constexpr (C::PRELOAD) {
+            // hi weights of block b at columns [16 b, 16 b + 16) of the slot, lo weights 64 further
+            const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(C::A_COL + a * C::A_SLOT);
+            uint4 q4[BLK_PER];
 #pragma unroll
-                for (int bb = 0; bb < BLK_PER; bb++)
-                    q4[bb] = *reinterpret_cast<const uint4*>(wrow + (((blk0 + bb) ^ sw) << 4));
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&wempty[st]);  // the warp's last read of the weight stage
-            }
+            for (int bb = 0; bb < BLK_PER; bb++) q4[bb] = *reinterpret_cast<const uint4*>(wrow + (((blk0 + bb) ^ sw) << 4));
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&wempty[st]);  // the warp's last read of the weight stage
             bool okw = true;
 #pragma unroll
-            for (int hh = 0; hh < NH; hh++) {
-                uint32_t v[16 * PER_ST];
-                uint4 qv[PER_ST];
+            for (int bb = 0; bb < BLK_PER; bb++) {
+                const int blk = blk0 + bb;
+                const uint32_t s32 = (blk < 2) ? sc.x : sc.y;
+                __half2 shi2, slo2;
+                split_scale((blk & 1) ? (s32 >> 16) : (s32 & 0xFFFFu), shi2, slo2);
+                uint32_t vh[16], vl[16];
+                const uint32_t w4[4] = {q4[bb].x, q4[bb].y, q4[bb].z, q4[bb].w};
 #pragma unroll
-                for (int bb = 0; bb < PER_ST; bb++) {
-                    if constexpr (C::PRELOAD)
-                        qv[bb] = q4[hh * PER_ST + bb];
-                    else
-                        qv[bb] = *reinterpret_cast<const uint4*>(wrow + (((blk0 + hh * PER_ST + bb) ^ sw) << 4));
-                }
-                if (!C::PRELOAD && hh == NH - 1) {
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&wempty[st]);  // the warp's last read of the weight stage
-                }
-#pragma unroll
-                for (int bb = 0; bb < PER_ST; bb++) {
-                    const int blk = blk0 + hh * PER_ST + bb;
-                    uint32_t s32 = (blk < 2) ? sc.x : sc.y;
-                    uint32_t s16 = (blk & 1) ? (s32 >> 16) : (s32 & 0xFFFFu);
-                    __half2 s2 = __half2half2(__ushort_as_half((unsigned short)s16));
-                    const uint32_t w4[4] = {qv[bb].x, qv[bb].y, qv[bb].z, qv[bb].w};
-#pragma unroll
-                    for (int wd = 0; wd < 4; wd++) deq_word(w4[wd], s2, &v[bb * 16 + wd * 4]);
-                }
-                if (C::PRELOAD && hh == 0 && slot_wait)
+                for (int wd = 0; wd < 4; wd++) deq_word_split(w4[wd], shi2, slo2, &vh[wd * 4], &vl[wd * 4]);
+                if (bb == 0 && slot_wait)
                     okw = warp_wait(&mdone[(j - S_TM) % S_X], (uint32_t)((j - S_TM) / S_X) & 1u, &abort_flag);
-                if (okw) tmem_st_x32(tbase + (uint32_t)((blk0 + hh * PER_ST) * 16), v);
+                if (okw) {
+                    tmem_st_x16(tbase + (uint32_t)(blk * 16), vh);
+                    tmem_st_x16(tbase + (uint32_t)(64 + blk * 16), vl);
+                }
             }
             if (!okw) {
                 ok = false;
@@ -544,7 +564,7 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
                                                       xb[(orow + GU_BLOCK) * (EPI_CH + 1) + jj]);
                             const size_t t = (size_t)(t0 + c0 + jj);
                             y[t * ldy + col] = o;
-                            if (y16) y16[t * ncols + perm_k(col)] = __float2half_rn(o);
+                            if (y16) store_x16(y16 + t * 2 * ncols, (int)ncols, col, o);
                         }
                     }
                     asm volatile("bar.sync 1, 128;" ::: "memory");  // before the next chunk reuses xb
@@ -630,17 +650,24 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
     if (threadIdx.x == 0 && abort_flag) atomicExch(err, 1);
 }
 
-// fp32 rows -> fp16 rows in the K order of the weight tiles (see deq_word):
+// fp32 rows -> the GEMM's split fp16 rows (store_x16): per token 2K halves,
+// hi then lo, each in the K order of the weight tiles (see deq_word_split):
 // within every 8 elements, [e0 e4 e1 e5 e2 e6 e3 e7].
 __global__ void k_rows_to_f16_perm(const float* __restrict__ x, size_t ldx, __half* __restrict__ out, int K, int T) {
     pdl_trigger();
     int t = blockIdx.y;
     const float* xr = x + (size_t)t * ldx;
-    __half2* o = reinterpret_cast<__half2*>(out + (size_t)t * K);
+    __half2* oh = reinterpret_cast<__half2*>(out + (size_t)t * 2 * K);
+    __half2* ol = oh + K / 2;
     for (int gi = blockIdx.x * blockDim.x + threadIdx.x; gi < K / 8; gi += gridDim.x * blockDim.x) {
         const float* e = xr + 8 * gi;
 #pragma unroll
-        for (int k = 0; k < 4; k++) o[4 * gi + k] = __floats2half2_rn(e[k], e[k + 4]);
+        for (int k = 0; k < 4; k++) {
+            const float a = e[k], b = e[k + 4];
+            const __half2 h = __floats2half2_rn(a, b);
+            oh[4 * gi + k] = h;
+            ol[4 * gi + k] = __floats2half2_rn(__fsub_rn(a, __low2float(h)), __fsub_rn(b, __high2float(h)));
+        }
     }
 }
 
@@ -693,8 +720,8 @@ struct GemmWorkspace {
     int device = -1;
     // (nibble plane, scale plane, n, k) -> nibble and scale tensor maps
     std::map<std::tuple<const void*, const void*, size_t, size_t>, std::pair<CUtensorMap, CUtensorMap>> wmaps;
-    // [token tile 32/64/128/256][splits] -> CTAs resident at once (0: not yet queried)
-    int slots[4][MAX_SPLITS + 1] = {};
+    // [token tile 32/64/128][splits] -> CTAs resident at once (0: not yet queried)
+    int slots[3][MAX_SPLITS + 1] = {};
 };
 
 GemmWorkspace* gemm_workspace_new() { return new GemmWorkspace(); }
@@ -714,15 +741,13 @@ bool gemm_tc_eligible(const hc_q4_matrix& w, size_t tokens) {
 }
 
 namespace {
-// Dynamic shared memory of a launch.  A 512-column CTA asks for at least
-// 116 KB, so it is alone on its SM; the 256-column (decode) CTAs fit two per
-// SM and never three (their shared memory), so tensor-memory allocation never
-// waits.
+// Dynamic shared memory of a launch.  A CTA (512 tensor-memory columns) asks
+// for at least 116 KB, so it is alone on its SM and its tensor-memory
+// allocation never waits for another CTA of this kernel.
 template <int TN>
 int launch_smem() {
     using C = Cfg<TN>;
-    static_assert(C::smem() <= 232448, "shared memory budget");
-    return (!C::DUAL && C::smem() < 118784) ? 118784 : C::smem();
+    return C::smem() < 118784 ? 118784 : C::smem();
 }
 
 // CTAs of the kernel resident at once when the splits of a tile form a
@@ -799,33 +824,30 @@ int launch_tc(const hc_q4_matrix& w, const CUtensorMap& xmap, const CUtensorMap&
 }
 
 // K splits per tile (1..MAX_SPLITS) minimizing a time model in units of one
-// pipeline stage (measured on decode shapes): a CTA costs a fixed ~10 stages
-// (launch, pipeline fill, epilogue) plus its stages, which run ~1.67x slower
-// when two CTAs share an SM (`dual` kernels with more CTAs than SMs); a split
-// tile adds the cluster barriers and the reduction (~7 stages for two
-// splits, ~10 up to four, ~15 up to eight); slots[sp] = CTAs resident at once
-// with clusters of sp, so CTAs beyond it run in further waves.
+// pipeline stage: a CTA costs a fixed ~10 stages (launch, pipeline fill,
+// epilogue) plus its stages; a split tile adds the cluster barriers and the
+// reduction (~7 stages for two splits, ~10 up to four, ~15 up to eight);
+// slots[sp] = CTAs resident at once with clusters of sp (one per SM without
+// clusters), so CTAs beyond it run in further waves.
 // With max_part > 0 the splits are not reduced in a cluster but written as
 // slabs the caller adds (up to max_part of them): no cluster residency limit,
 // and each extra slab costs the consumer about half a stage of reading.
-int choose_splits(size_t tiles, size_t nk, const int* slots, int nsm, bool dual, int max_part = 0) {
-    const double fixed = 10.0, shared = 1.67;
+int choose_splits(size_t tiles, size_t nk, const int* slots, int nsm, int max_part = 0) {
+    const double fixed = 10.0;
     const int max_sp = max_part > 0 ? std::min(max_part, MAX_SPLITS) : MAX_SPLITS;
     int best = 1;
     double best_cost = 1e300;
     for (size_t sp = 1; sp <= (size_t)max_sp && (sp == 1 || nk / sp >= 2); sp++) {
-        // slabs: plain CTAs, two per SM for the dual (decode) kernels by design
-        const int sl_raw = max_part > 0 ? nsm * (dual ? 2 : 1) : slots[sp];
+        const int sl_raw = max_part > 0 ? nsm : slots[sp];
         const size_t sl = (size_t)(sl_raw > 0 ? sl_raw : 1);
         const size_t ctas = tiles * sp;
         const size_t waves = (ctas + sl - 1) / sl;
-        const double pace = (dual && ctas > (size_t)nsm) ? shared : 1.0;
         const double reduce = max_part > 0 ? 0.5 * (double)(sp - 1)
                               : sp == 1    ? 0.0
                               : sp == 2    ? 7.0
                               : sp <= 4    ? 10.0
                                            : 15.0;
-        const double cost = (double)waves * (fixed + pace * (double)((nk + sp - 1) / sp)) + reduce;
+        const double cost = (double)waves * (fixed + (double)((nk + sp - 1) / sp)) + reduce;
         if (cost < best_cost - 1e-9) {
             best_cost = cost;
             best = (int)sp;
@@ -864,12 +886,12 @@ int gemm_tc_impl(GemmWorkspace* ws, const hc_q4_matrix& w, const float* x, size_
         HC_CUDA(cudaMalloc((void**)&ws->err, sizeof(int)));
         HC_CUDA(cudaMemset(ws->err, 0, sizeof(int)));
     }
-    if (!xh_ready && T * K > ws->xh_cap) {
+    if (!xh_ready && 2 * T * K > ws->xh_cap) {  // hi and lo rows
         if (ws->xh) cudaFree(ws->xh);
         ws->xh = nullptr;
         ws->generation++;
-        HC_CUDA(cudaMalloc((void**)&ws->xh, T * K * sizeof(__half)));
-        ws->xh_cap = T * K;
+        HC_CUDA(cudaMalloc((void**)&ws->xh, 2 * T * K * sizeof(__half)));
+        ws->xh_cap = 2 * T * K;
     }
     const __half* xh = xh_ready;
     if (!xh) {
@@ -878,10 +900,10 @@ int gemm_tc_impl(GemmWorkspace* ws, const hc_q4_matrix& w, const float* x, size_
         HC_LAUNCH_CHECK();
         xh = ws->xh;
     }
-    // Token tile: the smallest of 32/64/128/256 covering T (one tile for decode).
-    int tn = T <= 32 ? 32 : T <= 64 ? 64 : T <= 128 ? 128 : 256;
-    CUtensorMap xmap;
-    HC_TRY(encode_2d(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, const_cast<__half*>(xh), K, T, K * 2, 64, (uint32_t)tn,
+    // Token tile: the smallest of 32/64/128 covering T (one tile for decode).
+    const int tn = T <= 32 ? 32 : T <= 64 ? 64 : 128;
+    CUtensorMap xmap;  // rows of 2K halves: hi, then lo
+    HC_TRY(encode_2d(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, const_cast<__half*>(xh), 2 * K, T, K * 4, 64, (uint32_t)tn,
                      CU_TENSOR_MAP_SWIZZLE_128B));
     auto key = std::make_tuple((const void*)w.qs, (const void*)w.sc, w.n, w.k);
     auto itw = ws->wmaps.find(key);
@@ -902,20 +924,16 @@ int gemm_tc_impl(GemmWorkspace* ws, const hc_q4_matrix& w, const float* x, size_
     int splits = 1;
     switch (tn) {
         case 32:
-            if (!one) splits = choose_splits(tiles, nk, tile_slots<32>(ws, 0), nsm, Cfg<32>::DUAL, max_part);
+            if (!one) splits = choose_splits(tiles, nk, tile_slots<32>(ws, 0), nsm, max_part);
             HC_TRY(launch_tc<32>(w, xmap, wmap, smap, T, y, ldy, epi, res, ldres, splits, ws->err, s, stride, y16));
             break;
         case 64:
-            if (!one) splits = choose_splits(tiles, nk, tile_slots<64>(ws, 1), nsm, Cfg<64>::DUAL, max_part);
+            if (!one) splits = choose_splits(tiles, nk, tile_slots<64>(ws, 1), nsm, max_part);
             HC_TRY(launch_tc<64>(w, xmap, wmap, smap, T, y, ldy, epi, res, ldres, splits, ws->err, s, stride, y16));
             break;
-        case 128:
-            if (!one) splits = choose_splits(tiles, nk, tile_slots<128>(ws, 2), nsm, Cfg<128>::DUAL, max_part);
-            HC_TRY(launch_tc<128>(w, xmap, wmap, smap, T, y, ldy, epi, res, ldres, splits, ws->err, s, stride, y16));
-            break;
         default:
-            if (!one) splits = choose_splits(tiles, nk, tile_slots<256>(ws, 3), nsm, Cfg<256>::DUAL, max_part);
-            HC_TRY(launch_tc<256>(w, xmap, wmap, smap, T, y, ldy, epi, res, ldres, splits, ws->err, s, stride, y16));
+            if (!one) splits = choose_splits(tiles, nk, tile_slots<128>(ws, 2), nsm, max_part);
+            HC_TRY(launch_tc<128>(w, xmap, wmap, smap, T, y, ldy, epi, res, ldres, splits, ws->err, s, stride, y16));
             break;
     }
     if (splits_out) *splits_out = splits;
@@ -983,13 +1001,14 @@ int gemm_check(GemmWorkspace* ws) {
 // process that hands all device memory to its own pool at start-up and must
 // not grow it, or a caller that may not call cudaMalloc (which can
 // synchronize the device) while other work is in flight.  For them the
-// tensor-core matmul below keeps its scratch (the fp16 copy of the
+// tensor-core matmul below keeps its scratch (the split fp16 copy of the
 // activations and the pipeline abort flag) in a fixed array that lives in the
 // library's device image, so a call allocates nothing.
 namespace {
 
 // Stated maximum: 8 MiB per device, held by every GPU that loads the library
-// until the process exits.  tokens * k * 2 bytes must fit after the flag.
+// until the process exits.  The split fp16 rows (2 * tokens * k halves, i.e.
+// tokens * k * 4 bytes) must fit after the flag.
 constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;
 constexpr size_t kNoAllocFlagBytes = 256;
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
@@ -1001,7 +1020,7 @@ std::mutex g_noalloc_mu;
 // Device address of the array for the current device.  In host code the
 // symbol is only a host-side stand-in, never a device address, so the address
 // is looked up with cudaGetSymbolAddress once per device (with that device
-// current) and cached.
+// current), its abort flag is cleared, and the address is cached.
 int noalloc_scratch(uint8_t** out) {
     int dev = 0;
     HC_CUDA(cudaGetDevice(&dev));
@@ -1011,9 +1030,27 @@ int noalloc_scratch(uint8_t** out) {
         void* p = nullptr;
         cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
         if (e != cudaSuccess) return hc_cuda_fail(e, "cudaGetSymbolAddress(g_noalloc_scratch)", __FILE__, __LINE__);
+        HC_CUDA(cudaMemset(p, 0, sizeof(int)));  // the abort flag starts clear
         g_noalloc_ptr[dev] = static_cast<uint8_t*>(p);
     }
     *out = g_noalloc_ptr[dev];
+    return HC_OK;
+}
+
+// Reads the abort flag after the launch (a 4-byte copy into a host stack
+// variable, then a wait for the stream): a bounded pipeline wait that ran out
+// makes the kernel skip its stores, so the call must not report success.
+int noalloc_status(int* err, cudaStream_t s) {
+    int h = 0;
+    HC_CUDA(cudaMemcpyAsync(&h, err, sizeof(int), cudaMemcpyDeviceToHost, s));
+    HC_CUDA(cudaStreamSynchronize(s));
+    if (h) {
+        HC_CUDA(cudaMemsetAsync(err, 0, sizeof(int), s));
+        HC_CUDA(cudaStreamSynchronize(s));
+        hc_set_error("hc_q4_matmul_noalloc: a bounded pipeline wait timed out (the kernel aborted and skipped its "
+                     "stores; y is not written)");
+        return HC_ERR_TIMEOUT;
+    }
     return HC_OK;
 }
 
@@ -1022,7 +1059,8 @@ int noalloc_scratch(uint8_t** out) {
 // Y[mtok x n] = X[mtok x k] . W^T like hc_q4_matmul_dev, without allocating
 // device or host memory: shapes the tensor cores take (mtok >= 2, k % 256 ==
 // 0, n >= 128) run the tcgen05 kernel with its scratch in the fixed array and
-// no split-K; other shapes run the CUDA-core matvec, which needs no scratch.
+// no split-K, then wait for the stream to read the kernel's abort flag; other
+// shapes run the CUDA-core matvec, which needs no scratch.
 HC_EXPORT int hc_q4_matmul_noalloc(const hc_q4_matrix* w, const float* x, size_t mtok, float* y, void* stream) {
     HC_CHECK(w && x && y, HC_ERR_INVALID, "hc_q4_matmul_noalloc: NULL argument");
     cudaStream_t s = (cudaStream_t)stream;
@@ -1036,31 +1074,29 @@ HC_EXPORT int hc_q4_matmul_noalloc(const hc_q4_matrix* w, const float* x, size_t
         return hc::launch_matmul(dw, x, w->k, mtok, y, w->n, hc::EPI_STORE, nullptr, 0, s);
     }
     const size_t K = w->k, T = mtok;
-    HC_CHECK(T <= (kNoAllocScratchBytes - kNoAllocFlagBytes) / (K * sizeof(__half)), HC_ERR_INVALID,
+    const size_t max_t = (kNoAllocScratchBytes - kNoAllocFlagBytes) / (2 * K * sizeof(__half));
+    HC_CHECK(T <= max_t, HC_ERR_INVALID,
              "hc_q4_matmul_noalloc: %zu tokens x %zu columns exceed the fixed %zu-byte scratch (at most %zu tokens "
              "at this width)",
-             T, K, kNoAllocScratchBytes, (kNoAllocScratchBytes - kNoAllocFlagBytes) / (K * sizeof(__half)));
+             T, K, kNoAllocScratchBytes, max_t);
     uint8_t* base = nullptr;
     HC_TRY(noalloc_scratch(&base));
     int* err = reinterpret_cast<int*>(base);
     __half* xh = reinterpret_cast<__half*>(base + kNoAllocFlagBytes);
-    // The array keeps the previous call's contents: the abort flag must start at zero.
-    HC_CUDA(cudaMemsetAsync(err, 0, sizeof(int), s));
     {
         unsigned gx = (unsigned)std::min<size_t>((K / 8 + 255) / 256, 16);
         hc::k_rows_to_f16_perm<<<dim3(gx, (unsigned)T), 256, 0, s>>>(x, K, xh, (int)K, (int)T);
         HC_LAUNCH_CHECK();
     }
-    int tn = T <= 32 ? 32 : T <= 64 ? 64 : T <= 128 ? 128 : 256;
+    const int tn = T <= 32 ? 32 : T <= 64 ? 64 : 128;
     CUtensorMap xmap, wmap, smap;
-    HC_TRY(hc::encode_2d(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xh, K, T, K * 2, 64, (uint32_t)tn,
+    HC_TRY(hc::encode_2d(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xh, 2 * K, T, K * 4, 64, (uint32_t)tn,
                          CU_TENSOR_MAP_SWIZZLE_128B));
     HC_TRY(hc::encode_weight_maps(*w, &wmap, &smap));
     switch (tn) {
-        case 32: return hc::launch_tc<32>(*w, xmap, wmap, smap, T, y, w->n, hc::EPI_STORE, nullptr, 0, 1, err, s);
-        case 64: return hc::launch_tc<64>(*w, xmap, wmap, smap, T, y, w->n, hc::EPI_STORE, nullptr, 0, 1, err, s);
-        case 128: return hc::launch_tc<128>(*w, xmap, wmap, smap, T, y, w->n, hc::EPI_STORE, nullptr, 0, 1, err, s);
-        default: return hc::launch_tc<256>(*w, xmap, wmap, smap, T, y, w->n, hc::EPI_STORE, nullptr, 0, 1, err, s);
+        case 32: HC_TRY(hc::launch_tc<32>(*w, xmap, wmap, smap, T, y, w->n, hc::EPI_STORE, nullptr, 0, 1, err, s)); break;
+        case 64: HC_TRY(hc::launch_tc<64>(*w, xmap, wmap, smap, T, y, w->n, hc::EPI_STORE, nullptr, 0, 1, err, s)); break;
+        default: HC_TRY(hc::launch_tc<128>(*w, xmap, wmap, smap, T, y, w->n, hc::EPI_STORE, nullptr, 0, 1, err, s)); break;
     }
+    return noalloc_status(err, s);
 }
-

@@ -496,7 +496,7 @@ __global__ void k_rmsnorm(const float* __restrict__ x, size_t ldx, const float* 
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
         float o = __fmul_rn(__fmul_rn(xr[i], inv), w[i]);
         orow[i] = o;
-        if (out16) out16[(size_t)blockIdx.x * n + perm_k(i)] = __float2half_rn(o);
+        if (out16) store_x16(out16 + (size_t)blockIdx.x * 2 * n, n, i, o);
     }
 }
 
@@ -536,11 +536,11 @@ __global__ void k_rmsnorm_v4(const float* __restrict__ x, size_t ldx, const floa
             o.w = __fmul_rn(__fmul_rn(v[j].w, inv), ww.w);
             orow[i] = o;
             if (out16) {
-                __half* r16 = out16 + (size_t)blockIdx.x * n;
-                r16[perm_k(4 * i)] = __float2half_rn(o.x);
-                r16[perm_k(4 * i + 1)] = __float2half_rn(o.y);
-                r16[perm_k(4 * i + 2)] = __float2half_rn(o.z);
-                r16[perm_k(4 * i + 3)] = __float2half_rn(o.w);
+                __half* r16 = out16 + (size_t)blockIdx.x * (2 * (size_t)n);
+                store_x16(r16, n, 4 * i, o.x);
+                store_x16(r16, n, 4 * i + 1, o.y);
+                store_x16(r16, n, 4 * i + 2, o.z);
+                store_x16(r16, n, 4 * i + 3, o.w);
             }
         }
     }
@@ -627,11 +627,11 @@ __global__ void k_residual_splits_norm(const float* __restrict__ part, int split
             o.w = __fmul_rn(__fmul_rn(v[j].w, inv), ww.w);
             orow[i] = o;
             if (xn16) {
-                __half* r16 = xn16 + row * (size_t)n;
-                r16[perm_k(4 * i)] = __float2half_rn(o.x);
-                r16[perm_k(4 * i + 1)] = __float2half_rn(o.y);
-                r16[perm_k(4 * i + 2)] = __float2half_rn(o.z);
-                r16[perm_k(4 * i + 3)] = __float2half_rn(o.w);
+                __half* r16 = xn16 + row * (size_t)(2 * n);
+                store_x16(r16, n, 4 * i, o.x);
+                store_x16(r16, n, 4 * i + 1, o.y);
+                store_x16(r16, n, 4 * i + 2, o.z);
+                store_x16(r16, n, 4 * i + 3, o.w);
             }
         }
     }
@@ -716,7 +716,7 @@ __global__ void k_silu_mul(const float* __restrict__ gu, size_t ldgu, float* __r
         const int ui = blocked ? gi + GU_BLOCK : im + i;
         float o = __fmul_rn(silu_f(g[gi]), g[ui]);
         a[i] = o;
-        if (act16) act16[(size_t)blockIdx.y * im + perm_k(i)] = __float2half_rn(o);
+        if (act16) store_x16(act16 + (size_t)blockIdx.y * 2 * im, im, i, o);
     }
 }
 

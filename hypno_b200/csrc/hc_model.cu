@@ -417,7 +417,8 @@ int ensure_scratch(hc_model* m, size_t tokens, size_t logit_rows) {
             for (int i = 0; i < 3; i++) {
                 if (*h16[i]) cudaFree(*h16[i]);
                 *h16[i] = nullptr;
-                HC_CUDA(cudaMalloc((void**)h16[i], std::max<size_t>(t * w16[i], 8) * sizeof(__half)));
+                // the GEMM's split rows: hi then lo halves of every row (store_x16)
+                HC_CUDA(cudaMalloc((void**)h16[i], std::max<size_t>(2 * t * w16[i], 8) * sizeof(__half)));
             }
         }
         if (s.tp_tmp) cudaFree(s.tp_tmp);

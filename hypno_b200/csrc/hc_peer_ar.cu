@@ -124,7 +124,7 @@ __global__ void __launch_bounds__(1024) k_ar_residual_norm(ArParams P) {
         if (ok) {
             const float4* wr = reinterpret_cast<const float4*>(P.w);
             float4* orow = reinterpret_cast<float4*>(P.xn + (size_t)row * P.ldxn);
-            __half* r16 = P.xn16 ? P.xn16 + (size_t)row * P.H : nullptr;
+            __half* r16 = P.xn16 ? P.xn16 + (size_t)row * 2 * P.H : nullptr;
 #pragma unroll
             for (int j = 0; j < VPT; j++) {
                 const int i = threadIdx.x + j * blockDim.x;
@@ -136,10 +136,10 @@ __global__ void __launch_bounds__(1024) k_ar_residual_norm(ArParams P) {
                     o.w = __fmul_rn(__fmul_rn(v[j].w, inv), ww.w);
                     orow[i] = o;
                     if (r16) {
-                        r16[perm_k(4 * i)] = __float2half_rn(o.x);
-                        r16[perm_k(4 * i + 1)] = __float2half_rn(o.y);
-                        r16[perm_k(4 * i + 2)] = __float2half_rn(o.z);
-                        r16[perm_k(4 * i + 3)] = __float2half_rn(o.w);
+                        store_x16(r16, P.H, 4 * i, o.x);
+                        store_x16(r16, P.H, 4 * i + 1, o.y);
+                        store_x16(r16, P.H, 4 * i + 2, o.z);
+                        store_x16(r16, P.H, 4 * i + 3, o.w);
                     }
                 }
             }

@@ -114,14 +114,19 @@ int hc_q4_matmul_dev(const hc_q4_matrix* w, const float* x, size_t mtok, float* 
  * which can synchronize the device, while other work is in flight).  This
  * entry point has no counterpart in the reference engine.  It allocates
  * nothing: tensor-core shapes (mtok >= 2, k % 256 == 0, n >= 128) keep their
- * scratch in a fixed 8 MiB array inside the library's device image (held by
- * every GPU that loads the library until the process exits) and require
- * mtok * k * 2 <= 8 MiB - 256 bytes, else HC_ERR_INVALID; other shapes use the
- * CUDA-core matvec, which needs no scratch.  The first call on a device looks
- * up the array's device address (cudaGetSymbolAddress) and should come before
- * any stream capture.  Every call shares the array: calls that overlap on the
- * GPU (different streams, or different host threads on one device) race, so
- * order them on one stream.  Stream-ordered, no synchronization. */
+ * scratch (the hi + lo fp16 rows of x, mtok * k * 4 bytes, and the kernel's
+ * abort flag) in a fixed 8 MiB array inside the library's device image (held
+ * by every GPU that loads the library until the process exits) and require
+ * mtok * k * 4 <= 8 MiB - 256 bytes, else HC_ERR_INVALID; other shapes use the
+ * CUDA-core matvec, which needs no scratch and does not synchronize.  On the
+ * tensor-core path the call waits for the stream to finish the product so
+ * that it can read the abort flag: HC_ERR_TIMEOUT when a bounded pipeline
+ * wait ran out (y is then not written).  The first call on a device looks up
+ * the array's device address (cudaGetSymbolAddress) and should come before
+ * any stream capture; the cached address belongs to the device's primary
+ * context, so it is stale after cudaDeviceReset.  Every call shares the
+ * array: calls that overlap on the GPU (different streams, or different host
+ * threads on one device) race, so order them on one stream. */
 int hc_q4_matmul_noalloc(const hc_q4_matrix* w, const float* x, size_t mtok, float* y, void* stream);
 
 /* ---- model level: the forward passes ---------------------------------- */

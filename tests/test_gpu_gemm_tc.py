@@ -1,9 +1,12 @@
 """The tcgen05 Q4_0 GEMM (hc_gemm_tc.cu) against the oracle's per-token
 matvec on ragged token counts, row counts that are not multiples of the
-128-row tile, and every token-tile size (32 / 64 / 128 / 256).
+128-row tile, every token-tile size (32 / 64 / 128) and several token tiles.
 
-fp16 operands with f32 accumulation: the bar is the north_star tolerance
-max|gpu - ref| / max(1, max|ref|) <= 1e-3; the observed error is printed."""
+The GEMM multiplies exact two-term fp16 weights by fp16 hi + lo activations
+with f32 accumulation, so its error is that of an f32 dot product in another
+summation order: the bar is 1e-4 of max(1, max|ref|), ten times tighter than
+the north_star tolerance (1e-3), which a single fp16 operand per product
+(~3e-4 per product) would not leave room for; the observed error is printed."""
 import ctypes
 
 import numpy as np
@@ -14,6 +17,7 @@ from hypno_b200._lib import call
 from oracle import oracle as orc
 
 pytestmark = pytest.mark.gpu
+TOL_TC = 1e-4
 
 
 def rel_err(a, ref):
@@ -43,7 +47,7 @@ def test_tc_gemm_vs_oracle(cuda_device, N, K, T):
         ref = orc.matmul_q4_0(wq, X[t * K:(t + 1) * K], N, K)
         worst = max(worst, rel_err(Y[t], ref))
     print(f"N={N} K={K} T={T}: rel err {worst:.2e}")
-    assert worst <= 1e-3
+    assert worst <= TOL_TC
 
 
 def test_tc_gemm_residual_epilogue(cuda_device):
@@ -56,4 +60,4 @@ def test_tc_gemm_residual_epilogue(cuda_device):
     Y = np.empty(T * N, np.float32)
     ops.batch_matmul(Y, wq, ops.DTYPE_Q4_0, X, N, K, T)
     ref = orc.batch_matmul_q4_0(wq, X, N, K).reshape(-1)
-    assert rel_err(Y, ref) <= 1e-3
+    assert rel_err(Y, ref) <= TOL_TC
