@@ -54,12 +54,31 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+// Non-blocking probe of the phase with the given parity (try_wait may
+// suspend the thread for a while when the phase is still open; test_wait
+// returns at once).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 // Bounded wait on the phase with the given parity.  Returns false when the
-// deadline passes or another role already reported a failure.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+// deadline passes or another role already reported a failure.  Waits that are
+// off the critical path pass sleep_ns > 0 and back off between probes, which
+// leaves the issue slots of their SMSP to the warps doing the work.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          unsigned sleep_ns = 0) {
     long long start = clock64();
     for (uint32_t i = 0;; i++) {
         if (mbar_try_wait(bar, parity)) return true;
+        if (sleep_ns) __nanosleep(sleep_ns);
         if ((i & 255) == 255) {
             if (*abort_flag) return false;
             if (clock64() - start > WAIT_CYCLES) {

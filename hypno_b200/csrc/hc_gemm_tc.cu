@@ -202,14 +202,16 @@ __device__ __forceinline__ void tmem_st_x16(uint32_t taddr, const uint32_t* v) {
         : "memory");
 }
 
-// Warp-uniform bounded wait: lane 0 polls, the verdict is broadcast, then
-// every lane observes the completed phase once itself (acquire ordering for
-// its own reads of the data the barrier guards).
+// Warp-uniform bounded wait: lane 0 polls (its try_wait acquires the data
+// the barrier guards), the verdict is broadcast, and __syncwarp orders the
+// other lanes' accesses after lane 0's.  Only one lane touches the barrier:
+// every mbarrier operation costs ~100+ cycles when many warps use them, and
+// a 32-lane re-test per wait multiplied that traffic by 32.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
     bool ok = true;
     if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort_flag);
     ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-    if (ok) (void)mbar_try_wait(bar, parity);
+    __syncwarp();
     return ok;
 }
 
@@ -244,15 +246,27 @@ struct Cfg {
     // fp16 block scales of the stage's 128 rows: the aligned 16-byte box of
     // 8 scales (this stage's 4 and its pair's) per row
     static constexpr int S_STAGE = BM * 16;
-    static constexpr int S_X = TN <= 32 ? 6 : (TN <= 64 ? 3 : 2);  // X ring stages
+    static constexpr int S_X = TN <= 32 ? 6 : (TN <= 64 ? 4 : 2);  // X ring stages
     static constexpr int S_W = TN <= 64 ? 6 : 4;                    // weight ring stages
-    // Decode CTAs issue their MMAs from two warps taking alternate stages,
-    // each into its own accumulator (summed by the epilogue).
+    // Issuing warps.  A warp's instructions after a batch of MMAs wait for
+    // those MMAs to drain through the tensor pipe, so decode tiles (TN = 32,
+    // short MMAs) use two issuing warps that take alternate stages, each into
+    // its own accumulator D_i (summed by the epilogue): one warp's barrier
+    // waits overlap the other's MMAs.  With one issuer and TN = 64 the
+    // lo-weight products go to their own accumulator D_lo (TN columns after
+    // D), so consecutive MMAs never wait on each other's accumulator; with
+    // 128-token tiles every MMA is long enough for one accumulator.
     static constexpr int ISS = TN <= 32 ? 2 : 1;
-    static constexpr int A_COL = ISS * NB;                   // D_i at [i NB, (i + 1) NB); A slots from here
+    static constexpr bool DUALD = ISS == 1 && TN <= 64;
+    static constexpr int D_COLS = NB + (DUALD ? TN : 0);       // per issuer
+    static constexpr int A_COL = ISS * D_COLS <= 128 ? 128 : 256;  // D_i at [i D_COLS, ...); A slots from here
     static constexpr int A_SLOT = 128;                       // hi weights (64 columns), then lo weights
     static constexpr int S_TM = (COLS - A_COL) / A_SLOT;     // A slots
     static constexpr int MMA_BATCH = S_TM < 4 ? S_TM : 4;    // stages issued under one wait + fence
+    // Two dequant groups take alternate stages (matching the two issuers'
+    // stage parity), so one group's waits overlap the other's conversion;
+    // each converts its whole share of a stage before it waits for the A slot,
+    // so only the tensor-memory stores sit inside the slot's reuse cycle.
     static constexpr int RR = 2;                             // dequant groups working on different stages
     static constexpr int WG_PER = (DEQ_WARPS / 4) / RR;      // warpgroups per group, each 4 / WG_PER blocks
     // the dequant warps wait for the weight stage before the A slot (the
@@ -269,14 +283,13 @@ struct Cfg {
     static_assert(S_TM >= 2 && A_COL + A_SLOT * S_TM <= COLS, "tensor memory budget");
     static_assert(ISS == 1 || ISS == 2, "one or two issuing warps");
     static_assert(MMA_BATCH >= 1 && MMA_BATCH <= S_TM, "batched stages each need their own A slot");
-    // two issuers: issuer i takes the stages j % 2 == i, fed by dequant group
-    // i (RR == 2); the phase arguments below need the ring sizes to respect
-    // the stage parity
-    static_assert(ISS == 1 || (RR == 2 && S_X % 2 == 0 && S_W % S_TM == 0), "alternating issuers");
+    // two issuers: issuer i takes the stages j % 2 == i; the phase arguments
+    // of the issuer need the X ring to respect the stage parity
+    static_assert(ISS == 1 || (S_X % 2 == 0 && S_W % S_TM == 0), "alternating issuers");
     static_assert(S_X % S_TM == 0, "an A slot is freed by the MMA commit that frees an X stage");
     static_assert(RR <= S_TM && RR <= S_W, "dequant groups must not run more than one barrier phase apart");
     static_assert(S_W >= S_TM && RR <= S_X && (ISS == 1 || S_W % S_TM == 0), "barrier phase ordering (see the dequant warps)");
-    static_assert(WG_PER == 1 || WG_PER == 2, "dequant split: 4 or 2 blocks per warpgroup");
+    static_assert(WG_PER == 1 || WG_PER == 2 || WG_PER == 4, "dequant split: 4, 2 or 1 blocks per warpgroup");
     static_assert(!PRELOAD || S_W % RR == 0, "weight-first waits (see the dequant warps)");
     static_assert(smem() <= 232448, "shared memory budget");
     static_assert((TN * 128) % 1024 == 0, "each X box starts on a 1024-byte swizzle atom");
@@ -285,26 +298,39 @@ struct Cfg {
 };
 
 // Tokens [c0, c0 + EPI_CH) of TMEM lane quarter q of the accumulator: the
-// sum of its hi-token and lo-token column halves (and of D_1 when a second
-// issuer wrote it).  Warp-collective.
+// sum of its hi-token and lo-token column halves, of D_lo (the lo-weight
+// products) when it has its own columns, and of D_1 when a second issuer
+// wrote it.  Warp-collective.
 template <typename C>
 __device__ __forceinline__ void load_accumulators(uint32_t tmem, int q, int c0, int nk, uint32_t* v) {
     const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0;
-    uint32_t a[EPI_CH];
+    uint32_t a[EPI_CH], b[EPI_CH];
     tmem_ld_x16(base, v);
     tmem_ld_x16(base + (uint32_t)C::TN_, a);
+    if (C::DUALD) tmem_ld_x16(base + (uint32_t)C::NB, b);
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-    for (int jj = 0; jj < EPI_CH; jj++) v[jj] = __float_as_uint(__uint_as_float(v[jj]) + __uint_as_float(a[jj]));
+    for (int jj = 0; jj < EPI_CH; jj++) {
+        float o = __uint_as_float(v[jj]) + __uint_as_float(a[jj]);
+        if (C::DUALD) o = o + __uint_as_float(b[jj]);
+        v[jj] = __float_as_uint(o);
+    }
     if (C::ISS == 2 && nk > 1) {  // issuer 1 wrote D_1
-        uint32_t b[EPI_CH];
-        tmem_ld_x16(base + (uint32_t)C::NB, a);
-        tmem_ld_x16(base + (uint32_t)(C::NB + C::TN_), b);
+        tmem_ld_x16(base + (uint32_t)C::D_COLS, a);
+        tmem_ld_x16(base + (uint32_t)(C::D_COLS + C::TN_), b);
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
         for (int jj = 0; jj < EPI_CH; jj++)
             v[jj] = __float_as_uint(__uint_as_float(v[jj]) + (__uint_as_float(a[jj]) + __uint_as_float(b[jj])));
     }
+}
+
+// One lane of a converged warp (the MMA issue happens under it, so the
+// warp's loop, waits and descriptor arithmetic stay uniform).
+__device__ __forceinline__ bool elect_one() {
+    uint32_t pred = 0;
+    asm volatile("{\n\t.reg .pred px;\n\telect.sync _|px, 0xffffffff;\n\t@px mov.u32 %0, 1;\n\t}" : "+r"(pred));
+    return pred != 0;
 }
 
 template <int TN>
@@ -370,7 +396,7 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
         if (lane == 0) {
             for (int j = 0; j < nk; j++) {
                 const int st = j % S_W;
-                if (j >= S_W && !mbar_wait(&wempty[st], ((uint32_t)(j / S_W) & 1u) ^ 1u, &abort_flag)) break;
+                if (j >= S_W && !mbar_wait(&wempty[st], ((uint32_t)(j / S_W) & 1u) ^ 1u, &abort_flag, 64)) break;
                 mbar_expect_tx(&wfull[st], (uint32_t)(C::W_STAGE + C::S_STAGE));
                 tma_load_2d(smem + C::w_off(st), &wmap, &wfull[st], (it0 + j) * BK / 2, n0);
                 tma_load_2d(smem + C::s_off(st), &smap, &wfull[st], 8 * ((it0 + j) >> 1), n0);
@@ -382,7 +408,7 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
             grid_dependency_wait();
             for (int j = 0; j < nk; j++) {
                 const int st = j % S_X;
-                if (j >= S_X && !mbar_wait(&mdone[st], ((uint32_t)(j / S_X) & 1u) ^ 1u, &abort_flag)) break;
+                if (j >= S_X && !mbar_wait(&mdone[st], ((uint32_t)(j / S_X) & 1u) ^ 1u, &abort_flag, 64)) break;
                 mbar_expect_tx(&xfull[st], (uint32_t)C::X_STAGE);
                 uint8_t* xs = smem + C::x_off(st);
                 const int kk = (it0 + j) * BK;
@@ -397,57 +423,66 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
             }
         }
     } else if (warp == 1 || (C::ISS == 2 && warp == 3)) {
-        // ---------------- MMA issuer(s): issuer i takes the stages
-        // j = i, i + ISS, ... (all eight K steps) into accumulator D_i
-        // (columns [i TN, (i + 1) TN)).
-        // The tcgen05 fence that must follow each barrier wait stalls the
-        // issuing thread; a single issuer therefore takes every stage that is
-        // already dequantized (and whose X has landed) when the oldest one is,
-        // up to MMA_BATCH, under a single wait + fence.
+        // ---------------- MMA issuer(s): the whole warp runs the loop and its
+        // waits; one elected lane issues each batch of MMAs (a converged issue
+        // keeps the operands in uniform registers: ~40 cycles per MMA instead
+        // of ~110 from a lone lane).  Issuer i takes the stages j = i, i + ISS,
+        // ... into its accumulator D_i.  A single issuer takes every stage that
+        // is already dequantized (and whose X has landed) when the oldest one
+        // is, up to MMA_BATCH, under one wait + fence.  Per 16-wide K step:
+        // hi weights x [x_hi; x_lo] into D_i, lo weights x x_hi into D_lo (or
+        // into D_i's hi-token half).
         // Phases: an issuer's aready / xfull wait for stage j must find the
         // barrier's previous phase (stage j - S_TM, resp. j - S_X) complete.
         // With one issuer that stage was its own.  With two, stage j - S_X
         // (S_X even) is its own; stage j - S_TM may be the other issuer's, so
         // the issuer first waits for that stage's MMAs (mdone), which follow
         // its aready.  The next phases need this issuer's MMA of stage j.
-        if (lane == 0) {
-            constexpr uint32_t idesc_hi = make_idesc(C::NB);  // hi weights x (hi, lo) tokens
-            constexpr uint32_t idesc_lo = make_idesc(TN);     // lo weights x hi tokens
-            constexpr int KSTEPS = BK / 16;
-            const int iss = warp == 1 ? 0 : 1;
-            const uint32_t d_tmem = tmem + (uint32_t)(iss * C::NB);
-            bool ok = true;
-            for (int j = iss; j < nk;) {
-                if ((C::ISS == 2 && (S_TM & 1) && j >= S_TM &&
-                     !mbar_wait(&mdone[(j - S_TM) % S_X], (uint32_t)((j - S_TM) / S_X) & 1u, &abort_flag)) ||
-                    !mbar_wait(&xfull[j % S_X], (uint32_t)(j / S_X) & 1u, &abort_flag) ||
-                    !mbar_wait(&aready[j % S_TM], (uint32_t)(j / S_TM) & 1u, &abort_flag)) {
-                    ok = false;
-                    break;
-                }
-                int cnt = 1;
-                if constexpr (C::ISS == 1) {
-                    while (cnt < C::MMA_BATCH && j + cnt < nk &&
-                           mbar_try_wait(&aready[(j + cnt) % S_TM], (uint32_t)((j + cnt) / S_TM) & 1u) &&
-                           mbar_try_wait(&xfull[(j + cnt) % S_X], (uint32_t)((j + cnt) / S_X) & 1u))
-                        cnt++;
-                }
-                tmem_fence_after();
-                for (int b = 0; b < cnt; b++, j += C::ISS) {
-                    const int st = j % S_X, a = j % S_TM;
+        constexpr uint32_t idesc_hi = make_idesc(C::NB);  // hi weights x (hi, lo) tokens
+        constexpr uint32_t idesc_lo = make_idesc(TN);     // lo weights x hi tokens
+        constexpr int KSTEPS = BK / 16;
+        const int iss = warp == 1 ? 0 : 1;
+        const uint32_t d_hi = tmem + (uint32_t)(iss * C::D_COLS);
+        const uint32_t d_lo = d_hi + (uint32_t)(C::DUALD ? C::NB : 0);
+        bool ok = true;
+        for (int j = iss; j < nk;) {
+            if ((C::ISS == 2 && (S_TM & 1) && j >= S_TM &&
+                 !warp_wait(&mdone[(j - S_TM) % S_X], (uint32_t)((j - S_TM) / S_X) & 1u, &abort_flag)) ||
+                !warp_wait(&xfull[j % S_X], (uint32_t)(j / S_X) & 1u, &abort_flag) ||
+                !warp_wait(&aready[j % S_TM], (uint32_t)(j / S_TM) & 1u, &abort_flag)) {
+                ok = false;
+                break;
+            }
+            int cnt = 1;
+            if (C::ISS == 1 && lane == 0) {
+                while (cnt < C::MMA_BATCH && j + cnt < nk &&
+                       mbar_test_wait(&aready[(j + cnt) % S_TM], (uint32_t)((j + cnt) / S_TM) & 1u) &&
+                       mbar_test_wait(&xfull[(j + cnt) % S_X], (uint32_t)((j + cnt) / S_X) & 1u))
+                    cnt++;
+            }
+            cnt = __shfl_sync(0xffffffffu, cnt, 0);
+            __syncwarp();
+            tmem_fence_after();
+            if (elect_one()) {
+                for (int b = 0; b < cnt; b++) {
+                    const int jj = j + b * C::ISS, st = jj % S_X, a = jj % S_TM;
                     const uint32_t xs = smem_u32(smem + C::x_off(st));
 #pragma unroll
                     for (int kk = 0; kk < KSTEPS; kk++) {
                         const uint32_t a_tmem = tmem + (uint32_t)(C::A_COL + a * C::A_SLOT + kk * 8);
                         const uint64_t bd = sw128_desc(xs + (uint32_t)((kk >> 2) * C::NB * 128 + (kk & 3) * 32));
-                        mma_f16_ts(d_tmem, a_tmem, bd, idesc_hi, (j > iss || kk > 0) ? 1u : 0u);
-                        mma_f16_ts(d_tmem, a_tmem + 64u, bd, idesc_lo, 1u);
+                        const uint32_t first = (jj > iss || kk > 0) ? 1u : 0u;
+                        mma_f16_ts(d_hi, a_tmem, bd, idesc_hi, first);
+                        mma_f16_ts(d_lo, a_tmem + 64u, bd, idesc_lo, C::DUALD ? first : 1u);
                     }
                     mma_commit(&mdone[st]);  // frees the X stage and (S_TM | S_X) the A slot
                 }
             }
-            if (ok) mma_commit(dfull);  // also when this issuer had no stage
+            __syncwarp();
+            j += cnt * C::ISS;
         }
+        if (ok && elect_one()) mma_commit(dfull);  // also when this issuer had no stage
+        __syncwarp();
     } else if (warp >= 4) {
         // ---------------- dequant: thread <-> weight row (TMEM lane).  The
         // dequant warpgroups form RR groups; group g converts the stages j
@@ -471,7 +506,6 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
         //    done, so the load of j - S_W landed.  Its next phase needs this
         //    group's release of stage j.
         const int wg = (warp - 4) >> 2;
-        const int g = wg / C::WG_PER;
         const int part = wg % C::WG_PER;
         const int q = warp & 3;          // TMEM lane quarter of this warp
         const int r = q * 32 + lane;
@@ -481,12 +515,13 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
         constexpr int BLK_PER = 4 / C::WG_PER;  // Q4_0 blocks of the stage per thread
         const int blk0 = part * BLK_PER;
         const int sw = (r >> 1) & 3;  // 16-byte chunk c of row r is stored at chunk c ^ sw
+        const int g = wg / C::WG_PER;  // dequant group: stages j with j % RR == g
         for (int j = g; j < nk; j += C::RR) {
             const int st = j % S_W, a = j % S_TM;
             // A slot a was last read by the MMAs of stage j - S_TM, whose
             // completion is phase (j - S_TM) / S_X of mdone[(j - S_TM) % S_X].
-            // The warps read and release the weight stage and convert its
-            // first block before they wait for the slot.
+            // The warps read and release the weight stage and convert their
+            // blocks before they wait for the slot.
             const bool slot_wait = j >= S_TM;
             if (!warp_wait(&wfull[st], (uint32_t)(j / S_W) & 1u, &abort_flag)) {
                 ok = false;
@@ -502,27 +537,28 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
             for (int bb = 0; bb < BLK_PER; bb++) q4[bb] = *reinterpret_cast<const uint4*>(wrow + (((blk0 + bb) ^ sw) << 4));
             __syncwarp();
             if (lane == 0) mbar_arrive(&wempty[st]);  // the warp's last read of the weight stage
-            bool okw = true;
+            uint32_t vh[BLK_PER][16], vl[BLK_PER][16];
 #pragma unroll
             for (int bb = 0; bb < BLK_PER; bb++) {
                 const int blk = blk0 + bb;
                 const uint32_t s32 = (blk < 2) ? sc.x : sc.y;
                 __half2 shi2, slo2;
                 split_scale((blk & 1) ? (s32 >> 16) : (s32 & 0xFFFFu), shi2, slo2);
-                uint32_t vh[16], vl[16];
                 const uint32_t w4[4] = {q4[bb].x, q4[bb].y, q4[bb].z, q4[bb].w};
 #pragma unroll
-                for (int wd = 0; wd < 4; wd++) deq_word_split(w4[wd], shi2, slo2, &vh[wd * 4], &vl[wd * 4]);
-                if (bb == 0 && slot_wait)
-                    okw = warp_wait(&mdone[(j - S_TM) % S_X], (uint32_t)((j - S_TM) / S_X) & 1u, &abort_flag);
-                if (okw) {
-                    tmem_st_x16(tbase + (uint32_t)(blk * 16), vh);
-                    tmem_st_x16(tbase + (uint32_t)(64 + blk * 16), vl);
-                }
+                for (int wd = 0; wd < 4; wd++) deq_word_split(w4[wd], shi2, slo2, &vh[bb][wd * 4], &vl[bb][wd * 4]);
             }
-            if (!okw) {
-                ok = false;
-                break;
+            if (slot_wait) {
+                if (!warp_wait(&mdone[(j - S_TM) % S_X], (uint32_t)((j - S_TM) / S_X) & 1u, &abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                tmem_fence_after();
+            }
+#pragma unroll
+            for (int bb = 0; bb < BLK_PER; bb++) {
+                tmem_st_x16(tbase + (uint32_t)((blk0 + bb) * 16), vh[bb]);
+                tmem_st_x16(tbase + (uint32_t)(64 + (blk0 + bb) * 16), vl[bb]);
             }
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             tmem_fence_before();
