@@ -28,7 +28,6 @@ all-reduce after o_proj / down_proj, vocabulary-sharded LM head): the same
 import argparse
 import ctypes
 import json
-import re
 import os
 import subprocess
 import sys
@@ -41,6 +40,10 @@ sys.path.insert(0, ROOT)
 
 METRIC = "Q4_0 decode tok/s (Llama-3-8B shape, 32 sequences x 2048 context)"
 UNIT = "tok/s"
+# What the path computes in: Q4_0 weights; the tensor-core GEMMs multiply each
+# weight as two exact fp16 terms by each activation as fp16 hi + lo with f32
+# accumulation (an f32 dot product to ~1e-6); everything else is f32 (fp16 KV).
+DTYPE = "q4_0 weights; fp16 hi+lo tensor-core operands (f32-exact products), f32 accumulate; fp16 KV"
 FALLBACK_HBM_GBS = 6650.0
 
 
@@ -255,17 +258,10 @@ def roofline_gemv(dev, M=32, N=28672, K=4096, copies=4, reps=20):
     algo = 0.5625 * N * K + 4.0 * M * K + 4.0 * M * N
     peak, src = measured_peaks()
     achieved = algo / (ms * 1e-3) / 1e9
-    # DRAM bytes per launch of this kernel from the committed ncu summary
-    traffic = None
-    tp = os.path.join(ROOT, "profiles", "gemm_tc_gateup_c4_decode.md")
-    if os.path.exists(tp):
-        with open(tp) as f:
-            for line in f:
-                mt = re.match(r"\|\s*dram_bytes_per_launch\s*\|\s*(\d+)", line)
-                if mt:
-                    traffic = int(mt.group(1))
+    # DRAM bytes per launch need an ncu capture of this very run, which a
+    # timed run does not take: the captured figure lives in profiles/
     return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-            "frac": round(achieved / peak, 4), "traffic": traffic,
+            "frac": round(achieved / peak, 4), "traffic": None,
             "kernel": f"q4_0 matmul N={N} K={K} M={M}", "algorithmic_bytes": int(algo),
             "avg_launch_us": round(ms * 1e3, 2), "peak_source": f"{src} (hbm_gbs)"}
 
@@ -331,6 +327,7 @@ def q4_sweep(dev, reps=10):
 def cpu_baseline(img, cfg, budget_s=12.0, max_tokens=24):
     """The oracle decoding one sequence at context 2048 on the host cores."""
     from oracle import oracle as orc
+    orc.use_all_cores()  # torchrun sets OMP_NUM_THREADS=1 for every rank
     om = orc.OracleModel(img)
     kv = om.new_kv(cfg["max_pos"])
     kv.set_pos(cfg["prompt"])
@@ -507,7 +504,7 @@ def run_ours(args):
     if rank == 0:
         line = {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
-                "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": "q4_0 weights, f32 compute", "data": "synthetic",
+                "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": DTYPE, "data": "synthetic",
                 "config": dict(workload_config(world, "tp" if tp else "dp"), layers=cfg["layers"]), "e2e": e2e, "gpu_launches": int(launches),
                 "prefill_tok_s": round(prefill_tok_s, 1), "clocks": clk.summary(), "roofline": roof,
                 "cpu_baseline": cpu, "q4_sweep": sweep}
@@ -526,8 +523,14 @@ def run_reference(args):
         return
     from hypno_b200 import synth
     from oracle import oracle as orc
-    cfg = synth.CONFIGS["c4"]
-    img = synth.build_image(cfg, seed=0, quantize=orc.quantize_f32_to_q4_0)
+    cores = orc.use_all_cores()  # torchrun sets OMP_NUM_THREADS=1 for every rank
+    cfg = dict(synth.CONFIGS["c4"])
+    if args.layers:
+        cfg["layers"] = args.layers
+    # built on the CPU with the oracle's generator and quantizer: this arm never
+    # loads the GPU library
+    img = synth.build_image(cfg, seed=0, quantize=orc.quantize_f32_to_q4_0,
+                            normal=lambda sd, st, n, std: orc.synth_normal(sd, st, n, std))
     om = orc.OracleModel(img)
     kv = om.new_kv(cfg["max_pos"])
     kv.set_pos(cfg["prompt"])
@@ -539,13 +542,14 @@ def run_reference(args):
         orc.model_forward(om, 1 + i, kv)
     dt = time.perf_counter() - t0
     v = args.steps / dt
-    cpu = {"value": round(v, 3), "unit": UNIT, "cores": orc.lib().orc_num_threads(), "kind": "port",
+    cpu = {"value": round(v, 3), "unit": UNIT, "cores": cores, "kind": "port",
            "sample": f"each step = one model_forward of one sequence at context {cfg['prompt']} (the reference "
                      f"decodes sequences one at a time, serve.rs:175,193); {args.steps} steps in {dt:.1f} s"}
     line = {"impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 2),
             "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
-            "dtype": "q4_0 weights, f32 compute", "data": "synthetic", "config": workload_config(world),
+            "dtype": "q4_0 weights, f32 compute (CPU restatement of hypno)", "data": "synthetic",
+            "config": dict(workload_config(world), layers=cfg["layers"]),
             "cpu_baseline": cpu,
             "e2e": {"value": round(v, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)

@@ -102,23 +102,32 @@ def _stored_dtype(cfg, kind, n):
     return hf.effective_dtype(hf.DT_Q4_0, n)
 
 
-def build_image(cfg, seed=0, std=0.02, values=None, quantize=None, device=None):
+def build_image(cfg, seed=0, std=0.02, values=None, quantize=None, device=None, normal=None):
     """Returns the .hypno image (numpy uint8) of a synthetic model.
 
     values(name, n) -> float32 array overrides the seeded normal stream.
     quantize(f32 array) -> Q4_0 bytes overrides the backend quantizer (the
     parity-fixture script passes the oracle's, which is bit-identical).
+    normal(seed, stream, n, std) -> float32 array overrides the host
+    generator of the seeded stream (the CPU reference arm passes the
+    oracle's copy, so it never loads the GPU library).
     device: a torch CUDA device to generate and quantize on (fast path for
     the multi-GB benchmark models); None generates on the host.
     """
     if device is not None and values is None and quantize is None:
         return _build_image_device(cfg, seed, std, device)
-    from .ops import quantize_f32_to_q4_0
-    quantize = quantize or quantize_f32_to_q4_0
+    if quantize is None:
+        from .ops import quantize_f32_to_q4_0
+        quantize = quantize_f32_to_q4_0
     tensors = []
     for name, shape, kind in tensor_specs(cfg):
         n = int(np.prod(shape))
-        data = values(name, n) if values is not None else normal_host(seed, name, n, std)
+        if values is not None:
+            data = values(name, n)
+        elif normal is not None:
+            data = normal(seed, fnv1a64(name), n, std)
+        else:
+            data = normal_host(seed, name, n, std)
         dt = _stored_dtype(cfg, kind, n)
         if dt == hf.DT_Q4_0:
             payload = np.frombuffer(quantize(data), dtype=np.uint8)

@@ -933,3 +933,36 @@ ORC_API void orc_set_num_threads(int n) {
     (void)n;
 #endif
 }
+
+/* ------------------------------------------------------------------ */
+/* Seeded synthetic inputs (test harness, not a reference algorithm)   */
+/* ------------------------------------------------------------------ */
+
+/* The benchmark's synthetic weights and activations: element offset+i of the
+ * seeded stream (key from seed and stream id) is a 12-term Irwin-Hall sum of
+ * 16-bit uniforms taken from three SplitMix64 hashes, centred and scaled by
+ * std/65536 with one IEEE multiply, so the CPU reference arm builds the same
+ * model bytes as the GPU side without loading the GPU library. */
+static inline uint64_t orc_splitmix64(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+ORC_API void orc_synth_normal(uint64_t seed, uint64_t stream, uint64_t offset, uint64_t n, float std, float* out) {
+    const uint64_t key = orc_splitmix64(seed * 0x100000001B3ull ^ orc_splitmix64(stream + 0x51ED270B2ull));
+    const float scale = std / 65536.0f;
+    #pragma omp parallel for schedule(static)
+    for (long long i = 0; i < (long long)n; i++) {
+        const uint64_t idx = offset + (uint64_t)i;
+        uint32_t s = 0;
+        for (int j = 0; j < 3; j++) {
+            const uint64_t h = orc_splitmix64(key + 3ull * idx + (uint64_t)j);
+            s += (uint32_t)(h & 0xFFFF) + (uint32_t)((h >> 16) & 0xFFFF) + (uint32_t)((h >> 32) & 0xFFFF) +
+                 (uint32_t)(h >> 48);
+        }
+        const int32_t z = (int32_t)s - 393210;
+        out[i] = (float)z * scale;
+    }
+}

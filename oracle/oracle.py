@@ -66,6 +66,7 @@ def lib():
             "orc_batch_forward": (ctypes.c_int, [P, P, P, SZ, P]),
             "orc_num_threads": (ctypes.c_int, []),
             "orc_set_num_threads": (None, [ctypes.c_int]),
+            "orc_synth_normal": (None, [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, F, P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -77,6 +78,27 @@ def lib():
 
 def _f32(a):
     return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def synth_normal(seed, stream, n, std, offset=0):
+    """The benchmark's seeded synthetic stream on the CPU (the same floats as
+    hc_synth_normal_host); test-harness input generation, not a reference
+    algorithm."""
+    out = np.empty(n, dtype=np.float32)
+    if n:
+        lib().orc_synth_normal(seed, stream, offset, n, float(std), out.ctypes.data)
+    return out
+
+
+def use_all_cores():
+    """Sets the oracle's OpenMP thread count to the cores this process may run
+    on (torchrun exports OMP_NUM_THREADS=1 to every rank); returns it."""
+    try:
+        n = len(os.sched_getaffinity(0))
+    except AttributeError:
+        n = os.cpu_count() or 1
+    lib().orc_set_num_threads(n)
+    return n
 
 
 def f32_to_f16(x):

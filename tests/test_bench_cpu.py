@@ -54,3 +54,32 @@ def test_timing_contract_arguments(argv):
     r = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py")] + argv, capture_output=True, text=True,
                        timeout=120)
     assert r.returncode != 0 and ("warmup" in r.stderr or "steps" in r.stderr)
+
+
+def test_reference_arm_inputs_without_gpu_library():
+    """The reference arm builds its model from the oracle's copy of the seeded
+    generator and quantizer: the same image bytes as the GPU library's host
+    generator, without loading that library in the arm's process."""
+    import numpy as np
+    from hypno_b200 import synth
+    from oracle import oracle as orc
+    cfg = dict(hidden=256, inter=512, heads=4, kv_heads=2, layers=2, vocab=512, theta=10000.0, max_pos=64,
+               embed="q4", lm_head="tied")
+    a = synth.build_image(cfg, seed=3, quantize=orc.quantize_f32_to_q4_0,
+                          normal=lambda sd, st, n, std: orc.synth_normal(sd, st, n, std))
+    b = synth.build_image(cfg, seed=3, quantize=orc.quantize_f32_to_q4_0)
+    assert np.array_equal(a, b)
+    x = orc.synth_normal(5, synth.fnv1a64("w"), 4096, 0.02, offset=77)
+    assert np.array_equal(x, synth.normal_host(5, "w", 4096, 0.02, offset=77))
+    code = ("import sys, types; sys.argv = ['bench.py']; sys.path.insert(0, %r); import bench; "
+            "bench.run_reference(types.SimpleNamespace(warmup=3, steps=1, layers=1)); "
+            "print('GPULIB', 'libhypno_cuda' in open('/proc/self/maps').read())" % ROOT)
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=600,
+                       env=dict(os.environ, OMP_NUM_THREADS="1"))
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = r.stdout.strip().splitlines()
+    import json
+    line = json.loads(lines[-2])
+    assert lines[-1] == "GPULIB False"
+    assert line["impl"] == "reference" and line["config"]["layers"] == 1
+    assert line["cpu_baseline"]["cores"] == (len(os.sched_getaffinity(0)))  # not torchrun's OMP_NUM_THREADS=1
