@@ -472,6 +472,25 @@ def run_ours(args):
     e2e = {"value": round(jobs * S * args.steps / e2e_s, 2), "unit": UNIT,
            "h2d_bytes_per_step": 2 * 4 * S, "d2h_bytes_per_step": 4 * S}
 
+    # ---- per-phase device time of a decode step (eager launches with an event
+    # between phases, averaged over 3 steps; max over ranks per phase)
+    phases = None
+    if not args.no_phases:
+        names = [lib.hc_phase_name(i).decode() for i in range(lib.hc_phase_count())]
+        acc = (ctypes.c_float * len(names))()
+        reset_pos()
+        nrep = 3
+        for _ in range(nrep):
+            call("hc_decode_step_phases", model.handle, kv.handle, seqs_dev.data_ptr(), ids_dev.data_ptr(), S,
+                 ids_dev.data_ptr(), acc)
+        vals = torch.tensor([acc[i] / nrep for i in range(len(names))], device=dev)
+        if dist:
+            dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+        phases = {"ms_per_step": {n: round(float(v), 4) for n, v in zip(names, vals.tolist())},
+                  "sum_ms": round(float(vals.sum()), 4),
+                  "how": "one eager decode step (no CUDA graph) with a CUDA event between phases, mean of 3 steps, "
+                         "max over ranks per phase"}
+
     # ---- optional: the same 32 requests through the continuous-batching
     # scheduler (prefill of each prompt + `steps` greedy tokens each), wall-clocked
     serve = None
@@ -510,6 +529,8 @@ def run_ours(args):
                 "cpu_baseline": cpu, "q4_sweep": sweep}
         if serve is not None:
             line["serve"] = serve
+        if phases is not None:
+            line["decode_phases"] = phases
         print(json.dumps(line), flush=True)
     kv.close()
     model.close()
@@ -563,6 +584,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-sweep", action="store_true", help="skip the configs[1] operator sweep report")
+    ap.add_argument("--no-phases", action="store_true", help="skip the per-phase decode timing")
     ap.add_argument("--layers", type=int, default=0,
                     help="override the layer count (a small case for ncu captures; reported in config)")
     ap.add_argument("--serve", action="store_true",

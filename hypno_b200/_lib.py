@@ -97,6 +97,9 @@ SIGNATURES = {
     "hc_prefill": (_I, [_P, _P, _I, _P, _I, _P]),
     "hc_decode_step": (_I, [_P, _P, _P, _P, _I, _P, _P]),
     "hc_decode_step_dev": (_I, [_P, _P, _P, _P, _I, _P, _P]),
+    "hc_decode_step_phases": (_I, [_P, _P, _P, _P, _I, _P, _P]),
+    "hc_phase_count": (_I, []),
+    "hc_phase_name": (ctypes.c_char_p, [_I]),
     "hc_comm_unique_id": (_I, [_P]),
     "hc_comm_init": (_I, [_P, _P, _I, _I, ctypes.c_double]),
     "hc_synth_normal_host": (_I, [_U64, _U64, _U64, _U64, _F, _P]),

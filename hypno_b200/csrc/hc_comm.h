@@ -20,11 +20,14 @@ int comm_allgather_host(Comm* c, const void* send, void* recv, size_t bytes);
 struct PeerAr;
 int peer_ar_init(Comm* c, int rank, int size, size_t rows_cap, size_t H, PeerAr** out);
 void peer_ar_free(PeerAr* a, int rank, int size);
-float* peer_ar_partial(PeerAr* a);  // this rank's [rows_cap][H] partial buffer
+// This rank's [rows_cap][H] partial buffer of slot 0 (o_proj) or 1
+// (down_proj); the two slots must alternate from call to call.
+float* peer_ar_partial(PeerAr* a, int slot);
 bool peer_ar_fits(const PeerAr* a, size_t rows, size_t H);
-// hidden[r] += sum over ranks of partial[r] (rank order); then, when w is not
-// null, xn[r] = RMSNorm(hidden[r]) * w and its fp16 copy in GEMM K order.
-int peer_ar_residual_norm(PeerAr* a, int rank, int size, size_t rows, float* hidden, size_t ldh, const float* w,
-                          float eps, float* xn, size_t ldxn, __half* xn16, int* err, cudaStream_t s);
+// hidden[r] += sum over ranks of partial[r] of the slot (rank order); then,
+// when w is not null, xn[r] = RMSNorm(hidden[r]) * w and its fp16 copy in
+// GEMM K order.
+int peer_ar_residual_norm(PeerAr* a, int slot, int rank, int size, size_t rows, float* hidden, size_t ldh,
+                          const float* w, float eps, float* xn, size_t ldxn, __half* xn16, int* err, cudaStream_t s);
 
 }  // namespace hc

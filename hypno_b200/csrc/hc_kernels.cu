@@ -887,7 +887,11 @@ int launch_embed(const DevWeight& emb, const uint32_t* ids, size_t B, float* out
 
 // ============================================================ argmax
 // Greedy pick: the LAST maximal index wins (Iterator::max_by, run.rs:234-238).
-__global__ void k_argmax(const float* __restrict__ logits, int n, uint32_t* __restrict__ out) {
+// Row-wise last maximal index (the tie rule of Rust's max_by): out[row] =
+// index; with pairs, pairs[row] = (max, bits of idx0 + index) for the
+// vocabulary-sharded exchange of tensor parallelism.
+__global__ void k_argmax(const float* __restrict__ logits, int n, uint32_t* __restrict__ out,
+                         float2* __restrict__ pairs = nullptr, uint32_t idx0 = 0) {
     __shared__ float sv[32];
     __shared__ int si[32];
     const float* l = logits + (size_t)blockIdx.x * n;
@@ -942,8 +946,20 @@ __global__ void k_argmax(const float* __restrict__ logits, int n, uint32_t* __re
             int oi = __shfl_xor_sync(0xffffffffu, bi, o);
             if (oi >= 0 && (bi < 0 || ov > best || (ov == best && oi > bi))) { best = ov; bi = oi; }
         }
-        if (lane == 0) out[blockIdx.x] = (uint32_t)(bi < 0 ? 0 : bi);
+        if (lane == 0) {
+            if (pairs)
+                pairs[blockIdx.x] = make_float2(best, __uint_as_float(bi < 0 ? 0xFFFFFFFFu : idx0 + (uint32_t)bi));
+            else
+                out[blockIdx.x] = (uint32_t)(bi < 0 ? 0 : bi);
+        }
     }
+}
+
+int launch_argmax_pairs(const float* logits, size_t rows, size_t n, uint32_t idx0, float2* pairs, cudaStream_t s) {
+    if (rows == 0) return HC_OK;
+    k_argmax<<<(unsigned)rows, 1024, 0, s>>>(logits, (int)n, nullptr, pairs, idx0);
+    HC_LAUNCH_CHECK();
+    return HC_OK;
 }
 
 int launch_argmax(const float* logits, size_t rows, size_t n, uint32_t* out, cudaStream_t s) {

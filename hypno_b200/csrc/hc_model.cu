@@ -203,13 +203,47 @@ struct Scratch {
     float* tp_tmp = nullptr;      // [tokens][hidden] partial sums to all-reduce
     float* split_part = nullptr;  // [kPartSplits][min(tokens, kPartRows)][max(hidden, qkv)] split-K slabs
     float* tp_gather = nullptr;   // [tp][rows][vocab_shard] gathered logits
+    float2* tp_pairs = nullptr;   // [1 + tp][rows] (max logit, index bits): this rank's, then the gathered ones
     // grouped decode attention workspace
     size_t attn_cap = 0;
     float* attn_ws = nullptr;
 };
 
+// Per-phase device timing of one decode step (instrumentation): an event is
+// recorded on the model's stream at the start of every phase; the time to the
+// next event is charged to that phase.
+enum Phase : int {
+    PH_EMBED, PH_NORM, PH_QKV, PH_ROPE, PH_ATTN, PH_O, PH_REDUCE, PH_GATEUP, PH_DOWN, PH_LMHEAD, PH_LOGITS_X,
+    PH_ARGMAX, PH_COUNT
+};
+const char* const kPhaseNames[PH_COUNT] = {"embed",      "rmsnorm",   "qkv_gemm",       "rope_kv_store",
+                                           "attention",  "o_gemm",    "reduce_residual_norm", "gate_up_gemm",
+                                           "down_gemm",  "lm_head_gemm", "logits_exchange",  "argmax"};
+
+struct PhaseProf {
+    std::vector<cudaEvent_t> ev;
+    std::vector<int> ph;
+    size_t n = 0;
+    int mark(int p, cudaStream_t s) {
+        if (n == ev.size()) {
+            cudaEvent_t e;
+            HC_CUDA(cudaEventCreate(&e));
+            ev.push_back(e);
+            ph.push_back(0);
+        }
+        ph[n] = p;
+        HC_CUDA(cudaEventRecord(ev[n], s));
+        n++;
+        return HC_OK;
+    }
+    ~PhaseProf() {
+        for (cudaEvent_t e : ev) cudaEventDestroy(e);
+    }
+};
+
 struct hc_model {
     int refs = 1;            // the caller's handle + one per live hc_kv
+    PhaseProf* prof = nullptr;  // set only inside hc_decode_step_phases
     hc_config cfg{};
     int device = 0;
     cudaStream_t stream = nullptr;
@@ -389,6 +423,7 @@ void free_model(hc_model* m) {
     if (m->sc.tp_tmp) cudaFree(m->sc.tp_tmp);
     if (m->sc.split_part) cudaFree(m->sc.split_part);
     if (m->sc.tp_gather) cudaFree(m->sc.tp_gather);
+    if (m->sc.tp_pairs) cudaFree(m->sc.tp_pairs);
     if (m->par) hc::peer_ar_free(m->par, m->cfg.tp_rank, m->cfg.tp_size);
     if (m->comm) hc::comm_free(m->comm);
     if (m->stream) cudaStreamDestroy(m->stream);
@@ -442,8 +477,12 @@ int ensure_scratch(hc_model* m, size_t tokens, size_t logit_rows) {
         HC_CUDA(cudaMalloc((void**)&s.logits, r * c.vocab_size * sizeof(float)));
         if (s.tp_gather) cudaFree(s.tp_gather);
         s.tp_gather = nullptr;
-        if (m->cfg.tp_size > 1)
+        if (s.tp_pairs) cudaFree(s.tp_pairs);
+        s.tp_pairs = nullptr;
+        if (m->cfg.tp_size > 1) {
             HC_CUDA(cudaMalloc((void**)&s.tp_gather, r * m->vocab_shard * m->cfg.tp_size * sizeof(float)));
+            HC_CUDA(cudaMalloc((void**)&s.tp_pairs, r * (1 + m->cfg.tp_size) * sizeof(float2)));
+        }
         HC_CUDA(cudaMalloc((void**)&s.argmax, r * sizeof(uint32_t)));
         s.cap_logit_rows = r;
         s.generation++;
@@ -477,6 +516,8 @@ int ensure_attn_ws(hc_model* m, size_t rows, size_t nh, size_t max_pos, size_t n
     return HC_OK;
 }
 
+inline int phase(hc_model* m, int p) { return m->prof ? m->prof->mark(p, m->stream) : HC_OK; }
+
 // y = W . x for `tokens` rows (the Q4_0 path picks the CUDA-core matvec for
 // few tokens and the tcgen05 GEMM otherwise).
 int matmul(hc_model* m, const DevWeight& w, const float* x, size_t ldx, size_t tokens, float* y, size_t ldy, int epi,
@@ -499,10 +540,11 @@ __global__ void k_add_rows(float* __restrict__ y, const float* __restrict__ a, s
 // the next RMSNorm (weight next_norm, when given) and then sets *normed; other
 // sizes (prefill) use NCCL and leave the norm to the caller.
 int row_parallel(hc_model* m, const DevWeight& w, const float* x, size_t ldx, size_t rows, const __half* x16,
-                 const float* next_norm = nullptr, bool* normed = nullptr) {
+                 int gemm_phase, const float* next_norm = nullptr, bool* normed = nullptr) {
     const size_t H = m->cfg.hidden_size;
     Scratch& s = m->sc;
     if (normed) *normed = false;
+    HC_TRY(phase(m, gemm_phase));
     if (m->cfg.tp_size <= 1) {
         // decode sizes: K split over CTAs whose partial slabs are added by the
         // residual + next-RMSNorm kernel (no cluster reduction in the GEMM)
@@ -511,6 +553,7 @@ int row_parallel(hc_model* m, const DevWeight& w, const float* x, size_t ldx, si
             int splits = 1;
             HC_TRY(hc::gemm_tc_partials(m->gemm_ws, w.q4, x, ldx, rows, s.split_part, kPartSplits, &splits, m->stream,
                                         x16));
+            HC_TRY(phase(m, PH_REDUCE));
             HC_TRY(hc::launch_residual_splits_norm(s.split_part, splits, rows, H, s.hidden, H, next_norm,
                                                    m->cfg.rms_norm_eps, s.xn, H, s.xn16, m->stream));
             if (normed) *normed = next_norm != nullptr;
@@ -520,15 +563,19 @@ int row_parallel(hc_model* m, const DevWeight& w, const float* x, size_t ldx, si
     }
     HC_CHECK(m->comm, HC_ERR_STATE, "tensor-parallel model used before hc_comm_init");
     if (m->par && hc::peer_ar_fits(m->par, rows, H)) {
-        float* part = hc::peer_ar_partial(m->par);
+        // o_proj and down_proj alternate, each with its own partial buffer
+        const int slot = gemm_phase == PH_DOWN ? 1 : 0;
+        float* part = hc::peer_ar_partial(m->par, slot);
         HC_TRY(matmul(m, w, x, ldx, rows, part, H, hc::EPI_STORE, nullptr, 0, x16));
-        HC_TRY(hc::peer_ar_residual_norm(m->par, m->cfg.tp_rank, m->cfg.tp_size, rows, s.hidden, H, next_norm,
+        HC_TRY(phase(m, PH_REDUCE));
+        HC_TRY(hc::peer_ar_residual_norm(m->par, slot, m->cfg.tp_rank, m->cfg.tp_size, rows, s.hidden, H, next_norm,
                                          m->cfg.rms_norm_eps, s.xn, H, s.xn16, hc::gemm_error_flag(m->gemm_ws),
                                          m->stream));
         if (normed) *normed = next_norm != nullptr;
         return HC_OK;
     }
     HC_TRY(matmul(m, w, x, ldx, rows, s.tp_tmp, H, hc::EPI_STORE, nullptr, 0, x16));
+    HC_TRY(phase(m, PH_REDUCE));
     HC_TRY(hc::comm_allreduce_sum(m->comm, s.tp_tmp, rows * H, m->stream));
     size_t n = rows * H;
     k_add_rows<<<(unsigned)((n + 255) / 256), 256, 0, m->stream>>>(s.hidden, s.tp_tmp, n);
@@ -553,16 +600,58 @@ int lm_head_logits(hc_model* m, const float* x, size_t rows, float* logits, cons
         HC_CUDA(cudaMemsetAsync(logits, 0, rows * c.vocab_size * sizeof(float), m->stream));
         return HC_OK;
     }
+    HC_TRY(phase(m, PH_LMHEAD));
     if (c.tp_size <= 1)
         return matmul(m, m->lm_head, x, c.hidden_size, rows, logits, c.vocab_size, hc::EPI_STORE, nullptr, 0, x16);
     HC_CHECK(m->comm, HC_ERR_STATE, "tensor-parallel model used before hc_comm_init");
     const size_t vs = m->vocab_shard;
     float* mine = m->sc.tp_gather + (size_t)c.tp_rank * rows * vs;
     HC_TRY(matmul(m, m->lm_head, x, c.hidden_size, rows, mine, vs, hc::EPI_STORE, nullptr, 0, x16));
+    HC_TRY(phase(m, PH_LOGITS_X));
     HC_TRY(hc::comm_allgather(m->comm, mine, m->sc.tp_gather, rows * vs, m->stream));
     size_t n = rows * c.vocab_size;
     unsigned grid = (unsigned)std::min<size_t>((n + 255) / 256, 4096);
     k_unshard_logits<<<grid, 256, 0, m->stream>>>(m->sc.tp_gather, logits, (int)rows, (int)vs, c.tp_size);
+    HC_LAUNCH_CHECK();
+    return HC_OK;
+}
+
+// Greedy ids of a vocabulary-sharded LM head without gathering the logits:
+// each rank takes the last maximal index of its slice (k_argmax's rule), the
+// ranks exchange (max, index) pairs, and every rank keeps the largest max,
+// ties to the larger index, which the rank order makes the global last
+// maximal index (run.rs:234-238).
+__global__ void k_pick_pairs(const float2* __restrict__ pairs, int rows, int tp, uint32_t* __restrict__ out) {
+    const int row = blockIdx.x * blockDim.x + threadIdx.x;
+    if (row >= rows) return;
+    float best = -INFINITY;
+    int bi = -1;
+    for (int r = 0; r < tp; r++) {
+        const float2 p = pairs[(size_t)r * rows + row];
+        const int oi = (int)__float_as_uint(p.y);
+        if (oi >= 0 && (bi < 0 || p.x > best || (p.x == best && oi > bi))) {
+            best = p.x;
+            bi = oi;
+        }
+    }
+    out[row] = (uint32_t)(bi < 0 ? 0 : bi);
+}
+
+int lm_head_argmax_tp(hc_model* m, const float* x, size_t rows, uint32_t* argmax, const __half* x16) {
+    const hc_config& c = m->cfg;
+    HC_CHECK(m->comm, HC_ERR_STATE, "tensor-parallel model used before hc_comm_init");
+    HC_TRY(phase(m, PH_LMHEAD));
+    const size_t vs = m->vocab_shard;
+    float* mine = m->sc.tp_gather + (size_t)c.tp_rank * rows * vs;
+    HC_TRY(matmul(m, m->lm_head, x, c.hidden_size, rows, mine, vs, hc::EPI_STORE, nullptr, 0, x16));
+    HC_TRY(phase(m, PH_ARGMAX));
+    float2* local = m->sc.tp_pairs;
+    float2* all = local + rows;
+    HC_TRY(hc::launch_argmax_pairs(mine, rows, vs, (uint32_t)m->vocab0, local, m->stream));
+    HC_TRY(phase(m, PH_LOGITS_X));
+    HC_TRY(hc::comm_allgather(m->comm, reinterpret_cast<const float*>(local), reinterpret_cast<float*>(all), rows * 2,
+                              m->stream));
+    k_pick_pairs<<<(unsigned)((rows + 127) / 128), 128, 0, m->stream>>>(all, (int)rows, c.tp_size, argmax);
     HC_LAUNCH_CHECK();
     return HC_OK;
 }
@@ -592,9 +681,12 @@ int run_layers(hc_model* m, hc_kv* kv, size_t rows, bool prefill, int seq, int p
     if (tail_normed) *tail_normed = false;
     for (size_t li = 0; li < m->layers.size(); li++) {
         LayerW& L = m->layers[li];
-        if (!xn_ready)
+        if (!xn_ready) {
+            HC_TRY(phase(m, PH_NORM));
             HC_TRY(hc::launch_rmsnorm(s.hidden, H, L.in_norm, s.xn, H, rows, H, c.rms_norm_eps, m->stream, s.xn16));
+        }
         xn_ready = false;
+        HC_TRY(phase(m, PH_QKV));
         size_t lofs = li * kv->layer_stride * (kv->kv_fp16 ? 2 : 4);
         void* kc = (uint8_t*)kv->k + lofs;
         void* vc = (uint8_t*)kv->v + lofs;
@@ -618,17 +710,20 @@ int run_layers(hc_model* m, hc_kv* kv, size_t rows, bool prefill, int seq, int p
             ka.pos0 = pos0;
             ka.nq = (int)nq;
             ka.nk = (int)nk;
+            HC_TRY(phase(m, PH_ROPE));
             HC_TRY(hc::launch_rope_rows_slabs(s.split_part, splits, s.qkv, ldqkv, rows, ldqkv, nh_l + nkv_l, hd,
                                               m->rope, m->rope_rows, prefill ? nullptr : s.rowpos, pos0, m->stream,
                                               &ka));
         } else {
             HC_TRY(matmul(m, L.qkv, s.xn, H, rows, s.qkv, ldqkv, hc::EPI_STORE, nullptr, 0, s.xn16));
+            HC_TRY(phase(m, PH_ROPE));
             HC_TRY(hc::launch_rope_rows(s.qkv, ldqkv, rows, nh_l + nkv_l, hd, m->rope, m->rope_rows,
                                         prefill ? nullptr : s.rowpos, pos0, m->stream));
             HC_TRY(hc::launch_kv_store(s.qkv + nq, s.qkv + nq + nk, ldqkv, (int)rows, (int)nkv_l, (int)hd, kc, vc,
                                        kv->kv_fp16, kv->seq_stride, kv->head_stride, kv->max_pos,
                                        prefill ? nullptr : s.seqs, kv->pos_dev, seq, pos0, m->stream));
         }
+        HC_TRY(phase(m, PH_ATTN));
         hc::AttnParams P{};
         P.out16 = s.attn16;
         P.q = s.qkv;
@@ -727,10 +822,13 @@ int run_layers(hc_model* m, hc_kv* kv, size_t rows, bool prefill, int seq, int p
             HC_TRY(hc::launch_attention(P, (int)rows, kv->kv_fp16, m->stream));
         }
         bool normed = false;
-        HC_TRY(row_parallel(m, L.o, s.attn, nq, rows, s.attn16, L.post_norm, &normed));
-        if (!normed)
+        HC_TRY(row_parallel(m, L.o, s.attn, nq, rows, s.attn16, PH_O, L.post_norm, &normed));
+        if (!normed) {
+            HC_TRY(phase(m, PH_NORM));
             HC_TRY(hc::launch_rmsnorm(s.hidden, H, L.post_norm, s.xn, H, rows, H, c.rms_norm_eps, m->stream, s.xn16));
+        }
         size_t im = L.gu.n / 2;
+        HC_TRY(phase(m, PH_GATEUP));
         if (L.gu_blocked && hc::gemm_tc_eligible(L.gu.q4, rows)) {
             HC_TRY(hc::gemm_tc_silu(m->gemm_ws, L.gu.q4, s.xn, H, rows, s.act, im, s.act16, m->stream, s.xn16));
         } else {
@@ -739,7 +837,7 @@ int run_layers(hc_model* m, hc_kv* kv, size_t rows, bool prefill, int seq, int p
         }
         const bool last = li + 1 == m->layers.size();
         const float* next = last ? tail_norm : m->layers[li + 1].in_norm;
-        HC_TRY(row_parallel(m, L.down, s.act, im, rows, s.act16, next, &normed));
+        HC_TRY(row_parallel(m, L.down, s.act, im, rows, s.act16, PH_DOWN, next, &normed));
         if (last) {
             if (tail_normed) *tail_normed = normed;
         } else {
@@ -762,18 +860,27 @@ int decode_dev_impl(hc_model* m, hc_kv* kv, const int* seqs_dev, const uint32_t*
     HC_TRY(ensure_scratch(m, (size_t)B, (size_t)B));
     if (seqs_dev != s.seqs) HC_CUDA(cudaMemcpyAsync(s.seqs, seqs_dev, B * sizeof(int), cudaMemcpyDeviceToDevice, m->stream));
     if (ids_dev != s.ids) HC_CUDA(cudaMemcpyAsync(s.ids, ids_dev, B * sizeof(uint32_t), cudaMemcpyDeviceToDevice, m->stream));
+    HC_TRY(phase(m, PH_EMBED));
     k_gather_pos<<<(B + 127) / 128, 128, 0, m->stream>>>(s.seqs, kv->pos_dev, s.rowpos, B);
     HC_LAUNCH_CHECK();
     HC_TRY(hc::launch_embed(m->embed, s.ids, (size_t)B, s.hidden, c.hidden_size, m->stream));
     bool final_normed = false;
     HC_TRY(run_layers(m, kv, (size_t)B, false, 0, 0, m->final_norm, &final_normed));
+    HC_TRY(phase(m, PH_NORM));
     HC_TRY(hc::launch_advance(s.seqs, kv->pos_dev, B, m->stream));
     if (!final_normed)
         HC_TRY(hc::launch_rmsnorm(s.hidden, c.hidden_size, m->final_norm, s.xn, c.hidden_size, (size_t)B,
                                   c.hidden_size, c.rms_norm_eps, m->stream, s.xn16));
-    float* logits = logits_dev ? logits_dev : s.logits;
-    HC_TRY(lm_head_logits(m, s.xn, (size_t)B, logits, s.xn16));
-    if (argmax_dev) HC_TRY(hc::launch_argmax(logits, (size_t)B, c.vocab_size, argmax_dev, m->stream));
+    if (c.tp_size > 1 && !logits_dev && argmax_dev && m->lm_head.present) {
+        // greedy ids only: exchange (max, index) pairs instead of the logits
+        HC_TRY(lm_head_argmax_tp(m, s.xn, (size_t)B, argmax_dev, s.xn16));
+    } else {
+        float* logits = logits_dev ? logits_dev : s.logits;
+        HC_TRY(lm_head_logits(m, s.xn, (size_t)B, logits, s.xn16));
+        HC_TRY(phase(m, PH_ARGMAX));
+        if (argmax_dev) HC_TRY(hc::launch_argmax(logits, (size_t)B, c.vocab_size, argmax_dev, m->stream));
+    }
+    HC_TRY(phase(m, PH_COUNT));
     return HC_OK;
 }
 
@@ -1210,6 +1317,33 @@ HC_EXPORT int hc_decode_step_dev(hc_model* m, hc_kv* kv, const int* seqs_dev, co
     kv->host_stale = true;
     return HC_OK;
 }
+
+// One decode step like hc_decode_step_dev, launched eagerly with an event
+// between phases; waits for it and adds each phase's device time to
+// phase_ms[i] (hc_phase_count() entries, names from hc_phase_name).
+HC_EXPORT int hc_decode_step_phases(hc_model* m, hc_kv* kv, const int* seqs_dev, const uint32_t* ids_dev, int B,
+                                    uint32_t* argmax_dev, float* phase_ms) {
+    HC_CHECK(m && kv && kv->model == m, HC_ERR_INVALID, "hc_decode_step_phases: bad model/kv");
+    HC_CHECK(B > 0 && seqs_dev && ids_dev && phase_ms, HC_ERR_INVALID, "hc_decode_step_phases: bad arguments");
+    HC_CUDA(cudaSetDevice(m->device));
+    PhaseProf prof;
+    m->prof = &prof;
+    const int r = decode_dev_impl(m, kv, seqs_dev, ids_dev, B, nullptr, argmax_dev);
+    m->prof = nullptr;
+    HC_TRY(r);
+    HC_TRY(model_wait(m));
+    kv->host_stale = true;
+    for (size_t i = 0; i + 1 < prof.n; i++) {
+        float ms = 0.0f;
+        HC_CUDA(cudaEventElapsedTime(&ms, prof.ev[i], prof.ev[i + 1]));
+        if (prof.ph[i] < PH_COUNT) phase_ms[prof.ph[i]] += ms;
+    }
+    return HC_OK;
+}
+
+HC_EXPORT int hc_phase_count(void) { return PH_COUNT; }
+
+HC_EXPORT const char* hc_phase_name(int i) { return (i >= 0 && i < PH_COUNT) ? kPhaseNames[i] : ""; }
 
 // ============================================================ C ABI: tensor parallel
 

@@ -14,9 +14,11 @@
 //      rank, so the replicated residual stream stays identical), adds the
 //      residual, writes it back, and computes the RMSNorm of the new row
 //      (kernels.rs:592-625 arithmetic) plus its fp16 copy in GEMM K order,
-//   4. tells every peer it has finished reading, and waits for the same
-//      from all of them, so no rank overwrites its partial (the next
-//      projection) while a peer still reads it.
+// Each rank has two partial buffers, one for o_proj and one for down_proj,
+// which alternate.  A peer that says its partial for one of them is complete
+// has finished reading this rank's other buffer (its previous all-reduce
+// kernel completed before its projection ran), so a rank never overwrites a
+// partial a peer still reads, without a second handshake.
 // The epochs live in device memory, one counter per row slot, so the kernel
 // can be replayed from a CUDA graph.  Every wait is bounded; on expiry the
 // CTA sets the error flag the host checks after the step and skips the rest.
@@ -39,9 +41,7 @@ constexpr long long AR_WAIT_CYCLES = 2000000000LL;  // ~1 s at 1.9 GHz
 struct ArParams {
     const float* partial[AR_MAX_RANKS];  // rank-ordered partial buffers ([rows][H] each)
     uint32_t* ready_peer[AR_MAX_RANKS];  // rank p's ready flags ([row][AR_MAX_RANKS])
-    uint32_t* done_peer[AR_MAX_RANKS];
     uint32_t* ready_mine;
-    uint32_t* done_mine;
     uint32_t* epochs;  // [row] this rank's completed epochs
     int rank, size, H;
     float* hidden;
@@ -85,10 +85,8 @@ __global__ void __launch_bounds__(1024) k_ar_residual_norm(ArParams P) {
     __shared__ int ok_s;
     const int row = blockIdx.x;
     const int n4 = P.H / 4;
-    if (threadIdx.x == 0) {
-        const uint32_t e = P.epochs[row] + 1;
-        ok_s = handshake(P.ready_peer, P.ready_mine, row, P.rank, P.size, e) ? 1 : 0;
-    }
+    const uint32_t e = P.epochs[row] + 1;  // read by thread 0 alone below, after every thread read it here
+    if (threadIdx.x == 0) ok_s = handshake(P.ready_peer, P.ready_mine, row, P.rank, P.size, e) ? 1 : 0;
     __syncthreads();
     const bool ok = ok_s != 0;
     float4 v[VPT];
@@ -145,11 +143,8 @@ __global__ void __launch_bounds__(1024) k_ar_residual_norm(ArParams P) {
             }
         }
     }
-    __syncthreads();  // every read of the peers' partials of this row is done
     if (threadIdx.x == 0) {
-        const uint32_t e = P.epochs[row] + 1;
-        bool fine = ok && handshake(P.done_peer, P.done_mine, row, P.rank, P.size, e);
-        if (fine) P.epochs[row] = e;
+        if (ok) P.epochs[row] = e;
         else if (P.err) atomicExch(P.err, 1);
     }
 }
@@ -161,14 +156,15 @@ struct PeerAr {
     size_t rows_cap = 0, H = 0;
     uint8_t* base = nullptr;                  // this rank's block
     uint8_t* peer[AR_MAX_RANKS] = {};         // every rank's block (peer[rank] == base)
-    size_t partial_off = 0, ready_off = 0, done_off = 0, epoch_off = 0, bytes = 0;
+    size_t partial_off[2] = {0, 0}, ready_off = 0, epoch_off = 0, bytes = 0;
 };
 
 static void layout(PeerAr& a) {
-    a.partial_off = 0;
-    a.ready_off = (a.rows_cap * a.H * sizeof(float) + 255) & ~(size_t)255;
-    a.done_off = a.ready_off + a.rows_cap * AR_MAX_RANKS * sizeof(uint32_t);
-    a.epoch_off = a.done_off + a.rows_cap * AR_MAX_RANKS * sizeof(uint32_t);
+    const size_t part = (a.rows_cap * a.H * sizeof(float) + 255) & ~(size_t)255;
+    a.partial_off[0] = 0;
+    a.partial_off[1] = part;
+    a.ready_off = 2 * part;
+    a.epoch_off = a.ready_off + a.rows_cap * AR_MAX_RANKS * sizeof(uint32_t);
     a.bytes = a.epoch_off + a.rows_cap * sizeof(uint32_t);
 }
 
@@ -238,24 +234,24 @@ int peer_ar_init(Comm* c, int rank, int size, size_t rows_cap, size_t H, PeerAr*
     return HC_OK;
 }
 
-float* peer_ar_partial(PeerAr* a) { return a ? reinterpret_cast<float*>(a->base + a->partial_off) : nullptr; }
+float* peer_ar_partial(PeerAr* a, int slot) {
+    return a ? reinterpret_cast<float*>(a->base + a->partial_off[slot & 1]) : nullptr;
+}
 
 bool peer_ar_fits(const PeerAr* a, size_t rows, size_t H) { return a && rows >= 1 && rows <= a->rows_cap && H == a->H; }
 
-int peer_ar_residual_norm(PeerAr* a, int rank, int size, size_t rows, float* hidden, size_t ldh, const float* w,
-                          float eps, float* xn, size_t ldxn, __half* xn16, int* err, cudaStream_t s) {
+int peer_ar_residual_norm(PeerAr* a, int slot, int rank, int size, size_t rows, float* hidden, size_t ldh,
+                          const float* w, float eps, float* xn, size_t ldxn, __half* xn16, int* err, cudaStream_t s) {
     HC_CHECK(peer_ar_fits(a, rows, a ? a->H : 0), HC_ERR_INVALID, "peer all-reduce: %zu rows do not fit", rows);
     HC_CHECK((ldh % 4) == 0 && (ldxn % 4) == 0 && ((uintptr_t)hidden & 15) == 0 && ((uintptr_t)xn & 15) == 0 &&
                  (!w || ((uintptr_t)w & 15) == 0),
              HC_ERR_INVALID, "peer all-reduce: rows must be 16-byte aligned");
     ArParams P{};
     for (int p = 0; p < size; p++) {
-        P.partial[p] = reinterpret_cast<const float*>(a->peer[p] + a->partial_off);
+        P.partial[p] = reinterpret_cast<const float*>(a->peer[p] + a->partial_off[slot & 1]);
         P.ready_peer[p] = reinterpret_cast<uint32_t*>(a->peer[p] + a->ready_off);
-        P.done_peer[p] = reinterpret_cast<uint32_t*>(a->peer[p] + a->done_off);
     }
     P.ready_mine = reinterpret_cast<uint32_t*>(a->base + a->ready_off);
-    P.done_mine = reinterpret_cast<uint32_t*>(a->base + a->done_off);
     P.epochs = reinterpret_cast<uint32_t*>(a->base + a->epoch_off);
     P.rank = rank;
     P.size = size;

@@ -196,6 +196,18 @@ int hc_decode_step(hc_model* model, hc_kv* kv, const int* seqs, const uint32_t* 
 int hc_decode_step_dev(hc_model* model, hc_kv* kv, const int* seqs_dev, const uint32_t* ids_dev,
                        int B, float* logits_dev, uint32_t* argmax_dev);
 
+/* Instrumentation for benchmarks (no reference counterpart): one decode step
+ * as hc_decode_step_dev (argmax only), launched without a CUDA graph and with
+ * a CUDA event between phases; waits for the step and ADDS each phase's
+ * device milliseconds to phase_ms[0 .. hc_phase_count()).  Phase i is named
+ * by hc_phase_name(i) (embedding, norms, each projection GEMM, RoPE + KV
+ * store, attention, the reduction + residual + norm after o/down, LM head,
+ * logits exchange, argmax). */
+int hc_decode_step_phases(hc_model* model, hc_kv* kv, const int* seqs_dev, const uint32_t* ids_dev, int B,
+                          uint32_t* argmax_dev, float* phase_ms);
+int hc_phase_count(void);
+const char* hc_phase_name(int i);
+
 /* ---- tensor parallelism (new in this backend; the reference is single-CPU) */
 
 /* Writes a fresh 128-byte NCCL unique id (rank 0 creates it and shares it

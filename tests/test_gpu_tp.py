@@ -1,7 +1,9 @@
 """Tensor parallelism on 2, 4 and 8 GPUs: a small Llama-geometry model sharded
 over the ranks (all-reduce after o_proj / down_proj, vocabulary-sharded LM
-head) must match the single-device oracle.  Each size is skipped on a machine
-with fewer GPUs.  The 4- and 8-rank geometries leave one KV head per rank."""
+head) must match the single-device oracle, and the greedy ids of the
+argmax-only step (ranks exchange (max, index) pairs, no logits gather) must
+equal those of the gathered logits.  Each size is skipped on a machine with
+fewer GPUs.  The 4- and 8-rank geometries leave one KV head per rank."""
 import os
 import socket
 
@@ -38,15 +40,27 @@ def _rank(rank, size, port, q):
         m = engine.HypnoModel(img, rank, size)
         tp.join(m, rank, size, timeout_s=60)
         kv = engine.KVCache(m, n_seqs=2, max_pos=1024, kv_dtype=engine.KV_FP16)
+        kv2 = engine.KVCache(m, n_seqs=2, max_pos=1024, kv_dtype=engine.KV_FP16)  # greedy-only twin
         prompts = [synth.prompt_ids(geom["vocab"], T, seed=20 + s) for s, T in enumerate((300, 9))]
         first = [engine.batch_forward(m, p, kv, seq=s) for s, p in enumerate(prompts)]
+        for s, p in enumerate(prompts):
+            engine.batch_forward(m, p, kv2, seq=s)
         toks = [int(np.nonzero(f == f.max())[0][-1]) for f in first]
         steps = []
-        for _ in range(4):
+        ok, msg = True, ""
+        seqs_d = torch.tensor([0, 1], dtype=torch.int32, device=f"cuda:{rank}")
+        for st in range(4):
+            ids_d = torch.tensor(toks, dtype=torch.int32, device=f"cuda:{rank}")
             lg, am = engine.decode_step(m, kv, [0, 1], toks)
+            # greedy ids only: the ranks exchange (max, index) pairs instead of gathering the logits
+            out_d = torch.zeros(2, dtype=torch.int32, device=f"cuda:{rank}")
+            call("hc_decode_step_dev", m.handle, kv2.handle, seqs_d.data_ptr(), ids_d.data_ptr(), 2, None,
+                 out_d.data_ptr())
+            call("hc_sync", m.handle)
+            if [int(a) for a in am] != out_d.cpu().tolist():
+                ok, msg = False, f"pair-exchange greedy ids {out_d.cpu().tolist()} vs gathered logits {list(am)} step {st}"
             steps.append(lg)
             toks = [int(a) for a in am]
-        ok, msg = True, ""
         if rank == 0:
             om = orc.OracleModel(img)
             for s, p in enumerate(prompts):
@@ -64,6 +78,7 @@ def _rank(rank, size, port, q):
                 if err > 1e-3:
                     ok, msg = False, f"seq {s} rel err {err:.3e}"
         kv.close()
+        kv2.close()
         m.close()
         dist.barrier()
         dist.destroy_process_group()
