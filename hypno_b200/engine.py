@@ -9,6 +9,8 @@
                         (transformer.rs:465-528)
     decode_step         model_forward batched over sequences (the serve path
                         without its global mutex)
+    DeviceSampler       sample_token + XorShift64 (run.rs:203-278) on the device:
+                        a decode step returns token ids, not logits
 
 All of them call the C ABI (include/hypno_cuda.h); errors raise HypnoCudaError.
 """
@@ -18,7 +20,8 @@ import numpy as np
 
 from ._lib import KV_FP16, KV_FP32, HcConfig, call, load
 
-__all__ = ["HypnoModel", "KVCache", "batch_forward", "model_forward", "decode_step", "KV_FP32", "KV_FP16"]
+__all__ = ["HypnoModel", "KVCache", "batch_forward", "model_forward", "decode_step", "DeviceSampler", "KV_FP32",
+           "KV_FP16"]
 
 
 class HypnoModel:
@@ -141,3 +144,59 @@ def decode_step(model, kv, seqs, ids, want_logits=True, want_argmax=True):
     call("hc_decode_step", model.handle, kv.handle, s.ctypes.data, t.ctypes.data, B,
          logits.ctypes.data if logits is not None else None, am.ctypes.data if am is not None else None)
     return logits, am
+
+
+class DeviceSampler:
+    """sample_token (run.rs:203-251) with per-row XorShift64 states
+    (run.rs:267-278), run on the device by hc_sample_dev.
+
+    decode(...) runs one batched decode step with the logits kept in device
+    memory and returns, per row, the greedy id (last maximal logit) and the
+    sampled id; only 2 x B ids and B states cross to the host.  sample_host()
+    samples one row of host logits (the prefill's)."""
+
+    def __init__(self, model, max_rows):
+        import torch
+        self.model = model
+        self.V = int(model.config.vocab_size)
+        self.cap = int(max_rows)
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self.dev = dev
+        self.logits = torch.empty((self.cap, self.V), dtype=torch.float32, device=dev)
+        self.greedy = torch.empty(self.cap, dtype=torch.int32, device=dev)
+        self.out = torch.empty(self.cap, dtype=torch.int32, device=dev)
+
+    def _sample(self, B, logits_ptr, temps, top_ps, top_ks, states):
+        import torch
+        t = torch.tensor(np.asarray(temps, np.float32), device=self.dev)
+        p = torch.tensor(np.asarray(top_ps, np.float32), device=self.dev)
+        k = torch.tensor(np.asarray(top_ks, np.int32), device=self.dev)
+        st = torch.tensor(np.asarray(states, np.uint64).view(np.int64), device=self.dev)
+        torch.cuda.current_stream(self.dev).synchronize()  # the copies above land before the model's stream reads them
+        call("hc_sample_dev", logits_ptr, self.V, B, self.V, t.data_ptr(), p.data_ptr(), k.data_ptr(),
+             st.data_ptr(), self.out.data_ptr(), self.model.stream)
+        self.model.sync()
+        return self.out[:B].cpu().numpy().astype(np.uint32), st.cpu().numpy().view(np.uint64)
+
+    def decode(self, kv, seqs, ids, temps, top_ps, top_ks, states):
+        """One decode step of len(seqs) sequences; returns (greedy ids,
+        sampled ids, new states)."""
+        import torch
+        B = len(seqs)
+        if B > self.cap:
+            raise ValueError(f"{B} rows exceed the sampler's {self.cap}")
+        s = torch.tensor(np.asarray(seqs, np.int32), device=self.dev)
+        t = torch.tensor(np.asarray(ids, np.uint32).view(np.int32), device=self.dev)
+        torch.cuda.current_stream(self.dev).synchronize()
+        call("hc_decode_step_dev", self.model.handle, kv.handle, s.data_ptr(), t.data_ptr(), B,
+             self.logits.data_ptr(), self.greedy.data_ptr())
+        picked, new_states = self._sample(B, self.logits.data_ptr(), temps, top_ps, top_ks, states)
+        return self.greedy[:B].cpu().numpy().astype(np.uint32), picked, new_states
+
+    def sample_host(self, logits, temperature, top_p, top_k, state):
+        """One row of host logits; returns (token id, new state)."""
+        import torch
+        self.logits[0].copy_(torch.from_numpy(np.ascontiguousarray(logits, np.float32)))
+        torch.cuda.synchronize(self.dev)
+        picked, st = self._sample(1, self.logits.data_ptr(), [temperature], [top_p], [top_k], [state])
+        return int(picked[0]), int(st[0])

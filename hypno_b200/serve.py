@@ -23,11 +23,14 @@ reference's loop would end, with the same token count and finish reason:
 Differences that do not change the emitted tokens: the reference runs
 `model_forward` on its last emitted token although nothing reads those logits;
 the scheduler skips that forward.  The default token choice is the greedy
-last-maximal index (run.rs:234-238), taken on the device; a `sampler(logits,
-request)` callable gets the host logits instead (the reference's
-temperature / top-k / top-p sampler, serve.rs:279-305, is not part of this
-package).  Under tensor parallelism every rank runs the same scheduler with
-the same submissions, so all ranks issue the same collective steps.
+last-maximal index (run.rs:234-238), taken on the device.  A request
+submitted with `sampling=dict(temperature=, top_p=, top_k=, seed=)` is
+sampled like serve.rs:279-305 (temperature, top-k, top-p, XorShift64 seeded
+with `seed`), also on the device: the round's logits stay in device memory
+and only token ids come back.  A `sampler(logits, request)` callable gets the
+host logits instead.  Under tensor parallelism every rank runs the same
+scheduler with the same submissions, so all ranks issue the same collective
+steps.
 """
 from collections import deque
 
@@ -58,10 +61,16 @@ def greedy_last_max(logits):
 class Request:
     """One completion: the `Generation` of serve.rs plus its tokens."""
 
-    def __init__(self, rid, prompt_ids, max_tokens):
+    def __init__(self, rid, prompt_ids, max_tokens, sampling=None):
         self.id = rid
         self.prompt = np.ascontiguousarray(prompt_ids, dtype=np.uint32).reshape(-1)
         self.max_tokens = int(max_tokens)
+        self.sampling = None        # (temperature, top_p, top_k) when sampled
+        self.rng = 0                # XorShift64 state (XorShift64::new: seed.max(1))
+        if sampling is not None:
+            self.sampling = (float(sampling.get("temperature", 1.0)), float(sampling.get("top_p", 1.0)),
+                             int(sampling.get("top_k", 0)))
+            self.rng = max(int(sampling.get("seed", 0)) & 0xFFFFFFFFFFFFFFFF, 1)
         self.tokens = []            # emitted completion tokens
         self.finish_reason = None   # "stop" | "length" once done
         self.slot = -1
@@ -92,7 +101,7 @@ class BatchScheduler:
     """
 
     def __init__(self, model=None, kv=None, eos_id=None, sampler=None, prefill=None, decode=None,
-                 n_slots=None, max_pos=None):
+                 n_slots=None, max_pos=None, device_sampler=None):
         if prefill is None or decode is None:
             if model is None or kv is None:
                 raise ValueError("BatchScheduler needs a model and a KV cache, or prefill and decode callables")
@@ -109,6 +118,12 @@ class BatchScheduler:
         self._prefill, self._decode = prefill, decode
         self.eos_id = eos_id
         self.sampler = sampler
+        # requests submitted with sampling parameters are sampled on the device
+        self.device_sampler = device_sampler
+        if self.device_sampler is None and model is not None and kv is not None and sampler is None:
+            self._model, self._kv = model, kv
+        else:
+            self._model = self._kv = None
         self.n_slots, self.max_pos = int(n_slots), int(max_pos)
         self.free = list(range(self.n_slots - 1, -1, -1))   # pop() hands out slot 0 first
         self.waiting = deque()
@@ -119,10 +134,15 @@ class BatchScheduler:
         self.decode_steps = 0
 
     # ---- submission -----------------------------------------------------
-    def submit(self, prompt_ids, max_tokens):
+    def submit(self, prompt_ids, max_tokens, sampling=None):
         """Queues one request; returns its id.  A prompt that does not fit a
-        slot is refused here (the reference's cache would overflow)."""
-        r = Request(self._next_id, prompt_ids, max_tokens)
+        slot is refused here (the reference's cache would overflow).
+        `sampling`: None (greedy) or dict(temperature, top_p, top_k, seed)."""
+        r = Request(self._next_id, prompt_ids, max_tokens, sampling)
+        if r.sampling is not None and self.sampler is None and self.device_sampler is None:
+            if self._model is None:
+                raise ValueError("sampled requests need the device engine (or a sampler callable)")
+            self.device_sampler = engine.DeviceSampler(self._model, self.n_slots)
         if r.max_tokens < 0:
             raise ValueError("max_tokens must be >= 0")
         if r.prompt_tokens > self.max_pos:
@@ -137,7 +157,12 @@ class BatchScheduler:
 
     # ---- the reference loop body, one token -------------------------------
     def _pick(self, r, logits_row, greedy_id):
-        return self.sampler(logits_row, r) if self.sampler is not None else int(greedy_id)
+        if self.sampler is not None:
+            return self.sampler(logits_row, r)
+        if r.sampling is not None:  # prefill logits (host): one row through the device sampler
+            tok, r.rng = self.device_sampler.sample_host(logits_row, *r.sampling, r.rng)
+            return tok
+        return int(greedy_id)
 
     def _advance(self, r, nxt, emitted):
         """serve.rs:246-251 for one picked token; returns True if the request
@@ -182,6 +207,23 @@ class BatchScheduler:
             if not self._advance(r, self._pick(r, logits, greedy_last_max(logits)), emitted):
                 self._retire(r)
         slots = sorted(s for s, r in self.running.items() if r.feed is not None)
+        if slots and self.sampler is None and any(self.running[s].sampling is not None for s in slots):
+            # device sampling: logits stay on the device, ids and RNG states come back
+            rs = [self.running[s] for s in slots]
+            prm = [r.sampling if r.sampling is not None else (1.0, 1.0, 0) for r in rs]
+            greedy, picked, states = self.device_sampler.decode(
+                self._kv, slots, [r.feed for r in rs], [p[0] for p in prm], [p[1] for p in prm],
+                [p[2] for p in prm], [r.rng for r in rs])
+            self.decode_steps += 1
+            for i, (s, r) in enumerate(zip(slots, rs)):
+                self.pos[s] += 1
+                if r.sampling is not None:
+                    nxt, r.rng = int(picked[i]), int(states[i])
+                else:
+                    nxt = int(greedy[i])
+                if not self._advance(r, nxt, emitted):
+                    self._retire(r)
+            return emitted
         if slots:
             ids = [self.running[s].feed for s in slots]
             logits, greedy = self._decode(slots, ids, self.sampler is not None)

@@ -208,6 +208,22 @@ int hc_decode_step_phases(hc_model* model, hc_kv* kv, const int* seqs_dev, const
 int hc_phase_count(void);
 const char* hc_phase_name(int i);
 
+/* ---- sampling ---------------------------------------------------------- */
+
+/* run.rs:203-278 (sample_token with XorShift64::next_f32) for B rows of device
+ * logits (row stride ld floats, V entries each), one token per row, on the
+ * device: per-row temperature (exp(l / T) when T > 0, raw logits otherwise),
+ * top_k (0 = off) and top_p (1 = off) as device arrays of B, and a device
+ * array of B XorShift64 states (the caller seeds state = max(seed, 1)); a row
+ * that draws advances its state by one step.  The top-k and top-p thresholds
+ * are exact values of the row; sums are accumulated in f64 where the
+ * reference adds f32 terms in order, so a draw within that rounding of a
+ * boundary may pick the neighbouring token.  Stream-ordered, no
+ * synchronization. */
+int hc_sample_dev(const float* logits_dev, size_t ld, int B, int V, const float* temperature_dev,
+                  const float* top_p_dev, const int* top_k_dev, uint64_t* rng_state_dev, uint32_t* out_dev,
+                  void* stream);
+
 /* ---- tensor parallelism (new in this backend; the reference is single-CPU) */
 
 /* Writes a fresh 128-byte NCCL unique id (rank 0 creates it and shares it

@@ -966,3 +966,95 @@ ORC_API void orc_synth_normal(uint64_t seed, uint64_t stream, uint64_t offset, u
         out[i] = (float)z * scale;
     }
 }
+
+/* ------------------------------------------------------------------ */
+/* Sampling — run.rs:203-278                                           */
+/* ------------------------------------------------------------------ */
+
+/* XorShift64::next / next_f32, run.rs:267-278 (seed.max(1) at creation). */
+ORC_API uint64_t orc_xorshift_next(uint64_t* state) {
+    uint64_t x = *state;
+    x ^= x << 13;
+    x ^= x >> 7;
+    x ^= x << 17;
+    *state = x;
+    return x;
+}
+
+ORC_API float orc_xorshift_next_f32(uint64_t* state) { return (float)(orc_xorshift_next(state) >> 40) / 16777216.0f; }
+
+typedef struct { size_t i; float v; } orc_iv;
+
+/* sort_unstable_by(|a, b| b.1.partial_cmp(&a.1).unwrap_or(Equal)): descending;
+ * NaN compares Equal (its position is unspecified in the reference). */
+static int orc_cmp_desc(const void* a, const void* b) {
+    float x = ((const orc_iv*)a)->v, y = ((const orc_iv*)b)->v;
+    if (y > x) return 1;
+    if (y < x) return -1;
+    return 0;
+}
+
+/* Iterator::max_by with partial_cmp().unwrap_or(Equal): the last maximal
+ * element; an incomparable pair counts as Equal, so the later one wins. */
+static uint32_t orc_max_by_last(const float* v, size_t n) {
+    if (n == 0) return 0;
+    size_t bi = 0;
+    float best = v[0];
+    for (size_t i = 1; i < n; i++) {
+        float x = v[i];
+        int less = x < best;  /* partial_cmp(best, x) == Greater keeps best */
+        if (!less) { best = x; bi = i; }
+    }
+    return (uint32_t)bi;
+}
+
+/* sample_token, run.rs:203-251, step by step in f32 (sequential sums in index
+ * order, libm expf). */
+ORC_API uint32_t orc_sample_token(const float* logits, size_t n, float temperature, float top_p, size_t top_k,
+                                  uint64_t* rng_state) {
+    float* probs = (float*)malloc(n * sizeof(float));
+    orc_iv* idx = (orc_iv*)malloc((n ? n : 1) * sizeof(orc_iv));
+    memcpy(probs, logits, n * sizeof(float));
+    if (temperature > 0.0f) {
+        float inv_temp = 1.0f / temperature;
+        for (size_t i = 0; i < n; i++) probs[i] = expf(probs[i] * inv_temp);
+    }
+    if (top_k > 0 && top_k < n) {
+        for (size_t i = 0; i < n; i++) { idx[i].i = i; idx[i].v = probs[i]; }
+        qsort(idx, n, sizeof(orc_iv), orc_cmp_desc);
+        float threshold = idx[top_k - 1].v;
+        for (size_t i = 0; i < n; i++) if (probs[i] < threshold) probs[i] = 0.0f;
+    }
+    if (top_p < 1.0f) {
+        for (size_t i = 0; i < n; i++) { idx[i].i = i; idx[i].v = probs[i]; }
+        qsort(idx, n, sizeof(orc_iv), orc_cmp_desc);
+        float sum = 0.0f;
+        for (size_t i = 0; i < n; i++) sum += probs[i];
+        if (sum > 0.0f) {
+            float cumsum = 0.0f, threshold = 3.40282347e38f; /* f32::MAX */
+            for (size_t i = 0; i < n; i++) {
+                cumsum += idx[i].v / sum;
+                if (cumsum > top_p) { threshold = idx[i].v; break; }
+            }
+            for (size_t i = 0; i < n; i++) if (probs[i] < threshold) probs[i] = 0.0f;
+        }
+    }
+    float sum = 0.0f;
+    for (size_t i = 0; i < n; i++) sum += probs[i];
+    uint32_t out;
+    if (sum <= 0.0f) {
+        out = orc_max_by_last(logits, n);
+    } else {
+        float r = orc_xorshift_next_f32(rng_state);
+        float cumsum = 0.0f;
+        out = UINT32_MAX;
+        for (size_t i = 0; i < n; i++) {
+            cumsum += probs[i] / sum;
+            if (r < cumsum) { out = (uint32_t)i; break; }
+        }
+        if (out == UINT32_MAX) out = orc_max_by_last(probs, n);
+    }
+    free(probs);
+    free(idx);
+    return out;
+}

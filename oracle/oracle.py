@@ -67,6 +67,9 @@ def lib():
             "orc_num_threads": (ctypes.c_int, []),
             "orc_set_num_threads": (None, [ctypes.c_int]),
             "orc_synth_normal": (None, [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, F, P]),
+            "orc_xorshift_next": (ctypes.c_uint64, [P]),
+            "orc_xorshift_next_f32": (F, [P]),
+            "orc_sample_token": (ctypes.c_uint32, [P, SZ, F, F, SZ, P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -270,6 +273,23 @@ def batch_forward(model, ids, kv):
     if rc != 0:
         raise RuntimeError(f"oracle batch_forward failed ({rc})")
     return logits
+
+
+class XorShift64:
+    """run.rs:267-278 (state = seed.max(1))."""
+
+    def __init__(self, seed):
+        self.state = ctypes.c_uint64(max(int(seed), 1))
+
+    def next_f32(self):
+        return lib().orc_xorshift_next_f32(ctypes.byref(self.state))
+
+
+def sample_token(logits, temperature, top_p, top_k, rng):
+    """run.rs:203-251 (f32 step by step, sequential sums in index order)."""
+    l = _f32(logits)
+    return int(lib().orc_sample_token(l.ctypes.data, l.size, float(temperature), float(top_p), int(top_k),
+                                      ctypes.byref(rng.state)))
 
 
 def greedy(logits):

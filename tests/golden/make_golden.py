@@ -1,6 +1,7 @@
 """Generates the golden fixtures in tests/golden/ from the CPU oracle.
 
     python tests/golden/make_golden.py [--skip-c3]
+    python tests/golden/make_golden.py --c4      (BASELINE configs[3] at full size; ~30 min on 8 cores)
 
 The reference (Rust) cannot be built in this image and ships no golden
 vectors, so the fixtures come from the oracle (oracle/hypno_oracle.c, pinned
@@ -11,6 +12,9 @@ by the reference's own unit tests).  They freeze, per model:
     sum of squares of the logits, and every 499th logit.
 and, for BASELINE configs[1], the SHA-256 of the bit-exact Q4_0 packing of
 each sweep weight tensor.  GPU tests compare the backend against these.
+The c4 fixture is the full Llama-3-8B-shaped model (32 layers, hidden 4096):
+sequence 0's 2048-token prompt, then the prefill logits and 32 greedy steps,
+with the reference's FP32 KV cache (the oracle's faithful per-token path).
 """
 import argparse
 import hashlib
@@ -74,10 +78,25 @@ def sweep_fixture():
             "tensors": out}
 
 
+def c4_fixture():
+    cfg = synth.CONFIGS["c4"]
+    orc.use_all_cores()
+    img = synth.build_image(cfg, seed=0, quantize=orc.quantize_f32_to_q4_0,
+                            normal=lambda sd, st, n, std: orc.synth_normal(sd, st, n, std))
+    return model_fixture("configs[3] (c4), sequence 0", img, synth.prompt_ids(cfg["vocab"], cfg["prompt"], seed=0), 33)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--skip-c3", action="store_true")
+    ap.add_argument("--c4", action="store_true", help="only the full-size configs[3] fixture")
     args = ap.parse_args()
+    if args.c4:
+        v = c4_fixture()
+        with open(os.path.join(HERE, "c4.json"), "w") as f:
+            json.dump(v, f)
+        print("c4 greedy =", v["greedy"], "oracle s =", v["oracle_seconds"])
+        return
     fx = {}
     tiny = _models.reference_model_image(_models.TINY, 0.01, hf.DT_Q4_0)
     fx["tiny_q4"] = model_fixture("reference tiny model (turbo.rs:381-472), Q4_0", tiny,

@@ -56,3 +56,48 @@ def test_scheduler_on_device_equals_serial_oracle(cuda_device, image, n_slots, w
     finally:
         kv.close()
         model.close()
+
+
+def test_scheduler_device_sampling(cuda_device, image):
+    """Requests submitted with temperature / top_p / top_k / seed are sampled on
+    the device (logits never leave it) next to greedy ones.  Replaying every
+    request's emitted tokens through the oracle, each sampled token is the
+    oracle's sample_token on the oracle's logits with the request's XorShift64
+    sequence (serve.rs:279-305), or lies at a token boundary within rounding
+    of the draw; greedy requests get the oracle's greedy tokens."""
+    from ._sampling import boundary_margin
+    om = orc.OracleModel(image)
+    reqs = request_mix(SMALL["vocab"])
+    params = [dict(temperature=0.8, top_p=0.9, top_k=40, seed=11 + i) if i % 2 == 0 else None
+              for i in range(len(reqs))]
+    params[3] = dict(temperature=1.2, top_p=1.0, top_k=0, seed=5)
+    model = engine.HypnoModel(image)
+    kv = engine.KVCache(model, n_seqs=4, max_pos=SMALL["max_pos"], kv_dtype=engine.KV_FP32)
+    try:
+        sch = BatchScheduler(model, kv)
+        ids = [sch.submit(p, m, sampling=params[i]) for i, (p, m) in enumerate(reqs)]
+        out = sch.run()
+    finally:
+        kv.close()
+        model.close()
+    loose = []
+    for i, (p, m) in enumerate(reqs):
+        toks = out[ids[i]].tokens
+        assert len(toks) <= m
+        okv = om.new_kv(SMALL["max_pos"])
+        logits = orc.batch_forward(om, p, okv)
+        rng = orc.XorShift64(params[i]["seed"]) if params[i] else None
+        for st, t in enumerate(toks):
+            if rng is not None:
+                T, tp, tk = params[i]["temperature"], params[i]["top_p"], params[i]["top_k"]
+                before = int(rng.state.value)
+                want = orc.sample_token(logits, T, tp, tk, rng)
+                if t != want:
+                    loose.append((i, st, t, want, boundary_margin(logits, T, tp, tk, before, t, want)))
+                    break  # the trajectories part here
+            else:
+                assert t == orc.greedy(logits), (i, st)
+            if st + 1 < len(toks):
+                logits = orc.model_forward(om, t, okv)
+    assert all(x[-1] < 1e-4 for x in loose), loose
+    assert len(loose) <= 1, loose
