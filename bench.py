@@ -38,7 +38,18 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-METRIC = "Q4_0 decode tok/s (Llama-3-8B shape, 32 sequences x 2048 context)"
+SHAPES = {"c1": "SmolLM-135M shape", "c3": "TinyLlama-1.1B shape", "c4": "Llama-3-8B shape",
+          "c5": "Llama-3.1-70B shape"}
+GOLDEN_STEPS = 32  # greedy steps compared with the oracle's fixture
+
+
+def metric_name(name):
+    from hypno_b200 import synth
+    c = synth.CONFIGS[name]
+    n = c["seqs"]
+    return f"Q4_0 decode tok/s ({SHAPES[name]}, {n} sequence{'s' if n > 1 else ''} x {c['prompt']} context)"
+
+
 UNIT = "tok/s"
 # What the path computes in: Q4_0 weights; the tensor-core GEMMs multiply each
 # weight as two exact fp16 terms by each activation as fp16 hi + lo with f32
@@ -225,13 +236,17 @@ def graph_time_ms(fn, n, replays=3):
     return ms
 
 
-def roofline_gemv(dev, M=32, N=28672, K=4096, copies=4, reps=20):
+def roofline_gemv(dev, M=32, N=28672, K=4096, copies=0, reps=20):
     """Times the Q4_0 matmul of the fused gate/up shape over `copies` rotating
-    weight matrices (together larger than L2) and returns the roofline dict."""
+    weight matrices (together larger than L2: 256 MB or more) and returns the
+    roofline dict."""
     import torch
     from hypno_b200 import synth
     from hypno_b200._lib import call
     mats = []
+    if copies <= 0:
+        copies = max(2, -(-256 * 2 ** 20 // (N * K // 32 * 18)))
+    reps = max(reps, copies)
     w32 = torch.empty(N * K, dtype=torch.float32, device=dev)
     wq = torch.empty(N * K // 32 * 18, dtype=torch.uint8, device=dev)
     for c in range(copies):
@@ -262,7 +277,7 @@ def roofline_gemv(dev, M=32, N=28672, K=4096, copies=4, reps=20):
     # timed run does not take: the captured figure lives in profiles/
     return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
             "frac": round(achieved / peak, 4), "traffic": None,
-            "kernel": f"q4_0 matmul N={N} K={K} M={M}", "algorithmic_bytes": int(algo),
+            "kernel": f"q4_0 matmul N={N} K={K} M={M}", "algorithmic_bytes": int(algo), "copies": copies,
             "avg_launch_us": round(ms * 1e3, 2), "peak_source": f"{src} (hbm_gbs)"}
 
 
@@ -285,7 +300,7 @@ def q4_sweep(dev, reps=10):
     stream = torch.cuda.current_stream().cuda_stream
     for (N, K) in synth.SWEEP_NK:
         wbytes = N * K // 32 * 18
-        copies = max(2, min(6, -(-400 * 2 ** 20 // wbytes)))
+        copies = max(2, -(-400 * 2 ** 20 // wbytes))  # > L2 (126 MB) in total for every shape
         w32 = torch.empty(N * K, dtype=torch.float32, device=dev)
         wq = torch.empty(wbytes, dtype=torch.uint8, device=dev)
         mats = []
@@ -307,7 +322,7 @@ def q4_sweep(dev, reps=10):
 
             for i in range(3):
                 run(i)
-            ms = graph_time_ms(run, reps * copies)
+            ms = graph_time_ms(run, max(reps, copies))
             algo = 0.5625 * N * K + 4.0 * M * K + 4.0 * M * N
             flops = 2.0 * M * N * K
             row = {"N": N, "K": K, "M": M, "us": round(ms * 1e3, 2), "gbs": round(algo / (ms * 1e-3) / 1e9, 1),
@@ -324,8 +339,8 @@ def q4_sweep(dev, reps=10):
     return {"rows": out, "peaks": {"hbm_gbs": peak_gbs, "bf16_tflops": peak_tf, "source": src}}
 
 
-def cpu_baseline(img, cfg, budget_s=12.0, max_tokens=24):
-    """The oracle decoding one sequence at context 2048 on the host cores."""
+def cpu_baseline(img, cfg, budget_s=12.0, max_tokens=24, name="c4"):
+    """The oracle decoding one sequence at the prompt's context on the host cores."""
     from oracle import oracle as orc
     orc.use_all_cores()  # torchrun sets OMP_NUM_THREADS=1 for every rank
     om = orc.OracleModel(img)
@@ -339,18 +354,108 @@ def cpu_baseline(img, cfg, budget_s=12.0, max_tokens=24):
         n += 1
     dt = time.perf_counter() - t0
     return {"value": round(n / dt, 3), "unit": UNIT, "cores": orc.lib().orc_num_threads(), "kind": "port",
-            "sample": f"c4 model_forward, 1 sequence at context {cfg['prompt']} (KV positions set, zero-filled), "
+            "sample": f"{name} model_forward, 1 sequence at context {cfg['prompt']} (KV positions set, zero-filled), "
                       f"{n} tokens in {dt:.1f} s; the reference serialises sequences (serve.rs:175,193)"}
 
 
-def workload_config(world, mode="tp"):
+def prefill_roofline(cfg, tok_s, tp):
+    """Prefill as a fraction of the sustained dense bf16 tensor peak: the
+    useful flops per prompt token (2 x the matrix weights + the LM head on
+    the last token only, ignored, + causal attention scores and weighted V at
+    the prompt's mean context) per GPU."""
+    H, I, L = cfg["hidden"], cfg["inter"], cfg["layers"]
+    nh, nkv = cfg["heads"], cfg["kv_heads"]
+    hd = H // nh
+    w = L * (H * (nh + 2 * nkv) * hd + nh * hd * H + 3 * H * I)
+    attn = L * 2 * 2 * nh * hd * (cfg["prompt"] / 2)
+    fl = 2 * w + attn
+    peak = None
+    pth = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(pth):
+        with open(pth) as f:
+            peak = float(json.load(f).get("bf16_tflops_sustained", 0)) or None
+    src = "MEASURED_PEAKS.json bf16_tflops_sustained" if peak else "fallback 1400 TFLOP/s (sustained)"
+    peak = peak or 1400.0
+    ach = fl * tok_s / tp / 1e12
+    return {"bound": "tensor", "achieved": round(ach, 1), "peak": peak, "unit": "TFLOP/s per GPU",
+            "frac": round(ach / peak, 4), "flop_per_token": int(fl), "peak_source": src}
+
+
+def golden_parity(model, cfg, name, img_sha, engine):
+    """The oracle's committed fixture for this configuration
+    (tests/golden/<config>.json: the prompt of the workload's sequence 0, or a
+    short prompt for c5, then greedy steps), replayed through an FP32 KV cache:
+    greedy ids over the first 32 steps and the relative error of the recorded
+    logits.  Every rank runs it (tensor parallel collectives inside); rank 0
+    reports."""
+    path = os.path.join(ROOT, "tests", "golden", f"{name}.json")
+    if cfg["layers"] != synth_layers(name) or not os.path.exists(path):
+        return None
+    with open(path) as f:
+        g = json.load(f)
+    steps = min(GOLDEN_STEPS, g["steps"])
+    kv = engine.KVCache(model, n_seqs=1, max_pos=min(cfg["max_pos"], len(g["prompt"]) + steps + 1),
+                        kv_dtype=engine.KV_FP32)
+    logits = engine.batch_forward(model, np.array(g["prompt"], np.uint32), kv)
+    worst, match, first_bad = 0.0, 0, None
+    for st in range(steps):
+        rec = g["records"][st]
+        denom = max(1.0, max(abs(v) for _, v in rec["top"]))
+        err = float(np.max(np.abs(logits[::g["stride"]].astype(np.float64) - np.array(rec["sample"]))))
+        err = max([err] + [abs(float(logits[i]) - v) for i, v in rec["top"]]) / denom
+        worst = max(worst, err)
+        tok = int(np.nonzero(logits == logits.max())[0][-1])
+        if tok == g["greedy"][st]:
+            match += 1
+        elif first_bad is None:
+            first_bad = st
+        if st + 1 < steps:
+            lg, _ = engine.decode_step(model, kv, [0], [g["greedy"][st]])
+            logits = lg[0]
+    kv.close()
+    return {"fixture": f"tests/golden/{name}.json (CPU oracle: {len(g['prompt'])}-token prompt + {steps} greedy steps)",
+            "kv": "fp32", "image_sha256_match": None if img_sha is None else img_sha == g["image_sha256"],
+            "greedy_match": f"{match}/{steps}", "first_mismatch_step": first_bad,
+            "max_rel_err": float(f"{worst:.3e}"), "tolerance": 1e-3, "ok": match == steps and worst <= 1e-3}
+
+
+def synth_layers(name):
+    from hypno_b200 import synth
+    return synth.CONFIGS[name]["layers"]
+
+
+def workload_config(world, mode="tp", name="c4"):
+    from hypno_b200 import synth
+    c = synth.CONFIGS[name]
     par = "single" if world == 1 else (f"tp{world}" if mode == "tp" else f"replicas{world}")
-    return {"workload": "c4 decode: Llama-3-8B shape (hidden 4096, 32 layers, 32/8 heads, im 14336, vocab 128256), "
-                        "32 sequences each prefilled with 2048 random tokens, greedy batched decode, fp16 KV",
-            "model": "llama-3-8b-shape-random-q4_0", "global_batch": 32 if mode == "tp" else 32 * world,
-            "seq_len": 2048,
-            "parallelism": par,
-            "l2": "inputs larger than L2 (4.22 GB of Q4_0 weights + ~8.6 GB KV read per step)"}
+    S, P = c["seqs"], c["prompt"]
+    wgb = synth.model_bytes(c) / 1e9
+    desc = (f"{name} decode: {SHAPES[name]} (hidden {c['hidden']}, {c['layers']} layers, {c['heads']}/{c['kv_heads']} "
+            f"heads, im {c['inter']}, vocab {c['vocab']}), {S} sequence{'s' if S > 1 else ''} each prefilled with {P} "
+            f"random tokens, greedy batched decode, {c['kv']} KV")
+    return {"workload": desc, "model": SHAPES[name].lower().replace(" ", "-").replace(".", "") + "-random-q4_0",
+            "global_batch": S if mode == "tp" else S * world, "seq_len": P, "parallelism": par,
+            "l2": f"inputs larger than L2 ({wgb:.2f} GB of Q4_0 weights read per step)" if wgb > 0.126 else
+                  f"weights ({wgb * 1e3:.0f} MB) fit in L2: decode reads them from L2 after the first step"}
+
+
+def image_for(cfg, name, rank, world, dev, tp):
+    """The synthetic .hypno image of the configuration.  c5 (39 GB) is written
+    once to a file by rank 0 and memory-mapped by every rank (the page cache
+    holds one copy, as the reference's mmap loader would); the others are
+    built in host memory by each rank."""
+    from hypno_b200 import synth
+    if name != "c5":
+        return synth.build_image(cfg, seed=0, device=dev)
+    d = os.environ.get("HC_IMAGE_DIR", "/tmp")
+    path = os.path.join(d, f"hypno_synth_{name}_l{cfg['layers']}_seed0.hypno")
+    if rank == 0 and not os.path.exists(path):
+        synth.write_image_file(cfg, path + ".part", seed=0, device=dev)
+        os.replace(path + ".part", path)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    return np.memmap(path, dtype=np.uint8, mode="r")
 
 
 def run_ours(args):
@@ -362,7 +467,9 @@ def run_ours(args):
     if world > 1:
         import datetime
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+        # c5 writes its 39 GB image before the first barrier
+        tmo = 900 if args.config == "c5" else 180
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=tmo), device_id=dev)
     from hypno_b200 import build, engine, synth
     from hypno_b200._lib import call, load
     if rank == 0:
@@ -371,20 +478,30 @@ def run_ours(args):
         dist.barrier()
     lib = load()
     call("hc_set_device", local)
-    cfg = dict(synth.CONFIGS["c4"])
+    name = args.config
+    cfg = dict(synth.CONFIGS[name])
     if args.layers:
         cfg["layers"] = args.layers  # smaller model with the same per-layer kernels (profiling captures)
     S, P = cfg["seqs"], cfg["prompt"]
     tp = world > 1 and args.parallel == "tp"
-    img = synth.build_image(cfg, seed=0, device=dev)
+    img = image_for(cfg, name, rank, world, dev, tp)
+    torch.cuda.synchronize()
+    t_load = time.perf_counter()
     model = engine.HypnoModel(img, rank if tp else 0, world if tp else 1)
+    t_load = time.perf_counter() - t_load
+    load = {"seconds": t_load, "image_gb": img.nbytes / 1e9}
     if tp:
         from hypno_b200 import tp as tpmod
         tpmod.join(model, rank, world)
+    img_sha = None
+    if rank == 0:
+        import hashlib
+        img_sha = hashlib.sha256(img.data).hexdigest()
     if rank != 0:
         del img
         img = None
-    kv = engine.KVCache(model, n_seqs=S, max_pos=cfg["max_pos"], kv_dtype=engine.KV_FP16)
+    kv = engine.KVCache(model, n_seqs=S, max_pos=cfg["max_pos"],
+                        kv_dtype=engine.KV_FP16 if cfg["kv"] == "fp16" else engine.KV_FP32)
     stream = model.stream
 
     # ---- prefill (32 prompts), device-timed
@@ -404,7 +521,12 @@ def run_ours(args):
     e1.record(es)
     torch.cuda.synchronize()
     prefill_ms = e0.elapsed_time(e1)
-    prefill_tok_s = S * P / (prefill_ms * 1e-3)
+    if dist:
+        t = torch.tensor([prefill_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        prefill_ms = float(t.item())
+    prefill_tok_s = (1 if tp else world) * S * P / (prefill_ms * 1e-3)
+    prefill_roof = prefill_roofline(cfg, S * P / (prefill_ms * 1e-3), world if tp else 1)
 
     # ---- decode, device-resident inputs
     seqs_dev = torch.arange(S, dtype=torch.int32, device=dev)
@@ -491,10 +613,13 @@ def run_ours(args):
                   "how": "one eager decode step (no CUDA graph) with a CUDA event between phases, mean of 3 steps, "
                          "max over ranks per phase"}
 
+    # ---- parity of this very model against the oracle's fixture
+    parity = None if args.no_parity else golden_parity(model, cfg, name, img_sha, engine)
+
     # ---- optional: the same 32 requests through the continuous-batching
     # scheduler (prefill of each prompt + `steps` greedy tokens each), wall-clocked
     serve = None
-    if args.serve:
+    if not args.no_serve:
         from hypno_b200.serve import BatchScheduler
         sch = BatchScheduler(model, kv)
         for s in range(S):
@@ -513,24 +638,38 @@ def run_ours(args):
         serve = {"requests": S, "prompt_tokens": S * P, "completion_tokens": ntok, "seconds": round(serve_s, 3),
                  "completion_tok_s": round(ntok / serve_s, 1), "decode_rounds": sch.decode_steps}
 
-    roof = roofline_gemv(dev) if rank == 0 else None
-    sweep = q4_sweep(dev) if rank == 0 and not args.no_sweep else None
+    # model load: host image -> device weights (pinned chunked upload overlapped
+    # with the Q4_0 repack), wall-clocked per rank, max over ranks
+    lt = torch.tensor([load["seconds"]], device=dev)
+    if dist:
+        dist.all_reduce(lt, op=dist.ReduceOp.MAX)
+    load = {"seconds": round(float(lt.item()), 3), "image_gb": round(load["image_gb"], 3),
+            "image_gb_s": round(load["image_gb"] / float(lt.item()), 2),
+            "how": "hc_model_load of the whole .hypno image from host memory; with tensor parallelism each rank "
+                   "uploads its shard of it"}
+    # the dominant kernel: this rank's fused gate/up projection at the batch
+    rows_l = 2 * cfg["inter"] // (world if tp else 1)
+    roof = roofline_gemv(dev, M=S, N=rows_l, K=cfg["hidden"]) if rank == 0 else None
+    sweep = q4_sweep(dev) if rank == 0 and not args.no_sweep and name == "c4" else None
     cpu = None
     if rank == 0 and not args.no_cpu:
-        cpu = cpu_baseline(img, cfg)
+        cpu = cpu_baseline(img, cfg, name=name)
     if dist:
         dist.barrier()
     if rank == 0:
-        line = {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        line = {"metric": metric_name(name), "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
                 "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": DTYPE, "data": "synthetic",
-                "config": dict(workload_config(world, "tp" if tp else "dp"), layers=cfg["layers"]), "e2e": e2e, "gpu_launches": int(launches),
-                "prefill_tok_s": round(prefill_tok_s, 1), "clocks": clk.summary(), "roofline": roof,
+                "config": dict(workload_config(world, "tp" if tp else "dp", name), layers=cfg["layers"]), "e2e": e2e,
+                "gpu_launches": int(launches), "prefill_tok_s": round(prefill_tok_s, 1), "prefill": prefill_roof, "clocks": clk.summary(), "roofline": roof,
                 "cpu_baseline": cpu, "q4_sweep": sweep}
         if serve is not None:
             line["serve"] = serve
         if phases is not None:
             line["decode_phases"] = phases
+        line["model_load"] = load
+        if parity is not None:
+            line["parity"] = parity
         print(json.dumps(line), flush=True)
     kv.close()
     model.close()
@@ -545,7 +684,8 @@ def run_reference(args):
     from hypno_b200 import synth
     from oracle import oracle as orc
     cores = orc.use_all_cores()  # torchrun sets OMP_NUM_THREADS=1 for every rank
-    cfg = dict(synth.CONFIGS["c4"])
+    name = args.config
+    cfg = dict(synth.CONFIGS[name])
     if args.layers:
         cfg["layers"] = args.layers
     # built on the CPU with the oracle's generator and quantizer: this arm never
@@ -566,11 +706,11 @@ def run_reference(args):
     cpu = {"value": round(v, 3), "unit": UNIT, "cores": cores, "kind": "port",
            "sample": f"each step = one model_forward of one sequence at context {cfg['prompt']} (the reference "
                      f"decodes sequences one at a time, serve.rs:175,193); {args.steps} steps in {dt:.1f} s"}
-    line = {"impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": UNIT, "n_gpus": world,
+    line = {"impl": "reference", "metric": metric_name(name), "value": round(v, 3), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 2),
             "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
             "dtype": "q4_0 weights, f32 compute (CPU restatement of hypno)", "data": "synthetic",
-            "config": dict(workload_config(world), layers=cfg["layers"]),
+            "config": dict(workload_config(world, "tp", name), layers=cfg["layers"]),
             "cpu_baseline": cpu,
             "e2e": {"value": round(v, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -585,10 +725,13 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-sweep", action="store_true", help="skip the configs[1] operator sweep report")
     ap.add_argument("--no-phases", action="store_true", help="skip the per-phase decode timing")
+    ap.add_argument("--no-parity", action="store_true", help="skip the check against tests/golden/<config>.json")
+    ap.add_argument("--config", default="c4", choices=["c4", "c5", "c1", "c3"],
+                    help="BASELINE configuration (default c4, the headline; c5 writes its image under $HC_IMAGE_DIR)")
     ap.add_argument("--layers", type=int, default=0,
                     help="override the layer count (a small case for ncu captures; reported in config)")
-    ap.add_argument("--serve", action="store_true",
-                    help="also time the requests end to end through hypno_b200.serve.BatchScheduler")
+    ap.add_argument("--no-serve", action="store_true",
+                    help="skip timing the requests end to end through hypno_b200.serve.BatchScheduler")
     ap.add_argument("--parallel", default="tp", choices=["tp", "dp"],
                     help="N > 1: tensor parallel over the ranks (default) or independent replicas")
     args = ap.parse_args()
@@ -596,8 +739,10 @@ def main():
         ap.error("--warmup must be >= 3")
     if args.steps < 1:
         ap.error("--steps must be >= 1")
-    if args.steps + args.warmup > 250:
-        ap.error("steps + warmup must fit the 256 decode positions of the c4 workload")
+    from hypno_b200 import synth
+    room = synth.CONFIGS[args.config]["decode"] - 6
+    if args.steps + args.warmup > room:
+        ap.error(f"steps + warmup must fit the {room + 6} decode positions of the {args.config} workload")
     if args.impl == "reference":
         run_reference(args)
     else:

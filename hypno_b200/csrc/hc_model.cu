@@ -8,6 +8,8 @@
 #include "hc_gemm.h"
 #include "hc_comm.h"
 
+#include <omp.h>
+
 #include <algorithm>
 #include <cmath>
 #include <cstring>
@@ -303,6 +305,86 @@ int dev_alloc(hc_model* m, void** p, size_t bytes) {
     return HC_OK;
 }
 
+// Host -> device upload of the image's weights (loader.rs:39-148 mmaps the
+// file; here the bytes go to HBM once): a ring of pinned host chunks, each
+// filled by OpenMP threads from the image (gathering a tensor-parallel
+// shard's rows or columns), copied asynchronously to a device chunk on a copy
+// stream, and repacked (Q4_0 blocks -> nibble and scale planes) on the
+// model's stream, so the gather of one chunk, the copy of the next and the
+// repack of the one before overlap.
+struct UploadPipe {
+    static constexpr int NSLOT = 4;
+    static constexpr size_t CHUNK = size_t(32) << 20;  // bytes per slot
+    uint8_t* host[NSLOT] = {};
+    uint8_t* dev[NSLOT] = {};
+    cudaEvent_t copied[NSLOT] = {};  // the slot's host -> device copy landed
+    cudaEvent_t done[NSLOT] = {};    // the slot's buffers are free again
+    bool used[NSLOT] = {};
+    cudaStream_t cs = nullptr;
+    int next = 0, threads = 1;
+    size_t bytes = 0;  // moved so far
+
+    int init() {
+        for (int i = 0; i < NSLOT; i++) {
+            HC_CUDA(cudaHostAlloc((void**)&host[i], CHUNK, cudaHostAllocDefault));
+            HC_CUDA(cudaMalloc((void**)&dev[i], CHUNK));
+            HC_CUDA(cudaEventCreateWithFlags(&copied[i], cudaEventDisableTiming));
+            HC_CUDA(cudaEventCreateWithFlags(&done[i], cudaEventDisableTiming));
+        }
+        HC_CUDA(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking));
+        threads = std::max(1, std::min(16, omp_get_num_procs()));  // torchrun's OMP_NUM_THREADS=1 does not apply
+        return HC_OK;
+    }
+    void release() {
+        if (cs) cudaStreamSynchronize(cs);
+        for (int i = 0; i < NSLOT; i++) {
+            if (done[i] && used[i]) cudaEventSynchronize(done[i]);
+            if (host[i]) cudaFreeHost(host[i]);
+            if (dev[i]) cudaFree(dev[i]);
+            if (copied[i]) cudaEventDestroy(copied[i]);
+            if (done[i]) cudaEventDestroy(done[i]);
+            host[i] = dev[i] = nullptr;
+            copied[i] = done[i] = nullptr;
+        }
+        if (cs) cudaStreamDestroy(cs);
+        cs = nullptr;
+    }
+    // The next slot, once its previous chunk has been copied and repacked.
+    int acquire(int* s) {
+        const int k = next;
+        next = (next + 1) % NSLOT;
+        if (used[k]) HC_CUDA(cudaEventSynchronize(done[k]));
+        used[k] = true;
+        *s = k;
+        return HC_OK;
+    }
+    // host[s] <- `rows` runs of `run` bytes, run i starting at src + i * pitch
+    void gather(int s, const uint8_t* src, size_t rows, size_t run, size_t pitch) {
+        uint8_t* dst = host[s];
+        if (run == pitch) {  // one contiguous range: split it over the threads
+            const size_t n = rows * run, sl = size_t(1) << 20;
+            const long long pieces = (long long)((n + sl - 1) / sl);
+#pragma omp parallel for schedule(static) num_threads(threads)
+            for (long long i = 0; i < pieces; i++) {
+                const size_t o = (size_t)i * sl;
+                std::memcpy(dst + o, src + o, std::min(sl, n - o));
+            }
+        } else {
+#pragma omp parallel for schedule(static) num_threads(threads)
+            for (long long i = 0; i < (long long)rows; i++)
+                std::memcpy(dst + (size_t)i * run, src + (size_t)i * pitch, run);
+        }
+        bytes += rows * run;
+    }
+    // host[s] -> dev[s] on the copy stream; the model's stream waits for it
+    int copy_in(int s, size_t n, cudaStream_t model_stream) {
+        HC_CUDA(cudaMemcpyAsync(dev[s], host[s], n, cudaMemcpyHostToDevice, cs));
+        HC_CUDA(cudaEventRecord(copied[s], cs));
+        HC_CUDA(cudaStreamWaitEvent(model_stream, copied[s], 0));
+        return HC_OK;
+    }
+};
+
 // One dense 1-D f32 vector (norm weights): FP32 / FP16 converted, anything
 // else (or absent) -> ones (load_1d_f32, transformer.rs:250-264).
 int upload_norm(hc_model* m, const HypnoImage& img, const std::string& name, size_t len, float** out) {
@@ -327,9 +409,10 @@ struct Part {
 };
 
 // Uploads the row concatenation of `parts` (each an [rows x k_full] slice) as
-// one device weight of shape [sum rows x cols].  All parts share dtype.
+// one device weight of shape [sum rows x cols] through the upload pipeline.
+// All parts share dtype.
 int upload_weight(hc_model* m, const HypnoImage& img, const std::vector<Part>& parts, size_t k_full, DevWeight& w,
-                  uint8_t** staging, size_t* staging_cap) {
+                  UploadPipe& pipe) {
     uint32_t dt = parts[0].t->dtype;
     size_t n = 0, cols = parts[0].cols;
     for (auto& p : parts) {
@@ -357,55 +440,76 @@ int upload_weight(hc_model* m, const HypnoImage& img, const std::vector<Part>& p
         size_t blk_off = 0;
         for (auto& p : parts) {
             const uint8_t* src = img.payload(*p.t);
-            size_t kb_full = k_full / 32;
+            const size_t kb_full = k_full / 32;
+            // a run = the blocks of one row of the shard (or, for the flattened
+            // layout of widths % 32 != 0, one whole stretch of blocks)
+            size_t runs, run_blocks, pitch_blocks;
+            const uint8_t* base;
             if (k_full % 32 != 0) {
-                size_t nb = p.t->len / 18;
-                size_t bytes = nb * 18;
-                if (bytes > *staging_cap) {
-                    if (*staging) cudaFree(*staging);
-                    HC_CUDA(cudaMalloc((void**)staging, bytes));
-                    *staging_cap = bytes;
+                runs = 1;
+                run_blocks = p.t->len / 18;
+                pitch_blocks = run_blocks;
+                base = src;
+            } else {
+                HC_CHECK(p.t->len >= (p.row0 + p.rows) * kb_full * 18, HC_ERR_FORMAT,
+                         "Q4_0 tensor payload shorter than its shape");
+                runs = p.rows;
+                run_blocks = cols / 32;
+                pitch_blocks = kb_full;
+                base = src + (p.row0 * kb_full + p.col0 / 32) * 18;
+            }
+            if (runs == 1) {  // one long run: chunks of whole blocks
+                const size_t per = UploadPipe::CHUNK / 18;
+                for (size_t b0 = 0; b0 < run_blocks; b0 += per) {
+                    const size_t nb = std::min(per, run_blocks - b0);
+                    int sl;
+                    HC_TRY(pipe.acquire(&sl));
+                    pipe.gather(sl, base + b0 * 18, 1, nb * 18, nb * 18);
+                    HC_TRY(pipe.copy_in(sl, nb * 18, m->stream));
+                    HC_TRY(hc::launch_q4_split(pipe.dev[sl], nb, w.q4.qs + blk_off, w.q4.sc + blk_off, m->stream));
+                    HC_CUDA(cudaEventRecord(pipe.done[sl], m->stream));
+                    blk_off += nb;
                 }
-                HC_CUDA(cudaMemcpyAsync(*staging, src, bytes, cudaMemcpyHostToDevice, m->stream));
-                HC_TRY(hc::launch_q4_split(*staging, nb, w.q4.qs, w.q4.sc, m->stream));
-                HC_CUDA(cudaStreamSynchronize(m->stream));
                 continue;
             }
-            HC_CHECK(p.t->len >= (p.row0 + p.rows) * kb_full * 18, HC_ERR_FORMAT,
-                     "Q4_0 tensor payload shorter than its shape");
-            size_t kb = cols / 32, kb0 = p.col0 / 32;
-            // Gather the shard's blocks row by row into a host-contiguous AoS run.
-            size_t bytes = p.rows * kb * 18;
-            if (bytes > *staging_cap) {
-                if (*staging) cudaFree(*staging);
-                HC_CUDA(cudaMalloc((void**)staging, bytes));
-                *staging_cap = bytes;
+            const size_t per = std::max<size_t>(1, UploadPipe::CHUNK / (run_blocks * 18));  // rows per chunk
+            HC_CHECK(run_blocks * 18 <= UploadPipe::CHUNK, HC_ERR_UNSUPPORTED, "a row of %zu blocks exceeds an upload chunk",
+                     run_blocks);
+            for (size_t r0 = 0; r0 < runs; r0 += per) {
+                const size_t nr = std::min(per, runs - r0);
+                int sl;
+                HC_TRY(pipe.acquire(&sl));
+                pipe.gather(sl, base + r0 * pitch_blocks * 18, nr, run_blocks * 18, pitch_blocks * 18);
+                HC_TRY(pipe.copy_in(sl, nr * run_blocks * 18, m->stream));
+                HC_TRY(hc::launch_q4_split(pipe.dev[sl], nr * run_blocks, w.q4.qs + blk_off, w.q4.sc + blk_off,
+                                           m->stream));
+                HC_CUDA(cudaEventRecord(pipe.done[sl], m->stream));
+                blk_off += nr * run_blocks;
             }
-            if (kb == kb_full) {
-                HC_CUDA(cudaMemcpyAsync(*staging, src + p.row0 * kb_full * 18, bytes, cudaMemcpyHostToDevice,
-                                        m->stream));
-            } else {
-                HC_CUDA(cudaMemcpy2DAsync(*staging, kb * 18, src + (p.row0 * kb_full + kb0) * 18, kb_full * 18,
-                                          kb * 18, p.rows, cudaMemcpyHostToDevice, m->stream));
-            }
-            HC_TRY(hc::launch_q4_split(*staging, p.rows * kb, w.q4.qs + blk_off, w.q4.sc + blk_off, m->stream));
-            HC_CUDA(cudaStreamSynchronize(m->stream));
-            blk_off += p.rows * kb;
         }
         return HC_OK;
     }
     size_t es = (dt == HC_DTYPE_FP32) ? 4 : (dt == HC_DTYPE_FP16 ? 2 : 0);
     HC_CHECK(es != 0, HC_ERR_UNSUPPORTED, "weight dtype %u (Q8_0) is not supported by the GPU backend", dt);
     HC_TRY(dev_alloc(m, &w.dense, n * cols * es));
+    const size_t row_bytes = cols * es;
+    HC_CHECK(row_bytes <= UploadPipe::CHUNK, HC_ERR_UNSUPPORTED, "a row of %zu bytes exceeds an upload chunk", row_bytes);
+    const size_t per = UploadPipe::CHUNK / row_bytes;
     size_t row_off = 0;
     for (auto& p : parts) {
         HC_CHECK(p.t->len >= (p.row0 + p.rows) * k_full * es, HC_ERR_FORMAT, "tensor payload shorter than its shape");
         const uint8_t* src = img.payload(*p.t) + (p.row0 * k_full + p.col0) * es;
-        HC_CUDA(cudaMemcpy2DAsync((uint8_t*)w.dense + row_off * cols * es, cols * es, src, k_full * es, cols * es,
-                                  p.rows, cudaMemcpyHostToDevice, m->stream));
+        for (size_t r0 = 0; r0 < p.rows; r0 += per) {
+            const size_t nr = std::min(per, p.rows - r0);
+            int sl;
+            HC_TRY(pipe.acquire(&sl));
+            pipe.gather(sl, src + r0 * k_full * es, nr, row_bytes, k_full * es);
+            HC_CUDA(cudaMemcpyAsync((uint8_t*)w.dense + (row_off + r0) * row_bytes, pipe.host[sl], nr * row_bytes,
+                                    cudaMemcpyHostToDevice, pipe.cs));
+            HC_CUDA(cudaEventRecord(pipe.done[sl], pipe.cs));
+        }
         row_off += p.rows;
     }
-    HC_CUDA(cudaStreamSynchronize(m->stream));
     return HC_OK;
 }
 
@@ -929,13 +1033,13 @@ HC_EXPORT int hc_model_load(const uint8_t* image, size_t len, int tp_rank, int t
         delete m;
         return HC_ERR_CUDA;
     }
-    uint8_t* staging = nullptr;
-    size_t staging_cap = 0;
+    UploadPipe pipe;
     auto fail = [&](int r) {
-        if (staging) cudaFree(staging);
+        pipe.release();
         free_model(m);
         return r;
     };
+    if (int r0 = pipe.init()) return fail(r0);
     const size_t nh_l = nh / tp_size, nkv_l = nkv / tp_size, im_l = im / tp_size;
     m->nq = nh_l * hd;
     m->nk = nkv_l * hd;
@@ -957,15 +1061,14 @@ HC_EXPORT int hc_model_load(const uint8_t* image, size_t len, int tp_rank, int t
                               {{tq, tp_rank * nh_l * hd, nh_l * hd, 0, H},
                                {tk, tp_rank * nkv_l * hd, nkv_l * hd, 0, H},
                                {tv, tp_rank * nkv_l * hd, nkv_l * hd, 0, H}},
-                              H, L.qkv, &staging, &staging_cap);
+                              H, L.qkv, pipe);
         } else {
             hc_set_error("hypno: q/k/v projections of layer %zu must share a dtype and (for Q4_0) a width that is a "
                          "multiple of 32", li);
             r = HC_ERR_UNSUPPORTED;
         }
         if (r) return fail(r);
-        if ((r = upload_weight(m, img, {{to, 0, H, tp_rank * nh_l * hd, nh_l * hd}}, nh * hd, L.o, &staging,
-                               &staging_cap)))
+        if ((r = upload_weight(m, img, {{to, 0, H, tp_rank * nh_l * hd, nh_l * hd}}, nh * hd, L.o, pipe)))
             return fail(r);
         if (tg->dtype != tu->dtype) {
             hc_set_error("hypno: gate/up projections of layer %zu must share a dtype", li);
@@ -981,13 +1084,12 @@ HC_EXPORT int hc_model_load(const uint8_t* image, size_t len, int tp_rank, int t
                 parts.push_back({tg, tp_rank * im_l + b, (size_t)hc::GU_BLOCK, 0, H});
                 parts.push_back({tu, tp_rank * im_l + b, (size_t)hc::GU_BLOCK, 0, H});
             }
-            r = upload_weight(m, img, parts, H, L.gu, &staging, &staging_cap);
+            r = upload_weight(m, img, parts, H, L.gu, pipe);
         } else {
-            r = upload_weight(m, img, {{tg, tp_rank * im_l, im_l, 0, H}, {tu, tp_rank * im_l, im_l, 0, H}}, H, L.gu,
-                              &staging, &staging_cap);
+            r = upload_weight(m, img, {{tg, tp_rank * im_l, im_l, 0, H}, {tu, tp_rank * im_l, im_l, 0, H}}, H, L.gu, pipe);
         }
         if (r) return fail(r);
-        if ((r = upload_weight(m, img, {{td, 0, H, tp_rank * im_l, im_l}}, im, L.down, &staging, &staging_cap)))
+        if ((r = upload_weight(m, img, {{td, 0, H, tp_rank * im_l, im_l}}, im, L.down, pipe)))
             return fail(r);
         if ((r = upload_norm(m, img, p + "input_layernorm.weight", H, &L.in_norm))) return fail(r);
         if ((r = upload_norm(m, img, p + "post_attention_layernorm.weight", H, &L.post_norm))) return fail(r);
@@ -997,7 +1099,7 @@ HC_EXPORT int hc_model_load(const uint8_t* image, size_t len, int tp_rank, int t
     const TensorEntry* te = img.find("model.embed_tokens.weight");
     const TensorEntry* tl = img.find("lm_head.weight");
     if (te) {
-        if ((r = upload_weight(m, img, {{te, 0, c.vocab_size, 0, H}}, H, m->embed, &staging, &staging_cap)))
+        if ((r = upload_weight(m, img, {{te, 0, c.vocab_size, 0, H}}, H, m->embed, pipe)))
             return fail(r);
         m->cfg.embed_dtype = te->dtype;
     }
@@ -1011,8 +1113,7 @@ HC_EXPORT int hc_model_load(const uint8_t* image, size_t len, int tp_rank, int t
         return fail(HC_ERR_UNSUPPORTED);
     }
     if (tl) {
-        if ((r = upload_weight(m, img, {{tl, m->vocab0, m->vocab_shard, 0, H}}, H, m->lm_head, &staging,
-                               &staging_cap)))
+        if ((r = upload_weight(m, img, {{tl, m->vocab0, m->vocab_shard, 0, H}}, H, m->lm_head, pipe)))
             return fail(r);
         m->cfg.lm_head_dtype = tl->dtype;
         m->cfg.lm_head_tied = 0;
@@ -1033,8 +1134,12 @@ HC_EXPORT int hc_model_load(const uint8_t* image, size_t len, int tp_rank, int t
         m->cfg.lm_head_dtype = te->dtype;
         m->cfg.lm_head_tied = 1;
     }
-    if (staging) cudaFree(staging);
-    staging = nullptr;
+    // every chunk repacked or copied before the pinned ring goes away
+    if (cudaStreamSynchronize(m->stream) != cudaSuccess || cudaStreamSynchronize(pipe.cs) != cudaSuccess) {
+        hc_set_error("hypno: weight upload failed (%s)", cudaGetErrorString(cudaGetLastError()));
+        return fail(HC_ERR_CUDA);
+    }
+    pipe.release();
     m->gemm_ws = hc::gemm_workspace_new();
     if (!hc::gemm_error_flag(m->gemm_ws)) {  // allocated now: kernels captured later refer to it
         hc_set_error("cannot allocate the pipeline error flag");

@@ -4,19 +4,24 @@
 //
 // Per row (temperature T, top_p, top_k, the row's XorShift64 state):
 //   p_i = T > 0 ? exp(l_i * (1 / T)) : l_i                     (run.rs:207-210)
-//   top_k in (0, V): keep p_i >= the top_k-th largest p        (run.rs:212-217)
-//   top_p < 1: with sum = sum of p, keep p_i >= the value at which the
-//     descending cumulative sum of p / sum first exceeds top_p; when it never
-//     does, keep nothing                                        (run.rs:219-231)
-//   sum of the kept p <= 0: the last maximal logit (max_by)     (run.rs:233-238)
-//   else r = next_f32(); the first i whose cumulative kept p / sum exceeds r,
-//     or the last maximal kept p when rounding leaves none      (run.rs:240-250)
-// The thresholds are exact values of the row, found by a 3-pass radix search
-// over order-preserving keys (11 + 11 + 10 bits) with per-bucket counts and
-// f64 sums; every sum is accumulated in f64, where the reference adds f32
-// terms one by one (up to ~V * 2^-24 relative apart), so a draw that falls
-// within that rounding of a bucket edge may pick the neighbouring token.
-// exp is CUDA's expf (within 2 ulp of libm); NaN values are never kept.
+//   top_k in (0, V): p_i = 0 where p_i < the top_k-th largest p (run.rs:212-217)
+//   top_p < 1: sum = sum of p; walking p in descending order, the first value
+//     at which the running sum of p / sum exceeds top_p is the threshold
+//     (f32::MAX when it never does); p_i = 0 below it          (run.rs:219-231)
+//   sum of p <= 0: the last maximal logit (max_by)              (run.rs:233-238)
+//   else r = next_f32(); the first i at which the running sum of p_i / sum
+//     exceeds r, or the last maximal p when rounding leaves none (run.rs:240-250)
+// Every sum is the reference's: f32 additions one term at a time in the
+// reference's order.  One thread performs each such chain while the other
+// warps produce the next chunk of terms (exp, masking, the IEEE division) in
+// shared memory, so a chain costs about one f32 add latency per term.  The
+// top-k threshold is an exact value of the row, found by a 3-pass radix search
+// over order-preserving keys (11 + 11 + 10 bits); the top-p walk visits the
+// positive values in descending order in sorted chunks of up to SORT_CAP keys
+// (each chunk bounded below by a radix-selected key, its ties added last).
+// exp is CUDA's expf (within 2 ulp of the C library's), so a draw can differ
+// from the reference's only when it falls within a few ulp of a boundary.
+// NaN values are never kept (the reference would panic comparing them).
 #include "hc_internal.h"
 #include "hc_common.cuh"
 
@@ -27,7 +32,9 @@ namespace hc {
 namespace {
 
 constexpr int SMP_THREADS = 1024;
-constexpr int HB = 2048;  // buckets per radix pass
+constexpr int HB = 2048;        // buckets per radix pass
+constexpr int CH = 2048;        // terms per chain chunk
+constexpr int SORT_CAP = 2048;  // keys per sorted top-p chunk (<= HB: the sort reuses the bucket array)
 
 // Larger float -> larger key (NaN with a clear sign bit above +inf).
 __device__ __forceinline__ uint32_t fkey(float f) {
@@ -44,98 +51,162 @@ struct SampleRow {
     bool texp;
     float inv;
     __device__ __forceinline__ float prob(int i) const { return texp ? expf(__fmul_rn(l[i], inv)) : l[i]; }
+    // p_i after masking everything below floor_v to 0 (NaN is dropped too)
+    __device__ __forceinline__ float kept(int i, float floor_v) const {
+        const float p = prob(i);
+        return p >= floor_v ? p : 0.0f;
+    }
 };
 
-__device__ __forceinline__ double block_sum_f64(double v, double* red) {
+struct __align__(16) Shared {
+    uint32_t hcnt[HB];   // radix buckets; the top-p sort buffer
+    float cbuf[2][CH];   // chain chunks (double-buffered)
+    float red_v[32];
+    int red_i[32];
+    uint32_t red_u[32];
+    int sel;
+    uint32_t above;
+    int stop;
+    int n_gather;
+    float r;
+    float sumv;
+};
+
+__device__ __forceinline__ uint32_t block_sum_u32(uint32_t v, Shared& S) {
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     __syncthreads();
-    if (lane == 0) red[w] = v;
+    if (lane == 0) S.red_u[w] = v;
     __syncthreads();
-    double t = lane < (int)(blockDim.x >> 5) ? red[lane] : 0.0;
+    uint32_t t = lane < (int)(blockDim.x >> 5) ? S.red_u[lane] : 0u;
     for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
     return t;
 }
 
+// The reference's sequential f32 chain over i = 0..V-1 of the terms
+// a_i = kept p_i (divided by `div` when div != 0):
+//   pick == false: returns the sum a_0 + a_1 + ... (added left to right);
+//   pick == true: returns the first i at which r < the running sum, or -1.
+// Thread 0 adds chunk c while warps 1.. fill chunk c + 1.
+__device__ float chain_index(const SampleRow& R, float floor_v, float div, bool pick, float r, Shared& S,
+                             int* pick_out) {
+    const int V = R.V, nch = (V + CH - 1) / CH;
+    for (int j = threadIdx.x; j < CH && j < V; j += blockDim.x) {
+        const float p = R.kept(j, floor_v);
+        S.cbuf[0][j] = div != 0.0f ? __fdiv_rn(p, div) : p;
+    }
+    if (threadIdx.x == 0) S.stop = -1;
+    __syncthreads();
+    float acc = 0.0f;
+    for (int c = 0; c < nch; c++) {
+        const int base = c * CH, len = min(CH, V - base);
+        if (threadIdx.x == 0) {
+            const float* b = S.cbuf[c & 1];
+            if (pick) {
+                for (int j = 0; j < len; j++) {
+                    acc = __fadd_rn(acc, b[j]);
+                    if (r < acc) {
+                        S.stop = base + j;
+                        break;
+                    }
+                }
+            } else {
+                int j = 0;
+                for (; j + 8 <= len; j += 8) {
+                    const float4 u = *reinterpret_cast<const float4*>(b + j);
+                    const float4 v = *reinterpret_cast<const float4*>(b + j + 4);
+                    acc = __fadd_rn(acc, u.x);
+                    acc = __fadd_rn(acc, u.y);
+                    acc = __fadd_rn(acc, u.z);
+                    acc = __fadd_rn(acc, u.w);
+                    acc = __fadd_rn(acc, v.x);
+                    acc = __fadd_rn(acc, v.y);
+                    acc = __fadd_rn(acc, v.z);
+                    acc = __fadd_rn(acc, v.w);
+                }
+                for (; j < len; j++) acc = __fadd_rn(acc, b[j]);
+            }
+        } else if (threadIdx.x >= 32 && c + 1 < nch) {
+            const int nb = (c + 1) * CH, nl = min(CH, V - nb);
+            float* d = S.cbuf[(c + 1) & 1];
+            for (int j = (int)threadIdx.x - 32; j < nl; j += (int)blockDim.x - 32) {
+                const float p = R.kept(nb + j, floor_v);
+                d[j] = div != 0.0f ? __fdiv_rn(p, div) : p;
+            }
+        }
+        __syncthreads();
+        if (S.stop >= 0) break;
+    }
+    if (pick_out) *pick_out = S.stop;
+    if (threadIdx.x == 0) S.sumv = acc;  // thread 0's chain
+    __syncthreads();
+    const float out = S.sumv;
+    __syncthreads();
+    return out;
+}
+
 // Warp 0 walks the buckets from the top: the first bucket at which the
-// running total (counts when by_sum is false, f64 sums otherwise) reaches
-// `need` (counts: >= need; sums: > need).  Returns the bucket and the total
-// of the buckets above it, or -1 when the total never gets there.
-__device__ void find_from_top(const uint32_t* cnt, const double* sum, int nb, bool by_sum, double need, int* sel_out,
-                              double* above_out) {
+// running count reaches `need`.  Returns the bucket and the count of the
+// buckets above it, or -1 when the count never gets there.
+__device__ void find_from_top(const uint32_t* cnt, int nb, uint32_t need, int* sel_out, uint32_t* above_out) {
     if (threadIdx.x >= 32) return;
     const int lane = threadIdx.x;
     const int per = nb / 32;  // buckets per lane, lane 0 taking the top ones
-    double mine = 0.0;
-    for (int k = 0; k < per; k++) {
-        const int b = nb - 1 - (lane * per + k);
-        mine += by_sum ? sum[b] : (double)cnt[b];
-    }
-    double incl = mine;  // inclusive scan over lanes (top buckets first)
+    uint32_t mine = 0;
+    for (int k = 0; k < per; k++) mine += cnt[nb - 1 - (lane * per + k)];
+    uint32_t incl = mine;  // inclusive scan over lanes (top buckets first)
     for (int o = 1; o < 32; o <<= 1) {
-        const double t = __shfl_up_sync(0xffffffffu, incl, o);
+        const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
         if (lane >= o) incl += t;
     }
-    const double excl = incl - mine;
-    const double total = __shfl_sync(0xffffffffu, incl, 31);
-    const bool hit = by_sum ? (incl > need) : (incl >= need);
-    const unsigned ball = __ballot_sync(0xffffffffu, hit);
+    const uint32_t excl = incl - mine;
+    const unsigned ball = __ballot_sync(0xffffffffu, incl >= need);
     if (!ball) {
-        if (lane == 0) {
-            *sel_out = -1;
-            *above_out = total;
-        }
+        if (lane == 0) *sel_out = -1;
         return;
     }
     const int first = __ffs(ball) - 1;
     if (lane == first) {
-        double run = excl;
+        uint32_t run = excl;
         int sel = nb - 1 - lane * per;
         for (int k = 0; k < per; k++) {
             const int b = nb - 1 - (lane * per + k);
-            const double add = by_sum ? sum[b] : (double)cnt[b];
-            if (by_sum ? (run + add > need) : (run + add >= need)) {
+            if (run + cnt[b] >= need) {
                 sel = b;
                 break;
             }
-            run += add;
+            run += cnt[b];
         }
         *sel_out = sel;
         *above_out = run;
     }
 }
 
-// The key of the row's value at which the descending running count reaches
-// `need` (by_sum false) or the descending running sum of the kept values
-// exceeds `need` (by_sum true); kept = value >= floor_v.  Returns false when
-// the sum never exceeds need.
-__device__ bool radix_select(const SampleRow& R, float floor_v, bool by_sum, double need, uint32_t* key_out,
-                             uint32_t* hcnt, double* hsum, int* s_sel, double* s_above) {
+// Candidates: p >= floor_v whose key lies in [lo_key, hi_key].  Returns the
+// key at which the descending running count of candidates reaches `need`
+// (the need-th largest), or false when there are fewer candidates.
+__device__ bool radix_select(const SampleRow& R, float floor_v, uint32_t lo_key, uint32_t hi_key, uint32_t need,
+                             uint32_t* key_out, Shared& S) {
     uint32_t prefix = 0, mask = 0;
     const int shifts[3] = {21, 10, 0};
     const int widths[3] = {11, 11, 10};
     for (int pass = 0; pass < 3; pass++) {
         const int nb = 1 << widths[pass];
-        for (int b = threadIdx.x; b < nb; b += blockDim.x) {
-            hcnt[b] = 0;
-            hsum[b] = 0.0;
-        }
+        for (int b = threadIdx.x; b < nb; b += blockDim.x) S.hcnt[b] = 0;
         __syncthreads();
         for (int i = threadIdx.x; i < R.V; i += blockDim.x) {
             const float p = R.prob(i);
             if (!(p >= floor_v)) continue;
             const uint32_t k = fkey(p);
-            if ((k & mask) != prefix) continue;
-            const int b = (int)((k >> shifts[pass]) & (uint32_t)(nb - 1));
-            if (by_sum) atomicAdd(&hsum[b], (double)p);
-            else atomicAdd(&hcnt[b], 1u);
+            if (k < lo_key || k > hi_key || (k & mask) != prefix) continue;
+            atomicAdd(&S.hcnt[(k >> shifts[pass]) & (uint32_t)(nb - 1)], 1u);
         }
         __syncthreads();
-        find_from_top(hcnt, hsum, nb, by_sum, need, s_sel, s_above);
+        find_from_top(S.hcnt, nb, need, &S.sel, &S.above);
         __syncthreads();
-        const int sel = *s_sel;
+        const int sel = S.sel;
         if (sel < 0) return false;
-        need -= *s_above;
+        need -= S.above;
         prefix |= (uint32_t)sel << shifts[pass];
         mask |= (uint32_t)(nb - 1) << shifts[pass];
         __syncthreads();
@@ -144,13 +215,123 @@ __device__ bool radix_select(const SampleRow& R, float floor_v, bool by_sum, dou
     return true;
 }
 
-// Last index of the row maximum (max_by: the later of equal values wins).
-__device__ int last_max(const SampleRow& R, bool use_prob, float floor_v, float* red_v, int* red_i) {
+// Descending bitonic sort of S.hcnt[0..n) (n <= SORT_CAP), padded with 0 keys.
+__device__ void sort_keys_desc(int n, Shared& S) {
+    int m = 1;
+    while (m < n) m <<= 1;
+    for (int j = n + (int)threadIdx.x; j < m; j += blockDim.x) S.hcnt[j] = 0u;
+    __syncthreads();
+    for (int k = 2; k <= m; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int i = threadIdx.x; i < m; i += blockDim.x) {
+                const int o = i ^ j;
+                if (o > i) {
+                    const uint32_t a = S.hcnt[i], b = S.hcnt[o];
+                    const bool desc = (i & k) == 0;
+                    if (desc ? (a < b) : (a > b)) {
+                        S.hcnt[i] = b;
+                        S.hcnt[o] = a;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    }
+}
+
+// run.rs:219-231: the top-p threshold over p >= floor_v (the top-k survivors),
+// given their sequential sum `sum` > 0.  The running sum of p / sum only
+// grows at positive terms, so the walk visits the positive values in
+// descending order: chunks of the SORT_CAP largest keys still unvisited
+// (radix-selected bound, gathered, sorted), then that bound's ties.  Returns
+// false when the running sum never exceeds top_p.
+__device__ bool top_p_threshold(const SampleRow& R, float floor_v, float sum, float top_p, Shared& S, float* thr_out) {
+    const uint32_t lo = 0x80000001u;  // key of the smallest positive (denormal) value
+    uint32_t hi = 0xFFFFFFFFu;
+    float cum = 0.0f;  // thread 0's chain
+    for (;;) {
+        // keys of positive candidates in [lo, hi]
+        uint32_t cut;
+        bool all = !radix_select(R, floor_v, lo, hi, (uint32_t)SORT_CAP, &cut, S);
+        // gather the keys above the cut (all of them when fewer than SORT_CAP remain)
+        if (threadIdx.x == 0) S.n_gather = 0;
+        __syncthreads();
+        for (int i = threadIdx.x; i < R.V; i += blockDim.x) {
+            const float p = R.prob(i);
+            if (!(p >= floor_v)) continue;
+            const uint32_t k = fkey(p);
+            if (k < lo || k > hi || (!all && k <= cut)) continue;
+            S.hcnt[atomicAdd(&S.n_gather, 1)] = k;
+        }
+        __syncthreads();
+        const int n = S.n_gather;
+        __syncthreads();
+        uint32_t ties = 0;
+        if (!all) {
+            uint32_t t = 0;
+            for (int i = threadIdx.x; i < R.V; i += blockDim.x) {
+                const float p = R.prob(i);
+                t += (p >= floor_v && fkey(p) == cut) ? 1u : 0u;
+            }
+            ties = block_sum_u32(t, S);
+        }
+        if (n > 0) {
+            sort_keys_desc(n, S);
+            for (int j = threadIdx.x; j < n; j += blockDim.x) S.cbuf[0][j] = __fdiv_rn(keyf(S.hcnt[j]), sum);
+            __syncthreads();
+            if (threadIdx.x == 0) {
+                S.stop = -1;
+                for (int j = 0; j < n; j++) {
+                    cum = __fadd_rn(cum, S.cbuf[0][j]);
+                    if (cum > top_p) {
+                        S.stop = j;
+                        S.r = keyf(S.hcnt[j]);
+                        break;
+                    }
+                }
+            }
+            __syncthreads();
+            const bool found = S.stop >= 0;
+            const float thr = S.r;
+            __syncthreads();
+            if (found) {
+                *thr_out = thr;
+                return true;
+            }
+        }
+        if (all) return false;
+        if (threadIdx.x == 0) {
+            const float v = keyf(cut), q = __fdiv_rn(v, sum);
+            S.stop = -1;
+            for (uint32_t t = 0; t < ties; t++) {
+                cum = __fadd_rn(cum, q);
+                if (cum > top_p) {
+                    S.stop = 0;
+                    S.r = v;
+                    break;
+                }
+            }
+        }
+        __syncthreads();
+        const bool found = S.stop >= 0;
+        const float thr = S.r;
+        __syncthreads();
+        if (found) {
+            *thr_out = thr;
+            return true;
+        }
+        if (cut <= lo) return false;
+        hi = cut - 1u;
+    }
+}
+
+// Last index of the row maximum (max_by: the later of equal values wins);
+// over the logits (use_prob false) or over the masked p.
+__device__ int last_max(const SampleRow& R, bool use_prob, float floor_v, Shared& S) {
     float best = -INFINITY;
     int bi = -1;
     for (int i = threadIdx.x; i < R.V; i += blockDim.x) {
-        float v = use_prob ? R.prob(i) : R.l[i];
-        if (use_prob && !(v >= floor_v)) v = 0.0f;
+        const float v = use_prob ? R.kept(i, floor_v) : R.l[i];
         if (bi < 0 || v >= best) {
             best = v;
             bi = i;
@@ -167,14 +348,14 @@ __device__ int last_max(const SampleRow& R, bool use_prob, float floor_v, float*
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     __syncthreads();
     if (lane == 0) {
-        red_v[w] = best;
-        red_i[w] = bi;
+        S.red_v[w] = best;
+        S.red_i[w] = bi;
     }
     __syncthreads();
     if (w == 0) {
         const int nw = blockDim.x >> 5;
-        best = lane < nw ? red_v[lane] : -INFINITY;
-        bi = lane < nw ? red_i[lane] : -1;
+        best = lane < nw ? S.red_v[lane] : -INFINITY;
+        bi = lane < nw ? S.red_i[lane] : -1;
         for (int o = 16; o > 0; o >>= 1) {
             const float ov = __shfl_xor_sync(0xffffffffu, best, o);
             const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
@@ -183,10 +364,10 @@ __device__ int last_max(const SampleRow& R, bool use_prob, float floor_v, float*
                 bi = oi;
             }
         }
-        if (lane == 0) red_i[0] = bi;
+        if (lane == 0) S.red_i[0] = bi;
     }
     __syncthreads();
-    const int r = red_i[0];
+    const int r = S.red_i[0];
     __syncthreads();
     return r < 0 ? 0 : r;
 }
@@ -195,15 +376,7 @@ __global__ void __launch_bounds__(SMP_THREADS) k_sample(const float* __restrict_
                                                         const float* __restrict__ temp, const float* __restrict__ top_p,
                                                         const int* __restrict__ top_k, uint64_t* __restrict__ rng,
                                                         uint32_t* __restrict__ out) {
-    __shared__ uint32_t hcnt[HB];
-    __shared__ double hsum[HB];
-    __shared__ double red[32];
-    __shared__ float red_v[32];
-    __shared__ int red_i[32];
-    __shared__ int s_sel;
-    __shared__ double s_above;
-    __shared__ double s_chunk[SMP_THREADS];
-    __shared__ float s_r;
+    __shared__ Shared S;
     const int row = blockIdx.x;
     const float T = temp[row], tp = top_p[row];
     const int tk = top_k[row];
@@ -213,40 +386,25 @@ __global__ void __launch_bounds__(SMP_THREADS) k_sample(const float* __restrict_
     R.texp = T > 0.0f;
     R.inv = R.texp ? __fdiv_rn(1.0f, T) : 1.0f;
 
-    // top-k: keep p >= the top_k-th largest value
+    // top-k: p below the top_k-th largest value become 0
     float floor_v = -INFINITY;
     if (tk > 0 && tk < V) {
         uint32_t key;
-        if (radix_select(R, -INFINITY, false, (double)tk, &key, hcnt, hsum, &s_sel, &s_above)) floor_v = keyf(key);
+        if (radix_select(R, -INFINITY, 0u, 0xFFFFFFFFu, (uint32_t)tk, &key, S)) floor_v = keyf(key);
     }
-    // top-p on the kept values
+    // top-p over what top-k kept
     bool none = false;
     if (tp < 1.0f) {
-        double s = 0.0;
-        for (int i = threadIdx.x; i < V; i += blockDim.x) {
-            const float p = R.prob(i);
-            if (p >= floor_v) s += (double)p;
-        }
-        const float sum = (float)block_sum_f64(s, red);
+        const float sum = chain_index(R, floor_v, 0.0f, false, 0.0f, S, nullptr);
         if (sum > 0.0f) {
-            uint32_t key;
-            // the running sum of p / sum exceeds top_p where the running sum of p exceeds top_p * sum
-            if (radix_select(R, floor_v, true, (double)tp * (double)sum, &key, hcnt, hsum, &s_sel, &s_above))
-                floor_v = fmaxf(floor_v, keyf(key));
-            else
-                none = true;  // threshold f32::MAX: every p is cleared
+            float thr;
+            if (top_p_threshold(R, floor_v, sum, tp, S, &thr)) floor_v = fmaxf(floor_v, thr);
+            else none = true;  // threshold f32::MAX: every p becomes 0
         }
     }
-    // the sum of what is kept
-    double s = 0.0;
-    if (!none)
-        for (int i = threadIdx.x; i < V; i += blockDim.x) {
-            const float p = R.prob(i);
-            if (p >= floor_v) s += (double)p;
-        }
-    const float sum = none ? 0.0f : (float)block_sum_f64(s, red);
+    const float sum = none ? 0.0f : chain_index(R, floor_v, 0.0f, false, 0.0f, S, nullptr);
     if (!(sum > 0.0f)) {
-        const int i = last_max(R, false, -INFINITY, red_v, red_i);
+        const int i = last_max(R, false, -INFINITY, S);
         if (threadIdx.x == 0) out[row] = (uint32_t)i;
         return;
     }
@@ -256,59 +414,18 @@ __global__ void __launch_bounds__(SMP_THREADS) k_sample(const float* __restrict_
         x ^= x >> 7;
         x ^= x << 17;
         rng[row] = x;
-        s_r = (float)(x >> 40) / 16777216.0f;
+        S.r = (float)(x >> 40) / 16777216.0f;
     }
     __syncthreads();
-    // first i (ascending) whose running kept p exceeds r * sum: contiguous
-    // chunks per thread, an exclusive scan of the chunk sums, then the thread
-    // whose chunk holds the crossing walks it
-    const double target = (double)s_r * (double)sum;
-    const int per = (V + (int)blockDim.x - 1) / (int)blockDim.x;
-    const int i0 = (int)threadIdx.x * per, i1 = min(V, i0 + per);
-    double cs = 0.0;
-    for (int i = i0; i < i1; i++) {
-        const float p = R.prob(i);
-        if (p >= floor_v) cs += (double)p;
-    }
-    s_chunk[threadIdx.x] = cs;
+    const float r = S.r;
     __syncthreads();
-    if (threadIdx.x < 32) {  // warp 0: exclusive scan over the chunks (32 per lane)
-        const int lane = threadIdx.x, nper = (int)blockDim.x / 32;
-        double mine = 0.0;
-        for (int k = 0; k < nper; k++) mine += s_chunk[lane * nper + k];
-        double incl = mine;
-        for (int o = 1; o < 32; o <<= 1) {
-            const double t = __shfl_up_sync(0xffffffffu, incl, o);
-            if (lane >= o) incl += t;
-        }
-        double run = incl - mine;
-        for (int k = 0; k < nper; k++) {
-            const double c = s_chunk[lane * nper + k];
-            s_chunk[lane * nper + k] = run;
-            run += c;
-        }
-    }
-    __shared__ unsigned int s_pick;
-    if (threadIdx.x == 0) s_pick = 0xFFFFFFFFu;
-    __syncthreads();
-    double run = s_chunk[threadIdx.x];
-    if (run <= target) {  // only the chunk holding the crossing finds one
-        for (int i = i0; i < i1; i++) {
-            const float p = R.prob(i);
-            if (p >= floor_v) run += (double)p;
-            if (run > target) {
-                atomicMin(&s_pick, (unsigned int)i);
-                break;
-            }
-        }
-    }
-    __syncthreads();
-    const int pick = s_pick == 0xFFFFFFFFu ? -1 : (int)s_pick;
+    int pick = -1;
+    chain_index(R, floor_v, sum, true, r, S, &pick);
     if (pick >= 0) {
         if (threadIdx.x == 0) out[row] = (uint32_t)pick;
         return;
     }
-    const int i = last_max(R, true, floor_v, red_v, red_i);
+    const int i = last_max(R, true, floor_v, S);
     if (threadIdx.x == 0) out[row] = (uint32_t)i;
 }
 

@@ -27,14 +27,15 @@ __all__ = ["HypnoModel", "KVCache", "batch_forward", "model_forward", "decode_st
 class HypnoModel:
     """A .hypno model uploaded to the current CUDA device.
 
-    image: the file's bytes (bytes, bytearray, numpy uint8 array) or a path.
+    image: the file's bytes (bytes, bytearray, numpy uint8 array) or a path
+    (memory-mapped read-only, like HypnoModel::open, loader.rs:39-148).
     The image is parsed and every weight uploaded once; the host buffer is not
     referenced after construction.
     """
 
     def __init__(self, image, tp_rank=0, tp_size=1):
         if isinstance(image, str):
-            buf = np.fromfile(image, dtype=np.uint8)
+            buf = np.memmap(image, dtype=np.uint8, mode="r")
         elif isinstance(image, (bytes, bytearray)):
             buf = np.frombuffer(image, dtype=np.uint8)
         else:
@@ -48,7 +49,7 @@ class HypnoModel:
 
     @classmethod
     def open(cls, path, tp_rank=0, tp_size=1):
-        return cls(np.fromfile(path, dtype=np.uint8), tp_rank, tp_size)
+        return cls(path, tp_rank, tp_size)
 
     @property
     def handle(self):

@@ -119,8 +119,13 @@ def build_image(cfg, seed=0, std=0.02, values=None, quantize=None, device=None, 
     if quantize is None:
         from .ops import quantize_f32_to_q4_0
         quantize = quantize_f32_to_q4_0
-    tensors = []
-    for name, shape, kind in tensor_specs(cfg):
+    specs = [(name, tuple(shape), _stored_dtype(cfg, kind, int(np.prod(shape)))) for name, shape, kind in
+             tensor_specs(cfg)]
+    # the image is allocated once and filled in place (one tensor's values
+    # in flight), so the largest configuration fits in host memory
+    img, offsets = hf.empty_image(metadata(cfg), [(nm, sh, dt, hf.data_bytes(dt, int(np.prod(sh))))
+                                                  for nm, sh, dt in specs])
+    for name, shape, dt in specs:
         n = int(np.prod(shape))
         if values is not None:
             data = values(name, n)
@@ -128,17 +133,19 @@ def build_image(cfg, seed=0, std=0.02, values=None, quantize=None, device=None, 
             data = normal(seed, fnv1a64(name), n, std)
         else:
             data = normal_host(seed, name, n, std)
-        dt = _stored_dtype(cfg, kind, n)
         if dt == hf.DT_Q4_0:
             payload = np.frombuffer(quantize(data), dtype=np.uint8)
-            assert payload.size == hf.data_bytes(dt, n) or n % 32 != 0
         else:
             payload = np.ascontiguousarray(data, dtype=np.float32).view(np.uint8)
-        tensors.append((name, shape, dt, payload))
-    return hf.write_image(metadata(cfg), tensors)
+        assert payload.size == hf.data_bytes(dt, n)
+        img[offsets[name]: offsets[name] + payload.size] = payload
+        del data, payload
+    return img
 
 
-def _build_image_device(cfg, seed, std, device):
+def _device_payloads(cfg, seed, std, device):
+    """(layout, iterator of (offset, host uint8 array)): every tensor generated
+    and quantized on `device`, copied to one reused pinned host buffer."""
     import torch
 
     entries = []
@@ -146,24 +153,57 @@ def _build_image_device(cfg, seed, std, device):
         n = int(np.prod(shape))
         dt = _stored_dtype(cfg, kind, n)
         entries.append((name, tuple(shape), dt, hf.data_bytes(dt, n)))
-    img, offsets = hf.empty_image(metadata(cfg), entries)
-    stream = torch.cuda.current_stream(device)
-    maxn = max(int(np.prod(s)) for _, s, _, _ in entries)
-    fbuf = torch.empty(maxn, dtype=torch.float32, device=device)
-    qbuf = torch.empty(maxn // 32 * 18 + 64, dtype=torch.uint8, device=device)
-    for name, shape, dt, nbytes in entries:
-        n = int(np.prod(shape))
-        call("hc_synth_normal_dev", seed, fnv1a64(name), 0, n, float(std), fbuf.data_ptr(), stream.cuda_stream)
-        off = offsets[name]
-        if dt == hf.DT_Q4_0:
-            call("hc_q4_0_quantize_dev", fbuf.data_ptr(), n, qbuf.data_ptr(), stream.cuda_stream)
-            host = qbuf[:nbytes].cpu().numpy()
-        else:
-            host = fbuf[:n].cpu().numpy().view(np.uint8)
-        img[off: off + nbytes] = host
-    del fbuf, qbuf
-    torch.cuda.empty_cache()
+    lay = hf.layout(metadata(cfg), entries)
+    offsets = lay[1]
+
+    def gen():
+        stream = torch.cuda.current_stream(device)
+        maxn = max(int(np.prod(s)) for _, s, _, _ in entries)
+        maxb = max(b for _, _, _, b in entries)
+        fbuf = torch.empty(maxn, dtype=torch.float32, device=device)
+        qbuf = torch.empty(maxn // 32 * 18 + 64, dtype=torch.uint8, device=device)
+        host = torch.empty(maxb, dtype=torch.uint8).pin_memory()
+        try:
+            for name, shape, dt, nbytes in entries:
+                n = int(np.prod(shape))
+                call("hc_synth_normal_dev", seed, fnv1a64(name), 0, n, float(std), fbuf.data_ptr(), stream.cuda_stream)
+                if dt == hf.DT_Q4_0:
+                    call("hc_q4_0_quantize_dev", fbuf.data_ptr(), n, qbuf.data_ptr(), stream.cuda_stream)
+                    host[:nbytes].copy_(qbuf[:nbytes])
+                else:
+                    host[:nbytes].copy_(fbuf[:n].view(torch.uint8))
+                yield offsets[name], host[:nbytes].numpy()
+        finally:
+            del fbuf, qbuf
+            torch.cuda.empty_cache()
+
+    return lay, gen()
+
+
+def _build_image_device(cfg, seed, std, device):
+    (head, _, total, _), payloads = _device_payloads(cfg, seed, std, device)
+    img = np.zeros(total, dtype=np.uint8)
+    img[: len(head)] = np.frombuffer(head, dtype=np.uint8)
+    for off, data in payloads:
+        img[off: off + data.size] = data
     return img
+
+
+def write_image_file(cfg, path, seed=0, std=0.02, device=None):
+    """Streams the .hypno image of a synthetic model to `path`, one tensor at a
+    time (generated and quantized on the CUDA `device`), so models larger than
+    host memory (c5: 39 GB) are written without holding the image; the bytes
+    are those build_image returns."""
+    import torch
+    device = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+    (head, _, total, _), payloads = _device_payloads(cfg, seed, std, device)
+    with open(path, "wb") as f:
+        f.truncate(total)  # alignment gaps read as zeros
+        f.write(head)
+        for off, data in payloads:
+            f.seek(off)
+            f.write(memoryview(data))
+    return path
 
 
 def prompt_ids(vocab, T, seed=0):

@@ -215,11 +215,11 @@ const char* hc_phase_name(int i);
  * device: per-row temperature (exp(l / T) when T > 0, raw logits otherwise),
  * top_k (0 = off) and top_p (1 = off) as device arrays of B, and a device
  * array of B XorShift64 states (the caller seeds state = max(seed, 1)); a row
- * that draws advances its state by one step.  The top-k and top-p thresholds
- * are exact values of the row; sums are accumulated in f64 where the
- * reference adds f32 terms in order, so a draw within that rounding of a
- * boundary may pick the neighbouring token.  Stream-ordered, no
- * synchronization. */
+ * that draws advances its state by one step.  Every sum is added in f32 in
+ * the reference's order, one term at a time (about one add latency per logit
+ * and pass: a few hundred microseconds per row at V = 128256); exp is CUDA's
+ * expf, so only a draw within a few ulp of a boundary can differ from the
+ * reference.  Stream-ordered, no synchronization. */
 int hc_sample_dev(const float* logits_dev, size_t ld, int B, int V, const float* temperature_dev,
                   const float* top_p_dev, const int* top_k_dev, uint64_t* rng_state_dev, uint32_t* out_dev,
                   void* stream);

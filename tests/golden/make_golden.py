@@ -1,7 +1,8 @@
 """Generates the golden fixtures in tests/golden/ from the CPU oracle.
 
     python tests/golden/make_golden.py [--skip-c3]
-    python tests/golden/make_golden.py --c4      (BASELINE configs[3] at full size; ~30 min on 8 cores)
+    python tests/golden/make_golden.py --c4      (BASELINE configs[3] at full size; ~40 min on 8 cores)
+    python tests/golden/make_golden.py --c5      (BASELINE configs[4] at full size; ~45 GB of host memory)
 
 The reference (Rust) cannot be built in this image and ships no golden
 vectors, so the fixtures come from the oracle (oracle/hypno_oracle.c, pinned
@@ -15,6 +16,9 @@ each sweep weight tensor.  GPU tests compare the backend against these.
 The c4 fixture is the full Llama-3-8B-shaped model (32 layers, hidden 4096):
 sequence 0's 2048-token prompt, then the prefill logits and 32 greedy steps,
 with the reference's FP32 KV cache (the oracle's faithful per-token path).
+The c5 fixture is the full Llama-3.1-70B-shaped model (80 layers, hidden
+8192, 39 GB): a 32-token prompt (seed 0), then the prefill logits and 32
+greedy steps; the bench's 4096-token prompts would take the oracle hours.
 """
 import argparse
 import hashlib
@@ -86,11 +90,30 @@ def c4_fixture():
     return model_fixture("configs[3] (c4), sequence 0", img, synth.prompt_ids(cfg["vocab"], cfg["prompt"], seed=0), 33)
 
 
+C5_PROMPT = 32
+
+
+def c5_fixture():
+    cfg = synth.CONFIGS["c5"]
+    orc.use_all_cores()
+    img = synth.build_image(cfg, seed=0, quantize=orc.quantize_f32_to_q4_0,
+                            normal=lambda sd, st, n, std: orc.synth_normal(sd, st, n, std))
+    return model_fixture(f"configs[4] (c5), a {C5_PROMPT}-token prompt", img,
+                         synth.prompt_ids(cfg["vocab"], C5_PROMPT, seed=0), 33)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--skip-c3", action="store_true")
     ap.add_argument("--c4", action="store_true", help="only the full-size configs[3] fixture")
+    ap.add_argument("--c5", action="store_true", help="only the full-size configs[4] fixture")
     args = ap.parse_args()
+    if args.c5:
+        v = c5_fixture()
+        with open(os.path.join(HERE, "c5.json"), "w") as f:
+            json.dump(v, f)
+        print("c5 greedy =", v["greedy"], "oracle s =", v["oracle_seconds"])
+        return
     if args.c4:
         v = c4_fixture()
         with open(os.path.join(HERE, "c4.json"), "w") as f:

@@ -20,6 +20,11 @@ def test_workload_config_layouts():
     assert tp["parallelism"] == "tp4" and tp["global_batch"] == 32  # strong scaling: same 32 sequences
     dp = bench.workload_config(4, "dp")
     assert dp["parallelism"] == "replicas4" and dp["global_batch"] == 128  # one c4 job per rank
+    c5 = bench.workload_config(8, "tp", "c5")
+    assert c5["parallelism"] == "tp8" and c5["global_batch"] == 8 and c5["seq_len"] == 4096
+    assert "hidden 8192, 80 layers" in c5["workload"] and "70B" in bench.metric_name("c5")
+    c1 = bench.workload_config(1, "tp", "c1")
+    assert c1["global_batch"] == 1 and "fit in L2" in c1["l2"]
 
 
 def test_clock_summary_keeps_timed_samples_only():
@@ -72,7 +77,7 @@ def test_reference_arm_inputs_without_gpu_library():
     x = orc.synth_normal(5, synth.fnv1a64("w"), 4096, 0.02, offset=77)
     assert np.array_equal(x, synth.normal_host(5, "w", 4096, 0.02, offset=77))
     code = ("import sys, types; sys.argv = ['bench.py']; sys.path.insert(0, %r); import bench; "
-            "bench.run_reference(types.SimpleNamespace(warmup=3, steps=1, layers=1)); "
+            "bench.run_reference(types.SimpleNamespace(warmup=3, steps=1, layers=1, config='c4')); "
             "print('GPULIB', 'libhypno_cuda' in open('/proc/self/maps').read())" % ROOT)
     r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=600,
                        env=dict(os.environ, OMP_NUM_THREADS="1"))

@@ -93,3 +93,35 @@ def test_sweep_pack_sha(cuda_device, nk):
     call("hc_q4_0_quantize_dev", w.data_ptr(), N * K, q.data_ptr(), None)
     torch.cuda.synchronize()
     assert hashlib.sha256(q.cpu().numpy().tobytes()).hexdigest() == load("sweep_pack.json")["tensors"][nk]["sha256"]
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(not os.path.exists(os.path.join(HERE, "c4.json")), reason="c4 fixture not generated")
+def test_backend_matches_golden_c4(cuda_device):
+    """BASELINE configs[3] at full size (Llama-3-8B shape, 32 layers): the
+    device-built image hashes to the oracle's, and sequence 0's 2048-token
+    prefill plus 32 greedy steps through an FP32 KV cache give the oracle's
+    greedy ids, logits within tolerance on the recorded samples."""
+    g = load("c4.json")
+    cfg = synth.CONFIGS["c4"]
+    img = synth.build_image(cfg, seed=0, device=cuda_device)
+    assert hashlib.sha256(img.tobytes()).hexdigest() == g["image_sha256"]
+    m = engine.HypnoModel(img)
+    del img
+    kv = engine.KVCache(m, n_seqs=1, max_pos=cfg["max_pos"], kv_dtype=engine.KV_FP32)
+    logits = engine.batch_forward(m, np.array(g["prompt"], np.uint32), kv)
+    worst, mism = 0.0, []
+    for st in range(g["steps"]):
+        rec = g["records"][st]
+        worst = max(worst, check_record(logits, rec, g["stride"]))
+        tok = orc.greedy(logits)
+        if tok != g["greedy"][st]:
+            mism.append((st, tok, g["greedy"][st], rec["margin"]))
+            tok = g["greedy"][st]
+        if st + 1 < g["steps"]:
+            lg, _ = engine.decode_step(m, kv, [0], [tok])
+            logits = lg[0]
+    kv.close()
+    m.close()
+    print(f"c4: max sampled-logit rel err {worst:.2e}, greedy mismatches {mism}")
+    assert not mism, mism

@@ -186,6 +186,23 @@ def test_synth_device_equals_host(cuda_device):
     assert np.array_equal(buf.cpu().numpy().view(np.uint32), host.view(np.uint32))
 
 
+def test_streamed_image_file_equals_host_image(cuda_device, tmp_path):
+    """synth.write_image_file (the c5 writer: one tensor at a time, generated
+    and quantized on the device) writes the bytes of the host-built image, and
+    a model opened from the file (memory-mapped) loads."""
+    from hypno_b200 import engine
+    cfg = dict(hidden=256, inter=512, heads=4, kv_heads=2, layers=2, vocab=512, theta=10000.0, max_pos=64,
+               embed="q4", lm_head="tied")
+    path = str(tmp_path / "m.hypno")
+    synth.write_image_file(cfg, path, seed=7, device=cuda_device)
+    want = synth.build_image(cfg, seed=7)
+    got = np.fromfile(path, dtype=np.uint8)
+    assert got.size == want.size and np.array_equal(got, want)
+    m = engine.HypnoModel.open(path)
+    assert m.config.num_hidden_layers == 2
+    m.close()
+
+
 # ---- configs[1]: the Q4_0 operator sweep ---------------------------------
 @pytest.mark.parametrize("N,K", synth.SWEEP_NK)
 def test_sweep_pack_and_matmul(cuda_device, N, K):

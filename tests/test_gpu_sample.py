@@ -1,11 +1,11 @@
 """On-device sampling (hc_sample_dev) against the oracle's restatement of
 sample_token and XorShift64 (run.rs:203-278) on identical logits: for every
 row and draw the device picks the oracle's token and advances the RNG state
-the same way.  The device accumulates its sums in f64 where the reference adds
-f32 terms one by one, and its exp is CUDA's expf, so a draw that lands within
-that rounding of a token boundary may pick the neighbour: at most a handful
-of such draws are allowed, and only with the draw within 1e-4 of the
-boundary between the two picks."""
+the same way.  The device adds its f32 sums in the reference's order, one term
+at a time, so the only difference left is its exp (CUDA's expf, within 2 ulp
+of the C library's): a draw that lands within that rounding of a token
+boundary may pick the neighbour, so at most a handful of such draws are
+allowed, each within 1e-5 of the boundary between the two picks."""
 import numpy as np
 import pytest
 
@@ -23,13 +23,13 @@ CASES = [  # temperature, top_p, top_k
     (0.0, 1.0, 0),    # raw logits as weights; a non-positive sum falls back to the last maximal logit
     (0.6, 1.0, 1),
     (1.0, 0.99, 0),
+    (1.0, 0.999999, 0),  # the running f32 sum may never exceed top_p: every weight cleared, greedy
+    (0.0, 0.9, 0),       # raw logits (some negative) as weights under top-p
+    (0.0, 0.8, 50),
 ]
-# top_p within f32 rounding of 1 is left out on purpose: there the reference's
-# running f32 sum may end just below top_p, clear every weight and fall back to
-# the greedy pick without drawing, where the device's f64 sum crosses top_p.
 
 
-@pytest.mark.parametrize("V", [4096, 128256])
+@pytest.mark.parametrize("V", [1000, 4096, 128256])
 def test_device_sampler_matches_oracle(cuda_device, V):
     import torch
     from hypno_b200._lib import call
@@ -37,6 +37,7 @@ def test_device_sampler_matches_oracle(cuda_device, V):
     g = np.random.default_rng(V)
     logits = (g.standard_normal((B, V)) * 3.0).astype(np.float32)
     logits[1] -= 20.0  # a row whose raw logits sum below zero
+    logits[3] = np.round(logits[3])  # many tied values (top-k / top-p thresholds on ties)
     ld = torch.from_numpy(logits).to(cuda_device)
     out = torch.zeros(B, dtype=torch.int32, device=cuda_device)
     loose = []
@@ -61,5 +62,5 @@ def test_device_sampler_matches_oracle(cuda_device, V):
                     margin = boundary_margin(logits[b], T, tp, tk, before[b], int(got[b]), want[b])
                     loose.append((T, tp, tk, d, b, int(got[b]), want[b], margin))
     print(f"V={V}: {len(CASES) * D * B} draws, boundary picks {loose}")
-    assert all(m[-1] < 1e-4 for m in loose), loose
+    assert all(m[-1] < 1e-5 for m in loose), loose
     assert len(loose) <= 3, loose
