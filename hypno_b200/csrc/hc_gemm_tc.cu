@@ -30,9 +30,8 @@
 // deadline; on expiry the kernel records an error flag, skips its stores, and
 // still frees its tensor memory before returning.
 #include "hc_gemm.h"
-#include "hc_common.cuh"
+#include "hc_tc.cuh"
 
-#include <cuda.h>
 #include <cudaTypedefs.h>
 
 #include <mutex>
@@ -45,70 +44,11 @@ namespace {
 
 constexpr int BM = 128;      // weight rows per tile (MMA M)
 constexpr int BK = 128;      // K per pipeline stage
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
-        "[%2];" ::"r"(smem_u32(dst)),
-        "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y)
-        : "memory");
-}
-
-__device__ __forceinline__ void tmem_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tmem_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ void tmem_ld_x16(uint32_t taddr, uint32_t* v) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-        "%15}, [%16];"
-        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
-          "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
-        : "r"(taddr)
-        : "memory");
-}
-
-// Shared-memory matrix descriptor of a K-major tile in the 128-byte swizzle
-// canonical layout: rows of 128 bytes, 8-row (1024-byte) atoms.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-    uint64_t d = 0;
-    d |= (uint64_t)((saddr >> 4) & 0x3FFF);         // start address
-    d |= (uint64_t)1 << 16;                          // leading byte offset (unused for swizzled K-major)
-    d |= (uint64_t)(1024 >> 4) << 32;                // stride byte offset: 8 rows x 128 B
-    d |= (uint64_t)1 << 46;                          // descriptor version (sm_100)
-    d |= (uint64_t)2 << 61;                          // layout: 128-byte swizzle
-    return d;
-}
-
 // Instruction descriptor: f16 x f16 -> f32, A and B K-major, M = 128, N = tn.
-__host__ __device__ constexpr uint32_t make_idesc(int tn) {
-    return (1u << 4)                       // D format f32
-           | (0u << 7) | (0u << 10)        // A, B format f16
-           | (0u << 15) | (0u << 16)       // A, B K-major
-           | ((uint32_t)(tn >> 3) << 17)   // N / 8
-           | ((uint32_t)(BM >> 4) << 24);  // M / 16
-}
-
-__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
-                                           uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-                 : "memory");
-}
+__host__ __device__ constexpr uint32_t make_idesc(int tn) { return make_idesc_mn(BM, tn); }
 
 constexpr int EPI_CH = 16;     // tokens per epilogue chunk (one tcgen05.ld x16)
 constexpr int MAX_SPLITS = 8;  // split-K cluster size limit (portable cluster size)
-
-// Programmatic dependent launch: wait until the grids this one depends on
-// have completed and their writes are visible (returns at once when the
-// kernel was launched without the attribute).
-__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 __device__ __forceinline__ void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
@@ -191,28 +131,6 @@ __device__ __forceinline__ void deq_word_split(uint32_t w, __half2 shi2, __half2
         hi_out[k] = *reinterpret_cast<uint32_t*>(&a);
         lo_out[k] = *reinterpret_cast<uint32_t*>(&b);
     }
-}
-
-__device__ __forceinline__ void tmem_st_x16(uint32_t taddr, const uint32_t* v) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-        "%15, %16};" ::"r"(taddr),
-        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
-        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
-        : "memory");
-}
-
-// Warp-uniform bounded wait: lane 0 polls (its try_wait acquires the data
-// the barrier guards), the verdict is broadcast, and __syncwarp orders the
-// other lanes' accesses after lane 0's.  Only one lane touches the barrier:
-// every mbarrier operation costs ~100+ cycles when many warps use them, and
-// a 32-lane re-test per wait multiplied that traffic by 32.
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
-    bool ok = true;
-    if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort_flag);
-    ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-    __syncwarp();
-    return ok;
 }
 
 // Pipeline shapes.  Every tile is 128 weight rows x TN tokens (TN = 32, 64
@@ -323,14 +241,6 @@ __device__ __forceinline__ void load_accumulators(uint32_t tmem, int q, int c0, 
         for (int jj = 0; jj < EPI_CH; jj++)
             v[jj] = __float_as_uint(__uint_as_float(v[jj]) + (__uint_as_float(a[jj]) + __uint_as_float(b[jj])));
     }
-}
-
-// One lane of a converged warp (the MMA issue happens under it, so the
-// warp's loop, waits and descriptor arithmetic stay uniform).
-__device__ __forceinline__ bool elect_one() {
-    uint32_t pred = 0;
-    asm volatile("{\n\t.reg .pred px;\n\telect.sync _|px, 0xffffffff;\n\t@px mov.u32 %0, 1;\n\t}" : "+r"(pred));
-    return pred != 0;
 }
 
 template <int TN>
@@ -707,7 +617,9 @@ __global__ void k_rows_to_f16_perm(const float* __restrict__ x, size_t ldx, __ha
     }
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+}  // namespace
+
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
     static std::once_flag once;
     std::call_once(once, [] {
@@ -745,7 +657,6 @@ int encode_weight_maps(const hc_q4_matrix& w, CUtensorMap* wmap, CUtensorMap* sm
     return HC_OK;
 }
 
-}  // namespace
 
 struct GemmWorkspace {
     std::mutex mu;
@@ -951,10 +862,10 @@ int gemm_tc_impl(GemmWorkspace* ws, const hc_q4_matrix& w, const float* x, size_
         HC_TRY(encode_weight_maps(w, &wmap, &smap));
         if (w.owns) ws->wmaps[key] = std::make_pair(wmap, smap);
     }
-    size_t tiles = ((w.n + BM - 1) / BM) * ((T + tn - 1) / tn);
-    const size_t nk = K / BK;
     int nsm = 148;
     HC_CUDA(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
+    size_t tiles = ((w.n + BM - 1) / BM) * ((T + tn - 1) / tn);
+    const size_t nk = K / BK;
     const size_t stride = max_part > 0 ? T * ldy : 0;  // slab stride in partial mode
     const bool one = epi == EPI_SILU;                  // the SiLU epilogue needs whole sums
     int splits = 1;
