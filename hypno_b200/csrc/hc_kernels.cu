@@ -571,6 +571,8 @@ int launch_rmsnorm(const float* x, size_t ldx, const float* w, float* out, size_
 // proj[i]`, transformer.rs:561-563, 595-598), then, when w is given,
 // xn[row] = RMSNorm(hidden[row]) * w and its fp16 copy in GEMM K order
 // (rms_norm_fused, kernels.rs:592-625).  One CTA per row.
+constexpr int RSN_MAX_SPLITS = 8;  // most slabs a projection writes (the model's kPartSplits)
+
 template <int VPT>
 __global__ void k_residual_splits_norm(const float* __restrict__ part, int splits, size_t slab, float* hidden,
                                        size_t ldh, const float* __restrict__ w, float* __restrict__ xn, size_t ldxn,
@@ -587,15 +589,23 @@ __global__ void k_residual_splits_norm(const float* __restrict__ part, int split
     for (int j = 0; j < VPT; j++) {
         const int i = threadIdx.x + j * blockDim.x;
         if (i < n4) {
-            float4 acc = prow[i];
-            for (int sp = 1; sp < splits; sp++) {
-                const float4 q = prow[(size_t)sp * (slab / 4) + i];
-                acc.x = acc.x + q.x;
-                acc.y = acc.y + q.y;
-                acc.z = acc.z + q.z;
-                acc.w = acc.w + q.w;
-            }
+            // every slab and the residual are loaded before the first add
+            // (one memory round trip); the sum keeps slab order
+            float4 q[RSN_MAX_SPLITS];
+#pragma unroll
+            for (int sp = 0; sp < RSN_MAX_SPLITS; sp++)
+                if (sp < splits) q[sp] = prow[(size_t)sp * (slab / 4) + i];
             float4 r = hrow[i];
+            float4 acc = q[0];
+#pragma unroll
+            for (int sp = 1; sp < RSN_MAX_SPLITS; sp++) {
+                if (sp < splits) {
+                    acc.x = acc.x + q[sp].x;
+                    acc.y = acc.y + q[sp].y;
+                    acc.z = acc.z + q[sp].z;
+                    acc.w = acc.w + q[sp].w;
+                }
+            }
             r.x = acc.x + r.x;
             r.y = acc.y + r.y;
             r.z = acc.z + r.z;
@@ -611,16 +621,22 @@ __global__ void k_residual_splits_norm(const float* __restrict__ part, int split
         ss = fmaf(v[j].w, v[j].w, ss);
     }
     if (!w) return;  // uniform over the grid
+    const float4* wr = reinterpret_cast<const float4*>(w);
+    float4 wv[VPT];  // the norm weights travel while the block reduces
+#pragma unroll
+    for (int j = 0; j < VPT; j++) {
+        const int i = threadIdx.x + j * blockDim.x;
+        wv[j] = i < n4 ? wr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     ss = block_sum(ss, red);
     const float ms = __fdiv_rn(ss, (float)n);
     const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
-    const float4* wr = reinterpret_cast<const float4*>(w);
     float4* orow = reinterpret_cast<float4*>(xn + row * ldxn);
 #pragma unroll
     for (int j = 0; j < VPT; j++) {
         const int i = threadIdx.x + j * blockDim.x;
         if (i < n4) {
-            float4 ww = wr[i], o;
+            float4 ww = wv[j], o;
             o.x = __fmul_rn(__fmul_rn(v[j].x, inv), ww.x);
             o.y = __fmul_rn(__fmul_rn(v[j].y, inv), ww.y);
             o.z = __fmul_rn(__fmul_rn(v[j].z, inv), ww.z);
@@ -644,7 +660,7 @@ bool residual_splits_norm_ok(size_t n, size_t ldh, size_t ldxn) {
 int launch_residual_splits_norm(const float* part, int splits, size_t rows, size_t n, float* hidden, size_t ldh,
                                 const float* w, float eps, float* xn, size_t ldxn, __half* xn16, cudaStream_t s) {
     if (rows == 0) return HC_OK;
-    HC_CHECK(splits >= 1 && residual_splits_norm_ok(n, ldh, ldxn) && ((uintptr_t)part & 15) == 0 &&
+    HC_CHECK(splits >= 1 && splits <= RSN_MAX_SPLITS && residual_splits_norm_ok(n, ldh, ldxn) && ((uintptr_t)part & 15) == 0 &&
                  ((uintptr_t)hidden & 15) == 0 && (!w || ((uintptr_t)w & 15) == 0) && (!w || ((uintptr_t)xn & 15) == 0),
              HC_ERR_INVALID, "residual_splits_norm: unsupported layout (n %zu)", n);
     const size_t n4 = n / 4;
@@ -786,11 +802,19 @@ __global__ void k_rope_rows_slabs(const float* __restrict__ part, int splits, si
     const float2* pr = reinterpret_cast<const float2*>(part + (size_t)row * width);
     float2* xr = reinterpret_cast<float2*>(x + (size_t)row * ldx);
     for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < width / 2; p += gridDim.x * blockDim.x) {
-        float2 v = pr[p];
-        for (int sp = 1; sp < splits; sp++) {
-            const float2 q = pr[(size_t)sp * (slab / 2) + p];
-            v.x = v.x + q.x;
-            v.y = v.y + q.y;
+        // every slab is loaded before the first add (one memory round trip);
+        // the sum keeps slab order
+        float2 q[RSN_MAX_SPLITS];
+#pragma unroll
+        for (int sp = 0; sp < RSN_MAX_SPLITS; sp++)
+            if (sp < splits) q[sp] = pr[(size_t)sp * (slab / 2) + p];
+        float2 v = q[0];
+#pragma unroll
+        for (int sp = 1; sp < RSN_MAX_SPLITS; sp++) {
+            if (sp < splits) {
+                v.x = v.x + q[sp].x;
+                v.y = v.y + q[sp].y;
+            }
         }
         const int h = p / half, i = p % half;
         if (h < heads && rot_ok) {
@@ -822,7 +846,7 @@ int launch_rope_rows_slabs(const float* part, int splits, float* x, size_t ldx, 
                            size_t heads, size_t hd, const float2* cs, size_t cs_rows, const int* pos_dev, int pos0,
                            cudaStream_t s, const KvStoreArgs* kv) {
     if (rows == 0) return HC_OK;
-    HC_CHECK(splits >= 1 && width % 2 == 0 && hd % 2 == 0 && ldx % 2 == 0 && heads * hd <= width &&
+    HC_CHECK(splits >= 1 && splits <= RSN_MAX_SPLITS && width % 2 == 0 && hd % 2 == 0 && ldx % 2 == 0 && heads * hd <= width &&
                  ((uintptr_t)part & 7) == 0 && ((uintptr_t)x & 7) == 0,
              HC_ERR_INVALID, "rope_rows_slabs: unsupported layout");
     KvStoreArgs k{};
