@@ -652,7 +652,7 @@ def run_ours(args):
     roof = roofline_gemv(dev, M=S, N=rows_l, K=cfg["hidden"]) if rank == 0 else None
     sweep = q4_sweep(dev) if rank == 0 and not args.no_sweep and name == "c4" else None
     cpu = None
-    if rank == 0 and not args.no_cpu:
+    if rank == 0 and world == 1 and not args.no_cpu:  # the CPU baseline is taken at N = 1 only
         cpu = cpu_baseline(img, cfg, name=name)
     if dist:
         dist.barrier()

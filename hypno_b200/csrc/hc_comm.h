@@ -26,8 +26,11 @@ float* peer_ar_partial(PeerAr* a, int slot);
 bool peer_ar_fits(const PeerAr* a, size_t rows, size_t H);
 // hidden[r] += sum over ranks of partial[r] of the slot (rank order); then,
 // when w is not null, xn[r] = RMSNorm(hidden[r]) * w and its fp16 copy in
-// GEMM K order.
-int peer_ar_residual_norm(PeerAr* a, int slot, int rank, int size, size_t rows, float* hidden, size_t ldh,
-                          const float* w, float eps, float* xn, size_t ldxn, __half* xn16, int* err, cudaStream_t s);
+// GEMM K order.  slabs (may be null): this rank's product as `splits`
+// split-K slabs of [rows][H] (local memory), added in slab order into the
+// slot's partial first; null: the partial already holds the product.
+int peer_ar_residual_norm(PeerAr* a, int slot, int rank, int size, size_t rows, const float* slabs, int splits,
+                          float* hidden, size_t ldh, const float* w, float eps, float* xn, size_t ldxn, __half* xn16,
+                          int* err, cudaStream_t s);
 
 }  // namespace hc

@@ -669,12 +669,21 @@ int row_parallel(hc_model* m, const DevWeight& w, const float* x, size_t ldx, si
     if (m->par && hc::peer_ar_fits(m->par, rows, H)) {
         // o_proj and down_proj alternate, each with its own partial buffer
         const int slot = gemm_phase == PH_DOWN ? 1 : 0;
-        float* part = hc::peer_ar_partial(m->par, slot);
-        HC_TRY(matmul(m, w, x, ldx, rows, part, H, hc::EPI_STORE, nullptr, 0, x16));
+        const float* slabs = nullptr;
+        int splits = 0;
+        if (s.split_part && rows <= kPartRows && w.dtype == HC_DTYPE_Q4_0 && hc::gemm_tc_eligible(w.q4, rows)) {
+            // split-K slabs in local memory (as on one GPU); the all-reduce
+            // kernel adds them into the peer-visible partial
+            HC_TRY(hc::gemm_tc_partials(m->gemm_ws, w.q4, x, ldx, rows, s.split_part, kPartSplits, &splits, m->stream,
+                                        x16));
+            slabs = s.split_part;
+        } else {
+            HC_TRY(matmul(m, w, x, ldx, rows, hc::peer_ar_partial(m->par, slot), H, hc::EPI_STORE, nullptr, 0, x16));
+        }
         HC_TRY(phase(m, PH_REDUCE));
-        HC_TRY(hc::peer_ar_residual_norm(m->par, slot, m->cfg.tp_rank, m->cfg.tp_size, rows, s.hidden, H, next_norm,
-                                         m->cfg.rms_norm_eps, s.xn, H, s.xn16, hc::gemm_error_flag(m->gemm_ws),
-                                         m->stream));
+        HC_TRY(hc::peer_ar_residual_norm(m->par, slot, m->cfg.tp_rank, m->cfg.tp_size, rows, slabs, splits, s.hidden,
+                                         H, next_norm, m->cfg.rms_norm_eps, s.xn, H, s.xn16,
+                                         hc::gemm_error_flag(m->gemm_ws), m->stream));
         if (normed) *normed = next_norm != nullptr;
         return HC_OK;
     }

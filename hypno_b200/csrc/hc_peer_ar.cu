@@ -14,6 +14,9 @@
 //      rank, so the replicated residual stream stays identical), adds the
 //      residual, writes it back, and computes the RMSNorm of the new row
 //      (kernels.rs:592-625 arithmetic) plus its fp16 copy in GEMM K order,
+// When the projection wrote split-K slabs (local memory), each CTA first adds
+// its row's slabs in slab order into this rank's peer-visible partial row and
+// fences before the handshake.
 // Each rank has two partial buffers, one for o_proj and one for down_proj,
 // which alternate.  A peer that says its partial for one of them is complete
 // has finished reading this rank's other buffer (its previous all-reduce
@@ -38,8 +41,14 @@ namespace {
 constexpr int AR_MAX_RANKS = 8;
 constexpr long long AR_WAIT_CYCLES = 2000000000LL;  // ~1 s at 1.9 GHz
 
+constexpr int AR_MAX_SLABS = 8;  // split-K slabs of the local product (the model's kPartSplits)
+
 struct ArParams {
     const float* partial[AR_MAX_RANKS];  // rank-ordered partial buffers ([rows][H] each)
+    float* partial_mine;                 // this rank's, written here when slabs are given
+    const float* slabs;                  // this rank's split-K slabs (slab i at slabs + i * slab), or null
+    int splits;
+    size_t slab;
     uint32_t* ready_peer[AR_MAX_RANKS];  // rank p's ready flags ([row][AR_MAX_RANKS])
     uint32_t* ready_mine;
     uint32_t* epochs;  // [row] this rank's completed epochs
@@ -86,6 +95,35 @@ __global__ void __launch_bounds__(1024) k_ar_residual_norm(ArParams P) {
     const int row = blockIdx.x;
     const int n4 = P.H / 4;
     const uint32_t e = P.epochs[row] + 1;  // read by thread 0 alone below, after every thread read it here
+    // This rank's partial row: the sum of its split-K slabs (slab order),
+    // published in its peer-visible buffer before the handshake.
+    float4 mine[VPT];
+    if (P.slabs) {
+        float4* prow = reinterpret_cast<float4*>(P.partial_mine + (size_t)row * P.H);
+        const float4* srow = reinterpret_cast<const float4*>(P.slabs + (size_t)row * P.H);
+#pragma unroll
+        for (int j = 0; j < VPT; j++) {
+            const int i = threadIdx.x + j * blockDim.x;
+            if (i < n4) {
+                float4 q[AR_MAX_SLABS];
+#pragma unroll
+                for (int sp = 0; sp < AR_MAX_SLABS; sp++)
+                    if (sp < P.splits) q[sp] = srow[(size_t)sp * (P.slab / 4) + i];
+                float4 acc = q[0];
+#pragma unroll
+                for (int sp = 1; sp < AR_MAX_SLABS; sp++) {
+                    if (sp < P.splits) {
+                        acc.x = acc.x + q[sp].x; acc.y = acc.y + q[sp].y; acc.z = acc.z + q[sp].z; acc.w = acc.w + q[sp].w;
+                    }
+                }
+                prow[i] = acc;
+                mine[j] = acc;
+            }
+        }
+    }
+    // every thread's stores happen before thread 0's system-scope fence and
+    // release stores in handshake() (ordered by this barrier)
+    __syncthreads();
     if (threadIdx.x == 0) ok_s = handshake(P.ready_peer, P.ready_mine, row, P.rank, P.size, e) ? 1 : 0;
     __syncthreads();
     const bool ok = ok_s != 0;
@@ -97,12 +135,27 @@ __global__ void __launch_bounds__(1024) k_ar_residual_norm(ArParams P) {
         for (int j = 0; j < VPT; j++) {
             const int i = threadIdx.x + j * blockDim.x;
             if (i < n4) {
-                float4 acc = __ldcg(reinterpret_cast<const float4*>(P.partial[0] + (size_t)row * P.H) + i);
-                for (int p = 1; p < P.size; p++) {
-                    float4 q = __ldcg(reinterpret_cast<const float4*>(P.partial[p] + (size_t)row * P.H) + i);
-                    acc.x += q.x; acc.y += q.y; acc.z += q.z; acc.w += q.w;
+                // every peer's partial (loads over NVLink) and the residual
+                // are requested before the first add: one round trip instead
+                // of one per rank; the sum keeps rank order
+                float4 q[AR_MAX_RANKS];
+#pragma unroll
+                for (int p = 0; p < AR_MAX_RANKS; p++)
+                    if (p < P.size && !(P.slabs && p == P.rank))
+                        q[p] = __ldcg(reinterpret_cast<const float4*>(P.partial[p] + (size_t)row * P.H) + i);
+                if (P.slabs) {
+#pragma unroll
+                    for (int p = 0; p < AR_MAX_RANKS; p++)
+                        if (p == P.rank) q[p] = mine[j];
                 }
                 float4 r = hrow[i];
+                float4 acc = q[0];
+#pragma unroll
+                for (int p = 1; p < AR_MAX_RANKS; p++) {
+                    if (p < P.size) {
+                        acc.x += q[p].x; acc.y += q[p].y; acc.z += q[p].z; acc.w += q[p].w;
+                    }
+                }
                 r.x = r.x + acc.x; r.y = r.y + acc.y; r.z = r.z + acc.z; r.w = r.w + acc.w;
                 hrow[i] = r;
                 v[j] = r;
@@ -116,18 +169,24 @@ __global__ void __launch_bounds__(1024) k_ar_residual_norm(ArParams P) {
         }
     }
     if (P.w) {  // uniform over the grid
+        const float4* wr = reinterpret_cast<const float4*>(P.w);
+        float4 wv[VPT];  // the norm weights travel while the block reduces
+#pragma unroll
+        for (int j = 0; j < VPT; j++) {
+            const int i = threadIdx.x + j * blockDim.x;
+            wv[j] = i < n4 ? wr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
         ss = block_sum(ss, red);
         const float ms = __fdiv_rn(ss, (float)P.H);
         const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, P.eps)));
         if (ok) {
-            const float4* wr = reinterpret_cast<const float4*>(P.w);
             float4* orow = reinterpret_cast<float4*>(P.xn + (size_t)row * P.ldxn);
             __half* r16 = P.xn16 ? P.xn16 + (size_t)row * 2 * P.H : nullptr;
 #pragma unroll
             for (int j = 0; j < VPT; j++) {
                 const int i = threadIdx.x + j * blockDim.x;
                 if (i < n4) {
-                    float4 ww = wr[i], o;
+                    float4 ww = wv[j], o;
                     o.x = __fmul_rn(__fmul_rn(v[j].x, inv), ww.x);
                     o.y = __fmul_rn(__fmul_rn(v[j].y, inv), ww.y);
                     o.z = __fmul_rn(__fmul_rn(v[j].z, inv), ww.z);
@@ -240,9 +299,12 @@ float* peer_ar_partial(PeerAr* a, int slot) {
 
 bool peer_ar_fits(const PeerAr* a, size_t rows, size_t H) { return a && rows >= 1 && rows <= a->rows_cap && H == a->H; }
 
-int peer_ar_residual_norm(PeerAr* a, int slot, int rank, int size, size_t rows, float* hidden, size_t ldh,
-                          const float* w, float eps, float* xn, size_t ldxn, __half* xn16, int* err, cudaStream_t s) {
+int peer_ar_residual_norm(PeerAr* a, int slot, int rank, int size, size_t rows, const float* slabs, int splits,
+                          float* hidden, size_t ldh, const float* w, float eps, float* xn, size_t ldxn, __half* xn16,
+                          int* err, cudaStream_t s) {
     HC_CHECK(peer_ar_fits(a, rows, a ? a->H : 0), HC_ERR_INVALID, "peer all-reduce: %zu rows do not fit", rows);
+    HC_CHECK(!slabs || (splits >= 1 && splits <= AR_MAX_SLABS && ((uintptr_t)slabs & 15) == 0), HC_ERR_INVALID,
+             "peer all-reduce: %d split-K slabs", splits);
     HC_CHECK((ldh % 4) == 0 && (ldxn % 4) == 0 && ((uintptr_t)hidden & 15) == 0 && ((uintptr_t)xn & 15) == 0 &&
                  (!w || ((uintptr_t)w & 15) == 0),
              HC_ERR_INVALID, "peer all-reduce: rows must be 16-byte aligned");
@@ -252,6 +314,10 @@ int peer_ar_residual_norm(PeerAr* a, int slot, int rank, int size, size_t rows, 
         P.ready_peer[p] = reinterpret_cast<uint32_t*>(a->peer[p] + a->ready_off);
     }
     P.ready_mine = reinterpret_cast<uint32_t*>(a->base + a->ready_off);
+    P.partial_mine = reinterpret_cast<float*>(a->base + a->partial_off[slot & 1]);
+    P.slabs = slabs;
+    P.splits = slabs ? splits : 0;
+    P.slab = rows * a->H;
     P.epochs = reinterpret_cast<uint32_t*>(a->base + a->epoch_off);
     P.rank = rank;
     P.size = size;
