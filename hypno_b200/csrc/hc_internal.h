@@ -103,9 +103,10 @@ int launch_rmsnorm(const float* x, size_t ldx, const float* w, float* out, size_
 int launch_softmax_rows(float* x, size_t rows, size_t n, cudaStream_t s);
 int launch_silu(float* x, size_t n, cudaStream_t s);
 // act[r][i] = silu(gu[r][i]) * gu[r][im + i] (blocked: gate/up alternate in
-// blocks of GU_BLOCK columns)
+// blocks of GU_BLOCK columns); splits > 1: gu holds that many split-K slabs of
+// [rows][ldgu] (slab i at gu + i * rows * ldgu), added in slab order first
 int launch_silu_mul(const float* gu, size_t ldgu, float* act, size_t ldact, size_t rows, size_t im,
-                    cudaStream_t s, __half* act16 = nullptr, bool blocked = false);
+                    cudaStream_t s, __half* act16 = nullptr, bool blocked = false, int splits = 1);
 // x[row] = sum of the split slabs part[i][row] (slab order; slab i at part +
 // i * rows * width, `width` elements per row), the first `heads` heads then
 // rotated as launch_rope_rows does.

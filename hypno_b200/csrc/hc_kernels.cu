@@ -722,26 +722,46 @@ int launch_silu(float* x, size_t n, cudaStream_t s) {
 // `blocked`, gate and up rows alternate in blocks of GU_BLOCK (the fused
 // weight's row order): gate i sits at column (i / B) * 2B + i % B, its up at
 // + B; otherwise gate i at i and up at im + i.
+// With splits > 1 the gate/up product arrives as split-K slabs (slab i at
+// gu + i * slab), added in slab order first.
 __global__ void k_silu_mul(const float* __restrict__ gu, size_t ldgu, float* __restrict__ act, size_t ldact,
-                           int im, __half* __restrict__ act16, int blocked) {
+                           int im, __half* __restrict__ act16, int blocked, int splits, size_t slab) {
     pdl_trigger();
     const float* g = gu + (size_t)blockIdx.y * ldgu;
     float* a = act + (size_t)blockIdx.y * ldact;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < im; i += gridDim.x * blockDim.x) {
         const int gi = blocked ? (i / GU_BLOCK) * (2 * GU_BLOCK) + i % GU_BLOCK : i;
         const int ui = blocked ? gi + GU_BLOCK : im + i;
-        float o = __fmul_rn(silu_f(g[gi]), g[ui]);
+        float gq[RSN_MAX_SPLITS], uq[RSN_MAX_SPLITS];  // every slab requested before the first add
+#pragma unroll
+        for (int sp = 0; sp < RSN_MAX_SPLITS; sp++) {
+            if (sp < splits) {
+                gq[sp] = g[(size_t)sp * slab + gi];
+                uq[sp] = g[(size_t)sp * slab + ui];
+            }
+        }
+        float gv = gq[0], uv = uq[0];
+#pragma unroll
+        for (int sp = 1; sp < RSN_MAX_SPLITS; sp++) {
+            if (sp < splits) {
+                gv = gv + gq[sp];
+                uv = uv + uq[sp];
+            }
+        }
+        float o = __fmul_rn(silu_f(gv), uv);
         a[i] = o;
         if (act16) store_x16(act16 + (size_t)blockIdx.y * 2 * im, im, i, o);
     }
 }
 
 int launch_silu_mul(const float* gu, size_t ldgu, float* act, size_t ldact, size_t rows, size_t im,
-                    cudaStream_t s, __half* act16, bool blocked) {
+                    cudaStream_t s, __half* act16, bool blocked, int splits) {
     if (rows == 0) return HC_OK;
     HC_CHECK(!blocked || im % GU_BLOCK == 0, HC_ERR_INVALID, "silu_mul: blocked layout needs im %% %d == 0", GU_BLOCK);
+    HC_CHECK(splits >= 1 && splits <= RSN_MAX_SPLITS, HC_ERR_INVALID, "silu_mul: %d slabs", splits);
     unsigned gx = (unsigned)std::min<size_t>((im + 255) / 256, 64);
-    k_silu_mul<<<dim3(gx, (unsigned)rows), 256, 0, s>>>(gu, ldgu, act, ldact, (int)im, act16, blocked ? 1 : 0);
+    k_silu_mul<<<dim3(gx, (unsigned)rows), 256, 0, s>>>(gu, ldgu, act, ldact, (int)im, act16, blocked ? 1 : 0, splits,
+                                                        rows * ldgu);
     HC_LAUNCH_CHECK();
     return HC_OK;
 }

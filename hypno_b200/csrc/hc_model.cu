@@ -190,6 +190,10 @@ struct LayerW {
 
 constexpr size_t kPartRows = 256;  // largest row count (decode batch) using split-K slabs
 constexpr int kPartSplits = 8;      // most slabs one projection writes
+// fused gate/up weights of at most this many rows (74 tiles of 128, half the
+// SMs of a B200) split K into slabs in decode instead of applying the SiLU
+// gate in the GEMM epilogue
+constexpr size_t kGuSlabRows = 74 * 128;
 
 struct Scratch {
     uint64_t generation = 0;  // bumped whenever a buffer moves
@@ -565,9 +569,13 @@ int ensure_scratch(hc_model* m, size_t tokens, size_t logit_rows) {
         if (m->cfg.tp_size > 1) HC_CUDA(cudaMalloc((void**)&s.tp_tmp, t * c.hidden_size * sizeof(float)));
         if (s.split_part) cudaFree(s.split_part);
         s.split_part = nullptr;
-        HC_CUDA(cudaMalloc((void**)&s.split_part, (size_t)kPartSplits * std::min(t, kPartRows) *
-                                                      std::max<size_t>(c.hidden_size, m->nq + 2 * m->nk) *
-                                                      sizeof(float)));
+        // widest slab user: o/down (hidden), qkv, or a narrow gate/up (see run_layers)
+        const size_t gu_w = m->layers.empty() ? 0 : m->layers[0].gu.n;
+        HC_CUDA(cudaMalloc((void**)&s.split_part,
+                           (size_t)kPartSplits * std::min(t, kPartRows) *
+                               std::max<size_t>(std::max<size_t>(c.hidden_size, m->nq + 2 * m->nk),
+                                                gu_w <= kGuSlabRows ? gu_w : 0) *
+                               sizeof(float)));
         HC_CUDA(cudaMalloc((void**)&s.ids, t * sizeof(uint32_t)));
         HC_CUDA(cudaMalloc((void**)&s.seqs, t * sizeof(int)));
         HC_CUDA(cudaMalloc((void**)&s.rowpos, t * sizeof(int)));
@@ -942,7 +950,16 @@ int run_layers(hc_model* m, hc_kv* kv, size_t rows, bool prefill, int seq, int p
         }
         size_t im = L.gu.n / 2;
         HC_TRY(phase(m, PH_GATEUP));
-        if (L.gu_blocked && hc::gemm_tc_eligible(L.gu.q4, rows)) {
+        if (s.split_part && rows <= kPartRows && L.gu_blocked && L.gu.n <= kGuSlabRows &&
+            hc::gemm_tc_eligible(L.gu.q4, rows)) {
+            // a narrow gate/up (a tensor-parallel rank's shard) has too few
+            // 128-row tiles to fill the GPU, and the SiLU epilogue needs whole
+            // sums: split K into slabs and apply the gate in the consumer
+            int splits = 1;
+            HC_TRY(hc::gemm_tc_partials(m->gemm_ws, L.gu.q4, s.xn, H, rows, s.split_part, kPartSplits, &splits,
+                                        m->stream, s.xn16));
+            HC_TRY(hc::launch_silu_mul(s.split_part, L.gu.n, s.act, im, rows, im, m->stream, s.act16, true, splits));
+        } else if (L.gu_blocked && hc::gemm_tc_eligible(L.gu.q4, rows)) {
             HC_TRY(hc::gemm_tc_silu(m->gemm_ws, L.gu.q4, s.xn, H, rows, s.act, im, s.act16, m->stream, s.xn16));
         } else {
             HC_TRY(matmul(m, L.gu, s.xn, H, rows, s.gu, 2 * im, hc::EPI_STORE, nullptr, 0, s.xn16));

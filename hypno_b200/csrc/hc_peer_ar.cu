@@ -90,6 +90,10 @@ __device__ bool handshake(uint32_t* const* peer_flags, const uint32_t* mine, int
 
 template <int VPT>
 __global__ void __launch_bounds__(1024) k_ar_residual_norm(ArParams P) {
+    // the next projection (a programmatic dependent) may start streaming its
+    // weights while this kernel waits for the peers; it reads nothing this
+    // kernel writes before its own grid-dependency wait
+    pdl_trigger();
     __shared__ float red[32];
     __shared__ int ok_s;
     const int row = blockIdx.x;
