@@ -25,7 +25,26 @@ __device__ __forceinline__ float ldkv<float>(const float* p) { return *p; }
 template <>
 __device__ __forceinline__ float ldkv<__half>(const __half* p) { return __half2float(*p); }
 
-// One CTA (4 warps) per (query row, query head).
+// Four consecutive K/V elements as f32 (16-byte / 8-byte aligned loads).
+template <typename KT>
+__device__ __forceinline__ float4 ld4(const KT* p);
+template <>
+__device__ __forceinline__ float4 ld4<float>(const float* p) { return *reinterpret_cast<const float4*>(p); }
+template <>
+__device__ __forceinline__ float4 ld4<__half>(const __half* p) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+    return make_float4(a.x, a.y, b.x, b.y);
+}
+
+// One CTA (4 warps) per (query row, query head): the path for head sizes and
+// group sizes the tiled kernels do not take (e.g. 9 query heads over 3 KV
+// heads).  Scores: one thread per position (its whole dot product, 4
+// elements per load); weighted V: thread (position group, column quad) adds
+// the weights times 4 columns over its group's positions, and the groups'
+// sums are added in group order (4 elements per load when head_dim is a
+// multiple of 4).
 template <typename KT>
 __global__ void __launch_bounds__(128) k_attention(AttnParams P) {
     pdl_trigger();
@@ -33,7 +52,6 @@ __global__ void __launch_bounds__(128) k_attention(AttnParams P) {
     const int row = blockIdx.x, h = blockIdx.y;
     const int hd = P.hd;
     const int kvh = h / (P.nh / P.nkv);
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     __shared__ float red[32];
 
     const float* q = P.q + (size_t)row * P.ldq + (size_t)h * hd;
@@ -66,16 +84,31 @@ __global__ void __launch_bounds__(128) k_attention(AttnParams P) {
         return;
     }
 
-    float* scores = smem;             // n floats
-    float* part = smem + P.smem_n;    // 4 * hd floats
+    // scores (smem_n floats, padded to a multiple of 4 so the float4 partial
+    // sums below stay 16-byte aligned), q (hd floats), the groups' partials
+    float* scores = smem;
+    float* qs = smem + ((P.smem_n + 3) & ~3);
+    float* part = qs + hd;  // [groups][hd]
+    for (int d = threadIdx.x; d < hd; d += blockDim.x) qs[d] = q[d];
+    __syncthreads();
 
-    // scores[p] = (q . k_p) * scale
-    for (int p = warp; p < n; p += 4) {
+    const bool vec = (hd & 3) == 0;  // 4 elements per load (every row start is then aligned)
+    // scores[p] = (q . k_p) * scale, in element order
+    for (int p = threadIdx.x; p < n; p += blockDim.x) {
         const KT* kp = kbase + (size_t)p * kstride;
         float dot = 0.0f;
-        for (int d = lane; d < hd; d += 32) dot = fmaf(q[d], ldkv<KT>(kp + d), dot);
-        dot = warp_sum(dot);
-        if (lane == 0) scores[p] = __fmul_rn(dot, P.scale);
+        if (vec) {
+            for (int d = 0; d < hd; d += 4) {
+                const float4 k4 = ld4<KT>(kp + d);
+                dot = fmaf(qs[d], k4.x, dot);
+                dot = fmaf(qs[d + 1], k4.y, dot);
+                dot = fmaf(qs[d + 2], k4.z, dot);
+                dot = fmaf(qs[d + 3], k4.w, dot);
+            }
+        } else {
+            for (int d = 0; d < hd; d++) dot = fmaf(qs[d], ldkv<KT>(kp + d), dot);
+        }
+        scores[p] = __fmul_rn(dot, P.scale);
     }
     __syncthreads();
     float mx = -INFINITY;
@@ -94,15 +127,31 @@ __global__ void __launch_bounds__(128) k_attention(AttnParams P) {
         scores[p] = (p < n8) ? __fmul_rn(scores[p], inv) : __fdiv_rn(scores[p], total);
     __syncthreads();
 
-    // out[d] = sum_p w_p v_p[d]; warp w takes positions w, w+4, ...
-    for (int d = lane; d < hd; d += 32) {
-        float acc = 0.0f;
-        for (int p = warp; p < n; p += 4) acc = fmaf(scores[p], ldkv<KT>(vbase + (size_t)p * kstride + d), acc);
-        part[warp * hd + d] = acc;
+    // out[d] = sum_p w_p v_p[d]
+    const int cols = vec ? hd / 4 : hd, groups = max(1, (int)blockDim.x / cols);
+    for (int t = threadIdx.x; t < groups * cols; t += blockDim.x) {
+        const int c = t % cols, grp = t / cols;
+        if (vec) {
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int p = grp; p < n; p += groups) {
+                const float w = scores[p];
+                const float4 v4 = ld4<KT>(vbase + (size_t)p * kstride + 4 * c);
+                acc.x = fmaf(w, v4.x, acc.x);
+                acc.y = fmaf(w, v4.y, acc.y);
+                acc.z = fmaf(w, v4.z, acc.z);
+                acc.w = fmaf(w, v4.w, acc.w);
+            }
+            *reinterpret_cast<float4*>(part + (size_t)grp * hd + 4 * c) = acc;
+        } else {
+            float acc = 0.0f;
+            for (int p = grp; p < n; p += groups) acc = fmaf(scores[p], ldkv<KT>(vbase + (size_t)p * kstride + c), acc);
+            part[(size_t)grp * hd + c] = acc;
+        }
     }
     __syncthreads();
     for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-        float o = (part[d] + part[hd + d]) + (part[2 * hd + d] + part[3 * hd + d]);
+        float o = part[d];
+        for (int g = 1; g < groups; g++) o = o + part[(size_t)g * hd + d];
         out[d] = o;
         if (P.out16) store_x16(P.out16 + (size_t)row * 2 * P.nh * hd, P.nh * hd, h * hd + d, o);
     }
@@ -110,7 +159,11 @@ __global__ void __launch_bounds__(128) k_attention(AttnParams P) {
 
 int launch_attention(const AttnParams& P, int rows, int kv_fp16, cudaStream_t s) {
     if (rows == 0) return HC_OK;
-    size_t smem = ((size_t)P.smem_n + 4 * (size_t)P.hd) * sizeof(float);
+    HC_CHECK(P.hd >= 1, HC_ERR_INVALID, "attention: head_dim %d", P.hd);
+    // scores, q, and the weighted-V partial sums of the position groups
+    const size_t cols = P.hd % 4 == 0 ? (size_t)P.hd / 4 : (size_t)P.hd;
+    const size_t groups = std::max<size_t>(1, 128 / cols);
+    size_t smem = ((((size_t)P.smem_n + 3) & ~(size_t)3) + (1 + groups) * (size_t)P.hd) * sizeof(float);
     if (smem > 200 * 1024) {
         hc_set_error("attention: context %d too long for the shared-memory score buffer", P.smem_n);
         return HC_ERR_UNSUPPORTED;

@@ -156,6 +156,31 @@ def test_c1_batched_sequences_equal_single(cuda_device, c1_image):
     assert [kv.seq_len(s) for s in range(4)] == [len(p) + 3 for p in prompts]
 
 
+@pytest.mark.parametrize("max_pos,kv_dtype", [(162, engine.KV_FP32), (161, engine.KV_FP16), (37, engine.KV_FP32)])
+def test_c1_ragged_cache_capacity(cuda_device, c1_image, max_pos, kv_dtype):
+    """configs[0]'s 9 query heads over 3 KV heads take the per-head attention
+    kernel; a cache capacity that is not a multiple of 4 (the bench's parity
+    replay allocates prompt + steps + 1 positions) must not disturb its
+    shared-memory layout.  Logits and greedy ids against the oracle."""
+    cfg = synth.CONFIGS["c1"]
+    T = min(cfg["prompt"], max_pos - 5)
+    prompt = synth.prompt_ids(cfg["vocab"], T, seed=1)
+    m = engine.HypnoModel(c1_image)
+    om = orc.OracleModel(c1_image)
+    kv = engine.KVCache(m, n_seqs=1, max_pos=max_pos, kv_dtype=kv_dtype)
+    okv = om.new_kv(max_pos)
+    g = engine.batch_forward(m, prompt, kv)
+    r = orc.batch_forward(om, prompt, okv)
+    assert rel_err(g, r) <= TOL
+    tok = orc.greedy(r)
+    for _ in range(4):
+        lg, am = engine.decode_step(m, kv, [0], [tok])
+        ref = orc.model_forward(om, tok, okv)
+        assert rel_err(lg[0], ref) <= TOL
+        assert int(am[0]) == orc.greedy(ref)
+        tok = int(am[0])
+
+
 def test_c1_fp16_kv(cuda_device, c1_image):
     """fp16 KV cache (new in this backend; the reference cache is FP32):
     logits stay within tolerance of the FP32-KV oracle."""
