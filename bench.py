@@ -515,9 +515,11 @@ def run_ours(args):
         dist.barrier()
         torch.cuda.synchronize()
     e0.record(es)
+    torch.cuda.nvtx.range_push("timed_prefill")
     for s in range(S):
         logits = engine.batch_forward(model, prompts[s], kv, seq=s)
         first[s] = int(np.nonzero(logits == logits.max())[0][-1])
+    torch.cuda.nvtx.range_pop()
     e1.record(es)
     torch.cuda.synchronize()
     prefill_ms = e0.elapsed_time(e1)

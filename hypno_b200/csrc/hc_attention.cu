@@ -1444,6 +1444,223 @@ __global__ void __launch_bounds__(PA_THREADS) k_pattn(AttnParams P, int T) {
     }
 }
 
+// ---- Tensor-core form of the tiled prefill attention (head_dim 64 or 128).
+// One CTA of four warps per (64-query block, query head); warp w owns queries
+// t0 + 16 w .. + 15.  Q, K and V tiles are split into fp16 hi = fp16(x) and
+// lo = fp16(x - hi) in shared memory (rows of HD halves, 16-byte chunk c of
+// row r stored at c ^ (r & 7) for conflict-free ldmatrix); every score is
+// Qh.Kh + Qh.Kl + Ql.Kh and every output Wh.Vh + Wh.Vl + Wl.Vh (mma.sync
+// m16n8k16, f32 accumulate), which keeps the f32 products to ~2^-22.  The
+// two passes are those of k_pattn: the row maxima over the visible keys
+// (s < t) first, then the weights (the reference's polynomial / exp with that
+// maximum) and W V; the score accumulators of two 8-key blocks are reused
+// directly as the A fragment of the W V step.  Query blocks run longest first.
+constexpr int PM_BQ = 64, PM_BK = 64, PM_THREADS = 128;
+
+// f32 tile rows [r0, r0 + 64) of `src` (row stride ld, HD features; rows past
+// nrows are zero) -> hi and lo fp16 tiles in the swizzled layout.
+template <int HD>
+__device__ __forceinline__ void pm_fill(const float* __restrict__ src, size_t ld, int r0, int nrows, __half* hi,
+                                        __half* lo) {
+    constexpr int Q4 = HD / 4;  // float4 per row
+    for (int i = threadIdx.x; i < PM_BQ * Q4; i += PM_THREADS) {
+        const int r = i / Q4, c4 = i % Q4;
+        const int gr = r0 + r;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (gr < nrows) v = *reinterpret_cast<const float4*>(src + (size_t)gr * ld + 4 * c4);
+        uint2 h, l;
+        h.x = split_pair(v.x, v.y, false);
+        h.y = split_pair(v.z, v.w, false);
+        l.x = split_pair(v.x, v.y, true);
+        l.y = split_pair(v.z, v.w, true);
+        const int chunk = (c4 >> 1) ^ (r & 7);
+        const size_t off = (size_t)r * HD + chunk * 8 + (c4 & 1) * 4;  // halves
+        *reinterpret_cast<uint2*>(hi + off) = h;
+        *reinterpret_cast<uint2*>(lo + off) = l;
+    }
+}
+
+// Address (for this lane) of the 8x8 matrix `mi` of an ldmatrix.x4 over rows
+// row0 + (row8 ? 8 : 0) + (lane & 7), 16-byte chunk `chunk`.
+template <int HD>
+__device__ __forceinline__ const __half* pm_addr(const __half* tile, int row, int chunk) {
+    return tile + (size_t)row * HD + ((chunk ^ (row & 7)) * 8);
+}
+
+template <int HD>
+__global__ void __launch_bounds__(PM_THREADS, 2) k_pattn_mma(AttnParams P, int T) {
+    constexpr int KS = HD / 16;  // 16-feature steps of a score
+    constexpr int NB = HD / 8;   // 8-feature blocks of an output row
+    pdl_trigger();
+    extern __shared__ __align__(16) uint8_t pm_smem[];
+    __half* Qh = reinterpret_cast<__half*>(pm_smem);
+    __half* Ql = Qh + PM_BQ * HD;
+    __half* Kh = Ql + PM_BQ * HD;
+    __half* Kl = Kh + PM_BK * HD;
+    __half* Vh = Kl + PM_BK * HD;
+    __half* Vl = Vh + PM_BK * HD;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int t = lane & 3, q4 = lane >> 2;
+    const int qb = (int)gridDim.x - 1 - (int)blockIdx.x;  // longest blocks first
+    const int t0 = qb * PM_BQ, h = blockIdx.y;
+    const int kvh = h / (P.nh / P.nkv);
+    const int qend = min(t0 + PM_BQ, T);
+    const int nkt = (qend - 1 + PM_BK - 1) / PM_BK;  // key tiles covering keys < qend - 1
+    const int ra = t0 + warp * 16 + q4, rb = ra + 8;   // this thread's two query rows
+
+    pm_fill<HD>(P.q + (size_t)h * HD, P.ldq, t0, T, Qh, Ql);
+    const float* kb = P.kp + (size_t)kvh * HD;
+    const float* vb = P.vp + (size_t)kvh * HD;
+    const int mi = lane >> 3, mr = lane & 7;
+
+    // S = Q K^T of key tile kt for the warp's 16 rows (acc[nb][0..3]: rows ra
+    // / rb, keys 64 kt + 8 nb + 2 t, + 1), scaled
+    auto scores = [&](float (&acc)[8][4]) {
+#pragma unroll
+        for (int nb = 0; nb < 8; nb++)
+#pragma unroll
+            for (int e = 0; e < 4; e++) acc[nb][e] = 0.0f;
+#pragma unroll
+        for (int kk = 0; kk < KS; kk++) {
+            uint32_t ah[4], al[4];
+            const int arow = warp * 16 + (mi & 1) * 8 + mr, achunk = 2 * kk + (mi >> 1);
+            ldsm_x4(ah, pm_addr<HD>(Qh, arow, achunk));
+            ldsm_x4(al, pm_addr<HD>(Ql, arow, achunk));
+#pragma unroll
+            for (int nb = 0; nb < 8; nb += 2) {
+                uint32_t bh[4], bl[4];
+                const int brow = 8 * (nb + (mi >> 1)) + mr, bchunk = 2 * kk + (mi & 1);
+                ldsm_x4(bh, pm_addr<HD>(Kh, brow, bchunk));
+                ldsm_x4(bl, pm_addr<HD>(Kl, brow, bchunk));
+                mma16816(acc[nb], ah, bh[0], bh[1]);
+                mma16816(acc[nb], ah, bl[0], bl[1]);
+                mma16816(acc[nb], al, bh[0], bh[1]);
+                mma16816(acc[nb + 1], ah, bh[2], bh[3]);
+                mma16816(acc[nb + 1], ah, bl[2], bl[3]);
+                mma16816(acc[nb + 1], al, bh[2], bh[3]);
+            }
+        }
+#pragma unroll
+        for (int nb = 0; nb < 8; nb++)
+#pragma unroll
+            for (int e = 0; e < 4; e++) acc[nb][e] = __fmul_rn(acc[nb][e], P.scale);
+    };
+
+    // ---- pass 1: row maxima over keys s < t
+    float mxa = -INFINITY, mxb = -INFINITY;
+    for (int kt = 0; kt < nkt; kt++) {
+        __syncthreads();
+        pm_fill<HD>(kb, P.ldkv, kt * PM_BK, T, Kh, Kl);
+        __syncthreads();
+        float acc[8][4];
+        scores(acc);
+#pragma unroll
+        for (int nb = 0; nb < 8; nb++) {
+            const int key = kt * PM_BK + 8 * nb + 2 * t;
+            if (key < ra) mxa = fmaxf(mxa, acc[nb][0]);
+            if (key + 1 < ra) mxa = fmaxf(mxa, acc[nb][1]);
+            if (key < rb) mxb = fmaxf(mxb, acc[nb][2]);
+            if (key + 1 < rb) mxb = fmaxf(mxb, acc[nb][3]);
+        }
+    }
+#pragma unroll
+    for (int o = 1; o <= 2; o <<= 1) {
+        mxa = fmaxf(mxa, __shfl_xor_sync(0xffffffffu, mxa, o));
+        mxb = fmaxf(mxb, __shfl_xor_sync(0xffffffffu, mxb, o));
+    }
+
+    // ---- pass 2: weights and W V
+    float o[NB][4];
+#pragma unroll
+    for (int nb = 0; nb < NB; nb++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) o[nb][e] = 0.0f;
+    float suma = 0.0f, sumb = 0.0f;
+    const int n8a = ra - (ra % 8), n8b = rb - (rb % 8);
+    for (int kt = 0; kt < nkt; kt++) {
+        __syncthreads();
+        pm_fill<HD>(kb, P.ldkv, kt * PM_BK, T, Kh, Kl);
+        pm_fill<HD>(vb, P.ldkv, kt * PM_BK, T, Vh, Vl);
+        __syncthreads();
+        float acc[8][4];
+        scores(acc);
+#pragma unroll
+        for (int nb = 0; nb < 8; nb++) {
+            const int key = kt * PM_BK + 8 * nb + 2 * t;
+            const float w0 = key < ra ? softmax_weight(acc[nb][0], mxa, key, n8a) : 0.0f;
+            const float w1 = key + 1 < ra ? softmax_weight(acc[nb][1], mxa, key + 1, n8a) : 0.0f;
+            const float w2 = key < rb ? softmax_weight(acc[nb][2], mxb, key, n8b) : 0.0f;
+            const float w3 = key + 1 < rb ? softmax_weight(acc[nb][3], mxb, key + 1, n8b) : 0.0f;
+            suma += w0 + w1;
+            sumb += w2 + w3;
+            acc[nb][0] = w0;
+            acc[nb][1] = w1;
+            acc[nb][2] = w2;
+            acc[nb][3] = w3;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; j++) {  // 16 keys: score blocks 2 j and 2 j + 1
+            uint32_t wh[4], wl[4];
+            wh[0] = split_pair(acc[2 * j][0], acc[2 * j][1], false);
+            wh[1] = split_pair(acc[2 * j][2], acc[2 * j][3], false);
+            wh[2] = split_pair(acc[2 * j + 1][0], acc[2 * j + 1][1], false);
+            wh[3] = split_pair(acc[2 * j + 1][2], acc[2 * j + 1][3], false);
+            wl[0] = split_pair(acc[2 * j][0], acc[2 * j][1], true);
+            wl[1] = split_pair(acc[2 * j][2], acc[2 * j][3], true);
+            wl[2] = split_pair(acc[2 * j + 1][0], acc[2 * j + 1][1], true);
+            wl[3] = split_pair(acc[2 * j + 1][2], acc[2 * j + 1][3], true);
+#pragma unroll
+            for (int nb = 0; nb < NB; nb += 2) {
+                uint32_t vh[4], vl[4];
+                const int vrow = 16 * j + 8 * (mi & 1) + mr, vchunk = nb + (mi >> 1);
+                ldsm_x4_t(vh, pm_addr<HD>(Vh, vrow, vchunk));
+                ldsm_x4_t(vl, pm_addr<HD>(Vl, vrow, vchunk));
+                mma16816(o[nb], wh, vh[0], vh[1]);
+                mma16816(o[nb], wh, vl[0], vl[1]);
+                mma16816(o[nb], wl, vh[0], vh[1]);
+                mma16816(o[nb + 1], wh, vh[2], vh[3]);
+                mma16816(o[nb + 1], wh, vl[2], vl[3]);
+                mma16816(o[nb + 1], wl, vh[2], vh[3]);
+            }
+        }
+    }
+#pragma unroll
+    for (int off = 1; off <= 2; off <<= 1) {
+        suma += __shfl_xor_sync(0xffffffffu, suma, off);
+        sumb += __shfl_xor_sync(0xffffffffu, sumb, off);
+    }
+#pragma unroll
+    for (int half = 0; half < 2; half++) {
+        const int tr = half ? rb : ra;
+        if (tr >= T) continue;
+        const float sum = half ? sumb : suma;
+        float* out = P.out + (size_t)tr * P.ldo + (size_t)h * HD;
+        __half* o16 = P.out16 ? P.out16 + (size_t)tr * 2 * P.nh * HD : nullptr;
+        const float* vs = P.vself + (size_t)tr * P.ldself + (size_t)kvh * HD;
+#pragma unroll
+        for (int nb = 0; nb < NB; nb++) {
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                const int d = 8 * nb + 2 * t + e;
+                const float r = (tr < 2) ? vs[d] : __fdiv_rn(o[nb][2 * half + e], sum);
+                out[d] = r;
+                if (o16) store_x16(o16, P.nh * HD, h * HD + d, r);
+            }
+        }
+    }
+}
+
+template <int HD>
+int launch_pattn_mma(const AttnParams& P, int T, cudaStream_t s) {
+    const size_t smem = (size_t)6 * PM_BQ * HD * sizeof(__half);
+    if (smem > 48 * 1024)
+        HC_CUDA(cudaFuncSetAttribute(k_pattn_mma<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    dim3 grid((unsigned)((T + PM_BQ - 1) / PM_BQ), (unsigned)P.nh);
+    k_pattn_mma<HD><<<grid, PM_THREADS, smem, s>>>(P, T);
+    HC_LAUNCH_CHECK();
+    return HC_OK;
+}
+
 template <int HD>
 int launch_pattn_hd(const AttnParams& P, int T, cudaStream_t s) {
     size_t smem = ((size_t)HD * PA_BQ + (size_t)HD * PA_KT_STRIDE + (size_t)PA_BQ * PA_BK) * sizeof(float);
@@ -1463,8 +1680,8 @@ int launch_prefill_attention(const AttnParams& P, int T, cudaStream_t s) {
     switch (P.hd) {
         case 16: return launch_pattn_hd<16>(P, T, s);
         case 32: return launch_pattn_hd<32>(P, T, s);
-        case 64: return launch_pattn_hd<64>(P, T, s);
-        case 128: return launch_pattn_hd<128>(P, T, s);
+        case 64: return launch_pattn_mma<64>(P, T, s);
+        case 128: return launch_pattn_mma<128>(P, T, s);
         default:
             hc_set_error("tiled prefill attention: unsupported head_dim %d", P.hd);
             return HC_ERR_UNSUPPORTED;
