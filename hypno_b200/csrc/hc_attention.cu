@@ -1487,6 +1487,38 @@ __device__ __forceinline__ const __half* pm_addr(const __half* tile, int row, in
     return tile + (size_t)row * HD + ((chunk ^ (row & 7)) * 8);
 }
 
+// The prompt's f32 K and V rows -> the four fp16 planes of kv16 (K hi, K lo,
+// V hi, V lo; rows of nk = nkv * hd halves), once per layer, so that the
+// attention CTAs copy ready tiles instead of converting every tile they read.
+__global__ void k_split_kv(const float* __restrict__ kp, const float* __restrict__ vp, size_t ldkv, int T, int nk,
+                           __half* __restrict__ kv16) {
+    const size_t plane = (size_t)T * nk, n4 = plane / 4;
+    const int q4 = nk / 4;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t t = i / q4, c = 4 * (i % q4);
+        const float4 k = *reinterpret_cast<const float4*>(kp + t * ldkv + c);
+        const float4 v = *reinterpret_cast<const float4*>(vp + t * ldkv + c);
+        const size_t o = t * nk + c;
+        *reinterpret_cast<uint2*>(kv16 + o) = make_uint2(split_pair(k.x, k.y, false), split_pair(k.z, k.w, false));
+        *reinterpret_cast<uint2*>(kv16 + plane + o) = make_uint2(split_pair(k.x, k.y, true), split_pair(k.z, k.w, true));
+        *reinterpret_cast<uint2*>(kv16 + 2 * plane + o) = make_uint2(split_pair(v.x, v.y, false), split_pair(v.z, v.w, false));
+        *reinterpret_cast<uint2*>(kv16 + 3 * plane + o) = make_uint2(split_pair(v.x, v.y, true), split_pair(v.z, v.w, true));
+    }
+}
+
+// Rows [r0, r0 + 64) of one KV head's fp16 plane (row stride nk halves, rows
+// past T zero) -> a swizzled tile, by cp.async (the caller commits and waits).
+template <int HD>
+__device__ __forceinline__ void pm_copy(const __half* __restrict__ plane, int nk, int r0, int T, __half* tile) {
+    constexpr int CPR = HD / 8;
+    for (int i = threadIdx.x; i < PM_BK * CPR; i += PM_THREADS) {
+        const int r = i / CPR, c = i % CPR;
+        const bool in = r0 + r < T;
+        cp_async16(tile + (size_t)r * HD + ((c ^ (r & 7)) * 8), plane + (size_t)(in ? r0 + r : 0) * nk + c * 8,
+                   in ? 16 : 0);
+    }
+}
+
 template <int HD>
 __global__ void __launch_bounds__(PM_THREADS, 2) k_pattn_mma(AttnParams P, int T) {
     constexpr int KS = HD / 16;  // 16-feature steps of a score
@@ -1512,6 +1544,26 @@ __global__ void __launch_bounds__(PM_THREADS, 2) k_pattn_mma(AttnParams P, int T
     const float* kb = P.kp + (size_t)kvh * HD;
     const float* vb = P.vp + (size_t)kvh * HD;
     const int mi = lane >> 3, mr = lane & 7;
+    // this KV head's columns of the fp16 planes (when the caller made them)
+    const int nk = P.nkv * HD;
+    const size_t plane = (size_t)T * nk;
+    const __half* k16 = P.kv16 ? P.kv16 + (size_t)kvh * HD : nullptr;
+    auto load_k = [&](int kt) {
+        if (k16) {
+            pm_copy<HD>(k16, nk, kt * PM_BK, T, Kh);
+            pm_copy<HD>(k16 + plane, nk, kt * PM_BK, T, Kl);
+        } else {
+            pm_fill<HD>(kb, P.ldkv, kt * PM_BK, T, Kh, Kl);
+        }
+    };
+    auto load_v = [&](int kt) {
+        if (k16) {
+            pm_copy<HD>(k16 + 2 * plane, nk, kt * PM_BK, T, Vh);
+            pm_copy<HD>(k16 + 3 * plane, nk, kt * PM_BK, T, Vl);
+        } else {
+            pm_fill<HD>(vb, P.ldkv, kt * PM_BK, T, Vh, Vl);
+        }
+    };
 
     // S = Q K^T of key tile kt for the warp's 16 rows (acc[nb][0..3]: rows ra
     // / rb, keys 64 kt + 8 nb + 2 t, + 1), scaled
@@ -1550,7 +1602,9 @@ __global__ void __launch_bounds__(PM_THREADS, 2) k_pattn_mma(AttnParams P, int T
     float mxa = -INFINITY, mxb = -INFINITY;
     for (int kt = 0; kt < nkt; kt++) {
         __syncthreads();
-        pm_fill<HD>(kb, P.ldkv, kt * PM_BK, T, Kh, Kl);
+        load_k(kt);
+        cp_async_commit();
+        cp_async_wait<0>();
         __syncthreads();
         float acc[8][4];
         scores(acc);
@@ -1579,8 +1633,10 @@ __global__ void __launch_bounds__(PM_THREADS, 2) k_pattn_mma(AttnParams P, int T
     const int n8a = ra - (ra % 8), n8b = rb - (rb % 8);
     for (int kt = 0; kt < nkt; kt++) {
         __syncthreads();
-        pm_fill<HD>(kb, P.ldkv, kt * PM_BK, T, Kh, Kl);
-        pm_fill<HD>(vb, P.ldkv, kt * PM_BK, T, Vh, Vl);
+        load_k(kt);
+        load_v(kt);
+        cp_async_commit();
+        cp_async_wait<0>();
         __syncthreads();
         float acc[8][4];
         scores(acc);
@@ -1653,6 +1709,16 @@ __global__ void __launch_bounds__(PM_THREADS, 2) k_pattn_mma(AttnParams P, int T
 template <int HD>
 int launch_pattn_mma(const AttnParams& P, int T, cudaStream_t s) {
     const size_t smem = (size_t)6 * PM_BQ * HD * sizeof(__half);
+    if (P.kv16) {
+        const int nk = P.nkv * HD;
+        HC_CHECK(P.ldkv % 4 == 0 && ((uintptr_t)P.kp & 15) == 0 && ((uintptr_t)P.vp & 15) == 0 &&
+                     ((uintptr_t)P.kv16 & 15) == 0,
+                 HC_ERR_INVALID, "prefill attention: K/V rows must be 16-byte aligned");
+        const size_t n4 = (size_t)T * nk / 4;
+        const unsigned g = (unsigned)std::min<size_t>((n4 + 255) / 256, 2048);
+        k_split_kv<<<g, 256, 0, s>>>(P.kp, P.vp, P.ldkv, T, nk, P.kv16);
+        HC_LAUNCH_CHECK();
+    }
     if (smem > 48 * 1024)
         HC_CUDA(cudaFuncSetAttribute(k_pattn_mma<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     dim3 grid((unsigned)((T + PM_BQ - 1) / PM_BQ), (unsigned)P.nh);

@@ -26,6 +26,9 @@ struct AttnParams {
     const float* vp;
     size_t ldkv;
     __half* out16 = nullptr;  // optional fp16 copy of out (rows of nh*hd, GEMM K order)
+    // prefill scratch (may be null): 4 planes of [T][nkv*hd] fp16 (K hi, K lo,
+    // V hi, V lo), filled by launch_prefill_attention for the tensor-core kernel
+    __half* kv16 = nullptr;
     int cluster = 1;          // > 1: that many CTAs of a cluster share a (sequence, KV head), chunk positions each
 };
 
@@ -62,6 +65,9 @@ struct DecAttnParams {
     float* opart;         // [rows][nh][nsplit][hd]
     float* spart;         // [rows][nh][nsplit]
     __half* out16 = nullptr;  // optional fp16 copy of out (rows of nh*hd, GEMM K order)
+    // prefill scratch (may be null): 4 planes of [T][nkv*hd] fp16 (K hi, K lo,
+    // V hi, V lo), filled by launch_prefill_attention for the tensor-core kernel
+    __half* kv16 = nullptr;
     int cluster = 1;          // > 1: that many CTAs of a cluster share a (sequence, KV head), chunk positions each
     int wide = 0;             // whole context (nsplit 1): one 16-warp CTA per SM (see dattn_wide_ok)
 };

@@ -863,6 +863,9 @@ int run_layers(hc_model* m, hc_kv* kv, size_t rows, bool prefill, int seq, int p
             P.kp = s.qkv + nq;
             P.vp = s.qkv + nq + nk;
             P.ldkv = ldqkv;
+            // the gate/up buffer is free until the MLP: it holds the fp16 K/V
+            // planes of the tensor-core prefill attention (2 * nk floats a row)
+            if (L.gu.n >= 2 * nk) P.kv16 = reinterpret_cast<__half*>(s.gu);
             if (hc::pattn_supported((int)hd))
                 HC_TRY(hc::launch_prefill_attention(P, (int)rows, m->stream));
             else
