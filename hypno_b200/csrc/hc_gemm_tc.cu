@@ -151,13 +151,27 @@ __device__ __forceinline__ void deq_word_split(uint32_t w, __half2 shi2, __half2
 // 128 columns (the hi weights of a 128-K stage, then its lo weights); S_TM
 // divides S_X, so the commit that frees X stage j % S_X also frees A slot
 // j % S_TM.
-template <int TN>
+//
+// Stream-K (SK, decode tiles of 32 tokens): a grid of G <= #SM CTAs, each
+// taking an equal run of the (tile, stage) units [c U / G, (c + 1) U / G),
+// U = tiles x stages per tile, instead of one tile per CTA: no second wave
+// of CTAs when the tiles do not divide over the SMs.  A CTA's run falls into
+// pieces, one per tile it touches; the stage counter j runs on across the
+// pieces, so the rings and their barrier phases are those of one long tile.
+// A fourth warpgroup drains the accumulators after every piece (the
+// issuers wait for it before the next piece's first MMA).  The piece that
+// holds a tile's first stage owns the tile: the CTAs holding its other
+// pieces (their first, or only, piece) store their partial sums in a
+// workspace slot and raise a per-warp flag, and the owner adds them in K
+// order before its usual epilogue.
+template <int TN, bool SK = false>
 struct Cfg {
     static constexpr int TN_ = TN;
     static constexpr int NB = 2 * TN;                        // B rows of an MMA: hi tokens, then lo tokens
     static constexpr int COLS = 512;                         // tensor-memory columns (one CTA per SM)
     static constexpr int DEQ_WARPS = 16;
-    static constexpr int THREADS = 128 + 32 * DEQ_WARPS;
+    static constexpr int EPI_WARP0 = 4 + DEQ_WARPS;          // SK: the epilogue warpgroup
+    static constexpr int THREADS = 128 + 32 * DEQ_WARPS + (SK ? 128 : 0);
     static constexpr int MIN_BLOCKS = 1;
     static constexpr int X_STAGE = 2 * NB * 128;             // two 64-element K halves, 128 B per B row
     static constexpr int W_STAGE = BM * (BK / 2);            // 128 rows x 64 nibble bytes
@@ -194,8 +208,19 @@ struct Cfg {
     __host__ __device__ static constexpr int w_off(int s) { return S_X * X_STAGE + s * W_STAGE; }
     __host__ __device__ static constexpr int s_off(int s) { return S_X * X_STAGE + S_W * W_STAGE + s * S_STAGE; }
     __host__ __device__ static constexpr int ring_bytes() { return S_X * X_STAGE + S_W * (W_STAGE + S_STAGE); }
-    __host__ __device__ static constexpr int bar_off() { return ring_bytes(); }
-    static constexpr int NBARS = 2 * S_W + 2 * S_X + S_TM + 1;
+    // SK: the epilogue's accumulator tile ([TN][BM] f32), apart from the busy rings
+    static constexpr int XB_BYTES = SK ? TN * BM * 4 : 0;
+    // SK register split (setmaxnreg): the launch gives every thread 80
+    // registers (768 threads); the producer / issuer warpgroup and the
+    // epilogue warpgroup hand theirs down so the four dequant warpgroups run
+    // with as many as the 640-thread kernel: 128 x 48 + 128 x 48 + 512 x 96
+    // = 768 x 80.
+    static constexpr int REG_LAUNCH = 80, REG_CTRL = 48, REG_EPI = 48, REG_DEQ = 96;
+    static_assert(!SK || 128 * REG_CTRL + 128 * REG_EPI + 32 * DEQ_WARPS * REG_DEQ <= THREADS * REG_LAUNCH,
+                  "register split above the launch's registers");
+    __host__ __device__ static constexpr int xb_off() { return ring_bytes(); }
+    __host__ __device__ static constexpr int bar_off() { return ring_bytes() + XB_BYTES; }
+    static constexpr int NBARS = 2 * S_W + 2 * S_X + S_TM + 1 + (SK ? 1 : 0);
     __host__ __device__ static constexpr int smem() { return bar_off() + NBARS * 8 + 16 + 1024; }
     static_assert(NB <= 256 && NB % 16 == 0, "MMA N of a 128-row tile");
     static_assert(S_TM >= 2 && A_COL + A_SLOT * S_TM <= COLS, "tensor memory budget");
@@ -209,6 +234,7 @@ struct Cfg {
     static_assert(S_W >= S_TM && RR <= S_X && (ISS == 1 || S_W % S_TM == 0), "barrier phase ordering (see the dequant warps)");
     static_assert(WG_PER == 1 || WG_PER == 2 || WG_PER == 4, "dequant split: 4, 2 or 1 blocks per warpgroup");
     static_assert(!PRELOAD || S_W % RR == 0, "weight-first waits (see the dequant warps)");
+    static_assert(!SK || (ISS == 2 && TN == 32), "stream-K runs decode tiles (two issuers)");
     static_assert(smem() <= 232448, "shared memory budget");
     static_assert((TN * 128) % 1024 == 0, "each X box starts on a 1024-byte swizzle atom");
     static constexpr int RED_PITCH = TN + 1;                  // floats per row of the split-K partial tiles
@@ -243,13 +269,35 @@ __device__ __forceinline__ void load_accumulators(uint32_t tmem, int q, int c0, 
     }
 }
 
-template <int TN>
-__global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
+// Stream-K flags (one per contributing CTA and TMEM lane quarter): the whole
+// warp polls with acquire loads, bounded like the barrier waits.
+__device__ __forceinline__ bool sk_flag_wait(const int* flag, volatile int* abort_flag) {
+    const long long start = clock64();
+    for (uint32_t i = 0;; i++) {
+        int v;
+        asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+        if (__all_sync(0xffffffffu, v != 0)) return true;
+        __nanosleep(128);
+        if ((i & 63) == 63) {
+            if (*abort_flag || clock64() - start > WAIT_CYCLES) {
+                *abort_flag = 1;
+                return false;
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ void sk_flag_set(int* flag, int v) {
+    asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(flag), "r"(v) : "memory");
+}
+
+template <int TN, bool SK = false>
+__global__ void __launch_bounds__(Cfg<TN, SK>::THREADS, Cfg<TN, SK>::MIN_BLOCKS)
     k_q4_gemm_tc(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
                  const __grid_constant__ CUtensorMap smap, float* __restrict__ y, size_t ldy, const float* res, size_t ldres,
                  int epi, int N, int K, int T, int splits, size_t split_stride, __half* __restrict__ y16,
-                 int* __restrict__ err) {
-    using C = Cfg<TN>;
+                 int* __restrict__ err, float* __restrict__ sk_part, int* __restrict__ sk_flag) {
+    using C = Cfg<TN, SK>;
     constexpr int S_X = C::S_X, S_W = C::S_W, S_TM = C::S_TM;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -258,8 +306,9 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
     uint64_t* xfull = wempty + S_W;                                      // [S_X] X stage landed
     uint64_t* mdone = xfull + S_X;                                       // [S_X] MMAs of the stage done
     uint64_t* aready = mdone + S_X;                                      // [S_TM] A slot written
-    uint64_t* dfull = aready + S_TM;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dfull + 1);
+    uint64_t* dfull = aready + S_TM;                                     // accumulators complete (per SK piece)
+    uint64_t* dempty = dfull + 1;                                        // SK: accumulators drained
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dfull + 1 + (SK ? 1 : 0));
     __shared__ int abort_flag;
     bool epi_ok = false;  // epilogue warpgroup: the accumulators are complete
 
@@ -267,7 +316,27 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
     const int n0 = blockIdx.x * BM, t0 = blockIdx.y * TN, split = blockIdx.z;
     const int nk_all = K / BK;
     const int it0 = (int)((long long)nk_all * split / splits), it1 = (int)((long long)nk_all * (split + 1) / splits);
-    const int nk = it1 - it0;
+    // SK: this CTA's run [sk_b, sk_e) of the sk_u (tile, stage) units
+    // (the host keeps sk_u x gridDim.x below 2^31)
+    int sk_b = 0, sk_e = 0, sk_u = 0;
+    if constexpr (SK) {
+        sk_u = ((N + BM - 1) / BM) * nk_all;
+        sk_b = (int)blockIdx.x * sk_u / (int)gridDim.x;
+        sk_e = ((int)blockIdx.x + 1) * sk_u / (int)gridDim.x;
+    }
+    const int nk = SK ? sk_e - sk_b : it1 - it0;
+    // first weight row and K stage of stage j
+    auto stage_at = [&](int j, int& row0, int& kst) {
+        if constexpr (SK) {
+            const int u = sk_b + j;
+            const int tile = u / nk_all;
+            row0 = tile * BM;
+            kst = u - tile * nk_all;
+        } else {
+            row0 = n0;
+            kst = it0 + j;
+        }
+    };
 
     if (threadIdx.x == 0) {
         abort_flag = 0;
@@ -281,6 +350,7 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
         }
         for (int a = 0; a < S_TM; a++) mbar_init(&aready[a], 4 * C::WG_PER);
         mbar_init(dfull, C::ISS);
+        if (SK) mbar_init(dempty, 4);  // the epilogue warps
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 2) {
@@ -299,101 +369,155 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
     // those of the j-th use of each barrier; every wait is at most one phase
     // away from the phase it observes (see the dequant note), which is what
     // parity waits require.
-    if (warp == 0) {
-        // ---------------- weight producer.  The weights do not depend on the
-        // previous kernel, so (launched as a programmatic dependent) this CTA
-        // streams them while the kernel producing X may still be running.
-        if (lane == 0) {
-            for (int j = 0; j < nk; j++) {
-                const int st = j % S_W;
-                if (j >= S_W && !mbar_wait(&wempty[st], ((uint32_t)(j / S_W) & 1u) ^ 1u, &abort_flag, 64)) break;
-                mbar_expect_tx(&wfull[st], (uint32_t)(C::W_STAGE + C::S_STAGE));
-                tma_load_2d(smem + C::w_off(st), &wmap, &wfull[st], (it0 + j) * BK / 2, n0);
-                tma_load_2d(smem + C::s_off(st), &smap, &wfull[st], 8 * ((it0 + j) >> 1), n0);
-            }
-        }
-    } else if (warp == 2) {
-        // ---------------- X producer (after the grid dependency)
-        if (lane == 0) {
-            grid_dependency_wait();
-            for (int j = 0; j < nk; j++) {
-                const int st = j % S_X;
-                if (j >= S_X && !mbar_wait(&mdone[st], ((uint32_t)(j / S_X) & 1u) ^ 1u, &abort_flag, 64)) break;
-                mbar_expect_tx(&xfull[st], (uint32_t)C::X_STAGE);
-                uint8_t* xs = smem + C::x_off(st);
-                const int kk = (it0 + j) * BK;
-                // K half h of the stage holds NB rows: the tile's hi rows
-                // (columns [0, K) of the activation rows), then its lo rows
-                // (columns [K, 2K)); rows past the last token read as zeros
-#pragma unroll
-                for (int h = 0; h < 2; h++)
-#pragma unroll
-                    for (int p = 0; p < 2; p++)
-                        tma_load_2d(xs + (h * C::NB + p * TN) * 128, &xmap, &xfull[st], p * K + kk + 64 * h, t0);
-            }
-        }
-    } else if (warp == 1 || (C::ISS == 2 && warp == 3)) {
-        // ---------------- MMA issuer(s): the whole warp runs the loop and its
-        // waits; one elected lane issues each batch of MMAs (a converged issue
-        // keeps the operands in uniform registers: ~40 cycles per MMA instead
-        // of ~110 from a lone lane).  Issuer i takes the stages j = i, i + ISS,
-        // ... into its accumulator D_i.  A single issuer takes every stage that
-        // is already dequantized (and whose X has landed) when the oldest one
-        // is, up to MMA_BATCH, under one wait + fence.  Per 16-wide K step:
-        // hi weights x [x_hi; x_lo] into D_i, lo weights x x_hi into D_lo (or
-        // into D_i's hi-token half).
-        // Phases: an issuer's aready / xfull wait for stage j must find the
-        // barrier's previous phase (stage j - S_TM, resp. j - S_X) complete.
-        // With one issuer that stage was its own.  With two, stage j - S_X
-        // (S_X even) is its own; stage j - S_TM may be the other issuer's, so
-        // the issuer first waits for that stage's MMAs (mdone), which follow
-        // its aready.  The next phases need this issuer's MMA of stage j.
-        constexpr uint32_t idesc_hi = make_idesc(C::NB);  // hi weights x (hi, lo) tokens
-        constexpr uint32_t idesc_lo = make_idesc(TN);     // lo weights x hi tokens
-        constexpr int KSTEPS = BK / 16;
-        const int iss = warp == 1 ? 0 : 1;
-        const uint32_t d_hi = tmem + (uint32_t)(iss * C::D_COLS);
-        const uint32_t d_lo = d_hi + (uint32_t)(C::DUALD ? C::NB : 0);
-        bool ok = true;
-        for (int j = iss; j < nk;) {
-            if ((C::ISS == 2 && (S_TM & 1) && j >= S_TM &&
-                 !warp_wait(&mdone[(j - S_TM) % S_X], (uint32_t)((j - S_TM) / S_X) & 1u, &abort_flag)) ||
-                !warp_wait(&xfull[j % S_X], (uint32_t)(j / S_X) & 1u, &abort_flag) ||
-                !warp_wait(&aready[j % S_TM], (uint32_t)(j / S_TM) & 1u, &abort_flag)) {
-                ok = false;
-                break;
-            }
-            int cnt = 1;
-            if (C::ISS == 1 && lane == 0) {
-                while (cnt < C::MMA_BATCH && j + cnt < nk &&
-                       mbar_test_wait(&aready[(j + cnt) % S_TM], (uint32_t)((j + cnt) / S_TM) & 1u) &&
-                       mbar_test_wait(&xfull[(j + cnt) % S_X], (uint32_t)((j + cnt) / S_X) & 1u))
-                    cnt++;
-            }
-            cnt = __shfl_sync(0xffffffffu, cnt, 0);
-            __syncwarp();
-            tmem_fence_after();
-            if (elect_one()) {
-                for (int b = 0; b < cnt; b++) {
-                    const int jj = j + b * C::ISS, st = jj % S_X, a = jj % S_TM;
-                    const uint32_t xs = smem_u32(smem + C::x_off(st));
-#pragma unroll
-                    for (int kk = 0; kk < KSTEPS; kk++) {
-                        const uint32_t a_tmem = tmem + (uint32_t)(C::A_COL + a * C::A_SLOT + kk * 8);
-                        const uint64_t bd = sw128_desc(xs + (uint32_t)((kk >> 2) * C::NB * 128 + (kk & 3) * 32));
-                        const uint32_t first = (jj > iss || kk > 0) ? 1u : 0u;
-                        mma_f16_ts(d_hi, a_tmem, bd, idesc_hi, first);
-                        mma_f16_ts(d_lo, a_tmem + 64u, bd, idesc_lo, C::DUALD ? first : 1u);
-                    }
-                    mma_commit(&mdone[st]);  // frees the X stage and (S_TM | S_X) the A slot
+    // Roles by warpgroup (an SK register split applies to whole warpgroups
+    // and must dominate only their code): warps 0-3 produce and issue,
+    // 4 .. EPI_WARP0-1 dequantize, the SK epilogue warpgroup drains.
+    if (warp < 4) {
+        if constexpr (SK) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(C::REG_CTRL));
+        if (warp == 0) {
+            // ---------------- weight producer.  The weights do not depend on the
+            // previous kernel, so (launched as a programmatic dependent) this CTA
+            // streams them while the kernel producing X may still be running.
+            if (lane == 0) {
+                for (int j = 0; j < nk; j++) {
+                    const int st = j % S_W;
+                    if (j >= S_W && !mbar_wait(&wempty[st], ((uint32_t)(j / S_W) & 1u) ^ 1u, &abort_flag, 64)) break;
+                    int row0, kst;
+                    stage_at(j, row0, kst);
+                    mbar_expect_tx(&wfull[st], (uint32_t)(C::W_STAGE + C::S_STAGE));
+                    tma_load_2d(smem + C::w_off(st), &wmap, &wfull[st], kst * BK / 2, row0);
+                    tma_load_2d(smem + C::s_off(st), &smap, &wfull[st], 8 * (kst >> 1), row0);
                 }
             }
+        } else if (warp == 2) {
+            // ---------------- X producer (after the grid dependency)
+            if (lane == 0) {
+                grid_dependency_wait();
+                for (int j = 0; j < nk; j++) {
+                    const int st = j % S_X;
+                    if (j >= S_X && !mbar_wait(&mdone[st], ((uint32_t)(j / S_X) & 1u) ^ 1u, &abort_flag, 64)) break;
+                    mbar_expect_tx(&xfull[st], (uint32_t)C::X_STAGE);
+                    uint8_t* xs = smem + C::x_off(st);
+                    int row0, kst;
+                    stage_at(j, row0, kst);
+                    const int kk = kst * BK;
+                    // K half h of the stage holds NB rows: the tile's hi rows
+                    // (columns [0, K) of the activation rows), then its lo rows
+                    // (columns [K, 2K)); rows past the last token read as zeros
+    #pragma unroll
+                    for (int h = 0; h < 2; h++)
+    #pragma unroll
+                        for (int p = 0; p < 2; p++)
+                            tma_load_2d(xs + (h * C::NB + p * TN) * 128, &xmap, &xfull[st], p * K + kk + 64 * h, t0);
+                }
+            }
+        } else if (warp == 1 || (C::ISS == 2 && warp == 3)) {
+            // ---------------- MMA issuer(s): the whole warp runs the loop and its
+            // waits; one elected lane issues each batch of MMAs (a converged issue
+            // keeps the operands in uniform registers: ~40 cycles per MMA instead
+            // of ~110 from a lone lane).  Issuer i takes the stages j = i, i + ISS,
+            // ... into its accumulator D_i.  A single issuer takes every stage that
+            // is already dequantized (and whose X has landed) when the oldest one
+            // is, up to MMA_BATCH, under one wait + fence.  Per 16-wide K step:
+            // hi weights x [x_hi; x_lo] into D_i, lo weights x x_hi into D_lo (or
+            // into D_i's hi-token half).
+            // Phases: an issuer's aready / xfull wait for stage j must find the
+            // barrier's previous phase (stage j - S_TM, resp. j - S_X) complete.
+            // With one issuer that stage was its own.  With two, stage j - S_X
+            // (S_X even) is its own; stage j - S_TM may be the other issuer's, so
+            // the issuer first waits for that stage's MMAs (mdone), which follow
+            // its aready.  The next phases need this issuer's MMA of stage j.
+            constexpr uint32_t idesc_hi = make_idesc(C::NB);  // hi weights x (hi, lo) tokens
+            constexpr uint32_t idesc_lo = make_idesc(TN);     // lo weights x hi tokens
+            constexpr int KSTEPS = BK / 16;
+            const int iss = warp == 1 ? 0 : 1;
+            const uint32_t d_hi = tmem + (uint32_t)(iss * C::D_COLS);
+            const uint32_t d_lo = d_hi + (uint32_t)(C::DUALD ? C::NB : 0);
+            bool ok = true;
+            if constexpr (SK) {
+                // one piece per tile of the run: the issuer's stages of the piece
+                // (every other one, from its first, jf) accumulate from zero;
+                // before a piece's first MMA the epilogue has read the last one
+                const int tb = sk_b / nk_all, te = (sk_e - 1) / nk_all;
+                for (int tp = tb; tp <= te && ok; tp++) {
+                    const int p = tp - tb;
+                    const int ps = max(sk_b, tp * nk_all) - sk_b;
+                    const int pe = min(sk_e, (tp + 1) * nk_all) - sk_b;
+                    if (p > 0 && !warp_wait(dempty, (uint32_t)(p - 1) & 1u, &abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    const int jf = ps + ((ps ^ iss) & 1);
+                    for (int j = jf; j < pe; j += 2) {
+                        if (((S_TM & 1) && j >= S_TM &&
+                             !warp_wait(&mdone[(j - S_TM) % S_X], (uint32_t)((j - S_TM) / S_X) & 1u, &abort_flag)) ||
+                            !warp_wait(&xfull[j % S_X], (uint32_t)(j / S_X) & 1u, &abort_flag) ||
+                            !warp_wait(&aready[j % S_TM], (uint32_t)(j / S_TM) & 1u, &abort_flag)) {
+                            ok = false;
+                            break;
+                        }
+                        __syncwarp();
+                        tmem_fence_after();
+                        if (elect_one()) {
+                            const int st = j % S_X, a = j % S_TM;
+                            const uint32_t xs = smem_u32(smem + C::x_off(st));
+    #pragma unroll
+                            for (int kk = 0; kk < KSTEPS; kk++) {
+                                const uint32_t a_tmem = tmem + (uint32_t)(C::A_COL + a * C::A_SLOT + kk * 8);
+                                const uint64_t bd = sw128_desc(xs + (uint32_t)((kk >> 2) * C::NB * 128 + (kk & 3) * 32));
+                                const uint32_t acc = (j > jf || kk > 0) ? 1u : 0u;
+                                mma_f16_ts(d_hi, a_tmem, bd, idesc_hi, acc);
+                                mma_f16_ts(d_lo, a_tmem + 64u, bd, idesc_lo, 1u);
+                            }
+                            mma_commit(&mdone[st]);
+                        }
+                        __syncwarp();
+                    }
+                    if (ok && elect_one()) mma_commit(dfull);  // also when the piece had no stage of this issuer
+                    __syncwarp();
+                }
+            } else
+            for (int j = iss; j < nk;) {
+                if ((C::ISS == 2 && (S_TM & 1) && j >= S_TM &&
+                     !warp_wait(&mdone[(j - S_TM) % S_X], (uint32_t)((j - S_TM) / S_X) & 1u, &abort_flag)) ||
+                    !warp_wait(&xfull[j % S_X], (uint32_t)(j / S_X) & 1u, &abort_flag) ||
+                    !warp_wait(&aready[j % S_TM], (uint32_t)(j / S_TM) & 1u, &abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                int cnt = 1;
+                if (C::ISS == 1 && lane == 0) {
+                    while (cnt < C::MMA_BATCH && j + cnt < nk &&
+                           mbar_test_wait(&aready[(j + cnt) % S_TM], (uint32_t)((j + cnt) / S_TM) & 1u) &&
+                           mbar_test_wait(&xfull[(j + cnt) % S_X], (uint32_t)((j + cnt) / S_X) & 1u))
+                        cnt++;
+                }
+                cnt = __shfl_sync(0xffffffffu, cnt, 0);
+                __syncwarp();
+                tmem_fence_after();
+                if (elect_one()) {
+                    for (int b = 0; b < cnt; b++) {
+                        const int jj = j + b * C::ISS, st = jj % S_X, a = jj % S_TM;
+                        const uint32_t xs = smem_u32(smem + C::x_off(st));
+    #pragma unroll
+                        for (int kk = 0; kk < KSTEPS; kk++) {
+                            const uint32_t a_tmem = tmem + (uint32_t)(C::A_COL + a * C::A_SLOT + kk * 8);
+                            const uint64_t bd = sw128_desc(xs + (uint32_t)((kk >> 2) * C::NB * 128 + (kk & 3) * 32));
+                            const uint32_t first = (jj > iss || kk > 0) ? 1u : 0u;
+                            mma_f16_ts(d_hi, a_tmem, bd, idesc_hi, first);
+                            mma_f16_ts(d_lo, a_tmem + 64u, bd, idesc_lo, C::DUALD ? first : 1u);
+                        }
+                        mma_commit(&mdone[st]);  // frees the X stage and (S_TM | S_X) the A slot
+                    }
+                }
+                __syncwarp();
+                j += cnt * C::ISS;
+            }
+            if (!SK && ok && elect_one()) mma_commit(dfull);  // also when this issuer had no stage
             __syncwarp();
-            j += cnt * C::ISS;
         }
-        if (ok && elect_one()) mma_commit(dfull);  // also when this issuer had no stage
-        __syncwarp();
-    } else if (warp >= 4) {
+    } else if (warp < C::EPI_WARP0) {
+        if constexpr (SK) asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(C::REG_DEQ));
         // ---------------- dequant: thread <-> weight row (TMEM lane).  The
         // dequant warpgroups form RR groups; group g converts the stages j
         // with j % RR == g (each of its WG_PER warpgroups 4 / WG_PER of the
@@ -438,7 +562,10 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
                 break;
             }
             // the stage's 4 scales of row r (the scale box holds the stage pair's 8)
-            const uint2 sc = *reinterpret_cast<const uint2*>(smem + C::s_off(st) + r * 16 + ((it0 + j) & 1) * 8);
+            // K stage parity (which half of the scale box): stages per tile
+            // are even (K % 256 == 0), so the unit's parity in an SK run
+            const int kpar = ((SK ? sk_b : it0) + j) & 1;
+            const uint2 sc = *reinterpret_cast<const uint2*>(smem + C::s_off(st) + r * 16 + kpar * 8);
             const uint8_t* wrow = smem + C::w_off(st) + r * (BK / 2);  // 64-byte rows of nibbles
             // hi weights of block b at columns [16 b, 16 b + 16) of the slot, lo weights 64 further
             const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(C::A_COL + a * C::A_SLOT);
@@ -475,8 +602,8 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
             __syncwarp();
             if (lane == 0) mbar_arrive(&aready[a]);
         }
-        // ---------------- epilogue (first warpgroup)
-        if (wg == 0) {
+        // ---------------- epilogue (first warpgroup; SK: its own warpgroup)
+        if (!SK && wg == 0) {
             epi_ok = __all_sync(0xffffffffu, ok) && warp_wait(dfull, 0, &abort_flag);
             grid_dependency_wait();  // y and the residual may be touched by the previous kernel
             // Every load of a 16-token chunk (residuals) is issued before the
@@ -530,6 +657,128 @@ __global__ void __launch_bounds__(Cfg<TN>::THREADS, Cfg<TN>::MIN_BLOCKS)
                     if (row_ok && tl > 0)
                         store_chunk(ys + (size_t)(t0 + c0) * ldy + n, ldy, v, tl,
                                     add ? res + (size_t)(t0 + c0) * ldres + n : nullptr, ldres);
+                }
+            }
+        }
+    } else if (SK) {
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(C::REG_EPI));
+        // ---------------- SK epilogue warpgroup.  Per piece: drain the
+        // accumulators (the warp's TMEM lane quarter = its 32 weight rows) and
+        // release them to the issuers; a piece that does not start its tile
+        // goes to this CTA's workspace slot ([TN][BM] floats) under the flag
+        // of (CTA, quarter); the owner piece adds the slots of the CTAs that
+        // hold the rest of the tile, in K order, then runs the epilogue.
+        // Every warp takes the same pieces and branches (the SiLU barriers).
+        grid_dependency_wait();  // y, the residual and the workspace may be in use by the previous kernel
+        const int q = warp & 3, r = q * 32 + lane;
+        const int G = (int)gridDim.x, cta = (int)blockIdx.x;
+        const int tb = sk_b / nk_all, te = (sk_e - 1) / nk_all;
+        float* acc = reinterpret_cast<float*>(smem + C::xb_off());  // [TN][BM]: token t of row r at t * BM + r
+        bool ok = true;
+        for (int tp = tb; tp <= te; tp++) {
+            const int p = tp - tb;
+            const int us = max(sk_b, tp * nk_all), ue = min(sk_e, (tp + 1) * nk_all);
+            const int len = ue - us, ps = us - sk_b;
+            const bool has[2] = {len >= 2 || (ps & 1) == 0, len >= 2 || (ps & 1) == 1};
+            const bool owner = us == tp * nk_all;
+            // the owner: CTAs cta + 1 .. last hold the rest of the tile; they
+            // published it early in their runs, so it is summed into acc
+            // while this piece's MMAs still run (then acc += this piece)
+            const int last = owner ? ((tp + 1) * nk_all * G + sk_u - 1) / sk_u - 1 : cta;
+            for (int cc = cta + 1; cc <= last && ok; cc++) {
+                ok = sk_flag_wait(sk_flag + cc * 4 + q, &abort_flag);
+                if (ok) {
+                    const float* slot = sk_part + (size_t)cc * TN * BM;
+#pragma unroll
+                    for (int c = 0; c < TN / EPI_CH; c++) {
+                        float w[EPI_CH];
+#pragma unroll
+                        for (int jj = 0; jj < EPI_CH; jj++) w[jj] = slot[(c * EPI_CH + jj) * BM + r];
+#pragma unroll
+                        for (int jj = 0; jj < EPI_CH; jj++) {
+                            float* o = acc + (c * EPI_CH + jj) * BM + r;
+                            *o = cc == cta + 1 ? w[jj] : *o + w[jj];
+                        }
+                    }
+                    __syncwarp();
+                    if (lane == 0) sk_flag_set(sk_flag + cc * 4 + q, 0);
+                }
+            }
+            // (tens of microseconds per piece: the warps sleep between polls
+            // rather than take issue slots from the dequant warps)
+            ok = ok && __all_sync(0xffffffffu, mbar_wait(dfull, (uint32_t)p & 1u, &abort_flag, 128));
+            if (ok) {
+                // acc (+)= (D_0 hi + lo) + (D_1 hi + lo) of the issuers that had stages
+                tmem_fence_after();
+                const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
+#pragma unroll
+                for (int i = 0; i < 2; i++) {
+                    if (!has[i]) continue;
+                    const bool first = last == cta && (i == 0 || !has[0]);
+#pragma unroll
+                    for (int c = 0; c < TN / EPI_CH; c++) {
+                        uint32_t a[EPI_CH], b[EPI_CH];
+                        const uint32_t base = lane_base + (uint32_t)(i * C::D_COLS + c * EPI_CH);
+                        tmem_ld_x16(base, a);
+                        tmem_ld_x16(base + (uint32_t)TN, b);
+                        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+                        for (int jj = 0; jj < EPI_CH; jj++) {
+                            const float d = __uint_as_float(a[jj]) + __uint_as_float(b[jj]);
+                            float* o = acc + (c * EPI_CH + jj) * BM + r;
+                            *o = first ? d : *o + d;
+                        }
+                    }
+                }
+                tmem_fence_before();
+            }
+            __syncwarp();
+            if (ok && lane == 0) mbar_arrive(dempty);
+            if (!owner) {  // a later part of a tile that an earlier CTA owns
+                if (ok) {
+                    float* slot = sk_part + (size_t)cta * TN * BM;
+#pragma unroll 8
+                    for (int t = 0; t < TN; t++) slot[t * BM + r] = acc[t * BM + r];
+                    __threadfence();
+                    __syncwarp();
+                    if (lane == 0) sk_flag_set(sk_flag + cta * 4 + q, 1);
+                }
+                continue;
+            }
+            const int n = tp * BM + r;
+            if (epi == EPI_SILU) {
+                // rows [0, 64) of the tile are gate rows, [64, 128) the
+                // matching up rows: thread e writes column tp * 64 + (e & 63)
+                // for the tokens [16 (e >> 6), + 16)
+                named_sync(1, 128);  // every row of acc is in
+                const int e = threadIdx.x - C::EPI_WARP0 * 32;
+                const int orow = e & (GU_BLOCK - 1), half = e >> 6;
+                const int col = tp * GU_BLOCK + orow;
+                const size_t ncols = (size_t)N / 2;
+                if (ok) {
+#pragma unroll 1
+                    for (int k = 0; k < TN / 2; k++) {
+                        const int t = half * (TN / 2) + k;
+                        if (t < T) {
+                            const float o = __fmul_rn(silu_f(acc[t * BM + orow]), acc[t * BM + orow + GU_BLOCK]);
+                            y[(size_t)t * ldy + col] = o;
+                            if (y16) store_x16(y16 + (size_t)t * 2 * ncols, (int)ncols, col, o);
+                        }
+                    }
+                }
+                named_sync(1, 128);  // before the next piece overwrites acc
+            } else if (ok && n < N) {
+                const bool add = epi == EPI_ADD && res && !split_stride;
+#pragma unroll 1
+                for (int c = 0; c < TN / EPI_CH; c++) {
+                    const int tl = min(EPI_CH, T - c * EPI_CH);
+                    if (tl > 0) {
+                        uint32_t v[EPI_CH];
+#pragma unroll
+                        for (int jj = 0; jj < EPI_CH; jj++) v[jj] = __float_as_uint(acc[(c * EPI_CH + jj) * BM + r]);
+                        store_chunk(y + (size_t)(c * EPI_CH) * ldy + n, ldy, v, tl,
+                                    add ? res + (size_t)(c * EPI_CH) * ldres + n : nullptr, ldres);
+                    }
                 }
             }
         }
@@ -669,6 +918,10 @@ struct GemmWorkspace {
     std::map<std::tuple<const void*, const void*, size_t, size_t>, std::pair<CUtensorMap, CUtensorMap>> wmaps;
     // [token tile 32/64/128][splits] -> CTAs resident at once (0: not yet queried)
     int slots[3][MAX_SPLITS + 1] = {};
+    // stream-K: one [32][BM] partial slot and 4 flags per CTA (sk_cap CTAs)
+    float* sk_part = nullptr;
+    int* sk_flag = nullptr;
+    int sk_cap = 0;
 };
 
 GemmWorkspace* gemm_workspace_new() { return new GemmWorkspace(); }
@@ -677,6 +930,8 @@ void gemm_workspace_free(GemmWorkspace* ws) {
     if (!ws) return;
     if (ws->xh) cudaFree(ws->xh);
     if (ws->err) cudaFree(ws->err);
+    if (ws->sk_part) cudaFree(ws->sk_part);
+    if (ws->sk_flag) cudaFree(ws->sk_flag);
     delete ws;
 }
 
@@ -691,9 +946,9 @@ namespace {
 // Dynamic shared memory of a launch.  A CTA (512 tensor-memory columns) asks
 // for at least 116 KB, so it is alone on its SM and its tensor-memory
 // allocation never waits for another CTA of this kernel.
-template <int TN>
+template <int TN, bool SK = false>
 int launch_smem() {
-    using C = Cfg<TN>;
+    using C = Cfg<TN, SK>;
     return C::smem() < 118784 ? 118784 : C::smem();
 }
 
@@ -733,18 +988,25 @@ int resident_ctas(int sp) {
     return nc * sp;
 }
 
-template <int TN>
+// SK: a stream-K grid of sk_grid CTAs (at most one per SM, so all of them
+// are resident together and a tile's owner can wait for the others' flags)
+// with its workspace; splits must then be 1.
+template <int TN, bool SK = false>
 int launch_tc(const hc_q4_matrix& w, const CUtensorMap& xmap, const CUtensorMap& wmap, const CUtensorMap& smap,
               size_t T, float* y,
               size_t ldy, int epi, const float* res, size_t ldres, int splits, int* err, cudaStream_t s,
-              size_t split_stride = 0, __half* y16 = nullptr) {
-    using C = Cfg<TN>;
-    auto kfn = k_q4_gemm_tc<TN>;
-    const int smem = launch_smem<TN>();
+              size_t split_stride = 0, __half* y16 = nullptr, float* sk_part = nullptr, int* sk_flag = nullptr,
+              int sk_grid = 0) {
+    using C = Cfg<TN, SK>;
+    auto kfn = k_q4_gemm_tc<TN, SK>;
+    const int smem = launch_smem<TN, SK>();
     HC_CUDA(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     HC_CHECK(splits >= 1 && splits <= MAX_SPLITS, HC_ERR_INVALID, "tcgen05 GEMM: %d K splits", splits);
+    HC_CHECK(!SK || (splits == 1 && T <= (size_t)TN && sk_grid >= 1 && sk_part && sk_flag), HC_ERR_INVALID,
+             "tcgen05 GEMM: stream-K launch arguments");
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)((w.n + BM - 1) / BM), (unsigned)((T + TN - 1) / TN), (unsigned)splits);
+    cfg.gridDim = SK ? dim3((unsigned)sk_grid)
+                     : dim3((unsigned)((w.n + BM - 1) / BM), (unsigned)((T + TN - 1) / TN), (unsigned)splits);
     cfg.blockDim = dim3(C::THREADS);
     cfg.dynamicSmemBytes = (size_t)smem;
     cfg.stream = s;
@@ -765,7 +1027,7 @@ int launch_tc(const hc_q4_matrix& w, const CUtensorMap& xmap, const CUtensorMap&
     cfg.attrs = attr;
     cfg.numAttrs = (unsigned)na;
     HC_CUDA(cudaLaunchKernelEx(&cfg, kfn, xmap, wmap, smap, y, ldy, res, ldres, epi, (int)w.n,
-                               (int)w.k, (int)T, splits, split_stride, y16, err));
+                               (int)w.k, (int)T, splits, split_stride, y16, err, sk_part, sk_flag));
     hc_count_launch();
     return HC_OK;
 }
@@ -779,7 +1041,7 @@ int launch_tc(const hc_q4_matrix& w, const CUtensorMap& xmap, const CUtensorMap&
 // With max_part > 0 the splits are not reduced in a cluster but written as
 // slabs the caller adds (up to max_part of them): no cluster residency limit,
 // and each extra slab costs the consumer about half a stage of reading.
-int choose_splits(size_t tiles, size_t nk, const int* slots, int nsm, int max_part = 0) {
+int choose_splits(size_t tiles, size_t nk, const int* slots, int nsm, int max_part = 0, double* cost_out = nullptr) {
     const double fixed = 10.0;
     const int max_sp = max_part > 0 ? std::min(max_part, MAX_SPLITS) : MAX_SPLITS;
     int best = 1;
@@ -800,7 +1062,21 @@ int choose_splits(size_t tiles, size_t nk, const int* slots, int nsm, int max_pa
             best = (int)sp;
         }
     }
+    if (cost_out) *cost_out = best_cost;
     return best;
+}
+
+// Stream-K on the same scale: every CTA of the grid (one per SM) pays the
+// fixed cost once and takes ceil(U / G) stages; a piece boundary costs the
+// issuers a wait for the accumulator drain (~1.5 stages), and a tile's owner
+// adds the partials of the CTAs that hold the rest of it one after another
+// (~0.75 stages each).  Taken when it beats the best tile-per-CTA launch by
+// at least two stages.
+double stream_k_cost(size_t tiles, size_t nk, int nsm) {
+    const size_t U = tiles * nk, G = std::min<size_t>((size_t)nsm, U);
+    const size_t per = (U + G - 1) / G;
+    const size_t others = (nk - 1 + per - 1) / per;  // CTAs after the owner on one tile, at most
+    return 10.0 + (double)per + 1.5 + 0.75 * (double)others;
 }
 
 template <int TN>
@@ -824,6 +1100,9 @@ int gemm_tc_impl(GemmWorkspace* ws, const hc_q4_matrix& w, const float* x, size_
         ws->xh = nullptr;
         ws->xh_cap = 0;
         ws->err = nullptr;
+        ws->sk_part = nullptr;
+        ws->sk_flag = nullptr;
+        ws->sk_cap = 0;
         ws->wmaps.clear();
         for (auto& row : ws->slots)
             for (int& v : row) v = 0;
@@ -832,6 +1111,20 @@ int gemm_tc_impl(GemmWorkspace* ws, const hc_q4_matrix& w, const float* x, size_
     if (!ws->err) {
         HC_CUDA(cudaMalloc((void**)&ws->err, sizeof(int)));
         HC_CUDA(cudaMemset(ws->err, 0, sizeof(int)));
+    }
+    int nsm = 148;
+    HC_CUDA(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
+    if (ws->sk_cap < nsm) {  // with the error flag, on the first (eager) call
+        if (ws->sk_part) cudaFree(ws->sk_part);
+        if (ws->sk_flag) cudaFree(ws->sk_flag);
+        ws->sk_part = nullptr;
+        ws->sk_flag = nullptr;
+        ws->sk_cap = 0;
+        HC_CUDA(cudaMalloc((void**)&ws->sk_part, (size_t)nsm * 32 * BM * sizeof(float)));
+        HC_CUDA(cudaMalloc((void**)&ws->sk_flag, (size_t)nsm * 4 * sizeof(int)));
+        HC_CUDA(cudaMemset(ws->sk_flag, 0, (size_t)nsm * 4 * sizeof(int)));
+        ws->sk_cap = nsm;
+        ws->generation++;
     }
     if (!xh_ready && 2 * T * K > ws->xh_cap) {  // hi and lo rows
         if (ws->xh) cudaFree(ws->xh);
@@ -862,18 +1155,29 @@ int gemm_tc_impl(GemmWorkspace* ws, const hc_q4_matrix& w, const float* x, size_
         HC_TRY(encode_weight_maps(w, &wmap, &smap));
         if (w.owns) ws->wmaps[key] = std::make_pair(wmap, smap);
     }
-    int nsm = 148;
-    HC_CUDA(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
     size_t tiles = ((w.n + BM - 1) / BM) * ((T + tn - 1) / tn);
     const size_t nk = K / BK;
     const size_t stride = max_part > 0 ? T * ldy : 0;  // slab stride in partial mode
     const bool one = epi == EPI_SILU;                  // the SiLU epilogue needs whole sums
     int splits = 1;
     switch (tn) {
-        case 32:
-            if (!one) splits = choose_splits(tiles, nk, tile_slots<32>(ws, 0), nsm, max_part);
-            HC_TRY(launch_tc<32>(w, xmap, wmap, smap, T, y, ldy, epi, res, ldres, splits, ws->err, s, stride, y16));
+        case 32: {
+            double cost = 0.0;
+            if (!one)
+                splits = choose_splits(tiles, nk, tile_slots<32>(ws, 0), nsm, max_part, &cost);
+            else
+                cost = (double)((tiles + nsm - 1) / nsm) * (10.0 + (double)nk);
+            if (tiles * nk * (size_t)nsm < ((size_t)1 << 31) && stream_k_cost(tiles, nk, nsm) + 2.0 < cost) {  // one slab (partial mode) or the whole product
+                splits = 1;
+                const int g = (int)std::min<size_t>((size_t)nsm, tiles * nk);
+                HC_TRY((launch_tc<32, true>(w, xmap, wmap, smap, T, y, ldy, epi, res, ldres, 1, ws->err, s, stride,
+                                            y16, ws->sk_part, ws->sk_flag, g)));
+            } else {
+                HC_TRY(launch_tc<32>(w, xmap, wmap, smap, T, y, ldy, epi, res, ldres, splits, ws->err, s, stride,
+                                     y16));
+            }
             break;
+        }
         case 64:
             if (!one) splits = choose_splits(tiles, nk, tile_slots<64>(ws, 1), nsm, max_part);
             HC_TRY(launch_tc<64>(w, xmap, wmap, smap, T, y, ldy, epi, res, ldres, splits, ws->err, s, stride, y16));
@@ -915,6 +1219,9 @@ int* gemm_error_flag(GemmWorkspace* ws) {
         ws->xh = nullptr;
         ws->xh_cap = 0;
         ws->err = nullptr;
+        ws->sk_part = nullptr;
+        ws->sk_flag = nullptr;
+        ws->sk_cap = 0;
         ws->wmaps.clear();
         for (auto& row : ws->slots)
             for (int& v : row) v = 0;

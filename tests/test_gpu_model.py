@@ -240,6 +240,45 @@ def test_c4_geometry_batched_decode(cuda_device, kv_dtype):
         toks = nxt
 
 
+# More 128-row weight tiles than SMs in the fused gate/up projection (160)
+# and in the LM head (160): at decode batches of up to 32 rows both run the
+# stream-K GEMM (a CTA per SM, runs of (tile, K stage) units, partial tiles
+# added by the tile's owner), the gate/up one with the SiLU epilogue.
+WIDE_MLP = dict(hidden=256, layers=1, heads=4, kv_heads=2, inter=10240, vocab=20480, theta=10000.0,
+                max_pos=256, embed="q4", lm_head="separate")
+
+
+@pytest.mark.parametrize("n_seqs", [3, 32])
+def test_stream_k_decode(cuda_device, n_seqs):
+    from hypno_b200 import synth as sy
+    img = sy.build_image(WIDE_MLP, seed=5, quantize=orc.quantize_f32_to_q4_0)
+    m = engine.HypnoModel(img)
+    om = orc.OracleModel(img)
+    rng = np.random.default_rng(7 + n_seqs)
+    lens = [int(v) for v in rng.integers(1, 25, n_seqs)]
+    kv = engine.KVCache(m, n_seqs=n_seqs, max_pos=256, kv_dtype=engine.KV_FP16)
+    okvs, toks = [], []
+    for s, T in enumerate(lens):
+        p = sy.prompt_ids(WIDE_MLP["vocab"], T, seed=200 + s)
+        engine.batch_forward(m, p, kv, seq=s)
+        okv = om.new_kv(256)
+        r = orc.batch_forward(om, p, okv)
+        okvs.append(okv)
+        toks.append(orc.greedy(r))
+    seqs = list(range(n_seqs))
+    for step in range(3):
+        lg, am = engine.decode_step(m, kv, seqs, toks)
+        nxt = []
+        for s in seqs:
+            ref = orc.model_forward(om, toks[s], okvs[s])
+            assert rel_err(lg[s], ref) <= TOL, (step, s, rel_err(lg[s], ref))
+            assert int(am[s]) == orc.greedy(ref), (step, s, margin(ref))
+            nxt.append(int(am[s]))
+        toks = nxt
+    kv.close()
+    m.close()
+
+
 @pytest.mark.parametrize("n_seqs", [16, 40, 60, 120])
 def test_decode_attention_paths(cuda_device, n_seqs):
     """Batched decode over 16, 40, 60 and 120 sequences of a 2-KV-head model:
