@@ -1070,11 +1070,17 @@ int choose_splits(size_t tiles, size_t nk, const int* slots, int nsm, int max_pa
 // fixed cost once and takes ceil(U / G) stages; a piece boundary costs the
 // issuers a wait for the accumulator drain (~1.5 stages), and a tile's owner
 // adds the partials of the CTAs that hold the rest of it one after another
-// (~0.75 stages each).  Taken when it beats the best tile-per-CTA launch by
-// at least two stages.
+// (~0.75 stages each).  Only runs of at least one tile (per >= nk) qualify:
+// then a piece that does not start its tile is the first piece of its CTA
+// and shorter than a tile, so it is published well before its owner's last
+// piece ends; with shorter runs it can be a CTA's whole run, and the owner
+// waits for it at the end (the 112-tile gate/up of a 2-way tensor-parallel
+// c4 rank ran 27.5 µs as stream-K against 24.7 µs as one wave of tiles).
+// Taken when it beats the best tile-per-CTA launch by at least two stages.
 double stream_k_cost(size_t tiles, size_t nk, int nsm) {
     const size_t U = tiles * nk, G = std::min<size_t>((size_t)nsm, U);
     const size_t per = (U + G - 1) / G;
+    if (U / G < nk) return 1e300;
     const size_t others = (nk - 1 + per - 1) / per;  // CTAs after the owner on one tile, at most
     return 10.0 + (double)per + 1.5 + 0.75 * (double)others;
 }

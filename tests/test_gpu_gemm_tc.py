@@ -24,7 +24,9 @@ def rel_err(a, ref):
     return float(np.max(np.abs(a.astype(np.float64) - ref)) / max(1.0, float(np.max(np.abs(ref)))))
 
 
-@pytest.mark.parametrize("N,K", [(128, 128), (256, 512), (200, 256), (1152, 4096), (640, 14336)])
+# (38400, 512): 300 tiles of 4 stages over 148 SMs, so at <= 32 tokens the
+# launcher takes the stream-K grid (runs of 8-9 stages crossing tiles)
+@pytest.mark.parametrize("N,K", [(128, 128), (256, 512), (200, 256), (1152, 4096), (640, 14336), (38400, 512)])
 @pytest.mark.parametrize("T", [2, 8, 31, 32, 33, 64, 100, 128, 129, 256, 300])
 def test_tc_gemm_vs_oracle(cuda_device, N, K, T):
     import torch
