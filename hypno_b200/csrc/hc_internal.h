@@ -98,6 +98,14 @@ int launch_matmul(const DevWeight& w, const float* x, size_t ldx, size_t mtok, f
 bool residual_splits_norm_ok(size_t n, size_t ldh, size_t ldxn);
 int launch_residual_splits_norm(const float* part, int splits, size_t rows, size_t n, float* hidden, size_t ldh,
                                 const float* w, float eps, float* xn, size_t ldxn, __half* xn16, cudaStream_t s);
+// Single-token Q4_0 matvec y = W . RMSNorm(x) * norm_w (x one row of w.k
+// floats), with the norm computed inside the kernel; silu: W is a blocked
+// fused gate/up weight and y gets its w.n / 2 SiLU-gated outputs.  Only where
+// gemv1_fusable holds (Q4_0, k % 32 == 0, k <= 24576, 16-byte aligned x and
+// norm_w, whole gate/up blocks).
+bool gemv1_fusable(const DevWeight& w, const float* x, const float* norm_w, bool silu);
+int launch_gemv1_fused(const DevWeight& w, const float* x, float* y, const float* norm_w, float eps, bool silu,
+                       cudaStream_t s);
 int launch_rmsnorm(const float* x, size_t ldx, const float* w, float* out, size_t ldo, size_t rows,
                    size_t n, float eps, cudaStream_t s, __half* out16 = nullptr);
 int launch_softmax_rows(float* x, size_t rows, size_t n, cudaStream_t s);

@@ -255,12 +255,40 @@ constexpr int G1_XS = 9;
 // arithmetic; each x chunk (one word's 8 elements) is read once for the R
 // rows; the warp then sums its lanes in a fixed tree.
 template <int R, int U>
+// nw (may be null): x is first replaced by RMSNorm(x) * nw, computed by
+// every CTA with k_rmsnorm_v4's arithmetic (the single-token forward then
+// needs no separate norm kernel).  silu: the weight is a fused gate/up
+// weight in blocks of GU_BLOCK gate rows and their GU_BLOCK up rows; a
+// warp takes a gate row and its up row and writes y[i] = silu(gate) * up
+// (k_silu_mul's arithmetic) for the N / 2 outputs.
 __global__ void __launch_bounds__(G1_THREADS, 3) k_q4_gemv1(const uint4* __restrict__ qs, const __half* __restrict__ sc,
                                                          const float* __restrict__ x, float* __restrict__ y, int epi,
-                                                         const float* res, int N, int KB) {
+                                                         const float* res, int N, int KB,
+                                                         const float* __restrict__ nw, float eps, int silu) {
     extern __shared__ float4 xs4[];  // x' = x scaled per nibble position, KB x G1_XS float4
+    __shared__ float red[32];
+    float inv = 1.0f;
+    if (nw) {
+        float ss = 0.0f;
+        for (int i = threadIdx.x; i < KB * 8; i += G1_THREADS) {
+            const float4 v = __ldg(reinterpret_cast<const float4*>(x) + i);
+            ss = fmaf(v.x, v.x, ss);
+            ss = fmaf(v.y, v.y, ss);
+            ss = fmaf(v.z, v.z, ss);
+            ss = fmaf(v.w, v.w, ss);
+        }
+        ss = block_sum(ss, red);
+        inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)(KB * 32)), eps)));
+    }
     for (int i = threadIdx.x; i < KB * 8; i += G1_THREADS) {
         float4 v = __ldg(reinterpret_cast<const float4*>(x) + i);
+        if (nw) {
+            const float4 ww = __ldg(reinterpret_cast<const float4*>(nw) + i);
+            v.x = __fmul_rn(__fmul_rn(v.x, inv), ww.x);
+            v.y = __fmul_rn(__fmul_rn(v.y, inv), ww.y);
+            v.z = __fmul_rn(__fmul_rn(v.z, inv), ww.z);
+            v.w = __fmul_rn(__fmul_rn(v.w, inv), ww.w);
+        }
         // elements 4i..4i+3: positions (4i & 7) + 0..3 of a word
         // x 2^(23-4p): 2^23, 2^19, 2^15, 2^11, 2^7 for positions 0..4
         if ((i & 1) == 0) {  // word elements 0..3: positions 0 1 2 3
@@ -278,11 +306,12 @@ __global__ void __launch_bounds__(G1_THREADS, 3) k_q4_gemv1(const uint4* __restr
     }
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int groups = (N + R - 1) / R;
+    const int groups = silu ? N / 2 : (N + R - 1) / R;
     for (int g = blockIdx.x * (G1_THREADS / 32) + warp; g < groups; g += gridDim.x * (G1_THREADS / 32)) {
         int rows[R];
 #pragma unroll
-        for (int r = 0; r < R; r++) rows[r] = min(g * R + r, N - 1);
+        for (int r = 0; r < R; r++)
+            rows[r] = silu ? (g / GU_BLOCK) * (2 * GU_BLOCK) + g % GU_BLOCK + r * GU_BLOCK : min(g * R + r, N - 1);
         float acc[R];
 #pragma unroll
         for (int r = 0; r < R; r++) acc[r] = 0.0f;
@@ -329,7 +358,9 @@ __global__ void __launch_bounds__(G1_THREADS, 3) k_q4_gemv1(const uint4* __restr
         }
 #pragma unroll
         for (int r = 0; r < R; r++) acc[r] = warp_sum(acc[r]);
-        if (lane == 0) {
+        if (lane == 0 && silu) {
+            y[g] = __fmul_rn(silu_f(acc[0]), acc[1]);
+        } else if (lane == 0) {
 #pragma unroll
             for (int r = 0; r < R; r++) {
                 const int row = g * R + r;
@@ -442,12 +473,37 @@ static void launch_gemv(const hc_q4_matrix& w, const float* x, size_t ldx, size_
         unsigned grid = (unsigned)std::min<size_t>((groups + per_cta - 1) / per_cta, 148 * 3);
         if (smem > 48 * 1024)
             cudaFuncSetAttribute(k_q4_gemv1<2, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        k_q4_gemv1<2, 4><<<grid, G1_THREADS, smem, s>>>(w.qs, w.sc, x, y, epi, res, (int)w.n, (int)kb);
+        k_q4_gemv1<2, 4><<<grid, G1_THREADS, smem, s>>>(w.qs, w.sc, x, y, epi, res, (int)w.n, (int)kb, nullptr, 0.0f,
+                                                         0);
         return;
     }
     if (mtok == 1) launch_gemv_mt<1>(w, x, ldx, mtok, y, ldy, epi, res, ldres, s);
     else if (mtok <= 4) launch_gemv_mt<4>(w, x, ldx, mtok, y, ldy, epi, res, ldres, s);
     else launch_gemv_mt<8>(w, x, ldx, mtok, y, ldy, epi, res, ldres, s);
+}
+
+bool gemv1_fusable(const DevWeight& w, const float* x, const float* norm_w, bool silu) {
+    if (w.dtype != HC_DTYPE_Q4_0) return false;
+    const hc_q4_matrix& q = w.q4;
+    return q.k % 32 == 0 && q.k / 32 <= 768 && q.nblocks >= q.n * (q.k / 32) && ((uintptr_t)x & 15) == 0 &&
+           ((uintptr_t)norm_w & 15) == 0 && (!silu || q.n % (2 * GU_BLOCK) == 0);
+}
+
+int launch_gemv1_fused(const DevWeight& w, const float* x, float* y, const float* norm_w, float eps, bool silu,
+                       cudaStream_t s) {
+    HC_CHECK(gemv1_fusable(w, x, norm_w, silu), HC_ERR_INVALID, "fused single-token matvec: unsupported weight");
+    const hc_q4_matrix& q = w.q4;
+    const size_t kb = q.k / 32;
+    const size_t smem = kb * G1_XS * sizeof(float4);
+    const size_t groups = silu ? q.n / 2 : (q.n + 1) / 2;
+    const size_t per_cta = G1_THREADS / 32;
+    const unsigned grid = (unsigned)std::min<size_t>((groups + per_cta - 1) / per_cta, 148 * 3);
+    if (smem > 48 * 1024)
+        HC_CUDA(cudaFuncSetAttribute(k_q4_gemv1<2, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    k_q4_gemv1<2, 4><<<grid, G1_THREADS, smem, s>>>(q.qs, q.sc, x, y, EPI_STORE, nullptr, (int)q.n, (int)kb, norm_w, eps,
+                                                     silu ? 1 : 0);
+    HC_LAUNCH_CHECK();
+    return HC_OK;
 }
 
 int launch_matmul(const DevWeight& w, const float* x, size_t ldx, size_t mtok, float* y, size_t ldy, int epi,

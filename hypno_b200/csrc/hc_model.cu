@@ -802,7 +802,12 @@ int run_layers(hc_model* m, hc_kv* kv, size_t rows, bool prefill, int seq, int p
     if (tail_normed) *tail_normed = false;
     for (size_t li = 0; li < m->layers.size(); li++) {
         LayerW& L = m->layers[li];
-        if (!xn_ready) {
+        // one token: the qkv matvec applies the input norm itself and writes
+        // a single slab, which the RoPE kernel rotates and stores into the
+        // cache (three kernels fewer per layer with the gate/up one below)
+        const bool one = rows == 1 && s.split_part && !hc::gemm_tc_eligible(L.qkv.q4, rows);
+        const bool qkv_fused = one && !xn_ready && hc::gemv1_fusable(L.qkv, s.hidden, L.in_norm, false);
+        if (!xn_ready && !qkv_fused) {
             HC_TRY(phase(m, PH_NORM));
             HC_TRY(hc::launch_rmsnorm(s.hidden, H, L.in_norm, s.xn, H, rows, H, c.rms_norm_eps, m->stream, s.xn16));
         }
@@ -811,13 +816,19 @@ int run_layers(hc_model* m, hc_kv* kv, size_t rows, bool prefill, int seq, int p
         size_t lofs = li * kv->layer_stride * (kv->kv_fp16 ? 2 : 4);
         void* kc = (uint8_t*)kv->k + lofs;
         void* vc = (uint8_t*)kv->v + lofs;
-        if (s.split_part && rows <= kPartRows && L.qkv.dtype == HC_DTYPE_Q4_0 &&
-            hc::gemm_tc_eligible(L.qkv.q4, rows)) {
-            // decode sizes: K split over CTAs into slabs that the RoPE kernel
-            // adds, also storing k and v into the cache
+        const bool qkv_tc = s.split_part && rows <= kPartRows && L.qkv.dtype == HC_DTYPE_Q4_0 &&
+                            hc::gemm_tc_eligible(L.qkv.q4, rows);
+        if (qkv_tc || qkv_fused) {
+            // decode sizes: K split over CTAs into slabs (or the one-token
+            // matvec's single slab) that the RoPE kernel adds, also storing k
+            // and v into the cache
             int splits = 1;
-            HC_TRY(hc::gemm_tc_partials(m->gemm_ws, L.qkv.q4, s.xn, H, rows, s.split_part, kPartSplits, &splits,
-                                        m->stream, s.xn16));
+            if (qkv_tc)
+                HC_TRY(hc::gemm_tc_partials(m->gemm_ws, L.qkv.q4, s.xn, H, rows, s.split_part, kPartSplits, &splits,
+                                            m->stream, s.xn16));
+            else
+                HC_TRY(hc::launch_gemv1_fused(L.qkv, s.hidden, s.split_part, L.in_norm, c.rms_norm_eps, false,
+                                              m->stream));
             hc::KvStoreArgs ka;
             ka.kc = kc;
             ka.vc = vc;
@@ -947,13 +958,17 @@ int run_layers(hc_model* m, hc_kv* kv, size_t rows, bool prefill, int seq, int p
         }
         bool normed = false;
         HC_TRY(row_parallel(m, L.o, s.attn, nq, rows, s.attn16, PH_O, L.post_norm, &normed));
-        if (!normed) {
+        // one token: the gate/up matvec applies the norm and the SiLU gate
+        const bool gu_fused = one && !normed && L.gu_blocked && hc::gemv1_fusable(L.gu, s.hidden, L.post_norm, true);
+        if (!normed && !gu_fused) {
             HC_TRY(phase(m, PH_NORM));
             HC_TRY(hc::launch_rmsnorm(s.hidden, H, L.post_norm, s.xn, H, rows, H, c.rms_norm_eps, m->stream, s.xn16));
         }
         size_t im = L.gu.n / 2;
         HC_TRY(phase(m, PH_GATEUP));
-        if (s.split_part && rows <= kPartRows && L.gu_blocked && L.gu.n <= kGuSlabRows &&
+        if (gu_fused) {
+            HC_TRY(hc::launch_gemv1_fused(L.gu, s.hidden, s.act, L.post_norm, c.rms_norm_eps, true, m->stream));
+        } else if (s.split_part && rows <= kPartRows && L.gu_blocked && L.gu.n <= kGuSlabRows &&
             hc::gemm_tc_eligible(L.gu.q4, rows)) {
             // a narrow gate/up (a tensor-parallel rank's shard) has too few
             // 128-row tiles to fill the GPU, and the SiLU epilogue needs whole
@@ -1001,10 +1016,20 @@ int decode_dev_impl(hc_model* m, hc_kv* kv, const int* seqs_dev, const uint32_t*
     HC_TRY(run_layers(m, kv, (size_t)B, false, 0, 0, m->final_norm, &final_normed));
     HC_TRY(phase(m, PH_NORM));
     HC_TRY(hc::launch_advance(s.seqs, kv->pos_dev, B, m->stream));
-    if (!final_normed)
+    // one token on one GPU: the LM head's matvec applies the final norm
+    const bool head_fused = !final_normed && B == 1 && c.tp_size <= 1 && m->lm_head.present &&
+                            !hc::gemm_tc_eligible(m->lm_head.q4, 1) &&
+                            hc::gemv1_fusable(m->lm_head, s.hidden, m->final_norm, false);
+    if (!final_normed && !head_fused)
         HC_TRY(hc::launch_rmsnorm(s.hidden, c.hidden_size, m->final_norm, s.xn, c.hidden_size, (size_t)B,
                                   c.hidden_size, c.rms_norm_eps, m->stream, s.xn16));
-    if (c.tp_size > 1 && !logits_dev && argmax_dev && m->lm_head.present) {
+    if (head_fused) {
+        float* logits = logits_dev ? logits_dev : s.logits;
+        HC_TRY(phase(m, PH_LMHEAD));
+        HC_TRY(hc::launch_gemv1_fused(m->lm_head, s.hidden, logits, m->final_norm, c.rms_norm_eps, false, m->stream));
+        HC_TRY(phase(m, PH_ARGMAX));
+        if (argmax_dev) HC_TRY(hc::launch_argmax(logits, (size_t)B, c.vocab_size, argmax_dev, m->stream));
+    } else if (c.tp_size > 1 && !logits_dev && argmax_dev && m->lm_head.present) {
         // greedy ids only: exchange (max, index) pairs instead of the logits
         HC_TRY(lm_head_argmax_tp(m, s.xn, (size_t)B, argmax_dev, s.xn16));
     } else {
