@@ -48,6 +48,7 @@ __device__ __forceinline__ float4 ld4<__half>(const __half* p) {
 template <typename KT>
 __global__ void __launch_bounds__(128) k_attention(AttnParams P) {
     pdl_trigger();
+    pdl_wait();
     extern __shared__ float smem[];
     const int row = blockIdx.x, h = blockIdx.y;
     const int hd = P.hd;
@@ -171,10 +172,10 @@ int launch_attention(const AttnParams& P, int rows, int kv_fp16, cudaStream_t s)
     dim3 grid((unsigned)rows, (unsigned)P.nh);
     if (kv_fp16) {
         if (smem > 48 * 1024) HC_CUDA(cudaFuncSetAttribute(k_attention<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        k_attention<__half><<<grid, 128, smem, s>>>(P);
+        HC_TRY(launch_pdl(k_attention<__half>, grid, dim3(128), smem, s, P));
     } else {
         if (smem > 48 * 1024) HC_CUDA(cudaFuncSetAttribute(k_attention<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        k_attention<float><<<grid, 128, smem, s>>>(P);
+        HC_TRY(launch_pdl(k_attention<float>, grid, dim3(128), smem, s, P));
     }
     HC_LAUNCH_CHECK();
     return HC_OK;
@@ -228,14 +229,15 @@ int launch_kv_store(const float* k, const float* v, size_t ld, int rows, int nkv
 // pos[seqs[b]] += 1 after a decode step (FlatKVCache::advance,
 // transformer.rs:158, 508-510).
 __global__ void k_advance(const int* __restrict__ seqs, int* __restrict__ pos, int B) {
+    pdl_trigger();
+    pdl_wait();
     int b = blockIdx.x * blockDim.x + threadIdx.x;
     if (b < B) pos[seqs[b]] += 1;
 }
 
 int launch_advance(const int* seqs, int* pos, int B, cudaStream_t s) {
     if (B == 0) return HC_OK;
-    k_advance<<<(B + 127) / 128, 128, 0, s>>>(seqs, pos, B);
-    HC_LAUNCH_CHECK();
+    HC_TRY(launch_pdl(k_advance, dim3((B + 127) / 128), dim3(128), 0, s, seqs, pos, B));
     return HC_OK;
 }
 

@@ -95,6 +95,12 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 // before it touches anything this grid writes.
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// The other side: a kernel launched as a programmatic dependent (launch_pdl)
+// may start while the previous kernel still runs; it calls this before its
+// first global memory access, which returns once that kernel has completed
+// and its writes are visible (a no-op for an ordinary launch).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ float block_sum(float v, float* red) {
     int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     v = warp_sum(v);

@@ -106,6 +106,26 @@ int launch_residual_splits_norm(const float* part, int splits, size_t rows, size
 bool gemv1_fusable(const DevWeight& w, const float* x, const float* norm_w, bool silu);
 int launch_gemv1_fused(const DevWeight& w, const float* x, float* y, const float* norm_w, float eps, bool silu,
                        cudaStream_t s);
+// Launches kfn as a programmatic dependent of the stream's previous kernel:
+// its CTAs may become resident while that kernel still runs, which hides the
+// launch gap of short dependent kernels (the single-token decode chain).
+// kfn must call pdl_wait() before its first global memory access.
+template <typename... KArgs, typename... Args>
+inline int launch_pdl(void (*kfn)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    HC_CUDA(cudaLaunchKernelEx(&cfg, kfn, args...));
+    return HC_OK;
+}
+
 int launch_rmsnorm(const float* x, size_t ldx, const float* w, float* out, size_t ldo, size_t rows,
                    size_t n, float eps, cudaStream_t s, __half* out16 = nullptr);
 int launch_softmax_rows(float* x, size_t rows, size_t n, cudaStream_t s);

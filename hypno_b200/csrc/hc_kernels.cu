@@ -265,6 +265,8 @@ __global__ void __launch_bounds__(G1_THREADS, 3) k_q4_gemv1(const uint4* __restr
                                                          const float* __restrict__ x, float* __restrict__ y, int epi,
                                                          const float* res, int N, int KB,
                                                          const float* __restrict__ nw, float eps, int silu) {
+    pdl_trigger();
+    pdl_wait();
     extern __shared__ float4 xs4[];  // x' = x scaled per nibble position, KB x G1_XS float4
     __shared__ float red[32];
     float inv = 1.0f;
@@ -462,8 +464,8 @@ static void launch_gemv_mt(const hc_q4_matrix& w, const float* x, size_t ldx, si
     }
 }
 
-static void launch_gemv(const hc_q4_matrix& w, const float* x, size_t ldx, size_t mtok, float* y, size_t ldy,
-                        int epi, const float* res, size_t ldres, cudaStream_t s) {
+static int launch_gemv(const hc_q4_matrix& w, const float* x, size_t ldx, size_t mtok, float* y, size_t ldy,
+                       int epi, const float* res, size_t ldres, cudaStream_t s) {
     const size_t kb = w.k / 32;
     if (mtok == 1 && kb <= 768) {
         // a few CTAs per SM, each staging x once and striding over row groups
@@ -473,13 +475,13 @@ static void launch_gemv(const hc_q4_matrix& w, const float* x, size_t ldx, size_
         unsigned grid = (unsigned)std::min<size_t>((groups + per_cta - 1) / per_cta, 148 * 3);
         if (smem > 48 * 1024)
             cudaFuncSetAttribute(k_q4_gemv1<2, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        k_q4_gemv1<2, 4><<<grid, G1_THREADS, smem, s>>>(w.qs, w.sc, x, y, epi, res, (int)w.n, (int)kb, nullptr, 0.0f,
-                                                         0);
-        return;
+        return launch_pdl(k_q4_gemv1<2, 4>, dim3(grid), dim3(G1_THREADS), smem, s, w.qs, w.sc, x, y, epi, res,
+                          (int)w.n, (int)kb, (const float*)nullptr, 0.0f, 0);
     }
     if (mtok == 1) launch_gemv_mt<1>(w, x, ldx, mtok, y, ldy, epi, res, ldres, s);
     else if (mtok <= 4) launch_gemv_mt<4>(w, x, ldx, mtok, y, ldy, epi, res, ldres, s);
     else launch_gemv_mt<8>(w, x, ldx, mtok, y, ldy, epi, res, ldres, s);
+    return HC_OK;
 }
 
 bool gemv1_fusable(const DevWeight& w, const float* x, const float* norm_w, bool silu) {
@@ -500,10 +502,8 @@ int launch_gemv1_fused(const DevWeight& w, const float* x, float* y, const float
     const unsigned grid = (unsigned)std::min<size_t>((groups + per_cta - 1) / per_cta, 148 * 3);
     if (smem > 48 * 1024)
         HC_CUDA(cudaFuncSetAttribute(k_q4_gemv1<2, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    k_q4_gemv1<2, 4><<<grid, G1_THREADS, smem, s>>>(q.qs, q.sc, x, y, EPI_STORE, nullptr, (int)q.n, (int)kb, norm_w, eps,
-                                                     silu ? 1 : 0);
-    HC_LAUNCH_CHECK();
-    return HC_OK;
+    return launch_pdl(k_q4_gemv1<2, 4>, dim3(grid), dim3(G1_THREADS), smem, s, q.qs, q.sc, x, y, (int)EPI_STORE,
+                      (const float*)nullptr, (int)q.n, (int)kb, norm_w, eps, silu ? 1 : 0);
 }
 
 int launch_matmul(const DevWeight& w, const float* x, size_t ldx, size_t mtok, float* y, size_t ldy, int epi,
@@ -514,7 +514,7 @@ int launch_matmul(const DevWeight& w, const float* x, size_t ldx, size_t mtok, f
         bool aligned = (q.k % 32 == 0) && (((uintptr_t)x & 15) == 0) && (ldx % 4 == 0) &&
                        (q.nblocks >= q.n * (q.k / 32));
         if (aligned) {
-            launch_gemv(q, x, ldx, mtok, y, ldy, epi, res, ldres, s);
+            HC_TRY(launch_gemv(q, x, ldx, mtok, y, ldy, epi, res, ldres, s));
         } else {
             size_t warps = q.n * mtok;
             k_q4_gemv_general<<<grid_for(warps * 32, 256), 256, 0, s>>>(q.qs, q.sc, q.nblocks, x, ldx, (int)mtok, y,
@@ -865,6 +865,8 @@ template <typename KT>
 __global__ void k_rope_rows_slabs(const float* __restrict__ part, int splits, size_t slab, float* __restrict__ x,
                                   size_t ldx, int width, int heads, int hd, const float2* __restrict__ cs, int cs_rows,
                                   const int* __restrict__ pos_dev, int pos0, KvStoreArgs kv) {
+    pdl_trigger();
+    pdl_wait();
     const int row = blockIdx.y;
     const int pos = pos_dev ? pos_dev[row] : pos0 + row;
     const bool rot_ok = pos >= 0 && pos < cs_rows;  // else the position is rejected elsewhere
@@ -934,13 +936,10 @@ int launch_rope_rows_slabs(const float* part, int splits, float* x, size_t ldx, 
     const size_t pairs = width / 2;
     const unsigned gx = (unsigned)std::min<size_t>((pairs + 127) / 128, 64);
     if (kv && k.kv_fp16)
-        k_rope_rows_slabs<__half><<<dim3(gx, (unsigned)rows), 128, 0, s>>>(
-            part, splits, rows * width, x, ldx, (int)width, (int)heads, (int)hd, cs, (int)cs_rows, pos_dev, pos0, k);
-    else
-        k_rope_rows_slabs<float><<<dim3(gx, (unsigned)rows), 128, 0, s>>>(
-            part, splits, rows * width, x, ldx, (int)width, (int)heads, (int)hd, cs, (int)cs_rows, pos_dev, pos0, k);
-    HC_LAUNCH_CHECK();
-    return HC_OK;
+        return launch_pdl(k_rope_rows_slabs<__half>, dim3(gx, (unsigned)rows), dim3(128), 0, s, part, splits,
+                          rows * width, x, ldx, (int)width, (int)heads, (int)hd, cs, (int)cs_rows, pos_dev, pos0, k);
+    return launch_pdl(k_rope_rows_slabs<float>, dim3(gx, (unsigned)rows), dim3(128), 0, s, part, splits, rows * width,
+                      x, ldx, (int)width, (int)heads, (int)hd, cs, (int)cs_rows, pos_dev, pos0, k);
 }
 
 // ============================================================ embedding
@@ -948,6 +947,8 @@ int launch_rope_rows_slabs(const float* part, int splits, float* x, size_t ldx, 
 __global__ void k_embed(uint32_t dtype, const void* __restrict__ dense, const uint4* __restrict__ qs,
                         const __half* __restrict__ sc, const uint32_t* __restrict__ ids, float* __restrict__ out,
                         int hidden) {
+    pdl_trigger();
+    pdl_wait();
     int b = blockIdx.y;
     size_t id = ids[b];
     float* o = out + (size_t)b * hidden;
@@ -980,9 +981,8 @@ int launch_embed(const DevWeight& emb, const uint32_t* ids, size_t B, float* out
         return HC_ERR_UNSUPPORTED;
     }
     unsigned gx = (unsigned)std::min<size_t>((hidden + 255) / 256, 32);
-    k_embed<<<dim3(gx, (unsigned)B), 256, 0, s>>>(emb.dtype, emb.dense, emb.q4.qs, emb.q4.sc, ids, out, (int)hidden);
-    HC_LAUNCH_CHECK();
-    return HC_OK;
+    return launch_pdl(k_embed, dim3(gx, (unsigned)B), dim3(256), 0, s, emb.dtype, emb.dense, emb.q4.qs, emb.q4.sc, ids,
+                      out, (int)hidden);
 }
 
 // ============================================================ argmax
@@ -992,6 +992,8 @@ int launch_embed(const DevWeight& emb, const uint32_t* ids, size_t B, float* out
 // vocabulary-sharded exchange of tensor parallelism.
 __global__ void k_argmax(const float* __restrict__ logits, int n, uint32_t* __restrict__ out,
                          float2* __restrict__ pairs = nullptr, uint32_t idx0 = 0) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ float sv[32];
     __shared__ int si[32];
     const float* l = logits + (size_t)blockIdx.x * n;
@@ -1057,16 +1059,13 @@ __global__ void k_argmax(const float* __restrict__ logits, int n, uint32_t* __re
 
 int launch_argmax_pairs(const float* logits, size_t rows, size_t n, uint32_t idx0, float2* pairs, cudaStream_t s) {
     if (rows == 0) return HC_OK;
-    k_argmax<<<(unsigned)rows, 1024, 0, s>>>(logits, (int)n, nullptr, pairs, idx0);
-    HC_LAUNCH_CHECK();
-    return HC_OK;
+    return launch_pdl(k_argmax, dim3((unsigned)rows), dim3(1024), 0, s, logits, (int)n, (uint32_t*)nullptr, pairs, idx0);
 }
 
 int launch_argmax(const float* logits, size_t rows, size_t n, uint32_t* out, cudaStream_t s) {
     if (rows == 0) return HC_OK;
-    k_argmax<<<(unsigned)rows, 1024, 0, s>>>(logits, (int)n, out);
-    HC_LAUNCH_CHECK();
-    return HC_OK;
+    return launch_pdl(k_argmax, dim3((unsigned)rows), dim3(1024), 0, s, logits, (int)n, out, (float2*)nullptr,
+                      (uint32_t)0);
 }
 
 // ============================================================ synthetic data

@@ -7,6 +7,7 @@
 #include "hc_attention.h"
 #include "hc_gemm.h"
 #include "hc_comm.h"
+#include "hc_common.cuh"
 
 #include <omp.h>
 
@@ -997,6 +998,8 @@ int run_layers(hc_model* m, hc_kv* kv, size_t rows, bool prefill, int seq, int p
 
 __global__ void k_gather_pos(const int* __restrict__ seqs, const int* __restrict__ pos, int* __restrict__ rowpos,
                              int B) {
+    hc::pdl_trigger();
+    hc::pdl_wait();
     int b = blockIdx.x * blockDim.x + threadIdx.x;
     if (b < B) rowpos[b] = pos[seqs[b]];
 }
@@ -1009,8 +1012,8 @@ int decode_dev_impl(hc_model* m, hc_kv* kv, const int* seqs_dev, const uint32_t*
     if (seqs_dev != s.seqs) HC_CUDA(cudaMemcpyAsync(s.seqs, seqs_dev, B * sizeof(int), cudaMemcpyDeviceToDevice, m->stream));
     if (ids_dev != s.ids) HC_CUDA(cudaMemcpyAsync(s.ids, ids_dev, B * sizeof(uint32_t), cudaMemcpyDeviceToDevice, m->stream));
     HC_TRY(phase(m, PH_EMBED));
-    k_gather_pos<<<(B + 127) / 128, 128, 0, m->stream>>>(s.seqs, kv->pos_dev, s.rowpos, B);
-    HC_LAUNCH_CHECK();
+    HC_TRY(hc::launch_pdl(k_gather_pos, dim3((B + 127) / 128), dim3(128), 0, m->stream, (const int*)s.seqs,
+                          (const int*)kv->pos_dev, s.rowpos, B));
     HC_TRY(hc::launch_embed(m->embed, s.ids, (size_t)B, s.hidden, c.hidden_size, m->stream));
     bool final_normed = false;
     HC_TRY(run_layers(m, kv, (size_t)B, false, 0, 0, m->final_norm, &final_normed));
