@@ -254,87 +254,103 @@ constexpr int G1_XS = 9;
 // l takes blocks l, l + 32, ... of the R rows, U blocks of loads before any
 // arithmetic; each x chunk (one word's 8 elements) is read once for the R
 // rows; the warp then sums its lanes in a fixed tree.
-template <int R, int U>
+// Elements 4i..4i+3 of x (word positions (4i & 7) + 0..3) times 2^(23-4p)
+// for nibble position p: 2^23, 2^19, 2^15, 2^11, 2^7 (exact).
+__device__ __forceinline__ float4 g1_prescale(float4 v, int i) {
+    if ((i & 1) == 0) {  // word elements 0..3: positions 0 1 2 3
+        v.x = __fmul_rn(v.x, 8388608.0f);
+        v.y = __fmul_rn(v.y, 524288.0f);
+        v.z = __fmul_rn(v.z, 32768.0f);
+        v.w = __fmul_rn(v.w, 2048.0f);
+    } else {             // word elements 4..7: positions 4 0 1 2
+        v.x = __fmul_rn(v.x, 128.0f);
+        v.y = __fmul_rn(v.y, 8388608.0f);
+        v.z = __fmul_rn(v.z, 524288.0f);
+        v.w = __fmul_rn(v.w, 32768.0f);
+    }
+    return v;
+}
+
 // nw (may be null): x is first replaced by RMSNorm(x) * nw, computed by
 // every CTA with k_rmsnorm_v4's arithmetic (the single-token forward then
 // needs no separate norm kernel).  silu: the weight is a fused gate/up
 // weight in blocks of GU_BLOCK gate rows and their GU_BLOCK up rows; a
 // warp takes a gate row and its up row and writes y[i] = silu(gate) * up
 // (k_silu_mul's arithmetic) for the N / 2 outputs.
+template <int R, int U>
 __global__ void __launch_bounds__(G1_THREADS, 3) k_q4_gemv1(const uint4* __restrict__ qs, const __half* __restrict__ sc,
                                                          const float* __restrict__ x, float* __restrict__ y, int epi,
                                                          const float* res, int N, int KB,
                                                          const float* __restrict__ nw, float eps, int silu) {
     pdl_trigger();
-    pdl_wait();
     extern __shared__ float4 xs4[];  // x' = x scaled per nibble position, KB x G1_XS float4
     __shared__ float red[32];
-    float inv = 1.0f;
-    if (nw) {
-        float ss = 0.0f;
-        for (int i = threadIdx.x; i < KB * 8; i += G1_THREADS) {
-            const float4 v = __ldg(reinterpret_cast<const float4*>(x) + i);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int groups = silu ? N / 2 : (N + R - 1) / R;
+    auto row_of = [&](int g, int r) {
+        return silu ? (g / GU_BLOCK) * (2 * GU_BLOCK) + g % GU_BLOCK + r * GU_BLOCK : min(g * R + r, N - 1);
+    };
+    // one batch of U blocks (lane + 32 u from b0) of the group's R rows
+    uint4 q[U][R];
+    float s[U][R];
+    auto load_batch = [&](int g, int b0) {
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int b = b0 + u * 32;
+#pragma unroll
+            for (int r = 0; r < R; r++) {
+                if (b < KB) {
+                    const size_t bi = (size_t)row_of(g, r) * KB + b;
+                    q[u][r] = __ldg(qs + bi);
+                    s[u][r] = __half2float(sc[bi]);
+                } else {
+                    q[u][r] = make_uint4(0x88888888u, 0x88888888u, 0x88888888u, 0x88888888u);
+                    s[u][r] = 0.0f;
+                }
+            }
+        }
+    };
+    // the weights do not depend on the previous kernel: the warp's first
+    // batch is in flight before the wait for it
+    const int g0 = blockIdx.x * (G1_THREADS / 32) + warp;
+    if (g0 < groups) load_batch(g0, lane);
+    pdl_wait();
+    // x, read once: staged raw while the sum of squares accumulates, then
+    // (with nw) normalized in place; each thread rewrites only its own
+    // elements
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < KB * 8; i += G1_THREADS) {
+        float4 v = __ldg(reinterpret_cast<const float4*>(x) + i);
+        if (nw) {
             ss = fmaf(v.x, v.x, ss);
             ss = fmaf(v.y, v.y, ss);
             ss = fmaf(v.z, v.z, ss);
             ss = fmaf(v.w, v.w, ss);
+        } else {
+            v = g1_prescale(v, i);
         }
-        ss = block_sum(ss, red);
-        inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)(KB * 32)), eps)));
+        xs4[(i >> 3) * G1_XS + (i & 7)] = v;
     }
-    for (int i = threadIdx.x; i < KB * 8; i += G1_THREADS) {
-        float4 v = __ldg(reinterpret_cast<const float4*>(x) + i);
-        if (nw) {
+    if (nw) {
+        ss = block_sum(ss, red);
+        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)(KB * 32)), eps)));
+        for (int i = threadIdx.x; i < KB * 8; i += G1_THREADS) {
+            float4 v = xs4[(i >> 3) * G1_XS + (i & 7)];
             const float4 ww = __ldg(reinterpret_cast<const float4*>(nw) + i);
             v.x = __fmul_rn(__fmul_rn(v.x, inv), ww.x);
             v.y = __fmul_rn(__fmul_rn(v.y, inv), ww.y);
             v.z = __fmul_rn(__fmul_rn(v.z, inv), ww.z);
             v.w = __fmul_rn(__fmul_rn(v.w, inv), ww.w);
+            xs4[(i >> 3) * G1_XS + (i & 7)] = g1_prescale(v, i);
         }
-        // elements 4i..4i+3: positions (4i & 7) + 0..3 of a word
-        // x 2^(23-4p): 2^23, 2^19, 2^15, 2^11, 2^7 for positions 0..4
-        if ((i & 1) == 0) {  // word elements 0..3: positions 0 1 2 3
-            v.x = __fmul_rn(v.x, 8388608.0f);
-            v.y = __fmul_rn(v.y, 524288.0f);
-            v.z = __fmul_rn(v.z, 32768.0f);
-            v.w = __fmul_rn(v.w, 2048.0f);
-        } else {             // word elements 4..7: positions 4 0 1 2
-            v.x = __fmul_rn(v.x, 128.0f);
-            v.y = __fmul_rn(v.y, 8388608.0f);
-            v.z = __fmul_rn(v.z, 524288.0f);
-            v.w = __fmul_rn(v.w, 32768.0f);
-        }
-        xs4[(i >> 3) * G1_XS + (i & 7)] = v;
     }
     __syncthreads();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int groups = silu ? N / 2 : (N + R - 1) / R;
-    for (int g = blockIdx.x * (G1_THREADS / 32) + warp; g < groups; g += gridDim.x * (G1_THREADS / 32)) {
-        int rows[R];
-#pragma unroll
-        for (int r = 0; r < R; r++)
-            rows[r] = silu ? (g / GU_BLOCK) * (2 * GU_BLOCK) + g % GU_BLOCK + r * GU_BLOCK : min(g * R + r, N - 1);
+    for (int g = g0; g < groups; g += gridDim.x * (G1_THREADS / 32)) {
         float acc[R];
 #pragma unroll
         for (int r = 0; r < R; r++) acc[r] = 0.0f;
         for (int b0 = lane; b0 < KB; b0 += 32 * U) {
-            uint4 q[U][R];
-            float s[U][R];
-#pragma unroll
-            for (int u = 0; u < U; u++) {
-                const int b = b0 + u * 32;
-#pragma unroll
-                for (int r = 0; r < R; r++) {
-                    if (b < KB) {
-                        size_t bi = (size_t)rows[r] * KB + b;
-                        q[u][r] = __ldg(qs + bi);
-                        s[u][r] = __half2float(sc[bi]);
-                    } else {
-                        q[u][r] = make_uint4(0x88888888u, 0x88888888u, 0x88888888u, 0x88888888u);
-                        s[u][r] = 0.0f;
-                    }
-                }
-            }
+            if (g != g0 || b0 != lane) load_batch(g, b0);
 #pragma unroll
             for (int u = 0; u < U; u++) {
                 const int b = b0 + u * 32;
