@@ -510,6 +510,11 @@ def run_ours(args):
     import torch.cuda as tc
     e0, e1 = tc.Event(enable_timing=True), tc.Event(enable_timing=True)
     es = torch.cuda.ExternalStream(stream)
+    # one untimed prefill first (first launches load the kernels, scratch and
+    # tensor maps are set up), then the sequence is emptied again: a config
+    # with one short prompt (c1, c3) would otherwise time mostly that set-up
+    engine.batch_forward(model, prompts[0], kv, seq=0)
+    kv.clear(0)
     torch.cuda.synchronize()
     if dist:
         dist.barrier()

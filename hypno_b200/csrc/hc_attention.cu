@@ -44,14 +44,16 @@ __device__ __forceinline__ float4 ld4<__half>(const __half* p) {
 // elements per load); weighted V: thread (position group, column quad) adds
 // the weights times 4 columns over its group's positions, and the groups'
 // sums are added in group order (4 elements per load when head_dim is a
-// multiple of 4).
-template <typename KT>
+// multiple of 4).  HD > 0 fixes head_dim at compile time (64, 128), so a
+// score's loads are all in flight at once and the weighted-V loop keeps
+// eight rows in flight; HD = 0 takes it from P.
+template <typename KT, int HD>
 __global__ void __launch_bounds__(128) k_attention(AttnParams P) {
     pdl_trigger();
     pdl_wait();
     extern __shared__ float smem[];
     const int row = blockIdx.x, h = blockIdx.y;
-    const int hd = P.hd;
+    const int hd = HD > 0 ? HD : P.hd;
     const int kvh = h / (P.nh / P.nkv);
     __shared__ float red[32];
 
@@ -99,6 +101,7 @@ __global__ void __launch_bounds__(128) k_attention(AttnParams P) {
         const KT* kp = kbase + (size_t)p * kstride;
         float dot = 0.0f;
         if (vec) {
+#pragma unroll
             for (int d = 0; d < hd; d += 4) {
                 const float4 k4 = ld4<KT>(kp + d);
                 dot = fmaf(qs[d], k4.x, dot);
@@ -134,6 +137,7 @@ __global__ void __launch_bounds__(128) k_attention(AttnParams P) {
         const int c = t % cols, grp = t / cols;
         if (vec) {
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
             for (int p = grp; p < n; p += groups) {
                 const float w = scores[p];
                 const float4 v4 = ld4<KT>(vbase + (size_t)p * kstride + 4 * c);
@@ -170,15 +174,18 @@ int launch_attention(const AttnParams& P, int rows, int kv_fp16, cudaStream_t s)
         return HC_ERR_UNSUPPORTED;
     }
     dim3 grid((unsigned)rows, (unsigned)P.nh);
+    auto run = [&](auto kfn) -> int {
+        if (smem > 48 * 1024) HC_CUDA(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        return launch_pdl(kfn, grid, dim3(128), smem, s, P);
+    };
     if (kv_fp16) {
-        if (smem > 48 * 1024) HC_CUDA(cudaFuncSetAttribute(k_attention<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        HC_TRY(launch_pdl(k_attention<__half>, grid, dim3(128), smem, s, P));
-    } else {
-        if (smem > 48 * 1024) HC_CUDA(cudaFuncSetAttribute(k_attention<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        HC_TRY(launch_pdl(k_attention<float>, grid, dim3(128), smem, s, P));
+        if (P.hd == 64) return run(k_attention<__half, 64>);
+        if (P.hd == 128) return run(k_attention<__half, 128>);
+        return run(k_attention<__half, 0>);
     }
-    HC_LAUNCH_CHECK();
-    return HC_OK;
+    if (P.hd == 64) return run(k_attention<float, 64>);
+    if (P.hd == 128) return run(k_attention<float, 128>);
+    return run(k_attention<float, 0>);
 }
 
 // Stores the (rotated) K and V of each row into the cache:
