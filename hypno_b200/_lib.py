@@ -100,6 +100,7 @@ SIGNATURES = {
     "hc_decode_step_phases": (_I, [_P, _P, _P, _P, _I, _P, _P]),
     "hc_phase_count": (_I, []),
     "hc_sample_dev": (_I, [_P, _SZ, _I, _I, _P, _P, _P, _P, _P, _P]),
+    "hc_argmax_dev": (_I, [_P, _SZ, _I, _I, _I, _P, _P, _P]),
     "hc_phase_name": (ctypes.c_char_p, [_I]),
     "hc_comm_unique_id": (_I, [_P]),
     "hc_comm_init": (_I, [_P, _P, _I, _I, ctypes.c_double]),

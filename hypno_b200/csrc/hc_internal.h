@@ -163,8 +163,13 @@ int launch_rope_rows(float* x, size_t ldx, size_t rows, size_t heads, size_t hd,
 int launch_embed(const DevWeight& emb, const uint32_t* ids, size_t B, float* out, size_t hidden,
                  cudaStream_t s);
 int launch_argmax(const float* logits, size_t rows, size_t n, uint32_t* out, cudaStream_t s);
+int launch_argmax(const float* logits, size_t rows, size_t n, size_t ld, uint32_t* out, cudaStream_t s);
 // pairs[row] = (max of the row, bits of idx0 + its last maximal index)
-int launch_argmax_pairs(const float* logits, size_t rows, size_t n, uint32_t idx0, float2* pairs, cudaStream_t s);
+int launch_argmax_pairs(const float* logits, size_t rows, size_t n, size_t ld, uint32_t idx0, float2* pairs,
+                        cudaStream_t s);
+// Greedy ids from [tp][rows] shard pairs (launch_argmax_pairs), shards in
+// vocabulary order.
+int launch_pick_pairs(const float2* pairs, size_t rows, int tp, uint32_t* out, cudaStream_t s);
 
 // Synthetic normal stream (host and device versions agree bit for bit).
 int launch_synth_normal(uint64_t seed, uint64_t stream, uint64_t offset, uint64_t n, float std,

@@ -1002,21 +1002,71 @@ int launch_embed(const DevWeight& emb, const uint32_t* ids, size_t B, float* out
 }
 
 // ============================================================ argmax
-// Greedy pick: the LAST maximal index wins (Iterator::max_by, run.rs:234-238).
-// Row-wise last maximal index (the tie rule of Rust's max_by): out[row] =
-// index; with pairs, pairs[row] = (max, bits of idx0 + index) for the
-// vocabulary-sharded exchange of tensor parallelism.
-__global__ void k_argmax(const float* __restrict__ logits, int n, uint32_t* __restrict__ out,
+// Greedy pick: Iterator::max_by with partial_cmp(..).unwrap_or(Equal)
+// (run.rs:234-238, serve.rs:300).  The fold keeps its accumulator only while
+// it is strictly greater than the next element, so the LAST maximal index
+// wins, and a NaN (Equal to everything) is taken and then replaced by the
+// element after it: the pick is the last maximal index after the row's last
+// NaN, or that NaN's index when it ends the row.
+
+// (best, bi) <- (ov, oi) when oi is the larger value or the same value at a
+// larger index (non-NaN values; bi < 0: nothing yet)
+__device__ __forceinline__ void am_take(float& best, int& bi, float ov, int oi) {
+    if (oi >= 0 && (bi < 0 || ov > best || (ov == best && oi > bi))) {
+        best = ov;
+        bi = oi;
+    }
+}
+
+// Block-wide am_take and max of nan_i; the result is in every thread.
+__device__ __forceinline__ void am_reduce(float& best, int& bi, int& nan_i, float* sv, int* si, int* sn) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        am_take(best, bi, __shfl_xor_sync(0xffffffffu, best, o), __shfl_xor_sync(0xffffffffu, bi, o));
+        nan_i = max(nan_i, __shfl_xor_sync(0xffffffffu, nan_i, o));
+    }
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    __syncthreads();  // (sv / si / sn may still be read by an earlier reduction)
+    if (lane == 0) {
+        sv[w] = best;
+        si[w] = bi;
+        sn[w] = nan_i;
+    }
+    __syncthreads();
+    best = lane < nw ? sv[lane] : -INFINITY;
+    bi = lane < nw ? si[lane] : -1;
+    nan_i = lane < nw ? sn[lane] : -1;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        am_take(best, bi, __shfl_xor_sync(0xffffffffu, best, o), __shfl_xor_sync(0xffffffffu, bi, o));
+        nan_i = max(nan_i, __shfl_xor_sync(0xffffffffu, nan_i, o));
+    }
+}
+
+// One CTA per row of n logits (row stride ld): out[row] = the pick; with
+// pairs, pairs[row] = (its value, bits of idx0 + pick, bit 31 set when the
+// row held a NaN; all bits set for an empty row) for the vocabulary-sharded
+// exchange of tensor parallelism (k_pick_pairs).
+__global__ void k_argmax(const float* __restrict__ logits, int n, size_t ld, uint32_t* __restrict__ out,
                          float2* __restrict__ pairs = nullptr, uint32_t idx0 = 0) {
     pdl_trigger();
     pdl_wait();
     __shared__ float sv[32];
-    __shared__ int si[32];
-    const float* l = logits + (size_t)blockIdx.x * n;
+    __shared__ int si[32], sn[32];
+    const float* l = logits + (size_t)blockIdx.x * ld;
     float best = -INFINITY;
-    int bi = -1;
+    int bi = -1, nan_i = -1;
     // Each thread visits its indices in increasing order, so ">=" keeps its
-    // last maximum; the reductions below break ties toward the larger index.
+    // last maximum and nan_i its last NaN; the reductions break ties toward
+    // the larger index.
+    auto visit = [&](float e, int i) {
+        if (e != e)
+            nan_i = i;
+        else if (bi < 0 || e >= best) {
+            best = e;
+            bi = i;
+        }
+    };
     if ((n & 3) == 0 && ((uintptr_t)l & 15) == 0) {
         constexpr int U = 4;  // float4 loads in flight per thread
         const float4* l4 = reinterpret_cast<const float4*>(l);
@@ -1032,56 +1082,85 @@ __global__ void k_argmax(const float* __restrict__ logits, int n, uint32_t* __re
             for (int u = 0; u < U; u++) {
                 int i = i0 + u * blockDim.x;
                 if (i < n4) {
-                    const float e[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
-#pragma unroll
-                    for (int c = 0; c < 4; c++)
-                        if (bi < 0 || e[c] >= best) { best = e[c]; bi = 4 * i + c; }
+                    visit(v[u].x, 4 * i);
+                    visit(v[u].y, 4 * i + 1);
+                    visit(v[u].z, 4 * i + 2);
+                    visit(v[u].w, 4 * i + 3);
                 }
             }
         }
     } else {
-        for (int i = threadIdx.x; i < n; i += blockDim.x) {
-            float v = l[i];
-            if (bi < 0 || v >= best) { best = v; bi = i; }
+        for (int i = threadIdx.x; i < n; i += blockDim.x) visit(l[i], i);
+    }
+    am_reduce(best, bi, nan_i, sv, si, sn);
+    const int last_nan = nan_i;
+    if (last_nan >= 0) {  // rare: the last maximum after the last NaN
+        best = -INFINITY;
+        bi = -1;
+        nan_i = -1;
+        for (int i = last_nan + 1 + threadIdx.x; i < n; i += blockDim.x) visit(l[i], i);
+        am_reduce(best, bi, nan_i, sv, si, sn);
+        if (bi < 0) {  // the NaN ends the row
+            bi = last_nan;
+            best = l[last_nan];
         }
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        float ov = __shfl_xor_sync(0xffffffffu, best, o);
-        int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (oi >= 0 && (bi < 0 || ov > best || (ov == best && oi > bi))) { best = ov; bi = oi; }
-    }
-    int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    if (lane == 0) { sv[w] = best; si[w] = bi; }
-    __syncthreads();
-    if (w == 0) {
-        int nw = blockDim.x >> 5;
-        best = lane < nw ? sv[lane] : -INFINITY;
-        bi = lane < nw ? si[lane] : -1;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            float ov = __shfl_xor_sync(0xffffffffu, best, o);
-            int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (oi >= 0 && (bi < 0 || ov > best || (ov == best && oi > bi))) { best = ov; bi = oi; }
-        }
-        if (lane == 0) {
-            if (pairs)
-                pairs[blockIdx.x] = make_float2(best, __uint_as_float(bi < 0 ? 0xFFFFFFFFu : idx0 + (uint32_t)bi));
-            else
-                out[blockIdx.x] = (uint32_t)(bi < 0 ? 0 : bi);
-        }
+    if (threadIdx.x == 0) {
+        if (pairs)
+            pairs[blockIdx.x] = make_float2(
+                best, __uint_as_float(bi < 0 ? 0xFFFFFFFFu : (idx0 + (uint32_t)bi) | (last_nan >= 0 ? 0x80000000u : 0u)));
+        else
+            out[blockIdx.x] = (uint32_t)(bi < 0 ? 0 : bi);
     }
 }
 
-int launch_argmax_pairs(const float* logits, size_t rows, size_t n, uint32_t idx0, float2* pairs, cudaStream_t s) {
+// Greedy ids from the shards' pairs ([tp][rows], shard order = vocabulary
+// order): the fold of max_by over the shards' picks, restarted at a shard
+// that held a NaN (everything before its last NaN is irrelevant); 0 for no
+// logits.
+__global__ void k_pick_pairs(const float2* __restrict__ pairs, int rows, int tp, uint32_t* __restrict__ out) {
+    pdl_trigger();
+    pdl_wait();
+    const int row = blockIdx.x * blockDim.x + threadIdx.x;
+    if (row >= rows) return;
+    float best = 0.0f;
+    int bi = -1;
+    for (int r = 0; r < tp; r++) {
+        const float2 p = pairs[(size_t)r * rows + row];
+        const uint32_t bits = __float_as_uint(p.y);
+        if (bits == 0xFFFFFFFFu) continue;  // an empty shard
+        const int oi = (int)(bits & 0x7FFFFFFFu);
+        // a shard with a NaN restarts the fold; otherwise its pick (the last
+        // maximum of NaN-free logits) replaces the accumulator unless that is
+        // strictly greater (a NaN accumulator is replaced)
+        if ((bits >> 31) || bi < 0 || !(best > p.x)) {
+            best = p.x;
+            bi = oi;
+        }
+    }
+    out[row] = (uint32_t)(bi < 0 ? 0 : bi);
+}
+
+int launch_argmax_pairs(const float* logits, size_t rows, size_t n, size_t ld, uint32_t idx0, float2* pairs,
+                        cudaStream_t s) {
     if (rows == 0) return HC_OK;
-    return launch_pdl(k_argmax, dim3((unsigned)rows), dim3(1024), 0, s, logits, (int)n, (uint32_t*)nullptr, pairs, idx0);
+    return launch_pdl(k_argmax, dim3((unsigned)rows), dim3(1024), 0, s, logits, (int)n, ld, (uint32_t*)nullptr, pairs,
+                      idx0);
+}
+
+int launch_pick_pairs(const float2* pairs, size_t rows, int tp, uint32_t* out, cudaStream_t s) {
+    if (rows == 0) return HC_OK;
+    return launch_pdl(k_pick_pairs, dim3((unsigned)((rows + 127) / 128)), dim3(128), 0, s, pairs, (int)rows, tp, out);
+}
+
+int launch_argmax(const float* logits, size_t rows, size_t n, size_t ld, uint32_t* out, cudaStream_t s) {
+    if (rows == 0) return HC_OK;
+    return launch_pdl(k_argmax, dim3((unsigned)rows), dim3(1024), 0, s, logits, (int)n, ld, out, (float2*)nullptr,
+                      (uint32_t)0);
 }
 
 int launch_argmax(const float* logits, size_t rows, size_t n, uint32_t* out, cudaStream_t s) {
-    if (rows == 0) return HC_OK;
-    return launch_pdl(k_argmax, dim3((unsigned)rows), dim3(1024), 0, s, logits, (int)n, out, (float2*)nullptr,
-                      (uint32_t)0);
+    return launch_argmax(logits, rows, n, n, out, s);
 }
 
 // ============================================================ synthetic data

@@ -739,26 +739,10 @@ int lm_head_logits(hc_model* m, const float* x, size_t rows, float* logits, cons
 }
 
 // Greedy ids of a vocabulary-sharded LM head without gathering the logits:
-// each rank takes the last maximal index of its slice (k_argmax's rule), the
-// ranks exchange (max, index) pairs, and every rank keeps the largest max,
-// ties to the larger index, which the rank order makes the global last
-// maximal index (run.rs:234-238).
-__global__ void k_pick_pairs(const float2* __restrict__ pairs, int rows, int tp, uint32_t* __restrict__ out) {
-    const int row = blockIdx.x * blockDim.x + threadIdx.x;
-    if (row >= rows) return;
-    float best = -INFINITY;
-    int bi = -1;
-    for (int r = 0; r < tp; r++) {
-        const float2 p = pairs[(size_t)r * rows + row];
-        const int oi = (int)__float_as_uint(p.y);
-        if (oi >= 0 && (bi < 0 || p.x > best || (p.x == best && oi > bi))) {
-            best = p.x;
-            bi = oi;
-        }
-    }
-    out[row] = (uint32_t)(bi < 0 ? 0 : bi);
-}
-
+// each rank takes the pick of its slice (k_argmax), the ranks exchange
+// (value, index, NaN bit) pairs, and every rank folds them in rank order
+// (k_pick_pairs), which gives the pick over the whole vocabulary
+// (run.rs:234-238).
 int lm_head_argmax_tp(hc_model* m, const float* x, size_t rows, uint32_t* argmax, const __half* x16) {
     const hc_config& c = m->cfg;
     HC_CHECK(m->comm, HC_ERR_STATE, "tensor-parallel model used before hc_comm_init");
@@ -769,13 +753,11 @@ int lm_head_argmax_tp(hc_model* m, const float* x, size_t rows, uint32_t* argmax
     HC_TRY(phase(m, PH_ARGMAX));
     float2* local = m->sc.tp_pairs;
     float2* all = local + rows;
-    HC_TRY(hc::launch_argmax_pairs(mine, rows, vs, (uint32_t)m->vocab0, local, m->stream));
+    HC_TRY(hc::launch_argmax_pairs(mine, rows, vs, vs, (uint32_t)m->vocab0, local, m->stream));
     HC_TRY(phase(m, PH_LOGITS_X));
     HC_TRY(hc::comm_allgather(m->comm, reinterpret_cast<const float*>(local), reinterpret_cast<float*>(all), rows * 2,
                               m->stream));
-    k_pick_pairs<<<(unsigned)((rows + 127) / 128), 128, 0, m->stream>>>(all, (int)rows, c.tp_size, argmax);
-    HC_LAUNCH_CHECK();
-    return HC_OK;
+    return hc::launch_pick_pairs(all, rows, c.tp_size, argmax, m->stream);
 }
 
 // Waits for the model's stream; with a communicator the wait is watched

@@ -454,3 +454,19 @@ HC_EXPORT int hc_sample_dev(const float* logits_dev, size_t ld, int B, int V, co
     return hc::launch_sample(logits_dev, ld, B, V, temperature_dev, top_p_dev, top_k_dev, rng_state_dev, out_dev,
                              (cudaStream_t)stream);
 }
+
+HC_EXPORT int hc_argmax_dev(const float* logits_dev, size_t ld, int B, int V, int shards, float* pairs_dev,
+                            uint32_t* out_dev, void* stream) {
+    HC_CHECK(B >= 0 && V > 0 && ld >= (size_t)V && shards >= 1 && V % shards == 0, HC_ERR_INVALID,
+             "hc_argmax_dev: bad shape (B %d, V %d, ld %zu, shards %d)", B, V, ld, shards);
+    HC_CHECK(B == 0 || (logits_dev && out_dev && (shards == 1 || pairs_dev)), HC_ERR_INVALID,
+             "hc_argmax_dev: NULL argument");
+    cudaStream_t s = (cudaStream_t)stream;
+    if (shards == 1) return hc::launch_argmax(logits_dev, (size_t)B, (size_t)V, ld, out_dev, s);
+    const size_t vs = (size_t)(V / shards);
+    float2* pairs = reinterpret_cast<float2*>(pairs_dev);
+    for (int r = 0; r < shards; r++)
+        HC_TRY(hc::launch_argmax_pairs(logits_dev + r * vs, (size_t)B, vs, ld, (uint32_t)(r * vs),
+                                       pairs + (size_t)r * B, s));
+    return hc::launch_pick_pairs(pairs, (size_t)B, shards, out_dev, s);
+}

@@ -224,6 +224,20 @@ int hc_sample_dev(const float* logits_dev, size_t ld, int B, int V, const float*
                   const float* top_p_dev, const int* top_k_dev, uint64_t* rng_state_dev, uint32_t* out_dev,
                   void* stream);
 
+/* run.rs:234-238, 249 and serve.rs:300, 304 (the greedy pick,
+ * Iterator::max_by with partial_cmp(..).unwrap_or(Equal)) for B rows of
+ * device logits (row stride ld floats, V entries each): out_dev[b] = the last
+ * maximal index after the row's last NaN, or that NaN's index when it ends
+ * the row (a NaN compares Equal, so the fold takes it and then the element
+ * after it); the last maximal index when there is no NaN.  shards > 1 splits
+ * every row into that many equal vocabulary slices (V % shards == 0), picks
+ * per slice and folds the slices' picks in order, the kernels a
+ * tensor-parallel LM head runs across its ranks; pairs_dev is then device
+ * scratch of 2 * shards * B floats (may be NULL for shards == 1).
+ * Stream-ordered, no synchronization. */
+int hc_argmax_dev(const float* logits_dev, size_t ld, int B, int V, int shards, float* pairs_dev, uint32_t* out_dev,
+                  void* stream);
+
 /* ---- tensor parallelism (new in this backend; the reference is single-CPU) */
 
 /* Writes a fresh 128-byte NCCL unique id (rank 0 creates it and shares it
