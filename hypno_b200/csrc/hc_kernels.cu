@@ -276,8 +276,11 @@ __device__ __forceinline__ float4 g1_prescale(float4 v, int i) {
 // needs no separate norm kernel).  silu: the weight is a fused gate/up
 // weight in blocks of GU_BLOCK gate rows and their GU_BLOCK up rows; a
 // warp takes a gate row and its up row and writes y[i] = silu(gate) * up
-// (k_silu_mul's arithmetic) for the N / 2 outputs.
-template <int R, int U>
+// (k_silu_mul's arithmetic) for the N / 2 outputs.  PRE (every warp has at
+// most one row group): the warp's weights are requested before the wait for
+// the previous kernel; with several groups per warp that hoisting slows the
+// loop (128256 x 4096: 81 against 74 µs), so it is left out there.
+template <int R, int U, bool PRE>
 __global__ void __launch_bounds__(G1_THREADS, 3) k_q4_gemv1(const uint4* __restrict__ qs, const __half* __restrict__ sc,
                                                          const float* __restrict__ x, float* __restrict__ y, int epi,
                                                          const float* res, int N, int KB,
@@ -313,7 +316,7 @@ __global__ void __launch_bounds__(G1_THREADS, 3) k_q4_gemv1(const uint4* __restr
     // the weights do not depend on the previous kernel: the warp's first
     // batch is in flight before the wait for it
     const int g0 = blockIdx.x * (G1_THREADS / 32) + warp;
-    if (g0 < groups) load_batch(g0, lane);
+    if (PRE && g0 < groups) load_batch(g0, lane);
     pdl_wait();
     // x, read once: staged raw while the sum of squares accumulates, then
     // (with nw) normalized in place; each thread rewrites only its own
@@ -350,7 +353,7 @@ __global__ void __launch_bounds__(G1_THREADS, 3) k_q4_gemv1(const uint4* __restr
 #pragma unroll
         for (int r = 0; r < R; r++) acc[r] = 0.0f;
         for (int b0 = lane; b0 < KB; b0 += 32 * U) {
-            if (g != g0 || b0 != lane) load_batch(g, b0);
+            if (!PRE || g != g0 || b0 != lane) load_batch(g, b0);
 #pragma unroll
             for (int u = 0; u < U; u++) {
                 const int b = b0 + u * 32;
@@ -489,10 +492,10 @@ static int launch_gemv(const hc_q4_matrix& w, const float* x, size_t ldx, size_t
         const size_t groups = (w.n + 1) / 2;  // 2 rows per warp
         const size_t per_cta = G1_THREADS / 32;
         unsigned grid = (unsigned)std::min<size_t>((groups + per_cta - 1) / per_cta, 148 * 3);
-        if (smem > 48 * 1024)
-            cudaFuncSetAttribute(k_q4_gemv1<2, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        return launch_pdl(k_q4_gemv1<2, 4>, dim3(grid), dim3(G1_THREADS), smem, s, w.qs, w.sc, x, y, epi, res,
-                          (int)w.n, (int)kb, (const float*)nullptr, 0.0f, 0);
+        auto kfn = groups <= (size_t)grid * per_cta ? k_q4_gemv1<2, 4, true> : k_q4_gemv1<2, 4, false>;
+        if (smem > 48 * 1024) cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        return launch_pdl(kfn, dim3(grid), dim3(G1_THREADS), smem, s, w.qs, w.sc, x, y, epi, res, (int)w.n, (int)kb,
+                          (const float*)nullptr, 0.0f, 0);
     }
     if (mtok == 1) launch_gemv_mt<1>(w, x, ldx, mtok, y, ldy, epi, res, ldres, s);
     else if (mtok <= 4) launch_gemv_mt<4>(w, x, ldx, mtok, y, ldy, epi, res, ldres, s);
@@ -516,9 +519,9 @@ int launch_gemv1_fused(const DevWeight& w, const float* x, float* y, const float
     const size_t groups = silu ? q.n / 2 : (q.n + 1) / 2;
     const size_t per_cta = G1_THREADS / 32;
     const unsigned grid = (unsigned)std::min<size_t>((groups + per_cta - 1) / per_cta, 148 * 3);
-    if (smem > 48 * 1024)
-        HC_CUDA(cudaFuncSetAttribute(k_q4_gemv1<2, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    return launch_pdl(k_q4_gemv1<2, 4>, dim3(grid), dim3(G1_THREADS), smem, s, q.qs, q.sc, x, y, (int)EPI_STORE,
+    auto kfn = groups <= (size_t)grid * per_cta ? k_q4_gemv1<2, 4, true> : k_q4_gemv1<2, 4, false>;
+    if (smem > 48 * 1024) HC_CUDA(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    return launch_pdl(kfn, dim3(grid), dim3(G1_THREADS), smem, s, q.qs, q.sc, x, y, (int)EPI_STORE,
                       (const float*)nullptr, (int)q.n, (int)kb, norm_w, eps, silu ? 1 : 0);
 }
 
