@@ -93,9 +93,18 @@ int launch_q4_dequantize(const uint8_t* q, size_t nblocks, float* out, cudaStrea
     HC_LAUNCH_CHECK();
     return HC_OK;
 }
+// Launched after the plane split, as an ordinary (not programmatic) launch:
+// the single-token matvec requests its weights before it waits for the
+// previous kernel, which is only safe when that kernel did not write them;
+// with this empty kernel in between, the split has completed and its stores
+// are visible before any matvec that follows on the stream can start.
+__global__ void k_weights_settled() {}
+
 int launch_q4_split(const uint8_t* aos, size_t nblocks, uint4* qs, __half* sc, cudaStream_t s) {
     if (nblocks == 0) return HC_OK;
     k_q4_split<<<grid_for(nblocks, 256), 256, 0, s>>>(aos, nblocks, qs, sc);
+    HC_LAUNCH_CHECK();
+    k_weights_settled<<<1, 32, 0, s>>>();
     HC_LAUNCH_CHECK();
     return HC_OK;
 }
