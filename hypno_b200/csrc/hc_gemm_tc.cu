@@ -1246,6 +1246,9 @@ int gemm_check(GemmWorkspace* ws) {
     HC_CUDA(cudaMemcpy(&h, ws->err, sizeof(int), cudaMemcpyDeviceToHost));
     if (h) {
         HC_CUDA(cudaMemset(ws->err, 0, sizeof(int)));
+        // an aborted stream-K launch may leave contributor flags raised;
+        // a later owner would then add a stale slot without waiting
+        if (ws->sk_flag) HC_CUDA(cudaMemset(ws->sk_flag, 0, (size_t)ws->sk_cap * 4 * sizeof(int)));
         hc_set_error("a bounded pipeline wait timed out in a tcgen05 GEMM or a TMA attention kernel (the kernel "
                      "aborted and skipped its stores)");
         return HC_ERR_TIMEOUT;
